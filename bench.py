@@ -1,0 +1,372 @@
+"""Benchmark: Llama-3.2-1B-shape Q4_0 decode tok/s and Q4 matvec HBM GB/s on B200.
+
+Workload: Llama-3.2-1B-shaped model (dim 2048,
+16 layers, 32/8 heads, FFN 8192, vocab 128256, tied Q4_0 embedding), random
+init N(0, 0.02) from a fixed seed, a 128-token seeded prompt prefilled
+untimed, then greedy batch-1 decode with the KV cache growing from position
+128 (wrapping back to 128 at position 640, the config's maximum).  A step is
+one decode token.  Every step streams all 695 MB of weights, far more than
+the 126 MB L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference algorithm on the host cores: the C
+restatement in oracle/ (the JavaScript reference cannot run: no JS engine in
+this image), on a bounded number of decode tokens.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(kind=0, emb_type=2, dim=2048, hidden_dim=8192, n_layers=16, n_heads=32, n_kv_heads=8, head_dim=64,
+           vocab=128256, seq_len=2048, rope_theta=500000.0, eps=1e-5)
+SEED = 20261201
+PROMPT = 128
+MAX_POS = 640
+METRIC = "Llama-3.2-1B-shape Q4 decode tok/s; Q4 matvec HBM GB/s vs B200 peak"
+WORKLOAD = "llama3.2-1B-shape Q4_0 batch-1 greedy decode (configs[3])"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.p:
+            self.p.terminate()
+            try:
+                out, _ = self.p.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+                out, _ = self.p.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_model(ctx):
+    from purebee_b200.runtime import LlamaConfig, StreamingLlamaRuntime
+    c = CFG
+    lc = LlamaConfig(dim=c["dim"], hiddenDim=c["hidden_dim"], nLayers=c["n_layers"], nHeads=c["n_heads"],
+                     nKvHeads=c["n_kv_heads"], vocabSize=c["vocab"], seqLen=c["seq_len"], headDim=c["head_dim"],
+                     ropeTheta=c["rope_theta"], rmsNormEps=c["eps"])
+    rt = StreamingLlamaRuntime(lc, ctx=ctx, emb_type=c["emb_type"])
+    rt.loadSynthetic(SEED)
+    return rt
+
+
+def prompt_tokens():
+    from purebee_b200 import _native as N
+    import ctypes
+    out = np.zeros(PROMPT, np.int32)
+    rc = N.lib().pb_synth_tokens(N.ptr(out), PROMPT, SEED, 1, CFG["vocab"])
+    assert rc == 0
+    return out.tolist()
+
+
+def matvec_roofline(ctx, torch, stream, peak, reps=50):
+    """Per-launch duration of the Q4_0 matvec kernel on the decode shapes,
+    weights rotated over copies totalling > 4x L2 so HBM is measured."""
+    from purebee_b200 import _native as N
+    L = N.lib()
+    shapes = {"qkv 3072x2048": (3072, 2048), "o 2048x2048": (2048, 2048), "gate|up 16384x2048": (16384, 2048),
+              "down 2048x8192": (2048, 8192)}
+    per_token_launches = {"qkv 3072x2048": 16, "o 2048x2048": 16, "gate|up 16384x2048": 16, "down 2048x8192": 16}
+    rng = np.random.default_rng(7)
+    res = {}
+    tot_b, tot_t = 0.0, 0.0
+    for name, (n, k) in shapes.items():
+        nbytes = n * k // 32 * 18
+        copies = max(2, int(np.ceil(4 * 126e6 / nbytes)))
+        raw = rng.integers(0, 256, n * (k // 32) * 18, dtype=np.uint8)
+        raw.reshape(-1, 18)[:, :2] = (rng.standard_normal(n * (k // 32)) * 0.01).astype(np.float16).view(
+            np.uint8).reshape(-1, 2)
+        mats = [N.QMat(ctx, N.TYPE_Q4_0, raw, n, k) for _ in range(copies)]
+        x = ctx.to_device(rng.standard_normal(k).astype(np.float32))
+        y = ctx.alloc(n * 4)
+        for i in range(3):
+            ctx._check(L.pb_qmat_matvec(ctx.h, mats[i % copies].h, x.ptr, y.ptr, 0, 0))
+        ctx.sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(reps):
+            ctx._check(L.pb_qmat_matvec(ctx.h, mats[i % copies].h, x.ptr, y.ptr, 0, 0))
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        alg = nbytes + k * 4 + n * 4
+        res[name] = {"us": round(ms * 1e3, 3), "GBps": round(alg / (ms * 1e-3) / 1e9, 1),
+                     "frac": round(alg / (ms * 1e-3) / 1e9 / peak, 3), "bytes": alg}
+        tot_b += alg * per_token_launches[name]
+        tot_t += ms * 1e-3 * per_token_launches[name]
+        for m in mats:
+            m.free()
+    return res, tot_b / tot_t / 1e9, tot_b / sum(per_token_launches.values())
+
+
+def run_ours(args, rank, world, torch, dist):
+    from purebee_b200 import _native as N
+    dev = int(os.environ.get("LOCAL_RANK", 0))
+    ctx = N.Context(dev)
+    ctx.set_timeout_ms(120000)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.ExternalStream(N.lib().pb_stream(ctx.h), device=dev)
+    peak, peak_kind = load_peaks()
+    rt = build_model(ctx)
+    m = rt.model
+    prompt = prompt_tokens()
+    # prefill (untimed), leaves the first greedy token on the device
+    rt.forward(prompt, 0)
+
+    def device_steps(pos, n):
+        """n graph replays starting at pos; wraps at MAX_POS."""
+        while n > 0:
+            room = MAX_POS - pos
+            if room <= 0:
+                pos = PROMPT
+                room = MAX_POS - pos
+            k = min(n, room)
+            ctx._check(N.lib().pb_model_decode_loop(m.h, pos, k, None))
+            pos += k
+            n -= k
+        return pos
+
+    pos = device_steps(PROMPT, args.warmup)
+    ctx.sync()
+    launches_per_step = int(N.lib().pb_model_decode_launches(m.h))
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record(stream)
+        pos_end = device_steps(pos, args.steps)
+        e1.record(stream)
+        e1.synchronize()
+    ctx.sync()
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    clocks = clk.summary()
+    # algorithmic bytes per token at the mean position of the timed steps
+    mid = min(pos + args.steps // 2, MAX_POS - 1)
+    step_bytes = int(N.lib().pb_model_decode_bytes(m.h, mid))
+
+    # ---- e2e through the public API: H2D token+pos, graph, D2H next token ----
+    e2e_steps = min(args.steps, 64)
+    rt.resetCache()
+    rt.forward(prompt, 0)
+    nxt, _ = m.decode(1, PROMPT)  # warm the host path
+    p = PROMPT + 1
+    tok = nxt
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        if p >= MAX_POS:
+            p = PROMPT
+        tok, _ = m.decode(tok, p)
+        p += 1
+    e2e_s = time.perf_counter() - t0
+    e2e_tps = e2e_steps / e2e_s
+    if dist:
+        t = torch.tensor([e2e_s], device=f"cuda:{dev}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_tps = e2e_steps / float(t.item())
+
+    result = None
+    if rank == 0:
+        mv, mv_agg, mv_bytes_avg = matvec_roofline(ctx, torch, stream, peak)
+        total_tokens = args.steps * world
+        value = total_tokens / (ms / 1e3)
+        step_gbs = step_bytes / (ms / 1e3 / args.steps) / 1e9
+        result = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "u4 weights, f32 math (f64 for the reference's double ops)",
+            "data": "synthetic (seeded N(0,0.02) weights, seeded prompt tokens)",
+            "config": {"workload": WORKLOAD, "model": "llama3.2-1B-shape", "global_batch": world, "seq_len": MAX_POS,
+                       "prompt": PROMPT, "parallelism": f"replicas{world}" if world > 1 else "single-gpu",
+                       "l2": "weights 695 MB per step > 126 MB L2 (no flush needed)"},
+            "decode_step": {"bytes": step_bytes, "GBps": round(step_gbs, 1), "frac_of_hbm": round(step_gbs / peak, 3),
+                            "launches": launches_per_step},
+            "roofline": {"bound": "hbm", "kernel": "k_matvec (Q4_0, WASM lane order)",
+                         "achieved": round(mv_agg, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(mv_agg / peak, 3), "traffic": None,
+                         "bytes_per_launch": int(mv_bytes_avg), "per_shape": mv},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "e2e": {"value": round(e2e_tps * world, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4, "steps": e2e_steps,
+                    "api": "StreamingLlamaRuntime model.decode (pb_model_decode)"},
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline(rt, sample_tokens=2)
+    rt.shutdown()
+    ctx.close()
+    return result
+
+
+def copy_to_oracle(rt):
+    """Oracle model holding the device's weights (same bits)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    om = O.Model(O.Config(**CFG))
+    for w in range(8):
+        for l in (range(CFG["n_layers"]) if w else [0]):
+            om.tensor(l, w)[:] = rt.getTensor(l, w)
+    om.refresh()
+    return O, om
+
+
+def cpu_baseline(rt, sample_tokens=2):
+    O, om = copy_to_oracle(rt)
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    om.forward([1], 0)  # warm
+    t0 = time.perf_counter()
+    tok = 1
+    for i in range(sample_tokens):
+        lg = om.forward([tok], 1 + i)
+        tok = O.argmax(lg)
+    dt = time.perf_counter() - t0
+    return {"value": round(sample_tokens / dt, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_tokens} decode tokens of the same model at positions 1-{sample_tokens} "
+                      f"(oracle/pb_oracle.c, WASM-order Q4 matvec, {threads} threads row split)"}
+
+
+def run_reference(args):
+    """The reference algorithm on the host cores (C restatement; no JS engine)."""
+    from purebee_b200 import _native as N
+    ctx = N.Context(int(os.environ.get("LOCAL_RANK", 0)))
+    rt = build_model(ctx)
+    O, om = copy_to_oracle(rt)
+    rt.shutdown()
+    ctx.close()
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    prompt = prompt_tokens()[:8]
+    om.forward(prompt, 0)
+    pos = len(prompt)
+    tok = 1
+    # bounded: each timed step is one decode token; cap the count so the run
+    # stays within a few minutes
+    steps = min(args.steps, args.ref_max_steps)
+    warm = min(args.warmup, 1)
+    for _ in range(warm):
+        tok = O.argmax(om.forward([tok], pos))
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tok = O.argmax(om.forward([tok], pos))
+        pos += 1
+    dt = time.perf_counter() - t0
+    v = steps / dt
+    return {"metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": 0, "steps": steps,
+            "requested_steps": args.steps, "warmup": warm, "ms_per_step": round(dt / steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (reference lane order)",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "model": "llama3.2-1B-shape", "global_batch": 1, "seq_len": MAX_POS},
+            "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": f"{steps} decode tokens after an 8-token prefill (oracle/pb_oracle.c; the "
+                                       f"JavaScript reference has no engine in this image)"},
+            "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-max-steps", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+    import torch
+    dist = None
+    if world > 1:
+        import torch.distributed as td
+        from datetime import timedelta
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        td.init_process_group("nccl", timeout=timedelta(seconds=300))
+        dist = td
+    res = run_ours(args, rank, world, torch, dist)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,237 @@
+/*
+ * purebee_cuda.h - C ABI of the B200 (sm_100a) backend for PureBee's
+ * quantized Llama inference path.
+ *
+ * Plain C: opaque handles, plain pointers and sizes.  Every entry point
+ * returns PB_OK (0) or a PB_ERR_* status; pb_last_error() gives the message.
+ * There is no CPU fallback: every compute entry point runs a CUDA kernel.
+ *
+ * Pointer conventions:
+ *   - arguments named *_host are host memory (copied in or out by the call);
+ *   - arguments named *_dev are device memory from pb_malloc (or any device
+ *     allocation on the context's device);
+ *   - calls that only take device pointers are asynchronous on the context
+ *     stream; calls that return host data block until it is ready, with the
+ *     deadline set by pb_set_timeout_ms (PB_ERR_TIMEOUT when it passes).
+ *
+ * Each declaration names the reference interface it replaces (file:line in
+ * sammcj/purebee).
+ */
+#ifndef PUREBEE_CUDA_H
+#define PUREBEE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PB_ABI_VERSION 1
+
+/* status codes (the reference throws Error with a message; the shim maps a
+ * non-zero status plus pb_last_error() to `throw new Error(msg)`) */
+#define PB_OK 0
+#define PB_ERR_ARG 1      /* bad argument (engine.js:97, engine.js:122 size checks) */
+#define PB_ERR_OOM 2      /* device allocation failed */
+#define PB_ERR_CUDA 3     /* CUDA runtime error */
+#define PB_ERR_TIMEOUT 4  /* host wait passed its deadline (thread-pool.js:232-238) */
+#define PB_ERR_DEVICE 5   /* a kernel raised its error word (bounds, bounded wait) */
+#define PB_ERR_STATE 6    /* call not valid in the current state */
+#define PB_ERR_NOTFOUND 7 /* name not in memory (memory.js:126) */
+
+/* GGML tensor types (gguf.js:30-33) */
+#define PB_TYPE_F32 0
+#define PB_TYPE_F16 1
+#define PB_TYPE_Q4_0 2
+#define PB_TYPE_Q4_1 3
+#define PB_TYPE_Q8_0 8
+
+typedef struct pb_ctx pb_ctx;
+typedef struct pb_qmat pb_qmat;
+typedef struct pb_model pb_model;
+
+/* ------------------------------------------------------------------ */
+/* context                                                              */
+/* ------------------------------------------------------------------ */
+
+/* Replaces wasm-q4.js:647-668 init() / wasm-simd.js:339-362 init(): binds a
+ * device, creates the stream, runs the Q4_0 self-test (wasm-q4.js:673-704). */
+int pb_init(int device, pb_ctx** out);
+int pb_shutdown(pb_ctx* ctx);
+const char* pb_last_error(const pb_ctx* ctx);
+int pb_abi_version(void);
+/* Host-wait deadline for blocking calls (default 10000 ms). */
+int pb_set_timeout_ms(pb_ctx* ctx, int timeout_ms);
+/* purebee.js:193-197 SYNC(): wait for all queued work, bounded by the deadline. */
+int pb_sync(pb_ctx* ctx);
+/* The cudaStream_t the context enqueues on, as an opaque pointer. */
+void* pb_stream(pb_ctx* ctx);
+/* Device error word: non-zero once a kernel recorded an error. */
+int pb_device_error(pb_ctx* ctx, int* code_out);
+/* Kernel launches issued by this context so far. */
+int64_t pb_launch_count(pb_ctx* ctx);
+
+/* ------------------------------------------------------------------ */
+/* device memory (memory.js:87-155 PureBeeMemory, now device resident)   */
+/* ------------------------------------------------------------------ */
+
+int pb_malloc(pb_ctx* ctx, size_t bytes, void** dptr);
+int pb_free(pb_ctx* ctx, void* dptr);
+/* memory.js:102-121 write(): host -> device (blocking on completion) */
+int pb_upload(pb_ctx* ctx, void* dst_dev, const void* src_host, size_t bytes);
+/* memory.js:124-128 read(): device -> host (blocking, deadline) */
+int pb_download(pb_ctx* ctx, void* dst_host, const void* src_dev, size_t bytes);
+int pb_memset(pb_ctx* ctx, void* dst_dev, int value, size_t bytes);
+int pb_memcpy_d2d(pb_ctx* ctx, void* dst_dev, const void* src_dev, size_t bytes);
+
+/* ------------------------------------------------------------------ */
+/* quantized matrices resident on the device                            */
+/* ------------------------------------------------------------------ */
+
+/* Upload GGUF blocks of an [N rows][K cols] matrix (K % 32 == 0) and repack
+ * them into the device layout.  type: PB_TYPE_Q4_0, PB_TYPE_Q4_1 or
+ * PB_TYPE_Q8_0.  Replaces the raw cache of streaming-loader.js:119-162 /
+ * 245-262 (raw GGUF bytes kept resident for the Q4 path). */
+int pb_qmat_upload(pb_ctx* ctx, int type, const void* gguf_host, int N, int K, pb_qmat** out);
+/* Same from GGUF bytes already on the device. */
+int pb_qmat_from_device(pb_ctx* ctx, int type, const void* gguf_dev, int N, int K, pb_qmat** out);
+/* Write the matrix back as GGUF bytes (bit-exact round trip). */
+int pb_qmat_download_gguf(pb_ctx* ctx, const pb_qmat* m, void* gguf_host);
+int pb_qmat_free(pb_ctx* ctx, pb_qmat* m);
+int pb_qmat_info(const pb_qmat* m, int* type, int* N, int* K);
+
+/* ------------------------------------------------------------------ */
+/* the Q4 matvec and LM head (wasm-q4.js module API)                    */
+/* ------------------------------------------------------------------ */
+
+/* y[n] = sum_k W[n,k] x[k] over a resident Q4_0 / Q4_1 matrix, with the
+ * f32 lane order of wasm-q4.js:118-267 / 275-435 (bit-exact).  Rows
+ * [row0, row0 + rows) only, so a caller can split rows across devices like
+ * thread-pool.js:165-246; rows <= 0 means all rows. */
+int pb_qmat_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, float* y_dev, int row0, int rows);
+/* wasm-q4.js:716-747 q4_0_matvec(x, rawBuf, N, K): host buffers in and out. */
+int pb_q4_0_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, int N, int K, float* y_host);
+/* wasm-q4.js:758-785 q4_1_matvec(x, rawBuf, N, K) */
+int pb_q4_1_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, int N, int K, float* y_host);
+/* wasm-q4.js:798-839 lmHead(hidden, embData, V, D): f32 row-major table on
+ * the host, batch_dot lane order (wasm-q4.js:447-566). */
+int pb_lm_head(pb_ctx* ctx, const float* h_host, const float* emb_host, int V, int D, float* logits_host);
+/* Head over a resident table (Q4_0 / Q8_0 tiles, dequantized exactly as
+ * gguf.js:239-286 does), batch_dot lane order, fused greedy argmax
+ * (llama-streaming.js:899-909).  argmax_dev may be NULL. */
+int pb_qmat_head(pb_ctx* ctx, const pb_qmat* emb, const float* h_dev, float* logits_dev, int* argmax_dev);
+/* argmax over logits: first index of the strict maximum. */
+int pb_argmax(pb_ctx* ctx, const float* logits_dev, int n, int* idx_dev);
+
+/* ------------------------------------------------------------------ */
+/* engine.js / purebee.js operators on device buffers                   */
+/* ------------------------------------------------------------------ */
+
+/* engine.js:119-167 / 180-244 TENSOR_MUL and LINEAR with f32 weights:
+ * C[M,N] = bias + A[M,K] B[K,N], f32 multiply then add per k in k order
+ * (wasm-simd.js:71-91).  bias_dev may be NULL. */
+int pb_matmul_f32(pb_ctx* ctx, const float* A_dev, int M, int K, const float* B_dev, int N,
+                  const float* bias_dev, float* C_dev);
+/* engine.js:259-269 -> quantize.js:224-266 matmul_q8 (LINEAR on a
+ * QuantizedTensor): W is quantize.js format (a) over a flat [K,N] array. */
+int pb_matmul_q8a(pb_ctx* ctx, const float* A_dev, int M, int K, const float* scales_dev,
+                  const int8_t* q_dev, int N, const float* bias_dev, float* out_dev);
+int pb_rmsnorm(pb_ctx* ctx, const float* x_dev, int seq, int dim, const float* w_dev, double eps,
+               float* out_dev);                                         /* engine.js:429-449 */
+int pb_softmax(pb_ctx* ctx, const float* in_dev, int rows, int cols, float* out_dev); /* engine.js:279-303 */
+int pb_layernorm(pb_ctx* ctx, const float* x_dev, int seq, int dim, const float* w_dev,
+                 const float* b_dev, double eps, float* out_dev);       /* engine.js:315-344 */
+int pb_gelu(pb_ctx* ctx, const float* x_dev, int64_t n, float* out_dev);         /* engine.js:354-360 */
+int pb_silu(pb_ctx* ctx, const float* x_dev, int64_t n, float* out_dev);         /* engine.js:459-463 */
+int pb_elementmul(pb_ctx* ctx, const float* a_dev, const float* b_dev, int64_t n, float* out_dev); /* engine.js:474-484 */
+int pb_tensoradd(pb_ctx* ctx, const float* a_dev, const float* b_dev, int64_t n, float* out_dev);  /* engine.js:96-106 */
+int pb_attention(pb_ctx* ctx, const float* Q_dev, const float* K_dev, const float* V_dev, int seqQ, int seqK,
+                 int dK, int dV, int causal, float* out_dev);           /* engine.js:374-415 */
+/* llama-streaming.js:310-339 _applyRoPE on q [seq, n_heads*hd], k [seq, n_kv*hd] in place */
+int pb_rope(pb_ctx* ctx, float* q_dev, float* k_dev, int seq, int start_pos, int n_heads, int n_kv,
+            int head_dim, double theta);
+/* llama-streaming.js:422-464 / 543-573: attention of seq queries at
+ * start_pos.. over a [seq_len, kv_dim] K/V cache (causal). */
+int pb_attn_cached(pb_ctx* ctx, const float* q_dev, const float* kc_dev, const float* vc_dev, int seq,
+                   int start_pos, int n_heads, int n_kv, int head_dim, float* out_dev);
+/* llama-streaming.js:590-595 fused SiLU(gate)*up */
+int pb_swiglu(pb_ctx* ctx, const float* g_dev, const float* u_dev, int n, float* out_dev);
+
+/* ------------------------------------------------------------------ */
+/* quantizers and decoders                                              */
+/* ------------------------------------------------------------------ */
+
+/* quantize.js:79-109 quantize_q8 / :124-161 quantize_q4 (format (a)) */
+int pb_quantize_q8a(pb_ctx* ctx, const float* x_dev, int64_t n, float* scales_dev, int8_t* q_dev);
+int pb_quantize_q4a(pb_ctx* ctx, const float* x_dev, int64_t n, float* scales_dev, uint8_t* q_dev);
+/* quantize.js:170-208 dequantize_q8 / dequantize_q4 */
+int pb_dequantize_q8a(pb_ctx* ctx, const float* scales_dev, const int8_t* q_dev, int64_t n, float* out_dev);
+int pb_dequantize_q4a(pb_ctx* ctx, const float* scales_dev, const uint8_t* q_dev, int64_t n, float* out_dev);
+/* gguf.js:219-315 loadTensorData for F32/F16/Q4_0/Q4_1/Q8_0 blocks */
+int pb_gguf_dequant(pb_ctx* ctx, int type, const void* raw_dev, int64_t n, float* out_dev);
+/* GGUF Q4_0 / Q8_0 block encoders (not in the reference, which only decodes
+ * GGUF; used to build quantized synthetic models on the device). */
+int pb_gguf_quantize(pb_ctx* ctx, int type, const float* x_dev, int64_t n, void* raw_dev);
+
+/* ------------------------------------------------------------------ */
+/* seeded synthetic inputs                                              */
+/* ------------------------------------------------------------------ */
+
+int pb_synth_weights(pb_ctx* ctx, float* out_dev, int64_t n, uint64_t seed, uint64_t tensor_id, double stdev);
+int pb_synth_activation(pb_ctx* ctx, float* out_dev, int64_t n, uint64_t seed, uint64_t stream);
+int pb_synth_tokens(int* out_host, int n, uint64_t seed, int lo, int hi);
+
+/* ------------------------------------------------------------------ */
+/* the model runtime (llama-streaming.js StreamingLlamaRuntime and       */
+/* llama.js LlamaRuntime)                                               */
+/* ------------------------------------------------------------------ */
+
+#define PB_MODEL_STREAMING_Q4 0 /* GGUF Q4_0 layers (llama-streaming.js) */
+#define PB_MODEL_LLAMA_Q8A 1    /* quantize.js Q8 layers, f32 embedding (llama.js) */
+
+typedef struct pb_model_config {
+  int kind;       /* PB_MODEL_* */
+  int emb_type;   /* PB_TYPE_Q4_0 / PB_TYPE_Q8_0 (streaming) or PB_TYPE_F32 (llama.js) */
+  int dim, hidden_dim, n_layers, n_heads, n_kv_heads, head_dim, vocab, seq_len;
+  double rope_theta;
+  double eps;
+} pb_model_config;
+
+int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model** out);
+int pb_model_free(pb_model* m);
+/* Random-init weights N(0, stdev) from the seed (device generator), norm
+ * gains 1, quantized on the device. */
+int pb_model_init_synthetic(pb_model* m, uint64_t seed, double stdev);
+/* Set / get one tensor.  which: 0 embedding, 1..7 = wq wk wv wo w1 w2 w3,
+ * 8 = attention norm, 9 = ffn norm (layer), 10 = final norm.  Streaming
+ * models take GGUF bytes; llama.js models take (scales f32[], int8 q[])
+ * packed back to back for 1..7 and f32 for the embedding. */
+int pb_model_set_tensor(pb_model* m, int layer, int which, const void* host, size_t bytes);
+int pb_model_get_tensor(pb_model* m, int layer, int which, void* host, size_t bytes);
+/* llama-streaming.js:738-815 / llama.js:204-371 forward(tokens, startPos):
+ * logits of the last position copied to logits_host (may be NULL). */
+int pb_model_forward(pb_model* m, const int* tokens_host, int n, int start_pos, float* logits_host);
+/* One graph-replayed decode step for token `token` at `pos`; writes the
+ * greedy next token (llama-streaming.js:899-909). */
+int pb_model_decode(pb_model* m, int token, int pos, int* next_host, float* logits_host);
+/* llama-streaming.js:914-970 generate(prompt, maxTokens, {greedy, eosId}) */
+int pb_model_generate(pb_model* m, const int* prompt_host, int n_prompt, int max_tokens, int eos_id,
+                      int* out_host, int out_cap, int* n_out);
+/* Device-resident decode loop for timing: `steps` greedy steps starting from
+ * the token already in the model's token slot at `pos0`; tokens stay on the
+ * device (out_dev may be NULL). */
+int pb_model_decode_loop(pb_model* m, int pos0, int steps, int* out_dev);
+int pb_model_set_token(pb_model* m, int token);
+int pb_model_reset_cache(pb_model* m);             /* llama-streaming.js:828-837 */
+int pb_model_rollback_cache(pb_model* m, int pos); /* llama-streaming.js:845-862 */
+int pb_model_kv(pb_model* m, int layer, int which_v, float* host, size_t floats);
+/* Algorithmic bytes one decode step reads at cache length `pos+1`. */
+int64_t pb_model_decode_bytes(const pb_model* m, int pos);
+/* Kernel launches of one decode step. */
+int pb_model_decode_launches(const pb_model* m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

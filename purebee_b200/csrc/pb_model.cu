@@ -1,0 +1,701 @@
+// pb_model.cu - the Llama runtime of llama-streaming.js (GGUF Q4_0 layers)
+// and llama.js (quantize.js Q8 layers) with every tensor resident on the
+// device and the decode step captured in a CUDA graph.
+//
+// Decode step (seq == 1, llama-streaming.js:505-606), per layer:
+//   rmsnorm -> fused [wq; wk; wv] Q4_0 matvec -> RoPE + KV append ->
+//   attention over the cache -> wo matvec (+ residual epilogue) -> rmsnorm ->
+//   fused [w1; w3] matvec -> SwiGLU -> w2 matvec (+ residual epilogue)
+// then the final rmsnorm and the head with the fused argmax.  Position and
+// token live in device memory, so one captured graph replays every step.
+#include <stdio.h>
+#include <string.h>
+
+#include <vector>
+
+#include "pb_internal.cuh"
+#include "pb_synth.h"
+
+// from pb_ops.cu / pb_q4.cu
+void pb_rope_table(double theta, int hd, int start, int n, double2* out);
+int pb_launch_attn_cached(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
+                          int start_pos, const int* pos_dev, int n_heads, int n_kv, int hd, float* out, int max_len);
+int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc);
+__global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
+                          float* __restrict__ out);
+__global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
+                          const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
+                          const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
+                          float* __restrict__ kc, float* __restrict__ vc, int max_len, int* err);
+__global__ void k_glu(const float* __restrict__ g, int g_stride, const float* __restrict__ u, int u_stride, int F,
+                      int mode, float* __restrict__ out);
+__global__ void k_embed(int type, const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc,
+                        const float* __restrict__ f32tiles, int V, int dim, const int* __restrict__ toks,
+                        const unsigned long long* __restrict__ key_dev, int* __restrict__ tok_out,
+                        unsigned long long* __restrict__ key_reset, float* __restrict__ x, int* err);
+__global__ void k_step_end(unsigned long long* __restrict__ key, int* __restrict__ tok_dev, int* __restrict__ pos_dev,
+                           int* __restrict__ hist, int hist_len);
+__global__ void k_elementwise(int op, const float* __restrict__ a, const float* __restrict__ b, int64_t n,
+                              float* __restrict__ out);
+
+struct pb_model {
+  pb_ctx* ctx = nullptr;
+  pb_model_config c{};
+  int kv_dim = 0;
+  // streaming weights
+  pb_qmat* emb = nullptr;                 // Q4_0 / Q8_0 tiles [V][dim]
+  std::vector<pb_qmat*> qkv, wo, gu, w2;  // per layer
+  // llama.js weights
+  float* emb_f32 = nullptr;               // tiles [V/32][dim][32]
+  pb_qmat emb_f32_view;                   // head view of emb_f32
+  std::vector<float*> q8s;                // scales per (layer, which 1..7)
+  std::vector<int8_t*> q8q;
+  // norms and cache
+  float *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr;
+  float *kc = nullptr, *vc = nullptr;
+  double2* rope_tab = nullptr;
+  // activations (sized for max_m rows)
+  int max_m = 0;
+  float *x = nullptr, *xn = nullptr, *qkvo = nullptr, *att = nullptr, *guo = nullptr, *hb = nullptr, *proj = nullptr,
+        *logits = nullptr;
+  int* toks = nullptr;
+  int* tok_dev = nullptr;  // [0] token, [1] position
+  int* hist = nullptr;     // greedy tokens by position
+  unsigned long long* key = nullptr;
+  // decode graph
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int launches_per_step = 0;
+  float* h_logits_pinned = nullptr;
+  int* h_io_pinned = nullptr;
+};
+
+static size_t kv_floats(const pb_model* m) { return (size_t)m->c.n_layers * m->c.seq_len * m->kv_dim; }
+static float* kcache(pb_model* m, int l) { return m->kc + (size_t)l * m->c.seq_len * m->kv_dim; }
+static float* vcache(pb_model* m, int l) { return m->vc + (size_t)l * m->c.seq_len * m->kv_dim; }
+
+// matrix shape (rows = outputs, cols = inputs) of tensor `which` (1..7)
+static void mshape(const pb_model_config& c, int which, int* rows, int* cols) {
+  int kv = c.n_kv_heads * c.head_dim;
+  switch (which) {
+    case 1: *rows = c.dim; *cols = c.dim; break;
+    case 2: case 3: *rows = kv; *cols = c.dim; break;
+    case 4: *rows = c.dim; *cols = c.dim; break;
+    case 5: case 7: *rows = c.hidden_dim; *cols = c.dim; break;
+    default: *rows = c.dim; *cols = c.hidden_dim; break;
+  }
+}
+
+static void free_graph(pb_model* m);
+
+static int ensure_act(pb_model* m, int M) {
+  if (M <= m->max_m) return PB_OK;
+  pb_ctx* ctx = m->ctx;
+  PB_TRY(pb_wait(ctx));
+  free_graph(m);  // a captured graph holds the old buffer addresses
+  cudaFree(m->x); cudaFree(m->xn); cudaFree(m->qkvo); cudaFree(m->att); cudaFree(m->guo); cudaFree(m->hb);
+  cudaFree(m->proj); cudaFree(m->toks);
+  const pb_model_config& c = m->c;
+  size_t qkvw = (size_t)c.dim + 2 * m->kv_dim;
+  PB_TRY_CUDA(ctx, cudaMalloc(&m->x, (size_t)M * c.dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&m->xn, (size_t)M * c.dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&m->qkvo, (size_t)M * qkvw * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&m->att, (size_t)M * c.dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&m->guo, (size_t)M * 2 * c.hidden_dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&m->hb, (size_t)M * c.hidden_dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&m->proj, (size_t)M * c.dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&m->toks, (size_t)M * 4));
+  m->max_m = M;
+  return PB_OK;
+}
+
+static void free_graph(pb_model* m) {
+  if (m->exec) cudaGraphExecDestroy(m->exec);
+  if (m->graph) cudaGraphDestroy(m->graph);
+  m->exec = nullptr;
+  m->graph = nullptr;
+}
+
+extern "C" int pb_model_free(pb_model* m) {
+  if (!m) return PB_OK;
+  pb_ctx* ctx = m->ctx;
+  if (ctx) pb_wait(ctx);
+  free_graph(m);
+  pb_qmat_free(nullptr, m->emb);
+  for (auto* p : m->qkv) pb_qmat_free(nullptr, p);
+  for (auto* p : m->wo) pb_qmat_free(nullptr, p);
+  for (auto* p : m->gu) pb_qmat_free(nullptr, p);
+  for (auto* p : m->w2) pb_qmat_free(nullptr, p);
+  for (auto* p : m->q8s) cudaFree(p);
+  for (auto* p : m->q8q) cudaFree(p);
+  cudaFree(m->emb_f32);
+  cudaFree(m->rms_att); cudaFree(m->rms_ffn); cudaFree(m->rms_final);
+  cudaFree(m->kc); cudaFree(m->vc); cudaFree(m->rope_tab);
+  cudaFree(m->x); cudaFree(m->xn); cudaFree(m->qkvo); cudaFree(m->att); cudaFree(m->guo); cudaFree(m->hb);
+  cudaFree(m->proj); cudaFree(m->logits); cudaFree(m->toks); cudaFree(m->tok_dev); cudaFree(m->hist);
+  cudaFree(m->key);
+  if (m->h_logits_pinned) cudaFreeHost(m->h_logits_pinned);
+  if (m->h_io_pinned) cudaFreeHost(m->h_io_pinned);
+  delete m;
+  return PB_OK;
+}
+
+__global__ void k_fill(float* p, int64_t n, float v) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = v;
+}
+
+extern "C" int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model** out) {
+  if (!ctx || !cfg || !out) return PB_ERR_ARG;
+  *out = nullptr;
+  const pb_model_config& c = *cfg;
+  if (c.dim <= 0 || c.hidden_dim <= 0 || c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim <= 0 ||
+      c.vocab <= 0 || c.seq_len <= 0 || c.n_heads % c.n_kv_heads || c.n_heads * c.head_dim != c.dim ||
+      (c.head_dim & 1) || c.dim % 32 || c.hidden_dim % 32 || (c.n_kv_heads * c.head_dim) % 32)
+    return pb_set_error(ctx, PB_ERR_ARG, "invalid model config");
+  if (c.kind != PB_MODEL_STREAMING_Q4 && c.kind != PB_MODEL_LLAMA_Q8A)
+    return pb_set_error(ctx, PB_ERR_ARG, "unknown model kind %d", c.kind);
+  if (c.kind == PB_MODEL_STREAMING_Q4 && c.emb_type != PB_TYPE_Q4_0 && c.emb_type != PB_TYPE_Q8_0)
+    return pb_set_error(ctx, PB_ERR_ARG, "streaming models take a Q4_0 or Q8_0 embedding");
+  if (c.kind == PB_MODEL_LLAMA_Q8A && c.emb_type != PB_TYPE_F32)
+    return pb_set_error(ctx, PB_ERR_ARG, "llama.js models take an f32 embedding");
+  pb_model* m = new pb_model();
+  m->ctx = ctx;
+  m->c = c;
+  m->kv_dim = c.n_kv_heads * c.head_dim;
+  int rc = PB_OK;
+  auto fail = [&](int code) { pb_model_free(m); return code; };
+  const int L = c.n_layers;
+  if (c.kind == PB_MODEL_STREAMING_Q4) {
+    rc = pb_qmat_alloc(ctx, c.emb_type, c.vocab, c.dim, &m->emb);
+    if (rc) return fail(rc);
+    m->qkv.assign(L, nullptr); m->wo.assign(L, nullptr); m->gu.assign(L, nullptr); m->w2.assign(L, nullptr);
+    for (int l = 0; l < L; ++l) {
+      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, c.dim + 2 * m->kv_dim, c.dim, &m->qkv[l]))) return fail(rc);
+      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, c.dim, c.dim, &m->wo[l]))) return fail(rc);
+      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, 2 * c.hidden_dim, c.dim, &m->gu[l]))) return fail(rc);
+      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, c.dim, c.hidden_dim, &m->w2[l]))) return fail(rc);
+    }
+  } else {
+    size_t ntile = (size_t)((c.vocab + 31) / 32) * 32;
+    if (cudaMalloc(&m->emb_f32, ntile * c.dim * 4) != cudaSuccess) return fail(pb_set_error(ctx, PB_ERR_OOM, "embedding"));
+    cudaMemsetAsync(m->emb_f32, 0, ntile * c.dim * 4, ctx->stream);
+    m->emb_f32_view.type = PB_TYPE_F32;
+    m->emb_f32_view.N = c.vocab;
+    m->emb_f32_view.K = c.dim;
+    m->emb_f32_view.N_pad = (int)ntile;
+    m->emb_f32_view.nb = c.dim / 32;
+    m->emb_f32_view.qs = (uint8_t*)m->emb_f32;
+    m->q8s.assign((size_t)L * 7, nullptr);
+    m->q8q.assign((size_t)L * 7, nullptr);
+    for (int l = 0; l < L; ++l)
+      for (int w = 1; w <= 7; ++w) {
+        int r, k;
+        mshape(c, w, &r, &k);
+        int64_t n = (int64_t)r * k, nblk = (n + 31) / 32;
+        if (cudaMalloc(&m->q8s[l * 7 + w - 1], nblk * 4) != cudaSuccess ||
+            cudaMalloc(&m->q8q[l * 7 + w - 1], nblk * 32) != cudaSuccess)
+          return fail(pb_set_error(ctx, PB_ERR_OOM, "Q8 weights"));
+      }
+  }
+  size_t nd = (size_t)L * c.dim;
+  if (cudaMalloc(&m->rms_att, nd * 4) || cudaMalloc(&m->rms_ffn, nd * 4) || cudaMalloc(&m->rms_final, c.dim * 4) ||
+      cudaMalloc(&m->kc, kv_floats(m) * 4) || cudaMalloc(&m->vc, kv_floats(m) * 4) ||
+      cudaMalloc(&m->logits, (size_t)c.vocab * 4) || cudaMalloc(&m->tok_dev, 16) ||
+      cudaMalloc(&m->hist, (size_t)(c.seq_len + 1) * 4) || cudaMalloc(&m->key, 16) ||
+      cudaMalloc(&m->rope_tab, (size_t)c.seq_len * (c.head_dim / 2) * sizeof(double2)))
+    return fail(pb_set_error(ctx, PB_ERR_OOM, "model buffers"));
+  k_fill<<<pb_cdiv(nd, 256), 256, 0, ctx->stream>>>(m->rms_att, nd, 1.0f);
+  k_fill<<<pb_cdiv(nd, 256), 256, 0, ctx->stream>>>(m->rms_ffn, nd, 1.0f);
+  k_fill<<<pb_cdiv(c.dim, 256), 256, 0, ctx->stream>>>(m->rms_final, c.dim, 1.0f);
+  cudaMemsetAsync(m->kc, 0, kv_floats(m) * 4, ctx->stream);
+  cudaMemsetAsync(m->vc, 0, kv_floats(m) * 4, ctx->stream);
+  cudaMemsetAsync(m->key, 0, 16, ctx->stream);
+  cudaMemsetAsync(m->tok_dev, 0, 16, ctx->stream);
+  cudaMemsetAsync(m->hist, 0, (size_t)(c.seq_len + 1) * 4, ctx->stream);
+  // RoPE rotation table built on the host as the reference builds it
+  std::vector<double2> tab((size_t)c.seq_len * (c.head_dim / 2));
+  pb_rope_table(c.rope_theta, c.head_dim, 0, c.seq_len, tab.data());
+  cudaMemcpyAsync(m->rope_tab, tab.data(), tab.size() * sizeof(double2), cudaMemcpyHostToDevice, ctx->stream);
+  if (cudaMallocHost(&m->h_logits_pinned, (size_t)c.vocab * 4) != cudaSuccess ||
+      cudaMallocHost(&m->h_io_pinned, 64) != cudaSuccess)
+    return fail(pb_set_error(ctx, PB_ERR_OOM, "pinned buffers"));
+  if ((rc = ensure_act(m, 1))) return fail(rc);
+  if ((rc = pb_wait(ctx))) return fail(rc);
+  *out = m;
+  return PB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// weights
+// ---------------------------------------------------------------------------
+
+// Row offset of tensor `which` inside its fused matrix.
+static pb_qmat* fused_target(pb_model* m, int l, int which, int* row_off) {
+  const pb_model_config& c = m->c;
+  switch (which) {
+    case 1: *row_off = 0; return m->qkv[l];
+    case 2: *row_off = c.dim; return m->qkv[l];
+    case 3: *row_off = c.dim + m->kv_dim; return m->qkv[l];
+    case 4: *row_off = 0; return m->wo[l];
+    case 5: *row_off = 0; return m->gu[l];
+    case 7: *row_off = c.hidden_dim; return m->gu[l];
+    default: *row_off = 0; return m->w2[l];
+  }
+}
+
+// GGUF rows -> tiles at a row offset of an existing matrix
+__global__ void k_pack_rows(const uint8_t* __restrict__ src, int rows, int row_off, int nb, int type,
+                            uint8_t* __restrict__ qs, uint16_t* __restrict__ d, int unpack) {
+  int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (int64_t)rows * nb) return;
+  int n = (int)(t / nb) + row_off, b = (int)(t % nb);
+  int bb = type == PB_TYPE_Q4_0 ? 18 : 34, pl = type == PB_TYPE_Q4_0 ? 16 : 32;
+  uint8_t* g = (uint8_t*)src + t * bb;
+  int64_t slot = ((int64_t)(n >> 5) * nb + b) * 32 + (n & 31);
+  if (!unpack) {
+    d[slot] = (uint16_t)(g[0] | (g[1] << 8));
+    for (int i = 0; i < pl; ++i) qs[slot * pl + i] = g[2 + i];
+  } else {
+    g[0] = (uint8_t)(d[slot] & 0xff);
+    g[1] = (uint8_t)(d[slot] >> 8);
+    for (int i = 0; i < pl; ++i) g[2 + i] = qs[slot * pl + i];
+  }
+}
+
+// row-major f32 [V][dim] <-> tiles [V/32][dim][32]
+__global__ void k_tile_f32(const float* __restrict__ src, int V, int dim, float* __restrict__ tiles, int untile) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)V * dim) return;
+  int v = (int)(i / dim), d = (int)(i % dim);
+  size_t t = ((size_t)(v >> 5) * dim + d) * 32 + (v & 31);
+  if (!untile) tiles[t] = src[i];
+  else ((float*)src)[i] = tiles[t];
+}
+
+static int pack_rows(pb_model* m, pb_qmat* dst, const void* gguf_dev, int rows, int row_off) {
+  pb_ctx* ctx = m->ctx;
+  int64_t tot = (int64_t)rows * dst->nb;
+  k_pack_rows<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>((const uint8_t*)gguf_dev, rows, row_off, dst->nb, dst->type,
+                                                          dst->qs, dst->d, 0);
+  PB_LAUNCHED(ctx, "k_pack_rows");
+  return PB_OK;
+}
+
+extern "C" int pb_model_init_synthetic(pb_model* m, uint64_t seed, double stdev) {
+  if (!m) return PB_ERR_ARG;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  free_graph(m);
+  // largest tensor: embedding or an FFN matrix
+  int64_t ne = (int64_t)c.vocab * c.dim;
+  int64_t nf = (int64_t)c.hidden_dim * c.dim;
+  int64_t nmax = ne > nf ? ne : nf;
+  float* tmp = nullptr;
+  uint8_t* gg = nullptr;
+  PB_TRY_CUDA(ctx, cudaMalloc(&tmp, nmax * 4));
+  int rc = PB_OK;
+  if (cudaMalloc(&gg, nmax / 32 * 34 + 64) != cudaSuccess) {
+    cudaFree(tmp);
+    return pb_set_error(ctx, PB_ERR_OOM, "synthetic init buffer");
+  }
+  auto gen = [&](uint64_t tid, int64_t n) { return pb_synth_weights(ctx, tmp, n, seed, tid, stdev); };
+  // embedding (tensor id 0)
+  if ((rc = gen(0, ne))) goto done;
+  if (c.kind == PB_MODEL_STREAMING_Q4) {
+    if ((rc = pb_gguf_quantize(ctx, c.emb_type, tmp, ne, gg))) goto done;
+    if ((rc = pack_rows(m, m->emb, gg, c.vocab, 0))) goto done;
+  } else {
+    k_tile_f32<<<pb_cdiv(ne, 256), 256, 0, ctx->stream>>>(tmp, c.vocab, c.dim, m->emb_f32, 0);
+    if ((rc = pb_check_launch(ctx, "k_tile_f32"))) goto done;
+  }
+  for (int l = 0; l < c.n_layers; ++l)
+    for (int w = 1; w <= 7; ++w) {
+      int r, k;
+      mshape(c, w, &r, &k);
+      int64_t n = (int64_t)r * k;
+      if ((rc = gen(1 + 7 * (uint64_t)l + (w - 1), n))) goto done;
+      if (c.kind == PB_MODEL_STREAMING_Q4) {
+        if ((rc = pb_gguf_quantize(ctx, PB_TYPE_Q4_0, tmp, n, gg))) goto done;
+        int off;
+        pb_qmat* dst = fused_target(m, l, w, &off);
+        if ((rc = pack_rows(m, dst, gg, r, off))) goto done;
+      } else {
+        if ((rc = pb_quantize_q8a(ctx, tmp, n, m->q8s[l * 7 + w - 1], m->q8q[l * 7 + w - 1]))) goto done;
+      }
+    }
+  rc = pb_wait(ctx);
+done:
+  cudaStreamSynchronize(ctx->stream);
+  cudaFree(tmp);
+  cudaFree(gg);
+  return rc;
+}
+
+static size_t tensor_bytes(const pb_model* m, int which) {
+  const pb_model_config& c = m->c;
+  if (which >= 8) return (size_t)c.dim * 4;
+  if (which == 0) {
+    int64_t ne = (int64_t)c.vocab * c.dim;
+    if (c.kind == PB_MODEL_LLAMA_Q8A) return (size_t)ne * 4;
+    return (size_t)(ne / 32) * (c.emb_type == PB_TYPE_Q4_0 ? 18 : 34);
+  }
+  int r, k;
+  mshape(c, which, &r, &k);
+  int64_t n = (int64_t)r * k;
+  if (c.kind == PB_MODEL_STREAMING_Q4) return (size_t)(n / 32) * 18;
+  int64_t nb = (n + 31) / 32;
+  return (size_t)(nb * 4 + nb * 32);
+}
+
+static int model_tensor_io(pb_model* m, int layer, int which, void* host, size_t bytes, int get) {
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  if (which < 0 || which > 10 || (which >= 1 && which <= 9 && (layer < 0 || layer >= c.n_layers)))
+    return pb_set_error(ctx, PB_ERR_ARG, "bad tensor (layer %d, which %d)", layer, which);
+  size_t need = tensor_bytes(m, which);
+  if (bytes != need) return pb_set_error(ctx, PB_ERR_ARG, "tensor %d needs %zu bytes, got %zu", which, need, bytes);
+  if (!get) free_graph(m);
+  if (which >= 8) {
+    float* p = which == 8 ? m->rms_att + (size_t)layer * c.dim : which == 9 ? m->rms_ffn + (size_t)layer * c.dim
+                                                                            : m->rms_final;
+    return get ? pb_download(ctx, host, p, bytes) : pb_upload(ctx, p, host, bytes);
+  }
+  if (c.kind == PB_MODEL_LLAMA_Q8A && which >= 1) {
+    int64_t nb = (int64_t)(bytes / 36);
+    float* s = m->q8s[layer * 7 + which - 1];
+    int8_t* q = m->q8q[layer * 7 + which - 1];
+    if (get) {
+      PB_TRY(pb_download(ctx, host, s, nb * 4));
+      return pb_download(ctx, (char*)host + nb * 4, q, nb * 32);
+    }
+    PB_TRY(pb_upload(ctx, s, host, nb * 4));
+    return pb_upload(ctx, q, (const char*)host + nb * 4, nb * 32);
+  }
+  PB_TRY(pb_ensure_scratch(ctx, bytes));
+  if (c.kind == PB_MODEL_LLAMA_Q8A) {  // f32 embedding
+    int64_t ne = (int64_t)c.vocab * c.dim;
+    if (!get) PB_TRY_CUDA(ctx, cudaMemcpyAsync(ctx->scratch, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    k_tile_f32<<<pb_cdiv(ne, 256), 256, 0, ctx->stream>>>((float*)ctx->scratch, c.vocab, c.dim, m->emb_f32, get);
+    PB_LAUNCHED(ctx, "k_tile_f32");
+    if (get) PB_TRY_CUDA(ctx, cudaMemcpyAsync(host, ctx->scratch, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    return pb_wait(ctx);
+  }
+  pb_qmat* dst;
+  int rows, off = 0;
+  if (which == 0) {
+    dst = m->emb;
+    rows = c.vocab;
+  } else {
+    int k;
+    mshape(c, which, &rows, &k);
+    dst = fused_target(m, layer, which, &off);
+  }
+  if (!get) PB_TRY_CUDA(ctx, cudaMemcpyAsync(ctx->scratch, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  int64_t tot = (int64_t)rows * dst->nb;
+  k_pack_rows<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>((const uint8_t*)ctx->scratch, rows, off, dst->nb, dst->type,
+                                                          dst->qs, dst->d, get);
+  PB_LAUNCHED(ctx, "k_pack_rows");
+  if (get) PB_TRY_CUDA(ctx, cudaMemcpyAsync(host, ctx->scratch, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  return pb_wait(ctx);
+}
+
+extern "C" int pb_model_set_tensor(pb_model* m, int layer, int which, const void* host, size_t bytes) {
+  if (!m || !host) return PB_ERR_ARG;
+  return model_tensor_io(m, layer, which, (void*)host, bytes, 0);
+}
+extern "C" int pb_model_get_tensor(pb_model* m, int layer, int which, void* host, size_t bytes) {
+  if (!m || !host) return PB_ERR_ARG;
+  return model_tensor_io(m, layer, which, host, bytes, 1);
+}
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+
+static int launch_norm(pb_model* m, const float* x, int M, const float* w, float* out) {
+  k_rmsnorm<<<M, 256, 0, m->ctx->stream>>>(x, m->c.dim, w, m->c.eps, out);
+  PB_LAUNCHED(m->ctx, "k_rmsnorm");
+  return PB_OK;
+}
+
+static int launch_q8a(pb_model* m, int l, int which, const float* A, int M, float* out) {
+  int r, k;
+  mshape(m->c, which, &r, &k);
+  return pb_matmul_q8a(m->ctx, A, M, k, m->q8s[l * 7 + which - 1], m->q8q[l * 7 + which - 1], r, nullptr, out);
+}
+
+// One layer for M rows at start_pos (or *pos_dev when `dev_pos`).
+static int run_layer(pb_model* m, int l, int M, int start_pos, bool dev_pos) {
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  const int dim = c.dim, F = c.hidden_dim, kv = m->kv_dim;
+  const int qkvw = dim + 2 * kv;
+  const int* pos_dev = dev_pos ? m->tok_dev + 1 : nullptr;
+  PB_TRY(launch_norm(m, m->x, M, m->rms_att + (size_t)l * dim, m->xn));
+  float *q, *k, *v;
+  int qs_, ks_, vs_;
+  if (c.kind == PB_MODEL_STREAMING_Q4) {
+    if (M == 1) PB_TRY(pb_launch_matvec(ctx, m->qkv[l], m->xn, m->qkvo, 0, qkvw, nullptr));
+    else PB_TRY(pb_launch_prefill_q4(ctx, m->qkv[l], m->xn, dim, M, m->qkvo, qkvw));
+    q = m->qkvo; k = m->qkvo + dim; v = m->qkvo + dim + kv;
+    qs_ = ks_ = vs_ = qkvw;
+  } else {
+    q = m->qkvo; k = m->qkvo + (size_t)M * dim; v = k + (size_t)M * kv;
+    qs_ = dim; ks_ = kv; vs_ = kv;
+    PB_TRY(launch_q8a(m, l, 1, m->xn, M, q));
+    PB_TRY(launch_q8a(m, l, 2, m->xn, M, k));
+    PB_TRY(launch_q8a(m, l, 3, m->xn, M, v));
+  }
+  {
+    int tot = (c.n_heads + c.n_kv_heads) * (c.head_dim / 2) + kv;
+    k_rope_kv<<<dim3(pb_cdiv(tot, 128), M), 128, 0, ctx->stream>>>(q, qs_, k, ks_, v, vs_, c.n_heads, c.n_kv_heads,
+                                                                   c.head_dim, m->rope_tab, start_pos, pos_dev,
+                                                                   kcache(m, l), vcache(m, l), c.seq_len, ctx->d_err);
+    PB_LAUNCHED(ctx, "k_rope_kv");
+  }
+  PB_TRY(pb_launch_attn_cached(ctx, q, qs_, kcache(m, l), vcache(m, l), M, start_pos, pos_dev, c.n_heads,
+                               c.n_kv_heads, c.head_dim, m->att, c.seq_len));
+  // output projection + residual
+  if (c.kind == PB_MODEL_STREAMING_Q4) {
+    if (M == 1) {
+      PB_TRY(pb_launch_matvec(ctx, m->wo[l], m->att, m->x, 0, dim, m->x));
+    } else {
+      PB_TRY(pb_launch_prefill_q4(ctx, m->wo[l], m->att, dim, M, m->proj, dim));
+      k_elementwise<<<pb_cdiv((int64_t)M * dim, 256), 256, 0, ctx->stream>>>(0, m->x, m->proj, (int64_t)M * dim, m->x);
+      PB_LAUNCHED(ctx, "k_elementwise");
+    }
+  } else {
+    PB_TRY(launch_q8a(m, l, 4, m->att, M, m->proj));
+    k_elementwise<<<pb_cdiv((int64_t)M * dim, 256), 256, 0, ctx->stream>>>(0, m->x, m->proj, (int64_t)M * dim, m->x);
+    PB_LAUNCHED(ctx, "k_elementwise");
+  }
+  PB_TRY(launch_norm(m, m->x, M, m->rms_ffn + (size_t)l * dim, m->xn));
+  // FFN
+  const float *g, *u;
+  int gs, us, mode;
+  if (c.kind == PB_MODEL_STREAMING_Q4) {
+    if (M == 1) PB_TRY(pb_launch_matvec(ctx, m->gu[l], m->xn, m->guo, 0, 2 * F, nullptr));
+    else PB_TRY(pb_launch_prefill_q4(ctx, m->gu[l], m->xn, dim, M, m->guo, 2 * F));
+    g = m->guo; u = m->guo + F; gs = us = 2 * F;
+    mode = M == 1 ? 0 : 1;  // decode fuses SiLU*up; prefill is SILU then ELEMENT_MUL
+  } else {
+    PB_TRY(launch_q8a(m, l, 5, m->xn, M, m->guo));
+    PB_TRY(launch_q8a(m, l, 7, m->xn, M, m->guo + (size_t)M * F));
+    g = m->guo; u = m->guo + (size_t)M * F; gs = us = F;
+    mode = 1;
+  }
+  k_glu<<<dim3(pb_cdiv(F, 256), M), 256, 0, ctx->stream>>>(g, gs, u, us, F, mode, m->hb);
+  PB_LAUNCHED(ctx, "k_glu");
+  if (c.kind == PB_MODEL_STREAMING_Q4) {
+    if (M == 1) {
+      PB_TRY(pb_launch_matvec(ctx, m->w2[l], m->hb, m->x, 0, dim, m->x));
+    } else {
+      PB_TRY(pb_launch_prefill_q4(ctx, m->w2[l], m->hb, F, M, m->proj, dim));
+      k_elementwise<<<pb_cdiv((int64_t)M * dim, 256), 256, 0, ctx->stream>>>(0, m->x, m->proj, (int64_t)M * dim, m->x);
+      PB_LAUNCHED(ctx, "k_elementwise");
+    }
+  } else {
+    PB_TRY(launch_q8a(m, l, 6, m->hb, M, m->proj));
+    k_elementwise<<<pb_cdiv((int64_t)M * dim, 256), 256, 0, ctx->stream>>>(0, m->x, m->proj, (int64_t)M * dim, m->x);
+    PB_LAUNCHED(ctx, "k_elementwise");
+  }
+  return PB_OK;
+}
+
+static int launch_embed(pb_model* m, const int* toks, int M) {
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  dim3 grid(pb_cdiv(c.dim, 256), M);
+  if (c.kind == PB_MODEL_STREAMING_Q4)
+    k_embed<<<grid, 256, 0, ctx->stream>>>(c.emb_type, m->emb->qs, m->emb->d, nullptr, c.vocab, c.dim, toks, nullptr,
+                                           nullptr, nullptr, m->x, ctx->d_err);
+  else
+    k_embed<<<grid, 256, 0, ctx->stream>>>(PB_TYPE_F32, nullptr, nullptr, m->emb_f32, c.vocab, c.dim, toks, nullptr,
+                                           nullptr, nullptr, m->x, ctx->d_err);
+  PB_LAUNCHED(ctx, "k_embed");
+  return PB_OK;
+}
+
+static int launch_head(pb_model* m, const float* last_x) {
+  pb_ctx* ctx = m->ctx;
+  PB_TRY(launch_norm(m, last_x, 1, m->rms_final, m->xn));
+  if (m->c.kind == PB_MODEL_STREAMING_Q4) return pb_launch_head(ctx, m->emb, m->xn, m->logits, m->key, 0);
+  return pb_launch_head(ctx, &m->emb_f32_view, m->xn, m->logits, m->key, 1);
+}
+
+// Enqueue one decode step that reads token and position from m->tok_dev.
+static int enqueue_decode_step(pb_model* m) {
+  pb_ctx* ctx = m->ctx;
+  PB_TRY(launch_embed(m, m->tok_dev, 1));
+  for (int l = 0; l < m->c.n_layers; ++l) PB_TRY(run_layer(m, l, 1, 0, true));
+  PB_TRY(launch_head(m, m->x));
+  k_step_end<<<1, 32, 0, ctx->stream>>>(m->key, m->tok_dev, m->tok_dev + 1, m->hist, m->c.seq_len + 1);
+  PB_LAUNCHED(ctx, "k_step_end");
+  return PB_OK;
+}
+
+static int ensure_graph(pb_model* m) {
+  if (m->exec) return PB_OK;
+  pb_ctx* ctx = m->ctx;
+  PB_TRY(ensure_act(m, 1));
+  int64_t before = ctx->launches;
+  PB_TRY_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_decode_step(m);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+  if (rc != PB_OK) { if (g) cudaGraphDestroy(g); return rc; }
+  if (e != cudaSuccess) return pb_cuda_error(ctx, e, "decode graph capture");
+  m->launches_per_step = (int)(ctx->launches - before);
+  e = cudaGraphInstantiate(&m->exec, g, 0);
+  if (e != cudaSuccess) { cudaGraphDestroy(g); return pb_cuda_error(ctx, e, "decode graph instantiate"); }
+  m->graph = g;
+  return PB_OK;
+}
+
+extern "C" int pb_model_forward(pb_model* m, const int* tokens, int n, int start_pos, float* logits_host) {
+  if (!m || !tokens || n <= 0) return PB_ERR_ARG;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  if (start_pos < 0 || start_pos + n > c.seq_len)
+    return pb_set_error(ctx, PB_ERR_ARG, "positions [%d, %d) exceed the cache length %d", start_pos, start_pos + n, c.seq_len);
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= c.vocab) return pb_set_error(ctx, PB_ERR_ARG, "token %d out of range", tokens[i]);
+  if (n == 1) {  // the graph-captured decode step
+    int next;
+    return pb_model_decode(m, tokens[0], start_pos, &next, logits_host);
+  }
+  PB_TRY(ensure_act(m, n));
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->toks, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
+  PB_TRY(launch_embed(m, m->toks, n));
+  for (int l = 0; l < c.n_layers; ++l) PB_TRY(run_layer(m, l, n, start_pos, false));
+  PB_TRY(launch_head(m, m->x + (size_t)(n - 1) * c.dim));
+  // leave the greedy token in the token slot, as a decode step would
+  m->h_io_pinned[0] = 0;
+  k_step_end<<<1, 32, 0, ctx->stream>>>(m->key, m->tok_dev, m->tok_dev + 1, nullptr, 0);
+  PB_LAUNCHED(ctx, "k_step_end");
+  if (logits_host) PB_TRY_CUDA(ctx, cudaMemcpyAsync(logits_host, m->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  PB_TRY(pb_wait(ctx));
+  // position after the prompt
+  int io[2] = {0, start_pos + n};
+  PB_TRY_CUDA(ctx, cudaMemcpy(io, m->tok_dev, 4, cudaMemcpyDeviceToHost));
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->tok_dev + 1, &io[1], 4, cudaMemcpyHostToDevice, ctx->stream));
+  return pb_wait(ctx);
+}
+
+extern "C" int pb_model_decode(pb_model* m, int token, int pos, int* next_host, float* logits_host) {
+  if (!m) return PB_ERR_ARG;
+  pb_ctx* ctx = m->ctx;
+  if (pos < 0 || pos >= m->c.seq_len) return pb_set_error(ctx, PB_ERR_ARG, "position %d outside the cache", pos);
+  if (token < 0 || token >= m->c.vocab) return pb_set_error(ctx, PB_ERR_ARG, "token %d out of range", token);
+  PB_TRY(ensure_graph(m));
+  m->h_io_pinned[0] = token;
+  m->h_io_pinned[1] = pos;
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->tok_dev, m->h_io_pinned, 8, cudaMemcpyHostToDevice, ctx->stream));
+  PB_TRY_CUDA(ctx, cudaGraphLaunch(m->exec, ctx->stream));
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->h_io_pinned + 2, m->tok_dev, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (logits_host)
+    PB_TRY_CUDA(ctx, cudaMemcpyAsync(logits_host, m->logits, (size_t)m->c.vocab * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  PB_TRY(pb_wait(ctx));
+  if (next_host) *next_host = m->h_io_pinned[2];
+  return PB_OK;
+}
+
+extern "C" int pb_model_set_token(pb_model* m, int token) {
+  if (!m) return PB_ERR_ARG;
+  if (token < 0 || token >= m->c.vocab) return pb_set_error(m->ctx, PB_ERR_ARG, "token %d out of range", token);
+  m->h_io_pinned[0] = token;
+  PB_TRY_CUDA(m->ctx, cudaMemcpyAsync(m->tok_dev, m->h_io_pinned, 4, cudaMemcpyHostToDevice, m->ctx->stream));
+  return pb_wait(m->ctx);
+}
+
+extern "C" int pb_model_decode_loop(pb_model* m, int pos0, int steps, int* out_dev) {
+  if (!m || steps < 0) return PB_ERR_ARG;
+  pb_ctx* ctx = m->ctx;
+  if (pos0 < 0 || pos0 + steps > m->c.seq_len)
+    return pb_set_error(ctx, PB_ERR_ARG, "positions [%d, %d) exceed the cache length", pos0, pos0 + steps);
+  PB_TRY(ensure_graph(m));
+  m->h_io_pinned[4] = pos0;
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->tok_dev + 1, &m->h_io_pinned[4], 4, cudaMemcpyHostToDevice, ctx->stream));
+  for (int s = 0; s < steps; ++s) PB_TRY_CUDA(ctx, cudaGraphLaunch(m->exec, ctx->stream));
+  if (out_dev && steps)
+    PB_TRY_CUDA(ctx, cudaMemcpyAsync(out_dev, m->hist + pos0 + 1, (size_t)steps * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  return PB_OK;  // asynchronous: pb_sync() waits
+}
+
+extern "C" int pb_model_generate(pb_model* m, const int* prompt, int n_prompt, int max_tokens, int eos_id, int* out,
+                                 int cap, int* n_out) {
+  if (!m || !prompt || n_prompt <= 0 || !out || cap <= 0) return PB_ERR_ARG;
+  if (n_out) *n_out = 0;
+  PB_TRY(pb_model_reset_cache(m));
+  int cnt = 0;
+  for (int i = 0; i < n_prompt && cnt < cap; ++i) out[cnt++] = prompt[i];
+  int next = 0;
+  if (n_prompt == 1) {
+    PB_TRY(pb_model_decode(m, prompt[0], 0, &next, nullptr));
+  } else {
+    PB_TRY(pb_model_forward(m, prompt, n_prompt, 0, nullptr));
+    PB_TRY_CUDA(m->ctx, cudaMemcpy(&next, m->tok_dev, 4, cudaMemcpyDeviceToHost));
+  }
+  int pos = n_prompt;
+  if (cnt < cap) out[cnt++] = next;
+  for (int i = 1; i < max_tokens; ++i) {
+    if (next == eos_id) break;
+    if (pos >= m->c.seq_len) break;
+    int nx;
+    PB_TRY(pb_model_decode(m, next, pos, &nx, nullptr));
+    pos++;
+    next = nx;
+    if (cnt < cap) out[cnt++] = next;
+    if (next == eos_id) break;
+  }
+  if (n_out) *n_out = cnt;
+  return PB_OK;
+}
+
+extern "C" int pb_model_reset_cache(pb_model* m) {
+  if (!m) return PB_ERR_ARG;
+  pb_ctx* ctx = m->ctx;
+  PB_TRY_CUDA(ctx, cudaMemsetAsync(m->kc, 0, kv_floats(m) * 4, ctx->stream));
+  PB_TRY_CUDA(ctx, cudaMemsetAsync(m->vc, 0, kv_floats(m) * 4, ctx->stream));
+  return pb_wait(ctx);
+}
+
+extern "C" int pb_model_rollback_cache(pb_model* m, int pos) {
+  if (!m) return PB_ERR_ARG;
+  pb_ctx* ctx = m->ctx;
+  if (pos < 0) pos = 0;
+  if (pos >= m->c.seq_len) return PB_OK;
+  size_t rowb = (size_t)m->kv_dim * 4;
+  for (int l = 0; l < m->c.n_layers; ++l) {
+    PB_TRY_CUDA(ctx, cudaMemsetAsync(kcache(m, l) + (size_t)pos * m->kv_dim, 0, (m->c.seq_len - pos) * rowb, ctx->stream));
+    PB_TRY_CUDA(ctx, cudaMemsetAsync(vcache(m, l) + (size_t)pos * m->kv_dim, 0, (m->c.seq_len - pos) * rowb, ctx->stream));
+  }
+  return pb_wait(ctx);
+}
+
+extern "C" int pb_model_kv(pb_model* m, int layer, int which_v, float* host, size_t floats) {
+  if (!m || !host || layer < 0 || layer >= m->c.n_layers) return PB_ERR_ARG;
+  size_t n = (size_t)m->c.seq_len * m->kv_dim;
+  if (floats != n) return pb_set_error(m->ctx, PB_ERR_ARG, "kv buffer needs %zu floats", n);
+  return pb_download(m->ctx, host, which_v ? vcache(m, layer) : kcache(m, layer), n * 4);
+}
+
+extern "C" int64_t pb_model_decode_bytes(const pb_model* m, int pos) {
+  if (!m) return 0;
+  const pb_model_config& c = m->c;
+  int64_t w = 0;
+  for (int which = 1; which <= 7; ++which) {
+    int r, k;
+    mshape(c, which, &r, &k);
+    int64_t n = (int64_t)r * k;
+    w += c.kind == PB_MODEL_STREAMING_Q4 ? n / 32 * 18 : (n + 31) / 32 * 36;
+  }
+  w *= c.n_layers;
+  int64_t ne = (int64_t)c.vocab * c.dim;
+  int64_t head = c.kind == PB_MODEL_LLAMA_Q8A ? ne * 4 : ne / 32 * (c.emb_type == PB_TYPE_Q4_0 ? 18 : 34);
+  int64_t kvb = (int64_t)2 * c.n_layers * (pos + 1) * m->kv_dim * 4;
+  return w + head + kvb;
+}
+
+extern "C" int pb_model_decode_launches(const pb_model* m) { return m ? m->launches_per_step : 0; }

@@ -1,0 +1,532 @@
+// pb_ops.cu - engine.js operators and the per-token Llama ops on the device.
+//
+// The reference evaluates these ops in JavaScript doubles and rounds to f32
+// on every Float32Array store; the kernels below do the same with explicit
+// *_rn double intrinsics (no contraction).  Products of two f32 values are
+// exact in double, so a DFMA that adds such a product equals the reference's
+// separate multiply and add.  Sums over many terms use a fixed tree instead of
+// the reference's left-to-right loop; the double result can differ in its last
+// bits, which changes the f32-rounded output only in rare ties (the parity
+// tests bound it).
+#include <math.h>
+#include <stdlib.h>
+
+#include <vector>
+
+#include "pb_internal.cuh"
+
+// ============================================================================
+// RMSNorm (engine.js:429-449)
+// ============================================================================
+
+__global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
+                          float* __restrict__ out) {
+  __shared__ double red[32];
+  const float* xr = x + (size_t)blockIdx.x * dim;
+  double ss = 0.0;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) ss = __fma_rn((double)xr[d], (double)xr[d], ss);
+  ss = pb_block_sum_d(ss, red);
+  double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)dim), eps));
+  for (int d = threadIdx.x; d < dim; d += blockDim.x)
+    out[(size_t)blockIdx.x * dim + d] = (float)__dmul_rn(__ddiv_rn((double)xr[d], rms), (double)w[d]);
+}
+
+extern "C" int pb_rmsnorm(pb_ctx* ctx, const float* x, int seq, int dim, const float* w, double eps, float* out) {
+  if (!ctx || !x || !w || !out || seq <= 0 || dim <= 0) return PB_ERR_ARG;
+  k_rmsnorm<<<seq, 256, 0, ctx->stream>>>(x, dim, w, eps, out);
+  PB_LAUNCHED(ctx, "k_rmsnorm");
+  return PB_OK;
+}
+
+// ============================================================================
+// softmax (engine.js:279-303), layerNorm (:315-344)
+// ============================================================================
+
+__global__ void k_softmax(const float* __restrict__ in, int cols, float* __restrict__ out) {
+  __shared__ double red[32];
+  __shared__ float fred[32];
+  __shared__ int nanflag;
+  const float* ir = in + (size_t)blockIdx.x * cols;
+  float* orow = out + (size_t)blockIdx.x * cols;
+  if (threadIdx.x == 0) nanflag = 0;
+  __syncthreads();
+  // Math.max over the row (NaN propagates)
+  float m = -INFINITY;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    float v = ir[c];
+    if (v != v) nanflag = 1;
+    m = fmaxf(m, v);
+  }
+  m = pb_warp_max_f(m);
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) fred[wid] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = -INFINITY;
+    for (int i = 0; i < (blockDim.x + 31) / 32; ++i) t = fmaxf(t, fred[i]);
+    fred[0] = nanflag ? __int_as_float(0x7fc00000) : t;
+  }
+  __syncthreads();
+  double mx = fred[0];
+  double s = 0.0;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    float e = (float)exp(__dsub_rn((double)ir[c], mx));
+    orow[c] = e;
+    s = __dadd_rn(s, (double)e);
+  }
+  s = pb_block_sum_d(s, red);
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) orow[c] = (float)__ddiv_rn((double)orow[c], s);
+}
+
+extern "C" int pb_softmax(pb_ctx* ctx, const float* in, int rows, int cols, float* out) {
+  if (!ctx || !in || !out || rows <= 0 || cols <= 0) return PB_ERR_ARG;
+  k_softmax<<<rows, 256, 0, ctx->stream>>>(in, cols, out);
+  PB_LAUNCHED(ctx, "k_softmax");
+  return PB_OK;
+}
+
+__global__ void k_layernorm(const float* __restrict__ x, int dim, const float* __restrict__ w,
+                            const float* __restrict__ b, double eps, float* __restrict__ out) {
+  __shared__ double red[32];
+  const float* xr = x + (size_t)blockIdx.x * dim;
+  double s = 0.0;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) s = __dadd_rn(s, (double)xr[d]);
+  double mean = __ddiv_rn(pb_block_sum_d(s, red), (double)dim);
+  // `variance += diff * diff`: diff*diff is not exact, so multiply then add
+  double v = 0.0;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    double df = __dsub_rn((double)xr[d], mean);
+    v = __dadd_rn(v, __dmul_rn(df, df));
+  }
+  double var = __ddiv_rn(pb_block_sum_d(v, red), (double)dim);
+  double sd = __dsqrt_rn(__dadd_rn(var, eps));
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    double t = __dmul_rn(__ddiv_rn(__dsub_rn((double)xr[d], mean), sd), (double)w[d]);
+    out[(size_t)blockIdx.x * dim + d] = (float)__dadd_rn(t, b ? (double)b[d] : 0.0);
+  }
+}
+
+extern "C" int pb_layernorm(pb_ctx* ctx, const float* x, int seq, int dim, const float* w, const float* b, double eps,
+                            float* out) {
+  if (!ctx || !x || !w || !out || seq <= 0 || dim <= 0) return PB_ERR_ARG;
+  k_layernorm<<<seq, 256, 0, ctx->stream>>>(x, dim, w, b, eps, out);
+  PB_LAUNCHED(ctx, "k_layernorm");
+  return PB_OK;
+}
+
+// ============================================================================
+// elementwise ops (engine.js:96-106, 354-360, 459-484; llama-streaming.js:590-595)
+// ============================================================================
+
+enum { EW_ADD = 0, EW_MUL, EW_SILU, EW_GELU, EW_SWIGLU };
+
+__global__ void k_elementwise(int op, const float* __restrict__ a, const float* __restrict__ b, int64_t n,
+                              float* __restrict__ out) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  double x = a[i];
+  double r;
+  switch (op) {
+    case EW_ADD: r = __dadd_rn(x, (double)b[i]); break;
+    case EW_MUL: r = __dmul_rn(x, (double)b[i]); break;
+    case EW_SILU: r = __ddiv_rn(x, __dadd_rn(1.0, exp(-x))); break;
+    case EW_GELU: {
+      const double c = __dsqrt_rn(__ddiv_rn(2.0, 3.141592653589793));  // Math.sqrt(2 / Math.PI)
+      double x3 = __dmul_rn(__dmul_rn(__dmul_rn(0.044715, x), x), x);
+      double inner = __dmul_rn(c, __dadd_rn(x, x3));
+      r = __dmul_rn(__dmul_rn(0.5, x), __dadd_rn(1.0, tanh(inner)));
+      break;
+    }
+    default: {  // fused SiLU(g) * u in double, one f32 rounding
+      double silu = __ddiv_rn(x, __dadd_rn(1.0, exp(-x)));
+      r = __dmul_rn(silu, (double)b[i]);
+    }
+  }
+  out[i] = (float)r;
+}
+
+static int ew(pb_ctx* ctx, int op, const float* a, const float* b, int64_t n, float* out) {
+  if (!ctx || !a || !out || n <= 0) return PB_ERR_ARG;
+  if ((op == EW_ADD || op == EW_MUL || op == EW_SWIGLU) && !b) return PB_ERR_ARG;
+  k_elementwise<<<pb_cdiv(n, 256), 256, 0, ctx->stream>>>(op, a, b, n, out);
+  PB_LAUNCHED(ctx, "k_elementwise");
+  return PB_OK;
+}
+
+extern "C" int pb_tensoradd(pb_ctx* ctx, const float* a, const float* b, int64_t n, float* out) { return ew(ctx, EW_ADD, a, b, n, out); }
+extern "C" int pb_elementmul(pb_ctx* ctx, const float* a, const float* b, int64_t n, float* out) { return ew(ctx, EW_MUL, a, b, n, out); }
+extern "C" int pb_silu(pb_ctx* ctx, const float* a, int64_t n, float* out) { return ew(ctx, EW_SILU, a, nullptr, n, out); }
+extern "C" int pb_gelu(pb_ctx* ctx, const float* a, int64_t n, float* out) { return ew(ctx, EW_GELU, a, nullptr, n, out); }
+extern "C" int pb_swiglu(pb_ctx* ctx, const float* g, const float* u, int n, float* out) { return ew(ctx, EW_SWIGLU, g, u, n, out); }
+
+// ============================================================================
+// f32 matmul in the WASM order (wasm-simd.js:71-91): C[m,n] = C[m,n] + a*B[k,n]
+// ============================================================================
+
+__global__ void k_matmul_f32(const float* __restrict__ A, int M, int K, const float* __restrict__ B, int N,
+                             const float* __restrict__ bias, float* __restrict__ C) {
+  int n = blockIdx.x * blockDim.x + threadIdx.x;
+  int m = blockIdx.y;
+  if (n >= N) return;
+  const float* ar = A + (size_t)m * K;
+  float c = bias ? bias[n] : 0.0f;
+  for (int k = 0; k < K; ++k) c = __fadd_rn(c, __fmul_rn(ar[k], B[(size_t)k * N + n]));
+  C[(size_t)m * N + n] = c;
+}
+
+extern "C" int pb_matmul_f32(pb_ctx* ctx, const float* A, int M, int K, const float* B, int N, const float* bias,
+                             float* C) {
+  if (!ctx || !A || !B || !C || M <= 0 || K <= 0 || N <= 0) return PB_ERR_ARG;
+  if (M > 65535) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
+  dim3 grid(pb_cdiv(N, 128), M);
+  k_matmul_f32<<<grid, 128, 0, ctx->stream>>>(A, M, K, B, N, bias, C);
+  PB_LAUNCHED(ctx, "k_matmul_f32");
+  return PB_OK;
+}
+
+// ============================================================================
+// quantize.js:224-266 matmul_q8: out[m,n] += (a*scale)*q in double, f32 store,
+// k ascending, zero activations skipped; the scale of a 32-column chunk is the
+// block of its first flat element (quantize.js:256).
+// ============================================================================
+
+__global__ void k_matmul_q8a(const float* __restrict__ A, int M, int K, const float* __restrict__ scales,
+                             const int8_t* __restrict__ q, int N, const float* __restrict__ bias,
+                             float* __restrict__ out) {
+  int n = blockIdx.x * blockDim.x + threadIdx.x;
+  int m = blockIdx.y;
+  if (n >= N) return;
+  const float* ar = A + (size_t)m * K;
+  int64_t nstart = (int64_t)(n / 32) * 32;
+  float o = bias ? bias[n] : 0.0f;
+  for (int k = 0; k < K; ++k) {
+    double a = ar[k];
+    if (a == 0.0) continue;
+    int64_t row = (int64_t)k * N;
+    double sc = scales[(row + nstart) / 32];
+    double as = __dmul_rn(a, sc);
+    double t = __dmul_rn(as, (double)q[row + n]);
+    o = (float)__dadd_rn((double)o, t);
+  }
+  out[(size_t)m * N + n] = o;
+}
+
+extern "C" int pb_matmul_q8a(pb_ctx* ctx, const float* A, int M, int K, const float* scales, const int8_t* q, int N,
+                             const float* bias, float* out) {
+  if (!ctx || !A || !scales || !q || !out || M <= 0 || K <= 0 || N <= 0) return PB_ERR_ARG;
+  if (M > 65535) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
+  dim3 grid(pb_cdiv(N, 128), M);
+  k_matmul_q8a<<<grid, 128, 0, ctx->stream>>>(A, M, K, scales, q, N, bias, out);
+  PB_LAUNCHED(ctx, "k_matmul_q8a");
+  return PB_OK;
+}
+
+// ============================================================================
+// generic attention (engine.js:374-415)
+// ============================================================================
+
+__global__ void k_attn_scores_generic(const float* __restrict__ Q, const float* __restrict__ Kt, int seqQ, int seqK,
+                                      int dK, int causal, double scale, float* __restrict__ S) {
+  int j = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y;
+  if (j >= seqK) return;
+  float v;
+  if (causal && j > i) {
+    v = -1e9f;
+  } else {
+    double dot = 0.0;
+    for (int k = 0; k < dK; ++k) dot = __fma_rn((double)Q[(size_t)i * dK + k], (double)Kt[(size_t)j * dK + k], dot);
+    v = (float)__dmul_rn(dot, scale);
+  }
+  S[(size_t)i * seqK + j] = v;
+}
+
+__global__ void k_attn_pv_generic(const float* __restrict__ W, const float* __restrict__ V, int seqK, int dV,
+                                  float* __restrict__ out) {
+  int d = blockIdx.x * blockDim.x + threadIdx.x, i = blockIdx.y;
+  if (d >= dV) return;
+  double s = 0.0;
+  for (int j = 0; j < seqK; ++j) s = __fma_rn((double)W[(size_t)i * seqK + j], (double)V[(size_t)j * dV + d], s);
+  out[(size_t)i * dV + d] = (float)s;
+}
+
+extern "C" int pb_attention(pb_ctx* ctx, const float* Q, const float* K, const float* V, int seqQ, int seqK, int dK,
+                            int dV, int causal, float* out) {
+  if (!ctx || !Q || !K || !V || !out || seqQ <= 0 || seqK <= 0 || dK <= 0 || dV <= 0) return PB_ERR_ARG;
+  size_t sb = (size_t)seqQ * seqK * 4;
+  PB_TRY(pb_ensure_scratch(ctx, 2 * sb + 256));
+  float* S = (float*)ctx->scratch;
+  float* Wt = (float*)((char*)ctx->scratch + ((sb + 255) & ~(size_t)255));
+  double scale = 1.0 / sqrt((double)dK);
+  k_attn_scores_generic<<<dim3(pb_cdiv(seqK, 128), seqQ), 128, 0, ctx->stream>>>(Q, K, seqQ, seqK, dK, causal, scale, S);
+  PB_LAUNCHED(ctx, "k_attn_scores_generic");
+  PB_TRY(pb_softmax(ctx, S, seqQ, seqK, Wt));
+  k_attn_pv_generic<<<dim3(pb_cdiv(dV, 64), seqQ), 64, 0, ctx->stream>>>(Wt, V, seqK, dV, out);
+  PB_LAUNCHED(ctx, "k_attn_pv_generic");
+  return PB_OK;
+}
+
+// ============================================================================
+// RoPE (llama-streaming.js:310-339) with a host-built rotation table
+// ============================================================================
+
+// tab[(pos - start) * (hd/2) + i/2] = {cos, sin} of pos / theta^(i/hd), in
+// double, computed on the host exactly as the reference does.
+__global__ void k_rope(float* __restrict__ q, float* __restrict__ k, int seq, int n_heads, int n_kv, int hd,
+                       const double2* __restrict__ tab) {
+  int t = blockIdx.y;
+  int half = hd / 2;
+  int nq = n_heads * half, nk = n_kv * half;
+  int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= nq + nk) return;
+  bool isq = idx < nq;
+  int rel = isq ? idx : idx - nq;
+  int h = rel / half, pr = rel % half;
+  double2 cs = tab[(size_t)t * half + pr];
+  float* base = isq ? q + (size_t)t * n_heads * hd : k + (size_t)t * n_kv * hd;
+  size_t off = (size_t)h * hd + 2 * pr;
+  double x0 = base[off], x1 = base[off + 1];
+  base[off] = (float)__dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y));
+  base[off + 1] = (float)__dadd_rn(__dmul_rn(x0, cs.y), __dmul_rn(x1, cs.x));
+}
+
+// Host table for positions [start, start + n): {cos, sin}(pos * 1/theta^(i/hd)).
+void pb_rope_table(double theta, int hd, int start, int n, double2* out) {
+  int half = hd / 2;
+  for (int i = 0; i < hd; i += 2) {
+    double freq = 1.0 / pow(theta, (double)i / hd);
+    for (int p = 0; p < n; ++p) {
+      double angle = (double)(start + p) * freq;
+      out[(size_t)p * half + i / 2] = make_double2(cos(angle), sin(angle));
+    }
+  }
+}
+
+extern "C" int pb_rope(pb_ctx* ctx, float* q, float* k, int seq, int start_pos, int n_heads, int n_kv, int hd,
+                       double theta) {
+  if (!ctx || !q || !k || seq <= 0 || start_pos < 0 || n_heads <= 0 || n_kv <= 0 || hd <= 0 || (hd & 1))
+    return PB_ERR_ARG;
+  std::vector<double2> tab((size_t)seq * (hd / 2));
+  pb_rope_table(theta, hd, start_pos, seq, tab.data());
+  size_t tb = tab.size() * sizeof(double2);
+  PB_TRY(pb_ensure_scratch(ctx, tb));
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(ctx->scratch, tab.data(), tb, cudaMemcpyHostToDevice, ctx->stream));
+  int tot = (n_heads + n_kv) * (hd / 2);
+  k_rope<<<dim3(pb_cdiv(tot, 128), seq), 128, 0, ctx->stream>>>(q, k, seq, n_heads, n_kv, hd, (const double2*)ctx->scratch);
+  PB_LAUNCHED(ctx, "k_rope");
+  return pb_wait(ctx);  // the table lives in scratch until the kernel ran
+}
+
+// ============================================================================
+// attention over the KV cache (llama-streaming.js:422-464 prefill, :543-573 decode)
+// One CTA per (query row t, head h).
+// ============================================================================
+
+__global__ void k_attn_cached(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                              int q_stride, int start_pos, const int* __restrict__ pos_dev, int n_heads, int n_kv,
+                              int hd, double scale, float* __restrict__ out, int max_len, int* err) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  __shared__ double red[32];
+  __shared__ float fred[32];
+  float* sc = (float*)sm;
+  const int t = blockIdx.y, h = blockIdx.x;
+  const int sp = pos_dev ? *pos_dev : start_pos;
+  const int cache_len = sp + gridDim.y;
+  if (cache_len > max_len) {
+    pb_raise(err, PB_DEVERR_BOUNDS);
+    return;
+  }
+  const int kv_dim = n_kv * hd, per = n_heads / n_kv, kh = h / per;
+  const float* qh = q + (size_t)t * q_stride + (size_t)h * hd;
+  // scores (f32 stores of a double dot)
+  for (int j = threadIdx.x; j < cache_len; j += blockDim.x) {
+    float v;
+    if (j > sp + t) {
+      v = -INFINITY;
+    } else {
+      const float* kr = kc + (size_t)j * kv_dim + (size_t)kh * hd;
+      double dot = 0.0;
+      for (int d = 0; d < hd; ++d) dot = __fma_rn((double)qh[d], (double)kr[d], dot);
+      v = (float)__dmul_rn(dot, scale);
+    }
+    sc[j] = v;
+  }
+  __syncthreads();
+  // max: `if (scores[j] > maxScore)` from -Infinity
+  float m = -INFINITY;
+  for (int j = threadIdx.x; j < cache_len; j += blockDim.x) m = sc[j] > m ? sc[j] : m;
+  m = pb_warp_max_f(m);
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  if (lane == 0) fred[wid] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t2 = -INFINITY;
+    for (int i = 0; i < nw; ++i) t2 = fred[i] > t2 ? fred[i] : t2;
+    fred[0] = t2;
+  }
+  __syncthreads();
+  double mx = fred[0];
+  double s = 0.0;
+  for (int j = threadIdx.x; j < cache_len; j += blockDim.x) {
+    float e = (float)exp(__dsub_rn((double)sc[j], mx));
+    sc[j] = e;
+    s = __dadd_rn(s, (double)e);
+  }
+  s = pb_block_sum_d(s, red);
+  for (int j = threadIdx.x; j < cache_len; j += blockDim.x) sc[j] = (float)__ddiv_rn((double)sc[j], s);
+  __syncthreads();
+  // out[d] = sum_j p_j * V[j, d]: threads = hd dims x (blockDim/hd) j-slices
+  int slices = blockDim.x / hd;
+  int d = threadIdx.x % hd, sl = threadIdx.x / hd;
+  double acc = 0.0;
+  if (sl < slices) {
+    const float* vb = vc + (size_t)kh * hd + d;
+    for (int j = sl; j < cache_len; j += slices) acc = __fma_rn((double)sc[j], (double)vb[(size_t)j * kv_dim], acc);
+  }
+  double* part = (double*)(sc + ((max_len + 1) & ~1));
+  __syncthreads();
+  if (sl < slices) part[sl * hd + d] = acc;
+  __syncthreads();
+  if (threadIdx.x < hd) {
+    double tot = 0.0;
+    for (int i = 0; i < slices; ++i) tot = __dadd_rn(tot, part[i * hd + threadIdx.x]);
+    out[(size_t)t * n_heads * hd + (size_t)h * hd + threadIdx.x] = (float)tot;
+  }
+}
+
+int pb_launch_attn_cached(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
+                          int start_pos, const int* pos_dev, int n_heads, int n_kv, int hd, float* out, int max_len) {
+  int threads = hd * 4 <= 1024 ? hd * 4 : hd;
+  if (threads < 64) threads = 64;
+  size_t smem = (size_t)((max_len + 1) & ~1) * 4 + (size_t)(threads / hd + 1) * hd * 8 + 16;
+  if (smem > 200 * 1024) return pb_set_error(ctx, PB_ERR_ARG, "cache length %d too long for one CTA", max_len);
+  double scale = 1.0 / sqrt((double)hd);
+  k_attn_cached<<<dim3(n_heads, seq), threads, smem, ctx->stream>>>(q, kc, vc, q_stride, start_pos, pos_dev, n_heads,
+                                                                    n_kv, hd, scale, out, max_len, ctx->d_err);
+  PB_LAUNCHED(ctx, "k_attn_cached");
+  return PB_OK;
+}
+
+extern "C" int pb_attn_cached(pb_ctx* ctx, const float* q, const float* kc, const float* vc, int seq, int start_pos,
+                              int n_heads, int n_kv, int hd, float* out) {
+  if (!ctx || !q || !kc || !vc || !out || seq <= 0 || start_pos < 0 || n_heads <= 0 || n_kv <= 0 || hd <= 0 ||
+      n_heads % n_kv)
+    return PB_ERR_ARG;
+  return pb_launch_attn_cached(ctx, q, n_heads * hd, kc, vc, seq, start_pos, nullptr, n_heads, n_kv, hd, out,
+                               start_pos + seq);
+}
+
+// ============================================================================
+// model-step kernels
+// ============================================================================
+
+// RoPE on q (in place, row stride q_stride) and k, then KV append
+// (llama-streaming.js:531-541): rows t = 0..seq-1 at position pos0 + t,
+// pos0 = *pos_dev when pos_dev is set.  tab has one entry per position.
+__global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
+                          const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
+                          const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
+                          float* __restrict__ kc, float* __restrict__ vc, int max_len, int* err) {
+  int t = blockIdx.y;
+  int pos = (pos_dev ? *pos_dev : start_pos) + t;
+  if (pos < 0 || pos >= max_len) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+    return;
+  }
+  int half = hd / 2, kv_dim = n_kv * hd;
+  int nq = n_heads * half, nk = n_kv * half;
+  int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx < nq + nk) {
+    bool isq = idx < nq;
+    int rel = isq ? idx : idx - nq;
+    int h = rel / half, pr = rel % half;
+    double2 cs = tab[(size_t)pos * half + pr];
+    size_t off = (size_t)h * hd + 2 * pr;
+    const float* src = isq ? q + (size_t)t * q_stride + off : k + (size_t)t * k_stride + off;
+    double x0 = src[0], x1 = src[1];
+    float r0 = (float)__dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y));
+    float r1 = (float)__dadd_rn(__dmul_rn(x0, cs.y), __dmul_rn(x1, cs.x));
+    if (isq) {
+      float* dst = q + (size_t)t * q_stride + off;
+      dst[0] = r0;
+      dst[1] = r1;
+    } else {
+      float* dst = kc + (size_t)pos * kv_dim + off;
+      dst[0] = r0;
+      dst[1] = r1;
+    }
+  } else if (idx < nq + nk + kv_dim) {
+    int dd = idx - nq - nk;
+    vc[(size_t)pos * kv_dim + dd] = v[(size_t)t * v_stride + dd];
+  }
+}
+
+// SwiGLU: mode 0 = fused f32((g/(1+e^-g))*u) (llama-streaming.js:590-595);
+// mode 1 = SILU then ELEMENT_MUL, two f32 roundings (llama.js:329-332,
+// llama-streaming.js:478-481).
+__global__ void k_glu(const float* __restrict__ g, int g_stride, const float* __restrict__ u, int u_stride, int F,
+                      int mode, float* __restrict__ out) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
+  if (i >= F) return;
+  double gv = g[(size_t)m * g_stride + i], uv = u[(size_t)m * u_stride + i];
+  double silu = __ddiv_rn(gv, __dadd_rn(1.0, exp(-gv)));
+  if (mode == 1) silu = (double)(float)silu;
+  out[(size_t)m * F + i] = (float)__dmul_rn(silu, uv);
+}
+
+// Embedding lookup (llama-streaming.js:748-759): x[i] = dequantized row tok_i
+// of a tiled Q4_0 / Q8_0 table (exact f16 decode, gguf.js:55-70) or f32 tiles.
+// When key_dev is set the token is the argmax of the previous step.
+__global__ void k_embed(int type, const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc,
+                        const float* __restrict__ f32tiles, int V, int dim, const int* __restrict__ toks,
+                        const unsigned long long* __restrict__ key_dev, int* __restrict__ tok_out,
+                        unsigned long long* __restrict__ key_reset, float* __restrict__ x, int* err) {
+  int i = blockIdx.y;
+  int tok = key_dev ? pb_argmax_index(*key_dev) : toks[i];
+  if (tok < 0 || tok >= V) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) pb_raise(err, PB_DEVERR_TOKEN);
+    return;
+  }
+  int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d < dim) {
+    int nb = dim / 32, tile = tok >> 5, r = tok & 31;
+    float v;
+    if (type == PB_TYPE_F32) {
+      v = f32tiles[((size_t)tile * dim + d) * 32 + r];
+    } else {
+      int b = d >> 5, j = d & 31;
+      size_t slot = ((size_t)tile * nb + b) * 32 + r;
+      float sc = pb_f16_exact(dsc[slot]);
+      if (type == PB_TYPE_Q4_0) {
+        uint8_t byte = qs[slot * 16 + (j & 15)];
+        int nib = j < 16 ? (byte & 15) : (byte >> 4);
+        v = __fmul_rn((float)(nib - 8), sc);
+      } else {
+        v = __fmul_rn((float)(int8_t)qs[slot * 32 + j], sc);
+      }
+    }
+    x[(size_t)i * dim + d] = v;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+    if (tok_out) *tok_out = tok;
+  }
+}
+
+// End of a device-resident decode step: record the greedy token, advance the
+// position and clear the argmax key for the next step.
+__global__ void k_step_end(unsigned long long* __restrict__ key, int* __restrict__ tok_dev, int* __restrict__ pos_dev,
+                           int* __restrict__ hist, int hist_len) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    int next = pb_argmax_index(*key);
+    *tok_dev = next;
+    int p = *pos_dev;
+    if (hist && p + 1 >= 0 && p + 1 < hist_len) hist[p + 1] = next;
+    *pos_dev = p + 1;
+    *key = 0ull;
+  }
+}
+
+int pb_setup_ops_kernels(void) {
+  cudaError_t e = cudaFuncSetAttribute(k_attn_cached, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
+}

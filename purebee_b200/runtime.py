@@ -1,0 +1,268 @@
+"""The Llama runtimes of the reference, backed by the device model (pb_model).
+
+StreamingLlamaRuntime mirrors llama-streaming.js:182-1002 (GGUF Q4_0 layer
+weights, raw Q4 matvecs for decode, dequantized f32 matmuls for prefill, the
+batch_dot LM head).  LlamaRuntime mirrors llama.js:36-511 (quantize.js Q8
+layer weights through matmul_q8, double-precision head over the f32
+embedding).  Weights live on the device for the whole session (the
+reference's raw SharedArrayBuffer cache, streaming-loader.js:119-162); the
+decode step is one replayed CUDA graph.
+"""
+from __future__ import annotations
+
+import ctypes
+import time
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+
+from . import _native as N
+
+
+@dataclass
+class LlamaConfig:
+    """llama.js:22-34 LlamaConfig (plus the GGUF fields of gguf.js:429-450)."""
+    dim: int
+    hiddenDim: int
+    nLayers: int
+    nHeads: int
+    nKvHeads: int
+    vocabSize: int
+    seqLen: int
+    headDim: int = 0
+    ropeTheta: float = 10000.0
+    rmsNormEps: float = 1e-5
+
+    def __post_init__(self):
+        if not self.headDim:
+            self.headDim = self.dim // self.nHeads  # llama.js:31
+
+
+class _DeviceModel:
+    def __init__(self, ctx: N.Context, cfg: LlamaConfig, kind: int, emb_type: int):
+        self.ctx = ctx
+        self.cfg = cfg
+        self.kind = kind
+        self.emb_type = emb_type
+        c = N.ModelConfig(kind, emb_type, cfg.dim, cfg.hiddenDim, cfg.nLayers, cfg.nHeads, cfg.nKvHeads,
+                          cfg.headDim, cfg.vocabSize, cfg.seqLen, float(cfg.ropeTheta), float(cfg.rmsNormEps))
+        h = ctypes.c_void_p()
+        ctx._check(N.lib().pb_model_create(ctx.h, ctypes.byref(c), ctypes.byref(h)))
+        self.h = h.value
+
+    def free(self):
+        if self.h:
+            N.lib().pb_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def init_synthetic(self, seed: int, stdev: float = 0.02):
+        self.ctx._check(N.lib().pb_model_init_synthetic(self.h, seed, stdev))
+
+    def tensor_bytes(self, layer: int, which: int) -> int:
+        c = self.cfg
+        if which >= 8:
+            return c.dim * 4
+        if which == 0:
+            ne = c.vocabSize * c.dim
+            if self.kind == N.MODEL_LLAMA_Q8A:
+                return ne * 4
+            return ne // 32 * (18 if self.emb_type == N.TYPE_Q4_0 else 34)
+        kv = c.nKvHeads * c.headDim
+        rows, cols = {1: (c.dim, c.dim), 2: (kv, c.dim), 3: (kv, c.dim), 4: (c.dim, c.dim),
+                      5: (c.hiddenDim, c.dim), 6: (c.dim, c.hiddenDim), 7: (c.hiddenDim, c.dim)}[which]
+        n = rows * cols
+        if self.kind == N.MODEL_STREAMING_Q4:
+            return n // 32 * 18
+        nb = (n + 31) // 32
+        return nb * 36
+
+    def set_tensor(self, layer: int, which: int, data: np.ndarray):
+        a = np.ascontiguousarray(data)
+        self.ctx._check(N.lib().pb_model_set_tensor(self.h, layer, which, N.ptr(a), a.nbytes))
+
+    def get_tensor(self, layer: int, which: int) -> np.ndarray:
+        out = np.empty(self.tensor_bytes(layer, which), np.uint8)
+        self.ctx._check(N.lib().pb_model_get_tensor(self.h, layer, which, N.ptr(out), out.nbytes))
+        return out
+
+    def forward_logits(self, tokens, start_pos: int) -> np.ndarray:
+        t = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(self.cfg.vocabSize, np.float32)
+        self.ctx._check(N.lib().pb_model_forward(self.h, N.ptr(t), t.size, int(start_pos), N.ptr(logits)))
+        return logits
+
+    def decode(self, token: int, pos: int, want_logits: bool = False):
+        nxt = ctypes.c_int()
+        logits = np.empty(self.cfg.vocabSize, np.float32) if want_logits else None
+        self.ctx._check(N.lib().pb_model_decode(self.h, int(token), int(pos), ctypes.byref(nxt),
+                                                N.ptr(logits) if logits is not None else None))
+        return nxt.value, logits
+
+    def generate_greedy(self, prompt, max_tokens: int, eos_id: int):
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(p.size + max_tokens + 1, np.int32)
+        n = ctypes.c_int()
+        self.ctx._check(N.lib().pb_model_generate(self.h, N.ptr(p), p.size, int(max_tokens), int(eos_id),
+                                                  N.ptr(out), out.size, ctypes.byref(n)))
+        return out[:n.value].tolist()
+
+    def reset_cache(self):
+        self.ctx._check(N.lib().pb_model_reset_cache(self.h))
+
+    def rollback_cache(self, pos: int):
+        self.ctx._check(N.lib().pb_model_rollback_cache(self.h, int(pos)))
+
+    def kv(self, layer: int, which_v: int) -> np.ndarray:
+        c = self.cfg
+        kvd = c.nKvHeads * c.headDim
+        out = np.empty(c.seqLen * kvd, np.float32)
+        self.ctx._check(N.lib().pb_model_kv(self.h, layer, which_v, N.ptr(out), out.size))
+        return out.reshape(c.seqLen, kvd)
+
+
+def argmax(logits) -> int:
+    """llama-streaming.js:899-909: first index of the strict maximum."""
+    best, idx = -np.inf, 0
+    arr = np.asarray(logits, np.float32)
+    finite = np.where(np.isnan(arr), -np.inf, arr)
+    m = finite.max() if finite.size else -np.inf
+    if m > best:
+        idx = int(np.argmax(finite == m))
+    return idx
+
+
+def sample(logits, topK: int = 40, temperature: float = 0.8, rng: Optional[np.random.Generator] = None) -> int:
+    """llama-streaming.js:868-894 top-K + temperature sampling (host side)."""
+    rng = rng or np.random.default_rng()
+    scaled = np.asarray(logits, np.float64) / temperature
+    order = np.argsort(-scaled, kind="stable")[:topK]
+    vals = scaled[order]
+    e = np.exp(vals - vals[0])
+    p = e / e.sum()
+    r = rng.random()
+    c = np.cumsum(p)
+    i = int(np.searchsorted(c, r, side="left"))
+    return int(order[min(i, len(order) - 1)])
+
+
+class _RuntimeBase:
+    KIND = N.MODEL_STREAMING_Q4
+
+    def __init__(self, config: LlamaConfig, options: Optional[dict] = None, ctx: Optional[N.Context] = None,
+                 emb_type: Optional[int] = None):
+        options = options or {}
+        self.config = config
+        self.ctx = ctx or N.Context(options.get("device", 0))
+        if emb_type is None:
+            emb_type = N.TYPE_F32 if self.KIND == N.MODEL_LLAMA_Q8A else N.TYPE_Q4_0
+        self.model = _DeviceModel(self.ctx, config, self.KIND, emb_type)
+        self._loaded = False
+        self._layersUsed = 0
+        self._totalForwards = 0
+
+    # -- weights --------------------------------------------------------
+    def loadSynthetic(self, seed: int, stdev: float = 0.02):
+        """Random-init weights N(0, stdev) from the seed; norm gains 1."""
+        self.model.init_synthetic(seed, stdev)
+        self._loaded = True
+
+    def setTensor(self, layer: int, which: int, data: np.ndarray):
+        self.model.set_tensor(layer, which, data)
+        self._loaded = True
+
+    def getTensor(self, layer: int, which: int) -> np.ndarray:
+        return self.model.get_tensor(layer, which)
+
+    # -- inference ------------------------------------------------------
+    def forward(self, tokenIds, startPos: int = 0, options: Optional[dict] = None):
+        if not self._loaded:
+            raise RuntimeError("Resident weights not loaded")  # llama-streaming.js:739
+        logits = self.model.forward_logits(tokenIds, startPos)
+        self._layersUsed += self.config.nLayers
+        self._totalForwards += 1
+        return {"logits": logits, "layersUsed": self.config.nLayers}
+
+    def argmax(self, logits) -> int:
+        return argmax(logits)
+
+    def sample(self, logits, topK: int = 40, temperature: float = 0.8) -> int:
+        return sample(logits, topK, temperature)
+
+    def generate(self, promptTokens, maxTokens: int = 50, opts: Optional[dict] = None):
+        """llama-streaming.js:914-970.  Greedy runs the device loop (argmax on
+        the device); sampling reads logits back every step."""
+        opts = opts or {}
+        eos = opts.get("eosId") or 2
+        greedy = opts.get("greedy", False)
+        on_token = opts.get("onToken")
+        t0 = time.perf_counter()
+        if greedy and on_token is None:
+            toks = self.model.generate_greedy(promptTokens, maxTokens, eos)
+            dt = time.perf_counter() - t0
+            generated = len(toks) - len(promptTokens)
+            return {"tokens": toks, "generated": generated, "prefillTime": None,
+                    "decodeTime": dt * 1000, "tokPerSec": max(generated - 1, 1) / max(dt, 1e-9),
+                    "avgLayers": self.config.nLayers, "earlyExits": 0}
+        temperature = opts.get("temperature") or 0.8
+        topK = opts.get("topK") or 40
+        self.resetCache()
+        allTokens = list(promptTokens)
+        out = self.forward(promptTokens, 0)
+        prefill = time.perf_counter() - t0
+        pos = len(promptTokens)
+        nxt = self.argmax(out["logits"]) if greedy else self.sample(out["logits"], topK, temperature)
+        allTokens.append(nxt)
+        if on_token:
+            on_token(nxt, 0)
+        d0 = time.perf_counter()
+        generated = 1
+        for i in range(1, maxTokens):
+            if nxt == eos:
+                break
+            step = self.forward([nxt], pos)
+            pos += 1
+            nxt = self.argmax(step["logits"]) if greedy else self.sample(step["logits"], topK, temperature)
+            allTokens.append(nxt)
+            generated += 1
+            if on_token:
+                on_token(nxt, i, step["layersUsed"])
+            if nxt == eos:
+                break
+        dt = time.perf_counter() - d0
+        return {"tokens": allTokens, "generated": generated, "prefillTime": prefill * 1000,
+                "decodeTime": dt * 1000, "tokPerSec": max(generated - 1, 1) / max(dt, 1e-9),
+                "avgLayers": self.config.nLayers, "earlyExits": 0}
+
+    def resetCache(self):
+        self.model.reset_cache()
+
+    def rollbackCache(self, pos: int):
+        self.model.rollback_cache(pos)
+
+    @property
+    def stats(self):
+        return {"totalForwards": self._totalForwards,
+                "avgLayers": (self._layersUsed / self._totalForwards) if self._totalForwards else 0,
+                "earlyExits": 0, "lastExitLayer": self.config.nLayers - 1, "launches": self.ctx.launches}
+
+    def shutdown(self):
+        self.model.free()
+
+
+class StreamingLlamaRuntime(_RuntimeBase):
+    """llama-streaming.js StreamingLlamaRuntime over GGUF Q4_0 layer weights and
+    a Q4_0 or Q8_0 tied embedding (emb_type)."""
+    KIND = N.MODEL_STREAMING_Q4
+
+
+class LlamaRuntime(_RuntimeBase):
+    """llama.js LlamaRuntime over quantize.js Q8 layer weights and an f32
+    embedding (the `run.js --q8` path)."""
+    KIND = N.MODEL_LLAMA_Q8A

@@ -1,0 +1,63 @@
+"""CPU checks of the drop-in boundary: the C-ABI library loads and exports
+every entry point include/*.h declares, the Python binding covers them, and
+the product path neither imports the oracle nor carries a CPU fallback."""
+import glob
+import os
+import re
+import subprocess
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    syms = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        txt = open(h).read()
+        txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+        syms |= set(re.findall(r"\b(pb_[a-z0-9_]+)\s*\(", txt))
+    return syms
+
+
+def test_library_exports_every_declared_symbol(native):
+    lib = os.path.join(ROOT, "purebee_b200", "libpurebee_b200.so")
+    out = subprocess.run(["nm", "-D", "--defined-only", lib], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r" T (pb_[a-z0-9_]+)$", out, flags=re.M))
+    missing = declared_symbols() - exported
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+
+
+def test_binding_covers_header(native):
+    assert declared_symbols() <= set(native.SIGNATURES)
+    L = native.lib()
+    for s in declared_symbols():
+        assert hasattr(L, s)
+
+
+def test_header_is_plain_c():
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        txt = open(h).read()
+        assert "torch" not in txt.lower()
+        assert 'extern "C"' in txt
+
+
+def test_product_does_not_import_oracle():
+    for f in glob.glob(os.path.join(ROOT, "purebee_b200", "**", "*.py"), recursive=True):
+        txt = open(f).read()
+        assert "import oracle" not in txt and "from oracle" not in txt, f
+        assert "_work/" not in txt and "'_work'" not in txt, f
+    for f in glob.glob(os.path.join(ROOT, "purebee_b200", "csrc", "*")):
+        txt = open(f).read()
+        assert "pb_oracle" not in txt and "orc_" not in txt, f
+
+
+def test_no_device_fails_loudly(native):
+    import torch
+    if torch.cuda.is_available():
+        return
+    import pytest
+    with pytest.raises(native.PureBeeError):
+        native.Context(0)
+
+
+def test_abi_version(native):
+    assert native.lib().pb_abi_version() == 1

@@ -1,0 +1,326 @@
+"""CPU tests of the oracle: the reference's own known-answer tests, an
+independent pure-Python restatement on small cases, and the golden fixtures.
+
+Each test names the reference lines it pins.
+"""
+import math
+import os
+
+import numpy as np
+import pytest
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "golden.npz")
+
+f32 = np.float32
+
+
+# ---------------------------------------------------------------------------
+# the reference's own known-answer tests
+# ---------------------------------------------------------------------------
+
+def kat_q4_raw():
+    """wasm-q4.js:673-704 selfTest: two rows, K=32, x = 1."""
+    raw = np.zeros(36, np.uint8)
+    raw[0], raw[1] = 0x00, 0x3C           # d = 1.0
+    raw[2:18] = 0x99                      # nibbles 9 -> +1
+    raw[18], raw[19] = 0x00, 0x40         # d = 2.0
+    raw[20:36] = 0xAA                     # nibbles 10 -> +2
+    return raw
+
+
+def test_kat_wasm_q4_selftest(oracle):
+    y = oracle.q4_0_matvec(np.ones(32, f32), kat_q4_raw(), 2, 32)
+    assert y.tolist() == [32.0, 128.0]
+    assert oracle.q4_0_matvec_js(np.ones(32, f32), kat_q4_raw(), 2, 32).tolist() == [32.0, 128.0]
+
+
+def test_kat_wasm_simd_selftest(oracle):
+    """wasm-simd.js:367-385: [2x3] x identity-ish [3x5]."""
+    A = np.array([1, 2, 3, 4, 5, 6], f32)
+    B = np.array([1, 0, 0, 0, 0, 0, 1, 0, 0, 0, 0, 0, 1, 0, 0], f32)
+    assert oracle.matmul_wasm(A, 2, 3, B, 5).tolist() == [1, 2, 3, 0, 0, 4, 5, 6, 0, 0]
+
+
+def test_kat_main_tensor_mul(oracle):
+    """main.js:65-74: [[1,2,3],[4,5,6]] x [[7,8],[9,10],[11,12]] = [58,64,139,154]."""
+    C = oracle.matmul_wasm(np.arange(1, 7, dtype=f32), 2, 3, np.arange(7, 13, dtype=f32), 2)
+    assert C.tolist() == [58, 64, 139, 154]
+
+
+def test_kat_main_softmax_and_layernorm(oracle):
+    """main.js:76-81 softmax of [1,2,3,4] sums to 1 (1e-5); :89-96 layernorm row mean ~ 0 (1e-4)."""
+    p = oracle.softmax(np.array([1, 2, 3, 4], f32), 1, 4)
+    assert abs(float(np.sum(p.astype(np.float64))) - 1.0) < 1e-5
+    ln = oracle.layernorm(np.arange(1, 9, dtype=f32), 2, 4, np.ones(4, f32), np.zeros(4, f32), 1e-5)
+    assert abs(float(ln[:4].astype(np.float64).mean())) < 1e-4
+
+
+# ---------------------------------------------------------------------------
+# f16 decode / encode (gguf.js:55-70, wasm-q4.js:88-109)
+# ---------------------------------------------------------------------------
+
+def test_f16_exact_all_patterns(oracle):
+    bits = np.arange(65536, dtype=np.uint16)
+    ref = bits.view(np.float16).astype(np.float32)
+    got = np.array([oracle.f16_exact(int(b)) for b in bits[::7]], f32)
+    r = ref[::7]
+    both_nan = np.isnan(got) & np.isnan(r)
+    assert np.array_equal(got.view(np.uint32)[~both_nan], r.view(np.uint32)[~both_nan])
+
+
+def test_f16_wasm_semantics(oracle):
+    assert oracle.f16_wasm(0x0001) == 0.0           # subnormal flushed (exp == 0)
+    assert math.copysign(1, oracle.f16_wasm(0x8000)) == 1.0  # -0 becomes +0
+    assert oracle.f16_wasm(0x3C00) == 1.0
+    assert oracle.f16_wasm(0x7C00) == 65536.0       # no inf case: exponent 31 -> 2^16
+    assert oracle.f16_wasm(0xC000) == -2.0
+
+
+def test_f32_to_f16_round_nearest_even(oracle):
+    rng = np.random.default_rng(1)
+    v = (rng.standard_normal(20000) * 10.0 ** rng.integers(-8, 5, 20000)).astype(f32)
+    v = np.concatenate([v, np.array([65504, 65519.99, 65520, 6.1035156e-05, 5.9604645e-08, 2.9802322e-08,
+                                     2.9802326e-08, 1e-9, 0.0, -0.0, 1.0009766], f32)])
+    with np.errstate(over="ignore"):
+        ref = v.astype(np.float16).view(np.uint16)
+    got = np.array([oracle.f32_to_f16(float(a)) for a in v], np.uint16)
+    assert np.array_equal(got, ref)
+
+
+# ---------------------------------------------------------------------------
+# independent pure-Python restatements (small cases)
+# ---------------------------------------------------------------------------
+
+def py_f16_wasm(bits):
+    e = (bits >> 10) & 0x1F
+    if e == 0:
+        return f32(0.0)
+    u = ((bits >> 15) << 31) | ((e + 112) << 23) | ((bits & 0x3FF) << 13)
+    return np.array([u], np.uint32).view(f32)[0]
+
+
+def py_q4_0_wasm(x, raw, N, K):
+    """wasm-q4.js:148-250 lane order in numpy float32 scalar arithmetic."""
+    nb = K // 32
+    y = np.zeros(N, f32)
+    for n in range(N):
+        acc = [f32(0)] * 4
+        for b in range(nb):
+            blk = raw[(n * nb + b) * 18:(n * nb + b + 1) * 18]
+            d = py_f16_wasm(int(blk[0]) | (int(blk[1]) << 8))
+            ba = [f32(0)] * 4
+            for g in (0, 4, 8, 12):
+                for L in range(4):
+                    byte = int(blk[2 + g + L])
+                    ba[L] = f32(ba[L] + f32(f32((byte & 15) - 8) * x[32 * b + g + L]))
+                    ba[L] = f32(ba[L] + f32(f32((byte >> 4) - 8) * x[32 * b + g + 16 + L]))
+            for L in range(4):
+                acc[L] = f32(acc[L] + f32(ba[L] * d))
+        y[n] = f32(f32(acc[1] + acc[3]) + f32(acc[0] + acc[2]))
+    return y
+
+
+def js_round(v):
+    f = math.floor(v)
+    return f + 1 if v - f >= 0.5 else f
+
+
+def py_matmul_q8(a, M, K, scales, q, N):
+    """quantize.js:224-266 in Python floats (doubles) with float32 stores."""
+    out = np.zeros(M * N, f32)
+    bpr = (N + 31) // 32
+    for m in range(M):
+        for k in range(K):
+            av = float(a[m * K + k])
+            if av == 0:
+                continue
+            row = k * N
+            for bn in range(bpr):
+                ns, ne = bn * 32, min(bn * 32 + 32, N)
+                sc = float(scales[(row + ns) // 32])
+                asc = av * sc
+                for n in range(ns, ne):
+                    out[m * N + n] = f32(float(out[m * N + n]) + asc * float(q[row + n]))
+    return out
+
+
+def test_q4_0_matvec_matches_python_restatement(oracle):
+    rng = np.random.default_rng(2)
+    for N, K in [(1, 32), (5, 64), (3, 96)]:
+        x = rng.standard_normal(K).astype(f32)
+        raw = rng.integers(0, 256, N * (K // 32) * 18, dtype=np.uint8)
+        d = (rng.standard_normal(N * (K // 32)) * 0.01).astype(np.float16).view(np.uint8).reshape(-1, 2)
+        raw.reshape(-1, 18)[:, :2] = d
+        assert np.array_equal(oracle.q4_0_matvec(x, raw, N, K).view(np.uint32), py_q4_0_wasm(x, raw, N, K).view(np.uint32))
+
+
+def test_q4_wasm_vs_js_fallback(oracle):
+    """the WASM-order kernel agrees with the double JS fallback."""
+    rng = np.random.default_rng(3)
+    N, K = 64, 512
+    x = rng.standard_normal(K).astype(f32)
+    raw = rng.integers(0, 256, N * (K // 32) * 18, dtype=np.uint8)
+    # normal (non-subnormal) f16 scales: the WASM decode flushes subnormals to 0
+    # (wasm-q4.js:95-97) while the JS fallback keeps them, by design
+    sgn = np.where(rng.random(N * (K // 32)) < 0.5, -1.0, 1.0)
+    d = (sgn * (np.abs(rng.standard_normal(N * (K // 32))) * 0.01 + 0.01)).astype(np.float16)
+    d = d.view(np.uint8).reshape(-1, 2)
+    raw.reshape(-1, 18)[:, :2] = d
+    yw = oracle.q4_0_matvec(x, raw, N, K).astype(np.float64)
+    yj = oracle.q4_0_matvec_js(x, raw, N, K).astype(np.float64)
+    assert np.max(np.abs(yw - yj)) <= 1e-5 * np.max(np.abs(yj))
+    raw1 = rng.integers(0, 256, N * (K // 32) * 20, dtype=np.uint8)
+    raw1.reshape(-1, 20)[:, :2] = d
+    raw1.reshape(-1, 20)[:, 2:4] = d
+    yw = oracle.q4_1_matvec(x, raw1, N, K).astype(np.float64)
+    yj = oracle.q4_1_matvec_js(x, raw1, N, K).astype(np.float64)
+    assert np.max(np.abs(yw - yj)) <= 1e-5 * np.max(np.abs(yj))
+
+
+def test_quantize_q8a_math_round_ties(oracle):
+    """quantize.js:79-109: Math.round rounds .5 toward +infinity (-2.5 -> -2)."""
+    data = np.zeros(32, f32)
+    data[:6] = [127.0, -2.5, 2.5, -0.5, 0.5, -126.5]
+    s, q = oracle.quantize_q8a(data)
+    assert s[0] == 1.0
+    assert q[:6].tolist() == [127, -2, 3, 0, 1, -126]
+    for i in range(32):
+        assert q[i] == js_round(float(data[i]) * (127 / 127.0))
+
+
+def test_quantize_q4a_pack_and_clamp(oracle):
+    """quantize.js:124-161: scale = max/7, clamp to [-8, 7], even index -> low nibble."""
+    data = np.zeros(40, f32)
+    data[:4] = [7.0, -7.0, -2.5, 2.5]
+    s, q = oracle.quantize_q4a(data)
+    assert s[0] == 1.0 and s[1] == 0.0
+    assert (q[0] & 15, q[0] >> 4, q[1] & 15, q[1] >> 4) == (15, 1, 6, 11)
+    assert q.size == 32  # ceil(numBlocks*32/2) bytes
+
+
+def test_matmul_q8_matches_python(oracle):
+    rng = np.random.default_rng(4)
+    M, K, N = 2, 12, 40
+    a = rng.standard_normal(M * K).astype(f32)
+    a[5] = 0.0
+    w = (rng.standard_normal(K * N) * 0.05).astype(f32)
+    s, q = oracle.quantize_q8a(w)
+    got = oracle.matmul_q8(a, M, K, s, q, N)
+    assert np.array_equal(got.view(np.uint32), py_matmul_q8(a, M, K, s, q, N).view(np.uint32))
+
+
+def test_gguf_q4_0_layout_and_error(oracle):
+    """gguf.js:259-286 decode of the build's encoder: low nibble = element j."""
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal(32 * 50) * 0.02).astype(f32)
+    raw = oracle.quantize_gguf_q4_0(x)
+    deq = oracle.dequant_q4_0(raw, x.size)
+    d = np.abs(raw.reshape(-1, 18)[:, :2].copy().view(np.float16).astype(np.float32)).repeat(32)
+    # half a step in general, one step where x/d > 7.5 is clamped to code 15,
+    # plus the f16 rounding of d (relative 2^-11, times at most 8 steps)
+    assert np.all(np.abs(deq - x) <= 1.0 * d + 8 * 2.0 ** -11 * d + 1e-12)
+    # the signed maximum of each block is reproduced up to the f16 rounding of d
+    xb, db = x.reshape(-1, 32), deq.reshape(-1, 32)
+    im = np.argmax(np.abs(xb), axis=1)
+    r = np.arange(xb.shape[0])
+    assert np.all(np.abs(db[r, im] - xb[r, im]) <= 8 * 2.0 ** -11 * np.abs(xb[r, im]) + 1e-12)
+    blk = raw[:18]
+    dd = np.frombuffer(blk[:2].tobytes(), np.float16)[0].astype(np.float64)
+    b2 = int(blk[2])
+    assert deq[0] == f32(((b2 & 15) - 8) * dd)
+    assert deq[16] == f32(((b2 >> 4) - 8) * dd)
+
+
+def test_gguf_q8_0_round_trip(oracle):
+    rng = np.random.default_rng(6)
+    x = (rng.standard_normal(32 * 20) * 0.02).astype(f32)
+    raw = oracle.quantize_gguf_q8_0(x)
+    deq = oracle.dequant_q8_0(raw, x.size)
+    d = np.abs(raw.reshape(-1, 34)[:, :2].copy().view(np.float16).astype(np.float32)).repeat(32)
+    assert np.all(np.abs(deq - x) <= 0.5 * d + 127 * 2.0 ** -11 * d + 1e-12)  # f16 rounding of d
+
+
+def test_synth_deterministic_and_normal(oracle):
+    a = oracle.synth_weights(100000, 42, 3, 0.02)
+    b = oracle.synth_weights(100000, 42, 3, 0.02)
+    c = oracle.synth_weights(100000, 42, 4, 0.02)
+    assert np.array_equal(a, b) and not np.array_equal(a, c)
+    assert abs(float(a.mean())) < 3e-4 and abs(float(a.std()) - 0.02) < 3e-4
+    t = oracle.synth_tokens(1000, 9, 1, 32000)
+    assert t.min() >= 1 and t.max() < 32000
+
+
+def test_argmax_first_strict_max(oracle):
+    """llama-streaming.js:899-909: ties -> lowest index; NaN never wins; all -inf -> 0."""
+    assert oracle.argmax(np.array([1, 3, 3, 2], f32)) == 1
+    assert oracle.argmax(np.array([np.nan, 1, np.nan], f32)) == 1
+    assert oracle.argmax(np.array([-np.inf, -np.inf], f32)) == 0
+
+
+# ---------------------------------------------------------------------------
+# golden fixtures (the oracle reproduces them bit for bit)
+# ---------------------------------------------------------------------------
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN)
+
+
+def bits_equal(a, b):
+    a, b = np.asarray(a), np.asarray(b)
+    return a.shape == b.shape and np.array_equal(a.view(np.uint8), b.view(np.uint8))
+
+
+def test_golden_kernels(oracle, golden):
+    g = golden
+    for tag in "abc":
+        N, K = g[f"q4_0_{tag}_shape"]
+        assert bits_equal(oracle.q4_0_matvec(g[f"q4_0_{tag}_x"], g[f"q4_0_{tag}_raw"], N, K), g[f"q4_0_{tag}_y"])
+    N, K = g["q4_1_shape"]
+    assert bits_equal(oracle.q4_1_matvec(g["q4_1_x"], g["q4_1_raw"], N, K), g["q4_1_y"])
+    assert bits_equal(oracle.batch_dot(g["bd_x"], g["bd_W"], 37, 70), g["bd_y"])
+    assert bits_equal(oracle.matmul_wasm(g["mm_A"], 3, 5, g["mm_B"], 7, g["mm_bias"]), g["mm_C"])
+    s8, q8 = oracle.quantize_q8a(g["qa_data"])
+    assert bits_equal(s8, g["q8a_scales"]) and bits_equal(q8, g["q8a_q"])
+    s4, q4 = oracle.quantize_q4a(g["qa_data"])
+    assert bits_equal(s4, g["q4a_scales"]) and bits_equal(q4, g["q4a_q"])
+    assert bits_equal(oracle.matmul_q8(g["mq_a"], 2, 40, g["mq_scales"], g["mq_q"], 40), g["mq_out"])
+    assert bits_equal(oracle.quantize_gguf_q4_0(g["gg_x"]), g["gg_q4_0"])
+    assert bits_equal(oracle.quantize_gguf_q8_0(g["gg_x"]), g["gg_q8_0"])
+    assert bits_equal(oracle.rmsnorm(g["op_x"], 3, 48, g["op_w"]), g["op_rmsnorm"])
+    assert bits_equal(oracle.softmax(g["op_x"], 3, 48), g["op_softmax"])
+    assert bits_equal(oracle.layernorm(g["op_x"], 3, 48, g["op_w"], g["op_b"]), g["op_layernorm"])
+    qr, kr = oracle.rope(g["rope_q"], g["rope_k"], 3, 5, 64, 4, 2, 16, 500000.0)
+    assert bits_equal(qr, g["rope_qr"]) and bits_equal(kr, g["rope_kr"])
+    assert bits_equal(oracle.attn_cached(g["att_q"], g["att_kc"], g["att_vc"], 3, 5, 64, 4, 2, 16), g["att_out"])
+
+
+def test_golden_tiny_models(oracle, golden):
+    import sys
+    sys.path.insert(0, os.path.dirname(GOLDEN))
+    import make_golden as mg
+    for tag, kw in {"ms": mg.TINY_STREAMING, "mq8e": mg.TINY_STREAMING_Q8E, "ml": mg.TINY_LLAMA_Q8A}.items():
+        p, t, lg = mg.model_case(kw, 7, 5, 10)
+        assert np.array_equal(p, golden[f"{tag}_prompt"])
+        assert np.array_equal(t, golden[f"{tag}_tokens"])
+        assert bits_equal(lg, golden[f"{tag}_logits"])
+
+
+def test_model_prefill_then_decode_consistency(oracle):
+    """Decode after a prefill continues the same sequence (generate vs forward)."""
+    import sys
+    sys.path.insert(0, os.path.dirname(GOLDEN))
+    import make_golden as mg
+    m = oracle.Model(oracle.Config(**mg.TINY_STREAMING))
+    m.init_synthetic(11)
+    prompt = oracle.synth_tokens(4, 11, 1, 96)
+    toks = m.generate(prompt, 6, eos_id=-1)
+    m.reset_cache()
+    lg = m.forward(prompt, 0)
+    assert oracle.argmax(lg) == toks[4]
+    # rollback: re-running a position after rollback reproduces it
+    lg1 = m.forward([toks[4]], 4)
+    m.rollback_cache(4)
+    assert np.all(m.kv(0, 0)[4:] == 0)
+    lg2 = m.forward([toks[4]], 4)
+    assert bits_equal(lg1, lg2)
