@@ -108,7 +108,9 @@ int pb_qmat_info(const pb_qmat* m, int* type, int* N, int* K);
 /* y[n] = sum_k W[n,k] x[k] over a resident Q4_0 / Q4_1 matrix, with the
  * f32 lane order of wasm-q4.js:118-267 / 275-435 (bit-exact).  Rows
  * [row0, row0 + rows) only, so a caller can split rows across devices like
- * thread-pool.js:165-246; rows <= 0 means all rows. */
+ * thread-pool.js:165-246; rows <= 0 means all rows.  row0 must be a
+ * multiple of 8 (rows are stored in 8-row tiles); anything else is
+ * PB_ERR_ARG. */
 int pb_qmat_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, float* y_dev, int row0, int rows);
 /* wasm-q4.js:716-747 q4_0_matvec(x, rawBuf, N, K): host buffers in and out. */
 int pb_q4_0_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, int N, int K, float* y_host);

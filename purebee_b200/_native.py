@@ -158,9 +158,9 @@ class DeviceBuffer:
         return out
 
     def free(self) -> None:
-        if self.ptr:
+        if self.ptr and self.ctx.h:
             lib().pb_free(self.ctx.h, self.ptr)
-            self.ptr = None
+        self.ptr = None
 
     def __del__(self):
         try:
@@ -239,9 +239,9 @@ class QMat:
         return out
 
     def free(self):
-        if self.h:
+        if self.h and self.ctx.h:
             lib().pb_qmat_free(self.ctx.h, self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:

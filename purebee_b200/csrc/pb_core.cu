@@ -2,6 +2,7 @@
 // GGUF decode and the device layout of quantized matrices.
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <chrono>
@@ -101,6 +102,8 @@ extern "C" int pb_init(int device, pb_ctx** out) {
     return PB_ERR_STATE;
   }
   ctx->sm_count = prop.multiProcessorCount;
+  const char* nopdl = getenv("PB_NO_PDL");  // programmatic dependent launch off (debugging aid)
+  ctx->pdl = !(nopdl && nopdl[0] == '1');
   ctx->l2_bytes = prop.l2CacheSize;
   if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) { delete ctx; return PB_ERR_CUDA; }
   if (cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess) { delete ctx; return PB_ERR_OOM; }
@@ -437,13 +440,13 @@ __global__ void k_gguf_quantize(int type, const float* __restrict__ x, int64_t n
     q = q > 15 ? 15 : q;
     // element j (< 16) -> low nibble of byte j; element j+16 -> high nibble
     int qhi = __shfl_down_sync(0xffffffffu, q, 16);
-    uint8_t* o = out + b * 18;
-    if (lane == 0) {
-      uint16_t h = __half_as_ushort(__float2half_rn(d));
-      o[0] = (uint8_t)(h & 0xff);
-      o[1] = (uint8_t)(h >> 8);
-    }
-    if (lane < 16) o[2 + lane] = (uint8_t)(q | (qhi << 4));
+    // byte j = element j (low nibble) | element j+16 (high nibble); pairs of
+    // bytes go out as aligned 16-bit stores (a block starts on an even address)
+    uint32_t byte = (uint32_t)(q | (qhi << 4)) & 0xFFu;
+    uint32_t nxt = __shfl_down_sync(0xffffffffu, byte, 1);
+    uint16_t* o16 = reinterpret_cast<uint16_t*>(out + b * 18);
+    if (lane < 16 && (lane & 1) == 0) o16[1 + lane / 2] = (uint16_t)(byte | (nxt << 8));
+    if (lane == 16) o16[0] = __half_as_ushort(__float2half_rn(d));
   } else {
     float am = a;
 #pragma unroll
@@ -453,13 +456,11 @@ __global__ void k_gguf_quantize(int type, const float* __restrict__ x, int64_t n
     float t = __fmul_rn(v, id);
     float r = (t != t) ? 0.0f : roundf(t);
     r = fminf(fmaxf(r, -127.0f), 127.0f);
-    uint8_t* o = out + b * 34;
-    if (lane == 0) {
-      uint16_t h = __half_as_ushort(__float2half_rn(d));
-      o[0] = (uint8_t)(h & 0xff);
-      o[1] = (uint8_t)(h >> 8);
-    }
-    o[2 + lane] = (uint8_t)(int8_t)(int)r;
+    uint32_t byte = (uint32_t)(uint8_t)(int8_t)(int)r;
+    uint32_t nxt = __shfl_down_sync(0xffffffffu, byte, 1);
+    uint16_t* o16 = reinterpret_cast<uint16_t*>(out + b * 34);
+    if ((lane & 1) == 0) o16[1 + lane / 2] = (uint16_t)(byte | (nxt << 8));
+    if (lane == 1) o16[0] = __half_as_ushort(__float2half_rn(d));
   }
 }
 
@@ -518,7 +519,7 @@ __global__ void k_qmat_pack(int type, const uint8_t* __restrict__ src, int N, in
   int hdr = type == PB_TYPE_Q4_1 ? 4 : 2;
   int pl = type == PB_TYPE_Q8_0 ? 32 : 16;
   uint8_t* g = (uint8_t*)src + t * bb;
-  int64_t slot = ((int64_t)(n >> 5) * nb + b) * 32 + (n & 31);
+  int64_t slot = pb_qslot(n, b, nb);
   uint8_t* p = qs + slot * pl;
   if (!unpack) {
     d[slot] = (uint16_t)(g[0] | (g[1] << 8));

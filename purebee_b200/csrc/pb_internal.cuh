@@ -17,17 +17,20 @@ struct pb_ctx {
   int timeout_ms = 10000;
   int* d_err = nullptr;         // device error word: 0 = ok
   int64_t launches = 0;
+  bool pdl = true;              // launch matvecs with programmatic stream serialization
   std::string err;
   // scratch for one-shot host-buffer calls (grown on demand)
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
 };
 
-// Device layout of a quantized matrix.
-//   qs: [N_pad/32 tiles][nb blocks][32 rows][QB bytes]  (QB = 16 for Q4, 32 for Q8)
-//   d : [N_pad/32 tiles][nb blocks][32 rows] u16 scale (Q4_1: a second array m)
-// A warp whose lanes are the 32 rows of a tile reads one block column with a
-// single coalesced 512 B (Q4) / 1 KB (Q8) access.
+// Device layout of a quantized matrix, in 8-row tiles:
+//   qs: [N_pad/8 tiles][nb blocks][8 rows][QB bytes]  (QB = 16 for Q4, 32 for Q8)
+//   d : [N_pad/8 tiles][nb blocks][8 rows] u16 scale (Q4_1: a second array m)
+// One tile is contiguous (nb * 8 * QB bytes of payload, nb * 16 bytes of
+// scales), so a CTA that owns 8 rows fetches them with one bulk copy each, and
+// any block column of 8 consecutive rows is one 128 B (Q4) line.
+// N_pad rounds N up to 32 so a warp of 32 rows never reads past the end.
 struct pb_qmat {
   int type = 0;
   int N = 0, K = 0, N_pad = 0, nb = 0;
@@ -60,6 +63,28 @@ int pb_ensure_scratch(pb_ctx* ctx, size_t bytes);
 
 static inline int pb_cdiv(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
+// Launch a kernel on the context stream, with programmatic dependent launch
+// when pdl is set (and not disabled on the context).  A kernel launched this
+// way must execute griddepcontrol.wait before it reads anything the previous
+// kernel writes, and write nothing before it.
+template <typename... KArgs, typename... Args>
+static inline int pb_launch(pb_ctx* ctx, const char* what, bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block,
+                            size_t smem, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (pdl && ctx->pdl) ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess) return pb_cuda_error(ctx, e, what);
+  return pb_check_launch(ctx, what);
+}
+
 // ---- device helpers -------------------------------------------------------
 
 // gguf.js:55-70 full IEEE half decode (exact for every half, subnormals too).
@@ -74,6 +99,16 @@ __device__ __forceinline__ float pb_f16_wasm(uint32_t bits) {
   uint32_t f = ((bits >> 15) << 31) | ((e + 112u) << 23) | ((bits & 0x3ffu) << 13);
   return e == 0 ? 0.0f : __uint_as_float(f);
 }
+
+// Index of (row, block) in the tiled layout.
+__host__ __device__ __forceinline__ int64_t pb_qslot(int row, int b, int nb) {
+  return ((int64_t)(row >> 3) * nb + b) * 8 + (row & 7);
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue, and wait for the previous kernel's results.
+__device__ __forceinline__ void pb_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pb_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Record the first device-side error; the host reads it with pb_device_error.
 __device__ __forceinline__ void pb_raise(int* err, int code) {
@@ -130,10 +165,30 @@ __device__ __forceinline__ double pb_block_sum_d(double v, double* red) {
 
 // ---- launches shared between translation units ----------------------------
 
+// Matvec epilogues (fused into the kernel that produces the rows).
+#define PB_EPI_STORE 0     // y[row] = v
+#define PB_EPI_RESIDUAL 1  // y[row] = residual[row] + v   (llama-streaming.js:579-580, 601)
+#define PB_EPI_ROPE_KV 2   // rows [q | k | v]: RoPE q, k; k, v into the cache at pos (:531-541)
+#define PB_EPI_SWIGLU4 3   // tiles [g_4i..g_4i+3 | u_4i..u_4i+3]: h_i = silu(g_i)*u_i (:590-595)
+
+struct pb_mv_epi {
+  int kind = PB_EPI_STORE;
+  const float* residual = nullptr;
+  const double2* rope_tab = nullptr;
+  const int* pos_dev = nullptr;
+  int start_pos = 0;
+  int q_rows = 0, kv_rows = 0, head_dim = 0, max_len = 0;
+  float* kc = nullptr;
+  float* vc = nullptr;
+  float* h_out = nullptr;
+};
+
 int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows,
-                     const float* residual);
+                     const pb_mv_epi* epi);
 int pb_launch_head(pb_ctx* ctx, const pb_qmat* emb, const float* h, float* logits,
                    unsigned long long* argmax_key, int mode);
+int pb_launch_head_norm(pb_ctx* ctx, const pb_qmat* emb, const float* h, const float* norm_w, double eps,
+                        float* logits, unsigned long long* argmax_key, int mode);
 int pb_launch_argmax_finish(pb_ctx* ctx, const unsigned long long* key, int* idx);
 int pb_qmat_alloc(pb_ctx* ctx, int type, int N, int K, pb_qmat** out);
 int pb_qmat_pack_from_device(pb_ctx* ctx, pb_qmat* m, const void* gguf_dev);

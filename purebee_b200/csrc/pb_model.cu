@@ -21,6 +21,10 @@ void pb_rope_table(double theta, int hd, int start, int n, double2* out);
 int pb_launch_attn_cached(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
                           int start_pos, const int* pos_dev, int n_heads, int n_kv, int hd, float* out, int max_len);
 int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc);
+int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
+                          int n_heads, int n_kv, int hd, float* out, int max_len, float* scratch);
+size_t pb_attn_decode_scratch_floats(int n_heads, int max_len);
+int pb_launch_rmsnorm_row(pb_ctx* ctx, const float* x, int dim, const float* w, double eps, float* out);
 __global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
                           float* __restrict__ out);
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
@@ -28,7 +32,7 @@ __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __re
                           const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
                           float* __restrict__ kc, float* __restrict__ vc, int max_len, int* err);
 __global__ void k_glu(const float* __restrict__ g, int g_stride, const float* __restrict__ u, int u_stride, int F,
-                      int mode, float* __restrict__ out);
+                      int mode, int interleave4, float* __restrict__ out);
 __global__ void k_embed(int type, const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc,
                         const float* __restrict__ f32tiles, int V, int dim, const int* __restrict__ toks,
                         const unsigned long long* __restrict__ key_dev, int* __restrict__ tok_out,
@@ -54,6 +58,7 @@ struct pb_model {
   float *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr;
   float *kc = nullptr, *vc = nullptr;
   double2* rope_tab = nullptr;
+  float* att_scratch = nullptr;  // decode attention scores and chunk maxima
   // activations (sized for max_m rows)
   int max_m = 0;
   float *x = nullptr, *xn = nullptr, *qkvo = nullptr, *att = nullptr, *guo = nullptr, *hb = nullptr, *proj = nullptr,
@@ -130,7 +135,7 @@ extern "C" int pb_model_free(pb_model* m) {
   for (auto* p : m->q8q) cudaFree(p);
   cudaFree(m->emb_f32);
   cudaFree(m->rms_att); cudaFree(m->rms_ffn); cudaFree(m->rms_final);
-  cudaFree(m->kc); cudaFree(m->vc); cudaFree(m->rope_tab);
+  cudaFree(m->kc); cudaFree(m->vc); cudaFree(m->rope_tab); cudaFree(m->att_scratch);
   cudaFree(m->x); cudaFree(m->xn); cudaFree(m->qkvo); cudaFree(m->att); cudaFree(m->guo); cudaFree(m->hb);
   cudaFree(m->proj); cudaFree(m->logits); cudaFree(m->toks); cudaFree(m->tok_dev); cudaFree(m->hist);
   cudaFree(m->key);
@@ -203,7 +208,8 @@ extern "C" int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model
       cudaMalloc(&m->kc, kv_floats(m) * 4) || cudaMalloc(&m->vc, kv_floats(m) * 4) ||
       cudaMalloc(&m->logits, (size_t)c.vocab * 4) || cudaMalloc(&m->tok_dev, 16) ||
       cudaMalloc(&m->hist, (size_t)(c.seq_len + 1) * 4) || cudaMalloc(&m->key, 16) ||
-      cudaMalloc(&m->rope_tab, (size_t)c.seq_len * (c.head_dim / 2) * sizeof(double2)))
+      cudaMalloc(&m->rope_tab, (size_t)c.seq_len * (c.head_dim / 2) * sizeof(double2)) ||
+      cudaMalloc(&m->att_scratch, pb_attn_decode_scratch_floats(c.n_heads, c.seq_len) * 4))
     return fail(pb_set_error(ctx, PB_ERR_OOM, "model buffers"));
   k_fill<<<pb_cdiv(nd, 256), 256, 0, ctx->stream>>>(m->rms_att, nd, 1.0f);
   k_fill<<<pb_cdiv(nd, 256), 256, 0, ctx->stream>>>(m->rms_ffn, nd, 1.0f);
@@ -231,28 +237,33 @@ extern "C" int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model
 // ---------------------------------------------------------------------------
 
 // Row offset of tensor `which` inside its fused matrix.
-static pb_qmat* fused_target(pb_model* m, int l, int which, int* row_off) {
+static pb_qmat* fused_target(pb_model* m, int l, int which, int* row_off, int* interleave4) {
   const pb_model_config& c = m->c;
+  *interleave4 = 0;
   switch (which) {
     case 1: *row_off = 0; return m->qkv[l];
     case 2: *row_off = c.dim; return m->qkv[l];
     case 3: *row_off = c.dim + m->kv_dim; return m->qkv[l];
     case 4: *row_off = 0; return m->wo[l];
-    case 5: *row_off = 0; return m->gu[l];
-    case 7: *row_off = c.hidden_dim; return m->gu[l];
+    case 5: *row_off = 0; *interleave4 = 1; return m->gu[l];
+    case 7: *row_off = 4; *interleave4 = 1; return m->gu[l];
     default: *row_off = 0; return m->w2[l];
   }
 }
 
 // GGUF rows -> tiles at a row offset of an existing matrix
-__global__ void k_pack_rows(const uint8_t* __restrict__ src, int rows, int row_off, int nb, int type,
+// interleave4: GGUF row i goes to tile row 8*(i/4) + i%4 + row_off, so an
+// 8-row tile holds gate rows 4i..4i+3 (row_off 0) and up rows 4i..4i+3
+// (row_off 4) and the gate|up matvec can finish SwiGLU in its epilogue.
+__global__ void k_pack_rows(const uint8_t* __restrict__ src, int rows, int row_off, int interleave4, int nb, int type,
                             uint8_t* __restrict__ qs, uint16_t* __restrict__ d, int unpack) {
   int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= (int64_t)rows * nb) return;
-  int n = (int)(t / nb) + row_off, b = (int)(t % nb);
+  int i = (int)(t / nb), b = (int)(t % nb);
+  int n = interleave4 ? 8 * (i >> 2) + (i & 3) + row_off : i + row_off;
   int bb = type == PB_TYPE_Q4_0 ? 18 : 34, pl = type == PB_TYPE_Q4_0 ? 16 : 32;
   uint8_t* g = (uint8_t*)src + t * bb;
-  int64_t slot = ((int64_t)(n >> 5) * nb + b) * 32 + (n & 31);
+  int64_t slot = pb_qslot(n, b, nb);
   if (!unpack) {
     d[slot] = (uint16_t)(g[0] | (g[1] << 8));
     for (int i = 0; i < pl; ++i) qs[slot * pl + i] = g[2 + i];
@@ -273,11 +284,11 @@ __global__ void k_tile_f32(const float* __restrict__ src, int V, int dim, float*
   else ((float*)src)[i] = tiles[t];
 }
 
-static int pack_rows(pb_model* m, pb_qmat* dst, const void* gguf_dev, int rows, int row_off) {
+static int pack_rows(pb_model* m, pb_qmat* dst, const void* gguf_dev, int rows, int row_off, int interleave4) {
   pb_ctx* ctx = m->ctx;
   int64_t tot = (int64_t)rows * dst->nb;
-  k_pack_rows<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>((const uint8_t*)gguf_dev, rows, row_off, dst->nb, dst->type,
-                                                          dst->qs, dst->d, 0);
+  k_pack_rows<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>((const uint8_t*)gguf_dev, rows, row_off, interleave4,
+                                                          dst->nb, dst->type, dst->qs, dst->d, 0);
   PB_LAUNCHED(ctx, "k_pack_rows");
   return PB_OK;
 }
@@ -304,7 +315,7 @@ extern "C" int pb_model_init_synthetic(pb_model* m, uint64_t seed, double stdev)
   if ((rc = gen(0, ne))) goto done;
   if (c.kind == PB_MODEL_STREAMING_Q4) {
     if ((rc = pb_gguf_quantize(ctx, c.emb_type, tmp, ne, gg))) goto done;
-    if ((rc = pack_rows(m, m->emb, gg, c.vocab, 0))) goto done;
+    if ((rc = pack_rows(m, m->emb, gg, c.vocab, 0, 0))) goto done;
   } else {
     k_tile_f32<<<pb_cdiv(ne, 256), 256, 0, ctx->stream>>>(tmp, c.vocab, c.dim, m->emb_f32, 0);
     if ((rc = pb_check_launch(ctx, "k_tile_f32"))) goto done;
@@ -317,9 +328,9 @@ extern "C" int pb_model_init_synthetic(pb_model* m, uint64_t seed, double stdev)
       if ((rc = gen(1 + 7 * (uint64_t)l + (w - 1), n))) goto done;
       if (c.kind == PB_MODEL_STREAMING_Q4) {
         if ((rc = pb_gguf_quantize(ctx, PB_TYPE_Q4_0, tmp, n, gg))) goto done;
-        int off;
-        pb_qmat* dst = fused_target(m, l, w, &off);
-        if ((rc = pack_rows(m, dst, gg, r, off))) goto done;
+        int off, il;
+        pb_qmat* dst = fused_target(m, l, w, &off, &il);
+        if ((rc = pack_rows(m, dst, gg, r, off, il))) goto done;
       } else {
         if ((rc = pb_quantize_q8a(ctx, tmp, n, m->q8s[l * 7 + w - 1], m->q8q[l * 7 + w - 1]))) goto done;
       }
@@ -382,19 +393,19 @@ static int model_tensor_io(pb_model* m, int layer, int which, void* host, size_t
     return pb_wait(ctx);
   }
   pb_qmat* dst;
-  int rows, off = 0;
+  int rows, off = 0, il = 0;
   if (which == 0) {
     dst = m->emb;
     rows = c.vocab;
   } else {
     int k;
     mshape(c, which, &rows, &k);
-    dst = fused_target(m, layer, which, &off);
+    dst = fused_target(m, layer, which, &off, &il);
   }
   if (!get) PB_TRY_CUDA(ctx, cudaMemcpyAsync(ctx->scratch, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
   int64_t tot = (int64_t)rows * dst->nb;
-  k_pack_rows<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>((const uint8_t*)ctx->scratch, rows, off, dst->nb, dst->type,
-                                                          dst->qs, dst->d, get);
+  k_pack_rows<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>((const uint8_t*)ctx->scratch, rows, off, il, dst->nb,
+                                                          dst->type, dst->qs, dst->d, get);
   PB_LAUNCHED(ctx, "k_pack_rows");
   if (get) PB_TRY_CUDA(ctx, cudaMemcpyAsync(host, ctx->scratch, bytes, cudaMemcpyDeviceToHost, ctx->stream));
   return pb_wait(ctx);
@@ -425,10 +436,49 @@ static int launch_q8a(pb_model* m, int l, int which, const float* A, int M, floa
   return pb_matmul_q8a(m->ctx, A, M, k, m->q8s[l * 7 + which - 1], m->q8q[l * 7 + which - 1], r, nullptr, out);
 }
 
-// One layer for M rows at start_pos (or *pos_dev when `dev_pos`).
+// Decode layer (M == 1) of the streaming model: four fused matvecs and the
+// attention (llama-streaming.js:505-606).
+static int run_layer_decode_q4(pb_model* m, int l) {
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  const int dim = c.dim, kv = m->kv_dim;
+  const int* pos_dev = m->tok_dev + 1;
+  pb_mv_epi e;
+  // RMSNorm -> [wq; wk; wv] -> RoPE on q, k; k, v into the cache at pos
+  e.kind = PB_EPI_ROPE_KV;
+  e.rope_tab = m->rope_tab;
+  e.pos_dev = pos_dev;
+  e.q_rows = dim;
+  e.kv_rows = kv;
+  e.head_dim = c.head_dim;
+  e.max_len = c.seq_len;
+  e.kc = kcache(m, l);
+  e.vc = vcache(m, l);
+  PB_TRY(pb_launch_rmsnorm_row(ctx, m->x, dim, m->rms_att + (size_t)l * dim, c.eps, m->xn));
+  PB_TRY(pb_launch_matvec(ctx, m->qkv[l], m->xn, m->qkvo, 0, dim + 2 * kv, &e));
+  PB_TRY(pb_launch_attn_decode(ctx, m->qkvo, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads,
+                               c.head_dim, m->att, c.seq_len, m->att_scratch));
+  // wo with the residual add
+  pb_mv_epi r;
+  r.kind = PB_EPI_RESIDUAL;
+  r.residual = m->x;
+  PB_TRY(pb_launch_matvec(ctx, m->wo[l], m->att, m->x, 0, dim, &r));
+  // RMSNorm -> [w1 | w3] interleaved -> SwiGLU
+  pb_mv_epi g;
+  g.kind = PB_EPI_SWIGLU4;
+  g.h_out = m->hb;
+  PB_TRY(pb_launch_rmsnorm_row(ctx, m->x, dim, m->rms_ffn + (size_t)l * dim, c.eps, m->xn));
+  PB_TRY(pb_launch_matvec(ctx, m->gu[l], m->xn, nullptr, 0, 2 * c.hidden_dim, &g));
+  // w2 with the residual add
+  PB_TRY(pb_launch_matvec(ctx, m->w2[l], m->hb, m->x, 0, dim, &r));
+  return PB_OK;
+}
+
+// One layer for M rows at start_pos (prefill, and every llama.js layer).
 static int run_layer(pb_model* m, int l, int M, int start_pos, bool dev_pos) {
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
+  if (c.kind == PB_MODEL_STREAMING_Q4 && M == 1 && dev_pos) return run_layer_decode_q4(m, l);
   const int dim = c.dim, F = c.hidden_dim, kv = m->kv_dim;
   const int qkvw = dim + 2 * kv;
   const int* pos_dev = dev_pos ? m->tok_dev + 1 : nullptr;
@@ -436,8 +486,7 @@ static int run_layer(pb_model* m, int l, int M, int start_pos, bool dev_pos) {
   float *q, *k, *v;
   int qs_, ks_, vs_;
   if (c.kind == PB_MODEL_STREAMING_Q4) {
-    if (M == 1) PB_TRY(pb_launch_matvec(ctx, m->qkv[l], m->xn, m->qkvo, 0, qkvw, nullptr));
-    else PB_TRY(pb_launch_prefill_q4(ctx, m->qkv[l], m->xn, dim, M, m->qkvo, qkvw));
+    PB_TRY(pb_launch_prefill_q4(ctx, m->qkv[l], m->xn, dim, M, m->qkvo, qkvw));
     q = m->qkvo; k = m->qkvo + dim; v = m->qkvo + dim + kv;
     qs_ = ks_ = vs_ = qkvw;
   } else {
@@ -454,52 +503,35 @@ static int run_layer(pb_model* m, int l, int M, int start_pos, bool dev_pos) {
                                                                    kcache(m, l), vcache(m, l), c.seq_len, ctx->d_err);
     PB_LAUNCHED(ctx, "k_rope_kv");
   }
-  PB_TRY(pb_launch_attn_cached(ctx, q, qs_, kcache(m, l), vcache(m, l), M, start_pos, pos_dev, c.n_heads,
-                               c.n_kv_heads, c.head_dim, m->att, c.seq_len));
+  if (M == 1 && pos_dev && c.n_heads / c.n_kv_heads <= 8 && c.head_dim % 16 == 0)
+    PB_TRY(pb_launch_attn_decode(ctx, q, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads, c.head_dim,
+                                 m->att, c.seq_len, m->att_scratch));
+  else
+    PB_TRY(pb_launch_attn_cached(ctx, q, qs_, kcache(m, l), vcache(m, l), M, start_pos, pos_dev, c.n_heads,
+                                 c.n_kv_heads, c.head_dim, m->att, c.seq_len));
   // output projection + residual
-  if (c.kind == PB_MODEL_STREAMING_Q4) {
-    if (M == 1) {
-      PB_TRY(pb_launch_matvec(ctx, m->wo[l], m->att, m->x, 0, dim, m->x));
-    } else {
-      PB_TRY(pb_launch_prefill_q4(ctx, m->wo[l], m->att, dim, M, m->proj, dim));
-      k_elementwise<<<pb_cdiv((int64_t)M * dim, 256), 256, 0, ctx->stream>>>(0, m->x, m->proj, (int64_t)M * dim, m->x);
-      PB_LAUNCHED(ctx, "k_elementwise");
-    }
-  } else {
-    PB_TRY(launch_q8a(m, l, 4, m->att, M, m->proj));
-    k_elementwise<<<pb_cdiv((int64_t)M * dim, 256), 256, 0, ctx->stream>>>(0, m->x, m->proj, (int64_t)M * dim, m->x);
-    PB_LAUNCHED(ctx, "k_elementwise");
-  }
+  if (c.kind == PB_MODEL_STREAMING_Q4) PB_TRY(pb_launch_prefill_q4(ctx, m->wo[l], m->att, dim, M, m->proj, dim));
+  else PB_TRY(launch_q8a(m, l, 4, m->att, M, m->proj));
+  k_elementwise<<<pb_cdiv((int64_t)M * dim, 256), 256, 0, ctx->stream>>>(0, m->x, m->proj, (int64_t)M * dim, m->x);
+  PB_LAUNCHED(ctx, "k_elementwise");
   PB_TRY(launch_norm(m, m->x, M, m->rms_ffn + (size_t)l * dim, m->xn));
-  // FFN
+  // FFN: SILU then ELEMENT_MUL (llama.js:329-332, llama-streaming.js:478-481)
   const float *g, *u;
-  int gs, us, mode;
+  int gs, us, il;
   if (c.kind == PB_MODEL_STREAMING_Q4) {
-    if (M == 1) PB_TRY(pb_launch_matvec(ctx, m->gu[l], m->xn, m->guo, 0, 2 * F, nullptr));
-    else PB_TRY(pb_launch_prefill_q4(ctx, m->gu[l], m->xn, dim, M, m->guo, 2 * F));
-    g = m->guo; u = m->guo + F; gs = us = 2 * F;
-    mode = M == 1 ? 0 : 1;  // decode fuses SiLU*up; prefill is SILU then ELEMENT_MUL
+    PB_TRY(pb_launch_prefill_q4(ctx, m->gu[l], m->xn, dim, M, m->guo, 2 * F));
+    g = m->guo; u = m->guo; gs = us = 2 * F; il = 1;  // interleaved [g4 | u4] columns
   } else {
     PB_TRY(launch_q8a(m, l, 5, m->xn, M, m->guo));
     PB_TRY(launch_q8a(m, l, 7, m->xn, M, m->guo + (size_t)M * F));
-    g = m->guo; u = m->guo + (size_t)M * F; gs = us = F;
-    mode = 1;
+    g = m->guo; u = m->guo + (size_t)M * F; gs = us = F; il = 0;
   }
-  k_glu<<<dim3(pb_cdiv(F, 256), M), 256, 0, ctx->stream>>>(g, gs, u, us, F, mode, m->hb);
+  k_glu<<<dim3(pb_cdiv(F, 256), M), 256, 0, ctx->stream>>>(g, gs, u, us, F, 1, il, m->hb);
   PB_LAUNCHED(ctx, "k_glu");
-  if (c.kind == PB_MODEL_STREAMING_Q4) {
-    if (M == 1) {
-      PB_TRY(pb_launch_matvec(ctx, m->w2[l], m->hb, m->x, 0, dim, m->x));
-    } else {
-      PB_TRY(pb_launch_prefill_q4(ctx, m->w2[l], m->hb, F, M, m->proj, dim));
-      k_elementwise<<<pb_cdiv((int64_t)M * dim, 256), 256, 0, ctx->stream>>>(0, m->x, m->proj, (int64_t)M * dim, m->x);
-      PB_LAUNCHED(ctx, "k_elementwise");
-    }
-  } else {
-    PB_TRY(launch_q8a(m, l, 6, m->hb, M, m->proj));
-    k_elementwise<<<pb_cdiv((int64_t)M * dim, 256), 256, 0, ctx->stream>>>(0, m->x, m->proj, (int64_t)M * dim, m->x);
-    PB_LAUNCHED(ctx, "k_elementwise");
-  }
+  if (c.kind == PB_MODEL_STREAMING_Q4) PB_TRY(pb_launch_prefill_q4(ctx, m->w2[l], m->hb, F, M, m->proj, dim));
+  else PB_TRY(launch_q8a(m, l, 6, m->hb, M, m->proj));
+  k_elementwise<<<pb_cdiv((int64_t)M * dim, 256), 256, 0, ctx->stream>>>(0, m->x, m->proj, (int64_t)M * dim, m->x);
+  PB_LAUNCHED(ctx, "k_elementwise");
   return PB_OK;
 }
 
@@ -517,11 +549,13 @@ static int launch_embed(pb_model* m, const int* toks, int M) {
   return PB_OK;
 }
 
+// Final RMSNorm (fused into the head kernel) and the LM head with the greedy
+// argmax (llama-streaming.js:616-642, :899-909; llama.js:340-367).
 static int launch_head(pb_model* m, const float* last_x) {
   pb_ctx* ctx = m->ctx;
-  PB_TRY(launch_norm(m, last_x, 1, m->rms_final, m->xn));
-  if (m->c.kind == PB_MODEL_STREAMING_Q4) return pb_launch_head(ctx, m->emb, m->xn, m->logits, m->key, 0);
-  return pb_launch_head(ctx, &m->emb_f32_view, m->xn, m->logits, m->key, 1);
+  if (m->c.kind == PB_MODEL_STREAMING_Q4)
+    return pb_launch_head_norm(ctx, m->emb, last_x, m->rms_final, m->c.eps, m->logits, m->key, 0);
+  return pb_launch_head_norm(ctx, &m->emb_f32_view, last_x, m->rms_final, m->c.eps, m->logits, m->key, 1);
 }
 
 // Enqueue one decode step that reads token and position from m->tok_dev.

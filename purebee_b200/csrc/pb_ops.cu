@@ -31,6 +31,28 @@ __global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __r
     out[(size_t)blockIdx.x * dim + d] = (float)__dmul_rn(__ddiv_rn((double)xr[d], rms), (double)w[d]);
 }
 
+// Decode-step RMSNorm of one row, spread over ceil(dim / 256) CTAs: each CTA
+// forms the same sum of squares with the k_rmsnorm tree (so the values equal
+// k_rmsnorm's) and writes its 256-wide slice.  Launched as a dependent launch:
+// the matvec after it starts fetching weights while this runs.
+__global__ void __launch_bounds__(256)
+k_rmsnorm_row(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps, float* __restrict__ out) {
+  __shared__ double red[32];
+  pb_pdl_trigger();
+  pb_pdl_wait();
+  double ss = 0.0;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) ss = __fma_rn((double)x[d], (double)x[d], ss);
+  ss = pb_block_sum_d(ss, red);
+  const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)dim), eps));
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d < dim) out[d] = (float)__dmul_rn(__ddiv_rn((double)x[d], rms), (double)w[d]);
+}
+
+int pb_launch_rmsnorm_row(pb_ctx* ctx, const float* x, int dim, const float* w, double eps, float* out) {
+  return pb_launch(ctx, "k_rmsnorm_row", true, k_rmsnorm_row, dim3(pb_cdiv(dim, 256)), dim3(256), 0, x, dim, w, eps,
+                   out);
+}
+
 extern "C" int pb_rmsnorm(pb_ctx* ctx, const float* x, int seq, int dim, const float* w, double eps, float* out) {
   if (!ctx || !x || !w || !out || seq <= 0 || dim <= 0) return PB_ERR_ARG;
   k_rmsnorm<<<seq, 256, 0, ctx->stream>>>(x, dim, w, eps, out);
@@ -328,6 +350,7 @@ __global__ void k_attn_cached(const float* __restrict__ q, const float* __restri
   __shared__ double red[32];
   __shared__ float fred[32];
   float* sc = (float*)sm;
+  pb_pdl_trigger();  // the next matvec may start fetching its weights
   const int t = blockIdx.y, h = blockIdx.x;
   const int sp = pos_dev ? *pos_dev : start_pos;
   const int cache_len = sp + gridDim.y;
@@ -463,11 +486,14 @@ __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __re
 // SwiGLU: mode 0 = fused f32((g/(1+e^-g))*u) (llama-streaming.js:590-595);
 // mode 1 = SILU then ELEMENT_MUL, two f32 roundings (llama.js:329-332,
 // llama-streaming.js:478-481).
+// interleave4: g and u are columns of one [g4 | u4]-tiled output row.
 __global__ void k_glu(const float* __restrict__ g, int g_stride, const float* __restrict__ u, int u_stride, int F,
-                      int mode, float* __restrict__ out) {
+                      int mode, int interleave4, float* __restrict__ out) {
   int i = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
   if (i >= F) return;
-  double gv = g[(size_t)m * g_stride + i], uv = u[(size_t)m * u_stride + i];
+  int gi = interleave4 ? 8 * (i >> 2) + (i & 3) : i;
+  int ui = interleave4 ? gi + 4 : i;
+  double gv = g[(size_t)m * g_stride + gi], uv = u[(size_t)m * u_stride + ui];
   double silu = __ddiv_rn(gv, __dadd_rn(1.0, exp(-gv)));
   if (mode == 1) silu = (double)(float)silu;
   out[(size_t)m * F + i] = (float)__dmul_rn(silu, uv);
@@ -480,6 +506,7 @@ __global__ void k_embed(int type, const uint8_t* __restrict__ qs, const uint16_t
                         const float* __restrict__ f32tiles, int V, int dim, const int* __restrict__ toks,
                         const unsigned long long* __restrict__ key_dev, int* __restrict__ tok_out,
                         unsigned long long* __restrict__ key_reset, float* __restrict__ x, int* err) {
+  pb_pdl_trigger();
   int i = blockIdx.y;
   int tok = key_dev ? pb_argmax_index(*key_dev) : toks[i];
   if (tok < 0 || tok >= V) {
@@ -494,7 +521,7 @@ __global__ void k_embed(int type, const uint8_t* __restrict__ qs, const uint16_t
       v = f32tiles[((size_t)tile * dim + d) * 32 + r];
     } else {
       int b = d >> 5, j = d & 31;
-      size_t slot = ((size_t)tile * nb + b) * 32 + r;
+      size_t slot = (size_t)pb_qslot(tok, b, nb);
       float sc = pb_f16_exact(dsc[slot]);
       if (type == PB_TYPE_Q4_0) {
         uint8_t byte = qs[slot * 16 + (j & 15)];
@@ -526,7 +553,178 @@ __global__ void k_step_end(unsigned long long* __restrict__ key, int* __restrict
   }
 }
 
+
+// ============================================================================
+// decode attention (one query, llama-streaming.js:543-573) in two kernels
+// ============================================================================
+// 1. k_attn_dec_scores: CTA (kv head g, chunk of 64 positions).  The chunk's K
+//    rows go to shared memory (coalesced float4 loads, rows padded by 4 floats
+//    so per-position reads are conflict-free); each thread computes one
+//    (query head of the group, position) score in the reference's order:
+//    double dot, d ascending, then f32(dot * scale).  Scores and the chunk's
+//    maximum per head go to global scratch.
+// 2. k_attn_dec_pv: CTA (head h, 16-wide slice of head_dim).  Global max over
+//    the chunk maxima, e_j = f32(exp(s_j - max)), the double sum of e_j (same
+//    tree in every CTA of the head), p_j = f32(e_j / sum), then
+//    out[d] = f32(sum_j p_j * V[j, d]) in double for the slice.
+
+constexpr int AD_CHUNK = 64;
+constexpr int AD_MAX_GROUP = 8;  // query heads per kv head
+
+__global__ void __launch_bounds__(256)
+k_attn_dec_scores(const float* __restrict__ q, const float* __restrict__ kc, const int* __restrict__ pos_dev,
+                  int n_heads, int n_kv, int hd, double scale, float* __restrict__ scores, float* __restrict__ cmax,
+                  int max_len, int* err) {
+  extern __shared__ __align__(16) unsigned char ad_raw[];
+  float* sm = reinterpret_cast<float*>(ad_raw);
+  __shared__ float sv[AD_MAX_GROUP * AD_CHUNK];
+  pb_pdl_trigger();
+  pb_pdl_wait();  // q and the new cache row come from the projection matvec
+  const int g = blockIdx.x, chunk = blockIdx.y;
+  const int pos = *pos_dev;
+  const int cache_len = pos + 1;
+  if (pos < 0 || cache_len > max_len) {
+    if (threadIdx.x == 0 && g == 0 && chunk == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+    return;
+  }
+  const int j0 = chunk * AD_CHUNK;
+  if (j0 >= cache_len) return;
+  const int per = n_heads / n_kv, kv_dim = n_kv * hd, ldk = hd + 4;
+  const int nj = cache_len - j0 < AD_CHUNK ? cache_len - j0 : AD_CHUNK;
+  const int nchunks = (max_len + AD_CHUNK - 1) / AD_CHUNK;
+  float* qs = sm;             // [per][hd]
+  float* ks = sm + per * hd;  // [AD_CHUNK][hd + 4]
+  for (int i = threadIdx.x; i < per * hd / 4; i += blockDim.x) {
+    const int hl = (i * 4) / hd, d = (i * 4) % hd;
+    reinterpret_cast<float4*>(qs)[i] = *reinterpret_cast<const float4*>(q + (size_t)(g * per + hl) * hd + d);
+  }
+  for (int i = threadIdx.x; i < nj * hd / 4; i += blockDim.x) {
+    const int j = (i * 4) / hd, d = (i * 4) % hd;
+    *reinterpret_cast<float4*>(ks + j * ldk + d) =
+        *reinterpret_cast<const float4*>(kc + (size_t)(j0 + j) * kv_dim + (size_t)g * hd + d);
+  }
+  __syncthreads();
+  for (int it = threadIdx.x; it < per * AD_CHUNK; it += blockDim.x) {
+    const int j = it % AD_CHUNK, hl = it / AD_CHUNK;
+    float v = -INFINITY;
+    if (j < nj) {
+      const float* qr = qs + hl * hd;
+      const float* kr = ks + j * ldk;
+      double dot = 0.0;
+      for (int d = 0; d < hd; d += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(qr + d);
+        const float4 b = *reinterpret_cast<const float4*>(kr + d);
+        dot = __fma_rn((double)a.x, (double)b.x, dot);  // exact product: one rounding per term
+        dot = __fma_rn((double)a.y, (double)b.y, dot);
+        dot = __fma_rn((double)a.z, (double)b.z, dot);
+        dot = __fma_rn((double)a.w, (double)b.w, dot);
+      }
+      v = (float)__dmul_rn(dot, scale);
+      scores[(size_t)(g * per + hl) * max_len + j0 + j] = v;
+    }
+    sv[it] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < per) {  // `if (scores[j] > maxScore)` from -Infinity (NaN never wins)
+    float m = -INFINITY;
+    for (int j = 0; j < nj; ++j) {
+      const float v = sv[threadIdx.x * AD_CHUNK + j];
+      m = v > m ? v : m;
+    }
+    cmax[(size_t)(g * per + threadIdx.x) * nchunks + chunk] = m;
+  }
+}
+
+constexpr int AD_SLICE = 16;
+
+__global__ void __launch_bounds__(256)
+k_attn_dec_pv(const float* __restrict__ scores, const float* __restrict__ cmax, const float* __restrict__ vc,
+              const int* __restrict__ pos_dev, int n_heads, int n_kv, int hd, float* __restrict__ out, int max_len) {
+  extern __shared__ __align__(16) unsigned char ad_raw[];
+  float* p = reinterpret_cast<float*>(ad_raw);  // [max_len] probabilities
+  __shared__ double red[256 / 32];
+  __shared__ double part[16][AD_SLICE];
+  __shared__ float smax;
+  pb_pdl_trigger();  // the output projection may start fetching its weights
+  pb_pdl_wait();
+  const int h = blockIdx.x, slice = blockIdx.y;
+  const int pos = *pos_dev;
+  const int cache_len = pos + 1;
+  if (pos < 0 || cache_len > max_len) return;  // k_attn_dec_scores raised the error
+  const int per = n_heads / n_kv, g = h / per, kv_dim = n_kv * hd;
+  const int nchunks = (max_len + AD_CHUNK - 1) / AD_CHUNK;
+  const int used = (cache_len + AD_CHUNK - 1) / AD_CHUNK;
+  if (threadIdx.x == 0) {
+    float m = -INFINITY;
+    for (int c = 0; c < used; ++c) {
+      const float v = cmax[(size_t)h * nchunks + c];
+      m = v > m ? v : m;
+    }
+    smax = m;
+  }
+  __syncthreads();
+  const double mx = smax;
+  const float* sr = scores + (size_t)h * max_len;
+  double s = 0.0;
+  for (int j = threadIdx.x; j < cache_len; j += blockDim.x) {
+    const float e = (float)exp(__dsub_rn((double)sr[j], mx));
+    p[j] = e;
+    s = __dadd_rn(s, (double)e);
+  }
+  s = pb_block_sum_d(s, red);  // __syncthreads inside: p[] is complete afterwards
+  for (int j = threadIdx.x; j < cache_len; j += blockDim.x) p[j] = (float)__ddiv_rn((double)p[j], s);
+  __syncthreads();
+  // thread (d, jg): positions j = jg, jg + 16, ...
+  const int d = threadIdx.x % AD_SLICE, jg = threadIdx.x / AD_SLICE;
+  const float* vb = vc + (size_t)g * hd + slice * AD_SLICE + d;
+  double acc = 0.0;
+  int j = jg;
+  for (; j + 3 * 16 < cache_len; j += 4 * 16) {
+    const float v0 = vb[(size_t)j * kv_dim], v1 = vb[(size_t)(j + 16) * kv_dim];
+    const float v2 = vb[(size_t)(j + 32) * kv_dim], v3 = vb[(size_t)(j + 48) * kv_dim];
+    acc = __fma_rn((double)p[j], (double)v0, acc);
+    acc = __fma_rn((double)p[j + 16], (double)v1, acc);
+    acc = __fma_rn((double)p[j + 32], (double)v2, acc);
+    acc = __fma_rn((double)p[j + 48], (double)v3, acc);
+  }
+  for (; j < cache_len; j += 16) acc = __fma_rn((double)p[j], (double)vb[(size_t)j * kv_dim], acc);
+  part[jg][d] = acc;
+  __syncthreads();
+  if (threadIdx.x < AD_SLICE) {
+    double t = 0.0;
+    for (int i = 0; i < 16; ++i) t = __dadd_rn(t, part[i][threadIdx.x]);
+    out[(size_t)h * hd + slice * AD_SLICE + threadIdx.x] = (float)t;
+  }
+}
+
+// Decode attention for one query at *pos_dev over the cache; scratch holds
+// n_heads * max_len scores plus n_heads * ceil(max_len / 64) chunk maxima.
+int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
+                          int n_heads, int n_kv, int hd, float* out, int max_len, float* scratch) {
+  const int per = n_heads / n_kv;
+  if (per > AD_MAX_GROUP || hd % AD_SLICE || hd % 4)
+    return pb_set_error(ctx, PB_ERR_ARG, "decode attention needs <= %d heads per kv head and head_dim %% 16 == 0",
+                        AD_MAX_GROUP);
+  const int nchunks = (max_len + AD_CHUNK - 1) / AD_CHUNK;
+  float* scores = scratch;
+  float* cmax = scratch + (size_t)n_heads * max_len;
+  const double scale = 1.0 / sqrt((double)hd);  // llama-streaming.js:546
+  size_t smem1 = (size_t)(per * hd + AD_CHUNK * (hd + 4)) * 4;
+  PB_TRY(pb_launch(ctx, "k_attn_dec_scores", true, k_attn_dec_scores, dim3(n_kv, nchunks), dim3(256), smem1, q, kc,
+                   pos_dev, n_heads, n_kv, hd, scale, scores, cmax, max_len, ctx->d_err));
+  size_t smem2 = (size_t)max_len * 4;
+  PB_TRY(pb_launch(ctx, "k_attn_dec_pv", true, k_attn_dec_pv, dim3(n_heads, hd / AD_SLICE), dim3(256), smem2,
+                   (const float*)scores, (const float*)cmax, vc, pos_dev, n_heads, n_kv, hd, out, max_len));
+  return PB_OK;
+}
+
+size_t pb_attn_decode_scratch_floats(int n_heads, int max_len) {
+  return (size_t)n_heads * max_len + (size_t)n_heads * ((max_len + AD_CHUNK - 1) / AD_CHUNK);
+}
+
 int pb_setup_ops_kernels(void) {
   cudaError_t e = cudaFuncSetAttribute(k_attn_cached, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
 }

@@ -136,162 +136,272 @@ __device__ __forceinline__ float4 q4_1_block(uint4 pl, float dl, float mn, const
 // ---------------------------------------------------------------------------
 // matvec kernel
 // ---------------------------------------------------------------------------
+// Persistent CTAs, each owning 8-row tiles t = first + k * gridDim.x.
+//   - each thread owns (row r = tid & 7, blocks bb, bb + 32, ...) of a tile;
+//     its 16 B payloads and scales are loaded straight into registers with
+//     coalesced loads (a warp reads 4 x 128 B lines), the next tile's loads
+//     are issued before the current tile is computed, and the first tile's
+//     loads before griddepcontrol.wait (weights never depend on the previous
+//     kernel);
+//   - x goes to shared memory once per CTA, in float4 chunks swizzled within
+//     each 32-value block so the 4 blocks a warp touches hit distinct banks;
+//   - block partials of the WASM lane order (wasm-q4.js:193-229) go to shared
+//     memory; warp 0 runs the in-order chains acc[L] += partial over the
+//     blocks (4 lanes per row) and the fused epilogue writes the rows.
 
-constexpr int MV_NP = 8;     // producer warps
-constexpr int MV_SLOTS = 4;  // ring depth (chunks)
-constexpr int MV_PF = 2;     // chunks of weights prefetched into registers
+constexpr int MV_THREADS = 256;
 
-template <int R>
-struct MvShape {
-  static constexpr int G = 32 / R;        // blocks per producer warp step
-  static constexpr int CH = MV_NP * G;    // blocks per chunk
-  static constexpr int PS_FLOAT4 = MV_SLOTS * CH * R;
+// Packed f32x2 arithmetic, each component rounded to nearest like the scalar
+// instruction.  The code generator fuses a packed multiply that feeds a packed
+// add into a packed FMA (one rounding instead of the reference's two), even
+// with .rn and --fmad=false, so products of f2mul are only ever consumed by
+// scalar __fadd_rn; f2add is used where its inputs are not products (exact
+// magic-number conversions).
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) {
+  float2 r;
+  asm("{ .reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd; }"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) {
+  float2 r;
+  asm("{ .reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd; }"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{ .reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd; }"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+
+
+// Q4_0 block partials for the four lanes, times d.  Conversions and products
+// are packed; the accumulation is scalar so nothing gets fused.
+__device__ __forceinline__ float4 q4_0_block_exact(uint4 pl, float d, const float4* xs, int b) {
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  const uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t w = wv[g], w2 = w >> 16;
+    const float4 xl = xchunk(xs, b, g), xh = xchunk(xs, b, 4 + g);
+    // lane 0: lo bits 0-3, hi 4-7; lane 1: 8-11, 12-15; lane 2: 16-19, 20-23;
+    // lane 3: 24-27, 28-31 (bytes g..g+3 of the block, wasm-q4.js:200-223)
+    const float2 l01 = f2add(make_float2(mag(w, 0xFu, PB_MAG0), mag(w, 0xF00u, PB_MAG8)),
+                             make_float2(-8388616.0f, -32776.0f));
+    const float2 l23 = f2add(make_float2(mag(w, 0xF0000u, PB_MAG16), mag(w2, 0xF00u, PB_MAG8)),
+                             make_float2(-136.0f, -32776.0f));
+    const float2 h01 = f2add(make_float2(mag(w, 0xF0u, PB_MAG4), mag(w, 0xF000u, PB_MAG12)),
+                             make_float2(-524296.0f, -2056.0f));
+    const float2 h23 = f2add(make_float2(mag(w2, 0xF0u, PB_MAG4), mag(w2, 0xF000u, PB_MAG12)),
+                             make_float2(-524296.0f, -2056.0f));
+    const float2 pl01 = f2mul(l01, make_float2(xl.x, xl.y)), pl23 = f2mul(l23, make_float2(xl.z, xl.w));
+    const float2 ph01 = f2mul(h01, make_float2(xh.x, xh.y)), ph23 = f2mul(h23, make_float2(xh.z, xh.w));
+    a0 = __fadd_rn(a0, pl01.x);
+    a1 = __fadd_rn(a1, pl01.y);
+    a2 = __fadd_rn(a2, pl23.x);
+    a3 = __fadd_rn(a3, pl23.y);
+    a0 = __fadd_rn(a0, ph01.x);
+    a1 = __fadd_rn(a1, ph01.y);
+    a2 = __fadd_rn(a2, ph23.x);
+    a3 = __fadd_rn(a3, ph23.y);
+  }
+  return make_float4(__fmul_rn(a0, d), __fmul_rn(a1, d), __fmul_rn(a2, d), __fmul_rn(a3, d));
+}
+
+template <int TYPE, int NI>
+struct MvRegs {
+  uint4 q[NI];
+  uint16_t d[NI];
+  uint16_t m[NI];
 };
 
-// Epilogue flags
-#define MV_EPI_RESIDUAL 1
-
-template <int R, int TYPE>
-__global__ void __launch_bounds__((MV_NP + 1) * 32)
-k_matvec(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, const uint16_t* __restrict__ msc,
-         int N, int nb, const float* __restrict__ x, float* __restrict__ y, const float* __restrict__ residual,
-         int row_begin, int row_end, int* err) {
-  using S = MvShape<R>;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  uint64_t* bar_full = (uint64_t*)smem_raw;
-  uint64_t* bar_empty = bar_full + MV_SLOTS;
-  float4* ps = (float4*)(smem_raw + 128);
-  float4* xs = ps + S::PS_FLOAT4;
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int row0 = row_begin + blockIdx.x * R;
-  const int tile = row0 >> 5, r_in_tile0 = row0 & 31;
-  const int K = nb * 32;
-
-  if (tid == 0) {
-    for (int s = 0; s < MV_SLOTS; ++s) {
-      mbar_init(&bar_full[s], MV_NP * 32);
-      mbar_init(&bar_empty[s], 1);
+template <int TYPE, int NI>
+__device__ __forceinline__ void mv_load(MvRegs<TYPE, NI>& R, const uint8_t* __restrict__ qs,
+                                        const uint16_t* __restrict__ dsc, const uint16_t* __restrict__ msc, int tile,
+                                        int nb, int r, int bb) {
+#pragma unroll
+  for (int i = 0; i < NI; ++i) {
+    const int b = 32 * i + bb;
+    if (b < nb) {
+      const size_t slot = ((size_t)tile * nb + b) * 8 + r;
+      R.q[i] = __ldcs(reinterpret_cast<const uint4*>(qs) + slot);
+      R.d[i] = __ldcs(dsc + slot);
+      if (TYPE == PB_TYPE_Q4_1) R.m[i] = __ldcs(msc + slot);
     }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // x -> shared memory, float4 chunks swizzled within each 32-value block
-  for (int c = tid; c < K / 4; c += blockDim.x) {
-    int b = c >> 3, i = c & 7;
+}
+
+template <int TYPE, int NI>
+__device__ __forceinline__ void mv_tile(const MvRegs<TYPE, NI>& R, int tile, int nb, int N, int row_end,
+                                        const float4* xs, float4* ps, float* __restrict__ y, const pb_mv_epi& epi,
+                                        int* err) {
+  const int tid = threadIdx.x, r = tid & 7, bb = tid >> 3;
+#pragma unroll
+  for (int i = 0; i < NI; ++i) {
+    const int b = 32 * i + bb;
+    if (b < nb) {
+      float4 p;
+      if (TYPE == PB_TYPE_Q4_0) p = q4_0_block_exact(R.q[i], pb_f16_wasm(R.d[i]), xs, b);
+      else p = q4_1_block(R.q[i], pb_f16_wasm(R.d[i]), pb_f16_wasm(R.m[i]), xs, b);
+      ps[b * 8 + r] = p;
+    }
+  }
+  __syncthreads();
+  if (tid < 32) {
+    // in-order chains: lane = 4 * row + L
+    const int rr = tid >> 2, L = tid & 3;
+    const float* pf = reinterpret_cast<const float*>(ps) + rr * 4 + L;
+    float acc = 0.0f;
+    int b = 0;
+    for (; b + 8 <= nb; b += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = pf[(b + u) * 32];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+    }
+    for (; b < nb; ++b) acc = __fadd_rn(acc, pf[b * 32]);
+    // y = (acc1 + acc3) + (acc0 + acc2)
+    const int base = tid & ~3;
+    const float a0 = __shfl_sync(0xffffffffu, acc, base + 0);
+    const float a1 = __shfl_sync(0xffffffffu, acc, base + 1);
+    const float a2 = __shfl_sync(0xffffffffu, acc, base + 2);
+    const float a3 = __shfl_sync(0xffffffffu, acc, base + 3);
+    const float v = __fadd_rn(__fadd_rn(a1, a3), __fadd_rn(a0, a2));
+    const int row = tile * 8 + rr;
+    const bool live = L == 0 && row < row_end && row < N;
+    if (epi.kind == PB_EPI_STORE) {
+      if (live) y[row] = v;
+    } else if (epi.kind == PB_EPI_RESIDUAL) {
+      if (live) y[row] = __fadd_rn(epi.residual[row], v);
+    } else if (epi.kind == PB_EPI_ROPE_KV) {
+      // rows of a tile are all q, all k or all v (q_rows, kv_rows % 8 == 0)
+      const float vp = __shfl_sync(0xffffffffu, v, tid ^ 4);  // partner row rr ^ 1
+      const int pos = epi.pos_dev ? *epi.pos_dev : epi.start_pos;
+      const bool in_range = pos >= 0 && pos < epi.max_len;
+      if (live && !in_range && rr == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+      if (live && in_range) {
+        const int kvd = epi.kv_rows;
+        if (row < epi.q_rows + kvd) {  // q or k: rotate the pair (2i, 2i+1)
+          const bool isq = row < epi.q_rows;
+          const int rel = isq ? row : row - epi.q_rows;
+          const int pr = (rel % epi.head_dim) >> 1;
+          const double2 cs = epi.rope_tab[(size_t)pos * (epi.head_dim >> 1) + pr];
+          const bool even = (rr & 1) == 0;
+          const double x0 = even ? (double)v : (double)vp, x1 = even ? (double)vp : (double)v;
+          const float o = even ? (float)__dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y))
+                               : (float)__dadd_rn(__dmul_rn(x0, cs.y), __dmul_rn(x1, cs.x));
+          if (isq) y[row] = o;
+          else epi.kc[(size_t)pos * kvd + rel] = o;
+        } else {
+          epi.vc[(size_t)pos * kvd + (row - epi.q_rows - kvd)] = v;
+        }
+      }
+    } else {  // PB_EPI_SWIGLU4: rows 0-3 gate, 4-7 up of indices 4*tile .. 4*tile+3
+      const float u = __shfl_sync(0xffffffffu, v, (tid + 16) & 31);
+      if (L == 0 && rr < 4 && row < N) {
+        const double g = v;
+        const double silu = __ddiv_rn(g, __dadd_rn(1.0, exp(-g)));
+        epi.h_out[tile * 4 + rr] = (float)__dmul_rn(silu, (double)u);
+      }
+    }
+  }
+  __syncthreads();
+}
+
+template <int TYPE, int NI>
+__global__ void __launch_bounds__(MV_THREADS)
+k_matvec(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, const uint16_t* __restrict__ msc, int N,
+         int nb, int tile_begin, int tile_end, int row_end, const float* __restrict__ x, float* __restrict__ y,
+         pb_mv_epi epi, int* err) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float4* ps = reinterpret_cast<float4*>(smem_raw);  // nb * 8 block partials
+  float4* xs = ps + (size_t)nb * 8;                   // K floats, swizzled
+  const int tid = threadIdx.x, r = tid & 7, bb = tid >> 3;
+  const int K = nb * 32;
+  MvRegs<TYPE, NI> A, B;
+  int t = tile_begin + blockIdx.x;
+  if (t < tile_end) mv_load<TYPE, NI>(A, qs, dsc, msc, t, nb, r, bb);
+  pb_pdl_trigger();
+  pb_pdl_wait();  // x (and the residual) come from the previous kernel
+  for (int c = tid; c < K / 4; c += MV_THREADS) {
+    const int b = c >> 3, i = c & 7;
     xs[b * 8 + (i ^ (b & 7))] = reinterpret_cast<const float4*>(x)[c];
   }
   __syncthreads();
-
-  const int nchunks = (nb + S::CH - 1) / S::CH;
-
-  if (warp < MV_NP) {
-    // ---------------- producers ----------------
-    const int r = lane % R, s = lane / R;
-    const int grow = row0 + r;
-    const size_t tile_base = (size_t)tile * nb;
-    uint4 pf_q[MV_PF];
-    uint16_t pf_d[MV_PF], pf_m[MV_PF];
-    auto load = [&](int c, int k) {
-      int b = c * S::CH + warp * S::G + s;
-      if (c < nchunks && b < nb) {
-        size_t slot = (tile_base + b) * 32 + r_in_tile0 + r;
-        pf_q[k] = __ldg(reinterpret_cast<const uint4*>(qs) + slot);
-        pf_d[k] = __ldg(dsc + slot);
-        if (TYPE == PB_TYPE_Q4_1) pf_m[k] = __ldg(msc + slot);
-      }
-    };
-#pragma unroll
-    for (int k = 0; k < MV_PF; ++k) load(k, k);
-    bool ok = true;
-    for (int c0 = 0; c0 < nchunks; c0 += MV_PF) {
-#pragma unroll
-      for (int k = 0; k < MV_PF; ++k) {
-        int c = c0 + k;
-        if (c >= nchunks) break;
-        int slot = c % MV_SLOTS;
-        if (c >= MV_SLOTS && ok) ok = mbar_wait(&bar_empty[slot], ((c / MV_SLOTS) - 1) & 1, err);
-        int b = c * S::CH + warp * S::G + s;
-        float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (b < nb) {
-          if (TYPE == PB_TYPE_Q4_0) p = q4_0_block(pf_q[k], pb_f16_wasm(pf_d[k]), xs, b);
-          else p = q4_1_block(pf_q[k], pb_f16_wasm(pf_d[k]), pb_f16_wasm(pf_m[k]), xs, b);
-        }
-        (void)grow;
-        ps[(slot * S::CH + warp * S::G + s) * R + r] = p;
-        load(c + MV_PF, k);
-        mbar_arrive(&bar_full[slot]);
-      }
-    }
-  } else {
-    // ---------------- consumer: in-order chains ----------------
-    constexpr int CPL = (R * 4) / 32;  // chains per lane
-    const int L = lane & 3, rq = lane >> 2;
-    float acc[CPL];
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) acc[j] = 0.0f;
-    bool ok = true;
-    for (int c = 0; c < nchunks; ++c) {
-      int slot = c % MV_SLOTS;
-      if (ok) ok = mbar_wait(&bar_full[slot], (c / MV_SLOTS) & 1, err);
-      int nblk = nb - c * S::CH;
-      nblk = nblk < S::CH ? nblk : S::CH;
-      const float* pslot = reinterpret_cast<const float*>(ps + slot * S::CH * R);
-      for (int bb = 0; bb < nblk; ++bb) {
-#pragma unroll
-        for (int j = 0; j < CPL; ++j) acc[j] = __fadd_rn(acc[j], pslot[(bb * R + rq + 8 * j) * 4 + L]);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_empty[slot]);
-    }
-    // y = (acc1 + acc3) + (acc0 + acc2) across the four lanes of a row
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      float a0 = __shfl_sync(0xffffffffu, acc[j], (lane & ~3) + 0);
-      float a1 = __shfl_sync(0xffffffffu, acc[j], (lane & ~3) + 1);
-      float a2 = __shfl_sync(0xffffffffu, acc[j], (lane & ~3) + 2);
-      float a3 = __shfl_sync(0xffffffffu, acc[j], (lane & ~3) + 3);
-      float v = __fadd_rn(__fadd_rn(a1, a3), __fadd_rn(a0, a2));
-      int row = row0 + rq + 8 * j;
-      if (L == 0 && row < row_end && row < N) {
-        if (residual) v = __fadd_rn(residual[row], v);
-        y[row] = v;
-      }
-    }
+  while (t < tile_end) {
+    int tn = t + gridDim.x;
+    if (tn < tile_end) mv_load<TYPE, NI>(B, qs, dsc, msc, tn, nb, r, bb);
+    mv_tile<TYPE, NI>(A, t, nb, N, row_end, xs, ps, y, epi, err);
+    t = tn;
+    if (t >= tile_end) break;
+    tn = t + gridDim.x;
+    if (tn < tile_end) mv_load<TYPE, NI>(A, qs, dsc, msc, tn, nb, r, bb);
+    mv_tile<TYPE, NI>(B, t, nb, N, row_end, xs, ps, y, epi, err);
+    t = tn;
   }
 }
 
-template <int R, int TYPE>
-static int launch_mv(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row_begin, int row_end,
-                     const float* residual) {
-  using S = MvShape<R>;
-  size_t smem = 128 + (size_t)S::PS_FLOAT4 * 16 + (size_t)w->K * 4;
-  int grid = pb_cdiv(row_end - row_begin, R);
-  k_matvec<R, TYPE><<<grid, (MV_NP + 1) * 32, smem, ctx->stream>>>(w->qs, w->d, w->m, w->N, w->nb, x, y, residual,
-                                                                    row_begin, row_end, ctx->d_err);
-  PB_LAUNCHED(ctx, "k_matvec");
-  return PB_OK;
+static size_t mv_smem(const pb_qmat* w) { return (size_t)w->nb * 8 * 16 + (size_t)w->nb * 32 * 4; }
+
+template <int TYPE, int NI>
+static int launch_mv(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int tile_begin, int ntiles, int row_end,
+                     const pb_mv_epi& epi) {
+  // persistent: as many CTAs as fit on the SMs at once (registers bound it)
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_matvec<TYPE, NI>, MV_THREADS, mv_smem(w)) !=
+          cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int grid = ntiles < per_sm * ctx->sm_count ? ntiles : per_sm * ctx->sm_count;
+  return pb_launch(ctx, "k_matvec", true, k_matvec<TYPE, NI>, dim3(grid), dim3(MV_THREADS), mv_smem(w),
+                   (const uint8_t*)w->qs, (const uint16_t*)w->d, (const uint16_t*)w->m, w->N, w->nb, tile_begin,
+                   tile_begin + ntiles, row_end, x, y, epi, ctx->d_err);
+}
+
+template <int TYPE>
+static int launch_mv_type(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int tile_begin, int ntiles,
+                          int row_end, const pb_mv_epi& epi) {
+  const int ni = (w->nb + 31) / 32;
+  if (ni <= 1) return launch_mv<TYPE, 1>(ctx, w, x, y, tile_begin, ntiles, row_end, epi);
+  if (ni <= 2) return launch_mv<TYPE, 2>(ctx, w, x, y, tile_begin, ntiles, row_end, epi);
+  if (ni <= 4) return launch_mv<TYPE, 4>(ctx, w, x, y, tile_begin, ntiles, row_end, epi);
+  return launch_mv<TYPE, 8>(ctx, w, x, y, tile_begin, ntiles, row_end, epi);
 }
 
 int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows,
-                     const float* residual) {
-  if (!ctx || !w || !x || !y) return PB_ERR_ARG;
+                     const pb_mv_epi* epi_in) {
+  if (!ctx || !w || !x) return PB_ERR_ARG;
   if (w->type != PB_TYPE_Q4_0 && w->type != PB_TYPE_Q4_1)
     return pb_set_error(ctx, PB_ERR_ARG, "matvec supports Q4_0 and Q4_1 matrices");
-  if (w->K > 32768) return pb_set_error(ctx, PB_ERR_ARG, "K=%d exceeds the 32768 supported", w->K);
+  if (w->nb > 256) return pb_set_error(ctx, PB_ERR_ARG, "K=%d exceeds the 8192 the matvec kernel supports", w->K);
   if (rows <= 0) { row0 = 0; rows = w->N; }
-  if (row0 < 0 || row0 + rows > w->N || (row0 & 31))
-    return pb_set_error(ctx, PB_ERR_ARG, "row range [%d, %d) invalid (start must be a multiple of 32)", row0, row0 + rows);
-  int row_end = row0 + rows;
-  int n = rows;
-  // Rows per CTA: small matrices use 8-row CTAs for parallelism, tall ones
-  // 32-row CTAs to amortise the in-order chain.
-  int R = n >= 32 * ctx->sm_count * 2 ? 32 : (n >= 16 * ctx->sm_count * 2 ? 16 : 8);
-  if (w->type == PB_TYPE_Q4_0) {
-    if (R == 32) return launch_mv<32, PB_TYPE_Q4_0>(ctx, w, x, y, row0, row_end, residual);
-    if (R == 16) return launch_mv<16, PB_TYPE_Q4_0>(ctx, w, x, y, row0, row_end, residual);
-    return launch_mv<8, PB_TYPE_Q4_0>(ctx, w, x, y, row0, row_end, residual);
-  }
-  return launch_mv<8, PB_TYPE_Q4_1>(ctx, w, x, y, row0, row_end, residual);
+  if (row0 < 0 || row0 + rows > w->N || (row0 & 7))
+    return pb_set_error(ctx, PB_ERR_ARG, "row range [%d, %d) invalid (start must be a multiple of 8)", row0, row0 + rows);
+  pb_mv_epi epi = epi_in ? *epi_in : pb_mv_epi();
+  if (!y && epi.kind != PB_EPI_SWIGLU4) return PB_ERR_ARG;
+  const int tile_begin = row0 / 8, ntiles = pb_cdiv(rows, 8);
+  if (w->type == PB_TYPE_Q4_0) return launch_mv_type<PB_TYPE_Q4_0>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
+  return launch_mv_type<PB_TYPE_Q4_1>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
 }
 
 extern "C" int pb_qmat_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows) {
@@ -339,37 +449,71 @@ extern "C" int pb_q4_1_matvec(pb_ctx* ctx, const float* x, const uint8_t* raw, i
 constexpr int HD_WARPS = 8;
 constexpr int HD_PF = 4;
 
+// The hidden vector into shared memory, RMS-normalised with the final norm
+// gains when norm_w is set (engine.js:429-449; the same fixed reduction tree
+// as every other RMSNorm here, so all CTAs get identical values).
+__device__ __forceinline__ void load_hidden(const float* __restrict__ h, const float* __restrict__ norm_w, double eps,
+                                            int K, float* hs) {
+  __shared__ double red[HD_WARPS];
+  if (norm_w) {
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) ss = __fma_rn((double)h[i], (double)h[i], ss);
+    ss = pb_block_sum_d(ss, red);
+    const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)K), eps));
+    for (int i = threadIdx.x; i < K; i += blockDim.x)
+      hs[i] = (float)__dmul_rn(__ddiv_rn((double)h[i], rms), (double)norm_w[i]);
+  } else {
+    for (int i = threadIdx.x; i < K; i += blockDim.x) hs[i] = h[i];
+  }
+  __syncthreads();
+}
+
+// acc[L] += h[4i + L] * e[4i + L] for L = 0..3: packed products, scalar sums
+// (a packed add of packed products would be contracted into an FMA).
+__device__ __forceinline__ void head_acc(float& a0, float& a1, float& a2, float& a3, float4 hv, float2 e01,
+                                         float2 e23) {
+  const float2 p01 = f2mul(make_float2(hv.x, hv.y), e01), p23 = f2mul(make_float2(hv.z, hv.w), e23);
+  a0 = __fadd_rn(a0, p01.x);
+  a1 = __fadd_rn(a1, p01.y);
+  a2 = __fadd_rn(a2, p23.x);
+  a3 = __fadd_rn(a3, p23.y);
+}
+
 // One lane per vocab row; lanes of a warp = the 32 rows of a tile.
 // mode 0: batch_dot order (wasm-q4.js:467-549) over Q4_0 / Q8_0 tiles.
 template <int TYPE>
 __global__ void __launch_bounds__(HD_WARPS * 32)
 k_head(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, int nb, const float* __restrict__ h,
-       float* __restrict__ logits, unsigned long long* __restrict__ amax) {
+       const float* __restrict__ norm_w, double eps, float* __restrict__ logits, unsigned long long* __restrict__ amax) {
   extern __shared__ __align__(16) float hs[];
   const int K = nb * 32;
-  for (int i = threadIdx.x; i < K / 4; i += blockDim.x) reinterpret_cast<float4*>(hs)[i] = reinterpret_cast<const float4*>(h)[i];
-  __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int tile = blockIdx.x * HD_WARPS + warp;
   const int row = tile * 32 + lane;
   const int ntiles = (N + 31) >> 5;
-  float result = 0.0f;
-  if (tile < ntiles) {
-    constexpr int PL = TYPE == PB_TYPE_Q8_0 ? 2 : 1;  // uint4 per block payload
-    const uint4* q4 = reinterpret_cast<const uint4*>(qs);
-    uint4 pq[HD_PF][PL];
-    uint16_t pd[HD_PF];
-    auto load = [&](int b, int k) {
-      if (b < nb) {
-        size_t slot = ((size_t)tile * nb + b) * 32 + lane;
+  constexpr int PL = TYPE == PB_TYPE_Q8_0 ? 2 : 1;  // uint4 per block payload
+  const uint4* q4 = reinterpret_cast<const uint4*>(qs);
+  uint4 pq[HD_PF][PL];
+  uint16_t pd[HD_PF];
+  auto load = [&](int b, int k) {
+    if (b < nb) {
+      size_t slot = (size_t)pb_qslot(tile * 32 + lane, b, nb);
 #pragma unroll
-        for (int u = 0; u < PL; ++u) pq[k][u] = __ldcs(q4 + slot * PL + u);
-        pd[k] = __ldcs(dsc + slot);
-      }
-    };
+      for (int u = 0; u < PL; ++u) pq[k][u] = __ldcs(q4 + slot * PL + u);
+      pd[k] = __ldcs(dsc + slot);
+    }
+  };
+  // the table does not depend on the previous kernel: fetch before waiting
+  if (tile < ntiles) {
 #pragma unroll
     for (int k = 0; k < HD_PF; ++k) load(k, k);
-    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+  }
+  pb_pdl_trigger();
+  pb_pdl_wait();
+  load_hidden(h, norm_w, eps, K, hs);
+  float result = 0.0f;
+  if (tile < ntiles) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;  // acc[k % 4] of batch_dot
     for (int b0 = 0; b0 < nb; b0 += HD_PF) {
 #pragma unroll
       for (int k = 0; k < HD_PF; ++k) {
@@ -378,72 +522,68 @@ k_head(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, 
         float d = pb_f16_exact(pd[k]);
         const float4* hb = reinterpret_cast<const float4*>(hs) + b * 8;
         if (TYPE == PB_TYPE_Q4_0) {
-          uint32_t wv[4] = {pq[k][0].x, pq[k][0].y, pq[k][0].z, pq[k][0].w};
-          float e[8][4];  // e[i][L]: element 4i+L of the block
+          const uint32_t wv[4] = {pq[k][0].x, pq[k][0].y, pq[k][0].z, pq[k][0].w};
           if (isfinite(d)) {
-            float c15 = __fmul_rn(-32776.0f, d), c11 = __fmul_rn(-2056.0f, d), c7 = __fmul_rn(-136.0f, d);
+            // e = (q - 8) * d rebuilt exactly: fma(2^k + q, d, -(2^k + 8) * d)
+            const float c15 = __fmul_rn(-32776.0f, d), c11 = __fmul_rn(-2056.0f, d), c7 = __fmul_rn(-136.0f, d);
+            const float2 dd = make_float2(d, d);
+            float2 e01[8], e23[8];  // element 4i+L for lanes (0,1) and (2,3)
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
-              uint32_t w = wv[g], wa = w << 8, wb = w >> 12;
-              // lo nibbles (elements g*4+L) and hi nibbles (elements 16+g*4+L)
-              e[g][0] = __fmaf_rn(mag(wa, 0xF00u, PB_MAG8), d, c15);
-              e[g + 4][0] = __fmaf_rn(mag(wa, 0xF000u, PB_MAG12), d, c11);
-              e[g][1] = __fmaf_rn(mag(w, 0xF00u, PB_MAG8), d, c15);
-              e[g + 4][1] = __fmaf_rn(mag(w, 0xF000u, PB_MAG12), d, c11);
-              e[g][2] = __fmaf_rn(mag(w, 0xF0000u, PB_MAG16), d, c7);
-              e[g + 4][2] = __fmaf_rn(mag(wb, 0xF00u, PB_MAG8), d, c15);
-              e[g][3] = __fmaf_rn(mag(wb, 0xF000u, PB_MAG12), d, c11);
-              e[g + 4][3] = __fmaf_rn(mag(wb, 0xF0000u, PB_MAG16), d, c7);
+              const uint32_t w = wv[g], wa = w << 8, wb = w >> 12;
+              e01[g] = f2fma(make_float2(mag(wa, 0xF00u, PB_MAG8), mag(w, 0xF00u, PB_MAG8)), dd, make_float2(c15, c15));
+              e23[g] = f2fma(make_float2(mag(w, 0xF0000u, PB_MAG16), mag(wb, 0xF000u, PB_MAG12)), dd, make_float2(c7, c11));
+              e01[g + 4] = f2fma(make_float2(mag(wa, 0xF000u, PB_MAG12), mag(w, 0xF000u, PB_MAG12)), dd,
+                                 make_float2(c11, c11));
+              e23[g + 4] = f2fma(make_float2(mag(wb, 0xF00u, PB_MAG8), mag(wb, 0xF0000u, PB_MAG16)), dd,
+                                 make_float2(c15, c7));
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 hv = hb[i];
+              head_acc(a0, a1, a2, a3, hv, e01[i], e23[i]);
             }
           } else {  // inf / NaN scale: the plain product, as gguf.js computes it
 #pragma unroll
-            for (int g = 0; g < 4; ++g)
+            for (int i = 0; i < 8; ++i) {
+              const float4 hv = hb[i];
+              float e[4];
 #pragma unroll
               for (int L = 0; L < 4; ++L) {
-                uint32_t byte = (wv[g] >> (8 * L)) & 0xFFu;
-                e[g][L] = __fmul_rn((float)((int)(byte & 15u) - 8), d);
-                e[g + 4][L] = __fmul_rn((float)((int)(byte >> 4) - 8), d);
+                const uint32_t byte = (wv[i & 3] >> (8 * L)) & 0xFFu;
+                const int q = i < 4 ? (int)(byte & 15u) : (int)(byte >> 4);
+                e[L] = __fmul_rn((float)(q - 8), d);
               }
-          }
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float4 hv = hb[i];
-            acc0 = __fadd_rn(acc0, __fmul_rn(hv.x, e[i][0]));
-            acc1 = __fadd_rn(acc1, __fmul_rn(hv.y, e[i][1]));
-            acc2 = __fadd_rn(acc2, __fmul_rn(hv.z, e[i][2]));
-            acc3 = __fadd_rn(acc3, __fmul_rn(hv.w, e[i][3]));
+              head_acc(a0, a1, a2, a3, hv, make_float2(e[0], e[1]), make_float2(e[2], e[3]));
+            }
           }
         } else {  // Q8_0: element j = byte j of the 32-byte payload
-          uint32_t wv[8] = {pq[k][0].x, pq[k][0].y, pq[k][0].z, pq[k][0].w,
-                            pq[k][1].x, pq[k][1].y, pq[k][1].z, pq[k][1].w};
-          bool fin = isfinite(d);
-          float c = __fmul_rn(-32896.0f, d);  // -(2^15 + 128) * d, exact
+          const uint32_t wv[8] = {pq[k][0].x, pq[k][0].y, pq[k][0].z, pq[k][0].w,
+                                  pq[k][1].x, pq[k][1].y, pq[k][1].z, pq[k][1].w};
+          const bool fin = isfinite(d);
+          const float c = __fmul_rn(-32896.0f, d);  // -(2^15 + 128) * d, exact
+          const float2 dd = make_float2(d, d), cc = make_float2(c, c);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            uint32_t u = wv[i] ^ 0x80808080u;  // biased bytes: q + 128
-            float4 hv = hb[i];
-            float e0, e1, e2, e3;
+            const uint32_t u = wv[i] ^ 0x80808080u;  // biased bytes: q + 128
+            const float4 hv = hb[i];
+            float2 e01, e23;
             if (fin) {
-              e0 = __fmaf_rn(__uint_as_float(__byte_perm(u, PB_MAG8, 0x7504)), d, c);
-              e1 = __fmaf_rn(__uint_as_float(__byte_perm(u, PB_MAG8, 0x7514)), d, c);
-              e2 = __fmaf_rn(__uint_as_float(__byte_perm(u, PB_MAG8, 0x7524)), d, c);
-              e3 = __fmaf_rn(__uint_as_float(__byte_perm(u, PB_MAG8, 0x7534)), d, c);
+              e01 = f2fma(make_float2(__uint_as_float(__byte_perm(u, PB_MAG8, 0x7504)),
+                                      __uint_as_float(__byte_perm(u, PB_MAG8, 0x7514))), dd, cc);
+              e23 = f2fma(make_float2(__uint_as_float(__byte_perm(u, PB_MAG8, 0x7524)),
+                                      __uint_as_float(__byte_perm(u, PB_MAG8, 0x7534))), dd, cc);
             } else {
-              e0 = __fmul_rn((float)(int8_t)(wv[i] & 0xFF), d);
-              e1 = __fmul_rn((float)(int8_t)((wv[i] >> 8) & 0xFF), d);
-              e2 = __fmul_rn((float)(int8_t)((wv[i] >> 16) & 0xFF), d);
-              e3 = __fmul_rn((float)(int8_t)((wv[i] >> 24) & 0xFF), d);
+              e01 = make_float2(__fmul_rn((float)(int8_t)(wv[i] & 0xFF), d), __fmul_rn((float)(int8_t)((wv[i] >> 8) & 0xFF), d));
+              e23 = make_float2(__fmul_rn((float)(int8_t)((wv[i] >> 16) & 0xFF), d), __fmul_rn((float)(int8_t)(wv[i] >> 24), d));
             }
-            acc0 = __fadd_rn(acc0, __fmul_rn(hv.x, e0));
-            acc1 = __fadd_rn(acc1, __fmul_rn(hv.y, e1));
-            acc2 = __fadd_rn(acc2, __fmul_rn(hv.z, e2));
-            acc3 = __fadd_rn(acc3, __fmul_rn(hv.w, e3));
+            head_acc(a0, a1, a2, a3, hv, e01, e23);
           }
         }
         load(b + HD_PF, k);
       }
     }
-    result = __fadd_rn(__fadd_rn(acc1, acc3), __fadd_rn(acc0, acc2));
+    result = __fadd_rn(__fadd_rn(a1, a3), __fadd_rn(a0, a2));
     if (row < N) logits[row] = result;
   }
   if (amax) {
@@ -460,11 +600,11 @@ k_head(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, 
 // llama.js:359-367 head: logit = f32(sum_d h[d]*E[v,d]) in double over an f32
 // table stored as tiles [V/32][D][32] (lanes = rows; coalesced 128 B loads).
 __global__ void __launch_bounds__(HD_WARPS * 32)
-k_head_f32_double(const float* __restrict__ E, int N, int D, const float* __restrict__ h, float* __restrict__ logits,
+k_head_f32_double(const float* __restrict__ E, int N, int D, const float* __restrict__ h,
+                  const float* __restrict__ norm_w, double eps, float* __restrict__ logits,
                   unsigned long long* __restrict__ amax) {
   extern __shared__ __align__(16) float hs[];
-  for (int i = threadIdx.x; i < D; i += blockDim.x) hs[i] = h[i];
-  __syncthreads();
+  load_hidden(h, norm_w, eps, D, hs);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int tile = blockIdx.x * HD_WARPS + warp;
   const int row = tile * 32 + lane;
@@ -521,16 +661,22 @@ __global__ void k_argmax_finish(const unsigned long long* key, int* idx) {
 
 // mode: 0 = batch_dot order over Q4_0/Q8_0 tiles; 1 = double order over f32 tiles
 int pb_launch_head(pb_ctx* ctx, const pb_qmat* emb, const float* h, float* logits, unsigned long long* amax, int mode) {
+  return pb_launch_head_norm(ctx, emb, h, nullptr, 0.0, logits, amax, mode);
+}
+
+int pb_launch_head_norm(pb_ctx* ctx, const pb_qmat* emb, const float* h, const float* norm_w, double eps, float* logits,
+                        unsigned long long* amax, int mode) {
   int ntiles = (emb->N + 31) / 32;
   int grid = pb_cdiv(ntiles, HD_WARPS);
   size_t smem = (size_t)emb->K * 4;
   if (smem > 200 * 1024) return pb_set_error(ctx, PB_ERR_ARG, "head dim %d too large", emb->K);
   if (mode == 1) {
-    k_head_f32_double<<<grid, HD_WARPS * 32, smem, ctx->stream>>>((const float*)emb->qs, emb->N, emb->K, h, logits, amax);
-  } else if (emb->type == PB_TYPE_Q4_0) {
-    k_head<PB_TYPE_Q4_0><<<grid, HD_WARPS * 32, smem, ctx->stream>>>(emb->qs, emb->d, emb->N, emb->nb, h, logits, amax);
-  } else if (emb->type == PB_TYPE_Q8_0) {
-    k_head<PB_TYPE_Q8_0><<<grid, HD_WARPS * 32, smem, ctx->stream>>>(emb->qs, emb->d, emb->N, emb->nb, h, logits, amax);
+    k_head_f32_double<<<grid, HD_WARPS * 32, smem, ctx->stream>>>((const float*)emb->qs, emb->N, emb->K, h, norm_w, eps,
+                                                                   logits, amax);
+  } else if (emb->type == PB_TYPE_Q4_0 || emb->type == PB_TYPE_Q8_0) {
+    return pb_launch(ctx, "k_head", true, emb->type == PB_TYPE_Q4_0 ? k_head<PB_TYPE_Q4_0> : k_head<PB_TYPE_Q8_0>,
+                     dim3(grid), dim3(HD_WARPS * 32), smem, (const uint8_t*)emb->qs, (const uint16_t*)emb->d, emb->N,
+                     emb->nb, h, norm_w, eps, logits, amax);
   } else {
     return pb_set_error(ctx, PB_ERR_ARG, "head table type %d not supported", emb->type);
   }
@@ -650,7 +796,7 @@ k_prefill_q4(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
     __syncthreads();
     if (tile < ntiles) {
       for (int bb = 0; bb < PF_KC && b0 + bb < nb; ++bb) {
-        size_t slot = ((size_t)tile * nb + b0 + bb) * 32 + lane;
+        size_t slot = (size_t)pb_qslot(tile * 32 + lane, b0 + bb, nb);
         uint4 pl = __ldg(reinterpret_cast<const uint4*>(qs) + slot);
         float d = pb_f16_exact(__ldg(dsc + slot));
         float e[32];
@@ -703,10 +849,14 @@ int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx,
 int pb_setup_q4_kernels(void) {
   const int lim = 200 * 1024;
   cudaError_t e = cudaSuccess;
-  e = e ? e : cudaFuncSetAttribute(k_matvec<8, PB_TYPE_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  e = e ? e : cudaFuncSetAttribute(k_matvec<16, PB_TYPE_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  e = e ? e : cudaFuncSetAttribute(k_matvec<32, PB_TYPE_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  e = e ? e : cudaFuncSetAttribute(k_matvec<8, PB_TYPE_Q4_1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_0, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_0, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_0, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_1, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
   e = e ? e : cudaFuncSetAttribute(k_head<PB_TYPE_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_head<PB_TYPE_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_head_f32_double, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);

@@ -52,9 +52,11 @@ class _DeviceModel:
         self.h = h.value
 
     def free(self):
-        if self.h:
+        # a model lives inside its context: once the context is closed the
+        # device memory is gone with it and the handle must not be touched
+        if self.h and self.ctx.h:
             N.lib().pb_model_free(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:
