@@ -116,13 +116,36 @@ def prompt_tokens():
     return out.tolist()
 
 
-def matvec_roofline(ctx, torch, stream, peak, reps=50):
-    """Per-launch duration of the Q4_0 matvec kernel on the decode shapes,
-    weights rotated over copies totalling > 4x L2 so HBM is measured."""
+def graph_time_us(ctx, torch, stream, launch, reps):
+    """Mean device time of one launch: `reps` launches recorded back to back
+    in one graph (pb_capture_begin / pb_capture_end), replayed once warm and
+    once timed with events on the launching stream (host launch cost
+    excluded)."""
+    ctx.sync()
+    g = ctx.capture(lambda: [launch(i) for i in range(reps)])
+    g.launch()  # warm
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    g.launch()
+    e1.record(stream)
+    e1.synchronize()
+    ctx.sync()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    g.free()
+    return us
+
+
+def matvec_roofline(ctx, torch, stream, peak, reps=200):
+    """Per-launch device time of the Q4_0 matvec kernel on the decode shapes
+    and the config-2 shapes: `reps` launches back to back in one CUDA graph,
+    each on a different weight copy, the copies together > 4x L2 so HBM is
+    measured rather than L2."""
     from purebee_b200 import _native as N
     L = N.lib()
     shapes = {"qkv 3072x2048": (3072, 2048), "o 2048x2048": (2048, 2048), "gate|up 16384x2048": (16384, 2048),
-              "down 2048x8192": (2048, 8192)}
+              "down 2048x8192": (2048, 8192), "kv 512x2048": (512, 2048), "ffn 8192x2048": (8192, 2048),
+              "vocab 128256x2048": (128256, 2048)}
     per_token_launches = {"qkv 3072x2048": 16, "o 2048x2048": 16, "gate|up 16384x2048": 16, "down 2048x8192": 16}
     rng = np.random.default_rng(7)
     res = {}
@@ -130,27 +153,22 @@ def matvec_roofline(ctx, torch, stream, peak, reps=50):
     for name, (n, k) in shapes.items():
         nbytes = n * k // 32 * 18
         copies = max(2, int(np.ceil(4 * 126e6 / nbytes)))
+        r = min(reps, max(20, copies * 2)) if n > 100000 else reps
         raw = rng.integers(0, 256, n * (k // 32) * 18, dtype=np.uint8)
         raw.reshape(-1, 18)[:, :2] = (rng.standard_normal(n * (k // 32)) * 0.01).astype(np.float16).view(
             np.uint8).reshape(-1, 2)
         mats = [N.QMat(ctx, N.TYPE_Q4_0, raw, n, k) for _ in range(copies)]
         x = ctx.to_device(rng.standard_normal(k).astype(np.float32))
         y = ctx.alloc(n * 4)
-        for i in range(3):
-            ctx._check(L.pb_qmat_matvec(ctx.h, mats[i % copies].h, x.ptr, y.ptr, 0, 0))
-        ctx.sync()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for i in range(reps):
-            ctx._check(L.pb_qmat_matvec(ctx.h, mats[i % copies].h, x.ptr, y.ptr, 0, 0))
-        e1.record(stream)
-        e1.synchronize()
-        ms = e0.elapsed_time(e1) / reps
+        us = graph_time_us(ctx, torch, stream,
+                           lambda i: ctx._check(L.pb_qmat_matvec(ctx.h, mats[i % copies].h, x.ptr, y.ptr, 0, 0)), r)
         alg = nbytes + k * 4 + n * 4
-        res[name] = {"us": round(ms * 1e3, 3), "GBps": round(alg / (ms * 1e-3) / 1e9, 1),
-                     "frac": round(alg / (ms * 1e-3) / 1e9 / peak, 3), "bytes": alg}
-        tot_b += alg * per_token_launches[name]
-        tot_t += ms * 1e-3 * per_token_launches[name]
+        gbs = alg / (us * 1e-6) / 1e9
+        res[name] = {"us": round(us, 3), "GBps": round(gbs, 1), "frac": round(gbs / peak, 3), "bytes": alg,
+                     "copies": copies}
+        if name in per_token_launches:
+            tot_b += alg * per_token_launches[name]
+            tot_t += us * 1e-6 * per_token_launches[name]
         for m in mats:
             m.free()
     return res, tot_b / tot_t / 1e9, tot_b / sum(per_token_launches.values())
@@ -336,6 +354,41 @@ def run_reference(args):
             "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_case(args):
+    """One kernel on a small case, for profiler captures: `--case matvec:NxK`
+    runs the Q4_0 matvec on one seeded N x K matrix (W plain launches, then K
+    launches in one CUDA graph, replayed twice); `--case head:VxD` the Q4_0 LM
+    head with argmax.  Prints the mean device time per launch."""
+    import torch
+    from purebee_b200 import _native as N
+    L = N.lib()
+    kind, shape = args.case.split(":")
+    n, k = (int(v) for v in shape.lower().split("x"))
+    ctx = N.Context(0)
+    torch.cuda.set_device(0)
+    stream = torch.cuda.ExternalStream(L.pb_stream(ctx.h), device=0)
+    rng = np.random.default_rng(7)
+    raw = rng.integers(0, 256, n * (k // 32) * 18, dtype=np.uint8)
+    raw.reshape(-1, 18)[:, :2] = (rng.standard_normal(n * (k // 32)) * 0.01).astype(np.float16).view(
+        np.uint8).reshape(-1, 2)
+    m = N.QMat(ctx, N.TYPE_Q4_0 | (N.QMAT_TABLE if kind == "head" else 0), raw, n, k)
+    x = ctx.to_device(rng.standard_normal(k).astype(np.float32))
+    y = ctx.alloc(n * 4)
+    idx = ctx.alloc(16)
+    if kind == "matvec":
+        call = lambda: ctx._check(L.pb_qmat_matvec(ctx.h, m.h, x.ptr, y.ptr, 0, 0))
+    elif kind == "head":
+        call = lambda: ctx._check(L.pb_qmat_head(ctx.h, m.h, x.ptr, y.ptr, idx.ptr))
+    else:
+        raise SystemExit(f"unknown case {kind}")
+    for _ in range(args.warmup):
+        call()
+    us = graph_time_us(ctx, torch, stream, lambda i: call(), args.steps)
+    print(json.dumps({"case": args.case, "us_per_launch": round(us, 3), "bytes": int(raw.nbytes)}), flush=True)
+    m.free()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -344,8 +397,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-max-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK or head:VxD")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.case:
+        run_case(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":

@@ -46,6 +46,10 @@ extern "C" {
 #define PB_TYPE_Q4_0 2
 #define PB_TYPE_Q4_1 3
 #define PB_TYPE_Q8_0 8
+/* OR'ed into the type of pb_qmat_upload / pb_qmat_from_device: store the
+ * matrix as a table read one row per lane (the layout pb_qmat_head needs)
+ * instead of the matvec layout. */
+#define PB_QMAT_TABLE 0x100
 
 typedef struct pb_ctx pb_ctx;
 typedef struct pb_qmat pb_qmat;
@@ -72,6 +76,20 @@ int pb_device_error(pb_ctx* ctx, int* code_out);
 /* Kernel launches issued by this context so far. */
 int64_t pb_launch_count(pb_ctx* ctx);
 
+/* Record the device-pointer calls made on the context between
+ * pb_capture_begin and pb_capture_end into a replayable graph (no
+ * counterpart in the reference, which has no device: this is how a caller
+ * replays a fixed sequence of calls, a layer loop or a benchmark loop,
+ * without paying the host launch cost per call).  Only calls that take
+ * device pointers may be recorded; calls that copy host data or wait return
+ * an error while recording.  pb_graph_launch enqueues one replay on the
+ * context stream. */
+typedef struct pb_graph pb_graph;
+int pb_capture_begin(pb_ctx* ctx);
+int pb_capture_end(pb_ctx* ctx, pb_graph** out);
+int pb_graph_launch(pb_ctx* ctx, pb_graph* g);
+int pb_graph_free(pb_graph* g);
+
 /* ------------------------------------------------------------------ */
 /* device memory (memory.js:87-155 PureBeeMemory, now device resident)   */
 /* ------------------------------------------------------------------ */
@@ -90,9 +108,11 @@ int pb_memcpy_d2d(pb_ctx* ctx, void* dst_dev, const void* src_dev, size_t bytes)
 /* ------------------------------------------------------------------ */
 
 /* Upload GGUF blocks of an [N rows][K cols] matrix (K % 32 == 0) and repack
- * them into the device layout.  type: PB_TYPE_Q4_0, PB_TYPE_Q4_1 or
- * PB_TYPE_Q8_0.  Replaces the raw cache of streaming-loader.js:119-162 /
- * 245-262 (raw GGUF bytes kept resident for the Q4 path). */
+ * them into a device layout.  type: PB_TYPE_Q4_0, PB_TYPE_Q4_1 or
+ * PB_TYPE_Q8_0, plus PB_QMAT_TABLE for an LM-head table (pb_qmat_head);
+ * without it the matrix is laid out for pb_qmat_matvec.  Replaces the raw
+ * cache of streaming-loader.js:119-162 / 245-262 (raw GGUF bytes kept
+ * resident for the Q4 path). */
 int pb_qmat_upload(pb_ctx* ctx, int type, const void* gguf_host, int N, int K, pb_qmat** out);
 /* Same from GGUF bytes already on the device. */
 int pb_qmat_from_device(pb_ctx* ctx, int type, const void* gguf_dev, int N, int K, pb_qmat** out);
@@ -119,9 +139,9 @@ int pb_q4_1_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, in
 /* wasm-q4.js:798-839 lmHead(hidden, embData, V, D): f32 row-major table on
  * the host, batch_dot lane order (wasm-q4.js:447-566). */
 int pb_lm_head(pb_ctx* ctx, const float* h_host, const float* emb_host, int V, int D, float* logits_host);
-/* Head over a resident table (Q4_0 / Q8_0 tiles, dequantized exactly as
- * gguf.js:239-286 does), batch_dot lane order, fused greedy argmax
- * (llama-streaming.js:899-909).  argmax_dev may be NULL. */
+/* Head over a resident table (Q4_0 / Q8_0, uploaded with PB_QMAT_TABLE;
+ * dequantized exactly as gguf.js:239-286 does), batch_dot lane order, fused
+ * greedy argmax (llama-streaming.js:899-909).  argmax_dev may be NULL. */
 int pb_qmat_head(pb_ctx* ctx, const pb_qmat* emb, const float* h_dev, float* logits_dev, int* argmax_dev);
 /* argmax over logits: first index of the strict maximum. */
 int pb_argmax(pb_ctx* ctx, const float* logits_dev, int n, int* idx_dev);

@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(HERE, "libpurebee_b200.so")
 
 PB_OK, PB_ERR_ARG, PB_ERR_OOM, PB_ERR_CUDA, PB_ERR_TIMEOUT, PB_ERR_DEVICE, PB_ERR_STATE, PB_ERR_NOTFOUND = range(8)
 TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q4_1, TYPE_Q8_0 = 0, 1, 2, 3, 8
+QMAT_TABLE = 0x100  # OR into the type: LM-head table layout (pb_qmat_head)
 MODEL_STREAMING_Q4, MODEL_LLAMA_Q8A = 0, 1
 
 _ERRNAMES = {1: "PB_ERR_ARG", 2: "PB_ERR_OOM", 3: "PB_ERR_CUDA", 4: "PB_ERR_TIMEOUT", 5: "PB_ERR_DEVICE",
@@ -55,6 +56,10 @@ SIGNATURES = {
     "pb_stream": (V, [V]),
     "pb_device_error": (I, [V, ctypes.POINTER(I)]),
     "pb_launch_count": (I64, [V]),
+    "pb_capture_begin": (I, [V]),
+    "pb_capture_end": (I, [V, ctypes.POINTER(V)]),
+    "pb_graph_launch": (I, [V, V]),
+    "pb_graph_free": (I, [V]),
     "pb_malloc": (I, [V, SZ, ctypes.POINTER(V)]),
     "pb_free": (I, [V, V]),
     "pb_upload": (I, [V, V, V, SZ]),
@@ -215,6 +220,17 @@ class Context:
         b.upload(a)
         return b
 
+    def capture(self, fn) -> "Graph":
+        """Record the device-pointer calls fn() makes into a replayable graph."""
+        self._check(lib().pb_capture_begin(self.h))
+        try:
+            fn()
+        finally:
+            g = V()
+            rc = lib().pb_capture_end(self.h, ctypes.byref(g))
+        self._check(rc)
+        return Graph(self, g.value)
+
     def device_error(self) -> int:
         c = I()
         self._check(lib().pb_device_error(self.h, ctypes.byref(c)))
@@ -230,7 +246,7 @@ class QMat:
         h = V()
         ctx._check(lib().pb_qmat_upload(ctx.h, type_, ptr(g), N, K, ctypes.byref(h)))
         self.h = h.value
-        self.type, self.N, self.K = type_, N, K
+        self.type, self.N, self.K = type_ & ~QMAT_TABLE, N, K
 
     def gguf_bytes(self) -> np.ndarray:
         bb = {TYPE_Q4_0: 18, TYPE_Q4_1: 20, TYPE_Q8_0: 34}[self.type]
@@ -241,6 +257,27 @@ class QMat:
     def free(self):
         if self.h and self.ctx.h:
             lib().pb_qmat_free(self.ctx.h, self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Graph:
+    """A recorded sequence of calls (pb_capture_begin / pb_capture_end)."""
+
+    def __init__(self, ctx: Context, h):
+        self.ctx, self.h = ctx, h
+
+    def launch(self) -> None:
+        self.ctx._check(lib().pb_graph_launch(self.ctx.h, self.h))
+
+    def free(self) -> None:
+        if self.h:
+            lib().pb_graph_free(self.h)
         self.h = None
 
     def __del__(self):

@@ -104,6 +104,7 @@ extern "C" int pb_init(int device, pb_ctx** out) {
   ctx->sm_count = prop.multiProcessorCount;
   const char* nopdl = getenv("PB_NO_PDL");  // programmatic dependent launch off (debugging aid)
   ctx->pdl = !(nopdl && nopdl[0] == '1');
+
   ctx->l2_bytes = prop.l2CacheSize;
   if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) { delete ctx; return PB_ERR_CUDA; }
   if (cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess) { delete ctx; return PB_ERR_OOM; }
@@ -166,6 +167,59 @@ extern "C" int pb_device_error(pb_ctx* ctx, int* code_out) {
 }
 
 extern "C" int64_t pb_launch_count(pb_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+// ============================================================================
+// capture / replay
+// ============================================================================
+
+struct pb_graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
+extern "C" int pb_capture_begin(pb_ctx* ctx) {
+  if (!ctx) return PB_ERR_ARG;
+  // thread-local mode: an unrelated thread's CUDA calls are not disturbed, and
+  // a blocking call on this thread fails instead of being recorded
+  PB_TRY_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  return PB_OK;
+}
+
+extern "C" int pb_capture_end(pb_ctx* ctx, pb_graph** out) {
+  if (!ctx || !out) return PB_ERR_ARG;
+  *out = nullptr;
+  cudaGraph_t g = nullptr;
+  cudaError_t ec = cudaStreamEndCapture(ctx->stream, &g);
+  if (ec != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    (void)cudaGetLastError();  // the failed recording must not surface in a later launch check
+    return pb_cuda_error(ctx, ec, "recording was invalidated (a blocking call was made while recording)");
+  }
+  pb_graph* pg = new pb_graph();
+  pg->graph = g;
+  cudaError_t e = cudaGraphInstantiate(&pg->exec, g, 0);
+  if (e != cudaSuccess) {
+    cudaGraphDestroy(g);
+    delete pg;
+    return pb_cuda_error(ctx, e, "cudaGraphInstantiate");
+  }
+  *out = pg;
+  return PB_OK;
+}
+
+extern "C" int pb_graph_launch(pb_ctx* ctx, pb_graph* g) {
+  if (!ctx || !g) return PB_ERR_ARG;
+  PB_TRY_CUDA(ctx, cudaGraphLaunch(g->exec, ctx->stream));
+  return PB_OK;
+}
+
+extern "C" int pb_graph_free(pb_graph* g) {
+  if (!g) return PB_OK;
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  if (g->graph) cudaGraphDestroy(g->graph);
+  delete g;
+  return PB_OK;
+}
 
 // ============================================================================
 // device memory
@@ -481,12 +535,13 @@ extern "C" int pb_gguf_quantize(pb_ctx* ctx, int type, const float* x, int64_t n
 static int qbytes(int type) { return type == PB_TYPE_Q8_0 ? 32 : 16; }
 static int gguf_block_bytes(int type) { return type == PB_TYPE_Q4_0 ? 18 : type == PB_TYPE_Q4_1 ? 20 : 34; }
 
-int pb_qmat_alloc(pb_ctx* ctx, int type, int N, int K, pb_qmat** out) {
+int pb_qmat_alloc(pb_ctx* ctx, int type, int layout, int N, int K, pb_qmat** out) {
   if (!ctx || !out || N <= 0 || K <= 0 || K % 32) return pb_set_error(ctx, PB_ERR_ARG, "matrix shape %dx%d: K must be a multiple of 32", N, K);
   if (type != PB_TYPE_Q4_0 && type != PB_TYPE_Q4_1 && type != PB_TYPE_Q8_0)
     return pb_set_error(ctx, PB_ERR_ARG, "unsupported matrix type %d", type);
   pb_qmat* m = new pb_qmat();
   m->type = type;
+  m->layout = layout;
   m->N = N;
   m->K = K;
   m->N_pad = (N + 31) / 32 * 32;
@@ -508,9 +563,9 @@ int pb_qmat_alloc(pb_ctx* ctx, int type, int N, int K, pb_qmat** out) {
   return PB_OK;
 }
 
-// GGUF [N][nb][block] -> tiles [N/32][nb][32][payload]; one thread per block.
-__global__ void k_qmat_pack(int type, const uint8_t* __restrict__ src, int N, int nb, uint8_t* __restrict__ qs,
-                            uint16_t* __restrict__ d, uint16_t* __restrict__ mn, int unpack) {
+// GGUF [N][nb][block] <-> the device layout; one thread per block.
+__global__ void k_qmat_pack(int type, int layout, const uint8_t* __restrict__ src, int N, int nb,
+                            uint8_t* __restrict__ qs, uint16_t* __restrict__ d, uint16_t* __restrict__ mn, int unpack) {
   int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int64_t total = (int64_t)N * nb;
   if (t >= total) return;
@@ -519,7 +574,7 @@ __global__ void k_qmat_pack(int type, const uint8_t* __restrict__ src, int N, in
   int hdr = type == PB_TYPE_Q4_1 ? 4 : 2;
   int pl = type == PB_TYPE_Q8_0 ? 32 : 16;
   uint8_t* g = (uint8_t*)src + t * bb;
-  int64_t slot = pb_qslot(n, b, nb);
+  int64_t slot = pb_slot(layout, n, b, nb);
   uint8_t* p = qs + slot * pl;
   if (!unpack) {
     d[slot] = (uint16_t)(g[0] | (g[1] << 8));
@@ -540,15 +595,17 @@ __global__ void k_qmat_pack(int type, const uint8_t* __restrict__ src, int N, in
 
 int pb_qmat_pack_from_device(pb_ctx* ctx, pb_qmat* m, const void* gguf_dev) {
   int64_t total = (int64_t)m->N * m->nb;
-  k_qmat_pack<<<pb_cdiv(total, 256), 256, 0, ctx->stream>>>(m->type, (const uint8_t*)gguf_dev, m->N, m->nb, m->qs,
-                                                            m->d, m->m, 0);
+  k_qmat_pack<<<pb_cdiv(total, 256), 256, 0, ctx->stream>>>(m->type, m->layout, (const uint8_t*)gguf_dev, m->N,
+                                                            m->nb, m->qs, m->d, m->m, 0);
   PB_LAUNCHED(ctx, "k_qmat_pack");
   return PB_OK;
 }
 
 extern "C" int pb_qmat_from_device(pb_ctx* ctx, int type, const void* gguf_dev, int N, int K, pb_qmat** out) {
   if (!ctx || !gguf_dev || !out) return PB_ERR_ARG;
-  PB_TRY(pb_qmat_alloc(ctx, type, N, K, out));
+  const int layout = (type & PB_QMAT_TABLE) ? PB_LAYOUT_TILED8 : PB_LAYOUT_ROWS;
+  type &= ~PB_QMAT_TABLE;
+  PB_TRY(pb_qmat_alloc(ctx, type, layout, N, K, out));
   int rc = pb_qmat_pack_from_device(ctx, *out, gguf_dev);
   if (rc != PB_OK) { pb_qmat_free(ctx, *out); *out = nullptr; }
   return rc;
@@ -557,7 +614,7 @@ extern "C" int pb_qmat_from_device(pb_ctx* ctx, int type, const void* gguf_dev, 
 extern "C" int pb_qmat_upload(pb_ctx* ctx, int type, const void* gguf_host, int N, int K, pb_qmat** out) {
   if (!ctx || !gguf_host || !out) return PB_ERR_ARG;
   if (K % 32 || N <= 0) return pb_set_error(ctx, PB_ERR_ARG, "matrix shape %dx%d: K must be a multiple of 32", N, K);
-  size_t bytes = (size_t)N * (K / 32) * gguf_block_bytes(type);
+  size_t bytes = (size_t)N * (K / 32) * gguf_block_bytes(type & ~PB_QMAT_TABLE);
   PB_TRY(pb_ensure_scratch(ctx, bytes));
   PB_TRY_CUDA(ctx, cudaMemcpyAsync(ctx->scratch, gguf_host, bytes, cudaMemcpyHostToDevice, ctx->stream));
   PB_TRY(pb_qmat_from_device(ctx, type, ctx->scratch, N, K, out));
@@ -569,8 +626,8 @@ extern "C" int pb_qmat_download_gguf(pb_ctx* ctx, const pb_qmat* m, void* gguf_h
   size_t bytes = (size_t)m->N * m->nb * gguf_block_bytes(m->type);
   PB_TRY(pb_ensure_scratch(ctx, bytes));
   int64_t total = (int64_t)m->N * m->nb;
-  k_qmat_pack<<<pb_cdiv(total, 256), 256, 0, ctx->stream>>>(m->type, (const uint8_t*)ctx->scratch, m->N, m->nb,
-                                                            m->qs, m->d, m->m, 1);
+  k_qmat_pack<<<pb_cdiv(total, 256), 256, 0, ctx->stream>>>(m->type, m->layout, (const uint8_t*)ctx->scratch, m->N,
+                                                            m->nb, m->qs, m->d, m->m, 1);
   PB_LAUNCHED(ctx, "k_qmat_unpack");
   PB_TRY_CUDA(ctx, cudaMemcpyAsync(gguf_host, ctx->scratch, bytes, cudaMemcpyDeviceToHost, ctx->stream));
   return pb_wait(ctx);

@@ -24,15 +24,21 @@ struct pb_ctx {
   size_t scratch_bytes = 0;
 };
 
-// Device layout of a quantized matrix, in 8-row tiles:
-//   qs: [N_pad/8 tiles][nb blocks][8 rows][QB bytes]  (QB = 16 for Q4, 32 for Q8)
-//   d : [N_pad/8 tiles][nb blocks][8 rows] u16 scale (Q4_1: a second array m)
-// One tile is contiguous (nb * 8 * QB bytes of payload, nb * 16 bytes of
-// scales), so a CTA that owns 8 rows fetches them with one bulk copy each, and
-// any block column of 8 consecutive rows is one 128 B (Q4) line.
-// N_pad rounds N up to 32 so a warp of 32 rows never reads past the end.
+// Device layouts of a quantized matrix (payload and scales split apart, so
+// every payload is 16-byte aligned; QB = 16 bytes for Q4, 32 for Q8):
+//   PB_LAYOUT_ROWS   (matvec weights): qs [N_pad][nb][QB], d [N_pad][nb] u16
+//     (Q4_1: a second array m).  Eight consecutive rows are one contiguous
+//     tile, and a warp reading block b..b+31 of one row reads 512 B in a row.
+//   PB_LAYOUT_TILED8 (tables read one row per lane: LM head, embedding):
+//     qs [N_pad/8][nb][8][QB], d [N_pad/8][nb][8]; block b of 8 consecutive
+//     rows is one 128 B (Q4) line.
+// N_pad rounds N up to 32; the padding rows hold zeros.
+#define PB_LAYOUT_ROWS 0
+#define PB_LAYOUT_TILED8 1
+
 struct pb_qmat {
   int type = 0;
+  int layout = PB_LAYOUT_ROWS;
   int N = 0, K = 0, N_pad = 0, nb = 0;
   uint8_t* qs = nullptr;
   uint16_t* d = nullptr;
@@ -105,6 +111,32 @@ __host__ __device__ __forceinline__ int64_t pb_qslot(int row, int b, int nb) {
   return ((int64_t)(row >> 3) * nb + b) * 8 + (row & 7);
 }
 
+// Index of (row, block) in either layout.
+__host__ __device__ __forceinline__ int64_t pb_slot(int layout, int row, int b, int nb) {
+  return layout == PB_LAYOUT_TILED8 ? pb_qslot(row, b, nb) : (int64_t)row * nb + b;
+}
+
+// Fire-and-forget bulk prefetch of [p, p + bytes) into L2 (p and bytes
+// multiples of 16).
+__device__ __forceinline__ void pb_l2_prefetch(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// CTA share i of n of a region, prefetched into L2 in pieces of at most 64 KB
+// (one thread issues them).
+__device__ __forceinline__ void pb_l2_prefetch_share(const void* base, size_t bytes, int i, int n) {
+  if (!base || !bytes) return;
+  const size_t per = ((bytes + n - 1) / n + 15) & ~(size_t)15;
+  size_t lo = (size_t)i * per;
+  if (lo >= bytes) return;
+  size_t hi = lo + per < bytes ? lo + per : bytes;
+  hi &= ~(size_t)15;
+  for (size_t o = lo; o < hi; o += 65536) {
+    const size_t n_ = hi - o < 65536 ? hi - o : 65536;
+    pb_l2_prefetch((const char*)base + o, (uint32_t)n_);
+  }
+}
+
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait for the previous kernel's results.
 __device__ __forceinline__ void pb_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -171,8 +203,14 @@ __device__ __forceinline__ double pb_block_sum_d(double v, double* red) {
 #define PB_EPI_ROPE_KV 2   // rows [q | k | v]: RoPE q, k; k, v into the cache at pos (:531-541)
 #define PB_EPI_SWIGLU4 3   // tiles [g_4i..g_4i+3 | u_4i..u_4i+3]: h_i = silu(g_i)*u_i (:590-595)
 
+#define PB_MAX_L2_NEXT 4
 struct pb_mv_epi {
   int kind = PB_EPI_STORE;
+  const float* norm_w = nullptr;  // when set, x is first RMS-normalised with these gains (engine.js:429-449)
+  double eps = 1e-5;
+  // regions later kernels read, prefetched into L2 by this one
+  const void* l2_next[PB_MAX_L2_NEXT] = {};
+  size_t l2_next_bytes[PB_MAX_L2_NEXT] = {};
   const float* residual = nullptr;
   const double2* rope_tab = nullptr;
   const int* pos_dev = nullptr;
@@ -190,7 +228,7 @@ int pb_launch_head(pb_ctx* ctx, const pb_qmat* emb, const float* h, float* logit
 int pb_launch_head_norm(pb_ctx* ctx, const pb_qmat* emb, const float* h, const float* norm_w, double eps,
                         float* logits, unsigned long long* argmax_key, int mode);
 int pb_launch_argmax_finish(pb_ctx* ctx, const unsigned long long* key, int* idx);
-int pb_qmat_alloc(pb_ctx* ctx, int type, int N, int K, pb_qmat** out);
+int pb_qmat_alloc(pb_ctx* ctx, int type, int layout, int N, int K, pb_qmat** out);
 int pb_qmat_pack_from_device(pb_ctx* ctx, pb_qmat* m, const void* gguf_dev);
 int pb_setup_q4_kernels(void);
 int pb_setup_ops_kernels(void);

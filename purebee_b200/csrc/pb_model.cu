@@ -24,7 +24,6 @@ int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx,
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
                           int n_heads, int n_kv, int hd, float* out, int max_len, float* scratch);
 size_t pb_attn_decode_scratch_floats(int n_heads, int max_len);
-int pb_launch_rmsnorm_row(pb_ctx* ctx, const float* x, int dim, const float* w, double eps, float* out);
 __global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
                           float* __restrict__ out);
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
@@ -172,14 +171,14 @@ extern "C" int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model
   auto fail = [&](int code) { pb_model_free(m); return code; };
   const int L = c.n_layers;
   if (c.kind == PB_MODEL_STREAMING_Q4) {
-    rc = pb_qmat_alloc(ctx, c.emb_type, c.vocab, c.dim, &m->emb);
+    rc = pb_qmat_alloc(ctx, c.emb_type, PB_LAYOUT_TILED8, c.vocab, c.dim, &m->emb);
     if (rc) return fail(rc);
     m->qkv.assign(L, nullptr); m->wo.assign(L, nullptr); m->gu.assign(L, nullptr); m->w2.assign(L, nullptr);
     for (int l = 0; l < L; ++l) {
-      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, c.dim + 2 * m->kv_dim, c.dim, &m->qkv[l]))) return fail(rc);
-      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, c.dim, c.dim, &m->wo[l]))) return fail(rc);
-      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, 2 * c.hidden_dim, c.dim, &m->gu[l]))) return fail(rc);
-      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, c.dim, c.hidden_dim, &m->w2[l]))) return fail(rc);
+      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, PB_LAYOUT_ROWS, c.dim + 2 * m->kv_dim, c.dim, &m->qkv[l]))) return fail(rc);
+      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, PB_LAYOUT_ROWS, c.dim, c.dim, &m->wo[l]))) return fail(rc);
+      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, PB_LAYOUT_ROWS, 2 * c.hidden_dim, c.dim, &m->gu[l]))) return fail(rc);
+      if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, PB_LAYOUT_ROWS, c.dim, c.hidden_dim, &m->w2[l]))) return fail(rc);
     }
   } else {
     size_t ntile = (size_t)((c.vocab + 31) / 32) * 32;
@@ -251,19 +250,19 @@ static pb_qmat* fused_target(pb_model* m, int l, int which, int* row_off, int* i
   }
 }
 
-// GGUF rows -> tiles at a row offset of an existing matrix
+// GGUF rows -> the device layout at a row offset of an existing matrix
 // interleave4: GGUF row i goes to tile row 8*(i/4) + i%4 + row_off, so an
 // 8-row tile holds gate rows 4i..4i+3 (row_off 0) and up rows 4i..4i+3
 // (row_off 4) and the gate|up matvec can finish SwiGLU in its epilogue.
 __global__ void k_pack_rows(const uint8_t* __restrict__ src, int rows, int row_off, int interleave4, int nb, int type,
-                            uint8_t* __restrict__ qs, uint16_t* __restrict__ d, int unpack) {
+                            int layout, uint8_t* __restrict__ qs, uint16_t* __restrict__ d, int unpack) {
   int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= (int64_t)rows * nb) return;
   int i = (int)(t / nb), b = (int)(t % nb);
   int n = interleave4 ? 8 * (i >> 2) + (i & 3) + row_off : i + row_off;
   int bb = type == PB_TYPE_Q4_0 ? 18 : 34, pl = type == PB_TYPE_Q4_0 ? 16 : 32;
   uint8_t* g = (uint8_t*)src + t * bb;
-  int64_t slot = pb_qslot(n, b, nb);
+  int64_t slot = pb_slot(layout, n, b, nb);
   if (!unpack) {
     d[slot] = (uint16_t)(g[0] | (g[1] << 8));
     for (int i = 0; i < pl; ++i) qs[slot * pl + i] = g[2 + i];
@@ -288,7 +287,7 @@ static int pack_rows(pb_model* m, pb_qmat* dst, const void* gguf_dev, int rows, 
   pb_ctx* ctx = m->ctx;
   int64_t tot = (int64_t)rows * dst->nb;
   k_pack_rows<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>((const uint8_t*)gguf_dev, rows, row_off, interleave4,
-                                                          dst->nb, dst->type, dst->qs, dst->d, 0);
+                                                          dst->nb, dst->type, dst->layout, dst->qs, dst->d, 0);
   PB_LAUNCHED(ctx, "k_pack_rows");
   return PB_OK;
 }
@@ -405,7 +404,7 @@ static int model_tensor_io(pb_model* m, int layer, int which, void* host, size_t
   if (!get) PB_TRY_CUDA(ctx, cudaMemcpyAsync(ctx->scratch, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
   int64_t tot = (int64_t)rows * dst->nb;
   k_pack_rows<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>((const uint8_t*)ctx->scratch, rows, off, il, dst->nb,
-                                                          dst->type, dst->qs, dst->d, get);
+                                                          dst->type, dst->layout, dst->qs, dst->d, get);
   PB_LAUNCHED(ctx, "k_pack_rows");
   if (get) PB_TRY_CUDA(ctx, cudaMemcpyAsync(host, ctx->scratch, bytes, cudaMemcpyDeviceToHost, ctx->stream));
   return pb_wait(ctx);
@@ -436,6 +435,18 @@ static int launch_q8a(pb_model* m, int l, int which, const float* A, int M, floa
   return pb_matmul_q8a(m->ctx, A, M, k, m->q8s[l * 7 + which - 1], m->q8q[l * 7 + which - 1], r, nullptr, out);
 }
 
+// Prefetch hint: the payload and scales of w (the payload capped at cap
+// bytes) in slots i, i + 1 of the epilogue's L2 list.
+static void l2_hint(pb_mv_epi* e, int i, const pb_qmat* w, size_t cap = ~(size_t)0) {
+  if (!w) return;
+  const size_t nblk = (size_t)w->N_pad * w->nb;
+  const size_t qb = nblk * (w->type == PB_TYPE_Q8_0 ? 32 : 16);
+  e->l2_next[i] = w->qs;
+  e->l2_next_bytes[i] = qb < cap ? qb : cap;
+  e->l2_next[i + 1] = w->d;
+  e->l2_next_bytes[i + 1] = (nblk * 2) & ~(size_t)15;
+}
+
 // Decode layer (M == 1) of the streaming model: four fused matvecs and the
 // attention (llama-streaming.js:505-606).
 static int run_layer_decode_q4(pb_model* m, int l) {
@@ -443,9 +454,14 @@ static int run_layer_decode_q4(pb_model* m, int l) {
   const pb_model_config& c = m->c;
   const int dim = c.dim, kv = m->kv_dim;
   const int* pos_dev = m->tok_dev + 1;
+  const bool last = l + 1 == c.n_layers;
+  // Each matvec also prefetches into L2 the weights of the matvecs after it,
+  // so HBM keeps streaming while the attention and the chains run.
   pb_mv_epi e;
   // RMSNorm -> [wq; wk; wv] -> RoPE on q, k; k, v into the cache at pos
   e.kind = PB_EPI_ROPE_KV;
+  e.norm_w = m->rms_att + (size_t)l * dim;
+  e.eps = c.eps;
   e.rope_tab = m->rope_tab;
   e.pos_dev = pos_dev;
   e.q_rows = dim;
@@ -454,23 +470,35 @@ static int run_layer_decode_q4(pb_model* m, int l) {
   e.max_len = c.seq_len;
   e.kc = kcache(m, l);
   e.vc = vcache(m, l);
-  PB_TRY(pb_launch_rmsnorm_row(ctx, m->x, dim, m->rms_att + (size_t)l * dim, c.eps, m->xn));
-  PB_TRY(pb_launch_matvec(ctx, m->qkv[l], m->xn, m->qkvo, 0, dim + 2 * kv, &e));
+  l2_hint(&e, 0, m->wo[l]);
+  l2_hint(&e, 2, m->w2[l]);
+  PB_TRY(pb_launch_matvec(ctx, m->qkv[l], m->x, m->qkvo, 0, dim + 2 * kv, &e));
   PB_TRY(pb_launch_attn_decode(ctx, m->qkvo, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads,
                                c.head_dim, m->att, c.seq_len, m->att_scratch));
   // wo with the residual add
   pb_mv_epi r;
   r.kind = PB_EPI_RESIDUAL;
   r.residual = m->x;
+  l2_hint(&r, 0, m->gu[l]);
   PB_TRY(pb_launch_matvec(ctx, m->wo[l], m->att, m->x, 0, dim, &r));
   // RMSNorm -> [w1 | w3] interleaved -> SwiGLU
   pb_mv_epi g;
   g.kind = PB_EPI_SWIGLU4;
+  g.norm_w = m->rms_ffn + (size_t)l * dim;
+  g.eps = c.eps;
   g.h_out = m->hb;
-  PB_TRY(pb_launch_rmsnorm_row(ctx, m->x, dim, m->rms_ffn + (size_t)l * dim, c.eps, m->xn));
-  PB_TRY(pb_launch_matvec(ctx, m->gu[l], m->xn, nullptr, 0, 2 * c.hidden_dim, &g));
+  if (!last) {
+    l2_hint(&g, 0, m->qkv[l + 1]);
+    l2_hint(&g, 2, m->wo[l + 1]);
+  }
+  PB_TRY(pb_launch_matvec(ctx, m->gu[l], m->x, nullptr, 0, 2 * c.hidden_dim, &g));
   // w2 with the residual add
-  PB_TRY(pb_launch_matvec(ctx, m->w2[l], m->hb, m->x, 0, dim, &r));
+  pb_mv_epi r2 = r;
+  r2.l2_next[0] = r2.l2_next[1] = nullptr;
+  r2.l2_next_bytes[0] = r2.l2_next_bytes[1] = 0;
+  if (!last) l2_hint(&r2, 0, m->gu[l + 1]);
+  else if (m->emb && m->emb->type != PB_TYPE_F32) l2_hint(&r2, 0, m->emb, (size_t)48 << 20);
+  PB_TRY(pb_launch_matvec(ctx, m->w2[l], m->hb, m->x, 0, dim, &r2));
   return PB_OK;
 }
 

@@ -31,28 +31,6 @@ __global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __r
     out[(size_t)blockIdx.x * dim + d] = (float)__dmul_rn(__ddiv_rn((double)xr[d], rms), (double)w[d]);
 }
 
-// Decode-step RMSNorm of one row, spread over ceil(dim / 256) CTAs: each CTA
-// forms the same sum of squares with the k_rmsnorm tree (so the values equal
-// k_rmsnorm's) and writes its 256-wide slice.  Launched as a dependent launch:
-// the matvec after it starts fetching weights while this runs.
-__global__ void __launch_bounds__(256)
-k_rmsnorm_row(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps, float* __restrict__ out) {
-  __shared__ double red[32];
-  pb_pdl_trigger();
-  pb_pdl_wait();
-  double ss = 0.0;
-  for (int d = threadIdx.x; d < dim; d += blockDim.x) ss = __fma_rn((double)x[d], (double)x[d], ss);
-  ss = pb_block_sum_d(ss, red);
-  const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)dim), eps));
-  const int d = blockIdx.x * blockDim.x + threadIdx.x;
-  if (d < dim) out[d] = (float)__dmul_rn(__ddiv_rn((double)x[d], rms), (double)w[d]);
-}
-
-int pb_launch_rmsnorm_row(pb_ctx* ctx, const float* x, int dim, const float* w, double eps, float* out) {
-  return pb_launch(ctx, "k_rmsnorm_row", true, k_rmsnorm_row, dim3(pb_cdiv(dim, 256)), dim3(256), 0, x, dim, w, eps,
-                   out);
-}
-
 extern "C" int pb_rmsnorm(pb_ctx* ctx, const float* x, int seq, int dim, const float* w, double eps, float* out) {
   if (!ctx || !x || !w || !out || seq <= 0 || dim <= 0) return PB_ERR_ARG;
   k_rmsnorm<<<seq, 256, 0, ctx->stream>>>(x, dim, w, eps, out);

@@ -20,41 +20,9 @@
 // The greedy argmax (llama-streaming.js:899-909) is fused as an ordered-key
 // atomicMax.
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "pb_internal.cuh"
-
-// ---------------------------------------------------------------------------
-// mbarrier helpers with bounded waits
-// ---------------------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(smem_u32(bar)) : "memory");
-}
-// Wait for the phase with the given parity to complete; gives up after about
-// two seconds of device clock, records PB_DEVERR_WAIT and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  uint32_t addr = smem_u32(bar);
-  long long t0 = clock64();
-  for (uint32_t it = 0;; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(ok)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    if ((it & 255) == 255 && clock64() - t0 > 4000000000LL) {
-      pb_raise(err, PB_DEVERR_WAIT);
-      return false;
-    }
-  }
-}
 
 // ---------------------------------------------------------------------------
 // exact nibble -> float conversions
@@ -71,92 +39,60 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 
 __device__ __forceinline__ float mag(uint32_t w, uint32_t mask, uint32_t e) { return __uint_as_float((w & mask) | e); }
 
-// x chunk (4 floats) i of block b in the swizzled shared copy of x.
-__device__ __forceinline__ float4 xchunk(const float4* xs, int b, int i) { return xs[b * 8 + (i ^ (b & 7))]; }
-
-// Partial sums of one Q4_0 block for the four lanes (wasm-q4.js:193-229),
-// already multiplied by d.
-__device__ __forceinline__ float4 q4_0_block(uint4 pl, float d, const float4* xs, int b) {
-  float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-  uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    uint32_t w = wv[g], w2 = w >> 16;
-    float4 xl = xchunk(xs, b, g), xh = xchunk(xs, b, 4 + g);
-    float l0 = __fsub_rn(mag(w, 0xFu, PB_MAG0), 8388616.0f);
-    float h0 = __fsub_rn(mag(w, 0xF0u, PB_MAG4), 524296.0f);
-    float l1 = __fsub_rn(mag(w, 0xF00u, PB_MAG8), 32776.0f);
-    float h1 = __fsub_rn(mag(w, 0xF000u, PB_MAG12), 2056.0f);
-    float l2 = __fsub_rn(mag(w, 0xF0000u, PB_MAG16), 136.0f);
-    float h2 = __fsub_rn(mag(w2, 0xF0u, PB_MAG4), 524296.0f);
-    float l3 = __fsub_rn(mag(w2, 0xF00u, PB_MAG8), 32776.0f);
-    float h3 = __fsub_rn(mag(w2, 0xF000u, PB_MAG12), 2056.0f);
-    a0 = __fadd_rn(a0, __fmul_rn(l0, xl.x));
-    a1 = __fadd_rn(a1, __fmul_rn(l1, xl.y));
-    a2 = __fadd_rn(a2, __fmul_rn(l2, xl.z));
-    a3 = __fadd_rn(a3, __fmul_rn(l3, xl.w));
-    a0 = __fadd_rn(a0, __fmul_rn(h0, xh.x));
-    a1 = __fadd_rn(a1, __fmul_rn(h1, xh.y));
-    a2 = __fadd_rn(a2, __fmul_rn(h2, xh.z));
-    a3 = __fadd_rn(a3, __fmul_rn(h3, xh.w));
-  }
-  return make_float4(__fmul_rn(a0, d), __fmul_rn(a1, d), __fmul_rn(a2, d), __fmul_rn(a3, d));
+// (w & MASK) | e as one three-input logic op, e held in a register (the
+// exponent patterns come in as kernel arguments, so they stay in registers
+// instead of being rebuilt from immediates).
+template <uint32_t MASK>
+__device__ __forceinline__ float magr(uint32_t w, uint32_t e) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w), "n"(MASK), "r"(e));
+  return __uint_as_float(r);
 }
 
-// Q4_1 (wasm-q4.js:357-398): nibAcc += n*x, xAcc += x per lane (lo then hi),
-// block value nibAcc*delta + xAcc*min.
-__device__ __forceinline__ float4 q4_1_block(uint4 pl, float dl, float mn, const float4* xs, int b) {
-  float n0 = 0, n1 = 0, n2 = 0, n3 = 0, s0 = 0, s1 = 0, s2 = 0, s3 = 0;
-  uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    uint32_t w = wv[g], w2 = w >> 16;
-    float4 xl = xchunk(xs, b, g), xh = xchunk(xs, b, 4 + g);
-    float l0 = __fsub_rn(mag(w, 0xFu, PB_MAG0), 8388608.0f);
-    float h0 = __fsub_rn(mag(w, 0xF0u, PB_MAG4), 524288.0f);
-    float l1 = __fsub_rn(mag(w, 0xF00u, PB_MAG8), 32768.0f);
-    float h1 = __fsub_rn(mag(w, 0xF000u, PB_MAG12), 2048.0f);
-    float l2 = __fsub_rn(mag(w, 0xF0000u, PB_MAG16), 128.0f);
-    float h2 = __fsub_rn(mag(w2, 0xF0u, PB_MAG4), 524288.0f);
-    float l3 = __fsub_rn(mag(w2, 0xF00u, PB_MAG8), 32768.0f);
-    float h3 = __fsub_rn(mag(w2, 0xF000u, PB_MAG12), 2048.0f);
-    n0 = __fadd_rn(n0, __fmul_rn(l0, xl.x)); s0 = __fadd_rn(s0, xl.x);
-    n1 = __fadd_rn(n1, __fmul_rn(l1, xl.y)); s1 = __fadd_rn(s1, xl.y);
-    n2 = __fadd_rn(n2, __fmul_rn(l2, xl.z)); s2 = __fadd_rn(s2, xl.z);
-    n3 = __fadd_rn(n3, __fmul_rn(l3, xl.w)); s3 = __fadd_rn(s3, xl.w);
-    n0 = __fadd_rn(n0, __fmul_rn(h0, xh.x)); s0 = __fadd_rn(s0, xh.x);
-    n1 = __fadd_rn(n1, __fmul_rn(h1, xh.y)); s1 = __fadd_rn(s1, xh.y);
-    n2 = __fadd_rn(n2, __fmul_rn(h2, xh.z)); s2 = __fadd_rn(s2, xh.z);
-    n3 = __fadd_rn(n3, __fmul_rn(h3, xh.w)); s3 = __fadd_rn(s3, xh.w);
-  }
-  return make_float4(__fadd_rn(__fmul_rn(n0, dl), __fmul_rn(s0, mn)), __fadd_rn(__fmul_rn(n1, dl), __fmul_rn(s1, mn)),
-                     __fadd_rn(__fmul_rn(n2, dl), __fmul_rn(s2, mn)), __fadd_rn(__fmul_rn(n3, dl), __fmul_rn(s3, mn)));
-}
+struct pb_magics {
+  uint32_t m0, m4, m8, m12, m16;
+};
 
 // ---------------------------------------------------------------------------
 // matvec kernel
 // ---------------------------------------------------------------------------
-// Persistent CTAs, each owning 8-row tiles t = first + k * gridDim.x.
-//   - each thread owns (row r = tid & 7, blocks bb, bb + 32, ...) of a tile;
-//     its 16 B payloads and scales are loaded straight into registers with
-//     coalesced loads (a warp reads 4 x 128 B lines), the next tile's loads
-//     are issued before the current tile is computed, and the first tile's
-//     loads before griddepcontrol.wait (weights never depend on the previous
-//     kernel);
-//   - x goes to shared memory once per CTA, in float4 chunks swizzled within
-//     each 32-value block so the 4 blocks a warp touches hit distinct banks;
-//   - block partials of the WASM lane order (wasm-q4.js:193-229) go to shared
-//     memory; warp 0 runs the in-order chains acc[L] += partial over the
-//     blocks (4 lanes per row) and the fused epilogue writes the rows.
+// Persistent CTAs of MV_THREADS threads, one per SM.  A tile is 8 consecutive
+// rows (contiguous in the row-major device layout); a CTA works on
+// S = MV_THREADS / (2 nb) tiles at a time ("slots").
+//   - thread (slot s, half h, block b) keeps x[32b .. 32b+31] in registers for
+//     the whole kernel (RMS-normalised in the prologue when the epilogue asks
+//     for it) and, for each tile of its slot, loads block b of rows
+//     4h .. 4h+3, so a warp reads 512 contiguous bytes per row;
+//   - every CTA first issues bulk L2 prefetches for all of its tiles and its
+//     share of the region the next kernel reads (before griddepcontrol.wait:
+//     weights never depend on the previous kernel), then keeps the next
+//     iteration's blocks in flight in registers while it computes;
+//   - the block partials of the WASM lane order (wasm-q4.js:193-229) go to
+//     shared memory (double-buffered); warp s then runs slot s's 32 in-order
+//     chains acc[L] += partial (8 rows x 4 lanes, wasm-q4.js:225-229) and the
+//     fused epilogue.
 
-constexpr int MV_THREADS = 256;
+constexpr int MV_THREADS = 512;
+constexpr int MV_RPT = 4;      // rows per thread
+constexpr int MV_PF_DIST = 4;  // iterations of L2 prefetch ahead of the loads
+
+// Tiles in flight per CTA ("slots"): 2 nb threads each, rounded up to whole
+// warps (a slot syncs on its own named barrier, ids 1..15).
+__host__ __device__ __forceinline__ int mv_slot_threads(int nb) { return (2 * nb + 31) / 32 * 32; }
+__host__ __device__ __forceinline__ int mv_slots(int nb, int nt) {
+  const int s = nt / mv_slot_threads(nb);
+  return s < 15 ? s : 15;
+}
 
 // Packed f32x2 arithmetic, each component rounded to nearest like the scalar
 // instruction.  The code generator fuses a packed multiply that feeds a packed
 // add into a packed FMA (one rounding instead of the reference's two), even
-// with .rn and --fmad=false, so products of f2mul are only ever consumed by
-// scalar __fadd_rn; f2add is used where its inputs are not products (exact
-// magic-number conversions).
+// with .rn and --fmad=false.  So a product that is summed afterwards is formed
+// as f2fma(a, b, nz) with nz = -0.0 passed in from the host: fma(a, b, -0)
+// rounds a*b exactly like mul.rn does (the -0 leaves +0 and -0 products
+// alone), and an FMA is never contracted into the add that follows.  nz comes
+// from a kernel argument so the compiler cannot turn the FMA back into a
+// multiply.
 __device__ __forceinline__ float2 f2mul(float2 a, float2 b) {
   float2 r;
   asm("{ .reg .b64 ra, rb, rd;\n\t"
@@ -194,198 +130,316 @@ __device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
 }
 
 
-// Q4_0 block partials for the four lanes, times d.  Conversions and products
-// are packed; the accumulation is scalar so nothing gets fused.
-__device__ __forceinline__ float4 q4_0_block_exact(uint4 pl, float d, const float4* xs, int b) {
-  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+// Q4_0 block partials of one row for the four lanes, times d, with the
+// block's x in registers (xr[j] = x[32b + j]).
+__device__ __forceinline__ float4 q4_0_row(uint4 pl, float d, const float (&xr)[32], float2 nz, const pb_magics& M) {
+  float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);  // blockAcc[0..1], [2..3]
   const uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     const uint32_t w = wv[g], w2 = w >> 16;
-    const float4 xl = xchunk(xs, b, g), xh = xchunk(xs, b, 4 + g);
-    // lane 0: lo bits 0-3, hi 4-7; lane 1: 8-11, 12-15; lane 2: 16-19, 20-23;
-    // lane 3: 24-27, 28-31 (bytes g..g+3 of the block, wasm-q4.js:200-223)
-    const float2 l01 = f2add(make_float2(mag(w, 0xFu, PB_MAG0), mag(w, 0xF00u, PB_MAG8)),
+    // byte 4g+L of the block feeds lane L: low nibble x[4g+L], high x[16+4g+L]
+    const float2 l01 = f2add(make_float2(magr<0xFu>(w, M.m0), magr<0xF00u>(w, M.m8)),
                              make_float2(-8388616.0f, -32776.0f));
-    const float2 l23 = f2add(make_float2(mag(w, 0xF0000u, PB_MAG16), mag(w2, 0xF00u, PB_MAG8)),
+    const float2 l23 = f2add(make_float2(magr<0xF0000u>(w, M.m16), magr<0xF00u>(w2, M.m8)),
                              make_float2(-136.0f, -32776.0f));
-    const float2 h01 = f2add(make_float2(mag(w, 0xF0u, PB_MAG4), mag(w, 0xF000u, PB_MAG12)),
+    const float2 h01 = f2add(make_float2(magr<0xF0u>(w, M.m4), magr<0xF000u>(w, M.m12)),
                              make_float2(-524296.0f, -2056.0f));
-    const float2 h23 = f2add(make_float2(mag(w2, 0xF0u, PB_MAG4), mag(w2, 0xF000u, PB_MAG12)),
+    const float2 h23 = f2add(make_float2(magr<0xF0u>(w2, M.m4), magr<0xF000u>(w2, M.m12)),
                              make_float2(-524296.0f, -2056.0f));
-    const float2 pl01 = f2mul(l01, make_float2(xl.x, xl.y)), pl23 = f2mul(l23, make_float2(xl.z, xl.w));
-    const float2 ph01 = f2mul(h01, make_float2(xh.x, xh.y)), ph23 = f2mul(h23, make_float2(xh.z, xh.w));
-    a0 = __fadd_rn(a0, pl01.x);
-    a1 = __fadd_rn(a1, pl01.y);
-    a2 = __fadd_rn(a2, pl23.x);
-    a3 = __fadd_rn(a3, pl23.y);
-    a0 = __fadd_rn(a0, ph01.x);
-    a1 = __fadd_rn(a1, ph01.y);
-    a2 = __fadd_rn(a2, ph23.x);
-    a3 = __fadd_rn(a3, ph23.y);
+    a01 = f2add(a01, f2fma(l01, make_float2(xr[4 * g], xr[4 * g + 1]), nz));
+    a23 = f2add(a23, f2fma(l23, make_float2(xr[4 * g + 2], xr[4 * g + 3]), nz));
+    a01 = f2add(a01, f2fma(h01, make_float2(xr[16 + 4 * g], xr[16 + 4 * g + 1]), nz));
+    a23 = f2add(a23, f2fma(h23, make_float2(xr[16 + 4 * g + 2], xr[16 + 4 * g + 3]), nz));
   }
-  return make_float4(__fmul_rn(a0, d), __fmul_rn(a1, d), __fmul_rn(a2, d), __fmul_rn(a3, d));
+  const float2 dd = make_float2(d, d);
+  const float2 r01 = f2mul(a01, dd), r23 = f2mul(a23, dd);
+  return make_float4(r01.x, r01.y, r23.x, r23.y);
 }
 
-template <int TYPE, int NI>
-struct MvRegs {
-  uint4 q[NI];
-  uint16_t d[NI];
-  uint16_t m[NI];
+// Two rows of the same block at once (the four accumulation chains of the two
+// rows are independent, so their adds overlap).
+__device__ __forceinline__ void q4_0_row2(uint4 pa, uint4 pb, float da, float db, const float (&xr)[32], float2 nz,
+                                          const pb_magics& M, float4& ra, float4& rb) {
+  float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+  float2 b01 = make_float2(0.f, 0.f), b23 = make_float2(0.f, 0.f);
+  const uint32_t wa[4] = {pa.x, pa.y, pa.z, pa.w}, wb[4] = {pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const float2 xl01 = make_float2(xr[4 * g], xr[4 * g + 1]), xl23 = make_float2(xr[4 * g + 2], xr[4 * g + 3]);
+    const float2 xh01 = make_float2(xr[16 + 4 * g], xr[16 + 4 * g + 1]);
+    const float2 xh23 = make_float2(xr[16 + 4 * g + 2], xr[16 + 4 * g + 3]);
+    const uint32_t w = wa[g], w2 = w >> 16, v = wb[g], v2 = v >> 16;
+    const float2 la01 = f2add(make_float2(magr<0xFu>(w, M.m0), magr<0xF00u>(w, M.m8)), make_float2(-8388616.0f, -32776.0f));
+    const float2 lb01 = f2add(make_float2(magr<0xFu>(v, M.m0), magr<0xF00u>(v, M.m8)), make_float2(-8388616.0f, -32776.0f));
+    const float2 la23 = f2add(make_float2(magr<0xF0000u>(w, M.m16), magr<0xF00u>(w2, M.m8)), make_float2(-136.0f, -32776.0f));
+    const float2 lb23 = f2add(make_float2(magr<0xF0000u>(v, M.m16), magr<0xF00u>(v2, M.m8)), make_float2(-136.0f, -32776.0f));
+    a01 = f2add(a01, f2fma(la01, xl01, nz));
+    b01 = f2add(b01, f2fma(lb01, xl01, nz));
+    a23 = f2add(a23, f2fma(la23, xl23, nz));
+    b23 = f2add(b23, f2fma(lb23, xl23, nz));
+    const float2 ha01 = f2add(make_float2(magr<0xF0u>(w, M.m4), magr<0xF000u>(w, M.m12)), make_float2(-524296.0f, -2056.0f));
+    const float2 hb01 = f2add(make_float2(magr<0xF0u>(v, M.m4), magr<0xF000u>(v, M.m12)), make_float2(-524296.0f, -2056.0f));
+    const float2 ha23 = f2add(make_float2(magr<0xF0u>(w2, M.m4), magr<0xF000u>(w2, M.m12)), make_float2(-524296.0f, -2056.0f));
+    const float2 hb23 = f2add(make_float2(magr<0xF0u>(v2, M.m4), magr<0xF000u>(v2, M.m12)), make_float2(-524296.0f, -2056.0f));
+    a01 = f2add(a01, f2fma(ha01, xh01, nz));
+    b01 = f2add(b01, f2fma(hb01, xh01, nz));
+    a23 = f2add(a23, f2fma(ha23, xh23, nz));
+    b23 = f2add(b23, f2fma(hb23, xh23, nz));
+  }
+  const float2 dA = make_float2(da, da), dB = make_float2(db, db);
+  const float2 ra01 = f2mul(a01, dA), ra23 = f2mul(a23, dA), rb01 = f2mul(b01, dB), rb23 = f2mul(b23, dB);
+  ra = make_float4(ra01.x, ra01.y, ra23.x, ra23.y);
+  rb = make_float4(rb01.x, rb01.y, rb23.x, rb23.y);
+}
+
+// Q4_1 (wasm-q4.js:357-398): nibAcc[L] += n*x (lo then hi), xAcc[L] += x;
+// block value nibAcc*delta + xAcc*min.  xAcc depends only on x, so sx holds
+// it for the thread's block.
+__device__ __forceinline__ float4 q4_1_row(uint4 pl, float dl, float mn, const float (&xr)[32], float4 sx,
+                                           float2 nz, const pb_magics& M) {
+  float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
+  const uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t w = wv[g], w2 = w >> 16;
+    const float2 l01 = f2add(make_float2(magr<0xFu>(w, M.m0), magr<0xF00u>(w, M.m8)),
+                             make_float2(-8388608.0f, -32768.0f));
+    const float2 l23 = f2add(make_float2(magr<0xF0000u>(w, M.m16), magr<0xF00u>(w2, M.m8)),
+                             make_float2(-128.0f, -32768.0f));
+    const float2 h01 = f2add(make_float2(magr<0xF0u>(w, M.m4), magr<0xF000u>(w, M.m12)),
+                             make_float2(-524288.0f, -2048.0f));
+    const float2 h23 = f2add(make_float2(magr<0xF0u>(w2, M.m4), magr<0xF000u>(w2, M.m12)),
+                             make_float2(-524288.0f, -2048.0f));
+    a01 = f2add(a01, f2fma(l01, make_float2(xr[4 * g], xr[4 * g + 1]), nz));
+    a23 = f2add(a23, f2fma(l23, make_float2(xr[4 * g + 2], xr[4 * g + 3]), nz));
+    a01 = f2add(a01, f2fma(h01, make_float2(xr[16 + 4 * g], xr[16 + 4 * g + 1]), nz));
+    a23 = f2add(a23, f2fma(h23, make_float2(xr[16 + 4 * g + 2], xr[16 + 4 * g + 3]), nz));
+  }
+  return make_float4(__fadd_rn(__fmul_rn(a01.x, dl), __fmul_rn(sx.x, mn)),
+                     __fadd_rn(__fmul_rn(a01.y, dl), __fmul_rn(sx.y, mn)),
+                     __fadd_rn(__fmul_rn(a23.x, dl), __fmul_rn(sx.z, mn)),
+                     __fadd_rn(__fmul_rn(a23.y, dl), __fmul_rn(sx.w, mn)));
+}
+
+struct MvBuf {
+  uint4 q[MV_RPT];
+  uint32_t d[MV_RPT];
+  uint32_t m[MV_RPT];
 };
 
-template <int TYPE, int NI>
-__device__ __forceinline__ void mv_load(MvRegs<TYPE, NI>& R, const uint8_t* __restrict__ qs,
-                                        const uint16_t* __restrict__ dsc, const uint16_t* __restrict__ msc, int tile,
-                                        int nb, int r, int bb) {
+template <int TYPE>
+__device__ __forceinline__ void mv_load(MvBuf& R, const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc,
+                                        const uint16_t* __restrict__ msc, int tile, int h, int b, int nb) {
 #pragma unroll
-  for (int i = 0; i < NI; ++i) {
-    const int b = 32 * i + bb;
-    if (b < nb) {
-      const size_t slot = ((size_t)tile * nb + b) * 8 + r;
-      R.q[i] = __ldcs(reinterpret_cast<const uint4*>(qs) + slot);
-      R.d[i] = __ldcs(dsc + slot);
-      if (TYPE == PB_TYPE_Q4_1) R.m[i] = __ldcs(msc + slot);
+  for (int i = 0; i < MV_RPT; ++i) {
+    const size_t slot = (size_t)(tile * 8 + h * MV_RPT + i) * nb + b;
+    R.q[i] = __ldcs(reinterpret_cast<const uint4*>(qs) + slot);
+    R.d[i] = __ldcs(dsc + slot);
+    if (TYPE == PB_TYPE_Q4_1) R.m[i] = __ldcs(msc + slot);
+  }
+}
+
+// Chain of slot `slot`'s tile over the nb block partials, then the epilogue.
+// Lane = 4 * row + L.
+__device__ __forceinline__ void mv_chain(const float* __restrict__ pc, int nb, int tile, int N, int row_end,
+                                         float* __restrict__ y, const pb_mv_epi& epi, int* err) {
+  const int lane = threadIdx.x & 31, rr = lane >> 2, L = lane & 3;
+  float acc = 0.0f;
+  int b = 0;
+  for (; b + 8 <= nb; b += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = pc[(b + u) * 32 + ((rr ^ u) << 2) + L];  // (b + u) & 7 == u
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+  }
+  for (; b < nb; ++b) acc = __fadd_rn(acc, pc[b * 32 + ((rr ^ (b & 7)) << 2) + L]);
+  // y = (acc1 + acc3) + (acc0 + acc2)  (wasm-q4.js:236-245)
+  const int base = lane & ~3;
+  const float a0 = __shfl_sync(0xffffffffu, acc, base + 0);
+  const float a1 = __shfl_sync(0xffffffffu, acc, base + 1);
+  const float a2 = __shfl_sync(0xffffffffu, acc, base + 2);
+  const float a3 = __shfl_sync(0xffffffffu, acc, base + 3);
+  const float v = __fadd_rn(__fadd_rn(a1, a3), __fadd_rn(a0, a2));
+  const int row = tile * 8 + rr;
+  const bool live = L == 0 && row < row_end && row < N;
+  if (epi.kind == PB_EPI_STORE) {
+    if (live) y[row] = v;
+  } else if (epi.kind == PB_EPI_RESIDUAL) {
+    if (live) y[row] = __fadd_rn(epi.residual[row], v);
+  } else if (epi.kind == PB_EPI_ROPE_KV) {
+    // rows of a tile are all q, all k or all v (q_rows, kv_rows % 8 == 0)
+    const float vp = __shfl_sync(0xffffffffu, v, lane ^ 4);  // partner row rr ^ 1
+    const int pos = epi.pos_dev ? *epi.pos_dev : epi.start_pos;
+    const bool in_range = pos >= 0 && pos < epi.max_len;
+    if (live && !in_range && rr == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+    if (live && in_range) {
+      const int kvd = epi.kv_rows;
+      if (row < epi.q_rows + kvd) {  // q or k: rotate the pair (2i, 2i+1)
+        const bool isq = row < epi.q_rows;
+        const int rel = isq ? row : row - epi.q_rows;
+        const int pr = (rel % epi.head_dim) >> 1;
+        const double2 cs = epi.rope_tab[(size_t)pos * (epi.head_dim >> 1) + pr];
+        const bool even = (rr & 1) == 0;
+        const double x0 = even ? (double)v : (double)vp, x1 = even ? (double)vp : (double)v;
+        const float o = even ? (float)__dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y))
+                             : (float)__dadd_rn(__dmul_rn(x0, cs.y), __dmul_rn(x1, cs.x));
+        if (isq) y[row] = o;
+        else epi.kc[(size_t)pos * kvd + rel] = o;
+      } else {
+        epi.vc[(size_t)pos * kvd + (row - epi.q_rows - kvd)] = v;
+      }
+    }
+  } else {  // PB_EPI_SWIGLU4: rows 0-3 gate, 4-7 up of indices 4*tile .. 4*tile+3
+    const float u = __shfl_sync(0xffffffffu, v, (lane + 16) & 31);
+    if (L == 0 && rr < 4 && row < N) {
+      const double g = v;
+      const double silu = __ddiv_rn(g, __dadd_rn(1.0, exp(-g)));
+      epi.h_out[tile * 4 + rr] = (float)__dmul_rn(silu, (double)u);
     }
   }
 }
 
-template <int TYPE, int NI>
-__device__ __forceinline__ void mv_tile(const MvRegs<TYPE, NI>& R, int tile, int nb, int N, int row_end,
-                                        const float4* xs, float4* ps, float* __restrict__ y, const pb_mv_epi& epi,
-                                        int* err) {
-  const int tid = threadIdx.x, r = tid & 7, bb = tid >> 3;
-#pragma unroll
-  for (int i = 0; i < NI; ++i) {
-    const int b = 32 * i + bb;
-    if (b < nb) {
-      float4 p;
-      if (TYPE == PB_TYPE_Q4_0) p = q4_0_block_exact(R.q[i], pb_f16_wasm(R.d[i]), xs, b);
-      else p = q4_1_block(R.q[i], pb_f16_wasm(R.d[i]), pb_f16_wasm(R.m[i]), xs, b);
-      ps[b * 8 + r] = p;
-    }
-  }
-  __syncthreads();
-  if (tid < 32) {
-    // in-order chains: lane = 4 * row + L
-    const int rr = tid >> 2, L = tid & 3;
-    const float* pf = reinterpret_cast<const float*>(ps) + rr * 4 + L;
-    float acc = 0.0f;
-    int b = 0;
-    for (; b + 8 <= nb; b += 8) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = pf[(b + u) * 32];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
-    }
-    for (; b < nb; ++b) acc = __fadd_rn(acc, pf[b * 32]);
-    // y = (acc1 + acc3) + (acc0 + acc2)
-    const int base = tid & ~3;
-    const float a0 = __shfl_sync(0xffffffffu, acc, base + 0);
-    const float a1 = __shfl_sync(0xffffffffu, acc, base + 1);
-    const float a2 = __shfl_sync(0xffffffffu, acc, base + 2);
-    const float a3 = __shfl_sync(0xffffffffu, acc, base + 3);
-    const float v = __fadd_rn(__fadd_rn(a1, a3), __fadd_rn(a0, a2));
-    const int row = tile * 8 + rr;
-    const bool live = L == 0 && row < row_end && row < N;
-    if (epi.kind == PB_EPI_STORE) {
-      if (live) y[row] = v;
-    } else if (epi.kind == PB_EPI_RESIDUAL) {
-      if (live) y[row] = __fadd_rn(epi.residual[row], v);
-    } else if (epi.kind == PB_EPI_ROPE_KV) {
-      // rows of a tile are all q, all k or all v (q_rows, kv_rows % 8 == 0)
-      const float vp = __shfl_sync(0xffffffffu, v, tid ^ 4);  // partner row rr ^ 1
-      const int pos = epi.pos_dev ? *epi.pos_dev : epi.start_pos;
-      const bool in_range = pos >= 0 && pos < epi.max_len;
-      if (live && !in_range && rr == 0) pb_raise(err, PB_DEVERR_BOUNDS);
-      if (live && in_range) {
-        const int kvd = epi.kv_rows;
-        if (row < epi.q_rows + kvd) {  // q or k: rotate the pair (2i, 2i+1)
-          const bool isq = row < epi.q_rows;
-          const int rel = isq ? row : row - epi.q_rows;
-          const int pr = (rel % epi.head_dim) >> 1;
-          const double2 cs = epi.rope_tab[(size_t)pos * (epi.head_dim >> 1) + pr];
-          const bool even = (rr & 1) == 0;
-          const double x0 = even ? (double)v : (double)vp, x1 = even ? (double)vp : (double)v;
-          const float o = even ? (float)__dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y))
-                               : (float)__dadd_rn(__dmul_rn(x0, cs.y), __dmul_rn(x1, cs.x));
-          if (isq) y[row] = o;
-          else epi.kc[(size_t)pos * kvd + rel] = o;
-        } else {
-          epi.vc[(size_t)pos * kvd + (row - epi.q_rows - kvd)] = v;
-        }
-      }
-    } else {  // PB_EPI_SWIGLU4: rows 0-3 gate, 4-7 up of indices 4*tile .. 4*tile+3
-      const float u = __shfl_sync(0xffffffffu, v, (tid + 16) & 31);
-      if (L == 0 && rr < 4 && row < N) {
-        const double g = v;
-        const double silu = __ddiv_rn(g, __dadd_rn(1.0, exp(-g)));
-        epi.h_out[tile * 4 + rr] = (float)__dmul_rn(silu, (double)u);
-      }
-    }
-  }
-  __syncthreads();
-}
-
-template <int TYPE, int NI>
-__global__ void __launch_bounds__(MV_THREADS)
+template <int TYPE, int NT>
+__global__ void __launch_bounds__(NT, 1)
 k_matvec(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, const uint16_t* __restrict__ msc, int N,
          int nb, int tile_begin, int tile_end, int row_end, const float* __restrict__ x, float* __restrict__ y,
-         pb_mv_epi epi, int* err) {
+         pb_mv_epi epi, float nzf, pb_magics M, int* err) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float4* ps = reinterpret_cast<float4*>(smem_raw);  // nb * 8 block partials
-  float4* xs = ps + (size_t)nb * 8;                   // K floats, swizzled
-  const int tid = threadIdx.x, r = tid & 7, bb = tid >> 3;
+  __shared__ double red[NT / 32];
+  const int S = mv_slots(nb, NT), stride = mv_slot_threads(nb);
   const int K = nb * 32;
-  MvRegs<TYPE, NI> A, B;
-  int t = tile_begin + blockIdx.x;
-  if (t < tile_end) mv_load<TYPE, NI>(A, qs, dsc, msc, t, nb, r, bb);
+  float* ps = reinterpret_cast<float*>(smem_raw);  // [S][2][nb][8 rows (swizzled)][4 lanes]
+  float4* xs4 = reinterpret_cast<float4*>(ps + (size_t)2 * S * nb * 32);  // x, chunks swizzled per block
+  const int tid = threadIdx.x;
+  const int s = tid / stride, rem = tid - s * stride, h = rem / nb, b = h < 2 ? rem - h * nb : 0;
+  const bool worker = s < S && h < 2;
+  const int per_iter = gridDim.x * S;
+  const float2 nz = make_float2(nzf, nzf);
+
+  // L2 prefetch of the slot's first MV_PF_DIST tiles (a tile is contiguous;
+  // each iteration then prefetches the tile MV_PF_DIST ahead) and of this
+  // CTA's share of the later kernels' operands, then the first tile's blocks
+  const size_t tq = (size_t)8 * nb * 16, td = (size_t)8 * nb * 2;
+  auto prefetch_tile = [&](int t) {
+    if (t < tile_end) {
+      pb_l2_prefetch(qs + (size_t)t * tq, (uint32_t)tq);
+      pb_l2_prefetch(dsc + (size_t)t * td / 2, (uint32_t)td);
+      if (TYPE == PB_TYPE_Q4_1) pb_l2_prefetch(msc + (size_t)t * td / 2, (uint32_t)td);
+    }
+  };
+  const bool pf_thread = s < S && rem == 0;
+  if (pf_thread)
+    for (int i = 0; i < MV_PF_DIST; ++i) prefetch_tile(tile_begin + i * per_iter + s * gridDim.x + blockIdx.x);
+  if (tid == 0)
+    for (int i = 0; i < PB_MAX_L2_NEXT; ++i) pb_l2_prefetch_share(epi.l2_next[i], epi.l2_next_bytes[i], blockIdx.x, gridDim.x);
+  MvBuf A, B;
+  {
+    const int t0 = tile_begin + s * gridDim.x + blockIdx.x;
+    if (worker && t0 < tile_end) mv_load<TYPE>(A, qs, dsc, msc, t0, h, b, nb);
+  }
   pb_pdl_trigger();
   pb_pdl_wait();  // x (and the residual) come from the previous kernel
-  for (int c = tid; c < K / 4; c += MV_THREADS) {
-    const int b = c >> 3, i = c & 7;
-    xs[b * 8 + (i ^ (b & 7))] = reinterpret_cast<const float4*>(x)[c];
+
+  // x (RMS-normalised when asked: engine.js:429-449 with a fixed reduction
+  // tree, identical in every CTA) into shared memory, then the block into
+  // registers
+  if (epi.norm_w) {
+    double ss = 0.0;
+    for (int j = tid; j < K; j += NT) ss = __fma_rn((double)x[j], (double)x[j], ss);
+    ss = pb_block_sum_d(ss, red);
+    const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)K), epi.eps));
+    for (int j = tid; j < K; j += NT) {
+      const float v = (float)__dmul_rn(__ddiv_rn((double)x[j], rms), (double)epi.norm_w[j]);
+      const int bj = j >> 5, c = (j >> 2) & 7;
+      reinterpret_cast<float*>(xs4 + bj * 8 + (c ^ (bj & 7)))[j & 3] = v;
+    }
+  } else {
+    for (int c = tid; c < K / 4; c += NT) {
+      const int bj = c >> 3, i = c & 7;
+      xs4[bj * 8 + (i ^ (bj & 7))] = reinterpret_cast<const float4*>(x)[c];
+    }
   }
   __syncthreads();
-  while (t < tile_end) {
-    int tn = t + gridDim.x;
-    if (tn < tile_end) mv_load<TYPE, NI>(B, qs, dsc, msc, tn, nb, r, bb);
-    mv_tile<TYPE, NI>(A, t, nb, N, row_end, xs, ps, y, epi, err);
-    t = tn;
-    if (t >= tile_end) break;
-    tn = t + gridDim.x;
-    if (tn < tile_end) mv_load<TYPE, NI>(A, qs, dsc, msc, tn, nb, r, bb);
-    mv_tile<TYPE, NI>(B, t, nb, N, row_end, xs, ps, y, epi, err);
-    t = tn;
+  if (s >= S) return;  // threads beyond the last slot have no further part
+  float xr[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 v = xs4[b * 8 + (i ^ (b & 7))];
+    xr[4 * i] = v.x;
+    xr[4 * i + 1] = v.y;
+    xr[4 * i + 2] = v.z;
+    xr[4 * i + 3] = v.w;
+  }
+  float4 sx = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (TYPE == PB_TYPE_Q4_1) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      sx.x = __fadd_rn(__fadd_rn(sx.x, xr[4 * g]), xr[16 + 4 * g]);
+      sx.y = __fadd_rn(__fadd_rn(sx.y, xr[4 * g + 1]), xr[16 + 4 * g + 1]);
+      sx.z = __fadd_rn(__fadd_rn(sx.z, xr[4 * g + 2]), xr[16 + 4 * g + 2]);
+      sx.w = __fadd_rn(__fadd_rn(sx.w, xr[4 * g + 3]), xr[16 + 4 * g + 3]);
+    }
+  }
+
+  // The slots run independently, each with its own named barrier (ids 1..S)
+  // and double-buffered partials; the slot's first warp runs the chains.
+  float* pslot = ps + (size_t)s * 2 * nb * 32;
+  const bool chain_warp = rem < 32;
+  auto iteration = [&](MvBuf& cur, MvBuf& nxt, int it) -> bool {
+    const int tc = tile_begin + it * per_iter + s * gridDim.x + blockIdx.x;  // slot-uniform
+    if (tc >= tile_end) return false;
+    if (pf_thread) prefetch_tile(tc + MV_PF_DIST * per_iter);
+    if (worker && tc + per_iter < tile_end) mv_load<TYPE>(nxt, qs, dsc, msc, tc + per_iter, h, b, nb);
+    float* pbuf = pslot + (size_t)(it & 1) * nb * 32;
+    if (worker) {
+      float* pw = pbuf + (size_t)b * 32;
+#pragma unroll
+      for (int i = 0; i < MV_RPT; i += 2) {  // two rows at a time: independent chains interleave
+        const int r = h * MV_RPT + i;
+        float4 p0, p1;
+        if (TYPE == PB_TYPE_Q4_0) {
+          q4_0_row2(cur.q[i], cur.q[i + 1], pb_f16_wasm(cur.d[i]), pb_f16_wasm(cur.d[i + 1]), xr, nz, M, p0, p1);
+        } else {
+          p0 = q4_1_row(cur.q[i], pb_f16_wasm(cur.d[i]), pb_f16_wasm(cur.m[i]), xr, sx, nz, M);
+          p1 = q4_1_row(cur.q[i + 1], pb_f16_wasm(cur.d[i + 1]), pb_f16_wasm(cur.m[i + 1]), xr, sx, nz, M);
+        }
+        *reinterpret_cast<float4*>(pw + ((r ^ (b & 7)) << 2)) = p0;
+        *reinterpret_cast<float4*>(pw + (((r + 1) ^ (b & 7)) << 2)) = p1;
+      }
+    }
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + s), "r"(stride) : "memory");
+    if (chain_warp) mv_chain(pbuf, nb, tc, N, row_end, y, epi, err);
+    return true;
+  };
+  for (int it = 0;; it += 2) {
+    if (!iteration(A, B, it)) break;
+    if (!iteration(B, A, it + 1)) break;
   }
 }
 
-static size_t mv_smem(const pb_qmat* w) { return (size_t)w->nb * 8 * 16 + (size_t)w->nb * 32 * 4; }
+static size_t mv_smem(const pb_qmat* w, int nt) {
+  return (size_t)2 * mv_slots(w->nb, nt) * w->nb * 32 * 4 + (size_t)w->nb * 32 * 4;
+}
 
-template <int TYPE, int NI>
-static int launch_mv(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int tile_begin, int ntiles, int row_end,
-                     const pb_mv_epi& epi) {
-  // persistent: as many CTAs as fit on the SMs at once (registers bound it)
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_matvec<TYPE, NI>, MV_THREADS, mv_smem(w)) !=
-          cudaSuccess ||
-      per_sm < 1)
-    per_sm = 1;
-  const int grid = ntiles < per_sm * ctx->sm_count ? ntiles : per_sm * ctx->sm_count;
-  return pb_launch(ctx, "k_matvec", true, k_matvec<TYPE, NI>, dim3(grid), dim3(MV_THREADS), mv_smem(w),
+template <int TYPE, int NT>
+static int launch_mv_nt(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int tile_begin, int ntiles,
+                        int row_end, const pb_mv_epi& epi) {
+  // persistent, at most one CTA per SM; a small matrix leaves SMs free, where
+  // the next kernel's CTAs start early (programmatic dependent launch)
+  const int S = mv_slots(w->nb, NT), groups = (ntiles + S - 1) / S;
+  const int grid = groups < ctx->sm_count ? groups : ctx->sm_count;
+  return pb_launch(ctx, "k_matvec", true, k_matvec<TYPE, NT>, dim3(grid), dim3(NT), mv_smem(w, NT),
                    (const uint8_t*)w->qs, (const uint16_t*)w->d, (const uint16_t*)w->m, w->N, w->nb, tile_begin,
-                   tile_begin + ntiles, row_end, x, y, epi, ctx->d_err);
+                   tile_begin + ntiles, row_end, x, y, epi, -0.0f,
+                   pb_magics{PB_MAG0, PB_MAG4, PB_MAG8, PB_MAG12, PB_MAG16}, ctx->d_err);
 }
 
 template <int TYPE>
-static int launch_mv_type(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int tile_begin, int ntiles,
-                          int row_end, const pb_mv_epi& epi) {
-  const int ni = (w->nb + 31) / 32;
-  if (ni <= 1) return launch_mv<TYPE, 1>(ctx, w, x, y, tile_begin, ntiles, row_end, epi);
-  if (ni <= 2) return launch_mv<TYPE, 2>(ctx, w, x, y, tile_begin, ntiles, row_end, epi);
-  if (ni <= 4) return launch_mv<TYPE, 4>(ctx, w, x, y, tile_begin, ntiles, row_end, epi);
-  return launch_mv<TYPE, 8>(ctx, w, x, y, tile_begin, ntiles, row_end, epi);
+static int launch_mv(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int tile_begin, int ntiles, int row_end,
+                     const pb_mv_epi& epi) {
+  return launch_mv_nt<TYPE, MV_THREADS>(ctx, w, x, y, tile_begin, ntiles, row_end, epi);
 }
 
 int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows,
@@ -393,15 +447,19 @@ int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, in
   if (!ctx || !w || !x) return PB_ERR_ARG;
   if (w->type != PB_TYPE_Q4_0 && w->type != PB_TYPE_Q4_1)
     return pb_set_error(ctx, PB_ERR_ARG, "matvec supports Q4_0 and Q4_1 matrices");
-  if (w->nb > 256) return pb_set_error(ctx, PB_ERR_ARG, "K=%d exceeds the 8192 the matvec kernel supports", w->K);
+  if (w->layout != PB_LAYOUT_ROWS)
+    return pb_set_error(ctx, PB_ERR_ARG, "matrix was uploaded as a head table (PB_QMAT_TABLE); the matvec needs the "
+                                         "row layout");
+  if (w->nb > MV_THREADS / 2)
+    return pb_set_error(ctx, PB_ERR_ARG, "K=%d exceeds the %d the matvec kernel supports", w->K, MV_THREADS * 16);
   if (rows <= 0) { row0 = 0; rows = w->N; }
   if (row0 < 0 || row0 + rows > w->N || (row0 & 7))
     return pb_set_error(ctx, PB_ERR_ARG, "row range [%d, %d) invalid (start must be a multiple of 8)", row0, row0 + rows);
   pb_mv_epi epi = epi_in ? *epi_in : pb_mv_epi();
   if (!y && epi.kind != PB_EPI_SWIGLU4) return PB_ERR_ARG;
   const int tile_begin = row0 / 8, ntiles = pb_cdiv(rows, 8);
-  if (w->type == PB_TYPE_Q4_0) return launch_mv_type<PB_TYPE_Q4_0>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
-  return launch_mv_type<PB_TYPE_Q4_1>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
+  if (w->type == PB_TYPE_Q4_0) return launch_mv<PB_TYPE_Q4_0>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
+  return launch_mv<PB_TYPE_Q4_1>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
 }
 
 extern "C" int pb_qmat_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows) {
@@ -674,6 +732,8 @@ int pb_launch_head_norm(pb_ctx* ctx, const pb_qmat* emb, const float* h, const f
     k_head_f32_double<<<grid, HD_WARPS * 32, smem, ctx->stream>>>((const float*)emb->qs, emb->N, emb->K, h, norm_w, eps,
                                                                    logits, amax);
   } else if (emb->type == PB_TYPE_Q4_0 || emb->type == PB_TYPE_Q8_0) {
+    if (emb->layout != PB_LAYOUT_TILED8)
+      return pb_set_error(ctx, PB_ERR_ARG, "head table must be uploaded with PB_QMAT_TABLE");
     return pb_launch(ctx, "k_head", true, emb->type == PB_TYPE_Q4_0 ? k_head<PB_TYPE_Q4_0> : k_head<PB_TYPE_Q8_0>,
                      dim3(grid), dim3(HD_WARPS * 32), smem, (const uint8_t*)emb->qs, (const uint16_t*)emb->d, emb->N,
                      emb->nb, h, norm_w, eps, logits, amax);
@@ -772,33 +832,51 @@ extern "C" int pb_lm_head(pb_ctx* ctx, const float* h, const float* emb, int V, 
 
 constexpr int PF_WARPS = 8;
 constexpr int PF_MT = 16;
-constexpr int PF_KC = 8;  // blocks per x chunk
+constexpr int PF_KC = 8;                        // blocks per chunk
+constexpr int PF_ROWS = PF_WARPS * 32;          // weight rows per CTA
+constexpr int PF_WSTRIDE = PF_KC * 16 + 16;     // bytes per staged row (padded: conflict-free lane reads)
 
+// Weight rows arrive in the row-major layout: a CTA stages its 256 rows x 8
+// blocks (coalesced: 8 threads per 128-byte row segment) in shared memory,
+// and lane n then reads its own row's blocks from there.
 __global__ void __launch_bounds__(PF_WARPS * 32)
-k_prefill_q4(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, int nb,
+k_prefill_q4(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, int N_pad, int nb,
              const float* __restrict__ X, int ldx, int M, float* __restrict__ C, int ldc) {
-  __shared__ __align__(16) float xs[PF_MT][PF_KC * 32];
+  extern __shared__ __align__(16) unsigned char pf_raw[];
+  float(*xs)[PF_KC * 32] = reinterpret_cast<float(*)[PF_KC * 32]>(pf_raw);            // [PF_MT][256]
+  uint8_t* ws = pf_raw + sizeof(float) * PF_MT * PF_KC * 32;                           // [256][PF_WSTRIDE]
+  uint16_t* ds = reinterpret_cast<uint16_t*>(ws + (size_t)PF_ROWS * PF_WSTRIDE);       // [256][PF_KC]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int tile = blockIdx.x * PF_WARPS + warp;
-  const int ntiles = (N + 31) >> 5;
+  const int row0 = blockIdx.x * PF_ROWS;
+  const int n = row0 + warp * 32 + lane;
   const int m0 = blockIdx.y * PF_MT;
   const int K = nb * 32;
   float acc[PF_MT];
 #pragma unroll
   for (int i = 0; i < PF_MT; ++i) acc[i] = 0.0f;
   for (int b0 = 0; b0 < nb; b0 += PF_KC) {
+    const int kc = nb - b0 < PF_KC ? nb - b0 : PF_KC;
     __syncthreads();
     for (int idx = threadIdx.x; idx < PF_MT * PF_KC * 32; idx += blockDim.x) {
       int mm = idx / (PF_KC * 32), kk = idx % (PF_KC * 32);
       int k = b0 * 32 + kk;
       xs[mm][kk] = (m0 + mm < M && k < K) ? X[(size_t)(m0 + mm) * ldx + k] : 0.0f;
     }
+    for (int idx = threadIdx.x; idx < PF_ROWS * PF_KC; idx += blockDim.x) {
+      const int r = idx / PF_KC, bb = idx % PF_KC;
+      const int row = row0 + r;
+      if (bb < kc && row < N_pad) {
+        const size_t slot = (size_t)row * nb + b0 + bb;
+        *reinterpret_cast<uint4*>(ws + (size_t)r * PF_WSTRIDE + bb * 16) = __ldcs(reinterpret_cast<const uint4*>(qs) + slot);
+        ds[r * PF_KC + bb] = __ldcs(dsc + slot);
+      }
+    }
     __syncthreads();
-    if (tile < ntiles) {
-      for (int bb = 0; bb < PF_KC && b0 + bb < nb; ++bb) {
-        size_t slot = (size_t)pb_qslot(tile * 32 + lane, b0 + bb, nb);
-        uint4 pl = __ldg(reinterpret_cast<const uint4*>(qs) + slot);
-        float d = pb_f16_exact(__ldg(dsc + slot));
+    if (n < N) {
+      const int r = warp * 32 + lane;
+      for (int bb = 0; bb < kc; ++bb) {
+        const uint4 pl = *reinterpret_cast<const uint4*>(ws + (size_t)r * PF_WSTRIDE + bb * 16);
+        float d = pb_f16_exact(ds[r * PF_KC + bb]);
         float e[32];
         uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
 #pragma unroll
@@ -826,20 +904,23 @@ k_prefill_q4(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
       }
     }
   }
-  int n = tile * 32 + lane;
-  if (tile < ntiles && n < N) {
+  if (n < N) {
 #pragma unroll
     for (int mm = 0; mm < PF_MT; ++mm)
       if (m0 + mm < M) C[(size_t)(m0 + mm) * ldc + n] = acc[mm];
   }
 }
 
+static size_t pf_smem() {
+  return sizeof(float) * PF_MT * PF_KC * 32 + (size_t)PF_ROWS * PF_WSTRIDE + (size_t)PF_ROWS * PF_KC * 2;
+}
+
 int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc) {
-  if (w->type != PB_TYPE_Q4_0) return pb_set_error(ctx, PB_ERR_ARG, "prefill GEMM needs a Q4_0 matrix");
-  int ntiles = (w->N + 31) / 32;
-  dim3 grid(pb_cdiv(ntiles, PF_WARPS), pb_cdiv(M, PF_MT));
+  if (w->type != PB_TYPE_Q4_0 || w->layout != PB_LAYOUT_ROWS)
+    return pb_set_error(ctx, PB_ERR_ARG, "prefill GEMM needs a Q4_0 matrix in the row layout");
+  dim3 grid(pb_cdiv(w->N, PF_ROWS), pb_cdiv(M, PF_MT));
   if (grid.y > 65535) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
-  k_prefill_q4<<<grid, PF_WARPS * 32, 0, ctx->stream>>>(w->qs, w->d, w->N, w->nb, X, ldx, M, C, ldc);
+  k_prefill_q4<<<grid, PF_WARPS * 32, pf_smem(), ctx->stream>>>(w->qs, w->d, w->N, w->N_pad, w->nb, X, ldx, M, C, ldc);
   PB_LAUNCHED(ctx, "k_prefill_q4");
   return PB_OK;
 }
@@ -849,14 +930,9 @@ int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx,
 int pb_setup_q4_kernels(void) {
   const int lim = 200 * 1024;
   cudaError_t e = cudaSuccess;
-  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_0, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_0, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_0, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_1, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_1, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_0, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_1, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_prefill_q4, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   e = e ? e : cudaFuncSetAttribute(k_head<PB_TYPE_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_head<PB_TYPE_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_head_f32_double, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);

@@ -151,12 +151,26 @@ def test_resident_head(native, ctx, oracle, typ, V, D):
         table = oracle.dequant_q8_0(raw, V * D)
     h = rng.standard_normal(D).astype(f32)
     want = oracle.batch_dot(h, table, V, D)
-    m = native.QMat(ctx, t, raw, V, D)
+    m = native.QMat(ctx, t | native.QMAT_TABLE, raw, V, D)
+    assert bits_equal(m.gguf_bytes(), raw)  # table layout round trip
     dh, dl, di = dev(ctx, h), out(ctx, V), out(ctx, 4, np.int32)
     ctx._check(native.lib().pb_qmat_head(ctx.h, m.h, dh.ptr, dl.ptr, di.ptr))
     ctx.sync()
     assert bits_equal(dl.download(count=V), want)
     assert int(di.download(np.int32, 1)[0]) == oracle.argmax(want)
+
+
+def test_layouts_are_checked(native, ctx):
+    """A matvec matrix is not a head table and vice versa: clean PB_ERR_ARG."""
+    rng = np.random.default_rng(14)
+    raw = rand_q4_0(rng, 64, 64)
+    L = native.lib()
+    rows = native.QMat(ctx, native.TYPE_Q4_0, raw, 64, 64)
+    table = native.QMat(ctx, native.TYPE_Q4_0 | native.QMAT_TABLE, raw, 64, 64)
+    dx, dy = out(ctx, 64), out(ctx, 64)
+    assert L.pb_qmat_head(ctx.h, rows.h, dx.ptr, dy.ptr, None) == native.PB_ERR_ARG
+    assert L.pb_qmat_matvec(ctx.h, table.h, dx.ptr, dy.ptr, 0, 0) == native.PB_ERR_ARG
+    assert bits_equal(rows.gguf_bytes(), table.gguf_bytes())
 
 
 def test_argmax_ties_nan(native, ctx):
@@ -338,3 +352,31 @@ def test_attention_cached_and_generic(native, ctx, oracle, golden):
     ctx._check(L.pb_attention(ctx.h, dQ.ptr, dK.ptr, dV.ptr, 5, 5, 8, 6, 1, o.ptr))
     ctx.sync()
     assert close(o.download(count=30), oracle.attention(Q, K, V, 5, 5, 8, 6, True))
+
+
+def test_capture_replay(native, ctx, oracle):
+    """pb_capture_begin/end record device-pointer calls; a replay gives the same bits."""
+    rng = np.random.default_rng(31)
+    N, K = 512, 2048
+    raw = rand_q4_0(rng, N, K)
+    x = rng.standard_normal(K).astype(f32)
+    m = native.QMat(ctx, native.TYPE_Q4_0, raw, N, K)
+    dx, dy = dev(ctx, x), out(ctx, N)
+    L = native.lib()
+    ctx.sync()
+    g = ctx.capture(lambda: ctx._check(L.pb_qmat_matvec(ctx.h, m.h, dx.ptr, dy.ptr, 0, 0)))
+    ctx._check(L.pb_memset(ctx.h, dy.ptr, 0, N * 4))
+    g.launch()
+    g.launch()
+    ctx.sync()
+    assert bits_equal(dy.download(count=N), oracle.q4_0_matvec(x, raw, N, K))
+    g.free()
+    # a blocking call while recording is refused, and the context stays usable
+    ctx._check(L.pb_capture_begin(ctx.h))
+    rc = L.pb_sync(ctx.h)
+    gh = native.V()
+    L.pb_capture_end(ctx.h, native.ctypes.byref(gh))
+    if gh.value:
+        L.pb_graph_free(gh.value)
+    assert rc != native.PB_OK
+    ctx.sync()
