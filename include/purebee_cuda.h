@@ -170,6 +170,21 @@ int pb_elementmul(pb_ctx* ctx, const float* a_dev, const float* b_dev, int64_t n
 int pb_tensoradd(pb_ctx* ctx, const float* a_dev, const float* b_dev, int64_t n, float* out_dev);  /* engine.js:96-106 */
 int pb_attention(pb_ctx* ctx, const float* Q_dev, const float* K_dev, const float* V_dev, int seqQ, int seqK,
                  int dK, int dV, int causal, float* out_dev);           /* engine.js:374-415 */
+/* pb_attention without allocating: no counterpart in the reference (it
+ * computes the same engine.js:374-415 attention, bit for bit equal to
+ * pb_attention).  pb_attention grows the context scratch on demand
+ * (cudaFree + cudaMalloc, which synchronise the whole device); this call
+ * instead keeps the seqQ x seqK scores and probabilities in one fixed device
+ * array of PB_NOALLOC_ATTN_BYTES per device, whose address pb_init looks up,
+ * so the call itself makes no allocation and no set-up.
+ * Limit: 2 * (4 * seqQ * seqK rounded up to 256) <= PB_NOALLOC_ATTN_BYTES
+ * (seqQ * seqK <= 524224), else PB_ERR_ARG before anything is launched.
+ * The array is shared by every context and stream on the device: calls that
+ * overlap in time race on it, so the caller serialises them (one stream, or
+ * an event between streams). */
+#define PB_NOALLOC_ATTN_BYTES (4u << 20)
+int pb_attention_noalloc(pb_ctx* ctx, const float* Q_dev, const float* K_dev, const float* V_dev, int seqQ,
+                         int seqK, int dK, int dV, int causal, float* out_dev);
 /* llama-streaming.js:310-339 _applyRoPE on q [seq, n_heads*hd], k [seq, n_kv*hd] in place */
 int pb_rope(pb_ctx* ctx, float* q_dev, float* k_dev, int seq, int start_pos, int n_heads, int n_kv,
             int head_dim, double theta);

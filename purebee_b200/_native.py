@@ -87,6 +87,7 @@ SIGNATURES = {
     "pb_elementmul": (I, [V, V, V, I64, V]),
     "pb_tensoradd": (I, [V, V, V, I64, V]),
     "pb_attention": (I, [V, V, V, V, I, I, I, I, I, V]),
+    "pb_attention_noalloc": (I, [V, V, V, V, I, I, I, I, I, V]),
     "pb_rope": (I, [V, V, V, I, I, I, I, I, D]),
     "pb_attn_cached": (I, [V, V, V, V, I, I, I, I, I, V]),
     "pb_swiglu": (I, [V, V, V, I, V]),

@@ -110,7 +110,7 @@ extern "C" int pb_init(int device, pb_ctx** out) {
   if (cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess) { delete ctx; return PB_ERR_OOM; }
   cudaMemset(ctx->d_err, 0, sizeof(int));
   cudaDeviceSynchronize();
-  if (pb_setup_q4_kernels() != PB_OK || pb_setup_ops_kernels() != PB_OK) {
+  if (pb_setup_q4_kernels() != PB_OK || pb_setup_ops_kernels() != PB_OK || pb_setup_noalloc(ctx) != PB_OK) {
     pb_shutdown(ctx);
     return PB_ERR_CUDA;
   }

@@ -22,6 +22,8 @@ struct pb_ctx {
   // scratch for one-shot host-buffer calls (grown on demand)
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
+  // fixed per-device array of pb_attention_noalloc (looked up in pb_init)
+  void* noalloc_attn = nullptr;
 };
 
 // Device layouts of a quantized matrix (payload and scales split apart, so
@@ -232,3 +234,4 @@ int pb_qmat_alloc(pb_ctx* ctx, int type, int layout, int N, int K, pb_qmat** out
 int pb_qmat_pack_from_device(pb_ctx* ctx, pb_qmat* m, const void* gguf_dev);
 int pb_setup_q4_kernels(void);
 int pb_setup_ops_kernels(void);
+int pb_setup_noalloc(pb_ctx* ctx);  // with ctx->device current

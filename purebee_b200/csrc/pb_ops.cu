@@ -13,6 +13,8 @@
 
 #include <vector>
 
+#include <mutex>
+
 #include "pb_internal.cuh"
 
 // ============================================================================
@@ -256,6 +258,51 @@ extern "C" int pb_attention(pb_ctx* ctx, const float* Q, const float* K, const f
   PB_TRY(pb_ensure_scratch(ctx, 2 * sb + 256));
   float* S = (float*)ctx->scratch;
   float* Wt = (float*)((char*)ctx->scratch + ((sb + 255) & ~(size_t)255));
+  double scale = 1.0 / sqrt((double)dK);
+  k_attn_scores_generic<<<dim3(pb_cdiv(seqK, 128), seqQ), 128, 0, ctx->stream>>>(Q, K, seqQ, seqK, dK, causal, scale, S);
+  PB_LAUNCHED(ctx, "k_attn_scores_generic");
+  PB_TRY(pb_softmax(ctx, S, seqQ, seqK, Wt));
+  k_attn_pv_generic<<<dim3(pb_cdiv(dV, 64), seqQ), 64, 0, ctx->stream>>>(Wt, V, seqK, dV, out);
+  PB_LAUNCHED(ctx, "k_attn_pv_generic");
+  return PB_OK;
+}
+
+// The same attention with its scores S and probabilities W in a fixed device
+// array instead of the context scratch, so the call allocates nothing.  S and
+// W are written in full before they are read (every S[i, j], then every
+// W[i, j] by the softmax), so nothing needs clearing between calls.  The array
+// is one per device and shared by all contexts: overlapping calls race.
+static __device__ __align__(256) unsigned char g_noalloc_attn[PB_NOALLOC_ATTN_BYTES];
+
+constexpr int PB_MAX_DEVICES = 64;
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_attn_ptr[PB_MAX_DEVICES];
+
+// Once per device, with that device current (pb_init): the array's address.
+int pb_setup_noalloc(pb_ctx* ctx) {
+  if (ctx->device < 0 || ctx->device >= PB_MAX_DEVICES)
+    return pb_set_error(ctx, PB_ERR_ARG, "device %d out of range", ctx->device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_attn_ptr[ctx->device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_attn);
+    if (e != cudaSuccess || !p) return pb_cuda_error(ctx, e, "cudaGetSymbolAddress(g_noalloc_attn)");
+    g_noalloc_attn_ptr[ctx->device] = p;
+  }
+  ctx->noalloc_attn = g_noalloc_attn_ptr[ctx->device];
+  return PB_OK;
+}
+
+extern "C" int pb_attention_noalloc(pb_ctx* ctx, const float* Q, const float* K, const float* V, int seqQ, int seqK,
+                                    int dK, int dV, int causal, float* out) {
+  if (!ctx || !Q || !K || !V || !out || seqQ <= 0 || seqK <= 0 || dK <= 0 || dV <= 0) return PB_ERR_ARG;
+  if (!ctx->noalloc_attn) return pb_set_error(ctx, PB_ERR_STATE, "no-alloc scratch not set up");
+  const size_t sb = (size_t)seqQ * seqK * 4, sb_al = (sb + 255) & ~(size_t)255;
+  if (2 * sb_al > PB_NOALLOC_ATTN_BYTES)
+    return pb_set_error(ctx, PB_ERR_ARG, "seqQ*seqK = %lld needs %zu bytes of scratch; the fixed array holds %u",
+                        (long long)seqQ * seqK, 2 * sb_al, (unsigned)PB_NOALLOC_ATTN_BYTES);
+  float* S = (float*)ctx->noalloc_attn;
+  float* Wt = (float*)((char*)ctx->noalloc_attn + sb_al);
   double scale = 1.0 / sqrt((double)dK);
   k_attn_scores_generic<<<dim3(pb_cdiv(seqK, 128), seqQ), 128, 0, ctx->stream>>>(Q, K, seqQ, seqK, dK, causal, scale, S);
   PB_LAUNCHED(ctx, "k_attn_scores_generic");
