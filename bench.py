@@ -174,6 +174,56 @@ def matvec_roofline(ctx, torch, stream, peak, reps=200):
     return res, tot_b / tot_t / 1e9, tot_b / sum(per_token_launches.values())
 
 
+def row_split_vocab(ctx, torch, dist, world, peak, reps=40):
+    """Config 2's vocab-head matvec (128256 x 2048 Q4_0) split by rows over the
+    ranks (thread-pool.js's row split, one GPU per worker) with the NCCL
+    all-gather of the y slices.  Each rank rotates over weight copies larger
+    than 4x L2 in total.  Times are device event times, max over ranks."""
+    from purebee_b200 import _native as N
+    from purebee_b200.thread_pool import RowSplitMatvec, rows_per_rank
+    n, k = 128256, 2048
+    rng = np.random.default_rng(11)
+    raw = rng.integers(0, 256, n * (k // 32) * 18, dtype=np.uint8)
+    raw.reshape(-1, 18)[:, :2] = (rng.standard_normal(n * (k // 32)) * 0.01).astype(np.float16).view(
+        np.uint8).reshape(-1, 2)
+    per = rows_per_rank(n, world)
+    slice_bytes = per * (k // 32) * 18
+    copies = max(2, int(np.ceil(4 * 126e6 / slice_bytes)))
+    mats = [RowSplitMatvec(ctx, raw, N.TYPE_Q4_0, n, k) for _ in range(copies)]
+    dev = mats[0].y_local.device
+    x = torch.randn(k, device=dev, dtype=torch.float32)
+    stream = mats[0].stream
+
+    def timed(fn):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(reps):
+            fn(i)
+        e1.record(stream)
+        e1.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / reps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    local_us = timed(lambda i: mats[i % copies].local(x))
+    full_us = timed(lambda i: mats[i % copies].matvec(x))
+    for m in mats:
+        m.free()
+    alg = n * k // 32 * 18 + 4 * k + 4 * n
+    return {"shape": "128256x2048 Q4_0 (vocab head)", "gpus": world, "rows_per_gpu": per, "copies_per_gpu": copies,
+            "local_us": round(local_us, 3),
+            "local_GBps_per_gpu": round((slice_bytes + 4 * k + 4 * per) / (local_us * 1e-6) / 1e9, 1),
+            "aggregate_GBps_local": round(alg / (local_us * 1e-6) / 1e9, 1),
+            "with_allgather_us": round(full_us, 3),
+            "aggregate_GBps_with_allgather": round(alg / (full_us * 1e-6) / 1e9, 1),
+            "frac_local_of_measured_peak_per_gpu": round((slice_bytes + 4 * k + 4 * per) / (local_us * 1e-6) / 1e9 / peak, 3)}
+
+
 def run_ours(args, rank, world, torch, dist):
     from purebee_b200 import _native as N
     dev = int(os.environ.get("LOCAL_RANK", 0))
@@ -247,6 +297,8 @@ def run_ours(args, rank, world, torch, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_tps = e2e_steps / float(t.item())
 
+    split = row_split_vocab(ctx, torch, dist, world, peak) if dist else None
+
     result = None
     if rank == 0:
         mv, mv_agg, mv_bytes_avg = matvec_roofline(ctx, torch, stream, peak)
@@ -281,6 +333,8 @@ def run_ours(args, rank, world, torch, dist):
                     "d2h_bytes_per_step": 4, "steps": e2e_steps,
                     "api": "StreamingLlamaRuntime model.decode (pb_model_decode)"},
         }
+        if split:
+            result["row_split"] = split
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(rt, sample_tokens=2)
     rt.shutdown()
@@ -415,7 +469,8 @@ def main():
         import torch.distributed as td
         from datetime import timedelta
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-        td.init_process_group("nccl", timeout=timedelta(seconds=300))
+        td.init_process_group("nccl", timeout=timedelta(seconds=180),
+                              device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))))
         dist = td
     res = run_ours(args, rank, world, torch, dist)
     if rank == 0:

@@ -1,0 +1,140 @@
+"""Row split of the Q4 matvec across GPUs: the multi-device form of
+thread-pool.js's AtomicsThreadPool (thread-pool.js:57-345).
+
+The reference splits the rows of every matvec over worker threads
+(thread-pool.js:165-246: rowsPerThread = floor(N / T), the remainder to the
+first workers, the main thread takes the tail) and copies the per-thread row
+slices back into one output.  Here the workers are GPUs, one process per GPU
+(torch.distributed over NCCL): each rank keeps a contiguous slice of the rows
+resident on its device, computes it with the CUDA matvec, and an all-gather
+assembles y on every rank.  A row's result does not depend on which rows
+share its launch, so the gathered y has the same bits as a one-device matvec.
+
+Slices are whole 8-row tiles (the device layout's unit) and all but the last
+rank get the same number of rows, so the gathered buffer's first N values are
+y in order with no reassembly.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional, Tuple
+
+import numpy as np
+
+from . import _native as N_
+
+TILE = 8
+_GGUF_BLOCK = {N_.TYPE_Q4_0: 18, N_.TYPE_Q4_1: 20}
+
+
+def row_split(n_rows: int, world: int) -> List[Tuple[int, int]]:
+    """[lo, hi) row range of each rank: ceil(tiles / world) tiles per rank,
+    the last rank takes what is left (possibly nothing)."""
+    if n_rows <= 0 or world <= 0:
+        raise ValueError("row_split needs n_rows > 0 and world > 0")
+    tiles = (n_rows + TILE - 1) // TILE
+    per = (tiles + world - 1) // world * TILE
+    return [(min(n_rows, r * per), min(n_rows, (r + 1) * per)) for r in range(world)]
+
+
+def rows_per_rank(n_rows: int, world: int) -> int:
+    """Padded slice length every rank contributes to the all-gather."""
+    lo, hi = row_split(n_rows, world)[0]
+    return hi - lo
+
+
+def gather_rows(y_local, n_rows: int, group=None):
+    """All-gather the ranks' padded slices (each rows_per_rank long, in rank
+    order) and return the first n_rows values: the full y on every rank.
+    Works for any torch.distributed backend (NCCL on GPUs, gloo in tests)."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    per = rows_per_rank(n_rows, world)
+    if y_local.numel() != per:
+        raise ValueError(f"local slice has {y_local.numel()} values, expected {per}")
+    out = torch.empty(world * per, dtype=y_local.dtype, device=y_local.device)
+    dist.all_gather_into_tensor(out, y_local.contiguous(), group=group)
+    return out[:n_rows]
+
+
+class RowSplitMatvec:
+    """One Q4_0/Q4_1 matrix split by rows over the ranks of a process group.
+
+    `raw` is the whole matrix as GGUF bytes (row-major blocks, as the
+    reference's rawBuf); each rank uploads only its own rows.  `matvec(x)`
+    takes x on this rank's device and returns the full y (a torch tensor on
+    the same device) after the all-gather."""
+
+    def __init__(self, ctx: N_.Context, raw: np.ndarray, quant_type: int, n_rows: int, k: int, group=None):
+        import torch
+        import torch.distributed as dist
+        if quant_type not in _GGUF_BLOCK:
+            raise ValueError("row-split matvec supports Q4_0 and Q4_1")
+        if k % 32:
+            raise ValueError("K must be a multiple of 32")
+        self.ctx, self.N, self.K, self.group = ctx, n_rows, k, group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.lo, self.hi = row_split(n_rows, self.world)[self.rank]
+        self.per = rows_per_rank(n_rows, self.world)
+        row_bytes = (k // 32) * _GGUF_BLOCK[quant_type]
+        raw = np.ascontiguousarray(raw, np.uint8)
+        if raw.size != n_rows * row_bytes:
+            raise ValueError(f"raw holds {raw.size} bytes, expected {n_rows * row_bytes}")
+        self.m = None
+        if self.hi > self.lo:
+            self.m = N_.QMat(ctx, quant_type, raw[self.lo * row_bytes:self.hi * row_bytes], self.hi - self.lo, k)
+        dev = torch.device("cuda", ctx.device)
+        self.y_local = torch.zeros(self.per, dtype=torch.float32, device=dev)
+        self.stream = torch.cuda.ExternalStream(N_.lib().pb_stream(ctx.h), device=dev)
+
+    def local(self, x) -> None:
+        """This rank's rows into y_local (enqueued on the library's stream)."""
+        if self.m is not None:
+            self.ctx._check(N_.lib().pb_qmat_matvec(self.ctx.h, self.m.h, ctypes.c_void_p(x.data_ptr()),
+                                                    ctypes.c_void_p(self.y_local.data_ptr()), 0, 0))
+
+    def matvec(self, x):
+        """Full y on every rank: local rows, then the all-gather, both ordered
+        on the library's stream."""
+        import torch
+        if x.numel() != self.K or x.dtype != torch.float32 or not x.is_cuda:
+            raise ValueError("x must be a float32 CUDA tensor of K values")
+        caller = torch.cuda.current_stream(x.device)
+        self.stream.wait_stream(caller)  # x was produced on the caller's stream
+        with torch.cuda.stream(self.stream):
+            self.local(x)
+            y = gather_rows(self.y_local, self.N, self.group)
+        caller.wait_stream(self.stream)
+        return y
+
+    def free(self) -> None:
+        if self.m is not None:
+            self.m.free()
+            self.m = None
+
+
+class AtomicsThreadPool:
+    """thread-pool.js:57-345 over GPUs: `matvec(x, rawBuf, quantType, N, K)`
+    with host arrays in and out, every rank computing its rows.  Like the
+    reference, each call copies the weight slice in (here to the device); a
+    runtime that keeps weights resident uses RowSplitMatvec instead."""
+
+    def __init__(self, ctx: N_.Context, group=None):
+        self.ctx, self.group = ctx, group
+
+    def matvec(self, x: np.ndarray, rawBuf: np.ndarray, quantType: int, N: int, K: int) -> np.ndarray:
+        import torch
+        rs = RowSplitMatvec(self.ctx, rawBuf, quantType, N, K, self.group)
+        try:
+            xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(rs.y_local.device)
+            torch.cuda.synchronize(rs.y_local.device)
+            y = rs.matvec(xd)
+            rs.stream.synchronize()
+            return y.cpu().numpy()
+        finally:
+            rs.free()
+
+    def shutdown(self) -> None:
+        pass
