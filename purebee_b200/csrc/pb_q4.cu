@@ -130,31 +130,66 @@ __device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) {
 }
 
 
-// Q4_0 block partials of one row for the four lanes, times d, with the
-// block's x in registers (xr[j] = x[32b + j]).
-__device__ __forceinline__ float4 q4_0_row(uint4 pl, float d, const float (&xr)[32], float2 nz, const pb_magics& M) {
-  float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);  // blockAcc[0..1], [2..3]
-  const uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
+// f32 pairs held as 64-bit registers, so packed operands never need moves.
+__device__ __forceinline__ uint64_t p2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 up2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t p2add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t p2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t p2mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// Two rows of the same block at once, x of the block as 16 pairs
+// xp[i] = (x[2i], x[2i+1]).  Same arithmetic as q4_0_row2.
+__device__ __forceinline__ void q4_0_row2p(uint4 pa, uint4 pb, float da, float db, const uint64_t (&xp)[16],
+                                           uint64_t nz, const pb_magics& M, float4& ra, float4& rb) {
+  const uint64_t c_l01 = p2(-8388616.0f, -32776.0f), c_l23 = p2(-136.0f, -32776.0f);
+  const uint64_t c_h = p2(-524296.0f, -2056.0f);
+  uint64_t a01 = 0, a23 = 0, b01 = 0, b23 = 0;  // +0.0f pairs
+  const uint32_t wa[4] = {pa.x, pa.y, pa.z, pa.w}, wb[4] = {pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
-    const uint32_t w = wv[g], w2 = w >> 16;
-    // byte 4g+L of the block feeds lane L: low nibble x[4g+L], high x[16+4g+L]
-    const float2 l01 = f2add(make_float2(magr<0xFu>(w, M.m0), magr<0xF00u>(w, M.m8)),
-                             make_float2(-8388616.0f, -32776.0f));
-    const float2 l23 = f2add(make_float2(magr<0xF0000u>(w, M.m16), magr<0xF00u>(w2, M.m8)),
-                             make_float2(-136.0f, -32776.0f));
-    const float2 h01 = f2add(make_float2(magr<0xF0u>(w, M.m4), magr<0xF000u>(w, M.m12)),
-                             make_float2(-524296.0f, -2056.0f));
-    const float2 h23 = f2add(make_float2(magr<0xF0u>(w2, M.m4), magr<0xF000u>(w2, M.m12)),
-                             make_float2(-524296.0f, -2056.0f));
-    a01 = f2add(a01, f2fma(l01, make_float2(xr[4 * g], xr[4 * g + 1]), nz));
-    a23 = f2add(a23, f2fma(l23, make_float2(xr[4 * g + 2], xr[4 * g + 3]), nz));
-    a01 = f2add(a01, f2fma(h01, make_float2(xr[16 + 4 * g], xr[16 + 4 * g + 1]), nz));
-    a23 = f2add(a23, f2fma(h23, make_float2(xr[16 + 4 * g + 2], xr[16 + 4 * g + 3]), nz));
+    const uint32_t w = wa[g], w2 = w >> 16, v = wb[g], v2 = v >> 16;
+    const uint64_t la01 = p2add(p2(magr<0xFu>(w, M.m0), magr<0xF00u>(w, M.m8)), c_l01);
+    const uint64_t lb01 = p2add(p2(magr<0xFu>(v, M.m0), magr<0xF00u>(v, M.m8)), c_l01);
+    const uint64_t la23 = p2add(p2(magr<0xF0000u>(w, M.m16), magr<0xF00u>(w2, M.m8)), c_l23);
+    const uint64_t lb23 = p2add(p2(magr<0xF0000u>(v, M.m16), magr<0xF00u>(v2, M.m8)), c_l23);
+    a01 = p2add(a01, p2fma(la01, xp[2 * g], nz));
+    b01 = p2add(b01, p2fma(lb01, xp[2 * g], nz));
+    a23 = p2add(a23, p2fma(la23, xp[2 * g + 1], nz));
+    b23 = p2add(b23, p2fma(lb23, xp[2 * g + 1], nz));
+    const uint64_t ha01 = p2add(p2(magr<0xF0u>(w, M.m4), magr<0xF000u>(w, M.m12)), c_h);
+    const uint64_t hb01 = p2add(p2(magr<0xF0u>(v, M.m4), magr<0xF000u>(v, M.m12)), c_h);
+    const uint64_t ha23 = p2add(p2(magr<0xF0u>(w2, M.m4), magr<0xF000u>(w2, M.m12)), c_h);
+    const uint64_t hb23 = p2add(p2(magr<0xF0u>(v2, M.m4), magr<0xF000u>(v2, M.m12)), c_h);
+    a01 = p2add(a01, p2fma(ha01, xp[8 + 2 * g], nz));
+    b01 = p2add(b01, p2fma(hb01, xp[8 + 2 * g], nz));
+    a23 = p2add(a23, p2fma(ha23, xp[9 + 2 * g], nz));
+    b23 = p2add(b23, p2fma(hb23, xp[9 + 2 * g], nz));
   }
-  const float2 dd = make_float2(d, d);
-  const float2 r01 = f2mul(a01, dd), r23 = f2mul(a23, dd);
-  return make_float4(r01.x, r01.y, r23.x, r23.y);
+  const uint64_t dA = p2(da, da), dB = p2(db, db);
+  const float2 ra01 = up2(p2mul(a01, dA)), ra23 = up2(p2mul(a23, dA));
+  const float2 rb01 = up2(p2mul(b01, dB)), rb23 = up2(p2mul(b23, dB));
+  ra = make_float4(ra01.x, ra01.y, ra23.x, ra23.y);
+  rb = make_float4(rb01.x, rb01.y, rb23.x, rb23.y);
 }
 
 // Two rows of the same block at once (the four accumulation chains of the two
@@ -419,6 +454,152 @@ k_matvec(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, const
   }
 }
 
+// ---------------------------------------------------------------------------
+// Warp-specialised matvec for K <= 4096 (nb <= 128).  Each slot is Cs =
+// roundup(2 nb, 32) compute threads plus one chain warp.  The compute threads
+// never wait for the chain: they hand each tile's partials over through a
+// two-buffer ring guarded by named barriers (FULL: compute arrives, chain
+// syncs; EMPTY: chain arrives, compute syncs before reusing a buffer).
+// ---------------------------------------------------------------------------
+
+constexpr int MVW_MAX_SLOTS = 3;  // 4 named barriers per slot, ids 1..12
+
+__host__ __device__ __forceinline__ int mvw_compute_threads(int nb) { return (2 * nb + 31) / 32 * 32; }
+__host__ __device__ __forceinline__ int mvw_slots(int nb) {
+  const int s = 512 / (mvw_compute_threads(nb) + 32);
+  return s < MVW_MAX_SLOTS ? s : MVW_MAX_SLOTS;
+}
+__host__ __device__ __forceinline__ int mvw_threads(int nb) { return mvw_slots(nb) * (mvw_compute_threads(nb) + 32); }
+
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void named_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(512, 1)
+k_matvec_ws(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, const uint16_t* __restrict__ msc, int N,
+            int nb, int tile_begin, int tile_end, int row_end, const float* __restrict__ x, float* __restrict__ y,
+            pb_mv_epi epi, float nzf, pb_magics M, int* err) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ double red[16];
+  const int S = mvw_slots(nb), Cs = mvw_compute_threads(nb), stride = Cs + 32;
+  const int K = nb * 32;
+  float* ps = reinterpret_cast<float*>(smem_raw);                         // [S][2][nb][8 rows (swizzled)][4]
+  float4* xs4 = reinterpret_cast<float4*>(ps + (size_t)2 * S * nb * 32);  // x, chunks swizzled per block
+  const int tid = threadIdx.x;
+  const int s = tid / stride, rem = tid - s * stride;
+  const bool chain = rem >= Cs;                 // the slot's last warp
+  const int h = chain ? 2 : rem / nb, b = (!chain && h < 2) ? rem - h * nb : 0;
+  const bool worker = !chain && h < 2;
+  const int per_iter = gridDim.x * S;
+  const float2 nz = make_float2(nzf, nzf);
+  const int first = tile_begin + s * gridDim.x + blockIdx.x;
+  const int n_iter = first < tile_end ? (tile_end - first + per_iter - 1) / per_iter : 0;  // slot-uniform
+
+  const size_t tq = (size_t)8 * nb * 16, td = (size_t)8 * nb * 2;
+  auto prefetch_tile = [&](int t) {
+    if (t < tile_end) {
+      pb_l2_prefetch(qs + (size_t)t * tq, (uint32_t)tq);
+      pb_l2_prefetch(dsc + (size_t)t * td / 2, (uint32_t)td);
+      if (TYPE == PB_TYPE_Q4_1) pb_l2_prefetch(msc + (size_t)t * td / 2, (uint32_t)td);
+    }
+  };
+  const bool pf_thread = rem == 0;
+  if (pf_thread)
+    for (int i = 0; i < MV_PF_DIST; ++i) prefetch_tile(first + i * per_iter);
+  if (tid == 0)
+    for (int i = 0; i < PB_MAX_L2_NEXT; ++i) pb_l2_prefetch_share(epi.l2_next[i], epi.l2_next_bytes[i], blockIdx.x, gridDim.x);
+  MvBuf A, B;
+  if (worker && n_iter > 0) mv_load<TYPE>(A, qs, dsc, msc, first, h, b, nb);
+  pb_pdl_trigger();
+  pb_pdl_wait();
+
+  if (epi.norm_w) {
+    double ss = 0.0;
+    for (int j = tid; j < K; j += blockDim.x) ss = __fma_rn((double)x[j], (double)x[j], ss);
+    ss = pb_block_sum_d(ss, red);
+    const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)K), epi.eps));
+    for (int j = tid; j < K; j += blockDim.x) {
+      const float v = (float)__dmul_rn(__ddiv_rn((double)x[j], rms), (double)epi.norm_w[j]);
+      const int bj = j >> 5, c = (j >> 2) & 7;
+      reinterpret_cast<float*>(xs4 + bj * 8 + (c ^ (bj & 7)))[j & 3] = v;
+    }
+  } else {
+    for (int c = tid; c < K / 4; c += blockDim.x) {
+      const int bj = c >> 3, i = c & 7;
+      xs4[bj * 8 + (i ^ (bj & 7))] = reinterpret_cast<const float4*>(x)[c];
+    }
+  }
+  __syncthreads();
+  float* pslot = ps + (size_t)s * 2 * nb * 32;
+  const int bar = 1 + 4 * s;  // FULL0, FULL1, EMPTY0, EMPTY1
+
+  if (chain) {
+    for (int it = 0; it < n_iter; ++it) {
+      named_sync(bar + (it & 1), stride);
+      mv_chain(pslot + (size_t)(it & 1) * nb * 32, nb, first + it * per_iter, N, row_end, y, epi, err);
+      if (it + 2 < n_iter) named_arrive(bar + 2 + (it & 1), stride);
+    }
+    return;
+  }
+
+  float xr[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 v = xs4[b * 8 + (i ^ (b & 7))];
+    xr[4 * i] = v.x;
+    xr[4 * i + 1] = v.y;
+    xr[4 * i + 2] = v.z;
+    xr[4 * i + 3] = v.w;
+  }
+  float4 sx = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (TYPE == PB_TYPE_Q4_1) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      sx.x = __fadd_rn(__fadd_rn(sx.x, xr[4 * g]), xr[16 + 4 * g]);
+      sx.y = __fadd_rn(__fadd_rn(sx.y, xr[4 * g + 1]), xr[16 + 4 * g + 1]);
+      sx.z = __fadd_rn(__fadd_rn(sx.z, xr[4 * g + 2]), xr[16 + 4 * g + 2]);
+      sx.w = __fadd_rn(__fadd_rn(sx.w, xr[4 * g + 3]), xr[16 + 4 * g + 3]);
+    }
+  }
+  uint64_t xp[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) xp[i] = p2(xr[2 * i], xr[2 * i + 1]);
+  const uint64_t nz64 = p2(nzf, nzf);
+  auto iteration = [&](MvBuf& cur, MvBuf& nxt, int it) {
+    const int tc = first + it * per_iter;
+    if (pf_thread) prefetch_tile(tc + MV_PF_DIST * per_iter);
+    if (worker && it + 1 < n_iter) mv_load<TYPE>(nxt, qs, dsc, msc, tc + per_iter, h, b, nb);
+    if (it >= 2) named_sync(bar + 2 + (it & 1), stride);  // the chain is done with this buffer
+    if (worker) {
+      float* pw = pslot + (size_t)(it & 1) * nb * 32 + (size_t)b * 32;
+#pragma unroll
+      for (int i = 0; i < MV_RPT; i += 2) {
+        const int r = h * MV_RPT + i;
+        float4 p0, p1;
+        if (TYPE == PB_TYPE_Q4_0) {
+          q4_0_row2p(cur.q[i], cur.q[i + 1], pb_f16_wasm(cur.d[i]), pb_f16_wasm(cur.d[i + 1]), xp, nz64, M, p0, p1);
+        } else {
+          p0 = q4_1_row(cur.q[i], pb_f16_wasm(cur.d[i]), pb_f16_wasm(cur.m[i]), xr, sx, nz, M);
+          p1 = q4_1_row(cur.q[i + 1], pb_f16_wasm(cur.d[i + 1]), pb_f16_wasm(cur.m[i + 1]), xr, sx, nz, M);
+        }
+        *reinterpret_cast<float4*>(pw + ((r ^ (b & 7)) << 2)) = p0;
+        *reinterpret_cast<float4*>(pw + (((r + 1) ^ (b & 7)) << 2)) = p1;
+      }
+    }
+    named_arrive(bar + (it & 1), stride);
+  };
+  for (int it = 0; it < n_iter; it += 2) {
+    iteration(A, B, it);
+    if (it + 1 < n_iter) iteration(B, A, it + 1);
+  }
+}
+
+static size_t mvw_smem(const pb_qmat* w) {
+  return (size_t)2 * mvw_slots(w->nb) * w->nb * 32 * 4 + (size_t)w->nb * 32 * 4;
+}
+
 static size_t mv_smem(const pb_qmat* w, int nt) {
   return (size_t)2 * mv_slots(w->nb, nt) * w->nb * 32 * 4 + (size_t)w->nb * 32 * 4;
 }
@@ -439,6 +620,14 @@ static int launch_mv_nt(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y,
 template <int TYPE>
 static int launch_mv(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int tile_begin, int ntiles, int row_end,
                      const pb_mv_epi& epi) {
+  if (w->nb <= 128) {
+    const int S = mvw_slots(w->nb), groups = (ntiles + S - 1) / S;
+    const int grid = groups < ctx->sm_count ? groups : ctx->sm_count;
+    return pb_launch(ctx, "k_matvec_ws", true, k_matvec_ws<TYPE>, dim3(grid), dim3(mvw_threads(w->nb)), mvw_smem(w),
+                     (const uint8_t*)w->qs, (const uint16_t*)w->d, (const uint16_t*)w->m, w->N, w->nb, tile_begin,
+                     tile_begin + ntiles, row_end, x, y, epi, -0.0f,
+                     pb_magics{PB_MAG0, PB_MAG4, PB_MAG8, PB_MAG12, PB_MAG16}, ctx->d_err);
+  }
   return launch_mv_nt<TYPE, MV_THREADS>(ctx, w, x, y, tile_begin, ntiles, row_end, epi);
 }
 
@@ -932,6 +1121,8 @@ int pb_setup_q4_kernels(void) {
   cudaError_t e = cudaSuccess;
   e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_0, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   e = e ? e : cudaFuncSetAttribute(k_matvec<PB_TYPE_Q4_1, 512>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_matvec_ws<PB_TYPE_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  e = e ? e : cudaFuncSetAttribute(k_matvec_ws<PB_TYPE_Q4_1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   e = e ? e : cudaFuncSetAttribute(k_prefill_q4, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   e = e ? e : cudaFuncSetAttribute(k_head<PB_TYPE_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_head<PB_TYPE_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
