@@ -416,8 +416,12 @@ def run_case(args):
     import torch
     from purebee_b200 import _native as N
     L = N.lib()
-    kind, shape = args.case.split(":")
-    n, k = (int(v) for v in shape.lower().split("x"))
+    kind, shape = args.case.split(":", 1)
+    mtok = 1
+    if kind == "gemm":  # gemm:MxNxK
+        mtok, n, k = (int(v) for v in shape.lower().split("x"))
+    else:
+        n, k = (int(v) for v in shape.lower().split("x"))
     ctx = N.Context(0)
     torch.cuda.set_device(0)
     stream = torch.cuda.ExternalStream(L.pb_stream(ctx.h), device=0)
@@ -429,7 +433,11 @@ def run_case(args):
     x = ctx.to_device(rng.standard_normal(k).astype(np.float32))
     y = ctx.alloc(n * 4)
     idx = ctx.alloc(16)
-    if kind == "matvec":
+    if kind == "gemm":
+        X = ctx.to_device(rng.standard_normal((mtok, k)).astype(np.float32))
+        Cb = ctx.alloc(mtok * n * 4)
+        call = lambda: ctx._check(L.pb_q4_gemm(ctx.h, m.h, X.ptr, mtok, k, Cb.ptr, n))
+    elif kind == "matvec":
         call = lambda: ctx._check(L.pb_qmat_matvec(ctx.h, m.h, x.ptr, y.ptr, 0, 0))
     elif kind == "head":
         call = lambda: ctx._check(L.pb_qmat_head(ctx.h, m.h, x.ptr, y.ptr, idx.ptr))
@@ -438,7 +446,10 @@ def run_case(args):
     for _ in range(args.warmup):
         call()
     us = graph_time_us(ctx, torch, stream, lambda i: call(), args.steps)
-    print(json.dumps({"case": args.case, "us_per_launch": round(us, 3), "bytes": int(raw.nbytes)}), flush=True)
+    line = {"case": args.case, "us_per_launch": round(us, 3), "bytes": int(raw.nbytes)}
+    if kind == "gemm":
+        line["TFLOPs"] = round(2.0 * mtok * n * k / (us * 1e-6) / 1e12, 1)
+    print(json.dumps(line), flush=True)
     m.free()
     ctx.close()
 
@@ -451,7 +462,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-max-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK or head:VxD")
+    ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK, head:VxD or gemm:MxNxK")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.case:

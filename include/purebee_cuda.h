@@ -136,6 +136,13 @@ int pb_qmat_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, float* y_d
 int pb_q4_0_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, int N, int K, float* y_host);
 /* wasm-q4.js:758-785 q4_1_matvec(x, rawBuf, N, K) */
 int pb_q4_1_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, int N, int K, float* y_host);
+/* Batched form of the Q4_0 matvec (the batched prefill / decode config):
+ * C[M][N] = X[M][K] . W[N][K]^T on the tensor cores (tcgen05, f16 operands,
+ * f32 accumulation), W a resident Q4_0 matrix (row layout).  Each operand is
+ * rounded to f16 once, so C agrees with the reference's f32 arithmetic
+ * (wasm-q4.js:118-267, wasm-simd.js:71-91) within a relative tolerance, not
+ * bit for bit.  x_dev 16-byte aligned, ldx a multiple of 4. */
+int pb_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int M, int ldx, float* c_dev, int ldc);
 /* wasm-q4.js:798-839 lmHead(hidden, embData, V, D): f32 row-major table on
  * the host, batch_dot lane order (wasm-q4.js:447-566). */
 int pb_lm_head(pb_ctx* ctx, const float* h_host, const float* emb_host, int V, int D, float* logits_host);

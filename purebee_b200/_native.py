@@ -75,6 +75,7 @@ SIGNATURES = {
     "pb_q4_0_matvec": (I, [V, V, V, I, I, V]),
     "pb_q4_1_matvec": (I, [V, V, V, I, I, V]),
     "pb_lm_head": (I, [V, V, V, I, I, V]),
+    "pb_q4_gemm": (I, [V, V, V, I, I, V, I]),
     "pb_qmat_head": (I, [V, V, V, V, V]),
     "pb_argmax": (I, [V, V, I, V]),
     "pb_matmul_f32": (I, [V, V, I, I, V, I, V, V]),

@@ -64,6 +64,19 @@ int pb_wait(pb_ctx* ctx) {
   return PB_OK;
 }
 
+int pb_ensure_gemm_scratch(pb_ctx* ctx, size_t bytes) {
+  if (ctx->gemm_scratch_bytes >= bytes) return PB_OK;
+  if (ctx->gemm_scratch) {
+    PB_TRY(pb_wait(ctx));
+    cudaFree(ctx->gemm_scratch);
+    ctx->gemm_scratch = nullptr;
+    ctx->gemm_scratch_bytes = 0;
+  }
+  PB_TRY_CUDA(ctx, cudaMalloc(&ctx->gemm_scratch, bytes));
+  ctx->gemm_scratch_bytes = bytes;
+  return PB_OK;
+}
+
 int pb_ensure_scratch(pb_ctx* ctx, size_t bytes) {
   if (ctx->scratch_bytes >= bytes) return PB_OK;
   if (ctx->scratch) {
@@ -110,7 +123,8 @@ extern "C" int pb_init(int device, pb_ctx** out) {
   if (cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess) { delete ctx; return PB_ERR_OOM; }
   cudaMemset(ctx->d_err, 0, sizeof(int));
   cudaDeviceSynchronize();
-  if (pb_setup_q4_kernels() != PB_OK || pb_setup_ops_kernels() != PB_OK || pb_setup_noalloc(ctx) != PB_OK) {
+  if (pb_setup_q4_kernels() != PB_OK || pb_setup_ops_kernels() != PB_OK || pb_setup_gemm_kernels() != PB_OK ||
+      pb_setup_noalloc(ctx) != PB_OK) {
     pb_shutdown(ctx);
     return PB_ERR_CUDA;
   }
@@ -139,6 +153,7 @@ extern "C" int pb_shutdown(pb_ctx* ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   if (ctx->scratch) cudaFree(ctx->scratch);
+  if (ctx->gemm_scratch) cudaFree(ctx->gemm_scratch);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;

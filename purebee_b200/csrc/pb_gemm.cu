@@ -1,0 +1,471 @@
+// pb_gemm.cu - tensor-core Q4_0 x f16 GEMM for the batched configuration.
+//
+// C[M tokens][N rows] = X[M][K] . W[N][K]^T, W a resident Q4_0 matrix in the
+// row layout.  This is the batched prefill / batched decode form of the
+// reference's per-row matvec (wasm-q4.js:118-267) and of its prefill matmul
+// (llama-streaming.js:398 -> wasm-simd.js:71-91).  It does not reproduce the
+// reference's f32 operation order: each operand is rounded to f16 once (the
+// weight value (q-8)*d is exact in f32 and rounded once; x is rounded once),
+// products are exact and the sums run in f32 on the tensor cores.  Results
+// therefore agree with the reference within a stated relative tolerance, not
+// bit for bit; the batch-1 decode path keeps the exact kernels.
+//
+// One CTA computes a 128-row x 128-token tile with tcgen05.mma (kind::f16,
+// M = 128, N = 128, K = 16 per instruction), the accumulator in 128 TMEM
+// columns.  Per 64-wide K step all 256 threads stage the operands into a
+// double-buffered shared-memory ring in the K-major 128-byte-swizzled layout
+// the MMA descriptors name: the weight tile is dequantized on the fly
+// (2 Q4_0 blocks per row), the activations are rounded to f16.  One thread
+// issues the four MMAs of a step and commits them to the stage's mbarrier;
+// the stage is rewritten only after that mbarrier's phase completes.  Every
+// wait is bounded and records PB_DEVERR_WAIT instead of hanging.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <mutex>
+
+#include "pb_internal.cuh"
+
+namespace {
+
+constexpr int GM_ROWS = 128;    // weight rows per CTA (MMA M)
+constexpr int GM_TOK = 128;     // tokens per CTA (MMA N)
+constexpr int GM_KSTEP = 64;    // K per stage: one 128-byte swizzle row of f16
+constexpr int GM_THREADS = 256;
+constexpr int GM_TILE_BYTES = GM_ROWS * GM_KSTEP * 2;  // 16 KB, A and B alike
+constexpr int GM_STAGE_BYTES = 2 * GM_TILE_BYTES;
+constexpr int PB_GEMM_TMA_MIN_M = 512;  // from here on the f16 copy of W pays for itself
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Byte offset of 16-byte chunk c (K elements 8c .. 8c+7) of row r in a
+// K-major, 128-byte-swizzled tile: 8-row groups of 1024 bytes, rows of 128
+// bytes, chunk index XOR (row mod 8).
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024
+// bytes apart (stride byte offset), sm100 descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: D f32, A and B f16, both K-major, N = 128, M = 128.
+constexpr uint32_t GM_IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(GM_TOK >> 3) << 17) |
+                              ((uint32_t)(GM_ROWS >> 4) << 24);
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// Wait for the phase of the given parity; gives up after ~2 s of device clock.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  const uint32_t addr = smem_addr(bar);
+  const long long t0 = clock64();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((it & 255) == 255 && clock64() - t0 > 4000000000LL) {
+      pb_raise(err, PB_DEVERR_WAIT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(GM_IDESC), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(GM_THREADS, 1)
+k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, int N_pad, int nb,
+             const float* __restrict__ X, int ldx, int M, float* __restrict__ C, int ldc, int* err) {
+  extern __shared__ __align__(1024) unsigned char gm_raw[];
+  __shared__ uint64_t bars[2];
+  __shared__ uint32_t tmem_base;
+  // 1024-byte alignment of the swizzled tiles (the swizzle repeats every 1024 bytes)
+  unsigned char* ring = gm_raw + ((1024 - (smem_addr(gm_raw) & 1023)) & 1023);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * GM_ROWS, m0 = blockIdx.y * GM_TOK;
+  const int K = nb * 32, ksteps = (K + GM_KSTEP - 1) / GM_KSTEP;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+                 "r"(GM_TOK)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_d = tmem_base;
+
+  bool ok = true;
+  for (int ks = 0; ks < ksteps && ok; ++ks) {
+    const int st = ks & 1;
+    unsigned char* sA = ring + st * GM_STAGE_BYTES;
+    unsigned char* sB = sA + GM_TILE_BYTES;
+    if (ks >= 2) ok = mbar_wait(&bars[st], ((ks >> 1) - 1) & 1, err);  // MMAs of step ks-2 are done with it
+    if (!ok) break;
+    // weights: thread -> (row, block) of the two Q4_0 blocks of this step
+    {
+      const int r = tid >> 1, blk = tid & 1, b = ks * 2 + blk, row = n0 + r;
+      uint4 pl = make_uint4(0, 0, 0, 0);
+      float d = 0.0f;
+      if (b < nb && row < N_pad) {
+        const size_t slot = (size_t)row * nb + b;
+        pl = __ldg(reinterpret_cast<const uint4*>(qs) + slot);
+        d = pb_f16_exact(__ldg(dsc + slot));
+      }
+      const uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
+      float e[32];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t byte = (wv[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+        e[j] = (float)((int)(byte & 15u) - 8) * d;       // exact in f32
+        e[16 + j] = (float)((int)(byte >> 4) - 8) * d;
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4 v;
+        v.x = pack_h2(e[8 * c + 0], e[8 * c + 1]);
+        v.y = pack_h2(e[8 * c + 2], e[8 * c + 3]);
+        v.z = pack_h2(e[8 * c + 4], e[8 * c + 5]);
+        v.w = pack_h2(e[8 * c + 6], e[8 * c + 7]);
+        *reinterpret_cast<uint4*>(sA + sw128(r, blk * 4 + c)) = v;
+      }
+    }
+    // activations: thread -> (token, half of the 64-wide step)
+    {
+      const int r = tid >> 1, hh = tid & 1, m = m0 + r;
+      const int k = ks * GM_KSTEP + hh * 32;
+      const bool live = m < M && k < K;
+      const float4* xr = reinterpret_cast<const float4*>(X + (size_t)m * ldx + k);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), bq = a;
+        if (live) {
+          a = __ldg(xr + 2 * c);
+          bq = __ldg(xr + 2 * c + 1);
+        }
+        uint4 v;
+        v.x = pack_h2(a.x, a.y);
+        v.y = pack_h2(a.z, a.w);
+        v.z = pack_h2(bq.x, bq.y);
+        v.w = pack_h2(bq.z, bq.w);
+        *reinterpret_cast<uint4*>(sB + sw128(r, hh * 4 + c)) = v;
+      }
+    }
+    // generic-proxy writes -> visible to the tensor core's async proxy
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (tid == 0) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sB));
+#pragma unroll
+      for (int kk = 0; kk < GM_KSTEP / 16; ++kk)  // +32 bytes (16 f16) along K per MMA
+        mma_f16(tmem_d, da + 2 * kk, db + 2 * kk, (ks > 0 || kk > 0) ? 1u : 0u);
+      mma_commit(&bars[st]);
+    }
+  }
+  // the last step's commit covers every MMA issued before it
+  if (ok && ksteps > 0) ok = mbar_wait(&bars[(ksteps - 1) & 1], ((ksteps - 1) >> 1) & 1, err);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (ok && warp < 4) {
+    // warp w reads TMEM lanes 32w .. 32w+31 (weight rows), 32 token columns at a time
+    const int row = n0 + warp * 32 + lane;
+#pragma unroll 1
+    for (int c0 = 0; c0 < GM_TOK; c0 += 32) {
+      uint32_t v[32];
+      tmem_ld32(tmem_d + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+      if (row < N) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int m = m0 + c0 + j;
+          if (m < M) C[(size_t)m * ldc + row] = __uint_as_float(v[j]);
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(GM_TOK) : "memory");
+}
+
+static size_t gm_smem() { return 2 * GM_STAGE_BYTES + 1024; }
+
+// ---------------------------------------------------------------------------
+// Large batches: a plain f16 GEMM fed by TMA.  The Q4_0 weights are first
+// dequantized to an f16 copy ((q-8)*d exact in f32, rounded once, the same
+// values the fused kernel stages) and x is rounded to f16 once; both then
+// stream through a 4-stage ring of 128-byte-swizzled tiles loaded by
+// cp.async.bulk.tensor.  Warp roles: warp 0 lane 0 issues the TMA loads,
+// warp 1 lane 0 issues the MMAs (128 x 256 x 16 per instruction, accumulator
+// in 256 TMEM columns) and commits each stage back to its "empty" barrier,
+// warps 4-7 (TMEM lane quadrants 0-3) drain the accumulator.  The dequant
+// copy costs N*K*2 bytes, about 1% of the GEMM time when M >= 512.
+// ---------------------------------------------------------------------------
+
+constexpr int TG_ROWS = 128, TG_TOK = 256, TG_K = 64, TG_STAGES = 4, TG_THREADS = 256;
+constexpr int TG_A_BYTES = TG_ROWS * TG_K * 2, TG_B_BYTES = TG_TOK * TG_K * 2;
+constexpr int TG_STAGE_BYTES = TG_A_BYTES + TG_B_BYTES;
+constexpr uint32_t TG_IDESC = (1u << 4) | ((uint32_t)(TG_TOK >> 3) << 17) | ((uint32_t)(TG_ROWS >> 4) << 24);
+
+namespace {
+
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_n256(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(TG_IDESC), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+      : "memory");
+}
+
+}  // namespace
+
+__global__ void k_dequant_q4_f16(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int64_t nblocks,
+                                 __half* __restrict__ out) {
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one block of 32 per thread
+  if (b >= nblocks) return;
+  const uint4 pl = __ldg(reinterpret_cast<const uint4*>(qs) + b);
+  const float d = pb_f16_exact(__ldg(dsc + b));
+  const uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
+  uint32_t lo[8], hi[8];
+#pragma unroll
+  for (int j = 0; j < 16; j += 2) {
+    const uint32_t b0 = (wv[j >> 2] >> (8 * (j & 3))) & 0xFFu, b1 = (wv[(j + 1) >> 2] >> (8 * ((j + 1) & 3))) & 0xFFu;
+    lo[j >> 1] = pack_h2((float)((int)(b0 & 15u) - 8) * d, (float)((int)(b1 & 15u) - 8) * d);
+    hi[j >> 1] = pack_h2((float)((int)(b0 >> 4) - 8) * d, (float)((int)(b1 >> 4) - 8) * d);
+  }
+  uint4* o = reinterpret_cast<uint4*>(out + b * 32);
+  o[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  o[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+  o[2] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  o[3] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+}
+
+__global__ void k_f32_to_f16(const float* __restrict__ x, int M, int K, int ldx, __half* __restrict__ out) {
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;  // 4 values per thread
+  if (i >= (int64_t)M * K) return;
+  const int m = (int)(i / K), k = (int)(i % K);
+  const float4 v = __ldg(reinterpret_cast<const float4*>(x + (size_t)m * ldx + k));
+  reinterpret_cast<uint2*>(out)[i / 4] = make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
+}
+
+__global__ void __launch_bounds__(TG_THREADS, 1)
+k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, int N, int M,
+               int K, float* __restrict__ C, int ldc, int* err) {
+  extern __shared__ __align__(1024) unsigned char tg_raw[];
+  __shared__ uint64_t full[TG_STAGES], empty[TG_STAGES], acc_full;
+  __shared__ uint32_t tmem_base;
+  unsigned char* ring = tg_raw + ((1024 - (smem_addr(tg_raw) & 1023)) & 1023);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * TG_ROWS, m0 = blockIdx.y * TG_TOK;
+  const int ksteps = K / TG_K;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+                 "r"(TG_TOK)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 32) {
+    for (int s = 0; s < TG_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&acc_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_d = tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // producer: stage s is free once the MMAs of step ks - STAGES committed to empty[s]
+    for (int ks = 0; ks < ksteps; ++ks) {
+      const int s = ks % TG_STAGES;
+      if (ks >= TG_STAGES && !mbar_wait(&empty[s], ((ks / TG_STAGES) - 1) & 1, err)) break;
+      unsigned char* sA = ring + s * TG_STAGE_BYTES;
+      mbar_arrive_tx(&full[s], TG_STAGE_BYTES);
+      tma_load_2d(sA, &map_w, ks * TG_K, n0, &full[s]);
+      tma_load_2d(sA + TG_A_BYTES, &map_x, ks * TG_K, m0, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer
+    bool ok = true;
+    for (int ks = 0; ks < ksteps && ok; ++ks) {
+      const int s = ks % TG_STAGES;
+      ok = mbar_wait(&full[s], (ks / TG_STAGES) & 1, err);
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      unsigned char* sA = ring + s * TG_STAGE_BYTES;
+      const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sA + TG_A_BYTES));
+#pragma unroll
+      for (int kk = 0; kk < TG_K / 16; ++kk) mma_f16_n256(tmem_d, da + 2 * kk, db + 2 * kk, (ks > 0 || kk > 0) ? 1u : 0u);
+      mma_commit(&empty[s]);
+    }
+    mma_commit(&acc_full);  // fires when every MMA above has completed
+  } else if (warp >= 4) {
+    const int q = warp - 4;  // TMEM lane quadrant
+    if (mbar_wait(&acc_full, 0, err)) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int row = n0 + q * 32 + lane;
+#pragma unroll 1
+      for (int c0 = 0; c0 < TG_TOK; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        if (row < N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < M) C[(size_t)m * ldc + row] = __uint_as_float(v[j]);
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(TG_TOK) : "memory");
+  }
+}
+
+static size_t tg_smem() { return (size_t)TG_STAGES * TG_STAGE_BYTES + 1024; }
+
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder(pb_ctx* ctx) {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) pb_set_error(ctx, PB_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  return fn;
+}
+
+// Row-major f16 [rows][K] with a box of box_rows x 64 elements, 128-byte swizzle.
+static int make_map(pb_ctx* ctx, CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+  auto enc = tensor_map_encoder(ctx);
+  if (!enc) return PB_ERR_CUDA;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)TG_K, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return pb_set_error(ctx, PB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return PB_OK;
+}
+
+static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc) {
+  const int K = w->K;
+  const size_t wbytes = (size_t)w->N_pad * K * 2, xbytes = (size_t)M * K * 2;
+  const size_t off_x = (wbytes + 1023) & ~(size_t)1023;
+  PB_TRY(pb_ensure_gemm_scratch(ctx, off_x + xbytes));
+  __half* w16 = reinterpret_cast<__half*>(ctx->gemm_scratch);
+  __half* x16 = reinterpret_cast<__half*>(static_cast<char*>(ctx->gemm_scratch) + off_x);
+  const int64_t nblk = (int64_t)w->N_pad * w->nb;
+  k_dequant_q4_f16<<<pb_cdiv(nblk, 256), 256, 0, ctx->stream>>>(w->qs, w->d, nblk, w16);
+  PB_LAUNCHED(ctx, "k_dequant_q4_f16");
+  k_f32_to_f16<<<pb_cdiv((int64_t)M * K / 4, 256), 256, 0, ctx->stream>>>(X, M, K, ldx, x16);
+  PB_LAUNCHED(ctx, "k_f32_to_f16");
+  CUtensorMap mw, mx;
+  PB_TRY(make_map(ctx, &mw, w16, w->N_pad, K, TG_ROWS));
+  PB_TRY(make_map(ctx, &mx, x16, M, K, TG_TOK));
+  dim3 grid(pb_cdiv(w->N, TG_ROWS), pb_cdiv(M, TG_TOK));
+  if (grid.y > 65535) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
+  k_gemm_f16_tma<<<grid, TG_THREADS, tg_smem(), ctx->stream>>>(mw, mx, w->N, M, K, C, ldc, ctx->d_err);
+  PB_LAUNCHED(ctx, "k_gemm_f16_tma");
+  return PB_OK;
+}
+
+int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc) {
+  if (!ctx || !w || !X || !C || M <= 0) return PB_ERR_ARG;
+  if (w->type != PB_TYPE_Q4_0 || w->layout != PB_LAYOUT_ROWS)
+    return pb_set_error(ctx, PB_ERR_ARG, "the tensor-core GEMM needs a Q4_0 matrix in the row layout");
+  if ((ldx & 3) || ((uintptr_t)X & 15))
+    return pb_set_error(ctx, PB_ERR_ARG, "X must be 16-byte aligned with a row stride that is a multiple of 4");
+  if (M >= PB_GEMM_TMA_MIN_M && w->K % TG_K == 0) return launch_gemm_tma(ctx, w, X, ldx, M, C, ldc);
+  dim3 grid(pb_cdiv(w->N, GM_ROWS), pb_cdiv(M, GM_TOK));
+  if (grid.y > 65535) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
+  k_q4_gemm_tc<<<grid, GM_THREADS, gm_smem(), ctx->stream>>>(w->qs, w->d, w->N, w->N_pad, w->nb, X, ldx, M, C, ldc,
+                                                           ctx->d_err);
+  PB_LAUNCHED(ctx, "k_q4_gemm_tc");
+  return PB_OK;
+}
+
+extern "C" int pb_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int M, int ldx, float* c_dev, int ldc) {
+  if (!w) return PB_ERR_ARG;
+  if (ldx < w->K || ldc < w->N) return pb_set_error(ctx, PB_ERR_ARG, "row strides smaller than the matrix");
+  return pb_launch_q4_gemm(ctx, w, x_dev, ldx, M, c_dev, ldc);
+}
+
+int pb_setup_gemm_kernels(void) {
+  cudaError_t e = cudaFuncSetAttribute(k_q4_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gm_smem());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_gemm_f16_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tg_smem());
+  return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
+}

@@ -22,6 +22,9 @@ struct pb_ctx {
   // scratch for one-shot host-buffer calls (grown on demand)
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
+  // f16 operand copies of the large-batch tensor-core GEMM (grown on demand)
+  void* gemm_scratch = nullptr;
+  size_t gemm_scratch_bytes = 0;
   // fixed per-device array of pb_attention_noalloc (looked up in pb_init)
   void* noalloc_attn = nullptr;
 };
@@ -54,6 +57,7 @@ int pb_cuda_error(pb_ctx* ctx, cudaError_t e, const char* what);
 int pb_wait(pb_ctx* ctx);  // bounded wait on the context stream
 int pb_check_launch(pb_ctx* ctx, const char* what);
 int pb_ensure_scratch(pb_ctx* ctx, size_t bytes);
+int pb_ensure_gemm_scratch(pb_ctx* ctx, size_t bytes);
 
 #define PB_TRY_CUDA(ctx, expr)                               \
   do {                                                       \
@@ -234,4 +238,5 @@ int pb_qmat_alloc(pb_ctx* ctx, int type, int layout, int N, int K, pb_qmat** out
 int pb_qmat_pack_from_device(pb_ctx* ctx, pb_qmat* m, const void* gguf_dev);
 int pb_setup_q4_kernels(void);
 int pb_setup_ops_kernels(void);
+int pb_setup_gemm_kernels(void);
 int pb_setup_noalloc(pb_ctx* ctx);  // with ctx->device current

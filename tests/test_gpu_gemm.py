@@ -1,0 +1,66 @@
+"""Tensor-core Q4_0 x f16 GEMM (pb_q4_gemm, the batched configuration), both
+the fused-dequant kernel (M < 512) and the TMA-fed kernel over f16 copies.
+
+Two references: the same f16-rounded operands summed in f64 (the only
+difference left is the f32 accumulation order on the tensor cores: rtol 2e-5
+of the output scale), and the reference's exact f32 arithmetic from the
+oracle (the per-row WASM matvec; f16 operand rounding: rtol 4e-3)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+f32 = np.float32
+RTOL_SAME_OPERANDS = 2e-5
+RTOL_VS_REFERENCE = 4e-3
+
+
+def rand_q4_0(rng, N, K):
+    raw = rng.integers(0, 256, N * (K // 32) * 18, dtype=np.uint8)
+    d = (rng.standard_normal(N * (K // 32)) * 0.01).astype(np.float16).view(np.uint8).reshape(-1, 2)
+    raw.reshape(-1, 18)[:, :2] = d
+    return raw
+
+
+def dequant_f16(raw, N, K):
+    blk = raw.reshape(N, K // 32, 18)
+    d = blk[:, :, :2].copy().view(np.float16).astype(np.float32)[:, :, 0]
+    q = blk[:, :, 2:]
+    lo = (q & 15).astype(np.int32) - 8
+    hi = (q >> 4).astype(np.int32) - 8
+    w = np.concatenate([lo, hi], axis=2).astype(np.float32) * d[:, :, None]
+    return w.reshape(N, K).astype(np.float16).astype(np.float64)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 128, 64), (37, 200, 2048), (128, 256, 128), (300, 1000, 576),
+                                   (64, 3072, 2048), (256, 2048, 8192), (130, 16384, 2048),
+                                   # M >= 512: f16 copies + TMA-fed pipeline (K % 64 == 0)
+                                   (512, 256, 2048), (1000, 3072, 2048), (600, 2048, 8192), (4096, 384, 576),
+                                   (513, 300, 1056)])
+def test_q4_gemm(native, ctx, oracle, M, N, K):
+    rng = np.random.default_rng(M * 131 + N + K)
+    raw = rand_q4_0(rng, N, K)
+    X = rng.standard_normal((M, K)).astype(f32)
+    m = native.QMat(ctx, native.TYPE_Q4_0, raw, N, K)
+    dx = ctx.to_device(X)
+    dc = ctx.alloc(M * N * 4)
+    ctx._check(native.lib().pb_q4_gemm(ctx.h, m.h, dx.ptr, M, K, dc.ptr, N))
+    ctx.sync()
+    assert ctx.device_error() == 0
+    C = dc.download(count=M * N).reshape(M, N)
+    ref16 = X.astype(np.float16).astype(np.float64) @ dequant_f16(raw, N, K).T
+    scale = np.max(np.abs(ref16))
+    assert np.max(np.abs(C - ref16)) <= RTOL_SAME_OPERANDS * scale
+    rows = [0, M // 2, M - 1]
+    exact = np.stack([oracle.q4_0_matvec(X[i], raw, N, K) for i in rows])
+    assert np.max(np.abs(C[rows] - exact)) <= RTOL_VS_REFERENCE * np.max(np.abs(exact))
+
+
+def test_q4_gemm_rejects(native, ctx):
+    rng = np.random.default_rng(1)
+    raw = rand_q4_0(rng, 64, 64)
+    L = native.lib()
+    table = native.QMat(ctx, native.TYPE_Q4_0 | native.QMAT_TABLE, raw, 64, 64)
+    dx, dc = ctx.alloc(64 * 64 * 4), ctx.alloc(64 * 64 * 4)
+    assert L.pb_q4_gemm(ctx.h, table.h, dx.ptr, 4, 64, dc.ptr, 64) == native.PB_ERR_ARG
+    rows = native.QMat(ctx, native.TYPE_Q4_0, raw, 64, 64)
+    assert L.pb_q4_gemm(ctx.h, rows.h, dx.ptr, 4, 63, dc.ptr, 64) == native.PB_ERR_ARG  # ldx < K
