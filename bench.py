@@ -38,6 +38,15 @@ METRIC = "Llama-3.2-1B-shape Q4 decode tok/s; Q4 matvec HBM GB/s vs B200 peak"
 WORKLOAD = "llama3.2-1B-shape Q4_0 batch-1 greedy decode (configs[3])"
 
 
+def load_flop_peak():
+    """Dense bf16 tensor peak (TFLOP/s): the measured burst figure, else the pool's fallback."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"])
+    return 1590.0
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -224,6 +233,52 @@ def row_split_vocab(ctx, torch, dist, world, peak, reps=40):
             "frac_local_of_measured_peak_per_gpu": round((slice_bytes + 4 * k + 4 * per) / (local_us * 1e-6) / 1e9 / peak, 3)}
 
 
+def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512, steps=256):
+    """configs[4] on this GPU: n_seqs seeded prompts of n_prompt tokens
+    prefilled as one batch (tensor-core GEMMs), then `steps` greedy decode
+    steps of every sequence (one replayed graph per step).  Device event
+    times; the linear-layer FLOPs of the prefill give its tensor roofline."""
+    from purebee_b200.runtime import BatchedLlamaRuntime
+    c = CFG
+    rng = np.random.default_rng(SEED + 5)
+    prompts = rng.integers(1, c["vocab"], (n_seqs, n_prompt)).astype(np.int32)
+    bt = BatchedLlamaRuntime(rt, n_seqs)
+    bt.prefill(prompts[:, :16])  # warm: allocations, GEMM scratch, kernels
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    ctx.sync()
+    e0.record(stream)
+    bt.prefill(prompts)
+    e1.record(stream)
+    e1.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    bt.decode(2)  # warm: records the decode graph
+    ctx.sync()
+    e1.record(stream)
+    toks = bt.decode(steps)
+    e2.record(stream)
+    e2.synchronize()
+    decode_ms = e1.elapsed_time(e2)
+    bt.free()
+    d, F, L, V, kv = c["dim"], c["hidden_dim"], c["n_layers"], c["vocab"], c["n_kv_heads"] * c["head_dim"]
+    lin_params = L * ((d + 2 * kv) * d + d * d + 2 * F * d + d * F)
+    tokens = n_seqs * n_prompt
+    lin_flops = 2.0 * lin_params * tokens + 2.0 * V * d * n_seqs
+    # decode step bytes: weights once + every sequence's K and V rows at the mean position
+    mid = n_prompt + 2 + steps // 2
+    step_bytes = lin_params * 18 / 32 + V * d * 18 / 32 + 2.0 * L * n_seqs * mid * kv * 4
+    dec_s = decode_ms / 1e3 / steps
+    return {"workload": f"configs[4]: {n_seqs} seqs x {n_prompt}-token seeded prompts, then {steps} greedy steps",
+            "prefill_ms": round(prefill_ms, 2), "prefill_tok_s": round(tokens / (prefill_ms / 1e3), 1),
+            "prefill_linear_TFLOPs": round(lin_flops / (prefill_ms / 1e3) / 1e12, 1),
+            "prefill_frac_of_bf16_peak": round(lin_flops / (prefill_ms / 1e3) / 1e12 / flop_peak, 3),
+            "decode_ms_per_step": round(decode_ms / steps, 3),
+            "decode_tok_s": round(n_seqs / dec_s, 1),
+            "decode_step_bytes": int(step_bytes),
+            "decode_frac_of_hbm": round(step_bytes / dec_s / 1e9 / peak, 3),
+            "tokens_sample": toks[-1][:4].tolist(),
+            "arithmetic": "projections and head: f16 operands, f32 accumulation (tcgen05); prefill attention f32"}
+
+
 def run_ours(args, rank, world, torch, dist):
     from purebee_b200 import _native as N
     dev = int(os.environ.get("LOCAL_RANK", 0))
@@ -298,6 +353,10 @@ def run_ours(args, rank, world, torch, dist):
         e2e_tps = e2e_steps / float(t.item())
 
     split = row_split_vocab(ctx, torch, dist, world, peak) if dist else None
+    batched = None
+    if not args.no_batched:
+        rt.resetCache()
+        batched = run_batched(ctx, torch, stream, rt, peak, load_flop_peak())
 
     result = None
     if rank == 0:
@@ -335,6 +394,8 @@ def run_ours(args, rank, world, torch, dist):
         }
         if split:
             result["row_split"] = split
+        if batched:
+            result["batched"] = batched
         if world == 1 and not args.no_cpu_baseline:
             result["cpu_baseline"] = cpu_baseline(rt, sample_tokens=2)
     rt.shutdown()
@@ -462,6 +523,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-max-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the batched configuration (configs[4])")
     ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK, head:VxD or gemm:MxNxK")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -138,7 +138,7 @@ int pb_q4_0_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, in
 int pb_q4_1_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, int N, int K, float* y_host);
 /* Batched form of the Q4_0 matvec (the batched prefill / decode config):
  * C[M][N] = X[M][K] . W[N][K]^T on the tensor cores (tcgen05, f16 operands,
- * f32 accumulation), W a resident Q4_0 matrix (row layout).  Each operand is
+ * f32 accumulation), W a resident Q4_0 matrix (either layout).  Each operand is
  * rounded to f16 once, so C agrees with the reference's f32 arithmetic
  * (wasm-q4.js:118-267, wasm-simd.js:71-91) within a relative tolerance, not
  * bit for bit.  x_dev 16-byte aligned, ldx a multiple of 4. */
@@ -274,6 +274,27 @@ int pb_model_kv(pb_model* m, int layer, int which_v, float* host, size_t floats)
 int64_t pb_model_decode_bytes(const pb_model* m, int pos);
 /* Kernel launches of one decode step. */
 int pb_model_decode_launches(const pb_model* m);
+
+/* ------------------------------------------------------------------ */
+/* batched serving (the batched configuration; the reference serves one  */
+/* sequence at a time, llama-streaming.js:738-815)                        */
+/* ------------------------------------------------------------------ */
+
+/* n_seqs (<= 256) independent sequences over a streaming model's weights
+ * (Q4_0 embedding), each with its own KV cache.  The projections and the LM
+ * head run as tensor-core GEMMs (pb_q4_gemm: f16 operands, f32 sums), so
+ * logits agree with the one-sequence path within a relative tolerance. */
+typedef struct pb_batch pb_batch;
+int pb_batch_create(pb_model* m, int n_seqs, pb_batch** out);
+int pb_batch_free(pb_batch* b);
+/* Prefill tokens_host [n_seqs][n_prompt] from position 0; next_host
+ * [n_seqs] gets each sequence's greedy token, logits_host [n_seqs][vocab]
+ * (optional) the last position's logits. */
+int pb_batch_prefill(pb_batch* b, const int* tokens_host, int n_prompt, int* next_host, float* logits_host);
+/* `steps` greedy decode steps of every sequence (one replayed CUDA graph per
+ * step); tokens_host [steps][n_seqs] (optional) gets the generated tokens,
+ * logits_host [n_seqs][vocab] (optional) the last step's logits. */
+int pb_batch_decode(pb_batch* b, int steps, int* tokens_host, float* logits_host);
 
 #ifdef __cplusplus
 }

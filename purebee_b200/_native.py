@@ -116,6 +116,10 @@ SIGNATURES = {
     "pb_model_kv": (I, [V, I, I, V, SZ]),
     "pb_model_decode_bytes": (I64, [V, I]),
     "pb_model_decode_launches": (I, [V]),
+    "pb_batch_create": (I, [V, I, ctypes.POINTER(V)]),
+    "pb_batch_free": (I, [V]),
+    "pb_batch_prefill": (I, [V, V, I, V, V]),
+    "pb_batch_decode": (I, [V, I, V, V]),
 }
 
 _lib = None

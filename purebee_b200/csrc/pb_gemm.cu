@@ -1,7 +1,7 @@
 // pb_gemm.cu - tensor-core Q4_0 x f16 GEMM for the batched configuration.
 //
-// C[M tokens][N rows] = X[M][K] . W[N][K]^T, W a resident Q4_0 matrix in the
-// row layout.  This is the batched prefill / batched decode form of the
+// C[M tokens][N rows] = X[M][K] . W[N][K]^T, W a resident Q4_0 matrix (either
+// device layout; the batched LM head runs it over the tiled table).  This is the batched prefill / batched decode form of the
 // reference's per-row matvec (wasm-q4.js:118-267) and of its prefill matmul
 // (llama-streaming.js:398 -> wasm-simd.js:71-91).  It does not reproduce the
 // reference's f32 operation order: each operand is rounded to f16 once (the
@@ -54,9 +54,10 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor: D f32, A and B f16, both K-major, N = 128, M = 128.
-constexpr uint32_t GM_IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(GM_TOK >> 3) << 17) |
-                              ((uint32_t)(GM_ROWS >> 4) << 24);
+// Instruction descriptor: D f32, A and B f16, both K-major, M = 128, N = tok.
+__host__ __device__ constexpr uint32_t gm_idesc(int tok) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(tok >> 3) << 17) | ((uint32_t)(GM_ROWS >> 4) << 24);
+}
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
@@ -81,12 +82,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(GM_IDESC), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
       : "memory");
 }
 
@@ -114,21 +116,28 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 
 }  // namespace
 
+// TOK tokens per CTA (MMA N = 64 or 128).  grid.z splits K: CTA z covers K
+// steps [z*kper, (z+1)*kper) and, when gridDim.z > 1, writes its partial tile
+// to C + z*M*ldc (a workspace the reduce kernel sums in order of z).
+template <int TOK>
 __global__ void __launch_bounds__(GM_THREADS, 1)
-k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, int N_pad, int nb,
-             const float* __restrict__ X, int ldx, int M, float* __restrict__ C, int ldc, int* err) {
+k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int layout, int N, int N_pad, int nb,
+             const float* __restrict__ X, int ldx, int M, float* __restrict__ C, int ldc, int kper, int* err) {
   extern __shared__ __align__(1024) unsigned char gm_raw[];
   __shared__ uint64_t bars[2];
   __shared__ uint32_t tmem_base;
   // 1024-byte alignment of the swizzled tiles (the swizzle repeats every 1024 bytes)
   unsigned char* ring = gm_raw + ((1024 - (smem_addr(gm_raw) & 1023)) & 1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * GM_ROWS, m0 = blockIdx.y * GM_TOK;
-  const int K = nb * 32, ksteps = (K + GM_KSTEP - 1) / GM_KSTEP;
+  const int n0 = blockIdx.x * GM_ROWS, m0 = blockIdx.y * TOK;
+  const int K = nb * 32, ktot = (K + GM_KSTEP - 1) / GM_KSTEP;
+  const int kbeg = blockIdx.z * kper, kend_ = kbeg + kper < ktot ? kbeg + kper : ktot;
+  const int ksteps = kend_ > kbeg ? kend_ - kbeg : 0;
+  C += (size_t)blockIdx.z * M * ldc;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
-                 "r"(GM_TOK)
+                 "r"(TOK)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -144,18 +153,18 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
 
   bool ok = true;
   for (int ks = 0; ks < ksteps && ok; ++ks) {
-    const int st = ks & 1;
+    const int st = ks & 1, kg = kbeg + ks;  // kg: global K step
     unsigned char* sA = ring + st * GM_STAGE_BYTES;
     unsigned char* sB = sA + GM_TILE_BYTES;
     if (ks >= 2) ok = mbar_wait(&bars[st], ((ks >> 1) - 1) & 1, err);  // MMAs of step ks-2 are done with it
     if (!ok) break;
     // weights: thread -> (row, block) of the two Q4_0 blocks of this step
     {
-      const int r = tid >> 1, blk = tid & 1, b = ks * 2 + blk, row = n0 + r;
+      const int r = tid >> 1, blk = tid & 1, b = kg * 2 + blk, row = n0 + r;
       uint4 pl = make_uint4(0, 0, 0, 0);
       float d = 0.0f;
       if (b < nb && row < N_pad) {
-        const size_t slot = (size_t)row * nb + b;
+        const size_t slot = (size_t)pb_slot(layout, row, b, nb);
         pl = __ldg(reinterpret_cast<const uint4*>(qs) + slot);
         d = pb_f16_exact(__ldg(dsc + slot));
       }
@@ -180,8 +189,8 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
     // activations: thread -> (token, half of the 64-wide step)
     {
       const int r = tid >> 1, hh = tid & 1, m = m0 + r;
-      const int k = ks * GM_KSTEP + hh * 32;
-      const bool live = m < M && k < K;
+      const int k = kg * GM_KSTEP + hh * 32;
+      const bool live = r < TOK && m < M && k < K;
       const float4* xr = reinterpret_cast<const float4*>(X + (size_t)m * ldx + k);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -195,7 +204,7 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
         v.y = pack_h2(a.z, a.w);
         v.z = pack_h2(bq.x, bq.y);
         v.w = pack_h2(bq.z, bq.w);
-        *reinterpret_cast<uint4*>(sB + sw128(r, hh * 4 + c)) = v;
+        if (r < TOK) *reinterpret_cast<uint4*>(sB + sw128(r, hh * 4 + c)) = v;
       }
     }
     // generic-proxy writes -> visible to the tensor core's async proxy
@@ -206,33 +215,36 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
       const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sB));
 #pragma unroll
       for (int kk = 0; kk < GM_KSTEP / 16; ++kk)  // +32 bytes (16 f16) along K per MMA
-        mma_f16(tmem_d, da + 2 * kk, db + 2 * kk, (ks > 0 || kk > 0) ? 1u : 0u);
+        mma_f16(tmem_d, da + 2 * kk, db + 2 * kk, gm_idesc(TOK), (ks > 0 || kk > 0) ? 1u : 0u);
       mma_commit(&bars[st]);
     }
   }
   // the last step's commit covers every MMA issued before it
   if (ok && ksteps > 0) ok = mbar_wait(&bars[(ksteps - 1) & 1], ((ksteps - 1) >> 1) & 1, err);
+  const bool empty_split = ksteps == 0;  // no MMA wrote the accumulator: the partial is zero
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   if (ok && warp < 4) {
     // warp w reads TMEM lanes 32w .. 32w+31 (weight rows), 32 token columns at a time
     const int row = n0 + warp * 32 + lane;
 #pragma unroll 1
-    for (int c0 = 0; c0 < GM_TOK; c0 += 32) {
+    for (int c0 = 0; c0 < TOK; c0 += 32) {
       uint32_t v[32];
       tmem_ld32(tmem_d + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
       if (row < N) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int m = m0 + c0 + j;
-          if (m < M) C[(size_t)m * ldc + row] = __uint_as_float(v[j]);
+          if (m < M) C[(size_t)m * ldc + row] = empty_split ? 0.0f : __uint_as_float(v[j]);
         }
       }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(GM_TOK) : "memory");
+  if (warp == 0) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(TOK) : "memory");
+  }
 }
 
 static size_t gm_smem() { return 2 * GM_STAGE_BYTES + 1024; }
@@ -278,12 +290,13 @@ __device__ __forceinline__ void mma_f16_n256(uint32_t tmem_d, uint64_t adesc, ui
 
 }  // namespace
 
-__global__ void k_dequant_q4_f16(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int64_t nblocks,
-                                 __half* __restrict__ out) {
-  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one block of 32 per thread
+__global__ void k_dequant_q4_f16(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int layout, int nb,
+                                 int64_t nblocks, __half* __restrict__ out) {
+  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // output block (row-major) per thread
   if (b >= nblocks) return;
-  const uint4 pl = __ldg(reinterpret_cast<const uint4*>(qs) + b);
-  const float d = pb_f16_exact(__ldg(dsc + b));
+  const int64_t slot = pb_slot(layout, (int)(b / nb), (int)(b % nb), nb);
+  const uint4 pl = __ldg(reinterpret_cast<const uint4*>(qs) + slot);
+  const float d = pb_f16_exact(__ldg(dsc + slot));
   const uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
   uint32_t lo[8], hi[8];
 #pragma unroll
@@ -428,7 +441,7 @@ static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, int ld
   __half* w16 = reinterpret_cast<__half*>(ctx->gemm_scratch);
   __half* x16 = reinterpret_cast<__half*>(static_cast<char*>(ctx->gemm_scratch) + off_x);
   const int64_t nblk = (int64_t)w->N_pad * w->nb;
-  k_dequant_q4_f16<<<pb_cdiv(nblk, 256), 256, 0, ctx->stream>>>(w->qs, w->d, nblk, w16);
+  k_dequant_q4_f16<<<pb_cdiv(nblk, 256), 256, 0, ctx->stream>>>(w->qs, w->d, w->layout, w->nb, nblk, w16);
   PB_LAUNCHED(ctx, "k_dequant_q4_f16");
   k_f32_to_f16<<<pb_cdiv((int64_t)M * K / 4, 256), 256, 0, ctx->stream>>>(X, M, K, ldx, x16);
   PB_LAUNCHED(ctx, "k_f32_to_f16");
@@ -442,29 +455,69 @@ static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, int ld
   return PB_OK;
 }
 
-int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc) {
+// C[m][n] = sum over z (ascending) of the split-K partials ws[z][m][n].
+__global__ void k_splitk_reduce(const float* __restrict__ ws, int splits, int M, int N, float* __restrict__ C,
+                                int ldc) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
+  if (n >= N) return;
+  float acc = 0.0f;
+  for (int z = 0; z < splits; ++z) acc += ws[((size_t)z * M + m) * N + n];
+  C[(size_t)m * ldc + n] = acc;
+}
+
+int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
+                      size_t ws_bytes) {
   if (!ctx || !w || !X || !C || M <= 0) return PB_ERR_ARG;
-  if (w->type != PB_TYPE_Q4_0 || w->layout != PB_LAYOUT_ROWS)
-    return pb_set_error(ctx, PB_ERR_ARG, "the tensor-core GEMM needs a Q4_0 matrix in the row layout");
+  if (w->type != PB_TYPE_Q4_0) return pb_set_error(ctx, PB_ERR_ARG, "the tensor-core GEMM needs a Q4_0 matrix");
   if ((ldx & 3) || ((uintptr_t)X & 15))
     return pb_set_error(ctx, PB_ERR_ARG, "X must be 16-byte aligned with a row stride that is a multiple of 4");
   if (M >= PB_GEMM_TMA_MIN_M && w->K % TG_K == 0) return launch_gemm_tma(ctx, w, X, ldx, M, C, ldc);
-  dim3 grid(pb_cdiv(w->N, GM_ROWS), pb_cdiv(M, GM_TOK));
+  const int tok = M <= 64 ? 64 : GM_TOK;
+  dim3 grid(pb_cdiv(w->N, GM_ROWS), pb_cdiv(M, tok), 1);
   if (grid.y > 65535) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
-  k_q4_gemm_tc<<<grid, GM_THREADS, gm_smem(), ctx->stream>>>(w->qs, w->d, w->N, w->N_pad, w->nb, X, ldx, M, C, ldc,
-                                                           ctx->d_err);
+  // With a workspace, split K over CTAs until the grid covers the SMs twice;
+  // the partial tiles are summed in split order, so the result does not
+  // depend on scheduling.
+  const int ktot = pb_cdiv(w->K, GM_KSTEP);
+  int splits = 1;
+  if (ws) {
+    const int base = grid.x * grid.y;
+    splits = pb_cdiv(2 * ctx->sm_count, base);
+    const int max_by_k = ktot / 4 > 1 ? ktot / 4 : 1;
+    const int max_by_ws = (int)(ws_bytes / ((size_t)M * w->N * 4));
+    splits = splits < max_by_k ? splits : max_by_k;
+    splits = splits < max_by_ws ? splits : max_by_ws;
+    if (splits < 1) splits = 1;
+  }
+  const int kper = pb_cdiv(ktot, splits);
+  splits = pb_cdiv(ktot, kper);
+  grid.z = splits;
+  float* dst = splits > 1 ? ws : C;
+  const int ldd = splits > 1 ? w->N : ldc;
+  if (tok == 64)
+    k_q4_gemm_tc<64><<<grid, GM_THREADS, gm_smem(), ctx->stream>>>(w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, X,
+                                                                  ldx, M, dst, ldd, kper, ctx->d_err);
+  else
+    k_q4_gemm_tc<128><<<grid, GM_THREADS, gm_smem(), ctx->stream>>>(w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, X,
+                                                                   ldx, M, dst, ldd, kper, ctx->d_err);
   PB_LAUNCHED(ctx, "k_q4_gemm_tc");
+  if (splits > 1) {
+    k_splitk_reduce<<<dim3(pb_cdiv(w->N, 256), M), 256, 0, ctx->stream>>>(ws, splits, M, w->N, C, ldc);
+    PB_LAUNCHED(ctx, "k_splitk_reduce");
+  }
   return PB_OK;
 }
 
 extern "C" int pb_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int M, int ldx, float* c_dev, int ldc) {
   if (!w) return PB_ERR_ARG;
   if (ldx < w->K || ldc < w->N) return pb_set_error(ctx, PB_ERR_ARG, "row strides smaller than the matrix");
-  return pb_launch_q4_gemm(ctx, w, x_dev, ldx, M, c_dev, ldc);
+  return pb_launch_q4_gemm(ctx, w, x_dev, ldx, M, c_dev, ldc, nullptr, 0);
 }
 
 int pb_setup_gemm_kernels(void) {
-  cudaError_t e = cudaFuncSetAttribute(k_q4_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gm_smem());
+  cudaError_t e = cudaFuncSetAttribute(k_q4_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gm_smem());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_q4_gemm_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gm_smem());
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_gemm_f16_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tg_smem());
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;

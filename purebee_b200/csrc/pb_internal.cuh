@@ -227,6 +227,12 @@ struct pb_mv_epi {
   float* h_out = nullptr;
 };
 
+// Per-sequence strides (floats) of batched attention launches: blockIdx.z is
+// the sequence; its query rows, cache and output rows sit these far apart.
+struct pb_seq_geo {
+  int64_t q = 0, kv = 0, out = 0;
+};
+
 int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows,
                      const pb_mv_epi* epi);
 int pb_launch_head(pb_ctx* ctx, const pb_qmat* emb, const float* h, float* logits,

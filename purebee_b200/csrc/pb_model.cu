@@ -19,17 +19,24 @@
 // from pb_ops.cu / pb_q4.cu
 void pb_rope_table(double theta, int hd, int start, int n, double2* out);
 int pb_launch_attn_cached(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
-                          int start_pos, const int* pos_dev, int n_heads, int n_kv, int hd, float* out, int max_len);
+                          int start_pos, const int* pos_dev, int n_heads, int n_kv, int hd, float* out, int max_len,
+                          int nseq, pb_seq_geo geo);
 int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc);
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
-                          int n_heads, int n_kv, int hd, float* out, int max_len, float* scratch);
+                          int n_heads, int n_kv, int hd, float* out, int max_len, float* scratch, int nseq,
+                          pb_seq_geo geo);
+int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
+                      size_t ws_bytes);
+int pb_launch_attn_prefill_f32(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
+                               int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo);
 size_t pb_attn_decode_scratch_floats(int n_heads, int max_len);
 __global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
                           float* __restrict__ out);
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
                           const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
                           const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
-                          float* __restrict__ kc, float* __restrict__ vc, int max_len, int* err);
+                          float* __restrict__ kc, float* __restrict__ vc, int max_len, int rows_per_seq,
+                          int64_t cache_seq_stride, int* err);
 __global__ void k_glu(const float* __restrict__ g, int g_stride, const float* __restrict__ u, int u_stride, int F,
                       int mode, int interleave4, float* __restrict__ out);
 __global__ void k_embed(int type, const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc,
@@ -474,7 +481,7 @@ static int run_layer_decode_q4(pb_model* m, int l) {
   l2_hint(&e, 2, m->w2[l]);
   PB_TRY(pb_launch_matvec(ctx, m->qkv[l], m->x, m->qkvo, 0, dim + 2 * kv, &e));
   PB_TRY(pb_launch_attn_decode(ctx, m->qkvo, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads,
-                               c.head_dim, m->att, c.seq_len, m->att_scratch));
+                               c.head_dim, m->att, c.seq_len, m->att_scratch, 1, pb_seq_geo()));
   // wo with the residual add
   pb_mv_epi r;
   r.kind = PB_EPI_RESIDUAL;
@@ -528,15 +535,16 @@ static int run_layer(pb_model* m, int l, int M, int start_pos, bool dev_pos) {
     int tot = (c.n_heads + c.n_kv_heads) * (c.head_dim / 2) + kv;
     k_rope_kv<<<dim3(pb_cdiv(tot, 128), M), 128, 0, ctx->stream>>>(q, qs_, k, ks_, v, vs_, c.n_heads, c.n_kv_heads,
                                                                    c.head_dim, m->rope_tab, start_pos, pos_dev,
-                                                                   kcache(m, l), vcache(m, l), c.seq_len, ctx->d_err);
+                                                                   kcache(m, l), vcache(m, l), c.seq_len, M, 0,
+                                                                   ctx->d_err);
     PB_LAUNCHED(ctx, "k_rope_kv");
   }
   if (M == 1 && pos_dev && c.n_heads / c.n_kv_heads <= 8 && c.head_dim % 16 == 0)
     PB_TRY(pb_launch_attn_decode(ctx, q, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads, c.head_dim,
-                                 m->att, c.seq_len, m->att_scratch));
+                                 m->att, c.seq_len, m->att_scratch, 1, pb_seq_geo()));
   else
     PB_TRY(pb_launch_attn_cached(ctx, q, qs_, kcache(m, l), vcache(m, l), M, start_pos, pos_dev, c.n_heads,
-                                 c.n_kv_heads, c.head_dim, m->att, c.seq_len));
+                                 c.n_kv_heads, c.head_dim, m->att, c.seq_len, 1, pb_seq_geo()));
   // output projection + residual
   if (c.kind == PB_MODEL_STREAMING_Q4) PB_TRY(pb_launch_prefill_q4(ctx, m->wo[l], m->att, dim, M, m->proj, dim));
   else PB_TRY(launch_q8a(m, l, 4, m->att, M, m->proj));
@@ -761,3 +769,301 @@ extern "C" int64_t pb_model_decode_bytes(const pb_model* m, int pos) {
 }
 
 extern "C" int pb_model_decode_launches(const pb_model* m) { return m ? m->launches_per_step : 0; }
+
+// ===========================================================================
+// batched serving: n_seqs independent sequences over one streaming model's
+// weights.  Every sequence has its own KV cache; all of them advance together
+// (same prompt length, same position).  The projections and the LM head run
+// as tensor-core GEMMs over the token rows of all sequences
+// (pb_launch_q4_gemm: f16 operands, f32 accumulation, so the logits agree with
+// the one-sequence path within a tolerance); RoPE, attention, SwiGLU and the
+// residual adds are launched over all sequences at once.  The reference runs
+// one sequence at a time (llama-streaming.js:738-815); this is the batched
+// configuration's form of it.
+// ===========================================================================
+
+struct pb_batch {
+  pb_model* m = nullptr;
+  int B = 0;
+  int rows_cap = 0;  // activation rows allocated
+  int P = 0;         // prompt length of the current batch
+  float *kc = nullptr, *vc = nullptr;  // [layer][seq][seq_len][kv]
+  float *x = nullptr, *xn = nullptr, *qkvo = nullptr, *att = nullptr, *guo = nullptr, *hb = nullptr,
+        *proj = nullptr;
+  float *xl = nullptr, *logits = nullptr;  // [B][dim], [B][V]
+  int* toks = nullptr;                     // [rows] token ids (prefill)
+  int* next = nullptr;                     // [B] greedy tokens of the last step
+  int* pos_dev = nullptr;                  // position of the tokens the next decode step reads
+  int* hist = nullptr;                     // [seq_len + 1][B] greedy token produced at each position
+  float* att_scratch = nullptr;
+  float* ws = nullptr;  // split-K partial tiles of the decode-step GEMMs
+  size_t ws_bytes = 0;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
+__global__ void k_gather_last(const float* __restrict__ x, int rows_per_seq, int dim, float* __restrict__ out) {
+  const int s = blockIdx.y, d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d < dim) out[(size_t)s * dim + d] = x[((size_t)s * rows_per_seq + rows_per_seq - 1) * dim + d];
+}
+
+// Greedy token of every row (llama-streaming.js:899-909: first strict maximum),
+// recorded at hist[*pos][row].
+__global__ void __launch_bounds__(1024)
+k_argmax_rows(const float* __restrict__ logits, int V, int* __restrict__ next, int* __restrict__ hist,
+              const int* __restrict__ pos_dev, int hist_len) {
+  __shared__ unsigned long long red[32];
+  const int r = blockIdx.x;
+  unsigned long long key = 0ull;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const unsigned long long k = pb_argmax_key(logits[(size_t)r * V + i], i);
+    key = k > key ? k : key;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
+    key = t > key ? t : key;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = key;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long best = 0ull;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+    const int tok = pb_argmax_index(best);
+    next[r] = tok;
+    if (hist && pos_dev) {
+      const int p = *pos_dev;
+      if (p >= 0 && p < hist_len) hist[(size_t)p * gridDim.x + r] = tok;
+    }
+  }
+}
+
+__global__ void k_batch_step_end(int* __restrict__ pos_dev) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *pos_dev += 1;
+}
+
+static void batch_free_graph(pb_batch* b) {
+  if (b->exec) cudaGraphExecDestroy(b->exec);
+  if (b->graph) cudaGraphDestroy(b->graph);
+  b->exec = nullptr;
+  b->graph = nullptr;
+}
+
+static int batch_ensure_rows(pb_batch* b, int rows) {
+  if (rows <= b->rows_cap) return PB_OK;
+  pb_model* m = b->m;
+  pb_ctx* ctx = m->ctx;
+  PB_TRY(pb_wait(ctx));
+  batch_free_graph(b);  // a recorded graph holds the old buffer addresses
+  cudaFree(b->x); cudaFree(b->xn); cudaFree(b->qkvo); cudaFree(b->att); cudaFree(b->guo); cudaFree(b->hb);
+  cudaFree(b->proj); cudaFree(b->toks);
+  b->x = b->xn = b->qkvo = b->att = b->guo = b->hb = b->proj = nullptr;
+  b->toks = nullptr;
+  b->rows_cap = 0;
+  const pb_model_config& c = m->c;
+  const size_t qkvw = (size_t)c.dim + 2 * m->kv_dim;
+  PB_TRY_CUDA(ctx, cudaMalloc(&b->x, (size_t)rows * c.dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&b->xn, (size_t)rows * c.dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&b->qkvo, (size_t)rows * qkvw * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&b->att, (size_t)rows * c.dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&b->guo, (size_t)rows * 2 * c.hidden_dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&b->hb, (size_t)rows * c.hidden_dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&b->proj, (size_t)rows * c.dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&b->toks, (size_t)rows * 4));
+  b->rows_cap = rows;
+  return PB_OK;
+}
+
+extern "C" int pb_batch_free(pb_batch* b) {
+  if (!b) return PB_OK;
+  if (b->m && b->m->ctx) pb_wait(b->m->ctx);
+  batch_free_graph(b);
+  cudaFree(b->kc); cudaFree(b->vc); cudaFree(b->x); cudaFree(b->xn); cudaFree(b->qkvo); cudaFree(b->att);
+  cudaFree(b->guo); cudaFree(b->hb); cudaFree(b->proj); cudaFree(b->xl); cudaFree(b->logits); cudaFree(b->toks);
+  cudaFree(b->next); cudaFree(b->pos_dev); cudaFree(b->hist); cudaFree(b->att_scratch); cudaFree(b->ws);
+  delete b;
+  return PB_OK;
+}
+
+extern "C" int pb_batch_create(pb_model* m, int n_seqs, pb_batch** out) {
+  if (!m || !out || n_seqs <= 0) return PB_ERR_ARG;
+  *out = nullptr;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  // decode steps run the fused-dequant GEMM, which needs no growable scratch
+  // (the recorded decode graph relies on that)
+  if (n_seqs > 256) return pb_set_error(ctx, PB_ERR_ARG, "at most 256 sequences per batch");
+  if (c.kind != PB_MODEL_STREAMING_Q4 || !m->emb || m->emb->type != PB_TYPE_Q4_0)
+    return pb_set_error(ctx, PB_ERR_ARG, "batched serving needs a streaming model with a Q4_0 embedding");
+  if (c.n_heads / c.n_kv_heads > 8 || c.head_dim % 16)
+    return pb_set_error(ctx, PB_ERR_ARG, "batched decode attention needs <= 8 heads per kv head, head_dim %% 16 == 0");
+  pb_batch* b = new pb_batch();
+  b->m = m;
+  b->B = n_seqs;
+  auto fail = [&](int rc) { pb_batch_free(b); return rc; };
+  const size_t kv = (size_t)c.n_layers * n_seqs * c.seq_len * m->kv_dim;
+  const int widest = 2 * c.hidden_dim > c.dim + 2 * m->kv_dim ? 2 * c.hidden_dim : c.dim + 2 * m->kv_dim;
+  b->ws_bytes = (size_t)8 * n_seqs * widest * 4;  // up to 8 K splits of the widest layer matrix
+  cudaError_t e = cudaMalloc(&b->kc, kv * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->vc, kv * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->xl, (size_t)n_seqs * c.dim * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->logits, (size_t)n_seqs * c.vocab * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->next, (size_t)n_seqs * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->pos_dev, 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->hist, (size_t)(c.seq_len + 1) * n_seqs * 4);
+  if (e == cudaSuccess)
+    e = cudaMalloc(&b->att_scratch, (size_t)n_seqs * pb_attn_decode_scratch_floats(c.n_heads, c.seq_len) * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->ws, b->ws_bytes);
+  if (e != cudaSuccess) return fail(pb_cuda_error(ctx, e, "batch allocation"));
+  cudaMemsetAsync(b->kc, 0, kv * 4, ctx->stream);
+  cudaMemsetAsync(b->vc, 0, kv * 4, ctx->stream);
+  cudaMemsetAsync(b->hist, 0, (size_t)(c.seq_len + 1) * n_seqs * 4, ctx->stream);
+  cudaMemsetAsync(b->pos_dev, 0, 4, ctx->stream);
+  *out = b;
+  return PB_OK;
+}
+
+// One layer over `rows` token rows: n_seqs sequences of rows_per_seq rows each,
+// at positions start (or *pos_dev) + row-in-sequence.
+static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start_pos, const int* pos_dev) {
+  pb_model* m = b->m;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  const int dim = c.dim, F = c.hidden_dim, kv = m->kv_dim, qkvw = dim + 2 * kv;
+  const int64_t cache_seq = (int64_t)c.seq_len * kv;
+  float* kc = b->kc + (size_t)l * b->B * cache_seq;
+  float* vc = b->vc + (size_t)l * b->B * cache_seq;
+  PB_TRY(launch_norm(m, b->x, rows, m->rms_att + (size_t)l * dim, b->xn));
+  PB_TRY(pb_launch_q4_gemm(ctx, m->qkv[l], b->xn, dim, rows, b->qkvo, qkvw, b->ws, b->ws_bytes));
+  {
+    const int tot = (c.n_heads + c.n_kv_heads) * (c.head_dim / 2) + kv;
+    k_rope_kv<<<dim3(pb_cdiv(tot, 128), rows), 128, 0, ctx->stream>>>(
+        b->qkvo, qkvw, b->qkvo + dim, qkvw, b->qkvo + dim + kv, qkvw, c.n_heads, c.n_kv_heads, c.head_dim, m->rope_tab,
+        start_pos, pos_dev, kc, vc, c.seq_len, rows_per_seq, cache_seq, ctx->d_err);
+    PB_LAUNCHED(ctx, "k_rope_kv");
+  }
+  pb_seq_geo geo;
+  geo.kv = cache_seq;
+  if (rows_per_seq == 1 && pos_dev) {
+    geo.q = qkvw;
+    geo.out = dim;
+    PB_TRY(pb_launch_attn_decode(ctx, b->qkvo, kc, vc, pos_dev, c.n_heads, c.n_kv_heads, c.head_dim, b->att,
+                                 c.seq_len, b->att_scratch, b->B, geo));
+  } else {
+    geo.q = (int64_t)rows_per_seq * qkvw;
+    geo.out = (int64_t)rows_per_seq * dim;
+    if (c.head_dim == 64 && !pos_dev)
+      PB_TRY(pb_launch_attn_prefill_f32(ctx, b->qkvo, qkvw, kc, vc, rows_per_seq, start_pos, c.n_heads, c.n_kv_heads,
+                                        c.head_dim, b->att, b->B, geo));
+    else
+      PB_TRY(pb_launch_attn_cached(ctx, b->qkvo, qkvw, kc, vc, rows_per_seq, start_pos, pos_dev, c.n_heads,
+                                   c.n_kv_heads, c.head_dim, b->att, c.seq_len, b->B, geo));
+  }
+  PB_TRY(pb_launch_q4_gemm(ctx, m->wo[l], b->att, dim, rows, b->proj, dim, b->ws, b->ws_bytes));
+  k_elementwise<<<pb_cdiv((int64_t)rows * dim, 256), 256, 0, ctx->stream>>>(0, b->x, b->proj, (int64_t)rows * dim, b->x);
+  PB_LAUNCHED(ctx, "k_elementwise");
+  PB_TRY(launch_norm(m, b->x, rows, m->rms_ffn + (size_t)l * dim, b->xn));
+  PB_TRY(pb_launch_q4_gemm(ctx, m->gu[l], b->xn, dim, rows, b->guo, 2 * F, b->ws, b->ws_bytes));
+  // prefill: SILU then ELEMENT_MUL (llama-streaming.js:478-481); decode: fused (:590-595)
+  k_glu<<<dim3(pb_cdiv(F, 256), rows), 256, 0, ctx->stream>>>(b->guo, 2 * F, b->guo, 2 * F, F,
+                                                              rows_per_seq > 1 ? 1 : 0, 1, b->hb);
+  PB_LAUNCHED(ctx, "k_glu");
+  PB_TRY(pb_launch_q4_gemm(ctx, m->w2[l], b->hb, F, rows, b->proj, dim, b->ws, b->ws_bytes));
+  k_elementwise<<<pb_cdiv((int64_t)rows * dim, 256), 256, 0, ctx->stream>>>(0, b->x, b->proj, (int64_t)rows * dim, b->x);
+  PB_LAUNCHED(ctx, "k_elementwise");
+  return PB_OK;
+}
+
+// Final RMSNorm of each sequence's last row, the LM head as one GEMM over the
+// table, the greedy token of every sequence.
+static int batch_head(pb_batch* b, const float* last_rows, const int* pos_dev) {
+  pb_model* m = b->m;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  PB_TRY(launch_norm(m, last_rows, b->B, m->rms_final, b->xn));
+  PB_TRY(pb_launch_q4_gemm(ctx, m->emb, b->xn, c.dim, b->B, b->logits, c.vocab, nullptr, 0));
+  k_argmax_rows<<<b->B, 1024, 0, ctx->stream>>>(b->logits, c.vocab, b->next, b->hist, pos_dev, c.seq_len + 1);
+  PB_LAUNCHED(ctx, "k_argmax_rows");
+  return PB_OK;
+}
+
+extern "C" int pb_batch_prefill(pb_batch* b, const int* tokens_host, int n_prompt, int* next_host,
+                                float* logits_host) {
+  if (!b || !tokens_host || n_prompt <= 0) return PB_ERR_ARG;
+  pb_model* m = b->m;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  if (n_prompt >= c.seq_len) return pb_set_error(ctx, PB_ERR_ARG, "prompt of %d tokens fills the cache", n_prompt);
+  const int rows = b->B * n_prompt;
+  PB_TRY(batch_ensure_rows(b, rows));
+  b->P = n_prompt;
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(b->toks, tokens_host, (size_t)rows * 4, cudaMemcpyHostToDevice, ctx->stream));
+  k_embed<<<dim3(pb_cdiv(c.dim, 256), rows), 256, 0, ctx->stream>>>(PB_TYPE_Q4_0, m->emb->qs, m->emb->d, nullptr,
+                                                                    c.vocab, c.dim, b->toks, nullptr, nullptr, nullptr,
+                                                                    b->x, ctx->d_err);
+  PB_LAUNCHED(ctx, "k_embed");
+  for (int l = 0; l < c.n_layers; ++l) PB_TRY(batch_layer(b, l, rows, n_prompt, 0, nullptr));
+  k_gather_last<<<dim3(pb_cdiv(c.dim, 256), b->B), 256, 0, ctx->stream>>>(b->x, n_prompt, c.dim, b->xl);
+  PB_LAUNCHED(ctx, "k_gather_last");
+  // the greedy token after the prompt is recorded at position n_prompt - 1
+  const int last = n_prompt - 1;
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(b->pos_dev, &last, 4, cudaMemcpyHostToDevice, ctx->stream));
+  PB_TRY(batch_head(b, b->xl, b->pos_dev));
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(b->pos_dev, &n_prompt, 4, cudaMemcpyHostToDevice, ctx->stream));
+  if (next_host)
+    PB_TRY_CUDA(ctx, cudaMemcpyAsync(next_host, b->next, (size_t)b->B * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (logits_host)
+    PB_TRY_CUDA(ctx, cudaMemcpyAsync(logits_host, b->logits, (size_t)b->B * c.vocab * 4, cudaMemcpyDeviceToHost,
+                                     ctx->stream));
+  return pb_wait(ctx);
+}
+
+// One decode step for every sequence: the tokens are the previous greedy
+// tokens (b->next), the position is *pos_dev (advanced at the end).
+static int batch_enqueue_step(pb_batch* b) {
+  pb_model* m = b->m;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  k_embed<<<dim3(pb_cdiv(c.dim, 256), b->B), 256, 0, ctx->stream>>>(PB_TYPE_Q4_0, m->emb->qs, m->emb->d, nullptr,
+                                                                    c.vocab, c.dim, b->next, nullptr, nullptr, nullptr,
+                                                                    b->x, ctx->d_err);
+  PB_LAUNCHED(ctx, "k_embed");
+  for (int l = 0; l < c.n_layers; ++l) PB_TRY(batch_layer(b, l, b->B, 1, 0, b->pos_dev));
+  PB_TRY(batch_head(b, b->x, b->pos_dev));
+  k_batch_step_end<<<1, 32, 0, ctx->stream>>>(b->pos_dev);
+  PB_LAUNCHED(ctx, "k_batch_step_end");
+  return PB_OK;
+}
+
+extern "C" int pb_batch_decode(pb_batch* b, int steps, int* tokens_host, float* logits_host) {
+  if (!b || steps <= 0) return PB_ERR_ARG;
+  pb_model* m = b->m;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  if (b->P <= 0) return pb_set_error(ctx, PB_ERR_STATE, "pb_batch_decode before pb_batch_prefill");
+  int pos = 0;
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(&pos, b->pos_dev, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  PB_TRY(pb_wait(ctx));
+  if (pos + steps > c.seq_len)
+    return pb_set_error(ctx, PB_ERR_ARG, "%d steps from position %d overflow the cache", steps, pos);
+  PB_TRY(batch_ensure_rows(b, b->B));
+  if (!b->exec) {
+    PB_TRY_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = batch_enqueue_step(b);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+    if (rc != PB_OK) { if (g) cudaGraphDestroy(g); return rc; }
+    if (e != cudaSuccess) return pb_cuda_error(ctx, e, "batch decode capture");
+    e = cudaGraphInstantiate(&b->exec, g, 0);
+    if (e != cudaSuccess) { cudaGraphDestroy(g); return pb_cuda_error(ctx, e, "batch decode instantiate"); }
+    b->graph = g;
+  }
+  for (int i = 0; i < steps; ++i) PB_TRY_CUDA(ctx, cudaGraphLaunch(b->exec, ctx->stream));
+  if (tokens_host)
+    PB_TRY_CUDA(ctx, cudaMemcpyAsync(tokens_host, b->hist + (size_t)pos * b->B, (size_t)steps * b->B * 4,
+                                     cudaMemcpyDeviceToHost, ctx->stream));
+  if (logits_host)
+    PB_TRY_CUDA(ctx, cudaMemcpyAsync(logits_host, b->logits, (size_t)b->B * c.vocab * 4, cudaMemcpyDeviceToHost,
+                                     ctx->stream));
+  return pb_wait(ctx);
+}

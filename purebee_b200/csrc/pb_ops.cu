@@ -370,7 +370,7 @@ extern "C" int pb_rope(pb_ctx* ctx, float* q, float* k, int seq, int start_pos, 
 
 __global__ void k_attn_cached(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                               int q_stride, int start_pos, const int* __restrict__ pos_dev, int n_heads, int n_kv,
-                              int hd, double scale, float* __restrict__ out, int max_len, int* err) {
+                              int hd, double scale, float* __restrict__ out, int max_len, pb_seq_geo geo, int* err) {
   extern __shared__ __align__(16) unsigned char sm[];
   __shared__ double red[32];
   __shared__ float fred[32];
@@ -384,6 +384,10 @@ __global__ void k_attn_cached(const float* __restrict__ q, const float* __restri
     return;
   }
   const int kv_dim = n_kv * hd, per = n_heads / n_kv, kh = h / per;
+  q += blockIdx.z * geo.q;  // sequence of a batched launch
+  kc += blockIdx.z * geo.kv;
+  vc += blockIdx.z * geo.kv;
+  out += blockIdx.z * geo.out;
   const float* qh = q + (size_t)t * q_stride + (size_t)h * hd;
   // scores (f32 stores of a double dot)
   for (int j = threadIdx.x; j < cache_len; j += blockDim.x) {
@@ -441,15 +445,160 @@ __global__ void k_attn_cached(const float* __restrict__ q, const float* __restri
   }
 }
 
+// ============================================================================
+// batched prefill attention in f32 (the batched configuration only)
+// ============================================================================
+// CTA = (64 queries, head, sequence).  Q, K and V tiles of 64 rows sit in
+// shared memory; thread (r, cg) owns query rows 4r..4r+3 and key columns (or,
+// for the output, head dims) 4cg..4cg+3.  Online softmax over 64-key tiles:
+// running max and sum per row, rescaled as the max grows; P goes through
+// shared memory for the P.V product.  f32 throughout with expf, so it agrees
+// with the reference's double-precision attention (llama-streaming.js:422-464)
+// within a relative tolerance; the one-sequence path keeps the exact kernel.
+constexpr int FA_Q = 64, FA_KT = 64, FA_HD = 64, FA_THREADS = 256;
+
+__global__ void __launch_bounds__(FA_THREADS)
+k_attn_prefill_f32(const float* __restrict__ q, int q_stride, const float* __restrict__ kc,
+                   const float* __restrict__ vc, int seq, int start_pos, int n_heads, int n_kv, float scale,
+                   float* __restrict__ out, pb_seq_geo geo) {
+  extern __shared__ __align__(16) unsigned char fa_raw[];
+  float(*Qs)[FA_HD + 4] = reinterpret_cast<float(*)[FA_HD + 4]>(fa_raw);
+  float(*Ks)[FA_HD + 4] = Qs + FA_Q;
+  float(*Vs)[FA_HD + 4] = Ks + FA_KT;
+  float(*Ps)[FA_KT + 4] = reinterpret_cast<float(*)[FA_KT + 4]>(Vs + FA_KT);
+  const int tid = threadIdx.x, r = tid >> 4, cg = tid & 15;
+  const int q0 = blockIdx.x * FA_Q, h = blockIdx.y, z = blockIdx.z;
+  const int per = n_heads / n_kv, kh = h / per, kv_dim = n_kv * FA_HD;
+  q += z * geo.q;
+  kc += z * geo.kv;
+  vc += z * geo.kv;
+  out += z * geo.out;
+  for (int i = tid; i < FA_Q * FA_HD / 4; i += FA_THREADS) {
+    const int qr = i / (FA_HD / 4), d4 = i % (FA_HD / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q0 + qr < seq) v = *reinterpret_cast<const float4*>(q + (size_t)(q0 + qr) * q_stride + (size_t)h * FA_HD + 4 * d4);
+    *reinterpret_cast<float4*>(&Qs[qr][4 * d4]) = v;
+  }
+  float m_i[4], l_i[4], o[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m_i[i] = -INFINITY;
+    l_i[i] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[i][j] = 0.0f;
+  }
+  // keys 0 .. start_pos + last query of the tile (causal)
+  const int qlast = (q0 + FA_Q < seq ? q0 + FA_Q : seq) - 1;
+  const int kend = start_pos + qlast + 1;
+  for (int k0 = 0; k0 < kend; k0 += FA_KT) {
+    __syncthreads();
+    for (int i = tid; i < FA_KT * FA_HD / 4; i += FA_THREADS) {
+      const int kr = i / (FA_HD / 4), d4 = i % (FA_HD / 4);
+      float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
+      if (k0 + kr < kend) {
+        kv4 = *reinterpret_cast<const float4*>(kc + (size_t)(k0 + kr) * kv_dim + (size_t)kh * FA_HD + 4 * d4);
+        vv4 = *reinterpret_cast<const float4*>(vc + (size_t)(k0 + kr) * kv_dim + (size_t)kh * FA_HD + 4 * d4);
+      }
+      *reinterpret_cast<float4*>(&Ks[kr][4 * d4]) = kv4;
+      *reinterpret_cast<float4*>(&Vs[kr][4 * d4]) = vv4;
+    }
+    __syncthreads();
+    float sc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
+    for (int d = 0; d < FA_HD; d += 4) {
+      float4 qa[4], kb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) qa[i] = *reinterpret_cast<const float4*>(&Qs[4 * r + i][d]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kb[j] = *reinterpret_cast<const float4*>(&Ks[4 * cg + j][d]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          sc[i][j] = __fmaf_rn(qa[i].w, kb[j].w,
+                               __fmaf_rn(qa[i].z, kb[j].z, __fmaf_rn(qa[i].y, kb[j].y, __fmaf_rn(qa[i].x, kb[j].x, sc[i][j]))));
+    }
+    float mt[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qpos = start_pos + q0 + 4 * r + i;
+      mt[i] = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int kp = k0 + 4 * cg + j;
+        sc[i][j] = (kp <= qpos && kp < kend) ? sc[i][j] * scale : -INFINITY;
+        mt[i] = fmaxf(mt[i], sc[i][j]);
+      }
+#pragma unroll
+      for (int o2 = 8; o2 > 0; o2 >>= 1) mt[i] = fmaxf(mt[i], __shfl_xor_sync(0xffffffffu, mt[i], o2));
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float mn = fmaxf(m_i[i], mt[i]);
+      const float alpha = mn == -INFINITY ? 1.0f : expf(m_i[i] - mn);
+      float ps = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = mn == -INFINITY ? 0.0f : expf(sc[i][j] - mn);
+        Ps[4 * r + i][4 * cg + j] = p;
+        ps += p;
+      }
+#pragma unroll
+      for (int o2 = 8; o2 > 0; o2 >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o2);
+      l_i[i] = l_i[i] * alpha + ps;
+      m_i[i] = mn;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[i][j] *= alpha;
+    }
+    __syncthreads();
+    for (int c = 0; c < FA_KT; ++c) {
+      const float4 vv = *reinterpret_cast<const float4*>(&Vs[c][4 * cg]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float p = Ps[4 * r + i][c];
+        o[i][0] = __fmaf_rn(p, vv.x, o[i][0]);
+        o[i][1] = __fmaf_rn(p, vv.y, o[i][1]);
+        o[i][2] = __fmaf_rn(p, vv.z, o[i][2]);
+        o[i][3] = __fmaf_rn(p, vv.w, o[i][3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qr = q0 + 4 * r + i;
+    if (qr < seq) {
+      const float inv = 1.0f / l_i[i];
+      float* dst = out + (size_t)qr * n_heads * FA_HD + (size_t)h * FA_HD + 4 * cg;
+      *reinterpret_cast<float4*>(dst) = make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+    }
+  }
+}
+
+static size_t fa_smem() { return sizeof(float) * ((FA_Q + 2 * FA_KT) * (FA_HD + 4) + FA_Q * (FA_KT + 4)); }
+
+int pb_launch_attn_prefill_f32(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
+                               int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo) {
+  if (hd != FA_HD || (q_stride & 3)) return PB_ERR_ARG;
+  k_attn_prefill_f32<<<dim3(pb_cdiv(seq, FA_Q), n_heads, nseq), FA_THREADS, fa_smem(), ctx->stream>>>(
+      q, q_stride, kc, vc, seq, start_pos, n_heads, n_kv, (float)(1.0 / sqrt((double)hd)), out, geo);
+  PB_LAUNCHED(ctx, "k_attn_prefill_f32");
+  return PB_OK;
+}
+
 int pb_launch_attn_cached(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
-                          int start_pos, const int* pos_dev, int n_heads, int n_kv, int hd, float* out, int max_len) {
+                          int start_pos, const int* pos_dev, int n_heads, int n_kv, int hd, float* out, int max_len,
+                          int nseq, pb_seq_geo geo) {
   int threads = hd * 4 <= 1024 ? hd * 4 : hd;
   if (threads < 64) threads = 64;
   size_t smem = (size_t)((max_len + 1) & ~1) * 4 + (size_t)(threads / hd + 1) * hd * 8 + 16;
   if (smem > 200 * 1024) return pb_set_error(ctx, PB_ERR_ARG, "cache length %d too long for one CTA", max_len);
   double scale = 1.0 / sqrt((double)hd);
-  k_attn_cached<<<dim3(n_heads, seq), threads, smem, ctx->stream>>>(q, kc, vc, q_stride, start_pos, pos_dev, n_heads,
-                                                                    n_kv, hd, scale, out, max_len, ctx->d_err);
+  k_attn_cached<<<dim3(n_heads, seq, nseq), threads, smem, ctx->stream>>>(q, kc, vc, q_stride, start_pos, pos_dev,
+                                                                          n_heads, n_kv, hd, scale, out, max_len, geo,
+                                                                          ctx->d_err);
   PB_LAUNCHED(ctx, "k_attn_cached");
   return PB_OK;
 }
@@ -460,7 +609,7 @@ extern "C" int pb_attn_cached(pb_ctx* ctx, const float* q, const float* kc, cons
       n_heads % n_kv)
     return PB_ERR_ARG;
   return pb_launch_attn_cached(ctx, q, n_heads * hd, kc, vc, seq, start_pos, nullptr, n_heads, n_kv, hd, out,
-                               start_pos + seq);
+                               start_pos + seq, 1, pb_seq_geo());
 }
 
 // ============================================================================
@@ -473,9 +622,13 @@ extern "C" int pb_attn_cached(pb_ctx* ctx, const float* q, const float* kc, cons
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
                           const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
                           const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
-                          float* __restrict__ kc, float* __restrict__ vc, int max_len, int* err) {
-  int t = blockIdx.y;
-  int pos = (pos_dev ? *pos_dev : start_pos) + t;
+                          float* __restrict__ kc, float* __restrict__ vc, int max_len, int rows_per_seq,
+                          int64_t cache_seq_stride, int* err) {
+  int t = blockIdx.y;  // row; rows of sequence s are s*rows_per_seq .. +rows_per_seq-1
+  const int sq = t / rows_per_seq;
+  kc += sq * cache_seq_stride;
+  vc += sq * cache_seq_stride;
+  int pos = (pos_dev ? *pos_dev : start_pos) + (t - sq * rows_per_seq);
   if (pos < 0 || pos >= max_len) {
     if (threadIdx.x == 0 && blockIdx.x == 0) pb_raise(err, PB_DEVERR_BOUNDS);
     return;
@@ -599,7 +752,7 @@ constexpr int AD_MAX_GROUP = 8;  // query heads per kv head
 __global__ void __launch_bounds__(256)
 k_attn_dec_scores(const float* __restrict__ q, const float* __restrict__ kc, const int* __restrict__ pos_dev,
                   int n_heads, int n_kv, int hd, double scale, float* __restrict__ scores, float* __restrict__ cmax,
-                  int max_len, int* err) {
+                  int max_len, pb_seq_geo geo, int* err) {
   extern __shared__ __align__(16) unsigned char ad_raw[];
   float* sm = reinterpret_cast<float*>(ad_raw);
   __shared__ float sv[AD_MAX_GROUP * AD_CHUNK];
@@ -617,6 +770,10 @@ k_attn_dec_scores(const float* __restrict__ q, const float* __restrict__ kc, con
   const int per = n_heads / n_kv, kv_dim = n_kv * hd, ldk = hd + 4;
   const int nj = cache_len - j0 < AD_CHUNK ? cache_len - j0 : AD_CHUNK;
   const int nchunks = (max_len + AD_CHUNK - 1) / AD_CHUNK;
+  q += blockIdx.z * geo.q;  // sequence of a batched launch
+  kc += blockIdx.z * geo.kv;
+  scores += (size_t)blockIdx.z * n_heads * max_len;
+  cmax += (size_t)blockIdx.z * n_heads * nchunks;
   float* qs = sm;             // [per][hd]
   float* ks = sm + per * hd;  // [AD_CHUNK][hd + 4]
   for (int i = threadIdx.x; i < per * hd / 4; i += blockDim.x) {
@@ -664,7 +821,8 @@ constexpr int AD_SLICE = 16;
 
 __global__ void __launch_bounds__(256)
 k_attn_dec_pv(const float* __restrict__ scores, const float* __restrict__ cmax, const float* __restrict__ vc,
-              const int* __restrict__ pos_dev, int n_heads, int n_kv, int hd, float* __restrict__ out, int max_len) {
+              const int* __restrict__ pos_dev, int n_heads, int n_kv, int hd, float* __restrict__ out, int max_len,
+              pb_seq_geo geo) {
   extern __shared__ __align__(16) unsigned char ad_raw[];
   float* p = reinterpret_cast<float*>(ad_raw);  // [max_len] probabilities
   __shared__ double red[256 / 32];
@@ -679,6 +837,10 @@ k_attn_dec_pv(const float* __restrict__ scores, const float* __restrict__ cmax, 
   const int per = n_heads / n_kv, g = h / per, kv_dim = n_kv * hd;
   const int nchunks = (max_len + AD_CHUNK - 1) / AD_CHUNK;
   const int used = (cache_len + AD_CHUNK - 1) / AD_CHUNK;
+  scores += (size_t)blockIdx.z * n_heads * max_len;  // sequence of a batched launch
+  cmax += (size_t)blockIdx.z * n_heads * nchunks;
+  vc += blockIdx.z * geo.kv;
+  out += blockIdx.z * geo.out;
   if (threadIdx.x == 0) {
     float m = -INFINITY;
     for (int c = 0; c < used; ++c) {
@@ -725,24 +887,26 @@ k_attn_dec_pv(const float* __restrict__ scores, const float* __restrict__ cmax, 
 // Decode attention for one query at *pos_dev over the cache; scratch holds
 // n_heads * max_len scores plus n_heads * ceil(max_len / 64) chunk maxima.
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
-                          int n_heads, int n_kv, int hd, float* out, int max_len, float* scratch) {
+                          int n_heads, int n_kv, int hd, float* out, int max_len, float* scratch, int nseq,
+                          pb_seq_geo geo) {
   const int per = n_heads / n_kv;
   if (per > AD_MAX_GROUP || hd % AD_SLICE || hd % 4)
     return pb_set_error(ctx, PB_ERR_ARG, "decode attention needs <= %d heads per kv head and head_dim %% 16 == 0",
                         AD_MAX_GROUP);
   const int nchunks = (max_len + AD_CHUNK - 1) / AD_CHUNK;
-  float* scores = scratch;
-  float* cmax = scratch + (size_t)n_heads * max_len;
+  float* scores = scratch;                                    // [nseq][n_heads][max_len]
+  float* cmax = scratch + (size_t)nseq * n_heads * max_len;  // [nseq][n_heads][nchunks]
   const double scale = 1.0 / sqrt((double)hd);  // llama-streaming.js:546
   size_t smem1 = (size_t)(per * hd + AD_CHUNK * (hd + 4)) * 4;
-  PB_TRY(pb_launch(ctx, "k_attn_dec_scores", true, k_attn_dec_scores, dim3(n_kv, nchunks), dim3(256), smem1, q, kc,
-                   pos_dev, n_heads, n_kv, hd, scale, scores, cmax, max_len, ctx->d_err));
+  PB_TRY(pb_launch(ctx, "k_attn_dec_scores", true, k_attn_dec_scores, dim3(n_kv, nchunks, nseq), dim3(256), smem1, q,
+                   kc, pos_dev, n_heads, n_kv, hd, scale, scores, cmax, max_len, geo, ctx->d_err));
   size_t smem2 = (size_t)max_len * 4;
-  PB_TRY(pb_launch(ctx, "k_attn_dec_pv", true, k_attn_dec_pv, dim3(n_heads, hd / AD_SLICE), dim3(256), smem2,
-                   (const float*)scores, (const float*)cmax, vc, pos_dev, n_heads, n_kv, hd, out, max_len));
+  PB_TRY(pb_launch(ctx, "k_attn_dec_pv", true, k_attn_dec_pv, dim3(n_heads, hd / AD_SLICE, nseq), dim3(256), smem2,
+                   (const float*)scores, (const float*)cmax, vc, pos_dev, n_heads, n_kv, hd, out, max_len, geo));
   return PB_OK;
 }
 
+// scratch of one sequence; a batched launch of nseq sequences needs nseq times this
 size_t pb_attn_decode_scratch_floats(int n_heads, int max_len) {
   return (size_t)n_heads * max_len + (size_t)n_heads * ((max_len + AD_CHUNK - 1) / AD_CHUNK);
 }
@@ -751,5 +915,7 @@ int pb_setup_ops_kernels(void) {
   cudaError_t e = cudaFuncSetAttribute(k_attn_cached, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_attn_prefill_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fa_smem());
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
 }

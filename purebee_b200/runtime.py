@@ -268,3 +268,50 @@ class LlamaRuntime(_RuntimeBase):
     """llama.js LlamaRuntime over quantize.js Q8 layer weights and an f32
     embedding (the `run.js --q8` path)."""
     KIND = N.MODEL_LLAMA_Q8A
+
+
+class BatchedLlamaRuntime:
+    """n_seqs sequences decoded together over one StreamingLlamaRuntime's
+    weights (the batched configuration).  The projections and the LM head
+    run as tensor-core GEMMs with f16 operands, so logits agree with the
+    one-sequence runtime within a relative tolerance, not bit for bit."""
+
+    def __init__(self, base: StreamingLlamaRuntime, n_seqs: int):
+        self.base = base
+        self.ctx = base.ctx
+        self.n_seqs = n_seqs
+        h = ctypes.c_void_p()
+        self.ctx._check(N.lib().pb_batch_create(base.model.h, n_seqs, ctypes.byref(h)))
+        self.h = h.value
+        self.n_prompt = 0
+
+    def prefill(self, prompts, want_logits: bool = False):
+        """prompts: [n_seqs][n_prompt] token ids -> next greedy token per sequence."""
+        t = np.ascontiguousarray(prompts, np.int32)
+        if t.ndim != 2 or t.shape[0] != self.n_seqs:
+            raise ValueError(f"prompts must be [{self.n_seqs}][n_prompt]")
+        nxt = np.zeros(self.n_seqs, np.int32)
+        lg = np.empty((self.n_seqs, self.base.config.vocabSize), np.float32) if want_logits else None
+        self.ctx._check(N.lib().pb_batch_prefill(self.h, N.ptr(t), t.shape[1], N.ptr(nxt),
+                                                 N.ptr(lg) if lg is not None else None))
+        self.n_prompt = t.shape[1]
+        return (nxt, lg) if want_logits else nxt
+
+    def decode(self, steps: int = 1, want_logits: bool = False):
+        """`steps` greedy steps of every sequence -> tokens [steps][n_seqs]."""
+        toks = np.zeros((steps, self.n_seqs), np.int32)
+        lg = np.empty((self.n_seqs, self.base.config.vocabSize), np.float32) if want_logits else None
+        self.ctx._check(N.lib().pb_batch_decode(self.h, int(steps), N.ptr(toks),
+                                                N.ptr(lg) if lg is not None else None))
+        return (toks, lg) if want_logits else toks
+
+    def free(self):
+        if self.h and self.ctx.h:
+            N.lib().pb_batch_free(self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

@@ -1,0 +1,72 @@
+"""Batched serving (pb_batch_*): every sequence's prefill and decode logits
+match the one-sequence device path (which matches the reference oracle) within
+the f16-GEMM tolerance; greedy tokens follow those logits."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+# f16 operands in every projection: relative to the largest logit of the row
+RTOL_LOGITS = 2e-2
+
+
+def make(native, ctx, seed=5, **kw):
+    from purebee_b200.runtime import LlamaConfig, StreamingLlamaRuntime
+    cfg = dict(dim=128, hiddenDim=256, nLayers=2, nHeads=4, nKvHeads=2, vocabSize=512, seqLen=160, headDim=32,
+               ropeTheta=10000.0)
+    cfg.update(kw)
+    rt = StreamingLlamaRuntime(LlamaConfig(**cfg), ctx=ctx, emb_type=native.TYPE_Q4_0)
+    rt.loadSynthetic(seed, 0.05)
+    return rt
+
+
+def close(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    err = np.max(np.abs(a - b)) / np.max(np.abs(b))
+    return err <= RTOL_LOGITS, err
+
+
+@pytest.mark.parametrize("n_seqs,n_prompt,hd,dim", [(3, 5, 32, 128), (4, 130, 32, 128), (3, 70, 64, 128),
+                                                    (2, 300, 64, 128), (4, 9, 64, 512)])
+def test_batch_matches_single_sequence(native, ctx, n_seqs, n_prompt, hd, dim):
+    """15 / 210 rows run the fused-dequant GEMM, 520 / 600 the TMA one; head_dim 64
+    takes the f32 tiled prefill attention, 32 the per-query kernel; dim 512
+    makes the decode GEMMs split K over CTAs."""
+    from purebee_b200.runtime import BatchedLlamaRuntime
+    rt = make(native, ctx, dim=dim, hiddenDim=2 * dim, headDim=hd, nHeads=dim // hd, nKvHeads=max(1, dim // (2 * hd)),
+              seqLen=400)
+    rng = np.random.default_rng(n_seqs * 100 + n_prompt)
+    prompts = rng.integers(1, 512, (n_seqs, n_prompt)).astype(np.int32)
+    bt = BatchedLlamaRuntime(rt, n_seqs)
+    nxt, lg = bt.prefill(prompts, want_logits=True)
+    for s in range(n_seqs):
+        rt.resetCache()
+        want = rt.forward(prompts[s].tolist(), 0)["logits"]
+        ok, err = close(lg[s], want)
+        assert ok, f"prefill seq {s}: rel err {err:.2e}"
+        assert nxt[s] == int(np.argmax(lg[s]))
+    # teacher-forced decode: the one-sequence path fed the batch's own tokens
+    fed = [nxt.copy()]
+    for step in range(3):
+        toks, lgd = bt.decode(1, want_logits=True)
+        for s in range(n_seqs):
+            rt.resetCache()
+            seq = prompts[s].tolist() + [int(t[s]) for t in fed]
+            want = rt.forward(seq, 0)["logits"]
+            ok, err = close(lgd[s], want)
+            assert ok, f"decode step {step} seq {s}: rel err {err:.2e}"
+            assert toks[0][s] == int(np.argmax(lgd[s]))
+        fed.append(toks[0].copy())
+    bt.free()
+    rt.shutdown()
+
+
+def test_batch_rejects(native, ctx):
+    from purebee_b200.runtime import BatchedLlamaRuntime
+    rt = make(native, ctx)
+    bt = BatchedLlamaRuntime(rt, 2)
+    with pytest.raises(native.PureBeeError):
+        bt.decode(1)  # before prefill
+    with pytest.raises(ValueError):
+        bt.prefill(np.ones((3, 4), np.int32))
+    bt.free()
+    rt.shutdown()

@@ -55,12 +55,31 @@ def test_q4_gemm(native, ctx, oracle, M, N, K):
     assert np.max(np.abs(C[rows] - exact)) <= RTOL_VS_REFERENCE * np.max(np.abs(exact))
 
 
+@pytest.mark.parametrize("M", [8, 600])
+def test_q4_gemm_table_layout(native, ctx, M):
+    """The batched LM head runs the GEMM over the head-table layout: same bits as the row layout."""
+    rng = np.random.default_rng(M)
+    N, K = 1000, 256
+    raw = rand_q4_0(rng, N, K)
+    X = rng.standard_normal((M, K)).astype(f32)
+    L = native.lib()
+    dx = ctx.to_device(X)
+    outs = []
+    for t in (native.TYPE_Q4_0, native.TYPE_Q4_0 | native.QMAT_TABLE):
+        m = native.QMat(ctx, t, raw, N, K)
+        dc = ctx.alloc(M * N * 4)
+        ctx._check(L.pb_q4_gemm(ctx.h, m.h, dx.ptr, M, K, dc.ptr, N))
+        ctx.sync()
+        outs.append(dc.download(count=M * N))
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+
+
 def test_q4_gemm_rejects(native, ctx):
     rng = np.random.default_rng(1)
     raw = rand_q4_0(rng, 64, 64)
     L = native.lib()
-    table = native.QMat(ctx, native.TYPE_Q4_0 | native.QMAT_TABLE, raw, 64, 64)
     dx, dc = ctx.alloc(64 * 64 * 4), ctx.alloc(64 * 64 * 4)
-    assert L.pb_q4_gemm(ctx.h, table.h, dx.ptr, 4, 64, dc.ptr, 64) == native.PB_ERR_ARG
     rows = native.QMat(ctx, native.TYPE_Q4_0, raw, 64, 64)
     assert L.pb_q4_gemm(ctx.h, rows.h, dx.ptr, 4, 63, dc.ptr, 64) == native.PB_ERR_ARG  # ldx < K
+    q8 = native.QMat(ctx, native.TYPE_Q8_0, np.zeros(64 * 2 * 34, np.uint8), 64, 64)
+    assert L.pb_q4_gemm(ctx.h, q8.h, dx.ptr, 4, 64, dc.ptr, 64) == native.PB_ERR_ARG  # Q4_0 only
