@@ -478,6 +478,21 @@ def run_case(args):
     from purebee_b200 import _native as N
     L = N.lib()
     kind, shape = args.case.split(":", 1)
+    if kind == "batched":  # batched:BxP -> one batched prefill of B x P seeded tokens, 3 decode steps
+        from purebee_b200 import _native as N
+        from purebee_b200.runtime import BatchedLlamaRuntime
+        nb_, np_ = (int(v) for v in shape.lower().split("x"))
+        ctx = N.Context(0)
+        rt = build_model(ctx)
+        bt = BatchedLlamaRuntime(rt, nb_)
+        bt.prefill(np.random.default_rng(1).integers(1, CFG["vocab"], (nb_, np_)).astype(np.int32))
+        bt.decode(3)
+        ctx.sync()
+        print(json.dumps({"case": args.case, "ok": True}), flush=True)
+        bt.free()
+        rt.shutdown()
+        ctx.close()
+        return
     mtok = 1
     if kind == "gemm":  # gemm:MxNxK
         mtok, n, k = (int(v) for v in shape.lower().split("x"))
@@ -524,7 +539,7 @@ def main():
     ap.add_argument("--ref-max-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched configuration (configs[4])")
-    ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK, head:VxD or gemm:MxNxK")
+    ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK, head:VxD, gemm:MxNxK, or batched:BxP (batched prefill + 3 steps)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.case:
