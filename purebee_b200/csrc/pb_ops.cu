@@ -780,10 +780,25 @@ k_attn_dec_scores(const float* __restrict__ q, const float* __restrict__ kc, con
     const int hl = (i * 4) / hd, d = (i * 4) % hd;
     reinterpret_cast<float4*>(qs)[i] = *reinterpret_cast<const float4*>(q + (size_t)(g * per + hl) * hd + d);
   }
-  for (int i = threadIdx.x; i < nj * hd / 4; i += blockDim.x) {
-    const int j = (i * 4) / hd, d = (i * 4) % hd;
-    *reinterpret_cast<float4*>(ks + j * ldk + d) =
-        *reinterpret_cast<const float4*>(kc + (size_t)(j0 + j) * kv_dim + (size_t)g * hd + d);
+  // the chunk's K rows: every load of a thread in flight before the stores
+  for (int base = 0; base < nj * hd / 4; base += 8 * 256) {
+    float4 kv4[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + threadIdx.x + u * 256;
+      if (i < nj * hd / 4) {
+        const int j = (i * 4) / hd, d = (i * 4) % hd;
+        kv4[u] = *reinterpret_cast<const float4*>(kc + (size_t)(j0 + j) * kv_dim + (size_t)g * hd + d);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + threadIdx.x + u * 256;
+      if (i < nj * hd / 4) {
+        const int j = (i * 4) / hd, d = (i * 4) % hd;
+        *reinterpret_cast<float4*>(ks + j * ldk + d) = kv4[u];
+      }
+    }
   }
   __syncthreads();
   for (int it = threadIdx.x; it < per * AD_CHUNK; it += blockDim.x) {
@@ -817,7 +832,8 @@ k_attn_dec_scores(const float* __restrict__ q, const float* __restrict__ kc, con
   }
 }
 
-constexpr int AD_SLICE = 16;
+constexpr int AD_SLICE = 16;  // head dims per PV CTA
+constexpr int AD_JG = 64;     // position groups per PV CTA (256 threads = 4 float4 lanes x 64 groups)
 
 __global__ void __launch_bounds__(256)
 k_attn_dec_pv(const float* __restrict__ scores, const float* __restrict__ cmax, const float* __restrict__ vc,
@@ -826,11 +842,11 @@ k_attn_dec_pv(const float* __restrict__ scores, const float* __restrict__ cmax, 
   extern __shared__ __align__(16) unsigned char ad_raw[];
   float* p = reinterpret_cast<float*>(ad_raw);  // [max_len] probabilities
   __shared__ double red[256 / 32];
-  __shared__ double part[16][AD_SLICE];
+  __shared__ double part[AD_JG][AD_SLICE];
   __shared__ float smax;
   pb_pdl_trigger();  // the output projection may start fetching its weights
   pb_pdl_wait();
-  const int h = blockIdx.x, slice = blockIdx.y;
+  const int h = blockIdx.x, slice = blockIdx.y, tid = threadIdx.x;
   const int pos = *pos_dev;
   const int cache_len = pos + 1;
   if (pos < 0 || cache_len > max_len) return;  // k_attn_dec_scores raised the error
@@ -841,46 +857,84 @@ k_attn_dec_pv(const float* __restrict__ scores, const float* __restrict__ cmax, 
   cmax += (size_t)blockIdx.z * n_heads * nchunks;
   vc += blockIdx.z * geo.kv;
   out += blockIdx.z * geo.out;
-  if (threadIdx.x == 0) {
+  if (tid < 32) {  // max over the chunk maxima (`if (scores[j] > maxScore)` from -Infinity)
     float m = -INFINITY;
-    for (int c = 0; c < used; ++c) {
+    for (int c = tid; c < used; c += 32) {
       const float v = cmax[(size_t)h * nchunks + c];
       m = v > m ? v : m;
     }
-    smax = m;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float t = __shfl_xor_sync(0xffffffffu, m, o);
+      m = t > m ? t : m;
+    }
+    if (tid == 0) smax = m;
   }
   __syncthreads();
   const double mx = smax;
   const float* sr = scores + (size_t)h * max_len;
   double s = 0.0;
-  for (int j = threadIdx.x; j < cache_len; j += blockDim.x) {
-    const float e = (float)exp(__dsub_rn((double)sr[j], mx));
-    p[j] = e;
-    s = __dadd_rn(s, (double)e);
+  for (int base = 0; base < cache_len; base += 8 * 256) {
+    float sv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = base + tid + u * 256;
+      sv[u] = j < cache_len ? sr[j] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = base + tid + u * 256;
+      if (j < cache_len) {
+        const float e = (float)exp(__dsub_rn((double)sv[u], mx));
+        p[j] = e;
+        s = __dadd_rn(s, (double)e);
+      }
+    }
   }
   s = pb_block_sum_d(s, red);  // __syncthreads inside: p[] is complete afterwards
-  for (int j = threadIdx.x; j < cache_len; j += blockDim.x) p[j] = (float)__ddiv_rn((double)p[j], s);
+  for (int j = tid; j < cache_len; j += blockDim.x) p[j] = (float)__ddiv_rn((double)p[j], s);
   __syncthreads();
-  // thread (d, jg): positions j = jg, jg + 16, ...
-  const int d = threadIdx.x % AD_SLICE, jg = threadIdx.x / AD_SLICE;
-  const float* vb = vc + (size_t)g * hd + slice * AD_SLICE + d;
-  double acc = 0.0;
-  int j = jg;
-  for (; j + 3 * 16 < cache_len; j += 4 * 16) {
-    const float v0 = vb[(size_t)j * kv_dim], v1 = vb[(size_t)(j + 16) * kv_dim];
-    const float v2 = vb[(size_t)(j + 32) * kv_dim], v3 = vb[(size_t)(j + 48) * kv_dim];
-    acc = __fma_rn((double)p[j], (double)v0, acc);
-    acc = __fma_rn((double)p[j + 16], (double)v1, acc);
-    acc = __fma_rn((double)p[j + 32], (double)v2, acc);
-    acc = __fma_rn((double)p[j + 48], (double)v3, acc);
+  // thread (d4, jg): dims 4*d4 .. 4*d4+3 of the slice, positions j = jg, jg + 64, ...
+  const int d4 = tid & 3, jg = tid >> 2;
+  const float* vb = vc + (size_t)g * hd + slice * AD_SLICE + 4 * d4;
+  double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+  for (int base = jg; base < cache_len; base += 8 * AD_JG) {
+    float4 vv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = base + u * AD_JG;
+      if (j < cache_len) vv[u] = *reinterpret_cast<const float4*>(vb + (size_t)j * kv_dim);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = base + u * AD_JG;
+      if (j < cache_len) {
+        const double pj = (double)p[j];
+        a0 = __fma_rn(pj, (double)vv[u].x, a0);
+        a1 = __fma_rn(pj, (double)vv[u].y, a1);
+        a2 = __fma_rn(pj, (double)vv[u].z, a2);
+        a3 = __fma_rn(pj, (double)vv[u].w, a3);
+      }
+    }
   }
-  for (; j < cache_len; j += 16) acc = __fma_rn((double)p[j], (double)vb[(size_t)j * kv_dim], acc);
-  part[jg][d] = acc;
+  part[jg][4 * d4 + 0] = a0;
+  part[jg][4 * d4 + 1] = a1;
+  part[jg][4 * d4 + 2] = a2;
+  part[jg][4 * d4 + 3] = a3;
   __syncthreads();
-  if (threadIdx.x < AD_SLICE) {
+  // fixed two-level sum over the 64 position groups: 16 sums of 4, then 16
+  {
+    const int d = tid & 15, k = tid >> 4;
+    const double t = __dadd_rn(__dadd_rn(__dadd_rn(part[4 * k][d], part[4 * k + 1][d]), part[4 * k + 2][d]),
+                               part[4 * k + 3][d]);
+    __syncthreads();
+    part[k][d] = t;
+  }
+  __syncthreads();
+  if (tid < AD_SLICE) {
     double t = 0.0;
-    for (int i = 0; i < 16; ++i) t = __dadd_rn(t, part[i][threadIdx.x]);
-    out[(size_t)h * hd + slice * AD_SLICE + threadIdx.x] = (float)t;
+    for (int i = 0; i < AD_JG / 4; ++i) t = __dadd_rn(t, part[i][tid]);
+    out[(size_t)h * hd + slice * AD_SLICE + tid] = (float)t;
   }
 }
 

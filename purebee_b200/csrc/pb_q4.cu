@@ -257,6 +257,59 @@ __device__ __forceinline__ float4 q4_1_row(uint4 pl, float dl, float mn, const f
                      __fadd_rn(__fmul_rn(a23.y, dl), __fmul_rn(sx.w, mn)));
 }
 
+// x, RMS-normalised with the gains w when w is set (engine.js:429-449), into
+// the shared copy whose float4 chunks are swizzled within each 32-value block.
+// Every global load of a thread is issued before any is used: one memory
+// latency for the prologue instead of one per element.  The sum of squares
+// runs per thread over its float4 chunks in order, then through the block's
+// fixed reduction tree, so every CTA forms the same value.  Needs
+// K / 4 <= MV_STAGE_CH * nthreads.
+constexpr int MV_STAGE_CH = 4;
+
+__device__ __forceinline__ void mv_stage_x(const float* __restrict__ x, const float* __restrict__ w, double eps, int K,
+                                           float4* xs4, double* red) {
+  const int tid = threadIdx.x, nt = blockDim.x, nc = K / 4;
+  float4 xv[MV_STAGE_CH], wv[MV_STAGE_CH];
+#pragma unroll
+  for (int i = 0; i < MV_STAGE_CH; ++i) {
+    const int c = tid + i * nt;
+    if (c < nc) {
+      xv[i] = reinterpret_cast<const float4*>(x)[c];
+      if (w) wv[i] = reinterpret_cast<const float4*>(w)[c];
+    }
+  }
+  double rms = 0.0;
+  if (w) {
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < MV_STAGE_CH; ++i) {
+      if (tid + i * nt < nc) {
+        ss = __fma_rn((double)xv[i].x, (double)xv[i].x, ss);
+        ss = __fma_rn((double)xv[i].y, (double)xv[i].y, ss);
+        ss = __fma_rn((double)xv[i].z, (double)xv[i].z, ss);
+        ss = __fma_rn((double)xv[i].w, (double)xv[i].w, ss);
+      }
+    }
+    ss = pb_block_sum_d(ss, red);
+    rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)K), eps));
+  }
+#pragma unroll
+  for (int i = 0; i < MV_STAGE_CH; ++i) {
+    const int c = tid + i * nt;
+    if (c < nc) {
+      float4 v = xv[i];
+      if (w) {
+        v.x = (float)__dmul_rn(__ddiv_rn((double)v.x, rms), (double)wv[i].x);
+        v.y = (float)__dmul_rn(__ddiv_rn((double)v.y, rms), (double)wv[i].y);
+        v.z = (float)__dmul_rn(__ddiv_rn((double)v.z, rms), (double)wv[i].z);
+        v.w = (float)__dmul_rn(__ddiv_rn((double)v.w, rms), (double)wv[i].w);
+      }
+      const int bj = c >> 3, ci = c & 7;
+      xs4[bj * 8 + (ci ^ (bj & 7))] = v;
+    }
+  }
+}
+
 struct MvBuf {
   uint4 q[MV_RPT];
   uint32_t d[MV_RPT];
@@ -380,22 +433,7 @@ k_matvec(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, const
   // x (RMS-normalised when asked: engine.js:429-449 with a fixed reduction
   // tree, identical in every CTA) into shared memory, then the block into
   // registers
-  if (epi.norm_w) {
-    double ss = 0.0;
-    for (int j = tid; j < K; j += NT) ss = __fma_rn((double)x[j], (double)x[j], ss);
-    ss = pb_block_sum_d(ss, red);
-    const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)K), epi.eps));
-    for (int j = tid; j < K; j += NT) {
-      const float v = (float)__dmul_rn(__ddiv_rn((double)x[j], rms), (double)epi.norm_w[j]);
-      const int bj = j >> 5, c = (j >> 2) & 7;
-      reinterpret_cast<float*>(xs4 + bj * 8 + (c ^ (bj & 7)))[j & 3] = v;
-    }
-  } else {
-    for (int c = tid; c < K / 4; c += NT) {
-      const int bj = c >> 3, i = c & 7;
-      xs4[bj * 8 + (i ^ (bj & 7))] = reinterpret_cast<const float4*>(x)[c];
-    }
-  }
+  mv_stage_x(x, epi.norm_w, epi.eps, K, xs4, red);
   __syncthreads();
   if (s >= S) return;  // threads beyond the last slot have no further part
   float xr[32];
@@ -515,22 +553,7 @@ k_matvec_ws(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, co
   pb_pdl_trigger();
   pb_pdl_wait();
 
-  if (epi.norm_w) {
-    double ss = 0.0;
-    for (int j = tid; j < K; j += blockDim.x) ss = __fma_rn((double)x[j], (double)x[j], ss);
-    ss = pb_block_sum_d(ss, red);
-    const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)K), epi.eps));
-    for (int j = tid; j < K; j += blockDim.x) {
-      const float v = (float)__dmul_rn(__ddiv_rn((double)x[j], rms), (double)epi.norm_w[j]);
-      const int bj = j >> 5, c = (j >> 2) & 7;
-      reinterpret_cast<float*>(xs4 + bj * 8 + (c ^ (bj & 7)))[j & 3] = v;
-    }
-  } else {
-    for (int c = tid; c < K / 4; c += blockDim.x) {
-      const int bj = c >> 3, i = c & 7;
-      xs4[bj * 8 + (i ^ (bj & 7))] = reinterpret_cast<const float4*>(x)[c];
-    }
-  }
+  mv_stage_x(x, epi.norm_w, epi.eps, K, xs4, red);
   __syncthreads();
   float* pslot = ps + (size_t)s * 2 * nb * 32;
   const int bar = 1 + 4 * s;  // FULL0, FULL1, EMPTY0, EMPTY1
@@ -694,23 +717,53 @@ extern "C" int pb_q4_1_matvec(pb_ctx* ctx, const float* x, const uint8_t* raw, i
 // ---------------------------------------------------------------------------
 
 constexpr int HD_WARPS = 8;
-constexpr int HD_PF = 4;
+constexpr int HD_PF_Q4 = 8, HD_PF_Q8 = 4;  // blocks of loads in flight per lane
 
 // The hidden vector into shared memory, RMS-normalised with the final norm
-// gains when norm_w is set (engine.js:429-449; the same fixed reduction tree
-// as every other RMSNorm here, so all CTAs get identical values).
+// gains when norm_w is set (engine.js:429-449; a fixed reduction tree, so all
+// CTAs get identical values).  A thread's global loads are all issued before
+// any is used (K <= 16 * blockDim.x).
 __device__ __forceinline__ void load_hidden(const float* __restrict__ h, const float* __restrict__ norm_w, double eps,
                                             int K, float* hs) {
   __shared__ double red[HD_WARPS];
+  const int tid = threadIdx.x, nt = blockDim.x, nc = K / 4;
+  float4 hv[4], wv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = tid + i * nt;
+    if (c < nc) {
+      hv[i] = reinterpret_cast<const float4*>(h)[c];
+      if (norm_w) wv[i] = reinterpret_cast<const float4*>(norm_w)[c];
+    }
+  }
+  double rms = 0.0;
   if (norm_w) {
     double ss = 0.0;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) ss = __fma_rn((double)h[i], (double)h[i], ss);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (tid + i * nt < nc) {
+        ss = __fma_rn((double)hv[i].x, (double)hv[i].x, ss);
+        ss = __fma_rn((double)hv[i].y, (double)hv[i].y, ss);
+        ss = __fma_rn((double)hv[i].z, (double)hv[i].z, ss);
+        ss = __fma_rn((double)hv[i].w, (double)hv[i].w, ss);
+      }
+    }
     ss = pb_block_sum_d(ss, red);
-    const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)K), eps));
-    for (int i = threadIdx.x; i < K; i += blockDim.x)
-      hs[i] = (float)__dmul_rn(__ddiv_rn((double)h[i], rms), (double)norm_w[i]);
-  } else {
-    for (int i = threadIdx.x; i < K; i += blockDim.x) hs[i] = h[i];
+    rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)K), eps));
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = tid + i * nt;
+    if (c < nc) {
+      float4 v = hv[i];
+      if (norm_w) {
+        v.x = (float)__dmul_rn(__ddiv_rn((double)v.x, rms), (double)wv[i].x);
+        v.y = (float)__dmul_rn(__ddiv_rn((double)v.y, rms), (double)wv[i].y);
+        v.z = (float)__dmul_rn(__ddiv_rn((double)v.z, rms), (double)wv[i].z);
+        v.w = (float)__dmul_rn(__ddiv_rn((double)v.w, rms), (double)wv[i].w);
+      }
+      reinterpret_cast<float4*>(hs)[c] = v;
+    }
   }
   __syncthreads();
 }
@@ -740,6 +793,7 @@ k_head(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, 
   const int ntiles = (N + 31) >> 5;
   constexpr int PL = TYPE == PB_TYPE_Q8_0 ? 2 : 1;  // uint4 per block payload
   const uint4* q4 = reinterpret_cast<const uint4*>(qs);
+  constexpr int HD_PF = TYPE == PB_TYPE_Q8_0 ? HD_PF_Q8 : HD_PF_Q4;
   uint4 pq[HD_PF][PL];
   uint16_t pd[HD_PF];
   auto load = [&](int b, int k) {
@@ -916,7 +970,8 @@ int pb_launch_head_norm(pb_ctx* ctx, const pb_qmat* emb, const float* h, const f
   int ntiles = (emb->N + 31) / 32;
   int grid = pb_cdiv(ntiles, HD_WARPS);
   size_t smem = (size_t)emb->K * 4;
-  if (smem > 200 * 1024) return pb_set_error(ctx, PB_ERR_ARG, "head dim %d too large", emb->K);
+  if (emb->K > 16 * HD_WARPS * 32 || (emb->K & 3))
+    return pb_set_error(ctx, PB_ERR_ARG, "head dim %d: at most %d and a multiple of 4", emb->K, 16 * HD_WARPS * 32);
   if (mode == 1) {
     k_head_f32_double<<<grid, HD_WARPS * 32, smem, ctx->stream>>>((const float*)emb->qs, emb->N, emb->K, h, norm_w, eps,
                                                                    logits, amax);
