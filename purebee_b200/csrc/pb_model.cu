@@ -23,13 +23,13 @@ int pb_launch_attn_cached(pb_ctx* ctx, const float* q, int q_stride, const float
                           int nseq, pb_seq_geo geo);
 int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc);
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
-                          int n_heads, int n_kv, int hd, float* out, int max_len, float* scratch, int nseq,
-                          pb_seq_geo geo);
+                          int n_heads, int n_kv, int hd, float* out, int max_len, int nseq, pb_seq_geo geo);
 int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
                       size_t ws_bytes);
 int pb_launch_attn_prefill_f32(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
                                int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo);
-size_t pb_attn_decode_scratch_floats(int n_heads, int max_len);
+bool pb_attn_decode_ok(int n_heads, int n_kv, int hd, int max_len);
+bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len);
 __global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
                           float* __restrict__ out);
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
@@ -64,7 +64,6 @@ struct pb_model {
   float *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr;
   float *kc = nullptr, *vc = nullptr;
   double2* rope_tab = nullptr;
-  float* att_scratch = nullptr;  // decode attention scores and chunk maxima
   // activations (sized for max_m rows)
   int max_m = 0;
   float *x = nullptr, *xn = nullptr, *qkvo = nullptr, *att = nullptr, *guo = nullptr, *hb = nullptr, *proj = nullptr,
@@ -141,7 +140,7 @@ extern "C" int pb_model_free(pb_model* m) {
   for (auto* p : m->q8q) cudaFree(p);
   cudaFree(m->emb_f32);
   cudaFree(m->rms_att); cudaFree(m->rms_ffn); cudaFree(m->rms_final);
-  cudaFree(m->kc); cudaFree(m->vc); cudaFree(m->rope_tab); cudaFree(m->att_scratch);
+  cudaFree(m->kc); cudaFree(m->vc); cudaFree(m->rope_tab);
   cudaFree(m->x); cudaFree(m->xn); cudaFree(m->qkvo); cudaFree(m->att); cudaFree(m->guo); cudaFree(m->hb);
   cudaFree(m->proj); cudaFree(m->logits); cudaFree(m->toks); cudaFree(m->tok_dev); cudaFree(m->hist);
   cudaFree(m->key);
@@ -214,8 +213,7 @@ extern "C" int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model
       cudaMalloc(&m->kc, kv_floats(m) * 4) || cudaMalloc(&m->vc, kv_floats(m) * 4) ||
       cudaMalloc(&m->logits, (size_t)c.vocab * 4) || cudaMalloc(&m->tok_dev, 16) ||
       cudaMalloc(&m->hist, (size_t)(c.seq_len + 1) * 4) || cudaMalloc(&m->key, 16) ||
-      cudaMalloc(&m->rope_tab, (size_t)c.seq_len * (c.head_dim / 2) * sizeof(double2)) ||
-      cudaMalloc(&m->att_scratch, pb_attn_decode_scratch_floats(c.n_heads, c.seq_len) * 4))
+      cudaMalloc(&m->rope_tab, (size_t)c.seq_len * (c.head_dim / 2) * sizeof(double2)))
     return fail(pb_set_error(ctx, PB_ERR_OOM, "model buffers"));
   k_fill<<<pb_cdiv(nd, 256), 256, 0, ctx->stream>>>(m->rms_att, nd, 1.0f);
   k_fill<<<pb_cdiv(nd, 256), 256, 0, ctx->stream>>>(m->rms_ffn, nd, 1.0f);
@@ -481,7 +479,7 @@ static int run_layer_decode_q4(pb_model* m, int l) {
   l2_hint(&e, 2, m->w2[l]);
   PB_TRY(pb_launch_matvec(ctx, m->qkv[l], m->x, m->qkvo, 0, dim + 2 * kv, &e));
   PB_TRY(pb_launch_attn_decode(ctx, m->qkvo, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads,
-                               c.head_dim, m->att, c.seq_len, m->att_scratch, 1, pb_seq_geo()));
+                               c.head_dim, m->att, c.seq_len, 1, pb_seq_geo()));
   // wo with the residual add
   pb_mv_epi r;
   r.kind = PB_EPI_RESIDUAL;
@@ -539,9 +537,9 @@ static int run_layer(pb_model* m, int l, int M, int start_pos, bool dev_pos) {
                                                                    ctx->d_err);
     PB_LAUNCHED(ctx, "k_rope_kv");
   }
-  if (M == 1 && pos_dev && c.n_heads / c.n_kv_heads <= 8 && c.head_dim % 16 == 0)
+  if (M == 1 && pos_dev && pb_attn_decode_ok(c.n_heads, c.n_kv_heads, c.head_dim, c.seq_len))
     PB_TRY(pb_launch_attn_decode(ctx, q, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads, c.head_dim,
-                                 m->att, c.seq_len, m->att_scratch, 1, pb_seq_geo()));
+                                 m->att, c.seq_len, 1, pb_seq_geo()));
   else
     PB_TRY(pb_launch_attn_cached(ctx, q, qs_, kcache(m, l), vcache(m, l), M, start_pos, pos_dev, c.n_heads,
                                  c.n_kv_heads, c.head_dim, m->att, c.seq_len, 1, pb_seq_geo()));
@@ -795,7 +793,6 @@ struct pb_batch {
   int* next = nullptr;                     // [B] greedy tokens of the last step
   int* pos_dev = nullptr;                  // position of the tokens the next decode step reads
   int* hist = nullptr;                     // [seq_len + 1][B] greedy token produced at each position
-  float* att_scratch = nullptr;
   float* ws = nullptr;  // split-K partial tiles of the decode-step GEMMs
   size_t ws_bytes = 0;
   cudaGraph_t graph = nullptr;
@@ -880,7 +877,7 @@ extern "C" int pb_batch_free(pb_batch* b) {
   batch_free_graph(b);
   cudaFree(b->kc); cudaFree(b->vc); cudaFree(b->x); cudaFree(b->xn); cudaFree(b->qkvo); cudaFree(b->att);
   cudaFree(b->guo); cudaFree(b->hb); cudaFree(b->proj); cudaFree(b->xl); cudaFree(b->logits); cudaFree(b->toks);
-  cudaFree(b->next); cudaFree(b->pos_dev); cudaFree(b->hist); cudaFree(b->att_scratch); cudaFree(b->ws);
+  cudaFree(b->next); cudaFree(b->pos_dev); cudaFree(b->hist); cudaFree(b->ws);
   delete b;
   return PB_OK;
 }
@@ -895,8 +892,9 @@ extern "C" int pb_batch_create(pb_model* m, int n_seqs, pb_batch** out) {
   if (n_seqs > 256) return pb_set_error(ctx, PB_ERR_ARG, "at most 256 sequences per batch");
   if (c.kind != PB_MODEL_STREAMING_Q4 || !m->emb || m->emb->type != PB_TYPE_Q4_0)
     return pb_set_error(ctx, PB_ERR_ARG, "batched serving needs a streaming model with a Q4_0 embedding");
-  if (c.n_heads / c.n_kv_heads > 8 || c.head_dim % 16)
-    return pb_set_error(ctx, PB_ERR_ARG, "batched decode attention needs <= 8 heads per kv head, head_dim %% 16 == 0");
+  if (!pb_attn_decode_group_ok(c.n_heads, c.n_kv_heads, c.head_dim, c.seq_len))
+    return pb_set_error(ctx, PB_ERR_ARG, "batched decode attention needs <= 8 query heads per kv head, head_dim %% 4 "
+                                         "== 0, head_dim <= 256 and the scores of a kv head in shared memory");
   pb_batch* b = new pb_batch();
   b->m = m;
   b->B = n_seqs;
@@ -911,8 +909,6 @@ extern "C" int pb_batch_create(pb_model* m, int n_seqs, pb_batch** out) {
   if (e == cudaSuccess) e = cudaMalloc(&b->next, (size_t)n_seqs * 4);
   if (e == cudaSuccess) e = cudaMalloc(&b->pos_dev, 4);
   if (e == cudaSuccess) e = cudaMalloc(&b->hist, (size_t)(c.seq_len + 1) * n_seqs * 4);
-  if (e == cudaSuccess)
-    e = cudaMalloc(&b->att_scratch, (size_t)n_seqs * pb_attn_decode_scratch_floats(c.n_heads, c.seq_len) * 4);
   if (e == cudaSuccess) e = cudaMalloc(&b->ws, b->ws_bytes);
   if (e != cudaSuccess) return fail(pb_cuda_error(ctx, e, "batch allocation"));
   cudaMemsetAsync(b->kc, 0, kv * 4, ctx->stream);
@@ -948,7 +944,7 @@ static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start
     geo.q = qkvw;
     geo.out = dim;
     PB_TRY(pb_launch_attn_decode(ctx, b->qkvo, kc, vc, pos_dev, c.n_heads, c.n_kv_heads, c.head_dim, b->att,
-                                 c.seq_len, b->att_scratch, b->B, geo));
+                                 c.seq_len, b->B, geo));
   } else {
     geo.q = (int64_t)rows_per_seq * qkvw;
     geo.out = (int64_t)rows_per_seq * dim;

@@ -733,242 +733,367 @@ __global__ void k_step_end(unsigned long long* __restrict__ key, int* __restrict
 
 
 // ============================================================================
-// decode attention (one query, llama-streaming.js:543-573) in two kernels
+// decode attention (one query, llama-streaming.js:543-573) in one kernel
 // ============================================================================
-// 1. k_attn_dec_scores: CTA (kv head g, chunk of 64 positions).  The chunk's K
-//    rows go to shared memory (coalesced float4 loads, rows padded by 4 floats
-//    so per-position reads are conflict-free); each thread computes one
-//    (query head of the group, position) score in the reference's order:
-//    double dot, d ascending, then f32(dot * scale).  Scores and the chunk's
-//    maximum per head go to global scratch.
-// 2. k_attn_dec_pv: CTA (head h, 16-wide slice of head_dim).  Global max over
-//    the chunk maxima, e_j = f32(exp(s_j - max)), the double sum of e_j (same
-//    tree in every CTA of the head), p_j = f32(e_j / sum), then
-//    out[d] = f32(sum_j p_j * V[j, d]) in double for the slice.
+// k_attn_dec: CTA (query head h, sequence z), AF_THREADS threads.
+//   1. scores: thread per position j (j = tid, tid + AF_THREADS, ...): the K
+//      row's float4 loads all in flight, then the reference's order: double
+//      dot, d ascending, then f32(dot * scale);
+//   2. max over the f32 scores (`if (scores[j] > maxScore)` from -Infinity:
+//      NaN never wins, so a tree of the same comparison gives the same value);
+//   3. e_j = f32(exp(s_j - max)), the double sum of e_j (per-thread running
+//      sums, then a fixed block tree), p_j = f32(e_j / sum);
+//   4. out[d] = f32(sum_j p_j * V[j, d]) in double: thread (float4 lane d4,
+//      position group jg), V rows prefetched into L2 while the scores run,
+//      then the groups summed in a fixed two-level order.
+// The four query heads of a kv head read the same K and V rows; L2 serves the
+// repeats.  Scores and probabilities stay in shared memory: no scratch.
 
-constexpr int AD_CHUNK = 64;
-constexpr int AD_MAX_GROUP = 8;  // query heads per kv head
+constexpr int AF_THREADS = 512;
+constexpr int AF_MAX_HD = 256;
+// PV partials [groups][hd] (groups * hd <= 4 * AF_THREADS) and their first-level
+// sums [ceil(groups / 4)][hd] (<= AF_THREADS + AF_MAX_HD), in doubles
+constexpr int AF_PART = AF_THREADS * 5 + AF_MAX_HD;
 
-__global__ void __launch_bounds__(256)
-k_attn_dec_scores(const float* __restrict__ q, const float* __restrict__ kc, const int* __restrict__ pos_dev,
-                  int n_heads, int n_kv, int hd, double scale, float* __restrict__ scores, float* __restrict__ cmax,
-                  int max_len, pb_seq_geo geo, int* err) {
-  extern __shared__ __align__(16) unsigned char ad_raw[];
-  float* sm = reinterpret_cast<float*>(ad_raw);
-  __shared__ float sv[AD_MAX_GROUP * AD_CHUNK];
-  pb_pdl_trigger();
-  pb_pdl_wait();  // q and the new cache row come from the projection matvec
-  const int g = blockIdx.x, chunk = blockIdx.y;
+__global__ void __launch_bounds__(AF_THREADS, 1)
+k_attn_dec(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+           const int* __restrict__ pos_dev, int n_heads, int n_kv, int hd, double scale, float* __restrict__ out,
+           int max_len, pb_seq_geo geo, int* err) {
+  extern __shared__ __align__(16) unsigned char af_raw[];
+  double* part = reinterpret_cast<double*>(af_raw);     // [AF_PART] PV partials and their sums
+  float* sp = reinterpret_cast<float*>(part + AF_PART);  // [max_len] scores, then probabilities
+  __shared__ __align__(16) float qs[AF_MAX_HD];
+  __shared__ double red[AF_THREADS / 32];
+  __shared__ float wmax[AF_THREADS / 32];
+  pb_pdl_trigger();  // the output projection may start fetching its weights
+  pb_pdl_wait();     // q and the new cache row come from the projection matvec
+  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int pos = *pos_dev;
   const int cache_len = pos + 1;
   if (pos < 0 || cache_len > max_len) {
-    if (threadIdx.x == 0 && g == 0 && chunk == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+    if (tid == 0 && h == 0 && blockIdx.y == 0) pb_raise(err, PB_DEVERR_BOUNDS);
     return;
   }
-  const int j0 = chunk * AD_CHUNK;
-  if (j0 >= cache_len) return;
-  const int per = n_heads / n_kv, kv_dim = n_kv * hd, ldk = hd + 4;
-  const int nj = cache_len - j0 < AD_CHUNK ? cache_len - j0 : AD_CHUNK;
-  const int nchunks = (max_len + AD_CHUNK - 1) / AD_CHUNK;
-  q += blockIdx.z * geo.q;  // sequence of a batched launch
-  kc += blockIdx.z * geo.kv;
-  scores += (size_t)blockIdx.z * n_heads * max_len;
-  cmax += (size_t)blockIdx.z * n_heads * nchunks;
-  float* qs = sm;             // [per][hd]
-  float* ks = sm + per * hd;  // [AD_CHUNK][hd + 4]
-  for (int i = threadIdx.x; i < per * hd / 4; i += blockDim.x) {
-    const int hl = (i * 4) / hd, d = (i * 4) % hd;
-    reinterpret_cast<float4*>(qs)[i] = *reinterpret_cast<const float4*>(q + (size_t)(g * per + hl) * hd + d);
+  const int per = n_heads / n_kv, g = h / per, kv_dim = n_kv * hd, h4 = hd / 4;
+  q += blockIdx.y * geo.q;  // sequence of a batched launch
+  kc += blockIdx.y * geo.kv;
+  vc += blockIdx.y * geo.kv;
+  out += blockIdx.y * geo.out;
+  const float* vb = vc + (size_t)g * hd;
+  for (int j = tid; j < cache_len; j += AF_THREADS) pb_l2_prefetch(vb + (size_t)j * kv_dim, (uint32_t)hd * 4);
+  if (tid < h4) reinterpret_cast<float4*>(qs)[tid] = reinterpret_cast<const float4*>(q + (size_t)h * hd)[tid];
+  __syncthreads();
+
+  float m = -INFINITY;
+  for (int j = tid; j < cache_len; j += AF_THREADS) {
+    const float4* kr = reinterpret_cast<const float4*>(kc + (size_t)j * kv_dim + (size_t)g * hd);
+    double dot = 0.0;
+    for (int c0 = 0; c0 < h4; c0 += 16) {
+      float4 k4[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+        if (c0 + u < h4) k4[u] = kr[c0 + u];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        if (c0 + u < h4) {
+          const float4 a = reinterpret_cast<const float4*>(qs)[c0 + u];
+          dot = __fma_rn((double)a.x, (double)k4[u].x, dot);  // exact product: one rounding per term
+          dot = __fma_rn((double)a.y, (double)k4[u].y, dot);
+          dot = __fma_rn((double)a.z, (double)k4[u].z, dot);
+          dot = __fma_rn((double)a.w, (double)k4[u].w, dot);
+        }
+      }
+    }
+    const float s = (float)__dmul_rn(dot, scale);
+    sp[j] = s;
+    m = s > m ? s : m;
   }
-  // the chunk's K rows: every load of a thread in flight before the stores
-  for (int base = 0; base < nj * hd / 4; base += 8 * 256) {
-    float4 kv4[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = base + threadIdx.x + u * 256;
-      if (i < nj * hd / 4) {
-        const int j = (i * 4) / hd, d = (i * 4) % hd;
-        kv4[u] = *reinterpret_cast<const float4*>(kc + (size_t)(j0 + j) * kv_dim + (size_t)g * hd + d);
+  for (int o = 16; o > 0; o >>= 1) {
+    const float t = __shfl_xor_sync(0xffffffffu, m, o);
+    m = t > m ? t : m;
+  }
+  if (lane == 0) wmax[warp] = m;
+  __syncthreads();
+  m = wmax[0];
+  for (int w = 1; w < AF_THREADS / 32; ++w) m = wmax[w] > m ? wmax[w] : m;
+  const double mx = m;
+
+  double s = 0.0;
+  for (int j = tid; j < cache_len; j += AF_THREADS) {
+    const float e = (float)exp(__dsub_rn((double)sp[j], mx));
+    sp[j] = e;
+    s = __dadd_rn(s, (double)e);
+  }
+  s = pb_block_sum_d(s, red);
+  for (int j = tid; j < cache_len; j += AF_THREADS) sp[j] = (float)__ddiv_rn((double)sp[j], s);
+  __syncthreads();
+
+  const int jgroups = AF_THREADS / h4, d4 = tid % h4, jg = tid / h4;
+  double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+  if (jg < jgroups) {
+    const float* vl = vb + 4 * d4;
+    for (int base = jg; base < cache_len; base += 8 * jgroups) {
+      float4 vv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = base + u * jgroups;
+        if (j < cache_len) vv[u] = *reinterpret_cast<const float4*>(vl + (size_t)j * kv_dim);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = base + u * jgroups;
+        if (j < cache_len) {
+          const double pj = (double)sp[j];
+          a0 = __fma_rn(pj, (double)vv[u].x, a0);
+          a1 = __fma_rn(pj, (double)vv[u].y, a1);
+          a2 = __fma_rn(pj, (double)vv[u].z, a2);
+          a3 = __fma_rn(pj, (double)vv[u].w, a3);
+        }
       }
     }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = base + threadIdx.x + u * 256;
-      if (i < nj * hd / 4) {
-        const int j = (i * 4) / hd, d = (i * 4) % hd;
-        *reinterpret_cast<float4*>(ks + j * ldk + d) = kv4[u];
-      }
-    }
+    double* pr = part + (size_t)jg * hd + 4 * d4;  // part[jg][d]
+    pr[0] = a0;
+    pr[1] = a1;
+    pr[2] = a2;
+    pr[3] = a3;
   }
   __syncthreads();
-  for (int it = threadIdx.x; it < per * AD_CHUNK; it += blockDim.x) {
-    const int j = it % AD_CHUNK, hl = it / AD_CHUNK;
-    float v = -INFINITY;
-    if (j < nj) {
-      const float* qr = qs + hl * hd;
-      const float* kr = ks + j * ldk;
-      double dot = 0.0;
-      for (int d = 0; d < hd; d += 4) {
-        const float4 a = *reinterpret_cast<const float4*>(qr + d);
-        const float4 b = *reinterpret_cast<const float4*>(kr + d);
-        dot = __fma_rn((double)a.x, (double)b.x, dot);  // exact product: one rounding per term
-        dot = __fma_rn((double)a.y, (double)b.y, dot);
-        dot = __fma_rn((double)a.z, (double)b.z, dot);
-        dot = __fma_rn((double)a.w, (double)b.w, dot);
-      }
-      v = (float)__dmul_rn(dot, scale);
-      scores[(size_t)(g * per + hl) * max_len + j0 + j] = v;
-    }
-    sv[it] = v;
+  // fixed two-level sum over the position groups: sums of 4 consecutive groups, then those in order
+  const int n1 = (jgroups + 3) / 4;
+  double* lvl = part + (size_t)jgroups * hd;  // [n1][hd], past the partials
+  for (int idx = tid; idx < hd * n1; idx += AF_THREADS) {
+    const int d = idx % hd, k = idx / hd;
+    double t = part[(size_t)(4 * k) * hd + d];
+    for (int i = 4 * k + 1; i < 4 * k + 4 && i < jgroups; ++i) t = __dadd_rn(t, part[(size_t)i * hd + d]);
+    lvl[idx] = t;
   }
   __syncthreads();
-  if (threadIdx.x < per) {  // `if (scores[j] > maxScore)` from -Infinity (NaN never wins)
-    float m = -INFINITY;
-    for (int j = 0; j < nj; ++j) {
-      const float v = sv[threadIdx.x * AD_CHUNK + j];
-      m = v > m ? v : m;
-    }
-    cmax[(size_t)(g * per + threadIdx.x) * nchunks + chunk] = m;
+  if (tid < hd) {
+    double o = 0.0;
+    for (int k = 0; k < n1; ++k) o = __dadd_rn(o, lvl[(size_t)k * hd + tid]);
+    out[(size_t)h * hd + tid] = (float)o;
   }
 }
 
-constexpr int AD_SLICE = 16;  // head dims per PV CTA
-constexpr int AD_JG = 64;     // position groups per PV CTA (256 threads = 4 float4 lanes x 64 groups)
+// k_attn_dec_group: the batched form (configs with many sequences), in f32 like
+// the batched prefill attention.  CTA (kv head g, sequence z), AG_THREADS
+// threads, all `per` query heads of the group at once so each K and V row is
+// read once per CTA:
+//   1. scores: thread per position, f32 dots (d ascending) for every head;
+//   2. per-head max and f32 sum of e_j = exp(s_j - max) (warp then block tree),
+//      p_j = e_j / sum;
+//   3. out[h][d] = sum_j p_j[h] * V[j, d]: thread (float4 lane d4, position
+//      group jg) for every head, the groups summed in order.
+constexpr int AG_THREADS = 256;
+constexpr int AD_MAX_GROUP = 8;  // query heads per kv head
 
-__global__ void __launch_bounds__(256)
-k_attn_dec_pv(const float* __restrict__ scores, const float* __restrict__ cmax, const float* __restrict__ vc,
-              const int* __restrict__ pos_dev, int n_heads, int n_kv, int hd, float* __restrict__ out, int max_len,
-              pb_seq_geo geo) {
-  extern __shared__ __align__(16) unsigned char ad_raw[];
-  float* p = reinterpret_cast<float*>(ad_raw);  // [max_len] probabilities
-  __shared__ double red[256 / 32];
-  __shared__ double part[AD_JG][AD_SLICE];
-  __shared__ float smax;
-  pb_pdl_trigger();  // the output projection may start fetching its weights
+__global__ void __launch_bounds__(AG_THREADS)
+k_attn_dec_group(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                 const int* __restrict__ pos_dev, int n_heads, int n_kv, int hd, float scale, float* __restrict__ out,
+                 int max_len, pb_seq_geo geo, int* err) {
+  extern __shared__ __align__(16) unsigned char ag_raw[];
+  const int per = n_heads / n_kv, h4 = hd / 4;
+  float* qs = reinterpret_cast<float*>(ag_raw);  // [per][hd]
+  float* sp = qs + per * hd;                      // [per][max_len] scores, then probabilities
+  float* part = sp + (size_t)per * max_len;       // [jgroups][per][hd]
+  __shared__ float wred[AD_MAX_GROUP][AG_THREADS / 32];
+  __shared__ float hstat[AD_MAX_GROUP];
+  pb_pdl_trigger();
   pb_pdl_wait();
-  const int h = blockIdx.x, slice = blockIdx.y, tid = threadIdx.x;
+  const int g = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int pos = *pos_dev;
   const int cache_len = pos + 1;
-  if (pos < 0 || cache_len > max_len) return;  // k_attn_dec_scores raised the error
-  const int per = n_heads / n_kv, g = h / per, kv_dim = n_kv * hd;
-  const int nchunks = (max_len + AD_CHUNK - 1) / AD_CHUNK;
-  const int used = (cache_len + AD_CHUNK - 1) / AD_CHUNK;
-  scores += (size_t)blockIdx.z * n_heads * max_len;  // sequence of a batched launch
-  cmax += (size_t)blockIdx.z * n_heads * nchunks;
-  vc += blockIdx.z * geo.kv;
-  out += blockIdx.z * geo.out;
-  if (tid < 32) {  // max over the chunk maxima (`if (scores[j] > maxScore)` from -Infinity)
-    float m = -INFINITY;
-    for (int c = tid; c < used; c += 32) {
-      const float v = cmax[(size_t)h * nchunks + c];
-      m = v > m ? v : m;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float t = __shfl_xor_sync(0xffffffffu, m, o);
-      m = t > m ? t : m;
-    }
-    if (tid == 0) smax = m;
+  if (pos < 0 || cache_len > max_len) {
+    if (tid == 0 && g == 0 && blockIdx.y == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+    return;
   }
+  const int kv_dim = n_kv * hd;
+  q += blockIdx.y * geo.q + (size_t)g * per * hd;
+  kc += blockIdx.y * geo.kv + (size_t)g * hd;
+  vc += blockIdx.y * geo.kv + (size_t)g * hd;
+  out += blockIdx.y * geo.out + (size_t)g * per * hd;
+  for (int j = tid; j < cache_len; j += AG_THREADS) pb_l2_prefetch(vc + (size_t)j * kv_dim, (uint32_t)hd * 4);
+  for (int i = tid; i < per * h4; i += AG_THREADS)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q)[i];
   __syncthreads();
-  const double mx = smax;
-  const float* sr = scores + (size_t)h * max_len;
-  double s = 0.0;
-  for (int base = 0; base < cache_len; base += 8 * 256) {
-    float sv[8];
+
+  float mloc[AD_MAX_GROUP];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int j = base + tid + u * 256;
-      sv[u] = j < cache_len ? sr[j] : 0.0f;
+  for (int hl = 0; hl < AD_MAX_GROUP; ++hl) mloc[hl] = -INFINITY;
+  for (int j = tid; j < cache_len; j += AG_THREADS) {
+    const float4* kr = reinterpret_cast<const float4*>(kc + (size_t)j * kv_dim);
+    float dot[AD_MAX_GROUP];
+#pragma unroll
+    for (int hl = 0; hl < AD_MAX_GROUP; ++hl) dot[hl] = 0.0f;
+    for (int c0 = 0; c0 < h4; c0 += 8) {
+      float4 k4[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (c0 + u < h4) k4[u] = kr[c0 + u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (c0 + u < h4) {
+#pragma unroll
+          for (int hl = 0; hl < AD_MAX_GROUP; ++hl) {
+            if (hl < per) {
+              const float4 a = reinterpret_cast<const float4*>(qs + hl * hd)[c0 + u];
+              dot[hl] = __fmaf_rn(a.x, k4[u].x, dot[hl]);
+              dot[hl] = __fmaf_rn(a.y, k4[u].y, dot[hl]);
+              dot[hl] = __fmaf_rn(a.z, k4[u].z, dot[hl]);
+              dot[hl] = __fmaf_rn(a.w, k4[u].w, dot[hl]);
+            }
+          }
+        }
+      }
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int j = base + tid + u * 256;
-      if (j < cache_len) {
-        const float e = (float)exp(__dsub_rn((double)sv[u], mx));
-        p[j] = e;
-        s = __dadd_rn(s, (double)e);
+    for (int hl = 0; hl < AD_MAX_GROUP; ++hl) {
+      if (hl < per) {
+        const float sv = __fmul_rn(dot[hl], scale);
+        sp[(size_t)hl * max_len + j] = sv;
+        mloc[hl] = sv > mloc[hl] ? sv : mloc[hl];
       }
     }
   }
-  s = pb_block_sum_d(s, red);  // __syncthreads inside: p[] is complete afterwards
-  for (int j = tid; j < cache_len; j += blockDim.x) p[j] = (float)__ddiv_rn((double)p[j], s);
-  __syncthreads();
-  // thread (d4, jg): dims 4*d4 .. 4*d4+3 of the slice, positions j = jg, jg + 64, ...
-  const int d4 = tid & 3, jg = tid >> 2;
-  const float* vb = vc + (size_t)g * hd + slice * AD_SLICE + 4 * d4;
-  double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
-  for (int base = jg; base < cache_len; base += 8 * AD_JG) {
-    float4 vv[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int j = base + u * AD_JG;
-      if (j < cache_len) vv[u] = *reinterpret_cast<const float4*>(vb + (size_t)j * kv_dim);
+  for (int hl = 0; hl < AD_MAX_GROUP; ++hl) {
+    if (hl < per) {
+      float m = mloc[hl];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float t = __shfl_xor_sync(0xffffffffu, m, o);
+        m = t > m ? t : m;
+      }
+      if (lane == 0) wred[hl][warp] = m;
     }
+  }
+  __syncthreads();
+  if (tid < per) {
+    float m = wred[tid][0];
+    for (int w = 1; w < AG_THREADS / 32; ++w) m = wred[tid][w] > m ? wred[tid][w] : m;
+    hstat[tid] = m;
+  }
+  __syncthreads();
+  float sloc[AD_MAX_GROUP];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int j = base + u * AD_JG;
-      if (j < cache_len) {
-        const double pj = (double)p[j];
-        a0 = __fma_rn(pj, (double)vv[u].x, a0);
-        a1 = __fma_rn(pj, (double)vv[u].y, a1);
-        a2 = __fma_rn(pj, (double)vv[u].z, a2);
-        a3 = __fma_rn(pj, (double)vv[u].w, a3);
+  for (int hl = 0; hl < AD_MAX_GROUP; ++hl) {
+    sloc[hl] = 0.0f;
+    if (hl < per) {
+      const float mx = hstat[hl];
+      for (int j = tid; j < cache_len; j += AG_THREADS) {
+        const float e = expf(__fsub_rn(sp[(size_t)hl * max_len + j], mx));
+        sp[(size_t)hl * max_len + j] = e;
+        sloc[hl] = __fadd_rn(sloc[hl], e);
       }
     }
   }
-  part[jg][4 * d4 + 0] = a0;
-  part[jg][4 * d4 + 1] = a1;
-  part[jg][4 * d4 + 2] = a2;
-  part[jg][4 * d4 + 3] = a3;
-  __syncthreads();
-  // fixed two-level sum over the 64 position groups: 16 sums of 4, then 16
-  {
-    const int d = tid & 15, k = tid >> 4;
-    const double t = __dadd_rn(__dadd_rn(__dadd_rn(part[4 * k][d], part[4 * k + 1][d]), part[4 * k + 2][d]),
-                               part[4 * k + 3][d]);
-    __syncthreads();
-    part[k][d] = t;
+  __syncthreads();  // every thread has read hstat
+#pragma unroll
+  for (int hl = 0; hl < AD_MAX_GROUP; ++hl) {
+    if (hl < per) {
+      float t = sloc[hl];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
+      if (lane == 0) wred[hl][warp] = t;
+    }
   }
   __syncthreads();
-  if (tid < AD_SLICE) {
-    double t = 0.0;
-    for (int i = 0; i < AD_JG / 4; ++i) t = __dadd_rn(t, part[i][tid]);
-    out[(size_t)h * hd + slice * AD_SLICE + tid] = (float)t;
+  if (tid < per) {
+    float t = wred[tid][0];
+    for (int w = 1; w < AG_THREADS / 32; ++w) t = __fadd_rn(t, wred[tid][w]);
+    hstat[tid] = t;
+  }
+  __syncthreads();
+  for (int i = tid; i < per * cache_len; i += AG_THREADS) {
+    const int hl = i / cache_len, j = i - hl * cache_len;
+    sp[(size_t)hl * max_len + j] = __fdiv_rn(sp[(size_t)hl * max_len + j], hstat[hl]);
+  }
+  __syncthreads();
+
+  const int jgroups = AG_THREADS / h4, d4 = tid % h4, jg = tid / h4;
+  if (jg < jgroups) {
+    float4 acc[AD_MAX_GROUP];
+#pragma unroll
+    for (int hl = 0; hl < AD_MAX_GROUP; ++hl) acc[hl] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* vl = vc + 4 * d4;
+    for (int base = jg; base < cache_len; base += 4 * jgroups) {
+      float4 vv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = base + u * jgroups;
+        if (j < cache_len) vv[u] = *reinterpret_cast<const float4*>(vl + (size_t)j * kv_dim);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = base + u * jgroups;
+        if (j < cache_len) {
+#pragma unroll
+          for (int hl = 0; hl < AD_MAX_GROUP; ++hl) {
+            if (hl < per) {
+              const float pj = sp[(size_t)hl * max_len + j];
+              acc[hl].x = __fmaf_rn(pj, vv[u].x, acc[hl].x);
+              acc[hl].y = __fmaf_rn(pj, vv[u].y, acc[hl].y);
+              acc[hl].z = __fmaf_rn(pj, vv[u].z, acc[hl].z);
+              acc[hl].w = __fmaf_rn(pj, vv[u].w, acc[hl].w);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int hl = 0; hl < AD_MAX_GROUP; ++hl)
+      if (hl < per) reinterpret_cast<float4*>(part + ((size_t)jg * per + hl) * hd)[d4] = acc[hl];
+  }
+  __syncthreads();
+  for (int i = tid; i < per * hd; i += AG_THREADS) {
+    float t = part[i];
+    for (int k = 1; k < jgroups; ++k) t = __fadd_rn(t, part[(size_t)k * per * hd + i]);
+    out[i] = t;
   }
 }
 
-// Decode attention for one query at *pos_dev over the cache; scratch holds
-// n_heads * max_len scores plus n_heads * ceil(max_len / 64) chunk maxima.
+static size_t ag_smem(int per, int hd, int max_len) {
+  return ((size_t)per * hd + (size_t)per * max_len + (size_t)(AG_THREADS / (hd / 4)) * per * hd) * 4;
+}
+
+// Whether k_attn_dec takes this shape (the callers fall back to the general
+// cached attention otherwise).
+bool pb_attn_decode_ok(int n_heads, int n_kv, int hd, int max_len) {
+  return n_kv > 0 && n_heads % n_kv == 0 && hd % 4 == 0 && hd <= AF_MAX_HD &&
+         (size_t)AF_PART * 8 + (size_t)max_len * 4 <= 200 * 1024;
+}
+
+// The batched form also needs <= AD_MAX_GROUP query heads per kv head and its
+// per-head scores in shared memory.
+bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len) {
+  return pb_attn_decode_ok(n_heads, n_kv, hd, max_len) && n_heads / n_kv <= AD_MAX_GROUP && hd / 4 <= AG_THREADS &&
+         ag_smem(n_heads / n_kv, hd, max_len) <= 200 * 1024;
+}
+
+// Decode attention for one query at *pos_dev over the cache (nseq sequences
+// of a batched launch, `geo` apart).
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
-                          int n_heads, int n_kv, int hd, float* out, int max_len, float* scratch, int nseq,
-                          pb_seq_geo geo) {
-  const int per = n_heads / n_kv;
-  if (per > AD_MAX_GROUP || hd % AD_SLICE || hd % 4)
-    return pb_set_error(ctx, PB_ERR_ARG, "decode attention needs <= %d heads per kv head and head_dim %% 16 == 0",
-                        AD_MAX_GROUP);
-  const int nchunks = (max_len + AD_CHUNK - 1) / AD_CHUNK;
-  float* scores = scratch;                                    // [nseq][n_heads][max_len]
-  float* cmax = scratch + (size_t)nseq * n_heads * max_len;  // [nseq][n_heads][nchunks]
+                          int n_heads, int n_kv, int hd, float* out, int max_len, int nseq, pb_seq_geo geo) {
+  if (!(nseq > 1 ? pb_attn_decode_group_ok(n_heads, n_kv, hd, max_len) : pb_attn_decode_ok(n_heads, n_kv, hd, max_len)))
+    return pb_set_error(ctx, PB_ERR_ARG, "decode attention needs n_heads %% n_kv == 0, head_dim %% 4 == 0, "
+                                         "head_dim <= %d and max_len <= %d", AF_MAX_HD, (200 * 1024 - AF_PART * 8) / 4);
   const double scale = 1.0 / sqrt((double)hd);  // llama-streaming.js:546
-  size_t smem1 = (size_t)(per * hd + AD_CHUNK * (hd + 4)) * 4;
-  PB_TRY(pb_launch(ctx, "k_attn_dec_scores", true, k_attn_dec_scores, dim3(n_kv, nchunks, nseq), dim3(256), smem1, q,
-                   kc, pos_dev, n_heads, n_kv, hd, scale, scores, cmax, max_len, geo, ctx->d_err));
-  size_t smem2 = (size_t)max_len * 4;
-  PB_TRY(pb_launch(ctx, "k_attn_dec_pv", true, k_attn_dec_pv, dim3(n_heads, hd / AD_SLICE, nseq), dim3(256), smem2,
-                   (const float*)scores, (const float*)cmax, vc, pos_dev, n_heads, n_kv, hd, out, max_len, geo));
-  return PB_OK;
-}
-
-// scratch of one sequence; a batched launch of nseq sequences needs nseq times this
-size_t pb_attn_decode_scratch_floats(int n_heads, int max_len) {
-  return (size_t)n_heads * max_len + (size_t)n_heads * ((max_len + AD_CHUNK - 1) / AD_CHUNK);
+  if (nseq > 1) {
+    const int per = n_heads / n_kv;
+    return pb_launch(ctx, "k_attn_dec_group", true, k_attn_dec_group, dim3(n_kv, nseq), dim3(AG_THREADS),
+                     ag_smem(per, hd, max_len), q, kc, vc, pos_dev, n_heads, n_kv, hd, (float)scale, out, max_len, geo,
+                     ctx->d_err);
+  }
+  const size_t smem = (size_t)AF_PART * 8 + (size_t)max_len * 4;
+  return pb_launch(ctx, "k_attn_dec", true, k_attn_dec, dim3(n_heads, nseq), dim3(AF_THREADS), smem, q, kc, vc,
+                   pos_dev, n_heads, n_kv, hd, scale, out, max_len, geo, ctx->d_err);
 }
 
 int pb_setup_ops_kernels(void) {
   cudaError_t e = cudaFuncSetAttribute(k_attn_cached, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec_group, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_attn_prefill_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fa_smem());
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
