@@ -59,29 +59,6 @@ __host__ __device__ constexpr uint32_t gm_idesc(int tok) {
   return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(tok >> 3) << 17) | ((uint32_t)(GM_ROWS >> 4) << 24);
 }
 
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-
-// Wait for the phase of the given parity; gives up after ~2 s of device clock.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  const uint32_t addr = smem_addr(bar);
-  const long long t0 = clock64();
-  for (uint32_t it = 0;; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(ok)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    if ((it & 255) == 255 && clock64() - t0 > 4000000000LL) {
-      pb_raise(err, PB_DEVERR_WAIT);
-      return false;
-    }
-  }
-}
-
 __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                         uint32_t accumulate) {
   asm volatile(
@@ -142,8 +119,8 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+    pb_mbar_init(&bars[0], 1);
+    pb_mbar_init(&bars[1], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -156,7 +133,7 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
     const int st = ks & 1, kg = kbeg + ks;  // kg: global K step
     unsigned char* sA = ring + st * GM_STAGE_BYTES;
     unsigned char* sB = sA + GM_TILE_BYTES;
-    if (ks >= 2) ok = mbar_wait(&bars[st], ((ks >> 1) - 1) & 1, err);  // MMAs of step ks-2 are done with it
+    if (ks >= 2) ok = pb_mbar_wait(&bars[st], ((ks >> 1) - 1) & 1, err);  // MMAs of step ks-2 are done with it
     if (!ok) break;
     // weights: thread -> (row, block) of the two Q4_0 blocks of this step
     {
@@ -220,7 +197,7 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
     }
   }
   // the last step's commit covers every MMA issued before it
-  if (ok && ksteps > 0) ok = mbar_wait(&bars[(ksteps - 1) & 1], ((ksteps - 1) >> 1) & 1, err);
+  if (ok && ksteps > 0) ok = pb_mbar_wait(&bars[(ksteps - 1) & 1], ((ksteps - 1) >> 1) & 1, err);
   const bool empty_split = ksteps == 0;  // no MMA wrote the accumulator: the partial is zero
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   if (ok && warp < 4) {
@@ -267,10 +244,6 @@ constexpr int TG_STAGE_BYTES = TG_A_BYTES + TG_B_BYTES;
 constexpr uint32_t TG_IDESC = (1u << 4) | ((uint32_t)(TG_TOK >> 3) << 17) | ((uint32_t)(TG_ROWS >> 4) << 24);
 
 namespace {
-
-__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
-}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -339,10 +312,10 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   }
   if (tid == 32) {
     for (int s = 0; s < TG_STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      pb_mbar_init(&full[s], 1);
+      pb_mbar_init(&empty[s], 1);
     }
-    mbar_init(&acc_full, 1);
+    pb_mbar_init(&acc_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -354,9 +327,9 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     // producer: stage s is free once the MMAs of step ks - STAGES committed to empty[s]
     for (int ks = 0; ks < ksteps; ++ks) {
       const int s = ks % TG_STAGES;
-      if (ks >= TG_STAGES && !mbar_wait(&empty[s], ((ks / TG_STAGES) - 1) & 1, err)) break;
+      if (ks >= TG_STAGES && !pb_mbar_wait(&empty[s], ((ks / TG_STAGES) - 1) & 1, err)) break;
       unsigned char* sA = ring + s * TG_STAGE_BYTES;
-      mbar_arrive_tx(&full[s], TG_STAGE_BYTES);
+      pb_mbar_arrive_tx(&full[s], TG_STAGE_BYTES);
       tma_load_2d(sA, &map_w, ks * TG_K, n0, &full[s]);
       tma_load_2d(sA + TG_A_BYTES, &map_x, ks * TG_K, m0, &full[s]);
     }
@@ -365,7 +338,7 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     bool ok = true;
     for (int ks = 0; ks < ksteps && ok; ++ks) {
       const int s = ks % TG_STAGES;
-      ok = mbar_wait(&full[s], (ks / TG_STAGES) & 1, err);
+      ok = pb_mbar_wait(&full[s], (ks / TG_STAGES) & 1, err);
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       unsigned char* sA = ring + s * TG_STAGE_BYTES;
@@ -377,7 +350,7 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     mma_commit(&acc_full);  // fires when every MMA above has completed
   } else if (warp >= 4) {
     const int q = warp - 4;  // TMEM lane quadrant
-    if (mbar_wait(&acc_full, 0, err)) {
+    if (pb_mbar_wait(&acc_full, 0, err)) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int row = n0 + q * 32 + lane;
 #pragma unroll 1

@@ -158,6 +158,43 @@ __device__ __forceinline__ void pb_raise(int* err, int code) {
 #define PB_DEVERR_WAIT 2
 #define PB_DEVERR_TOKEN 3
 
+// ---- mbarriers and bulk copies into shared memory -------------------------
+__device__ __forceinline__ uint32_t pb_smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void pb_mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(pb_smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void pb_mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(pb_smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+// Wait for the phase of the given parity; gives up after ~2 s of device clock
+// (PB_DEVERR_WAIT) and returns false.
+__device__ __forceinline__ bool pb_mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  const uint32_t addr = pb_smem_addr(bar);
+  const long long t0 = clock64();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((it & 255) == 255 && clock64() - t0 > 4000000000LL) {
+      pb_raise(err, PB_DEVERR_WAIT);
+      return false;
+    }
+  }
+}
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+// global memory into this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void pb_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   pb_smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(pb_smem_addr(bar))
+               : "memory");
+}
+
 // Ordered-key argmax: larger key = larger value, ties -> lower index.
 // Values that are NaN or -inf never win (llama-streaming.js:899-909 uses a
 // strict `>` from -Infinity and index 0).
