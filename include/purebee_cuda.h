@@ -248,9 +248,14 @@ int pb_model_free(pb_model* m);
  * gains 1, quantized on the device. */
 int pb_model_init_synthetic(pb_model* m, uint64_t seed, double stdev);
 /* Set / get one tensor.  which: 0 embedding, 1..7 = wq wk wv wo w1 w2 w3,
- * 8 = attention norm, 9 = ffn norm (layer), 10 = final norm.  Streaming
- * models take GGUF bytes; llama.js models take (scales f32[], int8 q[])
- * packed back to back for 1..7 and f32 for the embedding. */
+ * 8 = attention norm, 9 = ffn norm (layer), 10 = final norm, 11 = untied LM
+ * head (after pb_model_attach_head).  Streaming models take GGUF bytes;
+ * llama.js models take (scales f32[], int8 q[]) packed back to back for 1..7
+ * and f32 for the embedding. */
+/* Give a streaming model its own LM head table (GGUF output.weight, Q4_0 or
+ * Q8_0) instead of the tied embedding (streaming-loader.js:77-86
+ * sharedWeights, llama-streaming.js:616-679). */
+int pb_model_attach_head(pb_model* m, int type);
 int pb_model_set_tensor(pb_model* m, int layer, int which, const void* host, size_t bytes);
 int pb_model_get_tensor(pb_model* m, int layer, int which, void* host, size_t bytes);
 /* llama-streaming.js:738-815 / llama.js:204-371 forward(tokens, startPos):
@@ -274,6 +279,46 @@ int pb_model_kv(pb_model* m, int layer, int which_v, float* host, size_t floats)
 int64_t pb_model_decode_bytes(const pb_model* m, int pos);
 /* Kernel launches of one decode step. */
 int pb_model_decode_launches(const pb_model* m);
+
+/* ------------------------------------------------------------------ */
+/* GGUF files (gguf.js:76-194 GGUFParser, :402-424 extractConfig;        */
+/* streaming-loader.js:35-87 parseHeader, :245-262 loadTensorRaw)        */
+/* ------------------------------------------------------------------ */
+
+/* A parsed GGUF v2/v3 file: metadata and the tensor index in host memory,
+ * tensor bytes read on demand.  Errors: PB_ERR_ARG with the message in
+ * pb_gguf_last_error() (the reference throws Error with a message). */
+typedef struct pb_gguf pb_gguf;
+const char* pb_gguf_last_error(void);
+int pb_gguf_open(const char* path, pb_gguf** out);
+int pb_gguf_close(pb_gguf* g);
+int pb_gguf_version(const pb_gguf* g);
+int64_t pb_gguf_data_start(const pb_gguf* g); /* aligned start of the tensor data */
+int64_t pb_gguf_alignment(const pb_gguf* g);  /* general.alignment, default 32 */
+/* Metadata: value types are GGUF's (0 u8 .. 12 f64; 8 string, 9 array).
+ * Strings are returned as borrowed pointers with their byte length. */
+int pb_gguf_meta_count(const pb_gguf* g);
+int pb_gguf_meta_find(const pb_gguf* g, const char* key); /* index or -1 */
+int pb_gguf_meta_key(const pb_gguf* g, int i, const char** key);
+int pb_gguf_meta_type(const pb_gguf* g, int i, int* type, int* arr_type, int64_t* arr_len);
+int pb_gguf_meta_int(const pb_gguf* g, int i, int64_t* v);
+int pb_gguf_meta_float(const pb_gguf* g, int i, double* v);
+int pb_gguf_meta_string(const pb_gguf* g, int i, const char** s, int64_t* len);
+int pb_gguf_meta_array_string(const pb_gguf* g, int i, int64_t j, const char** s, int64_t* len);
+int pb_gguf_meta_array_number(const pb_gguf* g, int i, int64_t j, double* v);
+/* Tensor index: dims[4] (unused dims 1), absolute file offset, byte size. */
+int pb_gguf_tensor_count(const pb_gguf* g);
+int pb_gguf_tensor_find(const pb_gguf* g, const char* name); /* index or -1 */
+int pb_gguf_tensor_info(const pb_gguf* g, int i, const char** name, int* type, int* n_dims, int64_t* dims,
+                        int64_t* file_offset, int64_t* bytes);
+int pb_gguf_tensor_read(const pb_gguf* g, int i, void* host, size_t bytes);
+/* extractConfig with the reference's defaults; vocab from the tokenizer's
+ * token list; a streaming (Q4_0) model with a Q4_0 or Q8_0 embedding. */
+int pb_gguf_config(const pb_gguf* g, pb_model_config* cfg);
+/* Create a streaming model from the file (every tensor uploaded once into the
+ * packed device layout; output.weight, when present, as an untied head).
+ * seq_len > 0 overrides the file's context length. */
+int pb_model_load_gguf(pb_ctx* ctx, const pb_gguf* g, int seq_len, pb_model** out);
 
 /* ------------------------------------------------------------------ */
 /* batched serving (the batched configuration; the reference serves one  */

@@ -103,6 +103,7 @@ def lib():
         "orc_model_q8a_scales": (ctypes.POINTER(ctypes.c_float), [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                                                   ctypes.POINTER(c_i64)]),
         "orc_model_refresh": (None, [ctypes.c_void_p]),
+        "orc_model_set_head": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
         "orc_forward": (ctypes.c_int, [ctypes.c_void_p, I32P, ctypes.c_int, ctypes.c_int, F32P]),
         "orc_generate": (ctypes.c_int, [ctypes.c_void_p, I32P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                         I32P, ctypes.c_int]),
@@ -406,6 +407,12 @@ class Model:
 
     def refresh(self):
         lib().orc_model_refresh(self.h)
+
+    def set_head(self, emb_type, raw):
+        """Untied LM head (GGUF Q4_0 / Q8_0 bytes of output.weight)."""
+        raw = np.ascontiguousarray(raw, np.uint8)
+        if lib().orc_model_set_head(self.h, emb_type, raw.ctypes.data) != 0:
+            raise ValueError("orc_model_set_head: unsupported type")
 
     def forward(self, tokens, start_pos):
         toks = np.ascontiguousarray(tokens, np.int32)

@@ -757,6 +757,7 @@ struct orc_model {
   float* q8a_scales[1 + 7 * 512];
   int64_t q8a_count[1 + 7 * 512];
   float* emb_f32;            /* dequantized embedding [V][dim] */
+  float* head_f32;           /* dequantized untied LM head [V][dim], NULL when tied */
   float* rms_att;            /* [L][dim] */
   float* rms_ffn;
   float* rms_final;
@@ -807,6 +808,7 @@ void orc_model_free(orc_model* m) {
   if (!m) return;
   for (int i = 0; i < 1 + 7 * m->c.n_layers; ++i) { free(m->raw[i]); free(m->q8a_scales[i]); }
   if (m->c.emb_type != ORC_EMB_F32) free(m->emb_f32);
+  free(m->head_f32);
   free(m->rms_att); free(m->rms_ffn); free(m->rms_final); free(m->kc); free(m->vc);
   free(m);
 }
@@ -1014,6 +1016,18 @@ static void head_double_rows(void* c, int64_t lo, int64_t hi) {
   }
 }
 
+/* An untied LM head (GGUF output.weight, streaming-loader.js:77-86 and
+ * :330-334): dequantized to f32 like the embedding, then used by the head in
+ * place of the tied table. */
+int orc_model_set_head(orc_model* m, int emb_type, const uint8_t* raw) {
+  const int64_t ne = (int64_t)m->c.vocab * m->c.dim;
+  if (!m->head_f32) m->head_f32 = (float*)malloc(sizeof(float) * (size_t)ne);
+  if (emb_type == ORC_EMB_Q4_0) orc_dequant_q4_0(raw, ne, m->head_f32);
+  else if (emb_type == ORC_EMB_Q8_0) orc_dequant_q8_0(raw, ne, m->head_f32);
+  else return -1;
+  return 0;
+}
+
 int orc_forward(orc_model* m, const int* tokens, int n, int start_pos, float* logits) {
   const orc_config* c = &m->c;
   int dim = c->dim;
@@ -1034,7 +1048,7 @@ int orc_forward(orc_model* m, const int* tokens, int n, int start_pos, float* lo
     orc_parallel_rows(c->vocab, head_double_rows, &a);
   } else {
     /* llama-streaming.js:640-642 -> wasm-q4.js:798-839 (batch_dot) */
-    orc_batch_dot(hn, m->emb_f32, c->vocab, dim, logits);
+    orc_batch_dot(hn, m->head_f32 ? m->head_f32 : m->emb_f32, c->vocab, dim, logits);
   }
   free(hn);
   free(x);

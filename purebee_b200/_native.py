@@ -105,6 +105,29 @@ SIGNATURES = {
     "pb_model_free": (I, [V]),
     "pb_model_init_synthetic": (I, [V, U64, D]),
     "pb_model_set_tensor": (I, [V, I, I, V, SZ]),
+    "pb_model_attach_head": (I, [V, I]),
+    "pb_gguf_last_error": (ctypes.c_char_p, []),
+    "pb_gguf_open": (I, [ctypes.c_char_p, ctypes.POINTER(V)]),
+    "pb_gguf_close": (I, [V]),
+    "pb_gguf_version": (I, [V]),
+    "pb_gguf_data_start": (I64, [V]),
+    "pb_gguf_alignment": (I64, [V]),
+    "pb_gguf_meta_count": (I, [V]),
+    "pb_gguf_meta_find": (I, [V, ctypes.c_char_p]),
+    "pb_gguf_meta_key": (I, [V, I, ctypes.POINTER(ctypes.c_char_p)]),
+    "pb_gguf_meta_type": (I, [V, I, ctypes.POINTER(I), ctypes.POINTER(I), ctypes.POINTER(I64)]),
+    "pb_gguf_meta_int": (I, [V, I, ctypes.POINTER(I64)]),
+    "pb_gguf_meta_float": (I, [V, I, ctypes.POINTER(D)]),
+    "pb_gguf_meta_string": (I, [V, I, ctypes.POINTER(V), ctypes.POINTER(I64)]),
+    "pb_gguf_meta_array_string": (I, [V, I, I64, ctypes.POINTER(V), ctypes.POINTER(I64)]),
+    "pb_gguf_meta_array_number": (I, [V, I, I64, ctypes.POINTER(D)]),
+    "pb_gguf_tensor_count": (I, [V]),
+    "pb_gguf_tensor_find": (I, [V, ctypes.c_char_p]),
+    "pb_gguf_tensor_info": (I, [V, I, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(I), ctypes.POINTER(I),
+                                ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64)]),
+    "pb_gguf_tensor_read": (I, [V, I, V, SZ]),
+    "pb_gguf_config": (I, [V, ctypes.POINTER(ModelConfig)]),
+    "pb_model_load_gguf": (I, [V, V, I, ctypes.POINTER(V)]),
     "pb_model_get_tensor": (I, [V, I, I, V, SZ]),
     "pb_model_forward": (I, [V, V, I, I, V]),
     "pb_model_decode": (I, [V, I, I, ctypes.POINTER(I), V]),

@@ -54,6 +54,7 @@ struct pb_model {
   int kv_dim = 0;
   // streaming weights
   pb_qmat* emb = nullptr;                 // Q4_0 / Q8_0 tiles [V][dim]
+  pb_qmat* head = nullptr;                // untied output.weight tiles [V][dim] (nullptr: the head is emb)
   std::vector<pb_qmat*> qkv, wo, gu, w2;  // per layer
   // llama.js weights
   float* emb_f32 = nullptr;               // tiles [V/32][dim][32]
@@ -132,6 +133,7 @@ extern "C" int pb_model_free(pb_model* m) {
   if (ctx) pb_wait(ctx);
   free_graph(m);
   pb_qmat_free(nullptr, m->emb);
+  pb_qmat_free(nullptr, m->head);
   for (auto* p : m->qkv) pb_qmat_free(nullptr, p);
   for (auto* p : m->wo) pb_qmat_free(nullptr, p);
   for (auto* p : m->gu) pb_qmat_free(nullptr, p);
@@ -347,8 +349,25 @@ done:
   return rc;
 }
 
+// The LM head table: output.weight when the file has one, else the tied
+// embedding (llama-streaming.js:616-679, streaming-loader.js sharedWeights).
+static pb_qmat* head_of(const pb_model* m) { return m->head ? m->head : m->emb; }
+
+// Give a streaming model an untied LM head (GGUF output.weight) of `type`
+// (Q4_0 / Q8_0), set afterwards as tensor 11.
+extern "C" int pb_model_attach_head(pb_model* m, int type) {
+  if (!m) return PB_ERR_ARG;
+  if (m->c.kind != PB_MODEL_STREAMING_Q4 || (type != PB_TYPE_Q4_0 && type != PB_TYPE_Q8_0))
+    return pb_set_error(m->ctx, PB_ERR_ARG, "an untied head needs a streaming model and a Q4_0 or Q8_0 table");
+  free_graph(m);
+  pb_qmat_free(m->ctx, m->head);
+  m->head = nullptr;
+  return pb_qmat_alloc(m->ctx, type, PB_LAYOUT_TILED8, m->c.vocab, m->c.dim, &m->head);
+}
+
 static size_t tensor_bytes(const pb_model* m, int which) {
   const pb_model_config& c = m->c;
+  if (which == 11) return m->head ? (size_t)((int64_t)c.vocab * c.dim / 32) * (m->head->type == PB_TYPE_Q4_0 ? 18 : 34) : 0;
   if (which >= 8) return (size_t)c.dim * 4;
   if (which == 0) {
     int64_t ne = (int64_t)c.vocab * c.dim;
@@ -366,12 +385,13 @@ static size_t tensor_bytes(const pb_model* m, int which) {
 static int model_tensor_io(pb_model* m, int layer, int which, void* host, size_t bytes, int get) {
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
-  if (which < 0 || which > 10 || (which >= 1 && which <= 9 && (layer < 0 || layer >= c.n_layers)))
+  if (which < 0 || which > 11 || (which >= 1 && which <= 9 && (layer < 0 || layer >= c.n_layers)))
     return pb_set_error(ctx, PB_ERR_ARG, "bad tensor (layer %d, which %d)", layer, which);
+  if (which == 11 && !m->head) return pb_set_error(ctx, PB_ERR_ARG, "the model has no untied head (pb_model_attach_head)");
   size_t need = tensor_bytes(m, which);
   if (bytes != need) return pb_set_error(ctx, PB_ERR_ARG, "tensor %d needs %zu bytes, got %zu", which, need, bytes);
   if (!get) free_graph(m);
-  if (which >= 8) {
+  if (which >= 8 && which <= 10) {
     float* p = which == 8 ? m->rms_att + (size_t)layer * c.dim : which == 9 ? m->rms_ffn + (size_t)layer * c.dim
                                                                             : m->rms_final;
     return get ? pb_download(ctx, host, p, bytes) : pb_upload(ctx, p, host, bytes);
@@ -398,8 +418,8 @@ static int model_tensor_io(pb_model* m, int layer, int which, void* host, size_t
   }
   pb_qmat* dst;
   int rows, off = 0, il = 0;
-  if (which == 0) {
-    dst = m->emb;
+  if (which == 0 || which == 11) {
+    dst = which == 0 ? m->emb : m->head;
     rows = c.vocab;
   } else {
     int k;
@@ -502,7 +522,7 @@ static int run_layer_decode_q4(pb_model* m, int l) {
   r2.l2_next[0] = r2.l2_next[1] = nullptr;
   r2.l2_next_bytes[0] = r2.l2_next_bytes[1] = 0;
   if (!last) l2_hint(&r2, 0, m->gu[l + 1]);
-  else if (m->emb && m->emb->type != PB_TYPE_F32) l2_hint(&r2, 0, m->emb, (size_t)48 << 20);
+  else if (head_of(m)) l2_hint(&r2, 0, head_of(m), (size_t)48 << 20);
   PB_TRY(pb_launch_matvec(ctx, m->w2[l], m->hb, m->x, 0, dim, &r2));
   return PB_OK;
 }
@@ -588,7 +608,7 @@ static int launch_embed(pb_model* m, const int* toks, int M) {
 static int launch_head(pb_model* m, const float* last_x) {
   pb_ctx* ctx = m->ctx;
   if (m->c.kind == PB_MODEL_STREAMING_Q4)
-    return pb_launch_head_norm(ctx, m->emb, last_x, m->rms_final, m->c.eps, m->logits, m->key, 0);
+    return pb_launch_head_norm(ctx, head_of(m), last_x, m->rms_final, m->c.eps, m->logits, m->key, 0);
   return pb_launch_head_norm(ctx, &m->emb_f32_view, last_x, m->rms_final, m->c.eps, m->logits, m->key, 1);
 }
 
@@ -761,7 +781,8 @@ extern "C" int64_t pb_model_decode_bytes(const pb_model* m, int pos) {
   }
   w *= c.n_layers;
   int64_t ne = (int64_t)c.vocab * c.dim;
-  int64_t head = c.kind == PB_MODEL_LLAMA_Q8A ? ne * 4 : ne / 32 * (c.emb_type == PB_TYPE_Q4_0 ? 18 : 34);
+  const int ht = m->head ? m->head->type : c.emb_type;
+  int64_t head = c.kind == PB_MODEL_LLAMA_Q8A ? ne * 4 : ne / 32 * (ht == PB_TYPE_Q4_0 ? 18 : 34);
   int64_t kvb = (int64_t)2 * c.n_layers * (pos + 1) * m->kv_dim * 4;
   return w + head + kvb;
 }
@@ -890,8 +911,8 @@ extern "C" int pb_batch_create(pb_model* m, int n_seqs, pb_batch** out) {
   // decode steps run the fused-dequant GEMM, which needs no growable scratch
   // (the recorded decode graph relies on that)
   if (n_seqs > 256) return pb_set_error(ctx, PB_ERR_ARG, "at most 256 sequences per batch");
-  if (c.kind != PB_MODEL_STREAMING_Q4 || !m->emb || m->emb->type != PB_TYPE_Q4_0)
-    return pb_set_error(ctx, PB_ERR_ARG, "batched serving needs a streaming model with a Q4_0 embedding");
+  if (c.kind != PB_MODEL_STREAMING_Q4 || !m->emb || m->emb->type != PB_TYPE_Q4_0 || head_of(m)->type != PB_TYPE_Q4_0)
+    return pb_set_error(ctx, PB_ERR_ARG, "batched serving needs a streaming model with a Q4_0 embedding and head");
   if (!pb_attn_decode_group_ok(c.n_heads, c.n_kv_heads, c.head_dim, c.seq_len))
     return pb_set_error(ctx, PB_ERR_ARG, "batched decode attention needs <= 8 query heads per kv head, head_dim %% 4 "
                                          "== 0, head_dim <= 256 and the scores of a kv head in shared memory");
@@ -977,7 +998,7 @@ static int batch_head(pb_batch* b, const float* last_rows, const int* pos_dev) {
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
   PB_TRY(launch_norm(m, last_rows, b->B, m->rms_final, b->xn));
-  PB_TRY(pb_launch_q4_gemm(ctx, m->emb, b->xn, c.dim, b->B, b->logits, c.vocab, nullptr, 0));
+  PB_TRY(pb_launch_q4_gemm(ctx, head_of(m), b->xn, c.dim, b->B, b->logits, c.vocab, nullptr, 0));
   k_argmax_rows<<<b->B, 1024, 0, ctx->stream>>>(b->logits, c.vocab, b->next, b->hist, pos_dev, c.seq_len + 1);
   PB_LAUNCHED(ctx, "k_argmax_rows");
   return PB_OK;

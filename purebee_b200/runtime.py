@@ -40,16 +40,20 @@ class LlamaConfig:
 
 
 class _DeviceModel:
-    def __init__(self, ctx: N.Context, cfg: LlamaConfig, kind: int, emb_type: int):
+    def __init__(self, ctx: N.Context, cfg: LlamaConfig, kind: int, emb_type: int, handle: Optional[int] = None,
+                 head_type: Optional[int] = None):
         self.ctx = ctx
         self.cfg = cfg
         self.kind = kind
         self.emb_type = emb_type
-        c = N.ModelConfig(kind, emb_type, cfg.dim, cfg.hiddenDim, cfg.nLayers, cfg.nHeads, cfg.nKvHeads,
-                          cfg.headDim, cfg.vocabSize, cfg.seqLen, float(cfg.ropeTheta), float(cfg.rmsNormEps))
-        h = ctypes.c_void_p()
-        ctx._check(N.lib().pb_model_create(ctx.h, ctypes.byref(c), ctypes.byref(h)))
-        self.h = h.value
+        self.head_type = head_type  # untied LM head table type, None when tied
+        if handle is None:
+            c = N.ModelConfig(kind, emb_type, cfg.dim, cfg.hiddenDim, cfg.nLayers, cfg.nHeads, cfg.nKvHeads,
+                              cfg.headDim, cfg.vocabSize, cfg.seqLen, float(cfg.ropeTheta), float(cfg.rmsNormEps))
+            h = ctypes.c_void_p()
+            ctx._check(N.lib().pb_model_create(ctx.h, ctypes.byref(c), ctypes.byref(h)))
+            handle = h.value
+        self.h = handle
 
     def free(self):
         # a model lives inside its context: once the context is closed the
@@ -69,6 +73,10 @@ class _DeviceModel:
 
     def tensor_bytes(self, layer: int, which: int) -> int:
         c = self.cfg
+        if which == 11:
+            if self.head_type is None:
+                raise ValueError("the model has no untied head")
+            return c.vocabSize * c.dim // 32 * (18 if self.head_type == N.TYPE_Q4_0 else 34)
         if which >= 8:
             return c.dim * 4
         if which == 0:
@@ -262,6 +270,38 @@ class StreamingLlamaRuntime(_RuntimeBase):
     """llama-streaming.js StreamingLlamaRuntime over GGUF Q4_0 layer weights and
     a Q4_0 or Q8_0 tied embedding (emb_type)."""
     KIND = N.MODEL_STREAMING_Q4
+
+    @classmethod
+    def fromGGUF(cls, path: str, options: Optional[dict] = None, ctx: Optional[N.Context] = None):
+        """A runtime over a GGUF file (streaming-loader.js:35-87 parseHeader,
+        :119-162 resident raw weights, llama-streaming.js constructor): every
+        tensor goes once into the packed device layout; output.weight, when
+        the file has one, becomes an untied head.  options.seqLen overrides
+        the file's context length."""
+        from .gguf import GGUFFile
+        options = options or {}
+        ctx = ctx or N.Context(options.get("device", 0))
+        seq = int(options.get("seqLen") or 0)
+        with GGUFFile(path) as f:
+            cfg, extra = f.config()
+            if seq:
+                cfg.seqLen = seq
+            head = next((i for i in f.tensorInfos if i["name"] == "output.weight"), None)
+            h = ctypes.c_void_p()
+            ctx._check(N.lib().pb_model_load_gguf(ctx.h, f.h, seq, ctypes.byref(h)))
+            meta = f.metadata
+        rt = cls.__new__(cls)
+        rt.config = cfg
+        rt.ctx = ctx
+        head_type = None if head is None else (N.TYPE_Q4_0 if head["type"] == 2 else N.TYPE_Q8_0)
+        rt.model = _DeviceModel(ctx, cfg, cls.KIND, extra["embType"], handle=h.value, head_type=head_type)
+        rt._loaded = True
+        rt._layersUsed = 0
+        rt._totalForwards = 0
+        rt.sharedWeights = head is None
+        rt.bosId = meta.get("tokenizer.ggml.bos_token_id", 1)
+        rt.eosId = meta.get("tokenizer.ggml.eos_token_id", 2)
+        return rt
 
 
 class LlamaRuntime(_RuntimeBase):
