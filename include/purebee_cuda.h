@@ -281,6 +281,25 @@ int64_t pb_model_decode_bytes(const pb_model* m, int pos);
 int pb_model_decode_launches(const pb_model* m);
 
 /* ------------------------------------------------------------------ */
+/* sampling (llama-streaming.js:868-894 sample(logits, topK, temperature)) */
+/* ------------------------------------------------------------------ */
+
+/* Top-K of logits / temperature (ties to the lower index, as the stable JS
+ * sort), softmax over them in double, then the first index whose running
+ * probability reaches r.  The reference draws r from Math.random(); here r =
+ * pb_sample_uniform(seed, counter), uniform in [0, 1) with 53 bits.
+ * logits and token live on the device; enqueued on the context stream.
+ * 0 < top_k <= 256, temperature > 0; NaN logits are never chosen. */
+int pb_sample_topk(pb_ctx* ctx, const float* logits_dev, int V, int top_k, double temperature, uint64_t seed,
+                   uint64_t counter, int* token_dev);
+double pb_sample_uniform(uint64_t seed, uint64_t counter);
+/* llama-streaming.js:914-970 generate(prompt, maxTokens, {temperature,
+ * topK}) with device sampling: draw i uses pb_sample_uniform(seed, i) (the
+ * prefill's token is draw 0); decode steps replay one recorded graph. */
+int pb_model_generate_sampled(pb_model* m, const int* prompt_host, int n_prompt, int max_tokens, int eos_id, int top_k,
+                              double temperature, uint64_t seed, int* out_host, int out_cap, int* n_out);
+
+/* ------------------------------------------------------------------ */
 /* GGUF files (gguf.js:76-194 GGUFParser, :402-424 extractConfig;        */
 /* streaming-loader.js:35-87 parseHeader, :245-262 loadTensorRaw)        */
 /* ------------------------------------------------------------------ */

@@ -104,6 +104,8 @@ def lib():
                                                                   ctypes.POINTER(c_i64)]),
         "orc_model_refresh": (None, [ctypes.c_void_p]),
         "orc_model_set_head": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+        "orc_sample": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_double]),
+        "orc_sample_uniform": (ctypes.c_double, [ctypes.c_uint64, ctypes.c_uint64]),
         "orc_forward": (ctypes.c_int, [ctypes.c_void_p, I32P, ctypes.c_int, ctypes.c_int, F32P]),
         "orc_generate": (ctypes.c_int, [ctypes.c_void_p, I32P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                         I32P, ctypes.c_int]),
@@ -330,6 +332,16 @@ def swiglu_fused(g, u):
 def argmax(logits):
     l = _f32(logits).ravel()
     return int(lib().orc_argmax(l, l.size))
+
+
+def sample(logits, topK, temperature, r):
+    """llama-streaming.js:868-894 with the uniform draw r given."""
+    x = _f32(logits)
+    return int(lib().orc_sample(x.ctypes.data, x.size, topK, temperature, r))
+
+
+def sample_uniform(seed, counter):
+    return float(lib().orc_sample_uniform(seed, counter))
 
 
 def synth_weights(n, seed, tensor_id, stdev=0.02):

@@ -1075,3 +1075,48 @@ int orc_generate(orc_model* m, const int* prompt, int n_prompt, int max_tokens, 
   free(logits);
   return cnt;
 }
+
+/* ---- sampling (llama-streaming.js:868-894) ---------------------------- */
+typedef struct { double v; int i; } orc_vi;
+static int orc_vi_cmp(const void* a, const void* b) {
+  const orc_vi* x = (const orc_vi*)a;
+  const orc_vi* y = (const orc_vi*)b;
+  if (x->v != y->v) return x->v > y->v ? -1 : 1; /* value descending */
+  return x->i - y->i;                            /* stable: lower index first */
+}
+
+/* sample(logits, topK, temperature) with the uniform draw r given (the
+ * reference's Math.random()).  NaN logits are left out of the ranking. */
+int orc_sample(const float* logits, int V, int topK, double temperature, double r) {
+  orc_vi* a = (orc_vi*)malloc(sizeof(orc_vi) * (size_t)(V > 0 ? V : 1));
+  int n = 0;
+  for (int i = 0; i < V; ++i)
+    if (logits[i] == logits[i]) { a[n].v = (double)logits[i] / temperature; a[n].i = i; ++n; }
+  qsort(a, (size_t)n, sizeof(orc_vi), orc_vi_cmp);
+  const int k = topK < n ? topK : n;
+  int tok = k > 0 ? a[0].i : 0;
+  if (k > 0) {
+    double* e = (double*)malloc(sizeof(double) * (size_t)k);
+    const double maxv = a[0].v;
+    double sum = 0;
+    for (int i = 0; i < k; ++i) { e[i] = exp(a[i].v - maxv); sum += e[i]; }
+    double cum = 0;
+    for (int i = 0; i < k; ++i) {
+      cum += e[i] / sum;
+      if (r <= cum) { tok = a[i].i; break; }
+    }
+    free(e);
+  }
+  free(a);
+  return tok;
+}
+
+/* splitmix64 (Steele, Lea, Flood 2014) of seed + (counter + 1) * golden
+ * gamma, top 53 bits as a double in [0, 1): the draw the device uses. */
+double orc_sample_uniform(uint64_t seed, uint64_t counter) {
+  uint64_t z = seed + (counter + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (double)(z >> 11) * (1.0 / 9007199254740992.0);
+}

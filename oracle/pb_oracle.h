@@ -117,6 +117,9 @@ float* orc_model_q8a_scales(orc_model* m, int layer, int which, int64_t* count);
 void orc_model_refresh(orc_model* m);
 /* Untied LM head from GGUF bytes (emb_type ORC_EMB_Q4_0 / ORC_EMB_Q8_0). */
 int orc_model_set_head(orc_model* m, int emb_type, const uint8_t* raw);
+/* llama-streaming.js:868-894 sample() with the uniform draw r given. */
+int orc_sample(const float* logits, int V, int topK, double temperature, double r);
+double orc_sample_uniform(uint64_t seed, uint64_t counter);
 /* forward(tokens, startPos) -> logits[vocab] (llama-streaming.js:738-815, llama.js:204-371) */
 int orc_forward(orc_model* m, const int* tokens, int n, int start_pos, float* logits);
 /* generate, greedy (llama-streaming.js:914-970, llama.js:452-505); returns tokens written */

@@ -106,6 +106,9 @@ SIGNATURES = {
     "pb_model_init_synthetic": (I, [V, U64, D]),
     "pb_model_set_tensor": (I, [V, I, I, V, SZ]),
     "pb_model_attach_head": (I, [V, I]),
+    "pb_sample_topk": (I, [V, V, I, I, D, U64, U64, V]),
+    "pb_sample_uniform": (D, [U64, U64]),
+    "pb_model_generate_sampled": (I, [V, V, I, I, I, I, D, U64, V, I, ctypes.POINTER(I)]),
     "pb_gguf_last_error": (ctypes.c_char_p, []),
     "pb_gguf_open": (I, [ctypes.c_char_p, ctypes.POINTER(V)]),
     "pb_gguf_close": (I, [V]),

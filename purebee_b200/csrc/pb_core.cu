@@ -124,6 +124,7 @@ extern "C" int pb_init(int device, pb_ctx** out) {
   cudaMemset(ctx->d_err, 0, sizeof(int));
   cudaDeviceSynchronize();
   if (pb_setup_q4_kernels() != PB_OK || pb_setup_ops_kernels() != PB_OK || pb_setup_gemm_kernels() != PB_OK ||
+      pb_setup_sample_kernels() != PB_OK ||
       pb_setup_noalloc(ctx) != PB_OK) {
     pb_shutdown(ctx);
     return PB_ERR_CUDA;

@@ -282,4 +282,10 @@ int pb_qmat_pack_from_device(pb_ctx* ctx, pb_qmat* m, const void* gguf_dev);
 int pb_setup_q4_kernels(void);
 int pb_setup_ops_kernels(void);
 int pb_setup_gemm_kernels(void);
+int pb_setup_sample_kernels(void);
+// Top-K sampling (pb_sample.cu): candidate keys needed, and the two launches.
+size_t pb_sample_cand_count(int V, int K);
+int pb_launch_sample(pb_ctx* ctx, const float* logits, int V, int K, double temperature, uint64_t seed,
+                     uint64_t counter, uint64_t* ctr_dev, uint64_t* cand, int* tok_dev, int* pos_dev, int* hist,
+                     int hist_len, unsigned long long* key_reset);
 int pb_setup_noalloc(pb_ctx* ctx);  // with ctx->device current

@@ -76,6 +76,15 @@ struct pb_model {
   // decode graph
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  // the sampling decode step (pb_model_generate_sampled): its own graph, the
+  // draw counter and the candidate keys on the device
+  cudaGraph_t sgraph = nullptr;
+  cudaGraphExec_t sexec = nullptr;
+  int s_topk = 0;
+  double s_temp = 0.0;
+  uint64_t s_seed = 0;
+  uint64_t* samp_ctr = nullptr;
+  uint64_t* samp_cand = nullptr;
   int launches_per_step = 0;
   float* h_logits_pinned = nullptr;
   int* h_io_pinned = nullptr;
@@ -123,8 +132,12 @@ static int ensure_act(pb_model* m, int M) {
 static void free_graph(pb_model* m) {
   if (m->exec) cudaGraphExecDestroy(m->exec);
   if (m->graph) cudaGraphDestroy(m->graph);
+  if (m->sexec) cudaGraphExecDestroy(m->sexec);
+  if (m->sgraph) cudaGraphDestroy(m->sgraph);
   m->exec = nullptr;
   m->graph = nullptr;
+  m->sexec = nullptr;
+  m->sgraph = nullptr;
 }
 
 extern "C" int pb_model_free(pb_model* m) {
@@ -132,6 +145,8 @@ extern "C" int pb_model_free(pb_model* m) {
   pb_ctx* ctx = m->ctx;
   if (ctx) pb_wait(ctx);
   free_graph(m);
+  cudaFree(m->samp_ctr);
+  cudaFree(m->samp_cand);
   pb_qmat_free(nullptr, m->emb);
   pb_qmat_free(nullptr, m->head);
   for (auto* p : m->qkv) pb_qmat_free(nullptr, p);
@@ -736,6 +751,84 @@ extern "C" int pb_model_generate(pb_model* m, const int* prompt, int n_prompt, i
     next = nx;
     if (cnt < cap) out[cnt++] = next;
     if (next == eos_id) break;
+  }
+  if (n_out) *n_out = cnt;
+  return PB_OK;
+}
+
+// Decode step with top-K sampling in place of the greedy step end: the head
+// writes the logits, k_sample_cand / k_sample_pick draw the next token with
+// the device counter, advance the position and record the token.
+static int ensure_sample_buffers(pb_model* m) {
+  if (m->samp_ctr) return PB_OK;
+  PB_TRY_CUDA(m->ctx, cudaMalloc(&m->samp_ctr, 8));
+  PB_TRY_CUDA(m->ctx, cudaMalloc(&m->samp_cand, pb_sample_cand_count(m->c.vocab, 256) * 8));
+  return PB_OK;
+}
+
+static int ensure_sample_graph(pb_model* m, int top_k, double temperature, uint64_t seed) {
+  pb_ctx* ctx = m->ctx;
+  PB_TRY(ensure_sample_buffers(m));
+  if (m->sexec && m->s_topk == top_k && m->s_temp == temperature && m->s_seed == seed) return PB_OK;
+  if (m->sexec) cudaGraphExecDestroy(m->sexec);
+  if (m->sgraph) cudaGraphDestroy(m->sgraph);
+  m->sexec = nullptr;
+  m->sgraph = nullptr;
+  PB_TRY(ensure_act(m, 1));
+  PB_TRY_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = launch_embed(m, m->tok_dev, 1);
+  for (int l = 0; l < m->c.n_layers && rc == PB_OK; ++l) rc = run_layer(m, l, 1, 0, true);
+  if (rc == PB_OK) rc = launch_head(m, m->x);
+  if (rc == PB_OK)
+    rc = pb_launch_sample(ctx, m->logits, m->c.vocab, top_k, temperature, seed, 0, m->samp_ctr, m->samp_cand,
+                          m->tok_dev, m->tok_dev + 1, m->hist, m->c.seq_len + 1, m->key);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+  if (rc != PB_OK) { if (g) cudaGraphDestroy(g); return rc; }
+  if (e != cudaSuccess) return pb_cuda_error(ctx, e, "sampling graph capture");
+  e = cudaGraphInstantiate(&m->sexec, g, 0);
+  if (e != cudaSuccess) { cudaGraphDestroy(g); return pb_cuda_error(ctx, e, "sampling graph instantiate"); }
+  m->sgraph = g;
+  m->s_topk = top_k;
+  m->s_temp = temperature;
+  m->s_seed = seed;
+  return PB_OK;
+}
+
+extern "C" int pb_model_generate_sampled(pb_model* m, const int* prompt, int n_prompt, int max_tokens, int eos_id,
+                                         int top_k, double temperature, uint64_t seed, int* out, int cap, int* n_out) {
+  if (!m || !prompt || n_prompt <= 0 || !out || cap <= 0) return PB_ERR_ARG;
+  pb_ctx* ctx = m->ctx;
+  if (top_k <= 0 || top_k > 256 || !(temperature > 0.0))
+    return pb_set_error(ctx, PB_ERR_ARG, "sampling needs 0 < topK <= 256 and temperature > 0");
+  if (n_out) *n_out = 0;
+  PB_TRY(ensure_sample_buffers(m));
+  PB_TRY(pb_model_reset_cache(m));
+  PB_TRY_CUDA(ctx, cudaMemsetAsync(m->samp_ctr, 0, 8, ctx->stream));
+  int cnt = 0;
+  for (int i = 0; i < n_prompt && cnt < cap; ++i) out[cnt++] = prompt[i];
+  // the prompt's logits (llama-streaming.js:925-930), then draw 0
+  PB_TRY(pb_model_forward(m, prompt, n_prompt, 0, nullptr));
+  PB_TRY(pb_launch_sample(ctx, m->logits, m->c.vocab, top_k, temperature, seed, 0, m->samp_ctr, m->samp_cand,
+                          m->tok_dev, nullptr, nullptr, 0, nullptr));
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->h_io_pinned + 2, m->tok_dev, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  PB_TRY(pb_wait(ctx));
+  int next = m->h_io_pinned[2];
+  int pos = n_prompt;
+  if (cnt < cap) out[cnt++] = next;
+  // recorded after the prefill, which may have regrown the activations
+  if (max_tokens > 1) PB_TRY(ensure_sample_graph(m, top_k, temperature, seed));
+  for (int i = 1; i < max_tokens; ++i) {
+    if (next == eos_id || pos >= m->c.seq_len) break;
+    m->h_io_pinned[0] = next;
+    m->h_io_pinned[1] = pos;
+    PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->tok_dev, m->h_io_pinned, 8, cudaMemcpyHostToDevice, ctx->stream));
+    PB_TRY_CUDA(ctx, cudaGraphLaunch(m->sexec, ctx->stream));
+    PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->h_io_pinned + 2, m->tok_dev, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    PB_TRY(pb_wait(ctx));
+    next = m->h_io_pinned[2];
+    ++pos;
+    if (cnt < cap) out[cnt++] = next;
   }
   if (n_out) *n_out = cnt;
   return PB_OK;

@@ -11,6 +11,7 @@ decode step is one replayed CUDA graph.
 from __future__ import annotations
 
 import ctypes
+import os
 import time
 from dataclasses import dataclass
 from typing import Optional
@@ -123,6 +124,15 @@ class _DeviceModel:
                                                   N.ptr(out), out.size, ctypes.byref(n)))
         return out[:n.value].tolist()
 
+    def generate_sampled(self, prompt, max_tokens: int, eos_id: int, top_k: int, temperature: float, seed: int):
+        p = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(p.size + max_tokens + 1, np.int32)
+        n = ctypes.c_int()
+        self.ctx._check(N.lib().pb_model_generate_sampled(self.h, N.ptr(p), p.size, int(max_tokens), int(eos_id),
+                                                          int(top_k), float(temperature), seed & (2 ** 64 - 1),
+                                                          N.ptr(out), out.size, ctypes.byref(n)))
+        return out[:n.value].tolist()
+
     def reset_cache(self):
         self.ctx._check(N.lib().pb_model_reset_cache(self.h))
 
@@ -148,18 +158,22 @@ def argmax(logits) -> int:
     return idx
 
 
-def sample(logits, topK: int = 40, temperature: float = 0.8, rng: Optional[np.random.Generator] = None) -> int:
-    """llama-streaming.js:868-894 top-K + temperature sampling (host side)."""
-    rng = rng or np.random.default_rng()
-    scaled = np.asarray(logits, np.float64) / temperature
-    order = np.argsort(-scaled, kind="stable")[:topK]
-    vals = scaled[order]
-    e = np.exp(vals - vals[0])
-    p = e / e.sum()
-    r = rng.random()
-    c = np.cumsum(p)
-    i = int(np.searchsorted(c, r, side="left"))
-    return int(order[min(i, len(order) - 1)])
+def sample(ctx: N.Context, logits, topK: int = 40, temperature: float = 0.8, seed: Optional[int] = None,
+           counter: int = 0) -> int:
+    """llama-streaming.js:868-894 top-K + temperature sampling, on the device
+    (pb_sample_topk).  The reference draws r from the unseeded Math.random;
+    here r = pb_sample_uniform(seed, counter), a fresh seed when none is given."""
+    arr = np.ascontiguousarray(logits, np.float32)
+    if seed is None:
+        seed = int.from_bytes(os.urandom(8), "little")
+    d = ctx.to_device(arr)
+    t = ctx.alloc(16)
+    ctx._check(N.lib().pb_sample_topk(ctx.h, d.ptr, arr.size, int(topK), float(temperature), int(seed) & (2 ** 64 - 1),
+                                      int(counter), t.ptr))
+    tok = int(t.download(np.int32, 1)[0])
+    d.free()
+    t.free()
+    return tok
 
 
 class _RuntimeBase:
@@ -203,7 +217,7 @@ class _RuntimeBase:
         return argmax(logits)
 
     def sample(self, logits, topK: int = 40, temperature: float = 0.8) -> int:
-        return sample(logits, topK, temperature)
+        return sample(self.ctx, logits, topK, temperature)
 
     def generate(self, promptTokens, maxTokens: int = 50, opts: Optional[dict] = None):
         """llama-streaming.js:914-970.  Greedy runs the device loop (argmax on
@@ -222,6 +236,16 @@ class _RuntimeBase:
                     "avgLayers": self.config.nLayers, "earlyExits": 0}
         temperature = opts.get("temperature") or 0.8
         topK = opts.get("topK") or 40
+        if not greedy and on_token is None and self.KIND == N.MODEL_STREAMING_Q4:
+            seed = opts.get("seed")
+            if seed is None:
+                seed = int.from_bytes(os.urandom(8), "little")
+            toks = self.model.generate_sampled(promptTokens, maxTokens, eos, int(topK), float(temperature), int(seed))
+            dt = time.perf_counter() - t0
+            generated = len(toks) - len(promptTokens)
+            return {"tokens": toks, "generated": generated, "prefillTime": None,
+                    "decodeTime": dt * 1000, "tokPerSec": max(generated - 1, 1) / max(dt, 1e-9),
+                    "avgLayers": self.config.nLayers, "earlyExits": 0}
         self.resetCache()
         allTokens = list(promptTokens)
         out = self.forward(promptTokens, 0)
