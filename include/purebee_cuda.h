@@ -271,6 +271,22 @@ int pb_model_generate(pb_model* m, const int* prompt_host, int n_prompt, int max
  * the token already in the model's token slot at `pos0`; tokens stay on the
  * device (out_dev may be NULL). */
 int pb_model_decode_loop(pb_model* m, int pos0, int steps, int* out_dev);
+/* forward(tokenIds, startPos, {maxLayers}) (llama-streaming.js:738-815):
+ * only the first max_layers layers run (0: all), then the final norm and head;
+ * the layers actually run (early exit included) go to layers_used. */
+int pb_model_forward_ex(pb_model* m, const int* tokens_host, int n, int start_pos, int max_layers, float* logits_host,
+                        int* layers_used);
+int pb_model_decode_ex(pb_model* m, int token, int pos, int max_layers, int* next_host, float* logits_host,
+                       int* layers_used);
+/* options.earlyExitThreshold / earlyExitInterval (llama-streaming.js:202-203):
+ * single-token steps check the top-8 confidence of the partial hidden state
+ * every `interval` layers and stop at or above the threshold (0: off).  The
+ * reference's check throws (an undefined `candidates`, :717); this is the
+ * intended rule with tailCount = V - 8. */
+int pb_model_set_early_exit(pb_model* m, double threshold, int interval);
+int pb_model_exit_stats(const pb_model* m, int* layers_used, int* last_exit_layer, int* early_exits);
+/* sample(logits, topK, temperature) over the logits of the last forward. */
+int pb_model_sample(pb_model* m, int top_k, double temperature, uint64_t seed, uint64_t counter, int* token_host);
 int pb_model_set_token(pb_model* m, int token);
 int pb_model_reset_cache(pb_model* m);             /* llama-streaming.js:828-837 */
 int pb_model_rollback_cache(pb_model* m, int pos); /* llama-streaming.js:845-862 */

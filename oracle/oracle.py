@@ -106,6 +106,10 @@ def lib():
         "orc_model_set_head": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
         "orc_sample": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_double]),
         "orc_sample_uniform": (ctypes.c_double, [ctypes.c_uint64, ctypes.c_uint64]),
+        "orc_forward_ex": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_double, ctypes.c_int, ctypes.c_void_p,
+                                          ctypes.POINTER(ctypes.c_int)]),
+        "orc_exit_prob": (ctypes.c_double, [ctypes.c_void_p, ctypes.c_int]),
         "orc_forward": (ctypes.c_int, [ctypes.c_void_p, I32P, ctypes.c_int, ctypes.c_int, F32P]),
         "orc_generate": (ctypes.c_int, [ctypes.c_void_p, I32P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                         I32P, ctypes.c_int]),
@@ -340,6 +344,11 @@ def sample(logits, topK, temperature, r):
     return int(lib().orc_sample(x.ctypes.data, x.size, topK, temperature, r))
 
 
+def exit_prob(logits):
+    x = _f32(logits)
+    return float(lib().orc_exit_prob(x.ctypes.data, x.size))
+
+
 def sample_uniform(seed, counter):
     return float(lib().orc_sample_uniform(seed, counter))
 
@@ -433,6 +442,17 @@ class Model:
         if rc != 0:
             raise ValueError(f"orc_forward failed ({rc})")
         return logits
+
+    def forward_ex(self, tokens, start_pos, max_layers=0, exit_threshold=0.0, exit_interval=4):
+        """forward(tokens, startPos, {maxLayers}) with the early exit; returns (logits, layersUsed)."""
+        toks = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(self.cfg.vocab, np.float32)
+        used = ctypes.c_int()
+        rc = lib().orc_forward_ex(self.h, toks.ctypes.data, toks.size, start_pos, max_layers, exit_threshold,
+                                  exit_interval, logits.ctypes.data, ctypes.byref(used))
+        if rc != 0:
+            raise ValueError(f"orc_forward_ex failed ({rc})")
+        return logits, used.value
 
     def generate(self, prompt, max_tokens, eos_id=2):
         p = np.ascontiguousarray(prompt, np.int32)

@@ -1028,31 +1028,81 @@ int orc_model_set_head(orc_model* m, int emb_type, const uint8_t* raw) {
   return 0;
 }
 
-int orc_forward(orc_model* m, const int* tokens, int n, int start_pos, float* logits) {
+typedef struct { double v; int i; } orc_vi;
+static int orc_vi_cmp(const void* a, const void* b) {
+  const orc_vi* x = (const orc_vi*)a;
+  const orc_vi* y = (const orc_vi*)b;
+  if (x->v != y->v) return x->v > y->v ? -1 : 1; /* value descending */
+  return x->i - y->i;                            /* stable: lower index first */
+}
+
+/* final RMSNorm and LM head of one hidden state (llama-streaming.js:616-679). */
+static void orc_head(orc_model* m, const float* x, float* logits) {
+  const orc_config* c = &m->c;
+  float* hn = (float*)malloc(sizeof(float) * c->dim);
+  orc_rmsnorm(x, 1, c->dim, m->rms_final, c->eps, hn);
+  if (c->kind == ORC_KIND_LLAMA_Q8A) {
+    hd_args a = {hn, m->emb_f32, c->dim, logits};
+    orc_parallel_rows(c->vocab, head_double_rows, &a);
+  } else {
+    /* llama-streaming.js:640-642 -> wasm-q4.js:798-839 (batch_dot) */
+    orc_batch_dot(hn, m->head_f32 ? m->head_f32 : m->emb_f32, c->vocab, c->dim, logits);
+  }
+  free(hn);
+}
+
+/* _checkEarlyExit's confidence (llama-streaming.js:695-725), with the tail
+ * count the code means (logits.length - topK; the reference reads an
+ * undefined `candidates` there and throws). */
+double orc_exit_prob(const float* logits, int V) {
+  orc_vi* a = (orc_vi*)malloc(sizeof(orc_vi) * (size_t)(V > 0 ? V : 1));
+  int n = 0;
+  for (int i = 0; i < V; ++i)
+    if (logits[i] == logits[i]) { a[n].v = (double)logits[i]; a[n].i = i; ++n; }
+  qsort(a, (size_t)n, sizeof(orc_vi), orc_vi_cmp);
+  const int top = n < 8 ? n : 8;
+  double s = 0;
+  for (int i = 0; i < top; ++i) s += exp(a[i].v - a[0].v);
+  const int tail = V - 8 > 0 ? V - 8 : 0;
+  s += (double)tail * exp(-20.0);
+  free(a);
+  return exp(0.0) / s;
+}
+
+/* forward(tokenIds, startPos, {maxLayers}) with the early exit of
+ * llama-streaming.js:746-803 (single tokens, every `interval` layers, not
+ * after the last layer). */
+int orc_forward_ex(orc_model* m, const int* tokens, int n, int start_pos, int max_layers, double exit_threshold,
+                   int exit_interval, float* logits, int* layers_used) {
   const orc_config* c = &m->c;
   int dim = c->dim;
   if (n <= 0 || start_pos < 0 || start_pos + n > c->seq_len) return -1;
   for (int i = 0; i < n; ++i)
     if (tokens[i] < 0 || tokens[i] >= c->vocab) return -2;
+  const int L = max_layers <= 0 || max_layers > c->n_layers ? c->n_layers : max_layers;
+  const int interval = exit_interval > 0 ? exit_interval : 4;
+  const int early = exit_threshold > 0 && n == 1;
   float* x = (float*)malloc(sizeof(float) * (size_t)n * dim);
   for (int i = 0; i < n; ++i) memcpy(x + (size_t)i * dim, m->emb_f32 + (size_t)tokens[i] * dim, sizeof(float) * dim);
-  for (int l = 0; l < c->n_layers; ++l) {
+  int used = 0, exited = 0;
+  for (int l = 0; l < L && !exited; ++l) {
     if (c->kind == ORC_KIND_LLAMA_Q8A) run_layer_q8a(m, l, x, n, start_pos);
     else if (n == 1) run_layer_q4(m, l, x, start_pos);
     else run_layer_prefill(m, l, x, n, start_pos);
+    ++used;
+    if (early && l < c->n_layers - 1 && (l + 1) % interval == 0) {
+      orc_head(m, x, logits);
+      if (orc_exit_prob(logits, c->vocab) >= exit_threshold) exited = 1;
+    }
   }
-  float* hn = (float*)malloc(sizeof(float) * dim);
-  orc_rmsnorm(x + (size_t)(n - 1) * dim, 1, dim, m->rms_final, c->eps, hn);
-  if (c->kind == ORC_KIND_LLAMA_Q8A) {
-    hd_args a = {hn, m->emb_f32, dim, logits};
-    orc_parallel_rows(c->vocab, head_double_rows, &a);
-  } else {
-    /* llama-streaming.js:640-642 -> wasm-q4.js:798-839 (batch_dot) */
-    orc_batch_dot(hn, m->head_f32 ? m->head_f32 : m->emb_f32, c->vocab, dim, logits);
-  }
-  free(hn);
+  if (!exited) orc_head(m, x + (size_t)(n - 1) * dim, logits);
+  if (layers_used) *layers_used = used;
   free(x);
   return 0;
+}
+
+int orc_forward(orc_model* m, const int* tokens, int n, int start_pos, float* logits) {
+  return orc_forward_ex(m, tokens, n, start_pos, 0, 0.0, 0, logits, NULL);
 }
 
 int orc_generate(orc_model* m, const int* prompt, int n_prompt, int max_tokens, int eos_id, int* out, int cap) {
@@ -1077,13 +1127,6 @@ int orc_generate(orc_model* m, const int* prompt, int n_prompt, int max_tokens, 
 }
 
 /* ---- sampling (llama-streaming.js:868-894) ---------------------------- */
-typedef struct { double v; int i; } orc_vi;
-static int orc_vi_cmp(const void* a, const void* b) {
-  const orc_vi* x = (const orc_vi*)a;
-  const orc_vi* y = (const orc_vi*)b;
-  if (x->v != y->v) return x->v > y->v ? -1 : 1; /* value descending */
-  return x->i - y->i;                            /* stable: lower index first */
-}
 
 /* sample(logits, topK, temperature) with the uniform draw r given (the
  * reference's Math.random()).  NaN logits are left out of the ranking. */

@@ -122,6 +122,11 @@ int orc_sample(const float* logits, int V, int topK, double temperature, double 
 double orc_sample_uniform(uint64_t seed, uint64_t counter);
 /* forward(tokens, startPos) -> logits[vocab] (llama-streaming.js:738-815, llama.js:204-371) */
 int orc_forward(orc_model* m, const int* tokens, int n, int start_pos, float* logits);
+/* forward(tokenIds, startPos, {maxLayers}) with the early exit
+ * (llama-streaming.js:746-803); exit_threshold 0 turns it off. */
+int orc_forward_ex(orc_model* m, const int* tokens, int n, int start_pos, int max_layers, double exit_threshold,
+                   int exit_interval, float* logits, int* layers_used);
+double orc_exit_prob(const float* logits, int V);
 /* generate, greedy (llama-streaming.js:914-970, llama.js:452-505); returns tokens written */
 int orc_generate(orc_model* m, const int* prompt, int n_prompt, int max_tokens, int eos_id,
                  int* out_tokens, int out_cap);

@@ -106,6 +106,11 @@ SIGNATURES = {
     "pb_model_init_synthetic": (I, [V, U64, D]),
     "pb_model_set_tensor": (I, [V, I, I, V, SZ]),
     "pb_model_attach_head": (I, [V, I]),
+    "pb_model_forward_ex": (I, [V, V, I, I, I, V, ctypes.POINTER(I)]),
+    "pb_model_decode_ex": (I, [V, I, I, I, ctypes.POINTER(I), V, ctypes.POINTER(I)]),
+    "pb_model_set_early_exit": (I, [V, D, I]),
+    "pb_model_exit_stats": (I, [V, ctypes.POINTER(I), ctypes.POINTER(I), ctypes.POINTER(I)]),
+    "pb_model_sample": (I, [V, I, D, U64, U64, ctypes.POINTER(I)]),
     "pb_sample_topk": (I, [V, V, I, I, D, U64, U64, V]),
     "pb_sample_uniform": (D, [U64, U64]),
     "pb_model_generate_sampled": (I, [V, V, I, I, I, I, D, U64, V, I, ctypes.POINTER(I)]),

@@ -288,4 +288,5 @@ size_t pb_sample_cand_count(int V, int K);
 int pb_launch_sample(pb_ctx* ctx, const float* logits, int V, int K, double temperature, uint64_t seed,
                      uint64_t counter, uint64_t* ctr_dev, uint64_t* cand, int* tok_dev, int* pos_dev, int* hist,
                      int hist_len, unsigned long long* key_reset);
+int pb_launch_exit_prob(pb_ctx* ctx, const float* logits, int V, uint64_t* cand, double* prob_dev);
 int pb_setup_noalloc(pb_ctx* ctx);  // with ctx->device current

@@ -85,6 +85,15 @@ struct pb_model {
   uint64_t s_seed = 0;
   uint64_t* samp_ctr = nullptr;
   uint64_t* samp_cand = nullptr;
+  int* samp_tok = nullptr;
+  double* exit_prob = nullptr;
+  // early exit (llama-streaming.js:202-203, :746-789) and layer-limited
+  // decode steps (forward(..., {maxLayers}), the speculative draft)
+  double exit_threshold = 0.0;
+  int exit_interval = 4;
+  int layers_used = 0, last_exit_layer = -1, early_exits = 0;
+  std::vector<cudaGraph_t> lgraph;  // decode steps over the first L layers, index L
+  std::vector<cudaGraphExec_t> lexec;
   int launches_per_step = 0;
   float* h_logits_pinned = nullptr;
   int* h_io_pinned = nullptr;
@@ -138,6 +147,12 @@ static void free_graph(pb_model* m) {
   m->graph = nullptr;
   m->sexec = nullptr;
   m->sgraph = nullptr;
+  for (auto& e : m->lexec)
+    if (e) cudaGraphExecDestroy(e);
+  for (auto& g : m->lgraph)
+    if (g) cudaGraphDestroy(g);
+  m->lexec.clear();
+  m->lgraph.clear();
 }
 
 extern "C" int pb_model_free(pb_model* m) {
@@ -147,6 +162,8 @@ extern "C" int pb_model_free(pb_model* m) {
   free_graph(m);
   cudaFree(m->samp_ctr);
   cudaFree(m->samp_cand);
+  cudaFree(m->samp_tok);
+  cudaFree(m->exit_prob);
   pb_qmat_free(nullptr, m->emb);
   pb_qmat_free(nullptr, m->head);
   for (auto* p : m->qkv) pb_qmat_free(nullptr, p);
@@ -628,13 +645,22 @@ static int launch_head(pb_model* m, const float* last_x) {
 }
 
 // Enqueue one decode step that reads token and position from m->tok_dev.
-static int enqueue_decode_step(pb_model* m) {
+static int enqueue_decode_step(pb_model* m, int layers) {
   pb_ctx* ctx = m->ctx;
   PB_TRY(launch_embed(m, m->tok_dev, 1));
-  for (int l = 0; l < m->c.n_layers; ++l) PB_TRY(run_layer(m, l, 1, 0, true));
+  for (int l = 0; l < layers; ++l) PB_TRY(run_layer(m, l, 1, 0, true));
   PB_TRY(launch_head(m, m->x));
   k_step_end<<<1, 32, 0, ctx->stream>>>(m->key, m->tok_dev, m->tok_dev + 1, m->hist, m->c.seq_len + 1);
   PB_LAUNCHED(ctx, "k_step_end");
+  return PB_OK;
+}
+
+static int ensure_sample_buffers(pb_model* m) {
+  if (m->samp_ctr) return PB_OK;
+  PB_TRY_CUDA(m->ctx, cudaMalloc(&m->samp_ctr, 8));
+  PB_TRY_CUDA(m->ctx, cudaMalloc(&m->samp_cand, pb_sample_cand_count(m->c.vocab, 256) * 8));
+  PB_TRY_CUDA(m->ctx, cudaMalloc(&m->samp_tok, 16));
+  PB_TRY_CUDA(m->ctx, cudaMalloc(&m->exit_prob, 16));
   return PB_OK;
 }
 
@@ -644,7 +670,7 @@ static int ensure_graph(pb_model* m) {
   PB_TRY(ensure_act(m, 1));
   int64_t before = ctx->launches;
   PB_TRY_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
-  int rc = enqueue_decode_step(m);
+  int rc = enqueue_decode_step(m, m->c.n_layers);
   cudaGraph_t g = nullptr;
   cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
   if (rc != PB_OK) { if (g) cudaGraphDestroy(g); return rc; }
@@ -656,7 +682,8 @@ static int ensure_graph(pb_model* m) {
   return PB_OK;
 }
 
-extern "C" int pb_model_forward(pb_model* m, const int* tokens, int n, int start_pos, float* logits_host) {
+extern "C" int pb_model_forward_ex(pb_model* m, const int* tokens, int n, int start_pos, int max_layers,
+                                   float* logits_host, int* layers_used) {
   if (!m || !tokens || n <= 0) return PB_ERR_ARG;
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
@@ -666,12 +693,16 @@ extern "C" int pb_model_forward(pb_model* m, const int* tokens, int n, int start
     if (tokens[i] < 0 || tokens[i] >= c.vocab) return pb_set_error(ctx, PB_ERR_ARG, "token %d out of range", tokens[i]);
   if (n == 1) {  // the graph-captured decode step
     int next;
-    return pb_model_decode(m, tokens[0], start_pos, &next, logits_host);
+    return pb_model_decode_ex(m, tokens[0], start_pos, max_layers, &next, logits_host, layers_used);
   }
+  const int L = max_layers <= 0 || max_layers > c.n_layers ? c.n_layers : max_layers;
   PB_TRY(ensure_act(m, n));
   PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->toks, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
   PB_TRY(launch_embed(m, m->toks, n));
-  for (int l = 0; l < c.n_layers; ++l) PB_TRY(run_layer(m, l, n, start_pos, false));
+  for (int l = 0; l < L; ++l) PB_TRY(run_layer(m, l, n, start_pos, false));
+  m->layers_used = L;
+  m->last_exit_layer = L - 1;
+  if (layers_used) *layers_used = L;
   PB_TRY(launch_head(m, m->x + (size_t)(n - 1) * c.dim));
   // leave the greedy token in the token slot, as a decode step would
   m->h_io_pinned[0] = 0;
@@ -686,22 +717,140 @@ extern "C" int pb_model_forward(pb_model* m, const int* tokens, int n, int start
   return pb_wait(ctx);
 }
 
-extern "C" int pb_model_decode(pb_model* m, int token, int pos, int* next_host, float* logits_host) {
+extern "C" int pb_model_forward(pb_model* m, const int* tokens, int n, int start_pos, float* logits_host) {
+  return pb_model_forward_ex(m, tokens, n, start_pos, 0, logits_host, nullptr);
+}
+
+extern "C" int pb_model_set_early_exit(pb_model* m, double threshold, int interval) {
+  if (!m) return PB_ERR_ARG;
+  m->exit_threshold = threshold > 0.0 ? threshold : 0.0;  // options.earlyExitThreshold || 0
+  m->exit_interval = interval > 0 ? interval : 4;          // options.earlyExitInterval || 4
+  return PB_OK;
+}
+
+extern "C" int pb_model_exit_stats(const pb_model* m, int* layers_used, int* last_exit_layer, int* early_exits) {
+  if (!m) return PB_ERR_ARG;
+  if (layers_used) *layers_used = m->layers_used;
+  if (last_exit_layer) *last_exit_layer = m->last_exit_layer;
+  if (early_exits) *early_exits = m->early_exits;
+  return PB_OK;
+}
+
+// sample(logits, topK, temperature) over the logits of the model's last
+// forward, on the device; the draw is pb_sample_uniform(seed, counter).
+extern "C" int pb_model_sample(pb_model* m, int top_k, double temperature, uint64_t seed, uint64_t counter,
+                               int* token_host) {
+  if (!m || !token_host) return PB_ERR_ARG;
+  pb_ctx* ctx = m->ctx;
+  PB_TRY(ensure_sample_buffers(m));
+  PB_TRY(pb_launch_sample(ctx, m->logits, m->c.vocab, top_k, temperature, seed, counter, nullptr, m->samp_cand,
+                          m->samp_tok, nullptr, nullptr, 0, nullptr));
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->h_io_pinned + 3, m->samp_tok, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  PB_TRY(pb_wait(ctx));
+  *token_host = m->h_io_pinned[3];
+  return PB_OK;
+}
+
+// Decode step graph over the first L < n_layers layers (the draft of
+// self-speculative decoding, forward(..., {maxLayers: L})).
+static int ensure_graph_layers(pb_model* m, int L) {
+  if ((int)m->lexec.size() < m->c.n_layers) {
+    m->lexec.resize(m->c.n_layers, nullptr);
+    m->lgraph.resize(m->c.n_layers, nullptr);
+  }
+  if (m->lexec[L]) return PB_OK;
+  pb_ctx* ctx = m->ctx;
+  PB_TRY(ensure_act(m, 1));
+  if ((int)m->lexec.size() < m->c.n_layers) {  // ensure_act may have dropped every graph
+    m->lexec.resize(m->c.n_layers, nullptr);
+    m->lgraph.resize(m->c.n_layers, nullptr);
+  }
+  PB_TRY_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_decode_step(m, L);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+  if (rc != PB_OK) { if (g) cudaGraphDestroy(g); return rc; }
+  if (e != cudaSuccess) return pb_cuda_error(ctx, e, "draft graph capture");
+  e = cudaGraphInstantiate(&m->lexec[L], g, 0);
+  if (e != cudaSuccess) { cudaGraphDestroy(g); return pb_cuda_error(ctx, e, "draft graph instantiate"); }
+  m->lgraph[L] = g;
+  return PB_OK;
+}
+
+// One decode step with the early-exit check (llama-streaming.js:767-803):
+// after every `exit_interval` layers (not after the last) the final norm and
+// head run on the hidden state and k_exit_prob scores the top-8 confidence;
+// at or above the threshold those logits are the step's.  The host reads the
+// confidence at each check, so this step runs without a recorded graph.
+static int decode_early_exit(pb_model* m, int L) {
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  PB_TRY(ensure_act(m, 1));
+  PB_TRY(ensure_sample_buffers(m));
+  PB_TRY(launch_embed(m, m->tok_dev, 1));
+  int used = 0;
+  bool exited = false;
+  double* prob_host = reinterpret_cast<double*>(m->h_io_pinned + 6);
+  for (int l = 0; l < L && !exited; ++l) {
+    PB_TRY(run_layer(m, l, 1, 0, true));
+    ++used;
+    if (l < c.n_layers - 1 && (l + 1) % m->exit_interval == 0) {
+      PB_TRY_CUDA(ctx, cudaMemsetAsync(m->key, 0, 8, ctx->stream));
+      PB_TRY(launch_head(m, m->x));
+      PB_TRY(pb_launch_exit_prob(ctx, m->logits, c.vocab, m->samp_cand, m->exit_prob));
+      PB_TRY_CUDA(ctx, cudaMemcpyAsync(prob_host, m->exit_prob, 8, cudaMemcpyDeviceToHost, ctx->stream));
+      PB_TRY(pb_wait(ctx));
+      if (*prob_host >= m->exit_threshold) {
+        exited = true;
+        ++m->early_exits;
+        m->last_exit_layer = l;
+      }
+    }
+  }
+  if (!exited) {
+    PB_TRY_CUDA(ctx, cudaMemsetAsync(m->key, 0, 8, ctx->stream));
+    PB_TRY(launch_head(m, m->x));
+    m->last_exit_layer = used - 1;
+  }
+  m->layers_used = used;
+  k_step_end<<<1, 32, 0, ctx->stream>>>(m->key, m->tok_dev, m->tok_dev + 1, m->hist, c.seq_len + 1);
+  PB_LAUNCHED(ctx, "k_step_end");
+  return PB_OK;
+}
+
+extern "C" int pb_model_decode_ex(pb_model* m, int token, int pos, int max_layers, int* next_host, float* logits_host,
+                                  int* layers_used) {
   if (!m) return PB_ERR_ARG;
   pb_ctx* ctx = m->ctx;
   if (pos < 0 || pos >= m->c.seq_len) return pb_set_error(ctx, PB_ERR_ARG, "position %d outside the cache", pos);
   if (token < 0 || token >= m->c.vocab) return pb_set_error(ctx, PB_ERR_ARG, "token %d out of range", token);
-  PB_TRY(ensure_graph(m));
+  const int n = m->c.n_layers;
+  const int L = max_layers <= 0 || max_layers > n ? n : max_layers;  // Math.min(maxLayers, nLayers)
+  if (m->exit_threshold <= 0.0) {
+    if (L == n) PB_TRY(ensure_graph(m));
+    else PB_TRY(ensure_graph_layers(m, L));
+  }
   m->h_io_pinned[0] = token;
   m->h_io_pinned[1] = pos;
   PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->tok_dev, m->h_io_pinned, 8, cudaMemcpyHostToDevice, ctx->stream));
-  PB_TRY_CUDA(ctx, cudaGraphLaunch(m->exec, ctx->stream));
+  if (m->exit_threshold > 0.0) {
+    PB_TRY(decode_early_exit(m, L));
+  } else {
+    PB_TRY_CUDA(ctx, cudaGraphLaunch(L == n ? m->exec : m->lexec[L], ctx->stream));
+    m->layers_used = L;
+    m->last_exit_layer = L - 1;
+  }
   PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->h_io_pinned + 2, m->tok_dev, 4, cudaMemcpyDeviceToHost, ctx->stream));
   if (logits_host)
     PB_TRY_CUDA(ctx, cudaMemcpyAsync(logits_host, m->logits, (size_t)m->c.vocab * 4, cudaMemcpyDeviceToHost, ctx->stream));
   PB_TRY(pb_wait(ctx));
   if (next_host) *next_host = m->h_io_pinned[2];
+  if (layers_used) *layers_used = m->layers_used;
   return PB_OK;
+}
+
+extern "C" int pb_model_decode(pb_model* m, int token, int pos, int* next_host, float* logits_host) {
+  return pb_model_decode_ex(m, token, pos, 0, next_host, logits_host, nullptr);
 }
 
 extern "C" int pb_model_set_token(pb_model* m, int token) {
@@ -759,12 +908,6 @@ extern "C" int pb_model_generate(pb_model* m, const int* prompt, int n_prompt, i
 // Decode step with top-K sampling in place of the greedy step end: the head
 // writes the logits, k_sample_cand / k_sample_pick draw the next token with
 // the device counter, advance the position and record the token.
-static int ensure_sample_buffers(pb_model* m) {
-  if (m->samp_ctr) return PB_OK;
-  PB_TRY_CUDA(m->ctx, cudaMalloc(&m->samp_ctr, 8));
-  PB_TRY_CUDA(m->ctx, cudaMalloc(&m->samp_cand, pb_sample_cand_count(m->c.vocab, 256) * 8));
-  return PB_OK;
-}
 
 static int ensure_sample_graph(pb_model* m, int top_k, double temperature, uint64_t seed) {
   pb_ctx* ctx = m->ctx;

@@ -181,8 +181,45 @@ extern "C" int pb_sample_topk(pb_ctx* ctx, const float* logits_dev, int V, int t
                           token_dev, nullptr, nullptr, 0, nullptr);
 }
 
+
+// Early-exit confidence (llama-streaming.js:695-725 _checkEarlyExit): the 8
+// largest logits (ties to the lower index), sumExp = sum_i exp(l_i - max) in
+// order plus max(0, V - 8) * exp(-20) for the tail, topProb = exp(0) / sumExp.
+__global__ void __launch_bounds__(SP_THREADS)
+k_exit_prob(const float* __restrict__ logits, int V, const uint64_t* __restrict__ cand, int n_cand, int n2,
+            double* __restrict__ prob) {
+  extern __shared__ __align__(16) unsigned char sp_raw[];
+  uint64_t* keys = reinterpret_cast<uint64_t*>(sp_raw);
+  pb_pdl_trigger();
+  pb_pdl_wait();
+  for (int i = threadIdx.x; i < n2; i += blockDim.x) keys[i] = i < n_cand ? cand[i] : 0ull;
+  __syncthreads();
+  sp_sort_desc(keys, n2);
+  if (threadIdx.x == 0) {
+    const int top = V < 8 ? V : 8;
+    double s = 0.0, mx = 0.0;
+    for (int i = 0; i < top && keys[i] != 0ull; ++i) {
+      const double v = (double)logits[(int)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull))];
+      if (i == 0) mx = v;
+      s = __dadd_rn(s, exp(__dsub_rn(v, mx)));
+    }
+    const int tail = V - 8 > 0 ? V - 8 : 0;
+    s = __dadd_rn(s, __dmul_rn((double)tail, exp(-20.0)));
+    *prob = __ddiv_rn(exp(0.0), s);
+  }
+}
+
+int pb_launch_exit_prob(pb_ctx* ctx, const float* logits, int V, uint64_t* cand, double* prob_dev) {
+  const int chunks = sp_chunks(V), kc = V < 8 ? V : 8;
+  const int n_cand = chunks * kc, n2 = sp_pow2(n_cand);
+  if ((size_t)n2 * 8 > 200 * 1024) return pb_set_error(ctx, PB_ERR_ARG, "early exit: vocabulary too large");
+  PB_TRY(pb_launch(ctx, "k_sample_cand", true, k_sample_cand, dim3(chunks), dim3(SP_THREADS), 0, logits, V, kc, cand));
+  return pb_launch(ctx, "k_exit_prob", true, k_exit_prob, dim3(1), dim3(SP_THREADS), (size_t)n2 * 8, logits, V,
+                   (const uint64_t*)cand, n_cand, n2, prob_dev);
+}
+
 int pb_setup_sample_kernels(void) {
-  return cudaFuncSetAttribute(k_sample_pick, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) == cudaSuccess
-             ? PB_OK
-             : PB_ERR_CUDA;
+  cudaError_t e = cudaFuncSetAttribute(k_sample_pick, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_exit_prob, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
 }

@@ -103,6 +103,35 @@ class _DeviceModel:
         self.ctx._check(N.lib().pb_model_get_tensor(self.h, layer, which, N.ptr(out), out.nbytes))
         return out
 
+    def forward_ex(self, tokens, start_pos: int, max_layers: int = 0):
+        t = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(self.cfg.vocabSize, np.float32)
+        used = ctypes.c_int()
+        self.ctx._check(N.lib().pb_model_forward_ex(self.h, N.ptr(t), t.size, int(start_pos), int(max_layers),
+                                                    N.ptr(logits), ctypes.byref(used)))
+        return logits, used.value
+
+    def step(self, token: int, pos: int, max_layers: int = 0) -> int:
+        """One decode step (graph replay); the greedy next token, no logits copy."""
+        nxt = ctypes.c_int()
+        self.ctx._check(N.lib().pb_model_decode_ex(self.h, int(token), int(pos), int(max_layers), ctypes.byref(nxt),
+                                                   None, None))
+        return nxt.value
+
+    def sample_last(self, top_k: int, temperature: float, seed: int, counter: int) -> int:
+        tok = ctypes.c_int()
+        self.ctx._check(N.lib().pb_model_sample(self.h, int(top_k), float(temperature), seed & (2 ** 64 - 1),
+                                                int(counter), ctypes.byref(tok)))
+        return tok.value
+
+    def set_early_exit(self, threshold: float, interval: int):
+        self.ctx._check(N.lib().pb_model_set_early_exit(self.h, float(threshold), int(interval)))
+
+    def exit_stats(self):
+        u, l, e = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        self.ctx._check(N.lib().pb_model_exit_stats(self.h, ctypes.byref(u), ctypes.byref(l), ctypes.byref(e)))
+        return u.value, l.value, e.value
+
     def forward_logits(self, tokens, start_pos: int) -> np.ndarray:
         t = np.ascontiguousarray(tokens, np.int32)
         logits = np.empty(self.cfg.vocabSize, np.float32)
@@ -190,6 +219,11 @@ class _RuntimeBase:
         self._loaded = False
         self._layersUsed = 0
         self._totalForwards = 0
+        self._applyOptions(options)
+
+    def _applyOptions(self, options: dict):
+        """llama-streaming.js:202-203: earlyExitThreshold (0: off), earlyExitInterval (4)."""
+        self.model.set_early_exit(options.get("earlyExitThreshold") or 0.0, options.get("earlyExitInterval") or 4)
 
     # -- weights --------------------------------------------------------
     def loadSynthetic(self, seed: int, stdev: float = 0.02):
@@ -206,12 +240,27 @@ class _RuntimeBase:
 
     # -- inference ------------------------------------------------------
     def forward(self, tokenIds, startPos: int = 0, options: Optional[dict] = None):
+        """llama-streaming.js:738-815 forward(tokenIds, startPos, {maxLayers})."""
         if not self._loaded:
             raise RuntimeError("Resident weights not loaded")  # llama-streaming.js:739
-        logits = self.model.forward_logits(tokenIds, startPos)
-        self._layersUsed += self.config.nLayers
+        options = options or {}
+        logits, used = self.model.forward_ex(tokenIds, startPos, int(options.get("maxLayers") or 0))
+        self._layersUsed += used
         self._totalForwards += 1
-        return {"logits": logits, "layersUsed": self.config.nLayers}
+        return {"logits": logits, "layersUsed": used}
+
+    def step(self, token: int, pos: int, maxLayers: int = 0) -> int:
+        """forward([token], pos, {maxLayers}) followed by argmax, both on the
+        device: the greedy next token without copying the logits."""
+        nxt = self.model.step(token, pos, maxLayers)
+        used, _, _ = self.model.exit_stats()
+        self._layersUsed += used
+        self._totalForwards += 1
+        return nxt
+
+    def sampleLast(self, topK: int, temperature: float, seed: int, counter: int) -> int:
+        """sample(logits of the last forward, topK, temperature) on the device."""
+        return self.model.sample_last(topK, temperature, seed, counter)
 
     def argmax(self, logits) -> int:
         return argmax(logits)
@@ -282,9 +331,10 @@ class _RuntimeBase:
 
     @property
     def stats(self):
+        _, last, exits = self.model.exit_stats()
         return {"totalForwards": self._totalForwards,
                 "avgLayers": (self._layersUsed / self._totalForwards) if self._totalForwards else 0,
-                "earlyExits": 0, "lastExitLayer": self.config.nLayers - 1, "launches": self.ctx.launches}
+                "earlyExits": exits, "lastExitLayer": last, "launches": self.ctx.launches}
 
     def shutdown(self):
         self.model.free()
@@ -322,6 +372,7 @@ class StreamingLlamaRuntime(_RuntimeBase):
         rt._loaded = True
         rt._layersUsed = 0
         rt._totalForwards = 0
+        rt._applyOptions(options)
         rt.sharedWeights = head is None
         rt.bosId = meta.get("tokenizer.ggml.bos_token_id", 1)
         rt.eosId = meta.get("tokenizer.ggml.eos_token_id", 2)
