@@ -160,6 +160,11 @@ class GGUFFile:
                                                                       "name": m.get("general.name", "unknown"),
                                                                       "embType": c.emb_type}
 
+    def tokenizer(self):
+        """gguf.js:486-548 GGUFTokenizer from this file's metadata."""
+        from .tokenizer import GGUFTokenizer
+        return GGUFTokenizer(self.metadata)
+
     def close(self):
         if self.h:
             N.lib().pb_gguf_close(self.h)

@@ -364,6 +364,7 @@ class StreamingLlamaRuntime(_RuntimeBase):
             h = ctypes.c_void_p()
             ctx._check(N.lib().pb_model_load_gguf(ctx.h, f.h, seq, ctypes.byref(h)))
             meta = f.metadata
+            tok = f.tokenizer()
         rt = cls.__new__(cls)
         rt.config = cfg
         rt.ctx = ctx
@@ -374,8 +375,9 @@ class StreamingLlamaRuntime(_RuntimeBase):
         rt._totalForwards = 0
         rt._applyOptions(options)
         rt.sharedWeights = head is None
-        rt.bosId = meta.get("tokenizer.ggml.bos_token_id", 1)
-        rt.eosId = meta.get("tokenizer.ggml.eos_token_id", 2)
+        rt.tokenizer = tok
+        rt.bosId = tok.bosId
+        rt.eosId = tok.eosId
         return rt
 
 
