@@ -93,13 +93,39 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 
 }  // namespace
 
+// One TMEM row (weight row `row`) of 32 token columns m0c .. m0c+31 through
+// the epilogue.  Every lane of the warp calls it (the SwiGLU partner row is
+// row ^ 4, lane ^ 4 of the same warp).
+__device__ __forceinline__ void gemm_emit32(const uint32_t (&v)[32], bool zero, int row, int N, int m0c, int M,
+                                            float* __restrict__ C, int ldc, const pb_gemm_epi& epi) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float r = zero ? 0.0f : __uint_as_float(v[j]);
+    const int m = m0c + j;
+    if (epi.mode == PB_GEMM_SWIGLU) {
+      const float partner = __shfl_xor_sync(0xffffffffu, r, 4);
+      if (row < N && m < M && (row & 4) == 0) {
+        const float silu = __fdividef(r, 1.0f + __expf(-r));
+        const float h = __fmul_rn(silu, partner);
+        const size_t o = (size_t)m * (N / 2) + 4 * (row >> 3) + (row & 3);
+        if (epi.h16) epi.h16[o] = __float2half_rn(h);
+        else epi.h32[o] = h;
+      }
+    } else if (row < N && m < M) {
+      float* c = C + (size_t)m * ldc + row;
+      *c = epi.mode == PB_GEMM_ADD ? __fadd_rn(*c, r) : r;
+    }
+  }
+}
+
 // TOK tokens per CTA (MMA N = 64 or 128).  grid.z splits K: CTA z covers K
 // steps [z*kper, (z+1)*kper) and, when gridDim.z > 1, writes its partial tile
 // to C + z*M*ldc (a workspace the reduce kernel sums in order of z).
 template <int TOK>
 __global__ void __launch_bounds__(GM_THREADS, 1)
 k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int layout, int N, int N_pad, int nb,
-             const float* __restrict__ X, int ldx, int M, float* __restrict__ C, int ldc, int kper, int* err) {
+             const float* __restrict__ X, int ldx, int M, float* __restrict__ C, int ldc, int kper, pb_gemm_epi epi,
+             int* err) {
   extern __shared__ __align__(1024) unsigned char gm_raw[];
   __shared__ uint64_t bars[2];
   __shared__ uint32_t tmem_base;
@@ -207,13 +233,7 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
     for (int c0 = 0; c0 < TOK; c0 += 32) {
       uint32_t v[32];
       tmem_ld32(tmem_d + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-      if (row < N) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int m = m0 + c0 + j;
-          if (m < M) C[(size_t)m * ldc + row] = empty_split ? 0.0f : __uint_as_float(v[j]);
-        }
-      }
+      gemm_emit32(v, empty_split, row, N, m0 + c0, M, C, ldc, epi);  // split-K partials always STORE
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -295,7 +315,7 @@ __global__ void k_f32_to_f16(const float* __restrict__ x, int M, int K, int ldx,
 
 __global__ void __launch_bounds__(TG_THREADS, 1)
 k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, int N, int M,
-               int K, float* __restrict__ C, int ldc, int* err) {
+               int K, float* __restrict__ C, int ldc, pb_gemm_epi epi, int* err) {
   extern __shared__ __align__(1024) unsigned char tg_raw[];
   __shared__ uint64_t full[TG_STAGES], empty[TG_STAGES], acc_full;
   __shared__ uint32_t tmem_base;
@@ -348,22 +368,20 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       mma_commit(&empty[s]);
     }
     mma_commit(&acc_full);  // fires when every MMA above has completed
-  } else if (warp >= 4) {
-    const int q = warp - 4;  // TMEM lane quadrant
+  }
+  // epilogue on all eight warps: warps w and w + 4 share TMEM lane quadrant
+  // w % 4 and take one half of the token columns each
+  __syncwarp();
+  {
+    const int q = warp & 3, half = warp >> 2;
     if (pb_mbar_wait(&acc_full, 0, err)) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int row = n0 + q * 32 + lane;
 #pragma unroll 1
-      for (int c0 = 0; c0 < TG_TOK; c0 += 32) {
+      for (int c0 = half * (TG_TOK / 2); c0 < (half + 1) * (TG_TOK / 2); c0 += 32) {
         uint32_t v[32];
         tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-        if (row < N) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int m = m0 + c0 + j;
-            if (m < M) C[(size_t)m * ldc + row] = __uint_as_float(v[j]);
-          }
-        }
+        gemm_emit32(v, false, row, N, m0 + c0, M, C, ldc, epi);
       }
     }
   }
@@ -406,45 +424,71 @@ static int make_map(pb_ctx* ctx, CUtensorMap* map, const void* base, int rows, i
   return PB_OK;
 }
 
-static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc) {
+static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, const __half* Xh, int ldx, int M, float* C,
+                           int ldc, const pb_gemm_epi& epi) {
   const int K = w->K;
-  const size_t wbytes = (size_t)w->N_pad * K * 2, xbytes = (size_t)M * K * 2;
+  const size_t wbytes = (size_t)w->N_pad * K * 2, xbytes = Xh ? 0 : (size_t)M * K * 2;
   const size_t off_x = (wbytes + 1023) & ~(size_t)1023;
   PB_TRY(pb_ensure_gemm_scratch(ctx, off_x + xbytes));
   __half* w16 = reinterpret_cast<__half*>(ctx->gemm_scratch);
-  __half* x16 = reinterpret_cast<__half*>(static_cast<char*>(ctx->gemm_scratch) + off_x);
+  const __half* x16 = Xh;
   const int64_t nblk = (int64_t)w->N_pad * w->nb;
   k_dequant_q4_f16<<<pb_cdiv(nblk, 256), 256, 0, ctx->stream>>>(w->qs, w->d, w->layout, w->nb, nblk, w16);
   PB_LAUNCHED(ctx, "k_dequant_q4_f16");
-  k_f32_to_f16<<<pb_cdiv((int64_t)M * K / 4, 256), 256, 0, ctx->stream>>>(X, M, K, ldx, x16);
-  PB_LAUNCHED(ctx, "k_f32_to_f16");
+  if (!Xh) {  // the activations rounded to f16 once
+    __half* xs = reinterpret_cast<__half*>(static_cast<char*>(ctx->gemm_scratch) + off_x);
+    k_f32_to_f16<<<pb_cdiv((int64_t)M * K / 4, 256), 256, 0, ctx->stream>>>(X, M, K, ldx, xs);
+    PB_LAUNCHED(ctx, "k_f32_to_f16");
+    x16 = xs;
+  }
   CUtensorMap mw, mx;
   PB_TRY(make_map(ctx, &mw, w16, w->N_pad, K, TG_ROWS));
-  PB_TRY(make_map(ctx, &mx, x16, M, K, TG_TOK));
+  PB_TRY(make_map(ctx, &mx, const_cast<__half*>(x16), M, K, TG_TOK));
   dim3 grid(pb_cdiv(w->N, TG_ROWS), pb_cdiv(M, TG_TOK));
   if (grid.y > 65535) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
-  k_gemm_f16_tma<<<grid, TG_THREADS, tg_smem(), ctx->stream>>>(mw, mx, w->N, M, K, C, ldc, ctx->d_err);
+  k_gemm_f16_tma<<<grid, TG_THREADS, tg_smem(), ctx->stream>>>(mw, mx, w->N, M, K, C, ldc, epi, ctx->d_err);
   PB_LAUNCHED(ctx, "k_gemm_f16_tma");
   return PB_OK;
 }
 
-// C[m][n] = sum over z (ascending) of the split-K partials ws[z][m][n].
+// C[m][n] = sum over z (ascending) of the split-K partials ws[z][m][n], then
+// the epilogue: stored, added to C, or (SwiGLU, one thread per output f) the
+// gate and up rows of f summed and combined.
 __global__ void k_splitk_reduce(const float* __restrict__ ws, int splits, int M, int N, float* __restrict__ C,
-                                int ldc) {
-  const int n = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
-  if (n >= N) return;
+                                int ldc, pb_gemm_epi epi) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
+  if (epi.mode == PB_GEMM_SWIGLU) {
+    if (i >= N / 2) return;
+    const int ng = 8 * (i >> 2) + (i & 3), nu = ng + 4;
+    float g = 0.0f, u = 0.0f;
+    for (int z = 0; z < splits; ++z) {
+      g += ws[((size_t)z * M + m) * N + ng];
+      u += ws[((size_t)z * M + m) * N + nu];
+    }
+    const float h = __fdividef(g, 1.0f + __expf(-g)) * u;
+    if (epi.h16) epi.h16[(size_t)m * (N / 2) + i] = __float2half_rn(h);
+    else epi.h32[(size_t)m * (N / 2) + i] = h;
+    return;
+  }
+  if (i >= N) return;
   float acc = 0.0f;
-  for (int z = 0; z < splits; ++z) acc += ws[((size_t)z * M + m) * N + n];
-  C[(size_t)m * ldc + n] = acc;
+  for (int z = 0; z < splits; ++z) acc += ws[((size_t)z * M + m) * N + i];
+  float* c = C + (size_t)m * ldc + i;
+  *c = epi.mode == PB_GEMM_ADD ? __fadd_rn(*c, acc) : acc;
 }
 
+bool pb_gemm_uses_tma(const pb_qmat* w, int M) { return M >= PB_GEMM_TMA_MIN_M && w->K % TG_K == 0; }
+
 int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
-                      size_t ws_bytes) {
-  if (!ctx || !w || !X || !C || M <= 0) return PB_ERR_ARG;
+                      size_t ws_bytes, const pb_gemm_epi* epi_in, const __half* Xh) {
+  const pb_gemm_epi epi = epi_in ? *epi_in : pb_gemm_epi();
+  if (!ctx || !w || !(X || Xh) || M <= 0) return PB_ERR_ARG;
+  if (epi.mode == PB_GEMM_SWIGLU ? (!(epi.h16 || epi.h32) || w->N % 8) : !C) return PB_ERR_ARG;
   if (w->type != PB_TYPE_Q4_0) return pb_set_error(ctx, PB_ERR_ARG, "the tensor-core GEMM needs a Q4_0 matrix");
-  if ((ldx & 3) || ((uintptr_t)X & 15))
+  if (X && ((ldx & 3) || ((uintptr_t)X & 15)))
     return pb_set_error(ctx, PB_ERR_ARG, "X must be 16-byte aligned with a row stride that is a multiple of 4");
-  if (M >= PB_GEMM_TMA_MIN_M && w->K % TG_K == 0) return launch_gemm_tma(ctx, w, X, ldx, M, C, ldc);
+  if (pb_gemm_uses_tma(w, M)) return launch_gemm_tma(ctx, w, X, Xh, ldx, M, C, ldc, epi);
+  if (!X) return pb_set_error(ctx, PB_ERR_ARG, "f16 activations need the TMA path (M >= %d)", PB_GEMM_TMA_MIN_M);
   const int tok = M <= 64 ? 64 : GM_TOK;
   dim3 grid(pb_cdiv(w->N, GM_ROWS), pb_cdiv(M, tok), 1);
   if (grid.y > 65535) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
@@ -467,15 +511,17 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
   grid.z = splits;
   float* dst = splits > 1 ? ws : C;
   const int ldd = splits > 1 ? w->N : ldc;
+  const pb_gemm_epi kepi = splits > 1 ? pb_gemm_epi() : epi;  // split partials are stored, the reduce finishes
   if (tok == 64)
     k_q4_gemm_tc<64><<<grid, GM_THREADS, gm_smem(), ctx->stream>>>(w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, X,
-                                                                  ldx, M, dst, ldd, kper, ctx->d_err);
+                                                                  ldx, M, dst, ldd, kper, kepi, ctx->d_err);
   else
     k_q4_gemm_tc<128><<<grid, GM_THREADS, gm_smem(), ctx->stream>>>(w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, X,
-                                                                   ldx, M, dst, ldd, kper, ctx->d_err);
+                                                                   ldx, M, dst, ldd, kper, kepi, ctx->d_err);
   PB_LAUNCHED(ctx, "k_q4_gemm_tc");
   if (splits > 1) {
-    k_splitk_reduce<<<dim3(pb_cdiv(w->N, 256), M), 256, 0, ctx->stream>>>(ws, splits, M, w->N, C, ldc);
+    const int cols = epi.mode == PB_GEMM_SWIGLU ? w->N / 2 : w->N;
+    k_splitk_reduce<<<dim3(pb_cdiv(cols, 256), M), 256, 0, ctx->stream>>>(ws, splits, M, w->N, C, ldc, epi);
     PB_LAUNCHED(ctx, "k_splitk_reduce");
   }
   return PB_OK;

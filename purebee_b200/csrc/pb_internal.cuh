@@ -270,6 +270,23 @@ struct pb_seq_geo {
   int64_t q = 0, kv = 0, out = 0;
 };
 
+// Epilogues of the tensor-core GEMM (pb_gemm.cu).  The result r[m][n] is
+// stored (STORE), added to C (ADD: the residual x += proj, llama-streaming.js
+// :579-580), or, for a gate|up matrix in the interleave-4 row order, turned
+// into h[m][f] = silu(gate) * up in f32 (SWIGLU) and written as f16 (h16, the
+// next GEMM's operand) or f32 (h32), f = 4 * (n / 8) + n % 4.
+#define PB_GEMM_STORE 0
+#define PB_GEMM_ADD 1
+#define PB_GEMM_SWIGLU 2
+struct pb_gemm_epi {
+  int mode = PB_GEMM_STORE;
+  __half* h16 = nullptr;
+  float* h32 = nullptr;
+};
+int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
+                      size_t ws_bytes, const pb_gemm_epi* epi = nullptr, const __half* Xh = nullptr);
+bool pb_gemm_uses_tma(const pb_qmat* w, int M);  // the f16-operand TMA path (takes Xh)
+
 int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows,
                      const pb_mv_epi* epi);
 int pb_launch_head(pb_ctx* ctx, const pb_qmat* emb, const float* h, float* logits,

@@ -24,9 +24,8 @@ int pb_launch_attn_cached(pb_ctx* ctx, const float* q, int q_stride, const float
 int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc);
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
                           int n_heads, int n_kv, int hd, float* out, int max_len, int nseq, pb_seq_geo geo);
-int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
-                      size_t ws_bytes);
-int pb_launch_attn_prefill_f32(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
+
+int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
                                int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo);
 bool pb_attn_decode_ok(int n_heads, int n_kv, int hd, int max_len);
 bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len);
@@ -1043,8 +1042,8 @@ struct pb_batch {
   int rows_cap = 0;  // activation rows allocated
   int P = 0;         // prompt length of the current batch
   float *kc = nullptr, *vc = nullptr;  // [layer][seq][seq_len][kv]
-  float *x = nullptr, *xn = nullptr, *qkvo = nullptr, *att = nullptr, *guo = nullptr, *hb = nullptr,
-        *proj = nullptr;
+  float *x = nullptr, *xn = nullptr, *qkvo = nullptr, *att = nullptr;
+  float* hb = nullptr;  // SwiGLU output, the down GEMM's operand (f16 on the TMA path)
   float *xl = nullptr, *logits = nullptr;  // [B][dim], [B][V]
   int* toks = nullptr;                     // [rows] token ids (prefill)
   int* next = nullptr;                     // [B] greedy tokens of the last step
@@ -1109,9 +1108,8 @@ static int batch_ensure_rows(pb_batch* b, int rows) {
   pb_ctx* ctx = m->ctx;
   PB_TRY(pb_wait(ctx));
   batch_free_graph(b);  // a recorded graph holds the old buffer addresses
-  cudaFree(b->x); cudaFree(b->xn); cudaFree(b->qkvo); cudaFree(b->att); cudaFree(b->guo); cudaFree(b->hb);
-  cudaFree(b->proj); cudaFree(b->toks);
-  b->x = b->xn = b->qkvo = b->att = b->guo = b->hb = b->proj = nullptr;
+  cudaFree(b->x); cudaFree(b->xn); cudaFree(b->qkvo); cudaFree(b->att); cudaFree(b->hb); cudaFree(b->toks);
+  b->x = b->xn = b->qkvo = b->att = b->hb = nullptr;
   b->toks = nullptr;
   b->rows_cap = 0;
   const pb_model_config& c = m->c;
@@ -1120,9 +1118,7 @@ static int batch_ensure_rows(pb_batch* b, int rows) {
   PB_TRY_CUDA(ctx, cudaMalloc(&b->xn, (size_t)rows * c.dim * 4));
   PB_TRY_CUDA(ctx, cudaMalloc(&b->qkvo, (size_t)rows * qkvw * 4));
   PB_TRY_CUDA(ctx, cudaMalloc(&b->att, (size_t)rows * c.dim * 4));
-  PB_TRY_CUDA(ctx, cudaMalloc(&b->guo, (size_t)rows * 2 * c.hidden_dim * 4));
   PB_TRY_CUDA(ctx, cudaMalloc(&b->hb, (size_t)rows * c.hidden_dim * 4));
-  PB_TRY_CUDA(ctx, cudaMalloc(&b->proj, (size_t)rows * c.dim * 4));
   PB_TRY_CUDA(ctx, cudaMalloc(&b->toks, (size_t)rows * 4));
   b->rows_cap = rows;
   return PB_OK;
@@ -1133,7 +1129,7 @@ extern "C" int pb_batch_free(pb_batch* b) {
   if (b->m && b->m->ctx) pb_wait(b->m->ctx);
   batch_free_graph(b);
   cudaFree(b->kc); cudaFree(b->vc); cudaFree(b->x); cudaFree(b->xn); cudaFree(b->qkvo); cudaFree(b->att);
-  cudaFree(b->guo); cudaFree(b->hb); cudaFree(b->proj); cudaFree(b->xl); cudaFree(b->logits); cudaFree(b->toks);
+  cudaFree(b->hb); cudaFree(b->xl); cudaFree(b->logits); cudaFree(b->toks);
   cudaFree(b->next); cudaFree(b->pos_dev); cudaFree(b->hist); cudaFree(b->ws);
   delete b;
   return PB_OK;
@@ -1206,24 +1202,31 @@ static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start
     geo.q = (int64_t)rows_per_seq * qkvw;
     geo.out = (int64_t)rows_per_seq * dim;
     if (c.head_dim == 64 && !pos_dev)
-      PB_TRY(pb_launch_attn_prefill_f32(ctx, b->qkvo, qkvw, kc, vc, rows_per_seq, start_pos, c.n_heads, c.n_kv_heads,
+      PB_TRY(pb_launch_attn_prefill(ctx, b->qkvo, qkvw, kc, vc, rows_per_seq, start_pos, c.n_heads, c.n_kv_heads,
                                         c.head_dim, b->att, b->B, geo));
     else
       PB_TRY(pb_launch_attn_cached(ctx, b->qkvo, qkvw, kc, vc, rows_per_seq, start_pos, pos_dev, c.n_heads,
                                    c.n_kv_heads, c.head_dim, b->att, c.seq_len, b->B, geo));
   }
-  PB_TRY(pb_launch_q4_gemm(ctx, m->wo[l], b->att, dim, rows, b->proj, dim, b->ws, b->ws_bytes));
-  k_elementwise<<<pb_cdiv((int64_t)rows * dim, 256), 256, 0, ctx->stream>>>(0, b->x, b->proj, (int64_t)rows * dim, b->x);
-  PB_LAUNCHED(ctx, "k_elementwise");
+  // wo with the residual add in the GEMM epilogue (llama-streaming.js:579-580)
+  pb_gemm_epi add;
+  add.mode = PB_GEMM_ADD;
+  PB_TRY(pb_launch_q4_gemm(ctx, m->wo[l], b->att, dim, rows, b->x, dim, b->ws, b->ws_bytes, &add));
   PB_TRY(launch_norm(m, b->x, rows, m->rms_ffn + (size_t)l * dim, b->xn));
-  PB_TRY(pb_launch_q4_gemm(ctx, m->gu[l], b->xn, dim, rows, b->guo, 2 * F, b->ws, b->ws_bytes));
-  // prefill: SILU then ELEMENT_MUL (llama-streaming.js:478-481); decode: fused (:590-595)
-  k_glu<<<dim3(pb_cdiv(F, 256), rows), 256, 0, ctx->stream>>>(b->guo, 2 * F, b->guo, 2 * F, F,
-                                                              rows_per_seq > 1 ? 1 : 0, 1, b->hb);
-  PB_LAUNCHED(ctx, "k_glu");
-  PB_TRY(pb_launch_q4_gemm(ctx, m->w2[l], b->hb, F, rows, b->proj, dim, b->ws, b->ws_bytes));
-  k_elementwise<<<pb_cdiv((int64_t)rows * dim, 256), 256, 0, ctx->stream>>>(0, b->x, b->proj, (int64_t)rows * dim, b->x);
-  PB_LAUNCHED(ctx, "k_elementwise");
+  // gate|up with SwiGLU in the epilogue (f32); h goes out as the down
+  // GEMM's operand: f16 for the TMA path, f32 otherwise
+  const bool h16 = pb_gemm_uses_tma(m->w2[l], rows);
+  pb_gemm_epi glu;
+  glu.mode = PB_GEMM_SWIGLU;
+  if (h16) glu.h16 = reinterpret_cast<__half*>(b->hb);
+  else glu.h32 = b->hb;
+  PB_TRY(pb_launch_q4_gemm(ctx, m->gu[l], b->xn, dim, rows, nullptr, 2 * F, b->ws, b->ws_bytes, &glu));
+  // down with the residual add (:601)
+  if (h16)
+    PB_TRY(pb_launch_q4_gemm(ctx, m->w2[l], nullptr, F, rows, b->x, dim, b->ws, b->ws_bytes, &add,
+                             reinterpret_cast<const __half*>(b->hb)));
+  else
+    PB_TRY(pb_launch_q4_gemm(ctx, m->w2[l], b->hb, F, rows, b->x, dim, b->ws, b->ws_bytes, &add));
   return PB_OK;
 }
 

@@ -446,145 +446,188 @@ __global__ void k_attn_cached(const float* __restrict__ q, const float* __restri
 }
 
 // ============================================================================
-// batched prefill attention in f32 (the batched configuration only)
+// batched prefill attention on the tensor cores (the batched configuration only)
 // ============================================================================
-// CTA = (64 queries, head, sequence).  Q, K and V tiles of 64 rows sit in
-// shared memory; thread (r, cg) owns query rows 4r..4r+3 and key columns (or,
-// for the output, head dims) 4cg..4cg+3.  Online softmax over 64-key tiles:
-// running max and sum per row, rescaled as the max grows; P goes through
-// shared memory for the P.V product.  f32 throughout with expf, so it agrees
+// A flash-attention forward with mma.sync m16n8k16 (f16 operands, f32
+// accumulation).  CTA = (64 queries, head, sequence), four warps of 16 query
+// rows.  Q, K and V tiles are converted from the f32 activations and cache to
+// f16 in shared memory (rows padded to 72 halves so ldmatrix is conflict-free).
+// Per 64-key tile: S = Q K^T in registers, scaled by log2(e)/sqrt(hd), causal
+// mask, online softmax (running max and sum per row, exp2), P packed to f16
+// straight from the S accumulators into A fragments, O += P V with V read by
+// ldmatrix.trans.  The output is divided by the row sum at the end.  The
+// batched path already runs its projections with f16 operands; this agrees
 // with the reference's double-precision attention (llama-streaming.js:422-464)
-// within a relative tolerance; the one-sequence path keeps the exact kernel.
-constexpr int FA_Q = 64, FA_KT = 64, FA_HD = 64, FA_THREADS = 256;
+// within that path's tolerance, and the one-sequence path keeps the exact
+// kernels.
+constexpr int FT_Q = 64, FT_KT = 64, FT_HD = 64, FT_LD = 72, FT_THREADS = 128;
 
-__global__ void __launch_bounds__(FA_THREADS)
-k_attn_prefill_f32(const float* __restrict__ q, int q_stride, const float* __restrict__ kc,
-                   const float* __restrict__ vc, int seq, int start_pos, int n_heads, int n_kv, float scale,
-                   float* __restrict__ out, pb_seq_geo geo) {
-  extern __shared__ __align__(16) unsigned char fa_raw[];
-  float(*Qs)[FA_HD + 4] = reinterpret_cast<float(*)[FA_HD + 4]>(fa_raw);
-  float(*Ks)[FA_HD + 4] = Qs + FA_Q;
-  float(*Vs)[FA_HD + 4] = Ks + FA_KT;
-  float(*Ps)[FA_KT + 4] = reinterpret_cast<float(*)[FA_KT + 4]>(Vs + FA_KT);
-  const int tid = threadIdx.x, r = tid >> 4, cg = tid & 15;
-  const int q0 = blockIdx.x * FA_Q, h = blockIdx.y, z = blockIdx.z;
-  const int per = n_heads / n_kv, kh = h / per, kv_dim = n_kv * FA_HD;
+__device__ __forceinline__ void ft_ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(pb_smem_addr(p)));
+}
+__device__ __forceinline__ void ft_ldsm_x4_t(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(pb_smem_addr(p)));
+}
+__device__ __forceinline__ void ft_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+               "{%0, %1, %2, %3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t ft_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// 4 consecutive f32 of a row -> 4 halves in shared memory
+__device__ __forceinline__ void ft_store4(__half* dst, float4 v) {
+  uint2 u;
+  u.x = ft_h2(v.x, v.y);
+  u.y = ft_h2(v.z, v.w);
+  *reinterpret_cast<uint2*>(dst) = u;
+}
+
+__global__ void __launch_bounds__(FT_THREADS)
+k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __restrict__ kc,
+                  const float* __restrict__ vc, int seq, int start_pos, int n_heads, int n_kv, float scale,
+                  float* __restrict__ out, pb_seq_geo geo) {
+  __shared__ __align__(16) __half Qs[FT_Q][FT_LD];
+  __shared__ __align__(16) __half Ks[FT_KT][FT_LD];
+  __shared__ __align__(16) __half Vs[FT_KT][FT_LD];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int q0 = blockIdx.x * FT_Q, h = blockIdx.y, z = blockIdx.z;
+  const int per = n_heads / n_kv, kh = h / per, kv_dim = n_kv * FT_HD, dim = n_heads * FT_HD;
   q += z * geo.q;
   kc += z * geo.kv;
   vc += z * geo.kv;
   out += z * geo.out;
-  for (int i = tid; i < FA_Q * FA_HD / 4; i += FA_THREADS) {
-    const int qr = i / (FA_HD / 4), d4 = i % (FA_HD / 4);
+  for (int i = tid; i < FT_Q * FT_HD / 4; i += FT_THREADS) {
+    const int qr = i / (FT_HD / 4), d4 = i % (FT_HD / 4);
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (q0 + qr < seq) v = *reinterpret_cast<const float4*>(q + (size_t)(q0 + qr) * q_stride + (size_t)h * FA_HD + 4 * d4);
-    *reinterpret_cast<float4*>(&Qs[qr][4 * d4]) = v;
+    if (q0 + qr < seq) v = *reinterpret_cast<const float4*>(q + (size_t)(q0 + qr) * q_stride + (size_t)h * FT_HD + 4 * d4);
+    ft_store4(&Qs[qr][4 * d4], v);
   }
-  float m_i[4], l_i[4], o[4][4];
+  __syncthreads();
+  uint32_t qa[4][4];  // A fragments of this warp's 16 rows, 4 steps of 16 dims
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    m_i[i] = -INFINITY;
-    l_i[i] = 0.0f;
+  for (int kk = 0; kk < 4; ++kk)
+    ft_ldsm_x4(&Qs[warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8][kk * 16 + (lane >> 4) * 8], qa[kk][0], qa[kk][1],
+               qa[kk][2], qa[kk][3]);
+  float o[8][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) o[i][j] = 0.0f;
-  }
-  // keys 0 .. start_pos + last query of the tile (causal)
-  const int qlast = (q0 + FA_Q < seq ? q0 + FA_Q : seq) - 1;
-  const int kend = start_pos + qlast + 1;
-  for (int k0 = 0; k0 < kend; k0 += FA_KT) {
-    __syncthreads();
-    for (int i = tid; i < FA_KT * FA_HD / 4; i += FA_THREADS) {
-      const int kr = i / (FA_HD / 4), d4 = i % (FA_HD / 4);
+  for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.0f, 0.0f};
+  const float sl2 = scale * 1.4426950408889634f;
+  const int qlast = (q0 + FT_Q < seq ? q0 + FT_Q : seq) - 1;
+  const int kend = start_pos + qlast + 1;  // keys 0 .. start_pos + last query of the tile (causal)
+  const int qp0 = start_pos + q0 + warp * 16 + g, qp1 = qp0 + 8;
+  for (int k0 = 0; k0 < kend; k0 += FT_KT) {
+    __syncthreads();  // the previous tile is no longer read
+    for (int i = tid; i < FT_KT * FT_HD / 4; i += FT_THREADS) {
+      const int kr = i / (FT_HD / 4), d4 = i % (FT_HD / 4);
       float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
       if (k0 + kr < kend) {
-        kv4 = *reinterpret_cast<const float4*>(kc + (size_t)(k0 + kr) * kv_dim + (size_t)kh * FA_HD + 4 * d4);
-        vv4 = *reinterpret_cast<const float4*>(vc + (size_t)(k0 + kr) * kv_dim + (size_t)kh * FA_HD + 4 * d4);
+        kv4 = *reinterpret_cast<const float4*>(kc + (size_t)(k0 + kr) * kv_dim + (size_t)kh * FT_HD + 4 * d4);
+        vv4 = *reinterpret_cast<const float4*>(vc + (size_t)(k0 + kr) * kv_dim + (size_t)kh * FT_HD + 4 * d4);
       }
-      *reinterpret_cast<float4*>(&Ks[kr][4 * d4]) = kv4;
-      *reinterpret_cast<float4*>(&Vs[kr][4 * d4]) = vv4;
+      ft_store4(&Ks[kr][4 * d4], kv4);
+      ft_store4(&Vs[kr][4 * d4], vv4);
     }
     __syncthreads();
-    float sc[4][4];
+    float s[8][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
-    for (int d = 0; d < FA_HD; d += 4) {
-      float4 qa[4], kb[4];
+    for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) qa[i] = *reinterpret_cast<const float4*>(&Qs[4 * r + i][d]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) kb[j] = *reinterpret_cast<const float4*>(&Ks[4 * cg + j][d]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          sc[i][j] = __fmaf_rn(qa[i].w, kb[j].w,
-                               __fmaf_rn(qa[i].z, kb[j].z, __fmaf_rn(qa[i].y, kb[j].y, __fmaf_rn(qa[i].x, kb[j].x, sc[i][j]))));
-    }
-    float mt[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int qpos = start_pos + q0 + 4 * r + i;
-      mt[i] = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int kp = k0 + 4 * cg + j;
-        sc[i][j] = (kp <= qpos && kp < kend) ? sc[i][j] * scale : -INFINITY;
-        mt[i] = fmaxf(mt[i], sc[i][j]);
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b0, b1, b2, b3;
+        ft_ldsm_x4(&Ks[np * 16 + (lane & 7) + (lane >> 4) * 8][kk * 16 + ((lane >> 3) & 1) * 8], b0, b1, b2, b3);
+        ft_mma(s[2 * np], qa[kk], b0, b1);
+        ft_mma(s[2 * np + 1], qa[kk], b2, b3);
       }
-#pragma unroll
-      for (int o2 = 8; o2 > 0; o2 >>= 1) mt[i] = fmaxf(mt[i], __shfl_xor_sync(0xffffffffu, mt[i], o2));
     }
+    float mt0 = -INFINITY, mt1 = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float mn = fmaxf(m_i[i], mt[i]);
-      const float alpha = mn == -INFINITY ? 1.0f : expf(m_i[i] - mn);
-      float ps = 0.0f;
+    for (int j = 0; j < 8; ++j) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float p = mn == -INFINITY ? 0.0f : expf(sc[i][j] - mn);
-        Ps[4 * r + i][4 * cg + j] = p;
-        ps += p;
+      for (int c = 0; c < 2; ++c) {
+        const int key = k0 + 8 * j + 2 * t + c;
+        const bool kin = key < kend;
+        s[j][c] = (kin && key <= qp0) ? s[j][c] * sl2 : -INFINITY;
+        s[j][2 + c] = (kin && key <= qp1) ? s[j][2 + c] * sl2 : -INFINITY;
+        mt0 = fmaxf(mt0, s[j][c]);
+        mt1 = fmaxf(mt1, s[j][2 + c]);
       }
-#pragma unroll
-      for (int o2 = 8; o2 > 0; o2 >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o2);
-      l_i[i] = l_i[i] * alpha + ps;
-      m_i[i] = mn;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) o[i][j] *= alpha;
     }
-    __syncthreads();
-    for (int c = 0; c < FA_KT; ++c) {
-      const float4 vv = *reinterpret_cast<const float4*>(&Vs[c][4 * cg]);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float p = Ps[4 * r + i][c];
-        o[i][0] = __fmaf_rn(p, vv.x, o[i][0]);
-        o[i][1] = __fmaf_rn(p, vv.y, o[i][1]);
-        o[i][2] = __fmaf_rn(p, vv.z, o[i][2]);
-        o[i][3] = __fmaf_rn(p, vv.w, o[i][3]);
+    for (int off = 1; off <= 2; off <<= 1) {
+      mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, off));
+      mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, off));
+    }
+    const float mn0 = fmaxf(m_r[0], mt0), mn1 = fmaxf(m_r[1], mt1);
+    const float al0 = mn0 == -INFINITY ? 1.0f : exp2f(m_r[0] - mn0);
+    const float al1 = mn1 == -INFINITY ? 1.0f : exp2f(m_r[1] - mn1);
+    float ls0 = 0.0f, ls1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        s[j][c] = mn0 == -INFINITY ? 0.0f : exp2f(s[j][c] - mn0);
+        s[j][2 + c] = mn1 == -INFINITY ? 0.0f : exp2f(s[j][2 + c] - mn1);
+        ls0 += s[j][c];
+        ls1 += s[j][2 + c];
+      }
+      o[j][0] *= al0;
+      o[j][1] *= al0;
+      o[j][2] *= al1;
+      o[j][3] *= al1;
+    }
+    l_r[0] = l_r[0] * al0 + ls0;
+    l_r[1] = l_r[1] * al1 + ls1;
+    m_r[0] = mn0;
+    m_r[1] = mn1;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {  // 16 keys per step: S n-tiles 2kk, 2kk+1 as the A fragment
+      const uint32_t pa[4] = {ft_h2(s[2 * kk][0], s[2 * kk][1]), ft_h2(s[2 * kk][2], s[2 * kk][3]),
+                              ft_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]), ft_h2(s[2 * kk + 1][2], s[2 * kk + 1][3])};
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b0, b1, b2, b3;
+        ft_ldsm_x4_t(&Vs[kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8][np * 16 + (lane >> 4) * 8], b0, b1, b2, b3);
+        ft_mma(o[2 * np], pa, b0, b1);
+        ft_mma(o[2 * np + 1], pa, b2, b3);
       }
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int qr = q0 + 4 * r + i;
-    if (qr < seq) {
-      const float inv = 1.0f / l_i[i];
-      float* dst = out + (size_t)qr * n_heads * FA_HD + (size_t)h * FA_HD + 4 * cg;
-      *reinterpret_cast<float4*>(dst) = make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
-    }
+  for (int off = 1; off <= 2; off <<= 1) {
+    l_r[0] += __shfl_xor_sync(0xffffffffu, l_r[0], off);
+    l_r[1] += __shfl_xor_sync(0xffffffffu, l_r[1], off);
+  }
+  const float inv0 = 1.0f / l_r[0], inv1 = 1.0f / l_r[1];
+  const int r0 = q0 + warp * 16 + g, r1 = r0 + 8;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int d = 8 * j + 2 * t;
+    if (r0 < seq)
+      *reinterpret_cast<float2*>(out + (size_t)r0 * dim + (size_t)h * FT_HD + d) =
+          make_float2(o[j][0] * inv0, o[j][1] * inv0);
+    if (r1 < seq)
+      *reinterpret_cast<float2*>(out + (size_t)r1 * dim + (size_t)h * FT_HD + d) =
+          make_float2(o[j][2] * inv1, o[j][3] * inv1);
   }
 }
 
-static size_t fa_smem() { return sizeof(float) * ((FA_Q + 2 * FA_KT) * (FA_HD + 4) + FA_Q * (FA_KT + 4)); }
-
-int pb_launch_attn_prefill_f32(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
-                               int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo) {
-  if (hd != FA_HD || (q_stride & 3)) return PB_ERR_ARG;
-  k_attn_prefill_f32<<<dim3(pb_cdiv(seq, FA_Q), n_heads, nseq), FA_THREADS, fa_smem(), ctx->stream>>>(
+int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
+                           int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo) {
+  if (hd != FT_HD || (q_stride & 3)) return PB_ERR_ARG;
+  k_attn_prefill_tc<<<dim3(pb_cdiv(seq, FT_Q), n_heads, nseq), FT_THREADS, 0, ctx->stream>>>(
       q, q_stride, kc, vc, seq, start_pos, n_heads, n_kv, (float)(1.0 / sqrt((double)hd)), out, geo);
-  PB_LAUNCHED(ctx, "k_attn_prefill_f32");
+  PB_LAUNCHED(ctx, "k_attn_prefill_tc");
   return PB_OK;
 }
 
@@ -1094,7 +1137,5 @@ int pb_setup_ops_kernels(void) {
   cudaError_t e = cudaFuncSetAttribute(k_attn_cached, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec_group, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_attn_prefill_f32, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fa_smem());
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
 }
