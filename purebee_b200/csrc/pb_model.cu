@@ -30,7 +30,7 @@ int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const floa
 bool pb_attn_decode_ok(int n_heads, int n_kv, int hd, int max_len);
 bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len);
 __global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
-                          float* __restrict__ out);
+                          float* __restrict__ out, __half* __restrict__ out16);
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
                           const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
                           const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
@@ -479,8 +479,8 @@ extern "C" int pb_model_get_tensor(pb_model* m, int layer, int which, void* host
 // forward
 // ---------------------------------------------------------------------------
 
-static int launch_norm(pb_model* m, const float* x, int M, const float* w, float* out) {
-  k_rmsnorm<<<M, 256, 0, m->ctx->stream>>>(x, m->c.dim, w, m->c.eps, out);
+static int launch_norm(pb_model* m, const float* x, int M, const float* w, float* out, __half* out16 = nullptr) {
+  k_rmsnorm<<<M, 256, 0, m->ctx->stream>>>(x, m->c.dim, w, m->c.eps, out, out16);
   PB_LAUNCHED(m->ctx, "k_rmsnorm");
   return PB_OK;
 }
@@ -1182,8 +1182,15 @@ static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start
   const int64_t cache_seq = (int64_t)c.seq_len * kv;
   float* kc = b->kc + (size_t)l * b->B * cache_seq;
   float* vc = b->vc + (size_t)l * b->B * cache_seq;
-  PB_TRY(launch_norm(m, b->x, rows, m->rms_att + (size_t)l * dim, b->xn));
-  PB_TRY(pb_launch_q4_gemm(ctx, m->qkv[l], b->xn, dim, rows, b->qkvo, qkvw, b->ws, b->ws_bytes));
+  // the norm writes the GEMM's f16 operand directly on the TMA path
+  __half* xn16 = reinterpret_cast<__half*>(b->xn);
+  if (pb_gemm_uses_tma(m->qkv[l], rows)) {
+    PB_TRY(launch_norm(m, b->x, rows, m->rms_att + (size_t)l * dim, nullptr, xn16));
+    PB_TRY(pb_launch_q4_gemm(ctx, m->qkv[l], nullptr, dim, rows, b->qkvo, qkvw, b->ws, b->ws_bytes, nullptr, xn16));
+  } else {
+    PB_TRY(launch_norm(m, b->x, rows, m->rms_att + (size_t)l * dim, b->xn));
+    PB_TRY(pb_launch_q4_gemm(ctx, m->qkv[l], b->xn, dim, rows, b->qkvo, qkvw, b->ws, b->ws_bytes));
+  }
   {
     const int tot = (c.n_heads + c.n_kv_heads) * (c.head_dim / 2) + kv;
     k_rope_kv<<<dim3(pb_cdiv(tot, 128), rows), 128, 0, ctx->stream>>>(
@@ -1212,7 +1219,8 @@ static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start
   pb_gemm_epi add;
   add.mode = PB_GEMM_ADD;
   PB_TRY(pb_launch_q4_gemm(ctx, m->wo[l], b->att, dim, rows, b->x, dim, b->ws, b->ws_bytes, &add));
-  PB_TRY(launch_norm(m, b->x, rows, m->rms_ffn + (size_t)l * dim, b->xn));
+  const bool gu16 = pb_gemm_uses_tma(m->gu[l], rows);
+  PB_TRY(launch_norm(m, b->x, rows, m->rms_ffn + (size_t)l * dim, gu16 ? nullptr : b->xn, gu16 ? xn16 : nullptr));
   // gate|up with SwiGLU in the epilogue (f32); h goes out as the down
   // GEMM's operand: f16 for the TMA path, f32 otherwise
   const bool h16 = pb_gemm_uses_tma(m->w2[l], rows);
@@ -1220,7 +1228,10 @@ static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start
   glu.mode = PB_GEMM_SWIGLU;
   if (h16) glu.h16 = reinterpret_cast<__half*>(b->hb);
   else glu.h32 = b->hb;
-  PB_TRY(pb_launch_q4_gemm(ctx, m->gu[l], b->xn, dim, rows, nullptr, 2 * F, b->ws, b->ws_bytes, &glu));
+  if (gu16)
+    PB_TRY(pb_launch_q4_gemm(ctx, m->gu[l], nullptr, dim, rows, nullptr, 2 * F, b->ws, b->ws_bytes, &glu, xn16));
+  else
+    PB_TRY(pb_launch_q4_gemm(ctx, m->gu[l], b->xn, dim, rows, nullptr, 2 * F, b->ws, b->ws_bytes, &glu));
   // down with the residual add (:601)
   if (h16)
     PB_TRY(pb_launch_q4_gemm(ctx, m->w2[l], nullptr, F, rows, b->x, dim, b->ws, b->ws_bytes, &add,
