@@ -251,14 +251,18 @@ static size_t gm_smem() { return 2 * GM_STAGE_BYTES + 1024; }
 // dequantized to an f16 copy ((q-8)*d exact in f32, rounded once, the same
 // values the fused kernel stages) and x is rounded to f16 once; both then
 // stream through a 4-stage ring of 128-byte-swizzled tiles loaded by
-// cp.async.bulk.tensor.  Warp roles: warp 0 lane 0 issues the TMA loads,
-// warp 1 lane 0 issues the MMAs (128 x 256 x 16 per instruction, accumulator
-// in 256 TMEM columns) and commits each stage back to its "empty" barrier,
-// warps 4-7 (TMEM lane quadrants 0-3) drain the accumulator.  The dequant
+// cp.async.bulk.tensor.  Persistent CTAs, one per SM, walk the 128 x 256
+// output tiles.  Warp roles: warp 0 lane 0 issues the TMA loads (one ring
+// across all of the CTA's tiles), warp 1 lane 0 issues the MMAs (128 x 256 x
+// 16 per instruction) and commits each stage back to its "empty" barrier.
+// The accumulator alternates between two 256-column TMEM buffers, so warps
+// 4-11 (lane quadrant (w - 4) % 4, half (w - 4) / 4 of the columns) drain
+// tile i through the epilogue while the MMAs of tile i + 1 run.  The dequant
 // copy costs N*K*2 bytes, about 1% of the GEMM time when M >= 512.
 // ---------------------------------------------------------------------------
 
-constexpr int TG_ROWS = 128, TG_TOK = 256, TG_K = 64, TG_STAGES = 4, TG_THREADS = 256;
+constexpr int TG_ROWS = 128, TG_TOK = 256, TG_K = 64, TG_STAGES = 4, TG_THREADS = 384;
+constexpr int TG_EPI_WARPS = 8;  // warps 4..11
 constexpr int TG_A_BYTES = TG_ROWS * TG_K * 2, TG_B_BYTES = TG_TOK * TG_K * 2;
 constexpr int TG_STAGE_BYTES = TG_A_BYTES + TG_B_BYTES;
 constexpr uint32_t TG_IDESC = (1u << 4) | ((uint32_t)(TG_TOK >> 3) << 17) | ((uint32_t)(TG_ROWS >> 4) << 24);
@@ -317,16 +321,16 @@ __global__ void __launch_bounds__(TG_THREADS, 1)
 k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, int N, int M,
                int K, float* __restrict__ C, int ldc, pb_gemm_epi epi, int* err) {
   extern __shared__ __align__(1024) unsigned char tg_raw[];
-  __shared__ uint64_t full[TG_STAGES], empty[TG_STAGES], acc_full;
+  __shared__ uint64_t full[TG_STAGES], empty[TG_STAGES], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   unsigned char* ring = tg_raw + ((1024 - (smem_addr(tg_raw) & 1023)) & 1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * TG_ROWS, m0 = blockIdx.y * TG_TOK;
   const int ksteps = K / TG_K;
+  const int ntn = (N + TG_ROWS - 1) / TG_ROWS, ntm = (M + TG_TOK - 1) / TG_TOK, ntiles = ntn * ntm;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
-                 "r"(TG_TOK)
+                 "r"(2 * TG_TOK)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -335,7 +339,10 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       pb_mbar_init(&full[s], 1);
       pb_mbar_init(&empty[s], 1);
     }
-    pb_mbar_init(&acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      pb_mbar_init(&acc_full[b], 1);
+      pb_mbar_init(&acc_empty[b], TG_EPI_WARPS);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -344,52 +351,67 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   const uint32_t tmem_d = tmem_base;
 
   if (warp == 0 && lane == 0) {
-    // producer: stage s is free once the MMAs of step ks - STAGES committed to empty[s]
-    for (int ks = 0; ks < ksteps; ++ks) {
-      const int s = ks % TG_STAGES;
-      if (ks >= TG_STAGES && !pb_mbar_wait(&empty[s], ((ks / TG_STAGES) - 1) & 1, err)) break;
-      unsigned char* sA = ring + s * TG_STAGE_BYTES;
-      pb_mbar_arrive_tx(&full[s], TG_STAGE_BYTES);
-      tma_load_2d(sA, &map_w, ks * TG_K, n0, &full[s]);
-      tma_load_2d(sA + TG_A_BYTES, &map_x, ks * TG_K, m0, &full[s]);
+    // producer: stage s is free once the MMAs that read it committed to empty[s]
+    int g = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      const int n0 = (t % ntn) * TG_ROWS, m0 = (t / ntn) * TG_TOK;
+      for (int ks = 0; ks < ksteps; ++ks, ++g) {
+        const int s = g % TG_STAGES;
+        if (g >= TG_STAGES && !(ok = pb_mbar_wait(&empty[s], ((g / TG_STAGES) - 1) & 1, err))) break;
+        unsigned char* sA = ring + s * TG_STAGE_BYTES;
+        pb_mbar_arrive_tx(&full[s], TG_STAGE_BYTES);
+        tma_load_2d(sA, &map_w, ks * TG_K, n0, &full[s]);
+        tma_load_2d(sA + TG_A_BYTES, &map_x, ks * TG_K, m0, &full[s]);
+      }
     }
   } else if (warp == 1 && lane == 0) {
-    // MMA issuer
+    // MMA issuer: tile i accumulates into buffer i % 2 once the epilogue has drained tile i - 2
+    int g = 0, i = 0;
     bool ok = true;
-    for (int ks = 0; ks < ksteps && ok; ++ks) {
-      const int s = ks % TG_STAGES;
-      ok = pb_mbar_wait(&full[s], (ks / TG_STAGES) & 1, err);
-      if (!ok) break;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++i) {
+      const int b = i & 1;
+      if (i >= 2 && !(ok = pb_mbar_wait(&acc_empty[b], ((i >> 1) - 1) & 1, err))) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      unsigned char* sA = ring + s * TG_STAGE_BYTES;
-      const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sA + TG_A_BYTES));
+      const uint32_t acc = tmem_d + (uint32_t)(b * TG_TOK);
+      for (int ks = 0; ks < ksteps; ++ks, ++g) {
+        const int s = g % TG_STAGES;
+        if (!(ok = pb_mbar_wait(&full[s], (g / TG_STAGES) & 1, err))) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        unsigned char* sA = ring + s * TG_STAGE_BYTES;
+        const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sA + TG_A_BYTES));
 #pragma unroll
-      for (int kk = 0; kk < TG_K / 16; ++kk) mma_f16_n256(tmem_d, da + 2 * kk, db + 2 * kk, (ks > 0 || kk > 0) ? 1u : 0u);
-      mma_commit(&empty[s]);
+        for (int kk = 0; kk < TG_K / 16; ++kk) mma_f16_n256(acc, da + 2 * kk, db + 2 * kk, (ks > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&empty[s]);
+      }
+      mma_commit(&acc_full[b]);  // fires when every MMA of the tile has completed
     }
-    mma_commit(&acc_full);  // fires when every MMA above has completed
-  }
-  // epilogue on all eight warps: warps w and w + 4 share TMEM lane quadrant
-  // w % 4 and take one half of the token columns each
-  __syncwarp();
-  {
-    const int q = warp & 3, half = warp >> 2;
-    if (pb_mbar_wait(&acc_full, 0, err)) {
+  } else if (warp >= 4) {
+    // epilogue: lane quadrant q of the accumulator, half of its 256 columns
+    const int q = (warp - 4) & 3, half = (warp - 4) >> 2;
+    int i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      const int b = i & 1;
+      if (!pb_mbar_wait(&acc_full[b], (i >> 1) & 1, err)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int n0 = (t % ntn) * TG_ROWS, m0 = (t / ntn) * TG_TOK;
       const int row = n0 + q * 32 + lane;
 #pragma unroll 1
       for (int c0 = half * (TG_TOK / 2); c0 < (half + 1) * (TG_TOK / 2); c0 += 32) {
         uint32_t v[32];
-        tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * TG_TOK + c0), v);
         gemm_emit32(v, false, row, N, m0 + c0, M, C, ldc, epi);
       }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&acc_empty[b])) : "memory");
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0) {
     __syncwarp();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(TG_TOK) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(2 * TG_TOK) : "memory");
   }
 }
 
@@ -444,8 +466,9 @@ static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, const 
   CUtensorMap mw, mx;
   PB_TRY(make_map(ctx, &mw, w16, w->N_pad, K, TG_ROWS));
   PB_TRY(make_map(ctx, &mx, const_cast<__half*>(x16), M, K, TG_TOK));
-  dim3 grid(pb_cdiv(w->N, TG_ROWS), pb_cdiv(M, TG_TOK));
-  if (grid.y > 65535) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
+  const int64_t ntiles = (int64_t)pb_cdiv(w->N, TG_ROWS) * pb_cdiv(M, TG_TOK);
+  if (ntiles > (1ll << 30)) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
+  const int grid = (int)(ntiles < ctx->sm_count ? ntiles : ctx->sm_count);  // persistent: one CTA per SM
   k_gemm_f16_tma<<<grid, TG_THREADS, tg_smem(), ctx->stream>>>(mw, mx, w->N, M, K, C, ldc, epi, ctx->d_err);
   PB_LAUNCHED(ctx, "k_gemm_f16_tma");
   return PB_OK;
