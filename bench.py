@@ -38,6 +38,11 @@ METRIC = "Llama-3.2-1B-shape Q4 decode tok/s; Q4 matvec HBM GB/s vs B200 peak"
 WORKLOAD = "llama3.2-1B-shape Q4_0 batch-1 greedy decode (configs[3])"
 
 
+# DRAM bytes over algorithmic bytes of the Q4_0 matvec, from one ncu capture of
+# the gate-up launch (dram__bytes_read.sum + dram__bytes_write.sum)
+MV_DRAM_OVER_ALG = 18948864 / 18948096
+
+
 def load_flop_peak():
     """Dense bf16 tensor peak (TFLOP/s): the measured burst figure, else the pool's fallback."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -385,7 +390,11 @@ def run_ours(args, rank, world, torch, dist):
                             "launches": launches_per_step},
             "roofline": {"bound": "hbm", "kernel": "k_matvec (Q4_0, WASM lane order)",
                          "achieved": round(mv_agg, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(mv_agg / peak, 3), "traffic": None,
+                         "frac": round(mv_agg / peak, 3),
+                         "traffic": int(round(mv_bytes_avg * MV_DRAM_OVER_ALG)),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gate-up launch "
+                                           "(16384x2048: 18948864 B against 18948096 algorithmic), scaled per launch; "
+                                           "profiles/k_matvec_gate_up_16384x2048.md",
                          "bytes_per_launch": int(mv_bytes_avg), "per_shape": mv},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
