@@ -154,30 +154,51 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem_d = tmem_base;
 
+  // The CTA's whole weight slice into L2 first (row layout: one contiguous run
+  // per row), then a register double buffer: step ks + 1's weights and
+  // activations are loaded before step ks's MMAs are issued.
+  if (layout == PB_LAYOUT_ROWS && tid < GM_ROWS && ksteps > 0) {
+    const int row = n0 + tid, b0 = 2 * kbeg, b1 = 2 * kend_ < nb ? 2 * kend_ : nb;
+    if (row < N_pad && b1 > b0) pb_l2_prefetch(qs + ((size_t)row * nb + b0) * 16, (uint32_t)(b1 - b0) * 16);
+  }
+  const int wr = tid >> 1, wblk = tid & 1;  // weights: (row, block) of the two Q4_0 blocks of a step
+  const int xr_ = tid >> 1, xh = tid & 1;   // activations: (token, half of the 64-wide step)
+  const bool xlive_row = xr_ < TOK && m0 + xr_ < M;
+  uint4 pl;
+  float dsv;
+  float4 xa[8];
+  auto load_step = [&](int kg) {
+    const int b = kg * 2 + wblk, row = n0 + wr;
+    pl = make_uint4(0, 0, 0, 0);
+    dsv = 0.0f;
+    if (b < nb && row < N_pad) {
+      const size_t slot = (size_t)pb_slot(layout, row, b, nb);
+      pl = __ldg(reinterpret_cast<const uint4*>(qs) + slot);
+      dsv = pb_f16_exact(__ldg(dsc + slot));
+    }
+    const int k = kg * GM_KSTEP + xh * 32;
+    const bool live = xlive_row && k < K;
+    const float4* xr = reinterpret_cast<const float4*>(X + (size_t)(m0 + xr_) * ldx + k);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) xa[c] = live ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  };
+  if (ksteps > 0) load_step(kbeg);
+
   bool ok = true;
   for (int ks = 0; ks < ksteps && ok; ++ks) {
-    const int st = ks & 1, kg = kbeg + ks;  // kg: global K step
+    const int st = ks & 1;
     unsigned char* sA = ring + st * GM_STAGE_BYTES;
     unsigned char* sB = sA + GM_TILE_BYTES;
     if (ks >= 2) ok = pb_mbar_wait(&bars[st], ((ks >> 1) - 1) & 1, err);  // MMAs of step ks-2 are done with it
     if (!ok) break;
-    // weights: thread -> (row, block) of the two Q4_0 blocks of this step
     {
-      const int r = tid >> 1, blk = tid & 1, b = kg * 2 + blk, row = n0 + r;
-      uint4 pl = make_uint4(0, 0, 0, 0);
-      float d = 0.0f;
-      if (b < nb && row < N_pad) {
-        const size_t slot = (size_t)pb_slot(layout, row, b, nb);
-        pl = __ldg(reinterpret_cast<const uint4*>(qs) + slot);
-        d = pb_f16_exact(__ldg(dsc + slot));
-      }
       const uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
       float e[32];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const uint32_t byte = (wv[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-        e[j] = (float)((int)(byte & 15u) - 8) * d;       // exact in f32
-        e[16 + j] = (float)((int)(byte >> 4) - 8) * d;
+        e[j] = (float)((int)(byte & 15u) - 8) * dsv;       // exact in f32
+        e[16 + j] = (float)((int)(byte >> 4) - 8) * dsv;
       }
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -186,30 +207,21 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
         v.y = pack_h2(e[8 * c + 2], e[8 * c + 3]);
         v.z = pack_h2(e[8 * c + 4], e[8 * c + 5]);
         v.w = pack_h2(e[8 * c + 6], e[8 * c + 7]);
-        *reinterpret_cast<uint4*>(sA + sw128(r, blk * 4 + c)) = v;
+        *reinterpret_cast<uint4*>(sA + sw128(wr, wblk * 4 + c)) = v;
       }
     }
-    // activations: thread -> (token, half of the 64-wide step)
-    {
-      const int r = tid >> 1, hh = tid & 1, m = m0 + r;
-      const int k = kg * GM_KSTEP + hh * 32;
-      const bool live = r < TOK && m < M && k < K;
-      const float4* xr = reinterpret_cast<const float4*>(X + (size_t)m * ldx + k);
+    if (xr_ < TOK) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), bq = a;
-        if (live) {
-          a = __ldg(xr + 2 * c);
-          bq = __ldg(xr + 2 * c + 1);
-        }
         uint4 v;
-        v.x = pack_h2(a.x, a.y);
-        v.y = pack_h2(a.z, a.w);
-        v.z = pack_h2(bq.x, bq.y);
-        v.w = pack_h2(bq.z, bq.w);
-        if (r < TOK) *reinterpret_cast<uint4*>(sB + sw128(r, hh * 4 + c)) = v;
+        v.x = pack_h2(xa[2 * c].x, xa[2 * c].y);
+        v.y = pack_h2(xa[2 * c].z, xa[2 * c].w);
+        v.z = pack_h2(xa[2 * c + 1].x, xa[2 * c + 1].y);
+        v.w = pack_h2(xa[2 * c + 1].z, xa[2 * c + 1].w);
+        *reinterpret_cast<uint4*>(sB + sw128(xr_, xh * 4 + c)) = v;
       }
     }
+    if (ks + 1 < ksteps) load_step(kbeg + ks + 1);
     // generic-proxy writes -> visible to the tensor core's async proxy
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
