@@ -1069,15 +1069,15 @@ k_attn_dec_group(const float* __restrict__ q, const float* __restrict__ kc, cons
 #pragma unroll
     for (int hl = 0; hl < AD_MAX_GROUP; ++hl) acc[hl] = make_float4(0.f, 0.f, 0.f, 0.f);
     const float* vl = vc + 4 * d4;
-    for (int base = jg; base < cache_len; base += 4 * jgroups) {
-      float4 vv[4];
+    for (int base = jg; base < cache_len; base += 8 * jgroups) {
+      float4 vv[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         const int j = base + u * jgroups;
         if (j < cache_len) vv[u] = *reinterpret_cast<const float4*>(vl + (size_t)j * kv_dim);
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         const int j = base + u * jgroups;
         if (j < cache_len) {
 #pragma unroll
