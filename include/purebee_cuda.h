@@ -376,6 +376,54 @@ int pb_batch_prefill(pb_batch* b, const int* tokens_host, int n_prompt, int* nex
  * logits_host [n_seqs][vocab] (optional) the last step's logits. */
 int pb_batch_decode(pb_batch* b, int steps, int* tokens_host, float* logits_host);
 
+/* ------------------------------------------------------------------ */
+/* row split over GPUs (thread-pool.js:165-246 splits a matvec's output   */
+/* rows over worker threads, thread-pool.js:174-203 for the row ranges;   */
+/* here one rank per GPU holds a row range of every projection and of    */
+/* the LM head, and NCCL all-gathers complete the activations)           */
+/* ------------------------------------------------------------------ */
+
+/* Which rows rank `rank` of `world` holds.  Query heads and kv heads are
+ * split evenly (each rank attends over its own heads and holds their KV
+ * cache); wo and w2 by output rows in dim / world chunks, the interleaved
+ * gate|up matrix in 2F / world row chunks (hidden units [rank*F/world, ...));
+ * the vocab in chunks of vocab_chunk rows (a multiple of 32; the last rank
+ * takes the rest).  Needs n_kv_heads, dim / 64 and hidden_dim / 64
+ * divisible by world; PB_ERR_ARG otherwise.  Host only. */
+typedef struct pb_split_plan {
+  int world, rank;
+  int n_heads, n_kv_heads;      /* this rank's heads */
+  int q_row0, k_row0, v_row0;   /* first rows held of wq, wk, wv, as rows of [wq; wk; wv] */
+  int qkv_rows;                 /* (n_heads + 2 n_kv_heads) * head_dim */
+  int dim_chunk, hidden_chunk;  /* dim / world, hidden_dim / world */
+  int vocab_row0, vocab_rows, vocab_chunk;
+} pb_split_plan;
+int pb_batch_split_plan(const pb_model_config* c, int world, int rank, pb_split_plan* out);
+
+#define PB_COMM_ID_BYTES 128
+typedef struct pb_comm pb_comm;
+/* A new NCCL unique id (on one rank; the caller sends it to the others). */
+int pb_comm_id(void* id_out);
+/* Join communicator `id` as `rank` of `world` on ctx's device (collective
+ * over the ranks).  Release every batch that uses it before pb_comm_free. */
+int pb_comm_init(pb_ctx* ctx, int world, int rank, const void* id, pb_comm** out);
+int pb_comm_free(pb_comm* c);
+int pb_comm_rank(const pb_comm* c);
+int pb_comm_world(const pb_comm* c);
+/* recv_dev [world][bytes] <- every rank's send_dev [bytes], on ctx's stream */
+int pb_comm_allgather(pb_comm* c, const void* send_dev, void* recv_dev, size_t bytes);
+
+/* This process's rank of a row-split batch over comm's ranks: every rank
+ * calls prefill / decode with the same arguments, and every rank gets the
+ * same tokens and logits, with the same bits as pb_batch_create on one GPU.
+ * The exchanges are in-place NCCL all-gathers on the context stream, four per
+ * layer plus the argmax keys, recorded into the decode graph. */
+int pb_batch_create_split(pb_model* m, int n_seqs, pb_comm* comm, pb_batch** out);
+/* All `world` ranks of a row split in this process, on ctx's one device,
+ * with device copies in place of the all-gathers: the split's arithmetic on
+ * one GPU (tests compare it with pb_batch_create bit for bit). */
+int pb_batch_create_group(pb_model* m, int n_seqs, int world, pb_batch** out);
+
 #ifdef __cplusplus
 }
 #endif

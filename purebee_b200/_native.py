@@ -38,6 +38,15 @@ class ModelConfig(ctypes.Structure):
                 ("seq_len", ctypes.c_int), ("rope_theta", ctypes.c_double), ("eps", ctypes.c_double)]
 
 
+class SplitPlan(ctypes.Structure):
+    """pb_split_plan: the rows rank `rank` of `world` holds in a row-split batch."""
+    _fields_ = [(n, ctypes.c_int) for n in ("world", "rank", "n_heads", "n_kv_heads", "q_row0", "k_row0", "v_row0",
+                                           "qkv_rows", "dim_chunk", "hidden_chunk", "vocab_row0", "vocab_rows",
+                                           "vocab_chunk")]
+
+
+COMM_ID_BYTES = 128
+
 V = ctypes.c_void_p
 I = ctypes.c_int
 I64 = ctypes.c_int64
@@ -151,6 +160,15 @@ SIGNATURES = {
     "pb_batch_free": (I, [V]),
     "pb_batch_prefill": (I, [V, V, I, V, V]),
     "pb_batch_decode": (I, [V, I, V, V]),
+    "pb_batch_split_plan": (I, [ctypes.POINTER(ModelConfig), I, I, ctypes.POINTER(SplitPlan)]),
+    "pb_batch_create_split": (I, [V, I, V, ctypes.POINTER(V)]),
+    "pb_batch_create_group": (I, [V, I, I, ctypes.POINTER(V)]),
+    "pb_comm_id": (I, [V]),
+    "pb_comm_init": (I, [V, I, I, V, ctypes.POINTER(V)]),
+    "pb_comm_free": (I, [V]),
+    "pb_comm_rank": (I, [V]),
+    "pb_comm_world": (I, [V]),
+    "pb_comm_allgather": (I, [V, V, V, SZ]),
 }
 
 _lib = None

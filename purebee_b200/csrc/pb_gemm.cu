@@ -178,7 +178,9 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
     }
     const int k = kg * GM_KSTEP + xh * 32;
     const bool live = xlive_row && k < K;
-    const float4* xr = reinterpret_cast<const float4*>(X + (size_t)(m0 + xr_) * ldx + k);
+    const int xc = epi.x_chunk;  // a 32-wide half step never straddles a chunk (x_chunk % 64 == 0)
+    const float4* xr = reinterpret_cast<const float4*>(
+        xc ? X + (size_t)(k / xc) * M * xc + (size_t)(m0 + xr_) * xc + k % xc : X + (size_t)(m0 + xr_) * ldx + k);
 #pragma unroll
     for (int c = 0; c < 8; ++c) xa[c] = live ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
   };
@@ -288,6 +290,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_f16_n256(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -321,17 +330,20 @@ __global__ void k_dequant_q4_f16(const uint8_t* __restrict__ qs, const uint16_t*
   o[3] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
 }
 
-__global__ void k_f32_to_f16(const float* __restrict__ x, int M, int K, int ldx, __half* __restrict__ out) {
+// f32 X (row-major with stride ldx, or in column chunks of width kc) ->
+// row-major f16 [M][K]
+__global__ void k_f32_to_f16(const float* __restrict__ x, int M, int K, int ldx, int kc, __half* __restrict__ out) {
   const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;  // 4 values per thread
   if (i >= (int64_t)M * K) return;
   const int m = (int)(i / K), k = (int)(i % K);
-  const float4 v = __ldg(reinterpret_cast<const float4*>(x + (size_t)m * ldx + k));
+  const float* src = kc ? x + (size_t)(k / kc) * M * kc + (size_t)m * kc + k % kc : x + (size_t)m * ldx + k;
+  const float4 v = __ldg(reinterpret_cast<const float4*>(src));
   reinterpret_cast<uint2*>(out)[i / 4] = make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
 }
 
 __global__ void __launch_bounds__(TG_THREADS, 1)
 k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, int N, int M,
-               int K, float* __restrict__ C, int ldc, pb_gemm_epi epi, int* err) {
+               int K, int xkc, float* __restrict__ C, int ldc, pb_gemm_epi epi, int* err) {
   extern __shared__ __align__(1024) unsigned char tg_raw[];
   __shared__ uint64_t full[TG_STAGES], empty[TG_STAGES], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
@@ -374,7 +386,8 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
         unsigned char* sA = ring + s * TG_STAGE_BYTES;
         pb_mbar_arrive_tx(&full[s], TG_STAGE_BYTES);
         tma_load_2d(sA, &map_w, ks * TG_K, n0, &full[s]);
-        tma_load_2d(sA + TG_A_BYTES, &map_x, ks * TG_K, m0, &full[s]);
+        // X: column chunk (k / xkc), x coordinate k % xkc (a multiple of 64 elements)
+        tma_load_3d(sA + TG_A_BYTES, &map_x, (ks * TG_K) % xkc, m0, (ks * TG_K) / xkc, &full[s]);
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -458,6 +471,22 @@ static int make_map(pb_ctx* ctx, CUtensorMap* map, const void* base, int rows, i
   return PB_OK;
 }
 
+// f16 X as [K / kc][rows][kc] (kc == K: plain row-major [rows][K]) with a box
+// of box_rows x 64 elements of one chunk, 128-byte swizzle.
+static int make_map_x(pb_ctx* ctx, CUtensorMap* map, const void* base, int rows, int K, int kc, int box_rows) {
+  auto enc = tensor_map_encoder(ctx);
+  if (!enc) return PB_ERR_CUDA;
+  cuuint64_t dims[3] = {(cuuint64_t)kc, (cuuint64_t)rows, (cuuint64_t)(K / kc)};
+  cuuint64_t strides[2] = {(cuuint64_t)kc * 2, (cuuint64_t)rows * kc * 2};
+  cuuint32_t box[3] = {(cuuint32_t)TG_K, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return pb_set_error(ctx, PB_ERR_CUDA, "cuTensorMapEncodeTiled (3d) failed (%d)", (int)r);
+  return PB_OK;
+}
+
 static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, const __half* Xh, int ldx, int M, float* C,
                            int ldc, const pb_gemm_epi& epi) {
   const int K = w->K;
@@ -471,17 +500,19 @@ static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, const 
   PB_LAUNCHED(ctx, "k_dequant_q4_f16");
   if (!Xh) {  // the activations rounded to f16 once
     __half* xs = reinterpret_cast<__half*>(static_cast<char*>(ctx->gemm_scratch) + off_x);
-    k_f32_to_f16<<<pb_cdiv((int64_t)M * K / 4, 256), 256, 0, ctx->stream>>>(X, M, K, ldx, xs);
+    k_f32_to_f16<<<pb_cdiv((int64_t)M * K / 4, 256), 256, 0, ctx->stream>>>(X, M, K, ldx, epi.x_chunk, xs);
     PB_LAUNCHED(ctx, "k_f32_to_f16");
     x16 = xs;
   }
+  // the f32 conversion writes row-major f16; an f16 operand keeps its chunks
+  const int xkc = (Xh && epi.x_chunk) ? epi.x_chunk : K;
   CUtensorMap mw, mx;
   PB_TRY(make_map(ctx, &mw, w16, w->N_pad, K, TG_ROWS));
-  PB_TRY(make_map(ctx, &mx, const_cast<__half*>(x16), M, K, TG_TOK));
+  PB_TRY(make_map_x(ctx, &mx, const_cast<__half*>(x16), M, K, xkc, TG_TOK));
   const int64_t ntiles = (int64_t)pb_cdiv(w->N, TG_ROWS) * pb_cdiv(M, TG_TOK);
   if (ntiles > (1ll << 30)) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
   const int grid = (int)(ntiles < ctx->sm_count ? ntiles : ctx->sm_count);  // persistent: one CTA per SM
-  k_gemm_f16_tma<<<grid, TG_THREADS, tg_smem(), ctx->stream>>>(mw, mx, w->N, M, K, C, ldc, epi, ctx->d_err);
+  k_gemm_f16_tma<<<grid, TG_THREADS, tg_smem(), ctx->stream>>>(mw, mx, w->N, M, K, xkc, C, ldc, epi, ctx->d_err);
   PB_LAUNCHED(ctx, "k_gemm_f16_tma");
   return PB_OK;
 }
@@ -522,6 +553,9 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
   if (w->type != PB_TYPE_Q4_0) return pb_set_error(ctx, PB_ERR_ARG, "the tensor-core GEMM needs a Q4_0 matrix");
   if (X && ((ldx & 3) || ((uintptr_t)X & 15)))
     return pb_set_error(ctx, PB_ERR_ARG, "X must be 16-byte aligned with a row stride that is a multiple of 4");
+  if (epi.x_chunk && (epi.x_chunk % 64 || w->K % epi.x_chunk))
+    return pb_set_error(ctx, PB_ERR_ARG, "column chunks of %d do not tile K=%d in steps of 64", epi.x_chunk, w->K);
+  if (Xh && ((uintptr_t)Xh & 15)) return pb_set_error(ctx, PB_ERR_ARG, "f16 X must be 16-byte aligned");
   if (pb_gemm_uses_tma(w, M)) return launch_gemm_tma(ctx, w, X, Xh, ldx, M, C, ldc, epi);
   if (!X) return pb_set_error(ctx, PB_ERR_ARG, "f16 activations need the TMA path (M >= %d)", PB_GEMM_TMA_MIN_M);
   const int tok = M <= 64 ? 64 : GM_TOK;
@@ -533,12 +567,16 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
   const int ktot = pb_cdiv(w->K, GM_KSTEP);
   int splits = 1;
   if (ws) {
-    const int base = grid.x * grid.y;
+    // planned for split_n rows when set (a row slice keeps the whole matrix's plan)
+    const int plan_n = epi.split_n > 0 ? epi.split_n : w->N;
+    const int base = pb_cdiv(plan_n, GM_ROWS) * grid.y;
     splits = pb_cdiv(2 * ctx->sm_count, base);
     const int max_by_k = ktot / 4 > 1 ? ktot / 4 : 1;
-    const int max_by_ws = (int)(ws_bytes / ((size_t)M * w->N * 4));
+    const int max_by_ws = (int)(ws_bytes / ((size_t)M * plan_n * 4));
+    const int fit = (int)(ws_bytes / ((size_t)M * w->N * 4));  // the partials of this matrix must fit
     splits = splits < max_by_k ? splits : max_by_k;
     splits = splits < max_by_ws ? splits : max_by_ws;
+    splits = splits < fit ? splits : fit;
     if (splits < 1) splits = 1;
   }
   const int kper = pb_cdiv(ktot, splits);
@@ -546,7 +584,12 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
   grid.z = splits;
   float* dst = splits > 1 ? ws : C;
   const int ldd = splits > 1 ? w->N : ldc;
-  const pb_gemm_epi kepi = splits > 1 ? pb_gemm_epi() : epi;  // split partials are stored, the reduce finishes
+  pb_gemm_epi kepi = epi;  // split partials are stored (same X layout), the reduce finishes
+  if (splits > 1) {
+    kepi.mode = PB_GEMM_STORE;
+    kepi.h16 = nullptr;
+    kepi.h32 = nullptr;
+  }
   if (tok == 64)
     k_q4_gemm_tc<64><<<grid, GM_THREADS, gm_smem(), ctx->stream>>>(w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, X,
                                                                   ldx, M, dst, ldd, kper, kepi, ctx->d_err);

@@ -278,14 +278,29 @@ struct pb_seq_geo {
 #define PB_GEMM_STORE 0
 #define PB_GEMM_ADD 1
 #define PB_GEMM_SWIGLU 2
+// The struct also carries the operand layout and the split-K plan:
+//   x_chunk > 0: X (f32 or f16) is stored as K / x_chunk column chunks,
+//     [K / x_chunk][M][x_chunk] (the all-gathered operand of a row-split
+//     model, chunk r written by rank r); x_chunk divides K and is a multiple
+//     of 64.  0: row-major X with row stride ldx.
+//   split_n > 0: the split-K count is chosen as for a matrix of split_n rows,
+//     so a row slice of a matrix sums its K partials in the same order as the
+//     whole matrix (and gives the same bits).
 struct pb_gemm_epi {
   int mode = PB_GEMM_STORE;
   __half* h16 = nullptr;
   float* h32 = nullptr;
+  int x_chunk = 0;
+  int split_n = 0;
 };
 int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
                       size_t ws_bytes, const pb_gemm_epi* epi = nullptr, const __half* Xh = nullptr);
 bool pb_gemm_uses_tma(const pb_qmat* w, int M);  // the f16-operand TMA path (takes Xh)
+
+// pb_comm.cu: in-place all-gather on the communicator's context stream;
+// chunk `rank` of base (chunk_bytes each) goes to every rank
+int pb_comm_gather_inplace(pb_comm* c, void* base, size_t chunk_bytes);
+pb_ctx* pb_comm_ctx(const pb_comm* c);
 
 int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows,
                      const pb_mv_epi* epi);

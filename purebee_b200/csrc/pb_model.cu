@@ -30,7 +30,7 @@ int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const floa
 bool pb_attn_decode_ok(int n_heads, int n_kv, int hd, int max_len);
 bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len);
 __global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
-                          float* __restrict__ out, __half* __restrict__ out16);
+                          float* __restrict__ out, __half* __restrict__ out16, int xc);
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
                           const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
                           const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
@@ -479,8 +479,9 @@ extern "C" int pb_model_get_tensor(pb_model* m, int layer, int which, void* host
 // forward
 // ---------------------------------------------------------------------------
 
-static int launch_norm(pb_model* m, const float* x, int M, const float* w, float* out, __half* out16 = nullptr) {
-  k_rmsnorm<<<M, 256, 0, m->ctx->stream>>>(x, m->c.dim, w, m->c.eps, out, out16);
+static int launch_norm(pb_model* m, const float* x, int M, const float* w, float* out, __half* out16 = nullptr,
+                       int xc = 0) {
+  k_rmsnorm<<<M, 256, 0, m->ctx->stream>>>(x, m->c.dim, w, m->c.eps, out, out16, xc == m->c.dim ? 0 : xc);
   PB_LAUNCHED(m->ctx, "k_rmsnorm");
   return PB_OK;
 }
@@ -1034,30 +1035,200 @@ extern "C" int pb_model_decode_launches(const pb_model* m) { return m ? m->launc
 // residual adds are launched over all sequences at once.  The reference runs
 // one sequence at a time (llama-streaming.js:738-815); this is the batched
 // configuration's form of it.
+//
+// Row split over `world` ranks (thread-pool.js:165-246 splits one matvec's
+// output rows over worker threads; here every projection and the LM head is
+// split by output rows over GPUs).  Rank r holds
+//   - the query heads [r*H/w, (r+1)*H/w) and kv heads [r*Hkv/w, ...) of every
+//     layer: its rows of [wq; wk; wv] and its slice of the KV cache, so RoPE
+//     and attention stay local;
+//   - output rows [r*dim/w, ...) of wo and w2, rows [r*2F/w, ...) of the
+//     interleaved gate|up matrix (hidden units [r*F/w, ...)), and a contiguous
+//     range of vocab rows of the head.
+// Activations that every rank reads whole are stored as column chunks,
+// [w][rows][width/w], chunk r written by rank r, so one in-place all-gather
+// per exchange completes them: the attention output (before wo), the
+// residual x (after wo and after w2) and the SwiGLU output h (before w2).
+// The GEMMs read chunked operands directly (pb_gemm_epi.x_chunk) and plan
+// split K for the whole matrix (split_n), and the greedy token is the
+// largest of the ranks' argmax keys, so every rank's tokens and logits have
+// the same bits as one GPU's.  Across processes the all-gather is NCCL on
+// the context stream (recorded into the decode graph); an emulated group
+// runs all ranks' shards in one process on one device and copies the chunks.
 // ===========================================================================
+
+// One rank's weights, cache and activations.
+struct pb_shard {
+  int rank = 0;
+  bool owns = false;  // row copies (world > 1) rather than the model's own matrices
+  std::vector<pb_qmat*> qkv, wo, gu, w2;
+  pb_qmat* head = nullptr;
+  pb_split_plan p{};
+  float *kc = nullptr, *vc = nullptr;  // [layer][seq][seq_len][n_kv_heads(rank) * head_dim]
+  float* x = nullptr;     // residual, column chunks [world][rows][dim / world] (all ranks hold all)
+  float* xn = nullptr;    // normed rows, row-major (f16 on the TMA path)
+  float* qkvo = nullptr;  // the rank's q | k | v per token
+  float* att = nullptr;   // attention output chunks [world][rows][dim / world]
+  float* hb = nullptr;    // SwiGLU output chunks [world][rows][F / world] (f16 on the TMA path)
+  float* xl = nullptr;    // last row of every sequence, row-major [B][dim]
+  float* logits = nullptr;               // [world][B][vocab_chunk]; the rank's chunk is computed
+  unsigned long long* keys = nullptr;    // [world][B] argmax keys of each rank's vocab rows
+};
 
 struct pb_batch {
   pb_model* m = nullptr;
   int B = 0;
-  int rows_cap = 0;  // activation rows allocated
-  int P = 0;         // prompt length of the current batch
-  float *kc = nullptr, *vc = nullptr;  // [layer][seq][seq_len][kv]
-  float *x = nullptr, *xn = nullptr, *qkvo = nullptr, *att = nullptr;
-  float* hb = nullptr;  // SwiGLU output, the down GEMM's operand (f16 on the TMA path)
-  float *xl = nullptr, *logits = nullptr;  // [B][dim], [B][V]
-  int* toks = nullptr;                     // [rows] token ids (prefill)
-  int* next = nullptr;                     // [B] greedy tokens of the last step
-  int* pos_dev = nullptr;                  // position of the tokens the next decode step reads
-  int* hist = nullptr;                     // [seq_len + 1][B] greedy token produced at each position
-  float* ws = nullptr;  // split-K partial tiles of the decode-step GEMMs
+  int world = 1;
+  pb_comm* comm = nullptr;    // NCCL: this process holds one shard
+  std::vector<pb_shard> sh;   // one shard, or all `world` of an emulated group
+  int rows_cap = 0;           // activation rows allocated
+  int P = 0;                  // prompt length of the current batch
+  int* toks = nullptr;        // [rows] token ids (prefill)
+  int* next = nullptr;        // [B] greedy tokens of the last step
+  int* pos_dev = nullptr;     // position of the tokens the next decode step reads
+  int* hist = nullptr;        // [seq_len + 1][B] greedy token produced at each position
+  float* ws = nullptr;        // split-K partial tiles of the decode-step GEMMs
   size_t ws_bytes = 0;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
 };
 
-__global__ void k_gather_last(const float* __restrict__ x, int rows_per_seq, int dim, float* __restrict__ out) {
+extern "C" int pb_batch_split_plan(const pb_model_config* c, int world, int rank, pb_split_plan* out) {
+  if (!c || !out || world < 1 || rank < 0 || rank >= world) return PB_ERR_ARG;
+  if (c->n_heads <= 0 || c->n_kv_heads <= 0 || c->head_dim <= 0 || c->dim <= 0 || c->hidden_dim <= 0 || c->vocab <= 0)
+    return PB_ERR_ARG;
+  if (world > 1 && (c->n_kv_heads % world || c->dim % (64 * world) || c->hidden_dim % (64 * world)))
+    return PB_ERR_ARG;
+  pb_split_plan p{};
+  const int hd = c->head_dim, kv = c->n_kv_heads * hd;
+  p.world = world;
+  p.rank = rank;
+  p.n_heads = c->n_heads / world;
+  p.n_kv_heads = c->n_kv_heads / world;
+  p.q_row0 = rank * p.n_heads * hd;
+  p.k_row0 = c->dim + rank * p.n_kv_heads * hd;
+  p.v_row0 = c->dim + kv + rank * p.n_kv_heads * hd;
+  p.qkv_rows = (p.n_heads + 2 * p.n_kv_heads) * hd;
+  p.dim_chunk = c->dim / world;
+  p.hidden_chunk = c->hidden_dim / world;
+  // vocab rows in chunks of a multiple of 32 rows; the last rank takes the rest
+  const int per = world == 1 ? c->vocab : (c->vocab + world - 1) / world;
+  p.vocab_chunk = world == 1 ? c->vocab : (per + 31) / 32 * 32;
+  p.vocab_row0 = rank * p.vocab_chunk;
+  const int left = c->vocab - p.vocab_row0;
+  p.vocab_rows = left < 0 ? 0 : left < p.vocab_chunk ? left : p.vocab_chunk;
+  if (p.vocab_rows <= 0) return PB_ERR_ARG;  // more ranks than vocab chunks
+  *out = p;
+  return PB_OK;
+}
+
+// rows [src_row0, src_row0 + rows) of a row-layout matrix -> dst rows from dst_row0
+static int copy_rows(pb_ctx* ctx, pb_qmat* dst, int dst_row0, const pb_qmat* src, int src_row0, int rows) {
+  const size_t nb = (size_t)src->nb;
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(dst->qs + (size_t)dst_row0 * nb * 16, src->qs + (size_t)src_row0 * nb * 16,
+                                   (size_t)rows * nb * 16, cudaMemcpyDeviceToDevice, ctx->stream));
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(dst->d + (size_t)dst_row0 * nb, src->d + (size_t)src_row0 * nb, (size_t)rows * nb * 2,
+                                   cudaMemcpyDeviceToDevice, ctx->stream));
+  return PB_OK;
+}
+
+static int slice_rows(pb_ctx* ctx, const pb_qmat* src, int row0, int rows, pb_qmat** out) {
+  PB_TRY(pb_qmat_alloc(ctx, src->type, PB_LAYOUT_ROWS, rows, src->K, out));
+  return copy_rows(ctx, *out, 0, src, row0, rows);
+}
+
+static void shard_free(pb_ctx* ctx, pb_shard& s) {
+  if (s.owns) {
+    for (auto* q : s.qkv) pb_qmat_free(ctx, q);
+    for (auto* q : s.wo) pb_qmat_free(ctx, q);
+    for (auto* q : s.gu) pb_qmat_free(ctx, q);
+    for (auto* q : s.w2) pb_qmat_free(ctx, q);
+    pb_qmat_free(ctx, s.head);
+  }
+  s.qkv.clear(); s.wo.clear(); s.gu.clear(); s.w2.clear();
+  s.head = nullptr;
+  cudaFree(s.kc); cudaFree(s.vc); cudaFree(s.x); cudaFree(s.xn); cudaFree(s.qkvo); cudaFree(s.att); cudaFree(s.hb);
+  cudaFree(s.xl); cudaFree(s.logits); cudaFree(s.keys);
+  s.kc = s.vc = s.x = s.xn = s.qkvo = s.att = s.hb = s.xl = s.logits = nullptr;
+  s.keys = nullptr;
+}
+
+// The rank's weights (row copies when split) and its fixed-size buffers.
+static int shard_init(pb_batch* b, pb_shard& s, int rank) {
+  pb_model* m = b->m;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  s.rank = rank;
+  if (pb_batch_split_plan(&c, b->world, rank, &s.p) != PB_OK)
+    return pb_set_error(ctx, PB_ERR_ARG, "a row split over %d ranks needs n_kv_heads, dim / 64 and hidden_dim / 64 "
+                                         "divisible by it and a vocab of at least one row chunk per rank", b->world);
+  const pb_split_plan& p = s.p;
+  const int L = c.n_layers, hd = c.head_dim;
+  if (b->world == 1) {
+    s.qkv = m->qkv; s.wo = m->wo; s.gu = m->gu; s.w2 = m->w2;
+    s.head = head_of(m);
+  } else {
+    s.owns = true;
+    s.qkv.assign(L, nullptr); s.wo.assign(L, nullptr); s.gu.assign(L, nullptr); s.w2.assign(L, nullptr);
+    for (int l = 0; l < L; ++l) {
+      PB_TRY(pb_qmat_alloc(ctx, PB_TYPE_Q4_0, PB_LAYOUT_ROWS, p.qkv_rows, c.dim, &s.qkv[l]));
+      PB_TRY(copy_rows(ctx, s.qkv[l], 0, m->qkv[l], p.q_row0, p.n_heads * hd));
+      PB_TRY(copy_rows(ctx, s.qkv[l], p.n_heads * hd, m->qkv[l], p.k_row0, p.n_kv_heads * hd));
+      PB_TRY(copy_rows(ctx, s.qkv[l], (p.n_heads + p.n_kv_heads) * hd, m->qkv[l], p.v_row0, p.n_kv_heads * hd));
+      PB_TRY(slice_rows(ctx, m->wo[l], rank * p.dim_chunk, p.dim_chunk, &s.wo[l]));
+      // 2F/world rows of the interleave-4 gate|up matrix: hidden units [rank*F/world, ...)
+      PB_TRY(slice_rows(ctx, m->gu[l], rank * 2 * p.hidden_chunk, 2 * p.hidden_chunk, &s.gu[l]));
+      PB_TRY(slice_rows(ctx, m->w2[l], rank * p.dim_chunk, p.dim_chunk, &s.w2[l]));
+    }
+    // head rows [vocab_row0, +vocab_rows) of the tiled table: whole 8-row tiles
+    const pb_qmat* h = head_of(m);
+    PB_TRY(pb_qmat_alloc(ctx, h->type, PB_LAYOUT_TILED8, p.vocab_rows, c.dim, &s.head));
+    const size_t qb = h->type == PB_TYPE_Q8_0 ? 32 : 16, slots = (size_t)pb_cdiv(p.vocab_rows, 8) * 8 * h->nb;
+    const size_t s0 = (size_t)pb_qslot(p.vocab_row0, 0, h->nb);
+    PB_TRY_CUDA(ctx, cudaMemcpyAsync(s.head->qs, h->qs + s0 * qb, slots * qb, cudaMemcpyDeviceToDevice, ctx->stream));
+    PB_TRY_CUDA(ctx, cudaMemcpyAsync(s.head->d, h->d + s0, slots * 2, cudaMemcpyDeviceToDevice, ctx->stream));
+  }
+  const size_t kv = (size_t)L * b->B * c.seq_len * p.n_kv_heads * hd;
+  PB_TRY_CUDA(ctx, cudaMalloc(&s.kc, kv * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&s.vc, kv * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&s.xl, (size_t)b->B * c.dim * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&s.logits, (size_t)b->world * b->B * p.vocab_chunk * 4));
+  PB_TRY_CUDA(ctx, cudaMalloc(&s.keys, (size_t)b->world * b->B * 8));
+  PB_TRY_CUDA(ctx, cudaMemsetAsync(s.kc, 0, kv * 4, ctx->stream));
+  PB_TRY_CUDA(ctx, cudaMemsetAsync(s.vc, 0, kv * 4, ctx->stream));
+  return PB_OK;
+}
+
+__global__ void k_gather_last(const float* __restrict__ x, int rows_per_seq, int dim, int xc, int rows,
+                              float* __restrict__ out) {
   const int s = blockIdx.y, d = blockIdx.x * blockDim.x + threadIdx.x;
-  if (d < dim) out[(size_t)s * dim + d] = x[((size_t)s * rows_per_seq + rows_per_seq - 1) * dim + d];
+  if (d >= dim) return;
+  const size_t row = (size_t)s * rows_per_seq + rows_per_seq - 1;
+  out[(size_t)s * dim + d] = x[(size_t)(d / xc) * rows * xc + row * xc + d % xc];
+}
+
+// Embedding rows of a tiled Q4_0 / Q8_0 table (gguf.js:239-286 values) into
+// x's column chunks of width xc.
+__global__ void k_batch_embed(int type, const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int V,
+                              int dim, const int* __restrict__ toks, float* __restrict__ x, int xc, int rows, int* err) {
+  const int i = blockIdx.y, d = blockIdx.x * blockDim.x + threadIdx.x;
+  const int tok = toks[i];
+  if (tok < 0 || tok >= V) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) pb_raise(err, PB_DEVERR_TOKEN);
+    return;
+  }
+  if (d >= dim) return;
+  const int nb = dim / 32, b = d >> 5, j = d & 31;
+  const size_t slot = (size_t)pb_qslot(tok, b, nb);
+  const float sc = pb_f16_exact(dsc[slot]);
+  float v;
+  if (type == PB_TYPE_Q4_0) {
+    const uint8_t byte = qs[slot * 16 + (j & 15)];
+    v = __fmul_rn((float)((j < 16 ? (byte & 15) : (byte >> 4)) - 8), sc);
+  } else {
+    v = __fmul_rn((float)(int8_t)qs[slot * 32 + j], sc);
+  }
+  x[(size_t)(d / xc) * rows * xc + (size_t)i * xc + d % xc] = v;
 }
 
 // Greedy token of every row (llama-streaming.js:899-909: first strict maximum),
@@ -1091,6 +1262,46 @@ k_argmax_rows(const float* __restrict__ logits, int V, int* __restrict__ next, i
   }
 }
 
+// Argmax key of every row over this rank's vocab rows [v0, v0 + n) (row
+// stride ld): the key carries the global token index.
+__global__ void __launch_bounds__(1024)
+k_argmax_keys(const float* __restrict__ logits, int n, int ld, int v0, unsigned long long* __restrict__ keys) {
+  __shared__ unsigned long long red[32];
+  const int r = blockIdx.x;
+  unsigned long long key = 0ull;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long k = pb_argmax_key(logits[(size_t)r * ld + i], v0 + i);
+    key = k > key ? k : key;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
+    key = t > key ? t : key;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = key;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long best = 0ull;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+    keys[r] = best;
+  }
+}
+
+// The largest of the ranks' keys [world][B] per row: the global first maximum.
+__global__ void k_argmax_merge(const unsigned long long* __restrict__ keys, int world, int B, int* __restrict__ next,
+                               int* __restrict__ hist, const int* __restrict__ pos_dev, int hist_len) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= B) return;
+  unsigned long long best = 0ull;
+  for (int w = 0; w < world; ++w) best = keys[(size_t)w * B + r] > best ? keys[(size_t)w * B + r] : best;
+  const int tok = pb_argmax_index(best);
+  next[r] = tok;
+  if (hist && pos_dev) {
+    const int p = *pos_dev;
+    if (p >= 0 && p < hist_len) hist[(size_t)p * B + r] = tok;
+  }
+}
+
 __global__ void k_batch_step_end(int* __restrict__ pos_dev) {
   if (threadIdx.x == 0 && blockIdx.x == 0) *pos_dev += 1;
 }
@@ -1108,17 +1319,21 @@ static int batch_ensure_rows(pb_batch* b, int rows) {
   pb_ctx* ctx = m->ctx;
   PB_TRY(pb_wait(ctx));
   batch_free_graph(b);  // a recorded graph holds the old buffer addresses
-  cudaFree(b->x); cudaFree(b->xn); cudaFree(b->qkvo); cudaFree(b->att); cudaFree(b->hb); cudaFree(b->toks);
-  b->x = b->xn = b->qkvo = b->att = b->hb = nullptr;
+  cudaFree(b->toks);
   b->toks = nullptr;
   b->rows_cap = 0;
   const pb_model_config& c = m->c;
-  const size_t qkvw = (size_t)c.dim + 2 * m->kv_dim;
-  PB_TRY_CUDA(ctx, cudaMalloc(&b->x, (size_t)rows * c.dim * 4));
-  PB_TRY_CUDA(ctx, cudaMalloc(&b->xn, (size_t)rows * c.dim * 4));
-  PB_TRY_CUDA(ctx, cudaMalloc(&b->qkvo, (size_t)rows * qkvw * 4));
-  PB_TRY_CUDA(ctx, cudaMalloc(&b->att, (size_t)rows * c.dim * 4));
-  PB_TRY_CUDA(ctx, cudaMalloc(&b->hb, (size_t)rows * c.hidden_dim * 4));
+  for (auto& s : b->sh) {
+    cudaFree(s.x); cudaFree(s.xn); cudaFree(s.qkvo); cudaFree(s.att); cudaFree(s.hb);
+    s.x = s.xn = s.qkvo = s.att = s.hb = nullptr;
+  }
+  for (auto& s : b->sh) {
+    PB_TRY_CUDA(ctx, cudaMalloc(&s.x, (size_t)rows * c.dim * 4));
+    PB_TRY_CUDA(ctx, cudaMalloc(&s.xn, (size_t)rows * c.dim * 4));
+    PB_TRY_CUDA(ctx, cudaMalloc(&s.qkvo, (size_t)rows * s.p.qkv_rows * 4));
+    PB_TRY_CUDA(ctx, cudaMalloc(&s.att, (size_t)rows * c.dim * 4));
+    PB_TRY_CUDA(ctx, cudaMalloc(&s.hb, (size_t)rows * c.hidden_dim * 4));
+  }
   PB_TRY_CUDA(ctx, cudaMalloc(&b->toks, (size_t)rows * 4));
   b->rows_cap = rows;
   return PB_OK;
@@ -1126,17 +1341,17 @@ static int batch_ensure_rows(pb_batch* b, int rows) {
 
 extern "C" int pb_batch_free(pb_batch* b) {
   if (!b) return PB_OK;
-  if (b->m && b->m->ctx) pb_wait(b->m->ctx);
-  batch_free_graph(b);
-  cudaFree(b->kc); cudaFree(b->vc); cudaFree(b->x); cudaFree(b->xn); cudaFree(b->qkvo); cudaFree(b->att);
-  cudaFree(b->hb); cudaFree(b->xl); cudaFree(b->logits); cudaFree(b->toks);
-  cudaFree(b->next); cudaFree(b->pos_dev); cudaFree(b->hist); cudaFree(b->ws);
+  pb_ctx* ctx = b->m ? b->m->ctx : nullptr;
+  if (ctx) pb_wait(ctx);
+  batch_free_graph(b);  // before the communicator its NCCL nodes use goes away
+  for (auto& s : b->sh) shard_free(ctx, s);
+  cudaFree(b->toks); cudaFree(b->next); cudaFree(b->pos_dev); cudaFree(b->hist); cudaFree(b->ws);
   delete b;
   return PB_OK;
 }
 
-extern "C" int pb_batch_create(pb_model* m, int n_seqs, pb_batch** out) {
-  if (!m || !out || n_seqs <= 0) return PB_ERR_ARG;
+static int batch_create(pb_model* m, int n_seqs, int world, pb_comm* comm, pb_batch** out) {
+  if (!m || !out || n_seqs <= 0 || world < 1) return PB_ERR_ARG;
   *out = nullptr;
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
@@ -1145,112 +1360,241 @@ extern "C" int pb_batch_create(pb_model* m, int n_seqs, pb_batch** out) {
   if (n_seqs > 256) return pb_set_error(ctx, PB_ERR_ARG, "at most 256 sequences per batch");
   if (c.kind != PB_MODEL_STREAMING_Q4 || !m->emb || m->emb->type != PB_TYPE_Q4_0 || head_of(m)->type != PB_TYPE_Q4_0)
     return pb_set_error(ctx, PB_ERR_ARG, "batched serving needs a streaming model with a Q4_0 embedding and head");
-  if (!pb_attn_decode_group_ok(c.n_heads, c.n_kv_heads, c.head_dim, c.seq_len))
+  if (!pb_attn_decode_group_ok(c.n_heads / world, c.n_kv_heads / world, c.head_dim, c.seq_len))
     return pb_set_error(ctx, PB_ERR_ARG, "batched decode attention needs <= 8 query heads per kv head, head_dim %% 4 "
                                          "== 0, head_dim <= 256 and the scores of a kv head in shared memory");
   pb_batch* b = new pb_batch();
   b->m = m;
   b->B = n_seqs;
+  b->world = world;
+  b->comm = comm;
   auto fail = [&](int rc) { pb_batch_free(b); return rc; };
-  const size_t kv = (size_t)c.n_layers * n_seqs * c.seq_len * m->kv_dim;
+  const int nshards = comm ? 1 : world;
+  b->sh.resize(nshards);
+  for (int i = 0; i < nshards; ++i) {
+    const int rc = shard_init(b, b->sh[i], comm ? pb_comm_rank(comm) : i);
+    if (rc != PB_OK) return fail(rc);
+  }
   const int widest = 2 * c.hidden_dim > c.dim + 2 * m->kv_dim ? 2 * c.hidden_dim : c.dim + 2 * m->kv_dim;
   b->ws_bytes = (size_t)8 * n_seqs * widest * 4;  // up to 8 K splits of the widest layer matrix
-  cudaError_t e = cudaMalloc(&b->kc, kv * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&b->vc, kv * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&b->xl, (size_t)n_seqs * c.dim * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&b->logits, (size_t)n_seqs * c.vocab * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&b->next, (size_t)n_seqs * 4);
+  cudaError_t e = cudaMalloc(&b->next, (size_t)n_seqs * 4);
   if (e == cudaSuccess) e = cudaMalloc(&b->pos_dev, 4);
   if (e == cudaSuccess) e = cudaMalloc(&b->hist, (size_t)(c.seq_len + 1) * n_seqs * 4);
   if (e == cudaSuccess) e = cudaMalloc(&b->ws, b->ws_bytes);
   if (e != cudaSuccess) return fail(pb_cuda_error(ctx, e, "batch allocation"));
-  cudaMemsetAsync(b->kc, 0, kv * 4, ctx->stream);
-  cudaMemsetAsync(b->vc, 0, kv * 4, ctx->stream);
   cudaMemsetAsync(b->hist, 0, (size_t)(c.seq_len + 1) * n_seqs * 4, ctx->stream);
   cudaMemsetAsync(b->pos_dev, 0, 4, ctx->stream);
+  const int rc = pb_wait(ctx);
+  if (rc != PB_OK) return fail(rc);
   *out = b;
   return PB_OK;
 }
 
-// One layer over `rows` token rows: n_seqs sequences of rows_per_seq rows each,
-// at positions start (or *pos_dev) + row-in-sequence.
-static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start_pos, const int* pos_dev) {
-  pb_model* m = b->m;
-  pb_ctx* ctx = m->ctx;
-  const pb_model_config& c = m->c;
-  const int dim = c.dim, F = c.hidden_dim, kv = m->kv_dim, qkvw = dim + 2 * kv;
-  const int64_t cache_seq = (int64_t)c.seq_len * kv;
-  float* kc = b->kc + (size_t)l * b->B * cache_seq;
-  float* vc = b->vc + (size_t)l * b->B * cache_seq;
-  // the norm writes the GEMM's f16 operand directly on the TMA path
-  __half* xn16 = reinterpret_cast<__half*>(b->xn);
-  if (pb_gemm_uses_tma(m->qkv[l], rows)) {
-    PB_TRY(launch_norm(m, b->x, rows, m->rms_att + (size_t)l * dim, nullptr, xn16));
-    PB_TRY(pb_launch_q4_gemm(ctx, m->qkv[l], nullptr, dim, rows, b->qkvo, qkvw, b->ws, b->ws_bytes, nullptr, xn16));
-  } else {
-    PB_TRY(launch_norm(m, b->x, rows, m->rms_att + (size_t)l * dim, b->xn));
-    PB_TRY(pb_launch_q4_gemm(ctx, m->qkv[l], b->xn, dim, rows, b->qkvo, qkvw, b->ws, b->ws_bytes));
-  }
-  {
-    const int tot = (c.n_heads + c.n_kv_heads) * (c.head_dim / 2) + kv;
-    k_rope_kv<<<dim3(pb_cdiv(tot, 128), rows), 128, 0, ctx->stream>>>(
-        b->qkvo, qkvw, b->qkvo + dim, qkvw, b->qkvo + dim + kv, qkvw, c.n_heads, c.n_kv_heads, c.head_dim, m->rope_tab,
-        start_pos, pos_dev, kc, vc, c.seq_len, rows_per_seq, cache_seq, ctx->d_err);
-    PB_LAUNCHED(ctx, "k_rope_kv");
-  }
-  pb_seq_geo geo;
-  geo.kv = cache_seq;
-  if (rows_per_seq == 1 && pos_dev) {
-    geo.q = qkvw;
-    geo.out = dim;
-    PB_TRY(pb_launch_attn_decode(ctx, b->qkvo, kc, vc, pos_dev, c.n_heads, c.n_kv_heads, c.head_dim, b->att,
-                                 c.seq_len, b->B, geo));
-  } else {
-    geo.q = (int64_t)rows_per_seq * qkvw;
-    geo.out = (int64_t)rows_per_seq * dim;
-    if (c.head_dim == 64 && !pos_dev)
-      PB_TRY(pb_launch_attn_prefill(ctx, b->qkvo, qkvw, kc, vc, rows_per_seq, start_pos, c.n_heads, c.n_kv_heads,
-                                        c.head_dim, b->att, b->B, geo));
-    else
-      PB_TRY(pb_launch_attn_cached(ctx, b->qkvo, qkvw, kc, vc, rows_per_seq, start_pos, pos_dev, c.n_heads,
-                                   c.n_kv_heads, c.head_dim, b->att, c.seq_len, b->B, geo));
-  }
-  // wo with the residual add in the GEMM epilogue (llama-streaming.js:579-580)
-  pb_gemm_epi add;
-  add.mode = PB_GEMM_ADD;
-  PB_TRY(pb_launch_q4_gemm(ctx, m->wo[l], b->att, dim, rows, b->x, dim, b->ws, b->ws_bytes, &add));
-  const bool gu16 = pb_gemm_uses_tma(m->gu[l], rows);
-  PB_TRY(launch_norm(m, b->x, rows, m->rms_ffn + (size_t)l * dim, gu16 ? nullptr : b->xn, gu16 ? xn16 : nullptr));
-  // gate|up with SwiGLU in the epilogue (f32); h goes out as the down
-  // GEMM's operand: f16 for the TMA path, f32 otherwise
-  const bool h16 = pb_gemm_uses_tma(m->w2[l], rows);
-  pb_gemm_epi glu;
-  glu.mode = PB_GEMM_SWIGLU;
-  if (h16) glu.h16 = reinterpret_cast<__half*>(b->hb);
-  else glu.h32 = b->hb;
-  if (gu16)
-    PB_TRY(pb_launch_q4_gemm(ctx, m->gu[l], nullptr, dim, rows, nullptr, 2 * F, b->ws, b->ws_bytes, &glu, xn16));
-  else
-    PB_TRY(pb_launch_q4_gemm(ctx, m->gu[l], b->xn, dim, rows, nullptr, 2 * F, b->ws, b->ws_bytes, &glu));
-  // down with the residual add (:601)
-  if (h16)
-    PB_TRY(pb_launch_q4_gemm(ctx, m->w2[l], nullptr, F, rows, b->x, dim, b->ws, b->ws_bytes, &add,
-                             reinterpret_cast<const __half*>(b->hb)));
-  else
-    PB_TRY(pb_launch_q4_gemm(ctx, m->w2[l], b->hb, F, rows, b->x, dim, b->ws, b->ws_bytes, &add));
+extern "C" int pb_batch_create(pb_model* m, int n_seqs, pb_batch** out) {
+  return batch_create(m, n_seqs, 1, nullptr, out);
+}
+
+extern "C" int pb_batch_create_split(pb_model* m, int n_seqs, pb_comm* comm, pb_batch** out) {
+  if (!m || !comm || pb_comm_ctx(comm) != m->ctx) return PB_ERR_ARG;
+  const int world = pb_comm_world(comm);
+  return batch_create(m, n_seqs, world, world > 1 ? comm : nullptr, out);
+}
+
+extern "C" int pb_batch_create_group(pb_model* m, int n_seqs, int world, pb_batch** out) {
+  return batch_create(m, n_seqs, world, nullptr, out);
+}
+
+// In-place all-gather of chunk_bytes per rank: chunk r of buffer `field` is
+// rank r's; afterwards every shard's buffer holds every chunk.
+template <class F>
+static int batch_gather(pb_batch* b, F field, size_t chunk_bytes) {
+  if (b->world == 1) return PB_OK;
+  pb_ctx* ctx = b->m->ctx;
+  if (b->comm) return pb_comm_gather_inplace(b->comm, field(b->sh[0]), chunk_bytes);
+  for (auto& dst : b->sh)
+    for (auto& src : b->sh) {
+      if (&dst == &src) continue;
+      const size_t off = (size_t)src.rank * chunk_bytes;
+      PB_TRY_CUDA(ctx, cudaMemcpyAsync(reinterpret_cast<char*>(field(dst)) + off,
+                                       reinterpret_cast<char*>(field(src)) + off, chunk_bytes,
+                                       cudaMemcpyDeviceToDevice, ctx->stream));
+    }
   return PB_OK;
 }
 
-// Final RMSNorm of each sequence's last row, the LM head as one GEMM over the
-// table, the greedy token of every sequence.
-static int batch_head(pb_batch* b, const float* last_rows, const int* pos_dev) {
+// The x_chunk of an operand stored in `width`-wide chunks (0 when unsplit).
+static int chunk_of(const pb_batch* b, int width) { return b->world > 1 ? width : 0; }
+
+// norm -> this rank's q | k | v -> RoPE + KV append -> attention of its heads
+// into its chunk of att.
+static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_per_seq, int start_pos,
+                           const int* pos_dev) {
   pb_model* m = b->m;
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
-  PB_TRY(launch_norm(m, last_rows, b->B, m->rms_final, b->xn));
-  PB_TRY(pb_launch_q4_gemm(ctx, head_of(m), b->xn, c.dim, b->B, b->logits, c.vocab, nullptr, 0));
-  k_argmax_rows<<<b->B, 1024, 0, ctx->stream>>>(b->logits, c.vocab, b->next, b->hist, pos_dev, c.seq_len + 1);
-  PB_LAUNCHED(ctx, "k_argmax_rows");
+  const pb_split_plan& p = s.p;
+  const int dim = c.dim, hd = c.head_dim, qw = p.qkv_rows, dc = p.dim_chunk, kvl = p.n_kv_heads * hd;
+  const int64_t cache_seq = (int64_t)c.seq_len * kvl;
+  float* kc = s.kc + (size_t)l * b->B * cache_seq;
+  float* vc = s.vc + (size_t)l * b->B * cache_seq;
+  pb_gemm_epi st;
+  st.split_n = dim + 2 * m->kv_dim;
+  // the norm writes the GEMM's f16 operand directly on the TMA path
+  __half* xn16 = reinterpret_cast<__half*>(s.xn);
+  if (pb_gemm_uses_tma(s.qkv[l], rows)) {
+    PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, nullptr, xn16, dc));
+    PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], nullptr, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st, xn16));
+  } else {
+    PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, s.xn, nullptr, dc));
+    PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], s.xn, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st));
+  }
+  {
+    const int tot = (p.n_heads + p.n_kv_heads) * (hd / 2) + kvl;
+    k_rope_kv<<<dim3(pb_cdiv(tot, 128), rows), 128, 0, ctx->stream>>>(
+        s.qkvo, qw, s.qkvo + p.n_heads * hd, qw, s.qkvo + (p.n_heads + p.n_kv_heads) * hd, qw, p.n_heads,
+        p.n_kv_heads, hd, m->rope_tab, start_pos, pos_dev, kc, vc, c.seq_len, rows_per_seq, cache_seq, ctx->d_err);
+    PB_LAUNCHED(ctx, "k_rope_kv");
+  }
+  float* att = s.att + (size_t)s.rank * rows * dc;
+  pb_seq_geo geo;
+  geo.kv = cache_seq;
+  if (rows_per_seq == 1 && pos_dev) {
+    geo.q = qw;
+    geo.out = dc;
+    return pb_launch_attn_decode(ctx, s.qkvo, kc, vc, pos_dev, p.n_heads, p.n_kv_heads, hd, att, c.seq_len, b->B, geo);
+  }
+  geo.q = (int64_t)rows_per_seq * qw;
+  geo.out = (int64_t)rows_per_seq * dc;
+  if (hd == 64 && !pos_dev)
+    return pb_launch_attn_prefill(ctx, s.qkvo, qw, kc, vc, rows_per_seq, start_pos, p.n_heads, p.n_kv_heads, hd, att,
+                                  b->B, geo);
+  return pb_launch_attn_cached(ctx, s.qkvo, qw, kc, vc, rows_per_seq, start_pos, pos_dev, p.n_heads, p.n_kv_heads, hd,
+                               att, c.seq_len, b->B, geo);
+}
+
+// this rank's rows of wo with the residual add into its chunk of x
+// (llama-streaming.js:579-580)
+static int shard_wo(pb_batch* b, pb_shard& s, int l, int rows) {
+  pb_model* m = b->m;
+  const int dc = s.p.dim_chunk;
+  pb_gemm_epi add;
+  add.mode = PB_GEMM_ADD;
+  add.x_chunk = chunk_of(b, dc);
+  add.split_n = m->c.dim;
+  return pb_launch_q4_gemm(m->ctx, s.wo[l], s.att, m->c.dim, rows, s.x + (size_t)s.rank * rows * dc, dc, b->ws,
+                           b->ws_bytes, &add);
+}
+
+static bool hidden_f16(const pb_batch* b, const pb_shard& s, int l, int rows) { return pb_gemm_uses_tma(s.w2[l], rows); }
+
+// norm -> this rank's gate|up rows with SwiGLU in the epilogue, h into its
+// chunk of hb (f16 for the TMA path of w2, f32 otherwise)
+static int shard_gate_up(pb_batch* b, pb_shard& s, int l, int rows) {
+  pb_model* m = b->m;
+  pb_ctx* ctx = m->ctx;
+  const int dim = m->c.dim, fc = s.p.hidden_chunk;
+  const bool gu16 = pb_gemm_uses_tma(s.gu[l], rows);
+  __half* xn16 = reinterpret_cast<__half*>(s.xn);
+  PB_TRY(launch_norm(m, s.x, rows, m->rms_ffn + (size_t)l * dim, gu16 ? nullptr : s.xn, gu16 ? xn16 : nullptr,
+                     s.p.dim_chunk));
+  pb_gemm_epi glu;
+  glu.mode = PB_GEMM_SWIGLU;
+  glu.split_n = 2 * m->c.hidden_dim;
+  const size_t off = (size_t)s.rank * rows * fc;
+  if (hidden_f16(b, s, l, rows)) glu.h16 = reinterpret_cast<__half*>(s.hb) + off;
+  else glu.h32 = s.hb + off;
+  if (gu16) return pb_launch_q4_gemm(ctx, s.gu[l], nullptr, dim, rows, nullptr, 2 * fc, b->ws, b->ws_bytes, &glu, xn16);
+  return pb_launch_q4_gemm(ctx, s.gu[l], s.xn, dim, rows, nullptr, 2 * fc, b->ws, b->ws_bytes, &glu);
+}
+
+// this rank's rows of w2 with the residual add into its chunk of x (:601)
+static int shard_down(pb_batch* b, pb_shard& s, int l, int rows) {
+  pb_model* m = b->m;
+  const int F = m->c.hidden_dim, dc = s.p.dim_chunk;
+  pb_gemm_epi add;
+  add.mode = PB_GEMM_ADD;
+  add.x_chunk = chunk_of(b, s.p.hidden_chunk);
+  add.split_n = m->c.dim;
+  float* C = s.x + (size_t)s.rank * rows * dc;
+  if (hidden_f16(b, s, l, rows))
+    return pb_launch_q4_gemm(m->ctx, s.w2[l], nullptr, F, rows, C, dc, b->ws, b->ws_bytes, &add,
+                             reinterpret_cast<const __half*>(s.hb));
+  return pb_launch_q4_gemm(m->ctx, s.w2[l], s.hb, F, rows, C, dc, b->ws, b->ws_bytes, &add);
+}
+
+// One layer over `rows` token rows: n_seqs sequences of rows_per_seq rows each,
+// at positions start (or *pos_dev) + row-in-sequence.  Each phase runs on
+// every shard of this process, then the all-gather that the next phase needs.
+static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start_pos, const int* pos_dev) {
+  const pb_model_config& c = b->m->c;
+  const size_t dchunk = (size_t)rows * (c.dim / b->world) * 4;
+  for (auto& s : b->sh) PB_TRY(shard_attention(b, s, l, rows, rows_per_seq, start_pos, pos_dev));
+  PB_TRY(batch_gather(b, [](pb_shard& s) { return (void*)s.att; }, dchunk));
+  for (auto& s : b->sh) PB_TRY(shard_wo(b, s, l, rows));
+  PB_TRY(batch_gather(b, [](pb_shard& s) { return (void*)s.x; }, dchunk));
+  for (auto& s : b->sh) PB_TRY(shard_gate_up(b, s, l, rows));
+  const size_t hchunk = (size_t)rows * (c.hidden_dim / b->world) * (hidden_f16(b, b->sh[0], l, rows) ? 2 : 4);
+  PB_TRY(batch_gather(b, [](pb_shard& s) { return (void*)s.hb; }, hchunk));
+  for (auto& s : b->sh) PB_TRY(shard_down(b, s, l, rows));
+  return batch_gather(b, [](pb_shard& s) { return (void*)s.x; }, dchunk);
+}
+
+// Final RMSNorm of each sequence's last row (xl, or x itself when every row
+// is a last row), the LM head as one GEMM over this rank's vocab rows, the
+// greedy token of every sequence.
+static int batch_head(pb_batch* b, bool from_x, const int* pos_dev) {
+  pb_model* m = b->m;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  for (auto& s : b->sh) {
+    if (from_x) PB_TRY(launch_norm(m, s.x, b->B, m->rms_final, s.xn, nullptr, s.p.dim_chunk));
+    else PB_TRY(launch_norm(m, s.xl, b->B, m->rms_final, s.xn));
+    const int vc = s.p.vocab_chunk;
+    float* lg = s.logits + (size_t)s.rank * b->B * vc;
+    PB_TRY(pb_launch_q4_gemm(ctx, s.head, s.xn, c.dim, b->B, lg, vc, nullptr, 0));
+    if (b->world == 1) {
+      k_argmax_rows<<<b->B, 1024, 0, ctx->stream>>>(lg, c.vocab, b->next, b->hist, pos_dev, c.seq_len + 1);
+      PB_LAUNCHED(ctx, "k_argmax_rows");
+      return PB_OK;
+    }
+    k_argmax_keys<<<b->B, 1024, 0, ctx->stream>>>(lg, s.p.vocab_rows, vc, s.p.vocab_row0, s.keys + (size_t)s.rank * b->B);
+    PB_LAUNCHED(ctx, "k_argmax_keys");
+  }
+  PB_TRY(batch_gather(b, [](pb_shard& s) { return (void*)s.keys; }, (size_t)b->B * 8));
+  k_argmax_merge<<<pb_cdiv(b->B, 128), 128, 0, ctx->stream>>>(b->sh[0].keys, b->world, b->B, b->next, b->hist, pos_dev,
+                                                             c.seq_len + 1);
+  PB_LAUNCHED(ctx, "k_argmax_merge");
+  return PB_OK;
+}
+
+// Embedding of `rows` tokens into every shard's x.
+static int batch_embed(pb_batch* b, const int* toks, int rows) {
+  pb_model* m = b->m;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  for (auto& s : b->sh) {
+    k_batch_embed<<<dim3(pb_cdiv(c.dim, 256), rows), 256, 0, ctx->stream>>>(
+        m->emb->type, m->emb->qs, m->emb->d, c.vocab, c.dim, toks, s.x, s.p.dim_chunk, rows, ctx->d_err);
+    PB_LAUNCHED(ctx, "k_batch_embed");
+  }
+  return PB_OK;
+}
+
+// Every rank's logits [B][vocab] to the host (an all-gather of the chunks
+// first across processes).
+static int batch_logits_to_host(pb_batch* b, float* host) {
+  pb_ctx* ctx = b->m->ctx;
+  const pb_model_config& c = b->m->c;
+  const int vc = b->sh[0].p.vocab_chunk;
+  if (b->comm) PB_TRY(batch_gather(b, [](pb_shard& s) { return (void*)s.logits; }, (size_t)b->B * vc * 4));
+  for (int r = 0; r < b->world; ++r) {
+    const pb_shard& s = b->comm ? b->sh[0] : b->sh[r];
+    pb_split_plan p;
+    PB_TRY(pb_batch_split_plan(&c, b->world, r, &p));
+    PB_TRY_CUDA(ctx, cudaMemcpy2DAsync(host + p.vocab_row0, (size_t)c.vocab * 4, s.logits + (size_t)r * b->B * vc,
+                                       (size_t)vc * 4, (size_t)p.vocab_rows * 4, b->B, cudaMemcpyDeviceToHost,
+                                       ctx->stream));
+  }
   return PB_OK;
 }
 
@@ -1265,23 +1609,21 @@ extern "C" int pb_batch_prefill(pb_batch* b, const int* tokens_host, int n_promp
   PB_TRY(batch_ensure_rows(b, rows));
   b->P = n_prompt;
   PB_TRY_CUDA(ctx, cudaMemcpyAsync(b->toks, tokens_host, (size_t)rows * 4, cudaMemcpyHostToDevice, ctx->stream));
-  k_embed<<<dim3(pb_cdiv(c.dim, 256), rows), 256, 0, ctx->stream>>>(PB_TYPE_Q4_0, m->emb->qs, m->emb->d, nullptr,
-                                                                    c.vocab, c.dim, b->toks, nullptr, nullptr, nullptr,
-                                                                    b->x, ctx->d_err);
-  PB_LAUNCHED(ctx, "k_embed");
+  PB_TRY(batch_embed(b, b->toks, rows));
   for (int l = 0; l < c.n_layers; ++l) PB_TRY(batch_layer(b, l, rows, n_prompt, 0, nullptr));
-  k_gather_last<<<dim3(pb_cdiv(c.dim, 256), b->B), 256, 0, ctx->stream>>>(b->x, n_prompt, c.dim, b->xl);
-  PB_LAUNCHED(ctx, "k_gather_last");
+  for (auto& s : b->sh) {
+    k_gather_last<<<dim3(pb_cdiv(c.dim, 256), b->B), 256, 0, ctx->stream>>>(s.x, n_prompt, c.dim, s.p.dim_chunk, rows,
+                                                                            s.xl);
+    PB_LAUNCHED(ctx, "k_gather_last");
+  }
   // the greedy token after the prompt is recorded at position n_prompt - 1
   const int last = n_prompt - 1;
   PB_TRY_CUDA(ctx, cudaMemcpyAsync(b->pos_dev, &last, 4, cudaMemcpyHostToDevice, ctx->stream));
-  PB_TRY(batch_head(b, b->xl, b->pos_dev));
+  PB_TRY(batch_head(b, false, b->pos_dev));
   PB_TRY_CUDA(ctx, cudaMemcpyAsync(b->pos_dev, &n_prompt, 4, cudaMemcpyHostToDevice, ctx->stream));
   if (next_host)
     PB_TRY_CUDA(ctx, cudaMemcpyAsync(next_host, b->next, (size_t)b->B * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  if (logits_host)
-    PB_TRY_CUDA(ctx, cudaMemcpyAsync(logits_host, b->logits, (size_t)b->B * c.vocab * 4, cudaMemcpyDeviceToHost,
-                                     ctx->stream));
+  if (logits_host) PB_TRY(batch_logits_to_host(b, logits_host));
   return pb_wait(ctx);
 }
 
@@ -1291,12 +1633,9 @@ static int batch_enqueue_step(pb_batch* b) {
   pb_model* m = b->m;
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
-  k_embed<<<dim3(pb_cdiv(c.dim, 256), b->B), 256, 0, ctx->stream>>>(PB_TYPE_Q4_0, m->emb->qs, m->emb->d, nullptr,
-                                                                    c.vocab, c.dim, b->next, nullptr, nullptr, nullptr,
-                                                                    b->x, ctx->d_err);
-  PB_LAUNCHED(ctx, "k_embed");
+  PB_TRY(batch_embed(b, b->next, b->B));
   for (int l = 0; l < c.n_layers; ++l) PB_TRY(batch_layer(b, l, b->B, 1, 0, b->pos_dev));
-  PB_TRY(batch_head(b, b->x, b->pos_dev));
+  PB_TRY(batch_head(b, true, b->pos_dev));
   k_batch_step_end<<<1, 32, 0, ctx->stream>>>(b->pos_dev);
   PB_LAUNCHED(ctx, "k_batch_step_end");
   return PB_OK;
@@ -1329,8 +1668,6 @@ extern "C" int pb_batch_decode(pb_batch* b, int steps, int* tokens_host, float* 
   if (tokens_host)
     PB_TRY_CUDA(ctx, cudaMemcpyAsync(tokens_host, b->hist + (size_t)pos * b->B, (size_t)steps * b->B * 4,
                                      cudaMemcpyDeviceToHost, ctx->stream));
-  if (logits_host)
-    PB_TRY_CUDA(ctx, cudaMemcpyAsync(logits_host, b->logits, (size_t)b->B * c.vocab * 4, cudaMemcpyDeviceToHost,
-                                     ctx->stream));
+  if (logits_host) PB_TRY(batch_logits_to_host(b, logits_host));
   return pb_wait(ctx);
 }

@@ -24,27 +24,35 @@
 // With out16 (the batched path's f16 GEMM operand) the row is scaled in f32
 // by 1/rms and rounded to f16 once; otherwise the reference's double
 // arithmetic in f32 out.
+// One row per CTA.  xc > 0: x is stored in column chunks of width xc, chunk
+// c at x + c * gridDim.x * xc (the row-split batch's replicated residual);
+// the output rows are row-major either way.
 __global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
-                          float* __restrict__ out, __half* __restrict__ out16) {
+                          float* __restrict__ out, __half* __restrict__ out16, int xc) {
   __shared__ double red[32];
-  const float* xr = x + (size_t)blockIdx.x * dim;
+  const size_t row = blockIdx.x;
+  const float* xr = x + row * (xc ? xc : dim);
+  const size_t cs = (size_t)gridDim.x * xc;
+  auto X = [&](int d) { return xc ? xr[(size_t)(d / xc) * cs + d % xc] : xr[d]; };
   double ss = 0.0;
-  for (int d = threadIdx.x; d < dim; d += blockDim.x) ss = __fma_rn((double)xr[d], (double)xr[d], ss);
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    const double v = (double)X(d);
+    ss = __fma_rn(v, v, ss);
+  }
   ss = pb_block_sum_d(ss, red);
   double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)dim), eps));
   if (out16) {
     const float inv = (float)(1.0 / rms);
-    for (int d = threadIdx.x; d < dim; d += blockDim.x)
-      out16[(size_t)blockIdx.x * dim + d] = __float2half_rn(xr[d] * inv * w[d]);
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) out16[row * dim + d] = __float2half_rn(X(d) * inv * w[d]);
     return;
   }
   for (int d = threadIdx.x; d < dim; d += blockDim.x)
-    out[(size_t)blockIdx.x * dim + d] = (float)__dmul_rn(__ddiv_rn((double)xr[d], rms), (double)w[d]);
+    out[row * dim + d] = (float)__dmul_rn(__ddiv_rn((double)X(d), rms), (double)w[d]);
 }
 
 extern "C" int pb_rmsnorm(pb_ctx* ctx, const float* x, int seq, int dim, const float* w, double eps, float* out) {
   if (!ctx || !x || !w || !out || seq <= 0 || dim <= 0) return PB_ERR_ARG;
-  k_rmsnorm<<<seq, 256, 0, ctx->stream>>>(x, dim, w, eps, out, nullptr);
+  k_rmsnorm<<<seq, 256, 0, ctx->stream>>>(x, dim, w, eps, out, nullptr, 0);
   PB_LAUNCHED(ctx, "k_rmsnorm");
   return PB_OK;
 }

@@ -391,14 +391,30 @@ class BatchedLlamaRuntime:
     """n_seqs sequences decoded together over one StreamingLlamaRuntime's
     weights (the batched configuration).  The projections and the LM head
     run as tensor-core GEMMs with f16 operands, so logits agree with the
-    one-sequence runtime within a relative tolerance, not bit for bit."""
+    one-sequence runtime within a relative tolerance, not bit for bit.
 
-    def __init__(self, base: StreamingLlamaRuntime, n_seqs: int):
+    comm (thread_pool.NcclComm): this process is one rank of a row split
+    over comm's GPUs (pb_batch_create_split); every rank calls prefill and
+    decode with the same arguments and gets the same tokens and logits.
+    group=w: all w ranks of a row split in this process on one device
+    (pb_batch_create_group), the split's arithmetic without a second GPU.
+    Both give the same bits as the unsplit batch."""
+
+    def __init__(self, base: StreamingLlamaRuntime, n_seqs: int, comm=None, group: int = 0):
         self.base = base
         self.ctx = base.ctx
         self.n_seqs = n_seqs
+        self.comm = comm
         h = ctypes.c_void_p()
-        self.ctx._check(N.lib().pb_batch_create(base.model.h, n_seqs, ctypes.byref(h)))
+        if comm is not None:
+            self.world = comm.world
+            self.ctx._check(N.lib().pb_batch_create_split(base.model.h, n_seqs, comm.h, ctypes.byref(h)))
+        elif group:
+            self.world = int(group)
+            self.ctx._check(N.lib().pb_batch_create_group(base.model.h, n_seqs, self.world, ctypes.byref(h)))
+        else:
+            self.world = 1
+            self.ctx._check(N.lib().pb_batch_create(base.model.h, n_seqs, ctypes.byref(h)))
         self.h = h.value
         self.n_prompt = 0
 

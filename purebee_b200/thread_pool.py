@@ -138,3 +138,75 @@ class AtomicsThreadPool:
 
     def shutdown(self) -> None:
         pass
+
+
+def split_plan(config, world: int, rank: int) -> "N_.SplitPlan":
+    """pb_batch_split_plan: the rows `rank` of `world` holds in a row-split
+    batch (heads, wo / w2 / gate|up row chunks, vocab rows).  `config` is a
+    ModelConfig or a LlamaConfig."""
+    if isinstance(config, N_.ModelConfig):
+        c = config
+    else:
+        c = N_.ModelConfig(N_.MODEL_STREAMING_Q4, N_.TYPE_Q4_0, config.dim, config.hiddenDim, config.nLayers,
+                           config.nHeads, config.nKvHeads, config.headDim, config.vocabSize, config.seqLen,
+                           config.ropeTheta, config.rmsNormEps)
+    p = N_.SplitPlan()
+    rc = N_.lib().pb_batch_split_plan(ctypes.byref(c), int(world), int(rank), ctypes.byref(p))
+    if rc != N_.PB_OK:
+        raise ValueError(f"no row split of this model over {world} ranks (n_kv_heads, dim / 64 and hidden_dim / 64 "
+                         f"must divide by it)")
+    return p
+
+
+class NcclComm:
+    """An NCCL communicator of the library (pb_comm), one rank per process and
+    device: the row-split batch's all-gathers run on it, inside the recorded
+    decode graph.  `from_torch` sends rank 0's unique id to the other ranks
+    over an initialised torch.distributed group (any backend)."""
+
+    def __init__(self, ctx, world: int, rank: int, uid: bytes):
+        if len(uid) != N_.COMM_ID_BYTES:
+            raise ValueError("an NCCL unique id is 128 bytes")
+        self.ctx = ctx
+        self.world, self.rank = int(world), int(rank)
+        buf = ctypes.create_string_buffer(bytes(uid), N_.COMM_ID_BYTES)
+        h = ctypes.c_void_p()
+        ctx._check(N_.lib().pb_comm_init(ctx.h, self.world, self.rank, buf, ctypes.byref(h)))
+        self.h = h.value
+
+    @staticmethod
+    def new_id() -> bytes:
+        buf = ctypes.create_string_buffer(N_.COMM_ID_BYTES)
+        if N_.lib().pb_comm_id(buf) != N_.PB_OK:
+            raise RuntimeError("ncclGetUniqueId failed (is libnccl.so.2 present?)")
+        return buf.raw
+
+    @staticmethod
+    def exchange_id(group=None) -> bytes:
+        """Rank 0 makes the id; every rank returns it."""
+        import torch.distributed as dist
+        obj = [NcclComm.new_id() if dist.get_rank(group) == 0 else None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        return obj[0]
+
+    @classmethod
+    def from_torch(cls, ctx, group=None) -> "NcclComm":
+        import torch.distributed as dist
+        uid = cls.exchange_id(group)
+        return cls(ctx, dist.get_world_size(group), dist.get_rank(group), uid)
+
+    def allgather(self, send_ptr: int, recv_ptr: int, nbytes: int) -> None:
+        """recv [world][nbytes] <- every rank's send [nbytes] (device pointers,
+        on the context's stream)."""
+        self.ctx._check(N_.lib().pb_comm_allgather(self.h, send_ptr, recv_ptr, int(nbytes)))
+
+    def free(self):
+        if getattr(self, "h", None) and self.ctx.h:
+            N_.lib().pb_comm_free(self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
