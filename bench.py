@@ -238,32 +238,54 @@ def row_split_vocab(ctx, torch, dist, world, peak, reps=40):
             "frac_local_of_measured_peak_per_gpu": round((slice_bytes + 4 * k + 4 * per) / (local_us * 1e-6) / 1e9 / peak, 3)}
 
 
-def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512, steps=256):
-    """configs[4] on this GPU: n_seqs seeded prompts of n_prompt tokens
-    prefilled as one batch (tensor-core GEMMs), then `steps` greedy decode
-    steps of every sequence (one replayed graph per step).  Device event
-    times; the linear-layer FLOPs of the prefill give its tensor roofline."""
+def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512, steps=256, dist=None):
+    """n_seqs seeded prompts of n_prompt tokens prefilled as one
+    batch (tensor-core GEMMs), then `steps` greedy decode steps of every
+    sequence (one replayed graph per step).  With N ranks the model is row
+    split over the N GPUs (pb_batch_create_split: each GPU holds 1/N of every
+    projection, of the head and of the KV cache; NCCL all-gathers inside the
+    step), so the work is fixed and the time falls with N (strong scaling).
+    Device event times, max over ranks; the linear-layer FLOPs of the prefill
+    give its tensor roofline against N GPUs' peak."""
     from purebee_b200.runtime import BatchedLlamaRuntime
+    from purebee_b200.thread_pool import NcclComm
     c = CFG
+    world = dist.get_world_size() if dist else 1
     rng = np.random.default_rng(SEED + 5)
     prompts = rng.integers(1, c["vocab"], (n_seqs, n_prompt)).astype(np.int32)
-    bt = BatchedLlamaRuntime(rt, n_seqs)
+    comm = NcclComm.from_torch(ctx) if world > 1 else None
+    bt = BatchedLlamaRuntime(rt, n_seqs, comm=comm)
+    dev = torch.device("cuda", ctx.device) if hasattr(ctx, "device") else torch.device("cuda")
+
+    def max_over_ranks(ms):
+        if not dist:
+            return ms
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     bt.prefill(prompts)  # warm, at full size: activation buffers, GEMM scratch, kernels
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     ctx.sync()
+    if dist:
+        dist.barrier()
     e0.record(stream)
     bt.prefill(prompts)
     e1.record(stream)
     e1.synchronize()
-    prefill_ms = e0.elapsed_time(e1)
+    prefill_ms = max_over_ranks(e0.elapsed_time(e1))
     bt.decode(2)  # warm: records the decode graph
     ctx.sync()
+    if dist:
+        dist.barrier()
     e1.record(stream)
     toks = bt.decode(steps)
     e2.record(stream)
     e2.synchronize()
-    decode_ms = e1.elapsed_time(e2)
-    bt.free()
+    decode_ms = max_over_ranks(e1.elapsed_time(e2))
+    bt.free()  # before the communicator: the decode graph holds its NCCL work
+    if comm is not None:
+        comm.free()
     d, F, L, V, kv = c["dim"], c["hidden_dim"], c["n_layers"], c["vocab"], c["n_kv_heads"] * c["head_dim"]
     lin_params = L * ((d + 2 * kv) * d + d * d + 2 * F * d + d * F)
     tokens = n_seqs * n_prompt
@@ -272,14 +294,20 @@ def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512
     mid = n_prompt + 2 + steps // 2
     step_bytes = lin_params * 18 / 32 + V * d * 18 / 32 + 2.0 * L * n_seqs * mid * kv * 4
     dec_s = decode_ms / 1e3 / steps
+    hd_bytes = n_seqs * d * 4
+    gathered = c["n_layers"] * (3 * hd_bytes + n_seqs * F * 4) + n_seqs * 8  # per step, whole buffers
     return {"workload": f"configs[4]: {n_seqs} seqs x {n_prompt}-token seeded prompts, then {steps} greedy steps",
+            "n_gpus": world, "scaling": "strong",
+            "parallelism": f"rowsplit{world} (NCCL all-gather x{4 * c['n_layers'] + 1} per step)" if world > 1
+            else "single-gpu",
             "prefill_ms": round(prefill_ms, 2), "prefill_tok_s": round(tokens / (prefill_ms / 1e3), 1),
             "prefill_linear_TFLOPs": round(lin_flops / (prefill_ms / 1e3) / 1e12, 1),
-            "prefill_frac_of_bf16_peak": round(lin_flops / (prefill_ms / 1e3) / 1e12 / flop_peak, 3),
+            "prefill_frac_of_bf16_peak": round(lin_flops / (prefill_ms / 1e3) / 1e12 / (world * flop_peak), 3),
             "decode_ms_per_step": round(decode_ms / steps, 3),
             "decode_tok_s": round(n_seqs / dec_s, 1),
             "decode_step_bytes": int(step_bytes),
-            "decode_frac_of_hbm": round(step_bytes / dec_s / 1e9 / peak, 3),
+            "decode_frac_of_hbm": round(step_bytes / dec_s / 1e9 / (world * peak), 3),
+            "decode_allgather_bytes_per_step": int(gathered) if world > 1 else 0,
             "tokens_sample": toks[-1][:4].tolist(),
             "arithmetic": "projections and head: f16 operands, f32 accumulation (tcgen05); prefill attention: f16 "
                           "operands, f32 accumulation (mma.sync)"}
@@ -362,7 +390,7 @@ def run_ours(args, rank, world, torch, dist):
     batched = None
     if not args.no_batched:
         rt.resetCache()
-        batched = run_batched(ctx, torch, stream, rt, peak, load_flop_peak())
+        batched = run_batched(ctx, torch, stream, rt, peak, load_flop_peak(), dist=dist)
 
     result = None
     if rank == 0:
