@@ -254,6 +254,7 @@ def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512
     rng = np.random.default_rng(SEED + 5)
     prompts = rng.integers(1, c["vocab"], (n_seqs, n_prompt)).astype(np.int32)
     comm = NcclComm.from_torch(ctx) if world > 1 else None
+    comm_p2p = bool(comm is not None and comm.peer_access)
     bt = BatchedLlamaRuntime(rt, n_seqs, comm=comm)
     dev = torch.device("cuda", ctx.device) if hasattr(ctx, "device") else torch.device("cuda")
 
@@ -298,8 +299,9 @@ def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512
     gathered = c["n_layers"] * (3 * hd_bytes + n_seqs * F * 4) + n_seqs * 8  # per step, whole buffers
     return {"workload": f"configs[4]: {n_seqs} seqs x {n_prompt}-token seeded prompts, then {steps} greedy steps",
             "n_gpus": world, "scaling": "strong",
-            "parallelism": f"rowsplit{world} (NCCL all-gather x{4 * c['n_layers'] + 1} per step)" if world > 1
-            else "single-gpu",
+            "parallelism": (f"rowsplit{world}: {4 * c['n_layers'] + 1} all-gathers per decode step over "
+                            + ("NVLink peer memory (low-latency exchange)" if comm_p2p else "NCCL"))
+            if world > 1 else "single-gpu",
             "prefill_ms": round(prefill_ms, 2), "prefill_tok_s": round(tokens / (prefill_ms / 1e3), 1),
             "prefill_linear_TFLOPs": round(lin_flops / (prefill_ms / 1e3) / 1e12, 1),
             "prefill_frac_of_bf16_peak": round(lin_flops / (prefill_ms / 1e3) / 1e12 / (world * flop_peak), 3),

@@ -412,6 +412,26 @@ int pb_comm_rank(const pb_comm* c);
 int pb_comm_world(const pb_comm* c);
 /* recv_dev [world][bytes] <- every rank's send_dev [bytes], on ctx's stream */
 int pb_comm_allgather(pb_comm* c, const void* send_dev, void* recv_dev, size_t bytes);
+/* 1 when the ranks exchange over peer memory: pb_comm_init opened every
+ * rank's buffers in every process (CUDA IPC over NVLink) and all ranks
+ * agreed; then a row-split batch's all-gathers are one kernel each that
+ * stores this rank's chunk into the peers' buffers and waits (bounded by the
+ * context timeout) for theirs.  0: NCCL all-gathers (also with PB_NO_P2P=1). */
+int pb_comm_peer_access(const pb_comm* c);
+/* Register a device buffer (a whole pb_malloc allocation, the same size on
+ * every rank; collective) for in-place all-gathers: pb_comm_allgather_inplace
+ * sends chunk `rank` (chunk_bytes, a multiple of 8, from buf + rank *
+ * chunk_bytes) to every rank's copy, over peer memory when the communicator
+ * has peer access, else with NCCL. */
+typedef struct pb_peerbuf pb_peerbuf;
+int pb_comm_register(pb_comm* c, void* buf_dev, pb_peerbuf** out);
+int pb_comm_deregister(pb_comm* c, pb_peerbuf* pb);
+int pb_comm_allgather_inplace(pb_comm* c, pb_peerbuf* pb, size_t chunk_bytes);
+/* The peer exchange's bounded wait, on this device alone: a two-rank
+ * exchange whose peer never signals.  Returns PB_OK with *raised_code =
+ * the device error the kernel raised (PB_DEVERR_WAIT, 2, expected) after
+ * about timeout_ms, and clears it; the context stays usable. */
+int pb_comm_selftest_wait(pb_ctx* ctx, int timeout_ms, int* raised_code);
 
 /* This process's rank of a row-split batch over comm's ranks: every rank
  * calls prefill / decode with the same arguments, and every rank gets the

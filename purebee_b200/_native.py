@@ -169,6 +169,11 @@ SIGNATURES = {
     "pb_comm_rank": (I, [V]),
     "pb_comm_world": (I, [V]),
     "pb_comm_allgather": (I, [V, V, V, SZ]),
+    "pb_comm_peer_access": (I, [V]),
+    "pb_comm_register": (I, [V, V, ctypes.POINTER(V)]),
+    "pb_comm_deregister": (I, [V, V]),
+    "pb_comm_allgather_inplace": (I, [V, V, SZ]),
+    "pb_comm_selftest_wait": (I, [V, I, ctypes.POINTER(I)]),
 }
 
 _lib = None

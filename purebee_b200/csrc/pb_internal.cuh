@@ -301,6 +301,27 @@ bool pb_gemm_uses_tma(const pb_qmat* w, int M);  // the f16-operand TMA path (ta
 // chunk `rank` of base (chunk_bytes each) goes to every rank
 int pb_comm_gather_inplace(pb_comm* c, void* base, size_t chunk_bytes);
 pb_ctx* pb_comm_ctx(const pb_comm* c);
+// Peer memory of the ranks (CUDA IPC): tables of every rank's copy of a buffer
+#define PB_MAX_RANKS 8
+struct pb_peer_bufs {
+  char* p[PB_MAX_RANKS];
+};
+struct pb_peer_sync {
+  unsigned long long* flags[PB_MAX_RANKS];  // rank q's arrival epochs, one slot per sender
+};
+int pb_comm_share(pb_comm* c, void* const* local, int n, void** table);  // table [n][world]
+int pb_comm_share_agreed(pb_comm* c, void* const* local, int n, void** table, bool want, bool* agreed);
+void pb_comm_unshare(pb_comm* c, void** table, int n);
+bool pb_comm_p2p(const pb_comm* c);
+int pb_comm_peer_gather(pb_comm* c, void* const* table, size_t chunk_bytes);
+// Low-latency exchange slots: s[q] is rank q's slot array [2][world][cap_units]
+// (16 bytes = 8 data bytes + two epoch flags each); epoch / done are this
+// rank's counters for the exchanges over these slots.
+struct pb_ll_slots {
+  uint4* s[PB_MAX_RANKS];
+};
+int pb_comm_ll_gather(pb_comm* c, const pb_ll_slots& slots, size_t cap_units, char* buf, size_t chunk_bytes,
+                      unsigned int* epoch, unsigned int* done);
 
 int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows,
                      const pb_mv_epi* epi);

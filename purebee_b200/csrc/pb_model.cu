@@ -1091,7 +1091,81 @@ struct pb_batch {
   size_t ws_bytes = 0;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  // peer exchange (NCCL communicator with peer access on every rank): every
+  // rank's copy of the exchanged buffers, by XG_* id, [id][rank]
+  void* peer[5][PB_MAX_RANKS] = {};
+  bool p2p_fixed = false;  // keys, logits shared
+  bool p2p_rows = false;   // x, att, hb shared (re-shared when they grow)
+  // low-latency exchange slots (pb_comm_ll_gather) for chunks up to ll_cap
+  // units of 8 bytes: the decode step's exchanges
+  pb_ll_slots ll{};
+  size_t ll_cap = 0;
+  bool p2p_ll = false;
+  void* ll_mem = nullptr;  // this rank's slots, then its epoch and done counters
 };
+
+// the buffers the row split exchanges
+enum { XG_X = 0, XG_ATT = 1, XG_HB = 2, XG_KEYS = 3, XG_LOGITS = 4 };
+static void* xg_buf(pb_shard& s, int id) {
+  switch (id) {
+    case XG_X: return s.x;
+    case XG_ATT: return s.att;
+    case XG_HB: return s.hb;
+    case XG_KEYS: return s.keys;
+    default: return s.logits;
+  }
+}
+
+// Share buffers ids[0..n) of this process's shard with the other ranks (peer
+// exchange); false when some rank could not.
+static int batch_share(pb_batch* b, const int* ids, int n, bool* ok) {
+  *ok = false;
+  if (!b->comm || !pb_comm_p2p(b->comm)) return PB_OK;
+  void* local[5];
+  void* table[5 * PB_MAX_RANKS] = {};
+  for (int i = 0; i < n; ++i) local[i] = xg_buf(b->sh[0], ids[i]);
+  PB_TRY(pb_comm_share_agreed(b->comm, local, n, table, true, ok));
+  if (*ok)
+    for (int i = 0; i < n; ++i)
+      for (int q = 0; q < b->world; ++q) b->peer[ids[i]][q] = table[(size_t)i * b->world + q];
+  return PB_OK;
+}
+
+static void batch_unshare(pb_batch* b, const int* ids, int n) {
+  for (int i = 0; i < n; ++i) {
+    void* table[PB_MAX_RANKS];
+    for (int q = 0; q < b->world; ++q) table[q] = b->peer[ids[i]][q];
+    pb_comm_unshare(b->comm, table, 1);
+    for (int q = 0; q < PB_MAX_RANKS; ++q) b->peer[ids[i]][q] = nullptr;
+  }
+}
+
+// The low-latency slots, sized for the decode step's largest chunk (the
+// f32 SwiGLU output of all sequences); collective.
+static int batch_share_ll(pb_batch* b) {
+  if (!b->comm || !pb_comm_p2p(b->comm)) return PB_OK;
+  pb_ctx* ctx = b->m->ctx;
+  const pb_model_config& c = b->m->c;
+  const int widest = c.hidden_dim > c.dim ? c.hidden_dim : c.dim;
+  b->ll_cap = ((size_t)b->B * widest * 4 / b->world + 7) / 8;
+  const size_t slot_bytes = 2 * (size_t)b->world * b->ll_cap * 16;
+  PB_TRY_CUDA(ctx, cudaMalloc(&b->ll_mem, slot_bytes + 64));
+  PB_TRY_CUDA(ctx, cudaMemsetAsync(b->ll_mem, 0, slot_bytes + 64, ctx->stream));
+  PB_TRY(pb_wait(ctx));
+  void* table[PB_MAX_RANKS] = {};
+  void* local = b->ll_mem;
+  PB_TRY(pb_comm_share_agreed(b->comm, &local, 1, table, true, &b->p2p_ll));
+  if (b->p2p_ll)
+    for (int q = 0; q < b->world; ++q) b->ll.s[q] = static_cast<uint4*>(table[q]);
+  return PB_OK;
+}
+
+static unsigned int* ll_counters(pb_batch* b) {
+  return reinterpret_cast<unsigned int*>(static_cast<char*>(b->ll_mem) + 2 * (size_t)b->world * b->ll_cap * 16);
+}
+
+static const int XG_ROWS[3] = {XG_X, XG_ATT, XG_HB};
+static const int XG_FIXED[2] = {XG_KEYS, XG_LOGITS};
 
 extern "C" int pb_batch_split_plan(const pb_model_config* c, int world, int rank, pb_split_plan* out) {
   if (!c || !out || world < 1 || rank < 0 || rank >= world) return PB_ERR_ARG;
@@ -1319,6 +1393,8 @@ static int batch_ensure_rows(pb_batch* b, int rows) {
   pb_ctx* ctx = m->ctx;
   PB_TRY(pb_wait(ctx));
   batch_free_graph(b);  // a recorded graph holds the old buffer addresses
+  if (b->p2p_rows) batch_unshare(b, XG_ROWS, 3);
+  b->p2p_rows = false;
   cudaFree(b->toks);
   b->toks = nullptr;
   b->rows_cap = 0;
@@ -1336,7 +1412,8 @@ static int batch_ensure_rows(pb_batch* b, int rows) {
   }
   PB_TRY_CUDA(ctx, cudaMalloc(&b->toks, (size_t)rows * 4));
   b->rows_cap = rows;
-  return PB_OK;
+  // collective: every rank grows its buffers in the same call
+  return batch_share(b, XG_ROWS, 3, &b->p2p_rows);
 }
 
 extern "C" int pb_batch_free(pb_batch* b) {
@@ -1344,6 +1421,14 @@ extern "C" int pb_batch_free(pb_batch* b) {
   pb_ctx* ctx = b->m ? b->m->ctx : nullptr;
   if (ctx) pb_wait(ctx);
   batch_free_graph(b);  // before the communicator its NCCL nodes use goes away
+  if (b->p2p_rows) batch_unshare(b, XG_ROWS, 3);
+  if (b->p2p_fixed) batch_unshare(b, XG_FIXED, 2);
+  if (b->p2p_ll) {
+    void* table[PB_MAX_RANKS];
+    for (int q = 0; q < b->world; ++q) table[q] = b->ll.s[q];
+    pb_comm_unshare(b->comm, table, 1);
+  }
+  cudaFree(b->ll_mem);
   for (auto& s : b->sh) shard_free(ctx, s);
   cudaFree(b->toks); cudaFree(b->next); cudaFree(b->pos_dev); cudaFree(b->hist); cudaFree(b->ws);
   delete b;
@@ -1384,7 +1469,9 @@ static int batch_create(pb_model* m, int n_seqs, int world, pb_comm* comm, pb_ba
   if (e != cudaSuccess) return fail(pb_cuda_error(ctx, e, "batch allocation"));
   cudaMemsetAsync(b->hist, 0, (size_t)(c.seq_len + 1) * n_seqs * 4, ctx->stream);
   cudaMemsetAsync(b->pos_dev, 0, 4, ctx->stream);
-  const int rc = pb_wait(ctx);
+  int rc = pb_wait(ctx);
+  if (rc == PB_OK) rc = batch_share(b, XG_FIXED, 2, &b->p2p_fixed);
+  if (rc == PB_OK) rc = batch_share_ll(b);
   if (rc != PB_OK) return fail(rc);
   *out = b;
   return PB_OK;
@@ -1404,19 +1491,29 @@ extern "C" int pb_batch_create_group(pb_model* m, int n_seqs, int world, pb_batc
   return batch_create(m, n_seqs, world, nullptr, out);
 }
 
-// In-place all-gather of chunk_bytes per rank: chunk r of buffer `field` is
-// rank r's; afterwards every shard's buffer holds every chunk.
-template <class F>
-static int batch_gather(pb_batch* b, F field, size_t chunk_bytes) {
+// In-place all-gather of chunk_bytes per rank: chunk r of buffer `id` is
+// rank r's; afterwards every shard's buffer holds every chunk.  Across
+// processes: the peer exchange kernel when every rank shared the buffer,
+// else an NCCL all-gather; in an emulated group, device copies.
+static int batch_gather(pb_batch* b, int id, size_t chunk_bytes) {
   if (b->world == 1) return PB_OK;
   pb_ctx* ctx = b->m->ctx;
-  if (b->comm) return pb_comm_gather_inplace(b->comm, field(b->sh[0]), chunk_bytes);
+  if (b->comm) {
+    const bool p2p = (id == XG_KEYS || id == XG_LOGITS) ? b->p2p_fixed : b->p2p_rows;
+    if (b->p2p_ll && chunk_bytes % 8 == 0 && chunk_bytes / 8 <= b->ll_cap) {
+      unsigned int* cnt = ll_counters(b);
+      return pb_comm_ll_gather(b->comm, b->ll, b->ll_cap, static_cast<char*>(xg_buf(b->sh[0], id)), chunk_bytes, cnt,
+                               cnt + 1);
+    }
+    if (p2p) return pb_comm_peer_gather(b->comm, b->peer[id], chunk_bytes);
+    return pb_comm_gather_inplace(b->comm, xg_buf(b->sh[0], id), chunk_bytes);
+  }
   for (auto& dst : b->sh)
     for (auto& src : b->sh) {
       if (&dst == &src) continue;
       const size_t off = (size_t)src.rank * chunk_bytes;
-      PB_TRY_CUDA(ctx, cudaMemcpyAsync(reinterpret_cast<char*>(field(dst)) + off,
-                                       reinterpret_cast<char*>(field(src)) + off, chunk_bytes,
+      PB_TRY_CUDA(ctx, cudaMemcpyAsync(static_cast<char*>(xg_buf(dst, id)) + off,
+                                       static_cast<char*>(xg_buf(src, id)) + off, chunk_bytes,
                                        cudaMemcpyDeviceToDevice, ctx->stream));
     }
   return PB_OK;
@@ -1529,14 +1626,14 @@ static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start
   const pb_model_config& c = b->m->c;
   const size_t dchunk = (size_t)rows * (c.dim / b->world) * 4;
   for (auto& s : b->sh) PB_TRY(shard_attention(b, s, l, rows, rows_per_seq, start_pos, pos_dev));
-  PB_TRY(batch_gather(b, [](pb_shard& s) { return (void*)s.att; }, dchunk));
+  PB_TRY(batch_gather(b, XG_ATT, dchunk));
   for (auto& s : b->sh) PB_TRY(shard_wo(b, s, l, rows));
-  PB_TRY(batch_gather(b, [](pb_shard& s) { return (void*)s.x; }, dchunk));
+  PB_TRY(batch_gather(b, XG_X, dchunk));
   for (auto& s : b->sh) PB_TRY(shard_gate_up(b, s, l, rows));
   const size_t hchunk = (size_t)rows * (c.hidden_dim / b->world) * (hidden_f16(b, b->sh[0], l, rows) ? 2 : 4);
-  PB_TRY(batch_gather(b, [](pb_shard& s) { return (void*)s.hb; }, hchunk));
+  PB_TRY(batch_gather(b, XG_HB, hchunk));
   for (auto& s : b->sh) PB_TRY(shard_down(b, s, l, rows));
-  return batch_gather(b, [](pb_shard& s) { return (void*)s.x; }, dchunk);
+  return batch_gather(b, XG_X, dchunk);
 }
 
 // Final RMSNorm of each sequence's last row (xl, or x itself when every row
@@ -1560,7 +1657,7 @@ static int batch_head(pb_batch* b, bool from_x, const int* pos_dev) {
     k_argmax_keys<<<b->B, 1024, 0, ctx->stream>>>(lg, s.p.vocab_rows, vc, s.p.vocab_row0, s.keys + (size_t)s.rank * b->B);
     PB_LAUNCHED(ctx, "k_argmax_keys");
   }
-  PB_TRY(batch_gather(b, [](pb_shard& s) { return (void*)s.keys; }, (size_t)b->B * 8));
+  PB_TRY(batch_gather(b, XG_KEYS, (size_t)b->B * 8));
   k_argmax_merge<<<pb_cdiv(b->B, 128), 128, 0, ctx->stream>>>(b->sh[0].keys, b->world, b->B, b->next, b->hist, pos_dev,
                                                              c.seq_len + 1);
   PB_LAUNCHED(ctx, "k_argmax_merge");
@@ -1586,7 +1683,7 @@ static int batch_logits_to_host(pb_batch* b, float* host) {
   pb_ctx* ctx = b->m->ctx;
   const pb_model_config& c = b->m->c;
   const int vc = b->sh[0].p.vocab_chunk;
-  if (b->comm) PB_TRY(batch_gather(b, [](pb_shard& s) { return (void*)s.logits; }, (size_t)b->B * vc * 4));
+  if (b->comm) PB_TRY(batch_gather(b, XG_LOGITS, (size_t)b->B * vc * 4));
   for (int r = 0; r < b->world; ++r) {
     const pb_shard& s = b->comm ? b->sh[0] : b->sh[r];
     pb_split_plan p;

@@ -195,6 +195,11 @@ class NcclComm:
         uid = cls.exchange_id(group)
         return cls(ctx, dist.get_world_size(group), dist.get_rank(group), uid)
 
+    @property
+    def peer_access(self) -> bool:
+        """True when exchanges run over peer memory (else NCCL all-gathers)."""
+        return bool(N_.lib().pb_comm_peer_access(self.h))
+
     def allgather(self, send_ptr: int, recv_ptr: int, nbytes: int) -> None:
         """recv [world][nbytes] <- every rank's send [nbytes] (device pointers,
         on the context's stream)."""

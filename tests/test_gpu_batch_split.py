@@ -71,6 +71,22 @@ def test_group_split_rejects(native, ctx):
     rt.shutdown()
 
 
+def test_peer_exchange_wait_is_bounded(native, ctx):
+    """The peer exchange kernel's wait gives up: a two-rank exchange on this
+    device whose peer never signals raises PB_DEVERR_WAIT after the limit,
+    and the context keeps working."""
+    import ctypes
+    import time
+    code = ctypes.c_int()
+    t0 = time.perf_counter()
+    ctx._check(native.lib().pb_comm_selftest_wait(ctx.h, 200, ctypes.byref(code)))
+    dt = time.perf_counter() - t0
+    assert code.value == 2, f"expected PB_DEVERR_WAIT, got {code.value}"
+    assert 0.15 < dt < 5.0
+    rt = make(native, ctx)  # the context still runs work
+    rt.shutdown()
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -99,11 +115,18 @@ def _rank(rank, world, port, outdir):
         rng = np.random.default_rng(7)
         prompts = rng.integers(1, 1000, (3, 300)).astype(np.int32)
         want = run_batch(rt, prompts, 5)
-        comm = NcclComm.from_torch(ctx)
-        got = run_batch(rt, prompts, 5, comm=comm)
-        for i, (g, w) in enumerate(zip(got, want)):
-            np.save(os.path.join(outdir, f"r{rank}_{i}.npy"), g)
-            np.save(os.path.join(outdir, f"w{rank}_{i}.npy"), w)
+        for kind in ("p2p", "nccl"):
+            if kind == "nccl":
+                os.environ["PB_NO_P2P"] = "1"
+            comm = NcclComm.from_torch(ctx)
+            with open(os.path.join(outdir, f"{kind}{rank}.txt"), "w") as f:
+                f.write(str(int(comm.peer_access)))
+            got = run_batch(rt, prompts, 5, comm=comm)
+            comm.free()
+            comm = None
+            for i, (g, w) in enumerate(zip(got, want)):
+                np.save(os.path.join(outdir, f"{kind}{rank}_{i}.npy"), g)
+                np.save(os.path.join(outdir, f"w{rank}_{i}.npy"), w)
         rt.shutdown()
         dist.barrier()
     finally:
@@ -119,10 +142,14 @@ def test_nccl_split_two_gpus(tmp_path):
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     mp.spawn(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        assert open(tmp_path / f"p2p{r}.txt").read() == "1"  # NVLink peers: the peer exchange
+        assert open(tmp_path / f"nccl{r}.txt").read() == "0"  # PB_NO_P2P=1: NCCL all-gathers
     for i in range(4):
         w0 = np.load(tmp_path / f"w0_{i}.npy")
         for r in range(2):
             assert np.array_equal(np.load(tmp_path / f"w{r}_{i}.npy"), w0)  # the unsplit batch on each GPU
-            got = np.load(tmp_path / f"r{r}_{i}.npy")
-            assert got.shape == w0.shape and np.array_equal(got.view(np.uint32), w0.view(np.uint32)), \
-                f"rank {r} output {i} differs from the unsplit batch"
+            for kind in ("p2p", "nccl"):
+                got = np.load(tmp_path / f"{kind}{r}_{i}.npy")
+                assert got.shape == w0.shape and np.array_equal(got.view(np.uint32), w0.view(np.uint32)), \
+                    f"{kind} rank {r} output {i} differs from the unsplit batch"
