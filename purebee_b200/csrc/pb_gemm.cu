@@ -121,7 +121,7 @@ __device__ __forceinline__ void gemm_emit32(const uint32_t (&v)[32], bool zero, 
 // TOK tokens per CTA (MMA N = 64 or 128).  grid.z splits K: CTA z covers K
 // steps [z*kper, (z+1)*kper) and, when gridDim.z > 1, writes its partial tile
 // to C + z*M*ldc (a workspace the reduce kernel sums in order of z).
-template <int TOK>
+template <int TOK, bool XCH>
 __global__ void __launch_bounds__(GM_THREADS, 1)
 k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int layout, int N, int N_pad, int nb,
              const float* __restrict__ X, int ldx, int M, float* __restrict__ C, int ldc, int kper, pb_gemm_epi epi,
@@ -178,9 +178,10 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
     }
     const int k = kg * GM_KSTEP + xh * 32;
     const bool live = xlive_row && k < K;
-    const int xc = epi.x_chunk;  // a 32-wide half step never straddles a chunk (x_chunk % 64 == 0)
+    // XCH: X in column chunks; a 32-wide half step never straddles one (x_chunk % 64 == 0)
+    const int xc = epi.x_chunk;
     const float4* xr = reinterpret_cast<const float4*>(
-        xc ? X + (size_t)(k / xc) * M * xc + (size_t)(m0 + xr_) * xc + k % xc : X + (size_t)(m0 + xr_) * ldx + k);
+        XCH ? X + (size_t)(k / xc) * M * xc + (size_t)(m0 + xr_) * xc + k % xc : X + (size_t)(m0 + xr_) * ldx + k);
 #pragma unroll
     for (int c = 0; c < 8; ++c) xa[c] = live ? __ldg(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
   };
@@ -590,12 +591,10 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
     kepi.h16 = nullptr;
     kepi.h32 = nullptr;
   }
-  if (tok == 64)
-    k_q4_gemm_tc<64><<<grid, GM_THREADS, gm_smem(), ctx->stream>>>(w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, X,
-                                                                  ldx, M, dst, ldd, kper, kepi, ctx->d_err);
-  else
-    k_q4_gemm_tc<128><<<grid, GM_THREADS, gm_smem(), ctx->stream>>>(w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, X,
-                                                                   ldx, M, dst, ldd, kper, kepi, ctx->d_err);
+  auto kern = tok == 64 ? (epi.x_chunk ? k_q4_gemm_tc<64, true> : k_q4_gemm_tc<64, false>)
+                        : (epi.x_chunk ? k_q4_gemm_tc<128, true> : k_q4_gemm_tc<128, false>);
+  kern<<<grid, GM_THREADS, gm_smem(), ctx->stream>>>(w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, X, ldx, M, dst, ldd,
+                                                    kper, kepi, ctx->d_err);
   PB_LAUNCHED(ctx, "k_q4_gemm_tc");
   if (splits > 1) {
     const int cols = epi.mode == PB_GEMM_SWIGLU ? w->N / 2 : w->N;
@@ -612,9 +611,9 @@ extern "C" int pb_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int
 }
 
 int pb_setup_gemm_kernels(void) {
-  cudaError_t e = cudaFuncSetAttribute(k_q4_gemm_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gm_smem());
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_q4_gemm_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gm_smem());
+  cudaError_t e = cudaSuccess;
+  for (auto k : {k_q4_gemm_tc<64, false>, k_q4_gemm_tc<64, true>, k_q4_gemm_tc<128, false>, k_q4_gemm_tc<128, true>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gm_smem());
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_gemm_f16_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tg_smem());
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;

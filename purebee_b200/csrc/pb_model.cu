@@ -29,8 +29,8 @@ int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const floa
                                int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo);
 bool pb_attn_decode_ok(int n_heads, int n_kv, int hd, int max_len);
 bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len);
-__global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
-                          float* __restrict__ out, __half* __restrict__ out16, int xc);
+void pb_launch_rmsnorm(cudaStream_t st, const float* x, int rows, int dim, const float* w, double eps, float* out,
+                       __half* out16, int xc);
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
                           const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
                           const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
@@ -481,7 +481,7 @@ extern "C" int pb_model_get_tensor(pb_model* m, int layer, int which, void* host
 
 static int launch_norm(pb_model* m, const float* x, int M, const float* w, float* out, __half* out16 = nullptr,
                        int xc = 0) {
-  k_rmsnorm<<<M, 256, 0, m->ctx->stream>>>(x, m->c.dim, w, m->c.eps, out, out16, xc == m->c.dim ? 0 : xc);
+  pb_launch_rmsnorm(m->ctx->stream, x, M, m->c.dim, w, m->c.eps, out, out16, xc);
   PB_LAUNCHED(m->ctx, "k_rmsnorm");
   return PB_OK;
 }

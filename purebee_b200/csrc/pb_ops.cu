@@ -24,16 +24,17 @@
 // With out16 (the batched path's f16 GEMM operand) the row is scaled in f32
 // by 1/rms and rounded to f16 once; otherwise the reference's double
 // arithmetic in f32 out.
-// One row per CTA.  xc > 0: x is stored in column chunks of width xc, chunk
-// c at x + c * gridDim.x * xc (the row-split batch's replicated residual);
-// the output rows are row-major either way.
-__global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
-                          float* __restrict__ out, __half* __restrict__ out16, int xc) {
+// One row per CTA.  CH: x is stored in column chunks of width xc, chunk c at
+// x + c * gridDim.x * xc (the row-split batch's replicated residual); the
+// output rows are row-major either way.
+template <bool CH>
+__global__ void k_rmsnorm_t(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
+                            float* __restrict__ out, __half* __restrict__ out16, int xc) {
   __shared__ double red[32];
   const size_t row = blockIdx.x;
-  const float* xr = x + row * (xc ? xc : dim);
+  const float* xr = x + row * (CH ? xc : dim);
   const size_t cs = (size_t)gridDim.x * xc;
-  auto X = [&](int d) { return xc ? xr[(size_t)(d / xc) * cs + d % xc] : xr[d]; };
+  auto X = [&](int d) { return CH ? xr[(size_t)(d / xc) * cs + d % xc] : xr[d]; };
   double ss = 0.0;
   for (int d = threadIdx.x; d < dim; d += blockDim.x) {
     const double v = (double)X(d);
@@ -50,9 +51,15 @@ __global__ void k_rmsnorm(const float* __restrict__ x, int dim, const float* __r
     out[row * dim + d] = (float)__dmul_rn(__ddiv_rn((double)X(d), rms), (double)w[d]);
 }
 
+void pb_launch_rmsnorm(cudaStream_t st, const float* x, int rows, int dim, const float* w, double eps, float* out,
+                       __half* out16, int xc) {
+  if (xc > 0 && xc < dim) k_rmsnorm_t<true><<<rows, 256, 0, st>>>(x, dim, w, eps, out, out16, xc);
+  else k_rmsnorm_t<false><<<rows, 256, 0, st>>>(x, dim, w, eps, out, out16, 0);
+}
+
 extern "C" int pb_rmsnorm(pb_ctx* ctx, const float* x, int seq, int dim, const float* w, double eps, float* out) {
   if (!ctx || !x || !w || !out || seq <= 0 || dim <= 0) return PB_ERR_ARG;
-  k_rmsnorm<<<seq, 256, 0, ctx->stream>>>(x, dim, w, eps, out, nullptr, 0);
+  pb_launch_rmsnorm(ctx->stream, x, seq, dim, w, eps, out, nullptr, 0);
   PB_LAUNCHED(ctx, "k_rmsnorm");
   return PB_OK;
 }
