@@ -23,7 +23,8 @@ int pb_launch_attn_cached(pb_ctx* ctx, const float* q, int q_stride, const float
                           int nseq, pb_seq_geo geo);
 int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc);
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
-                          int n_heads, int n_kv, int hd, float* out, int max_len, int nseq, pb_seq_geo geo);
+                          int n_heads, int n_kv, int hd, float* out, int max_len, int nseq, pb_seq_geo geo,
+                          float* ws = nullptr, size_t ws_floats = 0, int* counters = nullptr);
 
 int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
                                int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo);
@@ -1087,8 +1088,9 @@ struct pb_batch {
   int* next = nullptr;        // [B] greedy tokens of the last step
   int* pos_dev = nullptr;     // position of the tokens the next decode step reads
   int* hist = nullptr;        // [seq_len + 1][B] greedy token produced at each position
-  float* ws = nullptr;        // split-K partial tiles of the decode-step GEMMs
+  float* ws = nullptr;        // split-K partial tiles of the decode-step GEMMs (and attention partials)
   size_t ws_bytes = 0;
+  int* attn_cnt = nullptr;    // [B][n_kv] split counters of the decode attention (reset by the kernel)
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   // peer exchange (NCCL communicator with peer access on every rank): every
@@ -1431,6 +1433,7 @@ extern "C" int pb_batch_free(pb_batch* b) {
   cudaFree(b->ll_mem);
   for (auto& s : b->sh) shard_free(ctx, s);
   cudaFree(b->toks); cudaFree(b->next); cudaFree(b->pos_dev); cudaFree(b->hist); cudaFree(b->ws);
+  cudaFree(b->attn_cnt);
   delete b;
   return PB_OK;
 }
@@ -1466,6 +1469,8 @@ static int batch_create(pb_model* m, int n_seqs, int world, pb_comm* comm, pb_ba
   if (e == cudaSuccess) e = cudaMalloc(&b->pos_dev, 4);
   if (e == cudaSuccess) e = cudaMalloc(&b->hist, (size_t)(c.seq_len + 1) * n_seqs * 4);
   if (e == cudaSuccess) e = cudaMalloc(&b->ws, b->ws_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&b->attn_cnt, (size_t)n_seqs * c.n_kv_heads * 4);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b->attn_cnt, 0, (size_t)n_seqs * c.n_kv_heads * 4, ctx->stream);
   if (e != cudaSuccess) return fail(pb_cuda_error(ctx, e, "batch allocation"));
   cudaMemsetAsync(b->hist, 0, (size_t)(c.seq_len + 1) * n_seqs * 4, ctx->stream);
   cudaMemsetAsync(b->pos_dev, 0, 4, ctx->stream);
@@ -1558,7 +1563,8 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
   if (rows_per_seq == 1 && pos_dev) {
     geo.q = qw;
     geo.out = dc;
-    return pb_launch_attn_decode(ctx, s.qkvo, kc, vc, pos_dev, p.n_heads, p.n_kv_heads, hd, att, c.seq_len, b->B, geo);
+    return pb_launch_attn_decode(ctx, s.qkvo, kc, vc, pos_dev, p.n_heads, p.n_kv_heads, hd, att, c.seq_len, b->B, geo,
+                                 b->ws, b->ws_bytes / 4, b->attn_cnt);
   }
   geo.q = (int64_t)rows_per_seq * qw;
   geo.out = (int64_t)rows_per_seq * dc;

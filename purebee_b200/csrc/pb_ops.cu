@@ -1120,6 +1120,220 @@ k_attn_dec_group(const float* __restrict__ q, const float* __restrict__ kc, cons
   }
 }
 
+// k_attn_dec_split: flash-decoding form of the batched decode attention for
+// head_dim 64.  CTA (kv head g, sequence z, split s) takes cache positions
+// [s * AS_SPLIT, (s + 1) * AS_SPLIT); its four warps take blocks of AS_BLK
+// positions in turn, staging K and V rows into shared memory with cp.async
+// (two buffers per warp, so the next block's rows load while this one is
+// used).  Per block: lane (position p = lane % 16, half of the dims) dots the
+// K row with every query head of the group, the halves combine by one
+// shuffle; each warp keeps an online softmax per head (running max, sum and
+// output, rescaled when the max grows) and accumulates p_j V_j with lane l
+// owning dims 2l, 2l + 1.  The warps merge in order 0..3, and the last CTA of
+// (g, z) to finish merges the splits in order s = 0, 1, ...  The split is
+// fixed by position, not by the grid, so the result does not depend on
+// scheduling or on how many kv heads share the launch.
+constexpr int AS_SPLIT = 256, AS_BLK = 16, AS_WARPS = 4, AS_HD = 64, AS_KLD = AS_HD + 4;
+
+struct as_warp_smem {
+  float k[2][AS_BLK][AS_KLD];  // padded rows: lanes reading rows p..p+7 hit distinct banks
+  float v[2][AS_BLK][AS_HD];
+  float p[AS_BLK][AD_MAX_GROUP];
+};
+
+__device__ __forceinline__ void as_cp16(void* smem, const void* gmem, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(pb_smem_addr(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(AS_WARPS * 32)
+k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                 const int* __restrict__ pos_dev, int n_heads, int n_kv, float scale, float* __restrict__ out,
+                 int max_len, pb_seq_geo geo, float* __restrict__ ws, int* __restrict__ counters, int* err) {
+  extern __shared__ __align__(16) unsigned char as_raw[];
+  float* qs = reinterpret_cast<float*>(as_raw);  // [per][64]
+  as_warp_smem* stage = reinterpret_cast<as_warp_smem*>(as_raw + AD_MAX_GROUP * AS_HD * 4);
+  __shared__ int last_cta;
+  pb_pdl_trigger();
+  pb_pdl_wait();
+  const int per = n_heads / n_kv;
+  const int g = blockIdx.x, z = blockIdx.y, s = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int pos = *pos_dev, cache_len = pos + 1;
+  if (pos < 0 || cache_len > max_len) {
+    if (tid == 0 && g == 0 && z == 0 && s == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+    return;
+  }
+  const int nsplit = (cache_len + AS_SPLIT - 1) / AS_SPLIT;
+  if (s >= nsplit) return;  // past the cache: no work, not counted
+  const int j0 = s * AS_SPLIT, j1 = min(cache_len, j0 + AS_SPLIT);
+  const int kv_dim = n_kv * AS_HD;
+  q += z * geo.q + (size_t)g * per * AS_HD;
+  kc += z * geo.kv + (size_t)g * AS_HD;
+  vc += z * geo.kv + (size_t)g * AS_HD;
+  for (int i = tid; i < per * (AS_HD / 4); i += AS_WARPS * 32)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q)[i];
+  __syncthreads();
+
+  as_warp_smem* w = stage + warp;
+  const int nblk = (j1 - j0 + AS_BLK - 1) / AS_BLK;
+  auto issue = [&](int b, int buf) {  // block b's K and V rows (zero rows past j1)
+    const int jb = j0 + b * AS_BLK;
+#pragma unroll
+    for (int i = 0; i < AS_BLK * (AS_HD / 4) / 32; ++i) {
+      const int idx = i * 32 + lane, r = idx >> 4, c = idx & 15;
+      const int j = jb + r;
+      const bool live = j < j1;
+      const size_t row = (size_t)(live ? j : j0) * kv_dim + 4 * c;
+      as_cp16(&w->k[buf][r][4 * c], kc + row, live ? 16 : 0);
+      as_cp16(&w->v[buf][r][4 * c], vc + row, live ? 16 : 0);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float m[AD_MAX_GROUP], l[AD_MAX_GROUP], acc[AD_MAX_GROUP][2];
+#pragma unroll
+  for (int h = 0; h < AD_MAX_GROUP; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.0f;
+    acc[h][0] = acc[h][1] = 0.0f;
+  }
+  const int p = lane & 15, hf = lane >> 4;
+  if (warp < nblk) issue(warp, 0);
+  int it = 0;
+  for (int b = warp; b < nblk; b += AS_WARPS, ++it) {
+    const int buf = it & 1;
+    if (b + AS_WARPS < nblk) {
+      issue(b + AS_WARPS, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncwarp();
+    const int j = j0 + b * AS_BLK + p;
+    float dot[AD_MAX_GROUP];
+#pragma unroll
+    for (int h = 0; h < AD_MAX_GROUP; ++h) dot[h] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const float4 k4 = *reinterpret_cast<const float4*>(&w->k[buf][p][hf * 32 + 4 * c]);
+#pragma unroll
+      for (int h = 0; h < AD_MAX_GROUP; ++h) {
+        if (h < per) {
+          const float4 a = *reinterpret_cast<const float4*>(qs + h * AS_HD + hf * 32 + 4 * c);
+          dot[h] = __fmaf_rn(a.x, k4.x, dot[h]);
+          dot[h] = __fmaf_rn(a.y, k4.y, dot[h]);
+          dot[h] = __fmaf_rn(a.z, k4.z, dot[h]);
+          dot[h] = __fmaf_rn(a.w, k4.w, dot[h]);
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < AD_MAX_GROUP; ++h) {
+      if (h < per) {
+        const float d = __fadd_rn(dot[h], __shfl_xor_sync(0xffffffffu, dot[h], 16));
+        const float sc = j < j1 ? __fmul_rn(d, scale) : -INFINITY;
+        float bm = sc;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+        const float mn = fmaxf(m[h], bm);  // finite: the block's first position is live
+        const float corr = m[h] == -INFINITY ? 0.0f : expf(__fsub_rn(m[h], mn));
+        const float e = j < j1 ? expf(__fsub_rn(sc, mn)) : 0.0f;
+        float bs = e;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) bs = __fadd_rn(bs, __shfl_xor_sync(0xffffffffu, bs, o));
+        l[h] = __fmaf_rn(l[h], corr, bs);
+        acc[h][0] = __fmul_rn(acc[h][0], corr);
+        acc[h][1] = __fmul_rn(acc[h][1], corr);
+        m[h] = mn;
+        if (hf == 0) w->p[p][h] = e;
+      }
+    }
+    __syncwarp();
+#pragma unroll 4
+    for (int jj = 0; jj < AS_BLK; ++jj) {
+      const float2 v = *reinterpret_cast<const float2*>(&w->v[buf][jj][2 * lane]);
+#pragma unroll
+      for (int h = 0; h < AD_MAX_GROUP; ++h) {
+        if (h < per) {
+          const float pj = w->p[jj][h];
+          acc[h][0] = __fmaf_rn(pj, v.x, acc[h][0]);
+          acc[h][1] = __fmaf_rn(pj, v.y, acc[h][1]);
+        }
+      }
+    }
+    __syncwarp();  // the block's buffers and p are free for the next issue
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();  // every warp is done with its staging: reuse it for the merge
+  float* mg = reinterpret_cast<float*>(stage);  // [warp][per][2 + 64]: max, sum, output
+  const int rec = 2 + AS_HD;
+#pragma unroll
+  for (int h = 0; h < AD_MAX_GROUP; ++h) {
+    if (h < per) {
+      float* r = mg + ((size_t)warp * per + h) * rec;
+      if (lane == 0) {
+        r[0] = m[h];
+        r[1] = l[h];
+      }
+      r[2 + 2 * lane] = acc[h][0];
+      r[3 + 2 * lane] = acc[h][1];
+    }
+  }
+  __syncthreads();
+  const bool split = nsplit > 1;
+  float* part = ws + (((size_t)z * n_kv + g) * ((max_len + AS_SPLIT - 1) / AS_SPLIT) + s) * per * rec;
+  for (int i = tid; i < per * AS_HD; i += AS_WARPS * 32) {
+    const int h = i / AS_HD, d = i % AS_HD;
+    float M = -INFINITY;
+    for (int wi = 0; wi < AS_WARPS; ++wi) M = fmaxf(M, mg[((size_t)wi * per + h) * rec]);
+    float L = 0.0f, O = 0.0f;
+    for (int wi = 0; wi < AS_WARPS; ++wi) {
+      const float* r = mg + ((size_t)wi * per + h) * rec;
+      const float f = r[0] == -INFINITY ? 0.0f : expf(__fsub_rn(r[0], M));
+      L = __fmaf_rn(r[1], f, L);
+      O = __fmaf_rn(r[2 + d], f, O);
+    }
+    if (!split) {
+      out[z * geo.out + (size_t)g * per * AS_HD + i] = __fdiv_rn(O, L);
+    } else {
+      if (d == 0) {
+        part[(size_t)h * rec] = M;
+        part[(size_t)h * rec + 1] = L;
+      }
+      part[(size_t)h * rec + 2 + d] = O;
+    }
+  }
+  if (!split) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last_cta = atomicAdd(counters + (size_t)z * n_kv + g, 1) == nsplit - 1;
+  __syncthreads();
+  if (!last_cta) return;
+  __threadfence();
+  const float* parts = ws + ((size_t)z * n_kv + g) * ((max_len + AS_SPLIT - 1) / AS_SPLIT) * per * rec;
+  for (int i = tid; i < per * AS_HD; i += AS_WARPS * 32) {
+    const int h = i / AS_HD, d = i % AS_HD;
+    float M = -INFINITY;
+    for (int si = 0; si < nsplit; ++si) M = fmaxf(M, __ldcg(parts + ((size_t)si * per + h) * rec));
+    float L = 0.0f, O = 0.0f;
+    for (int si = 0; si < nsplit; ++si) {
+      const float* r = parts + ((size_t)si * per + h) * rec;
+      const float f = expf(__fsub_rn(__ldcg(r), M));
+      L = __fmaf_rn(__ldcg(r + 1), f, L);
+      O = __fmaf_rn(__ldcg(r + 2 + d), f, O);
+    }
+    out[z * geo.out + (size_t)g * per * AS_HD + i] = __fdiv_rn(O, L);
+  }
+  if (tid == 0) counters[(size_t)z * n_kv + g] = 0;  // for the next launch
+}
+
+static size_t as_smem() { return (size_t)AD_MAX_GROUP * AS_HD * 4 + AS_WARPS * sizeof(as_warp_smem); }
+
+// Workspace floats and counters k_attn_dec_split needs for nseq sequences.
+size_t pb_attn_split_ws_floats(int n_heads, int n_kv, int max_len, int nseq) {
+  return (size_t)nseq * n_kv * ((max_len + AS_SPLIT - 1) / AS_SPLIT) * (n_heads / n_kv) * (2 + AS_HD);
+}
+
 static size_t ag_smem(int per, int hd, int max_len) {
   return ((size_t)per * hd + (size_t)per * max_len + (size_t)(AG_THREADS / (hd / 4)) * per * hd) * 4;
 }
@@ -1141,13 +1355,18 @@ bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len) {
 // Decode attention for one query at *pos_dev over the cache (nseq sequences
 // of a batched launch, `geo` apart).
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
-                          int n_heads, int n_kv, int hd, float* out, int max_len, int nseq, pb_seq_geo geo) {
+                          int n_heads, int n_kv, int hd, float* out, int max_len, int nseq, pb_seq_geo geo,
+                          float* ws, size_t ws_floats, int* counters) {
   if (!(nseq > 1 ? pb_attn_decode_group_ok(n_heads, n_kv, hd, max_len) : pb_attn_decode_ok(n_heads, n_kv, hd, max_len)))
     return pb_set_error(ctx, PB_ERR_ARG, "decode attention needs n_heads %% n_kv == 0, head_dim %% 4 == 0, "
                                          "head_dim <= %d and max_len <= %d", AF_MAX_HD, (200 * 1024 - AF_PART * 8) / 4);
   const double scale = 1.0 / sqrt((double)hd);  // llama-streaming.js:546
   if (nseq > 1) {
     const int per = n_heads / n_kv;
+    if (hd == AS_HD && ws && counters && ws_floats >= pb_attn_split_ws_floats(n_heads, n_kv, max_len, nseq))
+      return pb_launch(ctx, "k_attn_dec_split", true, k_attn_dec_split,
+                       dim3(n_kv, nseq, (max_len + AS_SPLIT - 1) / AS_SPLIT), dim3(AS_WARPS * 32), as_smem(), q, kc,
+                       vc, pos_dev, n_heads, n_kv, (float)scale, out, max_len, geo, ws, counters, ctx->d_err);
     return pb_launch(ctx, "k_attn_dec_group", true, k_attn_dec_group, dim3(n_kv, nseq), dim3(AG_THREADS),
                      ag_smem(per, hd, max_len), q, kc, vc, pos_dev, n_heads, n_kv, hd, (float)scale, out, max_len, geo,
                      ctx->d_err);
@@ -1161,5 +1380,7 @@ int pb_setup_ops_kernels(void) {
   cudaError_t e = cudaFuncSetAttribute(k_attn_cached, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec_group, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_attn_dec_split, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)as_smem());
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
 }
