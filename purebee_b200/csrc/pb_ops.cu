@@ -1146,17 +1146,18 @@ __device__ __forceinline__ void as_cp16(void* smem, const void* gmem, int src_by
                : "memory");
 }
 
+template <int PER>
 __global__ void __launch_bounds__(AS_WARPS * 32)
 k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                 const int* __restrict__ pos_dev, int n_heads, int n_kv, float scale, float* __restrict__ out,
-                 int max_len, pb_seq_geo geo, float* __restrict__ ws, int* __restrict__ counters, int* err) {
+                 const int* __restrict__ pos_dev, int n_kv, float scale, float* __restrict__ out, int max_len,
+                 pb_seq_geo geo, float* __restrict__ ws, int* __restrict__ counters, int* err) {
   extern __shared__ __align__(16) unsigned char as_raw[];
   float* qs = reinterpret_cast<float*>(as_raw);  // [per][64]
   as_warp_smem* stage = reinterpret_cast<as_warp_smem*>(as_raw + AD_MAX_GROUP * AS_HD * 4);
   __shared__ int last_cta;
   pb_pdl_trigger();
   pb_pdl_wait();
-  const int per = n_heads / n_kv;
+  constexpr int per = PER;
   const int g = blockIdx.x, z = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int pos = *pos_dev, cache_len = pos + 1;
@@ -1190,9 +1191,9 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  float m[AD_MAX_GROUP], l[AD_MAX_GROUP], acc[AD_MAX_GROUP][2];
+  float m[PER], l[PER], acc[PER][2];
 #pragma unroll
-  for (int h = 0; h < AD_MAX_GROUP; ++h) {
+  for (int h = 0; h < PER; ++h) {
     m[h] = -INFINITY;
     l[h] = 0.0f;
     acc[h][0] = acc[h][1] = 0.0f;
@@ -1210,55 +1211,67 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
     }
     __syncwarp();
     const int j = j0 + b * AS_BLK + p;
-    float dot[AD_MAX_GROUP];
+    const bool live = j < j1;
+    float dot[PER];
 #pragma unroll
-    for (int h = 0; h < AD_MAX_GROUP; ++h) dot[h] = 0.0f;
+    for (int h = 0; h < PER; ++h) dot[h] = 0.0f;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       const float4 k4 = *reinterpret_cast<const float4*>(&w->k[buf][p][hf * 32 + 4 * c]);
 #pragma unroll
-      for (int h = 0; h < AD_MAX_GROUP; ++h) {
-        if (h < per) {
-          const float4 a = *reinterpret_cast<const float4*>(qs + h * AS_HD + hf * 32 + 4 * c);
-          dot[h] = __fmaf_rn(a.x, k4.x, dot[h]);
-          dot[h] = __fmaf_rn(a.y, k4.y, dot[h]);
-          dot[h] = __fmaf_rn(a.z, k4.z, dot[h]);
-          dot[h] = __fmaf_rn(a.w, k4.w, dot[h]);
-        }
+      for (int h = 0; h < PER; ++h) {
+        const float4 a = *reinterpret_cast<const float4*>(qs + h * AS_HD + hf * 32 + 4 * c);
+        dot[h] = __fmaf_rn(a.x, k4.x, dot[h]);
+        dot[h] = __fmaf_rn(a.y, k4.y, dot[h]);
+        dot[h] = __fmaf_rn(a.z, k4.z, dot[h]);
+        dot[h] = __fmaf_rn(a.w, k4.w, dot[h]);
       }
     }
+    float e[PER];
 #pragma unroll
-    for (int h = 0; h < AD_MAX_GROUP; ++h) {
-      if (h < per) {
-        const float d = __fadd_rn(dot[h], __shfl_xor_sync(0xffffffffu, dot[h], 16));
-        const float sc = j < j1 ? __fmul_rn(d, scale) : -INFINITY;
-        float bm = sc;
+    for (int h = 0; h < PER; ++h) {
+      const float d = __fadd_rn(dot[h], __shfl_xor_sync(0xffffffffu, dot[h], 16));
+      const float sc = live ? __fmul_rn(d, scale) : -INFINITY;
+      float bm = sc;
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
-        const float mn = fmaxf(m[h], bm);  // finite: the block's first position is live
-        const float corr = m[h] == -INFINITY ? 0.0f : expf(__fsub_rn(m[h], mn));
-        const float e = j < j1 ? expf(__fsub_rn(sc, mn)) : 0.0f;
-        float bs = e;
+      for (int o = 8; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+      const float mn = fmaxf(m[h], bm);  // finite: the block's first position is live
+      const float corr = __expf(__fsub_rn(m[h], mn));  // 0 while m is -inf
+      e[h] = live ? __expf(__fsub_rn(sc, mn)) : 0.0f;
+      float bs = e[h];
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) bs = __fadd_rn(bs, __shfl_xor_sync(0xffffffffu, bs, o));
-        l[h] = __fmaf_rn(l[h], corr, bs);
-        acc[h][0] = __fmul_rn(acc[h][0], corr);
-        acc[h][1] = __fmul_rn(acc[h][1], corr);
-        m[h] = mn;
-        if (hf == 0) w->p[p][h] = e;
-      }
+      for (int o = 8; o > 0; o >>= 1) bs = __fadd_rn(bs, __shfl_xor_sync(0xffffffffu, bs, o));
+      l[h] = __fmaf_rn(l[h], corr, bs);
+      acc[h][0] = __fmul_rn(acc[h][0], corr);
+      acc[h][1] = __fmul_rn(acc[h][1], corr);
+      m[h] = mn;
+    }
+    if (hf == 0) {
+#pragma unroll
+      for (int h = 0; h < PER; ++h) w->p[p][h] = e[h];
     }
     __syncwarp();
 #pragma unroll 4
     for (int jj = 0; jj < AS_BLK; ++jj) {
       const float2 v = *reinterpret_cast<const float2*>(&w->v[buf][jj][2 * lane]);
+      float pj[PER];
+      if constexpr (PER % 4 == 0) {
 #pragma unroll
-      for (int h = 0; h < AD_MAX_GROUP; ++h) {
-        if (h < per) {
-          const float pj = w->p[jj][h];
-          acc[h][0] = __fmaf_rn(pj, v.x, acc[h][0]);
-          acc[h][1] = __fmaf_rn(pj, v.y, acc[h][1]);
+        for (int h = 0; h < PER; h += 4) {
+          const float4 t = *reinterpret_cast<const float4*>(&w->p[jj][h]);
+          pj[h] = t.x;
+          pj[h + 1] = t.y;
+          pj[h + 2] = t.z;
+          pj[h + 3] = t.w;
         }
+      } else {
+#pragma unroll
+        for (int h = 0; h < PER; ++h) pj[h] = w->p[jj][h];
+      }
+#pragma unroll
+      for (int h = 0; h < PER; ++h) {
+        acc[h][0] = __fmaf_rn(pj[h], v.x, acc[h][0]);
+        acc[h][1] = __fmaf_rn(pj[h], v.y, acc[h][1]);
       }
     }
     __syncwarp();  // the block's buffers and p are free for the next issue
@@ -1268,16 +1281,14 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
   float* mg = reinterpret_cast<float*>(stage);  // [warp][per][2 + 64]: max, sum, output
   const int rec = 2 + AS_HD;
 #pragma unroll
-  for (int h = 0; h < AD_MAX_GROUP; ++h) {
-    if (h < per) {
-      float* r = mg + ((size_t)warp * per + h) * rec;
-      if (lane == 0) {
-        r[0] = m[h];
-        r[1] = l[h];
-      }
-      r[2 + 2 * lane] = acc[h][0];
-      r[3 + 2 * lane] = acc[h][1];
+  for (int h = 0; h < PER; ++h) {
+    float* r = mg + ((size_t)warp * per + h) * rec;
+    if (lane == 0) {
+      r[0] = m[h];
+      r[1] = l[h];
     }
+    r[2 + 2 * lane] = acc[h][0];
+    r[3 + 2 * lane] = acc[h][1];
   }
   __syncthreads();
   const bool split = nsplit > 1;
@@ -1289,7 +1300,7 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
     float L = 0.0f, O = 0.0f;
     for (int wi = 0; wi < AS_WARPS; ++wi) {
       const float* r = mg + ((size_t)wi * per + h) * rec;
-      const float f = r[0] == -INFINITY ? 0.0f : expf(__fsub_rn(r[0], M));
+      const float f = r[0] == -INFINITY ? 0.0f : __expf(__fsub_rn(r[0], M));
       L = __fmaf_rn(r[1], f, L);
       O = __fmaf_rn(r[2 + d], f, O);
     }
@@ -1318,7 +1329,7 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
     float L = 0.0f, O = 0.0f;
     for (int si = 0; si < nsplit; ++si) {
       const float* r = parts + ((size_t)si * per + h) * rec;
-      const float f = expf(__fsub_rn(__ldcg(r), M));
+      const float f = __expf(__fsub_rn(__ldcg(r), M));
       L = __fmaf_rn(__ldcg(r + 1), f, L);
       O = __fmaf_rn(__ldcg(r + 2 + d), f, O);
     }
@@ -1363,10 +1374,19 @@ int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const fl
   const double scale = 1.0 / sqrt((double)hd);  // llama-streaming.js:546
   if (nseq > 1) {
     const int per = n_heads / n_kv;
-    if (hd == AS_HD && ws && counters && ws_floats >= pb_attn_split_ws_floats(n_heads, n_kv, max_len, nseq))
-      return pb_launch(ctx, "k_attn_dec_split", true, k_attn_dec_split,
-                       dim3(n_kv, nseq, (max_len + AS_SPLIT - 1) / AS_SPLIT), dim3(AS_WARPS * 32), as_smem(), q, kc,
-                       vc, pos_dev, n_heads, n_kv, (float)scale, out, max_len, geo, ws, counters, ctx->d_err);
+    if (hd == AS_HD && ws && counters && ws_floats >= pb_attn_split_ws_floats(n_heads, n_kv, max_len, nseq)) {
+      const dim3 grid(n_kv, nseq, (max_len + AS_SPLIT - 1) / AS_SPLIT);
+      switch (per) {
+#define PB_AS_CASE(P)                                                                                              \
+  case P:                                                                                                          \
+    return pb_launch(ctx, "k_attn_dec_split", true, k_attn_dec_split<P>, grid, dim3(AS_WARPS * 32), as_smem(), q, \
+                     kc, vc, pos_dev, n_kv, (float)scale, out, max_len, geo, ws, counters, ctx->d_err);
+        PB_AS_CASE(1) PB_AS_CASE(2) PB_AS_CASE(3) PB_AS_CASE(4) PB_AS_CASE(5) PB_AS_CASE(6) PB_AS_CASE(7)
+        PB_AS_CASE(8)
+#undef PB_AS_CASE
+        default: break;
+      }
+    }
     return pb_launch(ctx, "k_attn_dec_group", true, k_attn_dec_group, dim3(n_kv, nseq), dim3(AG_THREADS),
                      ag_smem(per, hd, max_len), q, kc, vc, pos_dev, n_heads, n_kv, hd, (float)scale, out, max_len, geo,
                      ctx->d_err);
@@ -1380,7 +1400,8 @@ int pb_setup_ops_kernels(void) {
   cudaError_t e = cudaFuncSetAttribute(k_attn_cached, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec_group, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_attn_dec_split, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)as_smem());
+  for (auto k : {k_attn_dec_split<1>, k_attn_dec_split<2>, k_attn_dec_split<3>, k_attn_dec_split<4>,
+                 k_attn_dec_split<5>, k_attn_dec_split<6>, k_attn_dec_split<7>, k_attn_dec_split<8>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)as_smem());
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
 }
