@@ -1123,28 +1123,26 @@ k_attn_dec_group(const float* __restrict__ q, const float* __restrict__ kc, cons
 // k_attn_dec_split: flash-decoding form of the batched decode attention for
 // head_dim 64.  CTA (kv head g, sequence z, split s) takes cache positions
 // [s * AS_SPLIT, (s + 1) * AS_SPLIT); its four warps take blocks of AS_BLK
-// positions in turn, staging K and V rows into shared memory with cp.async
-// (two buffers per warp, so the next block's rows load while this one is
-// used).  Per block: lane (position p = lane % 16, half of the dims) dots the
-// K row with every query head of the group, the halves combine by one
-// shuffle; each warp keeps an online softmax per head (running max, sum and
-// output, rescaled when the max grows) and accumulates p_j V_j with lane l
-// owning dims 2l, 2l + 1.  The warps merge in order 0..3, and the last CTA of
-// (g, z) to finish merges the splits in order s = 0, 1, ...  The split is
-// fixed by position, not by the grid, so the result does not depend on
-// scheduling or on how many kv heads share the launch.
-constexpr int AS_SPLIT = 256, AS_BLK = 16, AS_WARPS = 4, AS_HD = 64, AS_KLD = AS_HD + 4;
+// positions in turn.  A block's K and V rows (256 bytes each) are brought into
+// the warp's shared memory by bulk copies, one row per lane, completing on the
+// buffer's mbarrier; two buffers per warp, so the next block loads while this
+// one is used.  Per block: lane (position p = lane % 8, dim quarter lane / 8)
+// dots its 16 dims of the K row with every query head of the group, two
+// shuffles complete the dots; each warp keeps an online softmax per head
+// (running max, sum and output, rescaled when the max grows) and accumulates
+// p_j V_j with lane l owning dims 2l, 2l + 1.  The warps merge in order 0..3,
+// and the last CTA of (g, z) to finish merges the splits in order
+// s = 0, 1, ...  The split is fixed by position, not by the grid, so the
+// result does not depend on scheduling or on how many kv heads share the
+// launch.
+constexpr int AS_SPLIT = 256, AS_BLK = 8, AS_WARPS = 4, AS_HD = 64, AS_KLD = AS_HD + 4;
 
 struct as_warp_smem {
   float k[2][AS_BLK][AS_KLD];  // padded rows: lanes reading rows p..p+7 hit distinct banks
   float v[2][AS_BLK][AS_HD];
   float p[AS_BLK][AD_MAX_GROUP];
+  uint64_t bar[2];
 };
-
-__device__ __forceinline__ void as_cp16(void* smem, const void* gmem, int src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(pb_smem_addr(smem)), "l"(gmem), "r"(src_bytes)
-               : "memory");
-}
 
 template <int PER>
 __global__ void __launch_bounds__(AS_WARPS * 32)
@@ -1172,24 +1170,29 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
   q += z * geo.q + (size_t)g * per * AS_HD;
   kc += z * geo.kv + (size_t)g * AS_HD;
   vc += z * geo.kv + (size_t)g * AS_HD;
+  as_warp_smem* w = stage + warp;
+  if (lane == 0) {
+    pb_mbar_init(&w->bar[0], 1);
+    pb_mbar_init(&w->bar[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   for (int i = tid; i < per * (AS_HD / 4); i += AS_WARPS * 32)
     reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q)[i];
   __syncthreads();
 
-  as_warp_smem* w = stage + warp;
   const int nblk = (j1 - j0 + AS_BLK - 1) / AS_BLK;
-  auto issue = [&](int b, int buf) {  // block b's K and V rows (zero rows past j1)
-    const int jb = j0 + b * AS_BLK;
-#pragma unroll
-    for (int i = 0; i < AS_BLK * (AS_HD / 4) / 32; ++i) {
-      const int idx = i * 32 + lane, r = idx >> 4, c = idx & 15;
-      const int j = jb + r;
-      const bool live = j < j1;
-      const size_t row = (size_t)(live ? j : j0) * kv_dim + 4 * c;
-      as_cp16(&w->k[buf][r][4 * c], kc + row, live ? 16 : 0);
-      as_cp16(&w->v[buf][r][4 * c], vc + row, live ? 16 : 0);
+  // block b's live K rows (lanes 0..7) and V rows (lanes 8..15) into buffer buf
+  auto issue = [&](int b, int buf) {
+    const int jb = j0 + b * AS_BLK, live = min(AS_BLK, j1 - jb);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the warp's reads of this buffer
+    if (lane == 0) pb_mbar_arrive_tx(&w->bar[buf], (uint32_t)live * AS_HD * 4 * 2);
+    __syncwarp();
+    const int r = lane & 7;
+    if (lane < 16 && r < live) {
+      const size_t row = (size_t)(jb + r) * kv_dim;
+      if (lane < 8) pb_bulk_g2s(&w->k[buf][r][0], kc + row, AS_HD * 4, &w->bar[buf]);
+      else pb_bulk_g2s(&w->v[buf][r][0], vc + row, AS_HD * 4, &w->bar[buf]);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
   };
   float m[PER], l[PER], acc[PER][2];
 #pragma unroll
@@ -1198,29 +1201,25 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
     l[h] = 0.0f;
     acc[h][0] = acc[h][1] = 0.0f;
   }
-  const int p = lane & 15, hf = lane >> 4;
+  const int p = lane & 7, qd = lane >> 3;
   if (warp < nblk) issue(warp, 0);
   int it = 0;
-  for (int b = warp; b < nblk; b += AS_WARPS, ++it) {
+  bool ok = true;
+  for (int b = warp; b < nblk && ok; b += AS_WARPS, ++it) {
     const int buf = it & 1;
-    if (b + AS_WARPS < nblk) {
-      issue(b + AS_WARPS, buf ^ 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
-    __syncwarp();
-    const int j = j0 + b * AS_BLK + p;
-    const bool live = j < j1;
+    if (b + AS_WARPS < nblk) issue(b + AS_WARPS, buf ^ 1);
+    if (!(ok = pb_mbar_wait(&w->bar[buf], (it >> 1) & 1, err))) break;
+    const int jb = j0 + b * AS_BLK;
+    const bool live = jb + p < j1;
     float dot[PER];
 #pragma unroll
     for (int h = 0; h < PER; ++h) dot[h] = 0.0f;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const float4 k4 = *reinterpret_cast<const float4*>(&w->k[buf][p][hf * 32 + 4 * c]);
+    for (int c = 0; c < 4; ++c) {
+      const float4 k4 = *reinterpret_cast<const float4*>(&w->k[buf][p][qd * 16 + 4 * c]);
 #pragma unroll
       for (int h = 0; h < PER; ++h) {
-        const float4 a = *reinterpret_cast<const float4*>(qs + h * AS_HD + hf * 32 + 4 * c);
+        const float4 a = *reinterpret_cast<const float4*>(qs + h * AS_HD + qd * 16 + 4 * c);
         dot[h] = __fmaf_rn(a.x, k4.x, dot[h]);
         dot[h] = __fmaf_rn(a.y, k4.y, dot[h]);
         dot[h] = __fmaf_rn(a.z, k4.z, dot[h]);
@@ -1230,53 +1229,61 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
     float e[PER];
 #pragma unroll
     for (int h = 0; h < PER; ++h) {
-      const float d = __fadd_rn(dot[h], __shfl_xor_sync(0xffffffffu, dot[h], 16));
+      float d = __fadd_rn(dot[h], __shfl_xor_sync(0xffffffffu, dot[h], 8));
+      d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 16));
       const float sc = live ? __fmul_rn(d, scale) : -INFINITY;
       float bm = sc;
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+      for (int o = 4; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
       const float mn = fmaxf(m[h], bm);  // finite: the block's first position is live
       const float corr = __expf(__fsub_rn(m[h], mn));  // 0 while m is -inf
       e[h] = live ? __expf(__fsub_rn(sc, mn)) : 0.0f;
       float bs = e[h];
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) bs = __fadd_rn(bs, __shfl_xor_sync(0xffffffffu, bs, o));
+      for (int o = 4; o > 0; o >>= 1) bs = __fadd_rn(bs, __shfl_xor_sync(0xffffffffu, bs, o));
       l[h] = __fmaf_rn(l[h], corr, bs);
       acc[h][0] = __fmul_rn(acc[h][0], corr);
       acc[h][1] = __fmul_rn(acc[h][1], corr);
       m[h] = mn;
     }
-    if (hf == 0) {
+    if (qd == 0) {
 #pragma unroll
       for (int h = 0; h < PER; ++h) w->p[p][h] = e[h];
     }
     __syncwarp();
-#pragma unroll 4
+    const int nlive = min(AS_BLK, j1 - jb);  // rows past the cache were not loaded
+#pragma unroll
     for (int jj = 0; jj < AS_BLK; ++jj) {
-      const float2 v = *reinterpret_cast<const float2*>(&w->v[buf][jj][2 * lane]);
-      float pj[PER];
-      if constexpr (PER % 4 == 0) {
+      if (jj < nlive) {
+        const float2 v = *reinterpret_cast<const float2*>(&w->v[buf][jj][2 * lane]);
+        float pj[PER];
+        if constexpr (PER % 4 == 0) {
 #pragma unroll
-        for (int h = 0; h < PER; h += 4) {
-          const float4 t = *reinterpret_cast<const float4*>(&w->p[jj][h]);
-          pj[h] = t.x;
-          pj[h + 1] = t.y;
-          pj[h + 2] = t.z;
-          pj[h + 3] = t.w;
+          for (int h = 0; h < PER; h += 4) {
+            const float4 t = *reinterpret_cast<const float4*>(&w->p[jj][h]);
+            pj[h] = t.x;
+            pj[h + 1] = t.y;
+            pj[h + 2] = t.z;
+            pj[h + 3] = t.w;
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < PER; ++h) pj[h] = w->p[jj][h];
         }
-      } else {
 #pragma unroll
-        for (int h = 0; h < PER; ++h) pj[h] = w->p[jj][h];
-      }
-#pragma unroll
-      for (int h = 0; h < PER; ++h) {
-        acc[h][0] = __fmaf_rn(pj[h], v.x, acc[h][0]);
-        acc[h][1] = __fmaf_rn(pj[h], v.y, acc[h][1]);
+        for (int h = 0; h < PER; ++h) {
+          acc[h][0] = __fmaf_rn(pj[h], v.x, acc[h][0]);
+          acc[h][1] = __fmaf_rn(pj[h], v.y, acc[h][1]);
+        }
       }
     }
     __syncwarp();  // the block's buffers and p are free for the next issue
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (!ok) {
+    // a copy that never completed: wait (bounded) for the warp's other buffer
+    // too, so no bulk copy is in flight when the CTA exits
+    pb_mbar_wait(&w->bar[(it + 1) & 1], ((it + 1) >> 1) & 1, err);
+  }
   __syncthreads();  // every warp is done with its staging: reuse it for the merge
   float* mg = reinterpret_cast<float*>(stage);  // [warp][per][2 + 64]: max, sum, output
   const int rec = 2 + AS_HD;
