@@ -143,6 +143,12 @@ int pb_q4_1_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, in
  * (wasm-q4.js:118-267, wasm-simd.js:71-91) within a relative tolerance, not
  * bit for bit.  x_dev 16-byte aligned, ldx a multiple of 4. */
 int pb_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int M, int ldx, float* c_dev, int ldc);
+/* The same product with f16 activations x16_dev [M][K] (row-major, device):
+ * M <= 64 runs the warp-specialised decode-size kernel (TMA-fed Q4_0 payload
+ * and activations, half-precision dequant with the same values as the
+ * fused kernel), M >= 512 the persistent TMA kernel.  With the activations
+ * already rounded to f16, M <= 64 gives the same bits as pb_q4_gemm. */
+int pb_q4_gemm_f16(pb_ctx* ctx, const pb_qmat* w, const void* x16_dev, int M, float* c_dev, int ldc);
 /* wasm-q4.js:798-839 lmHead(hidden, embData, V, D): f32 row-major table on
  * the host, batch_dot lane order (wasm-q4.js:447-566). */
 int pb_lm_head(pb_ctx* ctx, const float* h_host, const float* emb_host, int V, int D, float* logits_host);

@@ -156,6 +156,7 @@ SIGNATURES = {
     "pb_model_kv": (I, [V, I, I, V, SZ]),
     "pb_model_decode_bytes": (I64, [V, I]),
     "pb_model_decode_launches": (I, [V]),
+    "pb_q4_gemm_f16": (I, [V, V, V, I, V, I]),
     "pb_batch_create": (I, [V, I, ctypes.POINTER(V)]),
     "pb_batch_free": (I, [V]),
     "pb_batch_prefill": (I, [V, V, I, V, V]),

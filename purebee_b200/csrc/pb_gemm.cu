@@ -545,6 +545,8 @@ __global__ void k_splitk_reduce(const float* __restrict__ ws, int splits, int M,
 }
 
 bool pb_gemm_uses_tma(const pb_qmat* w, int M) { return M >= PB_GEMM_TMA_MIN_M && w->K % TG_K == 0; }
+static int launch_gemm_ws(pb_ctx* ctx, const pb_qmat* w, const __half* Xh, int M, float* C, int ldc, float* ws,
+                          size_t ws_bytes, const pb_gemm_epi& epi);
 
 int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
                       size_t ws_bytes, const pb_gemm_epi* epi_in, const __half* Xh) {
@@ -558,7 +560,9 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
     return pb_set_error(ctx, PB_ERR_ARG, "column chunks of %d do not tile K=%d in steps of 64", epi.x_chunk, w->K);
   if (Xh && ((uintptr_t)Xh & 15)) return pb_set_error(ctx, PB_ERR_ARG, "f16 X must be 16-byte aligned");
   if (pb_gemm_uses_tma(w, M)) return launch_gemm_tma(ctx, w, X, Xh, ldx, M, C, ldc, epi);
-  if (!X) return pb_set_error(ctx, PB_ERR_ARG, "f16 activations need the TMA path (M >= %d)", PB_GEMM_TMA_MIN_M);
+  if (Xh && pb_gemm_uses_ws(w, M)) return launch_gemm_ws(ctx, w, Xh, M, C, ldc, ws, ws_bytes, epi);
+  if (!X)
+    return pb_set_error(ctx, PB_ERR_ARG, "f16 activations need M >= %d or M <= 64", PB_GEMM_TMA_MIN_M);
   const int tok = M <= 64 ? 64 : GM_TOK;
   dim3 grid(pb_cdiv(w->N, GM_ROWS), pb_cdiv(M, tok), 1);
   if (grid.y > 65535) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
@@ -604,16 +608,284 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
   return PB_OK;
 }
 
+extern "C" int pb_q4_gemm_f16(pb_ctx* ctx, const pb_qmat* w, const void* x16_dev, int M, float* c_dev, int ldc) {
+  if (!ctx || !w || !x16_dev || !c_dev || M <= 0) return PB_ERR_ARG;
+  if (ldc < w->N) return pb_set_error(ctx, PB_ERR_ARG, "row stride smaller than the matrix");
+  if (!pb_gemm_uses_ws(w, M) && !pb_gemm_uses_tma(w, M))
+    return pb_set_error(ctx, PB_ERR_ARG, "f16 activations take M <= 64 or M >= %d rows and K %% 64 == 0",
+                        PB_GEMM_TMA_MIN_M);
+  return pb_launch_q4_gemm(ctx, w, nullptr, w->K, M, c_dev, ldc, nullptr, 0, nullptr,
+                           static_cast<const __half*>(x16_dev));
+}
+
 extern "C" int pb_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int M, int ldx, float* c_dev, int ldc) {
   if (!w) return PB_ERR_ARG;
   if (ldx < w->K || ldc < w->N) return pb_set_error(ctx, PB_ERR_ARG, "row strides smaller than the matrix");
   return pb_launch_q4_gemm(ctx, w, x_dev, ldx, M, c_dev, ldc, nullptr, 0);
 }
 
+// ---------------------------------------------------------------------------
+// Decode-size batches (M <= 64 tokens, f16 activations): a warp-specialised
+// form of the fused-dequant GEMM.  CTA = 128 weight rows x 64 tokens, K split
+// over grid.z as in k_q4_gemm_tc.  A 3-stage ring per 64-wide K step holds the
+// raw Q4_0 payload tile (TMA from the resident layout), the activation tile
+// (TMA, 128-byte swizzle) and the dequantized f16 weight tile:
+//   warp 0 lane 0: TMA producer (payload + activations, one mbarrier);
+//   warp 1 lane 0: MMA issuer (four 128 x 64 x 16 MMAs per step, committed
+//     to the stage's "empty" mbarrier);
+//   warps 2-5: dequant, thread t = row t: its 2 blocks from shared memory,
+//     value (q - 8) * d in half precision: the nibble is OR-ed into the f16
+//     1024.0 (0x6400), 1032 is subtracted (exact) and the product with d is
+//     rounded once, the same bits as rounding the exact f32 product; the f16
+//     row goes to the swizzled tile; then the epilogue of its TMEM quadrant.
+// The weight values are the ones k_q4_gemm_tc stages; the K steps accumulate
+// in the same order, so both kernels give the same partial sums.
+// ---------------------------------------------------------------------------
+
+constexpr int GW_ROWS = 128, GW_TOK = 64, GW_K = 64, GW_STAGES = 3, GW_THREADS = 192;
+constexpr int GW_RAW_BYTES = GW_ROWS * 32;               // 2 Q4_0 payloads (16 B) per row
+constexpr int GW_X_BYTES = GW_TOK * GW_K * 2;            // f16 activations, swizzled
+constexpr int GW_A_BYTES = GW_ROWS * GW_K * 2;           // f16 weights, swizzled
+constexpr int GW_STAGE_BYTES = GW_A_BYTES + GW_X_BYTES + GW_RAW_BYTES;  // A first: 1024-aligned tiles
+
+static size_t gw_smem() { return (size_t)GW_STAGES * GW_STAGE_BYTES + 1024; }
+
+namespace {
+__device__ __forceinline__ uint32_t h2_sub_mul(uint32_t v, uint32_t magic, uint32_t d2) {
+  // (v - magic) * d2 on f16 pairs: the subtraction is exact, the product rounded once
+  uint32_t r;
+  asm("{\n\t.reg .b32 t;\n\tsub.rn.f16x2 t, %1, %2;\n\tmul.rn.f16x2 %0, t, %3;\n\t}"
+      : "=r"(r)
+      : "r"(v), "r"(magic), "r"(d2));
+  return r;
+}
+}  // namespace
+
+__global__ void __launch_bounds__(GW_THREADS, 1)
+k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_x,
+             const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int layout, int N, int N_pad, int nb, int M, int xkc,
+             float* __restrict__ C, int ldc, int kper, pb_gemm_epi epi, int* err) {
+  extern __shared__ __align__(1024) unsigned char gw_raw[];
+  __shared__ uint64_t full[GW_STAGES], aready[GW_STAGES], empty[GW_STAGES], accf;
+  __shared__ uint32_t tmem_base;
+  unsigned char* ring = gw_raw + ((1024 - (smem_addr(gw_raw) & 1023)) & 1023);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * GW_ROWS, m0 = blockIdx.y * GW_TOK;
+  const int ktot = nb / 2;  // K / 64
+  const int kbeg = blockIdx.z * kper, kend = kbeg + kper < ktot ? kbeg + kper : ktot;
+  const int ksteps = kend > kbeg ? kend - kbeg : 0;
+  C += (size_t)blockIdx.z * M * ldc;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+                 "r"(GW_TOK)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 32) {
+    for (int st = 0; st < GW_STAGES; ++st) {
+      pb_mbar_init(&full[st], 1);
+      pb_mbar_init(&aready[st], 128);
+      pb_mbar_init(&empty[st], 1);
+    }
+    pb_mbar_init(&accf, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_d = tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {  // producer
+      bool ok = true;
+      for (int g = 0; g < ksteps && ok; ++g) {
+        const int st = g % GW_STAGES;
+        if (g >= GW_STAGES && !(ok = pb_mbar_wait(&empty[st], ((g / GW_STAGES) - 1) & 1, err))) break;
+        unsigned char* sA = ring + st * GW_STAGE_BYTES;
+        pb_mbar_arrive_tx(&full[st], GW_X_BYTES + GW_RAW_BYTES);
+        const int ks = kbeg + g;
+        if (layout == PB_LAYOUT_TILED8)
+          asm volatile(
+              "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+              "[%5];" ::"r"(smem_addr(sA + GW_A_BYTES + GW_X_BYTES)),
+              "l"(&map_q), "r"(0), "r"(2 * ks), "r"(n0 >> 3), "r"(smem_addr(&full[st]))
+              : "memory");
+        else
+          tma_load_2d(sA + GW_A_BYTES + GW_X_BYTES, &map_q, 32 * ks, n0, &full[st]);
+        tma_load_3d(sA + GW_A_BYTES, &map_x, (ks * GW_K) % xkc, m0, (ks * GW_K) / xkc, &full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      bool ok = true;
+      for (int g = 0; g < ksteps && ok; ++g) {
+        const int st = g % GW_STAGES;
+        if (!(ok = pb_mbar_wait(&aready[st], (g / GW_STAGES) & 1, err))) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        unsigned char* sA = ring + st * GW_STAGE_BYTES;
+        const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sA + GW_A_BYTES));
+#pragma unroll
+        for (int kk = 0; kk < GW_K / 16; ++kk)
+          mma_f16(tmem_d, da + 2 * kk, db + 2 * kk, gm_idesc(GW_TOK), (g > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&empty[st]);
+      }
+      if (ok && ksteps > 0) mma_commit(&accf);
+    }
+  } else {
+    // dequant: thread t = weight row n0 + t
+    const int t = tid - 64, row = n0 + t;
+    const bool live_row = row < N_pad;
+    const uint32_t magic = 0x64086408u;  // f16 1032.0 twice
+    // the CTA's payload slice into L2 first (one run per row, or per 8-row tile)
+    if (ksteps > 0) {
+      const int b0 = 2 * kbeg, b1 = 2 * kend < nb ? 2 * kend : nb;
+      if (layout == PB_LAYOUT_TILED8) {
+        const int tile = (n0 >> 3) + t;
+        if (t < GW_ROWS / 8 && tile * 8 < N_pad)
+          pb_l2_prefetch(qs + ((size_t)tile * nb + b0) * 128, (uint32_t)(b1 - b0) * 128);
+      } else if (live_row) {
+        pb_l2_prefetch(qs + ((size_t)row * nb + b0) * 16, (uint32_t)(b1 - b0) * 16);
+      }
+    }
+    bool ok = true;
+    for (int g = 0; g < ksteps && ok; ++g) {
+      const int st = g % GW_STAGES, ks = kbeg + g;
+      // the two scales of this step (L2-resident; loaded before the wait)
+      uint32_t d2[2] = {0u, 0u};
+      if (live_row) {
+#pragma unroll
+        for (int bb = 0; bb < 2; ++bb) {
+          const uint32_t dv = __ldg(dsc + pb_slot(layout, row, 2 * ks + bb, nb));
+          d2[bb] = dv | (dv << 16);
+        }
+      }
+      if (!(ok = pb_mbar_wait(&full[st], (g / GW_STAGES) & 1, err))) break;
+      unsigned char* sA = ring + st * GW_STAGE_BYTES;
+      const unsigned char* raw = sA + GW_A_BYTES + GW_X_BYTES;
+#pragma unroll
+      for (int bb = 0; bb < 2; ++bb) {
+        const uint32_t off =
+            layout == PB_LAYOUT_TILED8 ? (uint32_t)((((t >> 3) * 2 + bb) * 8 + (t & 7)) * 16) : (uint32_t)(t * 32 + bb * 16);
+        const uint4 q = *reinterpret_cast<const uint4*>(raw + off);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        uint32_t lo[8], hi[8];  // f16 pairs (k, k+1): lo nibbles are k 0..15, hi nibbles k 16..31
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t a = __byte_perm(w[i], 0u, 0x4140u), b = __byte_perm(w[i], 0u, 0x4342u);
+          lo[2 * i] = h2_sub_mul((a & 0x000F000Fu) | 0x64006400u, magic, d2[bb]);
+          lo[2 * i + 1] = h2_sub_mul((b & 0x000F000Fu) | 0x64006400u, magic, d2[bb]);
+          hi[2 * i] = h2_sub_mul(((a >> 4) & 0x000F000Fu) | 0x64006400u, magic, d2[bb]);
+          hi[2 * i + 1] = h2_sub_mul(((b >> 4) & 0x000F000Fu) | 0x64006400u, magic, d2[bb]);
+        }
+        *reinterpret_cast<uint4*>(sA + sw128(t, 4 * bb + 0)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(sA + sw128(t, 4 * bb + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+        *reinterpret_cast<uint4*>(sA + sw128(t, 4 * bb + 2)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(sA + sw128(t, 4 * bb + 3)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+      }
+      // generic-proxy reads of the payload and writes of the tile -> the async proxy
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&aready[st])) : "memory");
+    }
+    // epilogue: TMEM lanes of this warp's quadrant, 64 token columns
+    const bool empty_split = ksteps == 0;
+    if (ok && !empty_split) ok = pb_mbar_wait(&accf, 0, err);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+      const int q4 = warp & 3, erow = n0 + q4 * 32 + lane;
+#pragma unroll 1
+      for (int c0 = 0; c0 < GW_TOK; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem_d + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
+        gemm_emit32(v, empty_split, erow, N, m0 + c0, M, C, ldc, epi);
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(GW_TOK) : "memory");
+  }
+}
+
+// The payload of a resident Q4_0 matrix as a TMA tensor: rows of nb * 16
+// bytes (row layout: box 32 B x 128 rows) or 8-row tiles (tiled layout:
+// {128 B, nb, N_pad / 8}, box 128 B x 2 blocks x 16 tiles).
+static int make_map_q(pb_ctx* ctx, CUtensorMap* map, const pb_qmat* w) {
+  auto enc = tensor_map_encoder(ctx);
+  if (!enc) return PB_ERR_CUDA;
+  CUresult r;
+  cuuint32_t estr[3] = {1, 1, 1};
+  if (w->layout == PB_LAYOUT_TILED8) {
+    cuuint64_t dims[3] = {128, (cuuint64_t)w->nb, (cuuint64_t)(w->N_pad / 8)};
+    cuuint64_t strides[2] = {128, (cuuint64_t)w->nb * 128};
+    cuuint32_t box[3] = {128, 2, GW_ROWS / 8};
+    r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, w->qs, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[2] = {(cuuint64_t)w->nb * 16, (cuuint64_t)w->N_pad};
+    cuuint64_t strides[1] = {(cuuint64_t)w->nb * 16};
+    cuuint32_t box[2] = {32, GW_ROWS};
+    r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->qs, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (r != CUDA_SUCCESS) return pb_set_error(ctx, PB_ERR_CUDA, "cuTensorMapEncodeTiled (Q4 payload) failed (%d)", (int)r);
+  return PB_OK;
+}
+
+bool pb_gemm_uses_ws(const pb_qmat* w, int M) {
+  return M <= GW_TOK && w->type == PB_TYPE_Q4_0 && w->K % GW_K == 0;
+}
+
+static int launch_gemm_ws(pb_ctx* ctx, const pb_qmat* w, const __half* Xh, int M, float* C, int ldc, float* ws,
+                          size_t ws_bytes, const pb_gemm_epi& epi) {
+  const int ktot = w->K / GW_K;
+  dim3 grid(pb_cdiv(w->N, GW_ROWS), 1, 1);
+  int splits = 1;
+  if (ws) {  // the plan of the fused kernel: split K until the grid covers the SMs twice
+    const int plan_n = epi.split_n > 0 ? epi.split_n : w->N;
+    splits = pb_cdiv(2 * ctx->sm_count, pb_cdiv(plan_n, GW_ROWS));
+    const int max_by_k = ktot / 4 > 1 ? ktot / 4 : 1;
+    const int max_by_ws = (int)(ws_bytes / ((size_t)M * plan_n * 4));
+    const int fit = (int)(ws_bytes / ((size_t)M * w->N * 4));
+    splits = splits < max_by_k ? splits : max_by_k;
+    splits = splits < max_by_ws ? splits : max_by_ws;
+    splits = splits < fit ? splits : fit;
+    if (splits < 1) splits = 1;
+  }
+  const int kper = pb_cdiv(ktot, splits);
+  splits = pb_cdiv(ktot, kper);
+  grid.z = splits;
+  float* dst = splits > 1 ? ws : C;
+  const int ldd = splits > 1 ? w->N : ldc;
+  pb_gemm_epi kepi = epi;
+  if (splits > 1) {
+    kepi.mode = PB_GEMM_STORE;
+    kepi.h16 = nullptr;
+    kepi.h32 = nullptr;
+  }
+  const int xkc = epi.x_chunk ? epi.x_chunk : w->K;
+  CUtensorMap mq, mx;
+  PB_TRY(make_map_q(ctx, &mq, w));
+  PB_TRY(make_map_x(ctx, &mx, Xh, M, w->K, xkc, GW_TOK));
+  k_q4_gemm_ws<<<grid, GW_THREADS, gw_smem(), ctx->stream>>>(mq, mx, w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, M, xkc,
+                                                             dst, ldd, kper, kepi, ctx->d_err);
+  PB_LAUNCHED(ctx, "k_q4_gemm_ws");
+  if (splits > 1) {
+    const int cols = epi.mode == PB_GEMM_SWIGLU ? w->N / 2 : w->N;
+    k_splitk_reduce<<<dim3(pb_cdiv(cols, 256), M), 256, 0, ctx->stream>>>(ws, splits, M, w->N, C, ldc, epi);
+    PB_LAUNCHED(ctx, "k_splitk_reduce");
+  }
+  return PB_OK;
+}
+
 int pb_setup_gemm_kernels(void) {
   cudaError_t e = cudaSuccess;
   for (auto k : {k_q4_gemm_tc<64, false>, k_q4_gemm_tc<64, true>, k_q4_gemm_tc<128, false>, k_q4_gemm_tc<128, true>})
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gm_smem());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_q4_gemm_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gw_smem());
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(k_gemm_f16_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tg_smem());
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;

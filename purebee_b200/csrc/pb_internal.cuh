@@ -296,6 +296,7 @@ struct pb_gemm_epi {
 int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
                       size_t ws_bytes, const pb_gemm_epi* epi = nullptr, const __half* Xh = nullptr);
 bool pb_gemm_uses_tma(const pb_qmat* w, int M);  // the f16-operand TMA path (takes Xh)
+bool pb_gemm_uses_ws(const pb_qmat* w, int M);   // the decode-size path with f16 activations (Xh)
 
 // pb_comm.cu: in-place all-gather on the communicator's context stream;
 // chunk `rank` of base (chunk_bytes each) goes to every rank

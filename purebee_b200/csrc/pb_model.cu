@@ -24,7 +24,8 @@ int pb_launch_attn_cached(pb_ctx* ctx, const float* q, int q_stride, const float
 int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc);
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
                           int n_heads, int n_kv, int hd, float* out, int max_len, int nseq, pb_seq_geo geo,
-                          float* ws = nullptr, size_t ws_floats = 0, int* counters = nullptr);
+                          float* ws = nullptr, size_t ws_floats = 0, int* counters = nullptr,
+                          __half* out16 = nullptr);
 
 int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
                                int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo);
@@ -1104,6 +1105,7 @@ struct pb_batch {
   size_t ll_cap = 0;
   bool p2p_ll = false;
   void* ll_mem = nullptr;  // this rank's slots, then its epoch and done counters
+  bool decoding = false;   // the layer being enqueued is a decode step (one row per sequence)
 };
 
 // the buffers the row split exchanges
@@ -1527,6 +1529,15 @@ static int batch_gather(pb_batch* b, int id, size_t chunk_bytes) {
 // The x_chunk of an operand stored in `width`-wide chunks (0 when unsplit).
 static int chunk_of(const pb_batch* b, int width) { return b->world > 1 ? width : 0; }
 
+// Decode-size steps (<= 64 token rows, head_dim 64): every GEMM takes f16
+// activations (the warp-specialised decode GEMM), which the norms, the split
+// attention and the SwiGLU epilogue write directly.
+static bool dec16(const pb_batch* b, const pb_shard& s, int l, int rows) {
+  return b->decoding && rows <= 64 && b->m->c.head_dim == 64 && pb_gemm_uses_ws(s.qkv[l], rows) &&
+         pb_gemm_uses_ws(s.wo[l], rows) &&
+         pb_gemm_uses_ws(s.gu[l], rows) && pb_gemm_uses_ws(s.w2[l], rows);
+}
+
 // norm -> this rank's q | k | v -> RoPE + KV append -> attention of its heads
 // into its chunk of att.
 static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_per_seq, int start_pos,
@@ -1541,9 +1552,10 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
   float* vc = s.vc + (size_t)l * b->B * cache_seq;
   pb_gemm_epi st;
   st.split_n = dim + 2 * m->kv_dim;
-  // the norm writes the GEMM's f16 operand directly on the TMA path
+  // the norm writes the GEMM's f16 operand directly on the TMA and decode paths
   __half* xn16 = reinterpret_cast<__half*>(s.xn);
-  if (pb_gemm_uses_tma(s.qkv[l], rows)) {
+  const bool d16 = dec16(b, s, l, rows);
+  if (pb_gemm_uses_tma(s.qkv[l], rows) || d16) {
     PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, nullptr, xn16, dc));
     PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], nullptr, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st, xn16));
   } else {
@@ -1563,8 +1575,9 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
   if (rows_per_seq == 1 && pos_dev) {
     geo.q = qw;
     geo.out = dc;
+    __half* att16 = d16 ? reinterpret_cast<__half*>(s.att) + (size_t)s.rank * rows * dc : nullptr;
     return pb_launch_attn_decode(ctx, s.qkvo, kc, vc, pos_dev, p.n_heads, p.n_kv_heads, hd, att, c.seq_len, b->B, geo,
-                                 b->ws, b->ws_bytes / 4, b->attn_cnt);
+                                 b->ws, b->ws_bytes / 4, b->attn_cnt, att16);
   }
   geo.q = (int64_t)rows_per_seq * qw;
   geo.out = (int64_t)rows_per_seq * dc;
@@ -1584,11 +1597,16 @@ static int shard_wo(pb_batch* b, pb_shard& s, int l, int rows) {
   add.mode = PB_GEMM_ADD;
   add.x_chunk = chunk_of(b, dc);
   add.split_n = m->c.dim;
+  if (dec16(b, s, l, rows))
+    return pb_launch_q4_gemm(m->ctx, s.wo[l], nullptr, m->c.dim, rows, s.x + (size_t)s.rank * rows * dc, dc, b->ws,
+                             b->ws_bytes, &add, reinterpret_cast<const __half*>(s.att));
   return pb_launch_q4_gemm(m->ctx, s.wo[l], s.att, m->c.dim, rows, s.x + (size_t)s.rank * rows * dc, dc, b->ws,
                            b->ws_bytes, &add);
 }
 
-static bool hidden_f16(const pb_batch* b, const pb_shard& s, int l, int rows) { return pb_gemm_uses_tma(s.w2[l], rows); }
+static bool hidden_f16(const pb_batch* b, const pb_shard& s, int l, int rows) {
+  return pb_gemm_uses_tma(s.w2[l], rows) || dec16(b, s, l, rows);
+}
 
 // norm -> this rank's gate|up rows with SwiGLU in the epilogue, h into its
 // chunk of hb (f16 for the TMA path of w2, f32 otherwise)
@@ -1596,7 +1614,7 @@ static int shard_gate_up(pb_batch* b, pb_shard& s, int l, int rows) {
   pb_model* m = b->m;
   pb_ctx* ctx = m->ctx;
   const int dim = m->c.dim, fc = s.p.hidden_chunk;
-  const bool gu16 = pb_gemm_uses_tma(s.gu[l], rows);
+  const bool gu16 = pb_gemm_uses_tma(s.gu[l], rows) || dec16(b, s, l, rows);
   __half* xn16 = reinterpret_cast<__half*>(s.xn);
   PB_TRY(launch_norm(m, s.x, rows, m->rms_ffn + (size_t)l * dim, gu16 ? nullptr : s.xn, gu16 ? xn16 : nullptr,
                      s.p.dim_chunk));
@@ -1630,9 +1648,11 @@ static int shard_down(pb_batch* b, pb_shard& s, int l, int rows) {
 // every shard of this process, then the all-gather that the next phase needs.
 static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start_pos, const int* pos_dev) {
   const pb_model_config& c = b->m->c;
+  b->decoding = rows_per_seq == 1 && pos_dev != nullptr;
   const size_t dchunk = (size_t)rows * (c.dim / b->world) * 4;
+  const size_t achunk = dec16(b, b->sh[0], l, rows) ? dchunk / 2 : dchunk;  // f16 attention output
   for (auto& s : b->sh) PB_TRY(shard_attention(b, s, l, rows, rows_per_seq, start_pos, pos_dev));
-  PB_TRY(batch_gather(b, XG_ATT, dchunk));
+  PB_TRY(batch_gather(b, XG_ATT, achunk));
   for (auto& s : b->sh) PB_TRY(shard_wo(b, s, l, rows));
   PB_TRY(batch_gather(b, XG_X, dchunk));
   for (auto& s : b->sh) PB_TRY(shard_gate_up(b, s, l, rows));
@@ -1650,11 +1670,14 @@ static int batch_head(pb_batch* b, bool from_x, const int* pos_dev) {
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
   for (auto& s : b->sh) {
-    if (from_x) PB_TRY(launch_norm(m, s.x, b->B, m->rms_final, s.xn, nullptr, s.p.dim_chunk));
-    else PB_TRY(launch_norm(m, s.xl, b->B, m->rms_final, s.xn));
+    const bool h16 = pb_gemm_uses_ws(s.head, b->B);
+    __half* xn16 = h16 ? reinterpret_cast<__half*>(s.xn) : nullptr;
+    if (from_x) PB_TRY(launch_norm(m, s.x, b->B, m->rms_final, h16 ? nullptr : s.xn, xn16, s.p.dim_chunk));
+    else PB_TRY(launch_norm(m, s.xl, b->B, m->rms_final, h16 ? nullptr : s.xn, xn16));
     const int vc = s.p.vocab_chunk;
     float* lg = s.logits + (size_t)s.rank * b->B * vc;
-    PB_TRY(pb_launch_q4_gemm(ctx, s.head, s.xn, c.dim, b->B, lg, vc, nullptr, 0));
+    if (h16) PB_TRY(pb_launch_q4_gemm(ctx, s.head, nullptr, c.dim, b->B, lg, vc, nullptr, 0, nullptr, xn16));
+    else PB_TRY(pb_launch_q4_gemm(ctx, s.head, s.xn, c.dim, b->B, lg, vc, nullptr, 0));
     if (b->world == 1) {
       k_argmax_rows<<<b->B, 1024, 0, ctx->stream>>>(lg, c.vocab, b->next, b->hist, pos_dev, c.seq_len + 1);
       PB_LAUNCHED(ctx, "k_argmax_rows");

@@ -1147,8 +1147,9 @@ struct as_warp_smem {
 template <int PER>
 __global__ void __launch_bounds__(AS_WARPS * 32)
 k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                 const int* __restrict__ pos_dev, int n_kv, float scale, float* __restrict__ out, int max_len,
-                 pb_seq_geo geo, float* __restrict__ ws, int* __restrict__ counters, int* err) {
+                 const int* __restrict__ pos_dev, int n_kv, float scale, float* __restrict__ out,
+                 __half* __restrict__ out16, int max_len, pb_seq_geo geo, float* __restrict__ ws,
+                 int* __restrict__ counters, int* err) {
   extern __shared__ __align__(16) unsigned char as_raw[];
   float* qs = reinterpret_cast<float*>(as_raw);  // [per][64]
   as_warp_smem* stage = reinterpret_cast<as_warp_smem*>(as_raw + AD_MAX_GROUP * AS_HD * 4);
@@ -1312,7 +1313,9 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
       O = __fmaf_rn(r[2 + d], f, O);
     }
     if (!split) {
-      out[z * geo.out + (size_t)g * per * AS_HD + i] = __fdiv_rn(O, L);
+      const size_t o = z * geo.out + (size_t)g * per * AS_HD + i;
+      if (out16) out16[o] = __float2half_rn(__fdiv_rn(O, L));
+      else out[o] = __fdiv_rn(O, L);
     } else {
       if (d == 0) {
         part[(size_t)h * rec] = M;
@@ -1340,7 +1343,9 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
       L = __fmaf_rn(__ldcg(r + 1), f, L);
       O = __fmaf_rn(__ldcg(r + 2 + d), f, O);
     }
-    out[z * geo.out + (size_t)g * per * AS_HD + i] = __fdiv_rn(O, L);
+    const size_t o = z * geo.out + (size_t)g * per * AS_HD + i;
+    if (out16) out16[o] = __float2half_rn(__fdiv_rn(O, L));
+    else out[o] = __fdiv_rn(O, L);
   }
   if (tid == 0) counters[(size_t)z * n_kv + g] = 0;  // for the next launch
 }
@@ -1374,7 +1379,7 @@ bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len) {
 // of a batched launch, `geo` apart).
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
                           int n_heads, int n_kv, int hd, float* out, int max_len, int nseq, pb_seq_geo geo,
-                          float* ws, size_t ws_floats, int* counters) {
+                          float* ws, size_t ws_floats, int* counters, __half* out16) {
   if (!(nseq > 1 ? pb_attn_decode_group_ok(n_heads, n_kv, hd, max_len) : pb_attn_decode_ok(n_heads, n_kv, hd, max_len)))
     return pb_set_error(ctx, PB_ERR_ARG, "decode attention needs n_heads %% n_kv == 0, head_dim %% 4 == 0, "
                                          "head_dim <= %d and max_len <= %d", AF_MAX_HD, (200 * 1024 - AF_PART * 8) / 4);
@@ -1387,13 +1392,14 @@ int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const fl
 #define PB_AS_CASE(P)                                                                                              \
   case P:                                                                                                          \
     return pb_launch(ctx, "k_attn_dec_split", true, k_attn_dec_split<P>, grid, dim3(AS_WARPS * 32), as_smem(), q, \
-                     kc, vc, pos_dev, n_kv, (float)scale, out, max_len, geo, ws, counters, ctx->d_err);
+                     kc, vc, pos_dev, n_kv, (float)scale, out, out16, max_len, geo, ws, counters, ctx->d_err);
         PB_AS_CASE(1) PB_AS_CASE(2) PB_AS_CASE(3) PB_AS_CASE(4) PB_AS_CASE(5) PB_AS_CASE(6) PB_AS_CASE(7)
         PB_AS_CASE(8)
 #undef PB_AS_CASE
         default: break;
       }
     }
+    if (out16) return pb_set_error(ctx, PB_ERR_ARG, "f16 attention output needs the split decode attention");
     return pb_launch(ctx, "k_attn_dec_group", true, k_attn_dec_group, dim3(n_kv, nseq), dim3(AG_THREADS),
                      ag_smem(per, hd, max_len), q, kc, vc, pos_dev, n_heads, n_kv, hd, (float)scale, out, max_len, geo,
                      ctx->d_err);

@@ -83,3 +83,36 @@ def test_q4_gemm_rejects(native, ctx):
     assert L.pb_q4_gemm(ctx.h, rows.h, dx.ptr, 4, 63, dc.ptr, 64) == native.PB_ERR_ARG  # ldx < K
     q8 = native.QMat(ctx, native.TYPE_Q8_0, np.zeros(64 * 2 * 34, np.uint8), 64, 64)
     assert L.pb_q4_gemm(ctx.h, q8.h, dx.ptr, 4, 64, dc.ptr, 64) == native.PB_ERR_ARG  # Q4_0 only
+
+
+@pytest.mark.parametrize("M,N,K,table", [(1, 128, 64, False), (3, 200, 2048, False), (64, 3072, 2048, False),
+                                         (17, 16384, 2048, False), (64, 2048, 8192, False), (40, 1000, 256, True),
+                                         (64, 4104, 2048, True)])
+def test_q4_gemm_f16_decode_size_same_bits(native, ctx, M, N, K, table):
+    """pb_q4_gemm_f16 at M <= 64 (the warp-specialised kernel: TMA-fed payload
+    and activations, half-precision dequant) gives the same bits as
+    pb_q4_gemm (the fused kernel) on activations already rounded to f16: the
+    same weight values, the same K-step order.  Both layouts."""
+    rng = np.random.default_rng(M * 7 + N + K)
+    raw = rand_q4_0(rng, N, K)
+    X = rng.standard_normal((M, K)).astype(np.float16)
+    L = native.lib()
+    m = native.QMat(ctx, native.TYPE_Q4_0 | (native.QMAT_TABLE if table else 0), raw, N, K)
+    dx32 = ctx.to_device(X.astype(f32))
+    dx16 = ctx.to_device(X)
+    c32, c16 = ctx.alloc(M * N * 4), ctx.alloc(M * N * 4)
+    ctx._check(L.pb_q4_gemm(ctx.h, m.h, dx32.ptr, M, K, c32.ptr, N))
+    ctx._check(L.pb_q4_gemm_f16(ctx.h, m.h, dx16.ptr, M, c16.ptr, N))
+    ctx.sync()
+    assert ctx.device_error() == 0
+    a, b = c32.download(count=M * N), c16.download(count=M * N)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"max abs diff {np.max(np.abs(a - b)):.3e}"
+    ref16 = X.astype(np.float64) @ dequant_f16(raw, N, K).T
+    assert np.max(np.abs(b.reshape(M, N) - ref16)) <= RTOL_SAME_OPERANDS * np.max(np.abs(ref16))
+
+
+def test_q4_gemm_f16_rejects(native, ctx):
+    rng = np.random.default_rng(2)
+    m = native.QMat(ctx, native.TYPE_Q4_0, rand_q4_0(rng, 64, 64), 64, 64)
+    dx, dc = ctx.alloc(100 * 64 * 2), ctx.alloc(100 * 64 * 4)
+    assert native.lib().pb_q4_gemm_f16(ctx.h, m.h, dx.ptr, 100, dc.ptr, 64) == native.PB_ERR_ARG  # 64 < M < 512
