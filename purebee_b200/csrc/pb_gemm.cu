@@ -627,12 +627,13 @@ extern "C" int pb_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int
 // ---------------------------------------------------------------------------
 // Decode-size batches (M <= 64 tokens, f16 activations): a warp-specialised
 // form of the fused-dequant GEMM.  CTA = 128 weight rows x 64 tokens, K split
-// over grid.z as in k_q4_gemm_tc.  A 3-stage ring per 64-wide K step holds the
-// raw Q4_0 payload tile (TMA from the resident layout), the activation tile
-// (TMA, 128-byte swizzle) and the dequantized f16 weight tile:
+// over grid.z as in k_q4_gemm_tc.  Per 64-wide K step a 6-stage ring holds the
+// raw Q4_0 payload tile (4 KB, TMA from the resident layout) and the
+// activation tile (TMA, 128-byte swizzle), so about 70 KB per SM stream in
+// flight; the dequantized f16 weight tile is double-buffered apart from it:
 //   warp 0 lane 0: TMA producer (payload + activations, one mbarrier);
 //   warp 1 lane 0: MMA issuer (four 128 x 64 x 16 MMAs per step, committed
-//     to the stage's "empty" mbarrier);
+//     to the stage's "empty" and the weight buffer's "free" mbarriers);
 //   warps 2-5: dequant, thread t = row t: its 2 blocks from shared memory,
 //     value (q - 8) * d in half precision: the nibble is OR-ed into the f16
 //     1024.0 (0x6400), 1032 is subtracted (exact) and the product with d is
@@ -642,13 +643,13 @@ extern "C" int pb_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int
 // in the same order, so both kernels give the same partial sums.
 // ---------------------------------------------------------------------------
 
-constexpr int GW_ROWS = 128, GW_TOK = 64, GW_K = 64, GW_STAGES = 3, GW_THREADS = 192;
+constexpr int GW_ROWS = 128, GW_TOK = 64, GW_K = 64, GW_STAGES = 6, GW_ABUF = 2, GW_THREADS = 192;
 constexpr int GW_RAW_BYTES = GW_ROWS * 32;               // 2 Q4_0 payloads (16 B) per row
 constexpr int GW_X_BYTES = GW_TOK * GW_K * 2;            // f16 activations, swizzled
 constexpr int GW_A_BYTES = GW_ROWS * GW_K * 2;           // f16 weights, swizzled
-constexpr int GW_STAGE_BYTES = GW_A_BYTES + GW_X_BYTES + GW_RAW_BYTES;  // A first: 1024-aligned tiles
-
-static size_t gw_smem() { return (size_t)GW_STAGES * GW_STAGE_BYTES + 1024; }
+constexpr int GW_STAGE_BYTES = GW_X_BYTES + GW_RAW_BYTES;  // X first: 1024-aligned
+// [GW_ABUF dequantized tiles][GW_STAGES (activations, payload) stages]
+static size_t gw_smem() { return (size_t)GW_ABUF * GW_A_BYTES + (size_t)GW_STAGES * GW_STAGE_BYTES + 1024; }
 
 namespace {
 __device__ __forceinline__ uint32_t h2_sub_mul(uint32_t v, uint32_t magic, uint32_t d2) {
@@ -666,7 +667,7 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
              const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int layout, int N, int N_pad, int nb, int M, int xkc,
              float* __restrict__ C, int ldc, int kper, pb_gemm_epi epi, int* err) {
   extern __shared__ __align__(1024) unsigned char gw_raw[];
-  __shared__ uint64_t full[GW_STAGES], aready[GW_STAGES], empty[GW_STAGES], accf;
+  __shared__ uint64_t full[GW_STAGES], empty[GW_STAGES], aready[GW_ABUF], afree[GW_ABUF], accf;
   __shared__ uint32_t tmem_base;
   unsigned char* ring = gw_raw + ((1024 - (smem_addr(gw_raw) & 1023)) & 1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -685,8 +686,11 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
   if (tid == 32) {
     for (int st = 0; st < GW_STAGES; ++st) {
       pb_mbar_init(&full[st], 1);
-      pb_mbar_init(&aready[st], 128);
       pb_mbar_init(&empty[st], 1);
+    }
+    for (int ab = 0; ab < GW_ABUF; ++ab) {
+      pb_mbar_init(&aready[ab], 128);
+      pb_mbar_init(&afree[ab], 1);
     }
     pb_mbar_init(&accf, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -702,33 +706,36 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       for (int g = 0; g < ksteps && ok; ++g) {
         const int st = g % GW_STAGES;
         if (g >= GW_STAGES && !(ok = pb_mbar_wait(&empty[st], ((g / GW_STAGES) - 1) & 1, err))) break;
-        unsigned char* sA = ring + st * GW_STAGE_BYTES;
+        unsigned char* sX = ring + GW_ABUF * GW_A_BYTES + st * GW_STAGE_BYTES;
         pb_mbar_arrive_tx(&full[st], GW_X_BYTES + GW_RAW_BYTES);
         const int ks = kbeg + g;
         if (layout == PB_LAYOUT_TILED8)
           asm volatile(
               "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-              "[%5];" ::"r"(smem_addr(sA + GW_A_BYTES + GW_X_BYTES)),
+              "[%5];" ::"r"(smem_addr(sX + GW_X_BYTES)),
               "l"(&map_q), "r"(0), "r"(2 * ks), "r"(n0 >> 3), "r"(smem_addr(&full[st]))
               : "memory");
         else
-          tma_load_2d(sA + GW_A_BYTES + GW_X_BYTES, &map_q, 32 * ks, n0, &full[st]);
-        tma_load_3d(sA + GW_A_BYTES, &map_x, (ks * GW_K) % xkc, m0, (ks * GW_K) / xkc, &full[st]);
+          tma_load_2d(sX + GW_X_BYTES, &map_q, 32 * ks, n0, &full[st]);
+        tma_load_3d(sX, &map_x, (ks * GW_K) % xkc, m0, (ks * GW_K) / xkc, &full[st]);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer
       bool ok = true;
       for (int g = 0; g < ksteps && ok; ++g) {
-        const int st = g % GW_STAGES;
-        if (!(ok = pb_mbar_wait(&aready[st], (g / GW_STAGES) & 1, err))) break;
+        const int st = g % GW_STAGES, ab = g % GW_ABUF;
+        // the weight tile of step g is written after the payload and activations landed
+        if (!(ok = pb_mbar_wait(&aready[ab], (g / GW_ABUF) & 1, err))) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        unsigned char* sA = ring + st * GW_STAGE_BYTES;
-        const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sA + GW_A_BYTES));
+        unsigned char* sA = ring + ab * GW_A_BYTES;
+        unsigned char* sX = ring + GW_ABUF * GW_A_BYTES + st * GW_STAGE_BYTES;
+        const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sX));
 #pragma unroll
         for (int kk = 0; kk < GW_K / 16; ++kk)
           mma_f16(tmem_d, da + 2 * kk, db + 2 * kk, gm_idesc(GW_TOK), (g > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&empty[st]);
+        mma_commit(&afree[ab]);
       }
       if (ok && ksteps > 0) mma_commit(&accf);
     }
@@ -760,9 +767,12 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
           d2[bb] = dv | (dv << 16);
         }
       }
+      const int ab = g % GW_ABUF;
       if (!(ok = pb_mbar_wait(&full[st], (g / GW_STAGES) & 1, err))) break;
-      unsigned char* sA = ring + st * GW_STAGE_BYTES;
-      const unsigned char* raw = sA + GW_A_BYTES + GW_X_BYTES;
+      // the weight buffer is free once the MMAs of step g - GW_ABUF completed
+      if (g >= GW_ABUF && !(ok = pb_mbar_wait(&afree[ab], ((g / GW_ABUF) - 1) & 1, err))) break;
+      unsigned char* sA = ring + ab * GW_A_BYTES;
+      const unsigned char* raw = ring + GW_ABUF * GW_A_BYTES + st * GW_STAGE_BYTES + GW_X_BYTES;
 #pragma unroll
       for (int bb = 0; bb < 2; ++bb) {
         const uint32_t off =
@@ -785,7 +795,7 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       }
       // generic-proxy reads of the payload and writes of the tile -> the async proxy
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&aready[st])) : "memory");
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&aready[ab])) : "memory");
     }
     // epilogue: TMEM lanes of this warp's quadrant, 64 token columns
     const bool empty_split = ksteps == 0;
@@ -843,9 +853,9 @@ static int launch_gemm_ws(pb_ctx* ctx, const pb_qmat* w, const __half* Xh, int M
   const int ktot = w->K / GW_K;
   dim3 grid(pb_cdiv(w->N, GW_ROWS), 1, 1);
   int splits = 1;
-  if (ws) {  // the plan of the fused kernel: split K until the grid covers the SMs twice
+  if (ws) {  // split K while the grid fits one wave of two CTAs per SM
     const int plan_n = epi.split_n > 0 ? epi.split_n : w->N;
-    splits = pb_cdiv(2 * ctx->sm_count, pb_cdiv(plan_n, GW_ROWS));
+    splits = 2 * ctx->sm_count / pb_cdiv(plan_n, GW_ROWS);
     const int max_by_k = ktot / 4 > 1 ? ktot / 4 : 1;
     const int max_by_ws = (int)(ws_bytes / ((size_t)M * plan_n * 4));
     const int fit = (int)(ws_bytes / ((size_t)M * w->N * 4));
