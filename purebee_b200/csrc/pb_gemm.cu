@@ -705,7 +705,7 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       bool ok = true;
       for (int g = 0; g < ksteps && ok; ++g) {
         const int st = g % GW_STAGES;
-        if (g >= GW_STAGES && !(ok = pb_mbar_wait(&empty[st], ((g / GW_STAGES) - 1) & 1, err))) break;
+        if (g >= GW_STAGES && !(ok = pb_mbar_wait_sleep(&empty[st], ((g / GW_STAGES) - 1) & 1, err))) break;
         unsigned char* sX = ring + GW_ABUF * GW_A_BYTES + st * GW_STAGE_BYTES;
         pb_mbar_arrive_tx(&full[st], GW_X_BYTES + GW_RAW_BYTES);
         const int ks = kbeg + g;
@@ -726,7 +726,7 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       for (int g = 0; g < ksteps && ok; ++g) {
         const int st = g % GW_STAGES, ab = g % GW_ABUF;
         // the weight tile of step g is written after the payload and activations landed
-        if (!(ok = pb_mbar_wait(&aready[ab], (g / GW_ABUF) & 1, err))) break;
+        if (!(ok = pb_mbar_wait_sleep(&aready[ab], (g / GW_ABUF) & 1, err))) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         unsigned char* sA = ring + ab * GW_A_BYTES;
         unsigned char* sX = ring + GW_ABUF * GW_A_BYTES + st * GW_STAGE_BYTES;
@@ -756,21 +756,24 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       }
     }
     bool ok = true;
+    // the two scales of a step, loaded one step ahead (L2-resident after the prefetch)
+    auto scales = [&](int ks, uint32_t (&d)[2]) {
+      d[0] = d[1] = 0u;
+      if (live_row && ks < kend) {
+#pragma unroll
+        for (int bb = 0; bb < 2; ++bb) d[bb] = __ldg(dsc + pb_slot(layout, row, 2 * ks + bb, nb));
+      }
+    };
+    uint32_t dnext[2];
+    scales(kbeg, dnext);
     for (int g = 0; g < ksteps && ok; ++g) {
       const int st = g % GW_STAGES, ks = kbeg + g;
-      // the two scales of this step (L2-resident; loaded before the wait)
-      uint32_t d2[2] = {0u, 0u};
-      if (live_row) {
-#pragma unroll
-        for (int bb = 0; bb < 2; ++bb) {
-          const uint32_t dv = __ldg(dsc + pb_slot(layout, row, 2 * ks + bb, nb));
-          d2[bb] = dv | (dv << 16);
-        }
-      }
+      const uint32_t d2[2] = {dnext[0] | (dnext[0] << 16), dnext[1] | (dnext[1] << 16)};
+      scales(ks + 1, dnext);
       const int ab = g % GW_ABUF;
-      if (!(ok = pb_mbar_wait(&full[st], (g / GW_STAGES) & 1, err))) break;
+      if (!(ok = pb_mbar_wait_sleep(&full[st], (g / GW_STAGES) & 1, err))) break;
       // the weight buffer is free once the MMAs of step g - GW_ABUF completed
-      if (g >= GW_ABUF && !(ok = pb_mbar_wait(&afree[ab], ((g / GW_ABUF) - 1) & 1, err))) break;
+      if (g >= GW_ABUF && !(ok = pb_mbar_wait_sleep(&afree[ab], ((g / GW_ABUF) - 1) & 1, err))) break;
       unsigned char* sA = ring + ab * GW_A_BYTES;
       const unsigned char* raw = ring + GW_ABUF * GW_A_BYTES + st * GW_STAGE_BYTES + GW_X_BYTES;
 #pragma unroll
@@ -799,7 +802,7 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
     }
     // epilogue: TMEM lanes of this warp's quadrant, 64 token columns
     const bool empty_split = ksteps == 0;
-    if (ok && !empty_split) ok = pb_mbar_wait(&accf, 0, err);
+    if (ok && !empty_split) ok = pb_mbar_wait_sleep(&accf, 0, err);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok) {
       const int q4 = warp & 3, erow = n0 + q4 * 32 + lane;

@@ -186,6 +186,26 @@ __device__ __forceinline__ bool pb_mbar_wait(uint64_t* bar, uint32_t parity, int
     }
   }
 }
+// As pb_mbar_wait, but each try_wait may suspend the thread (up to 20 us) until
+// the phase completes instead of returning at once: for role threads that
+// would otherwise spin through many polls.
+__device__ __forceinline__ bool pb_mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* err) {
+  const uint32_t addr = pb_smem_addr(bar);
+  const long long t0 = clock64();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity), "r"(20000u)
+        : "memory");
+    if (ok) return true;
+    if ((it & 15) == 15 && clock64() - t0 > 4000000000LL) {
+      pb_raise(err, PB_DEVERR_WAIT);
+      return false;
+    }
+  }
+}
 // Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
 // global memory into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void pb_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -293,6 +313,8 @@ struct pb_gemm_epi {
   int x_chunk = 0;
   int split_n = 0;
 };
+void pb_launch_rmsnorm(cudaStream_t st, const float* x, int rows, int dim, const float* w, double eps, float* out,
+                       __half* out16, int xc);
 int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
                       size_t ws_bytes, const pb_gemm_epi* epi = nullptr, const __half* Xh = nullptr);
 bool pb_gemm_uses_tma(const pb_qmat* w, int M);  // the f16-operand TMA path (takes Xh)

@@ -1272,6 +1272,7 @@ static int shard_init(pb_batch* b, pb_shard& s, int rank) {
   PB_TRY_CUDA(ctx, cudaMalloc(&s.xl, (size_t)b->B * c.dim * 4));
   PB_TRY_CUDA(ctx, cudaMalloc(&s.logits, (size_t)b->world * b->B * p.vocab_chunk * 4));
   PB_TRY_CUDA(ctx, cudaMalloc(&s.keys, (size_t)b->world * b->B * 8));
+  PB_TRY_CUDA(ctx, cudaMemsetAsync(s.keys, 0, (size_t)b->world * b->B * 8, ctx->stream));
   PB_TRY_CUDA(ctx, cudaMemsetAsync(s.kc, 0, kv * 4, ctx->stream));
   PB_TRY_CUDA(ctx, cudaMemsetAsync(s.vc, 0, kv * 4, ctx->stream));
   return PB_OK;
@@ -1309,45 +1310,18 @@ __global__ void k_batch_embed(int type, const uint8_t* __restrict__ qs, const ui
   x[(size_t)(d / xc) * rows * xc + (size_t)i * xc + d % xc] = v;
 }
 
-// Greedy token of every row (llama-streaming.js:899-909: first strict maximum),
-// recorded at hist[*pos][row].
-__global__ void __launch_bounds__(1024)
-k_argmax_rows(const float* __restrict__ logits, int V, int* __restrict__ next, int* __restrict__ hist,
-              const int* __restrict__ pos_dev, int hist_len) {
-  __shared__ unsigned long long red[32];
-  const int r = blockIdx.x;
+// Greedy token (llama-streaming.js:899-909: the first strict maximum) as an
+// ordered key per row over vocab chunks: CTA (row, chunk) folds its chunk
+// into keys[row] with atomicMax (the largest value, the lowest index among
+// equals, so the order of the atomics does not matter).  The key carries the
+// global token index (v0 + i).
+constexpr int AMX_CHUNK = 8192;
+__global__ void __launch_bounds__(256)
+k_argmax_chunks(const float* __restrict__ logits, int n, int ld, int v0, unsigned long long* __restrict__ keys) {
+  __shared__ unsigned long long red[8];
+  const int r = blockIdx.y, c0 = blockIdx.x * AMX_CHUNK, c1 = min(n, c0 + AMX_CHUNK);
   unsigned long long key = 0ull;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const unsigned long long k = pb_argmax_key(logits[(size_t)r * V + i], i);
-    key = k > key ? k : key;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
-    key = t > key ? t : key;
-  }
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = key;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned long long best = 0ull;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
-    const int tok = pb_argmax_index(best);
-    next[r] = tok;
-    if (hist && pos_dev) {
-      const int p = *pos_dev;
-      if (p >= 0 && p < hist_len) hist[(size_t)p * gridDim.x + r] = tok;
-    }
-  }
-}
-
-// Argmax key of every row over this rank's vocab rows [v0, v0 + n) (row
-// stride ld): the key carries the global token index.
-__global__ void __launch_bounds__(1024)
-k_argmax_keys(const float* __restrict__ logits, int n, int ld, int v0, unsigned long long* __restrict__ keys) {
-  __shared__ unsigned long long red[32];
-  const int r = blockIdx.x;
-  unsigned long long key = 0ull;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  for (int i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
     const unsigned long long k = pb_argmax_key(logits[(size_t)r * ld + i], v0 + i);
     key = k > key ? k : key;
   }
@@ -1360,18 +1334,22 @@ k_argmax_keys(const float* __restrict__ logits, int n, int ld, int v0, unsigned 
   __syncthreads();
   if (threadIdx.x == 0) {
     unsigned long long best = 0ull;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
-    keys[r] = best;
+    for (int w = 0; w < 8; ++w) best = red[w] > best ? red[w] : best;
+    atomicMax(keys + r, best);
   }
 }
 
 // The largest of the ranks' keys [world][B] per row: the global first maximum.
-__global__ void k_argmax_merge(const unsigned long long* __restrict__ keys, int world, int B, int* __restrict__ next,
-                               int* __restrict__ hist, const int* __restrict__ pos_dev, int hist_len) {
+// reset: clear this rank's keys for the next step's atomicMax.
+__global__ void k_argmax_merge(unsigned long long* __restrict__ keys, int world, int B, int* __restrict__ next,
+                               int* __restrict__ hist, const int* __restrict__ pos_dev, int hist_len,
+                               unsigned long long* __restrict__ reset) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= B) return;
   unsigned long long best = 0ull;
   for (int w = 0; w < world; ++w) best = keys[(size_t)w * B + r] > best ? keys[(size_t)w * B + r] : best;
+  if (reset) reset[r] = 0ull;
+  if (!next) return;
   const int tok = pb_argmax_index(best);
   next[r] = tok;
   if (hist && pos_dev) {
@@ -1678,18 +1656,19 @@ static int batch_head(pb_batch* b, bool from_x, const int* pos_dev) {
     float* lg = s.logits + (size_t)s.rank * b->B * vc;
     if (h16) PB_TRY(pb_launch_q4_gemm(ctx, s.head, nullptr, c.dim, b->B, lg, vc, nullptr, 0, nullptr, xn16));
     else PB_TRY(pb_launch_q4_gemm(ctx, s.head, s.xn, c.dim, b->B, lg, vc, nullptr, 0));
-    if (b->world == 1) {
-      k_argmax_rows<<<b->B, 1024, 0, ctx->stream>>>(lg, c.vocab, b->next, b->hist, pos_dev, c.seq_len + 1);
-      PB_LAUNCHED(ctx, "k_argmax_rows");
-      return PB_OK;
-    }
-    k_argmax_keys<<<b->B, 1024, 0, ctx->stream>>>(lg, s.p.vocab_rows, vc, s.p.vocab_row0, s.keys + (size_t)s.rank * b->B);
-    PB_LAUNCHED(ctx, "k_argmax_keys");
+    // this rank's keys (zero: cleared by the previous merge or at creation)
+    k_argmax_chunks<<<dim3(pb_cdiv(s.p.vocab_rows, AMX_CHUNK), b->B), 256, 0, ctx->stream>>>(
+        lg, s.p.vocab_rows, vc, s.p.vocab_row0, s.keys + (size_t)s.rank * b->B);
+    PB_LAUNCHED(ctx, "k_argmax_chunks");
   }
   PB_TRY(batch_gather(b, XG_KEYS, (size_t)b->B * 8));
-  k_argmax_merge<<<pb_cdiv(b->B, 128), 128, 0, ctx->stream>>>(b->sh[0].keys, b->world, b->B, b->next, b->hist, pos_dev,
-                                                             c.seq_len + 1);
-  PB_LAUNCHED(ctx, "k_argmax_merge");
+  for (auto& s : b->sh) {  // every shard reads the gathered keys and clears its own for the next step
+    const bool first = &s == &b->sh[0];
+    k_argmax_merge<<<pb_cdiv(b->B, 128), 128, 0, ctx->stream>>>(
+        s.keys, b->world, b->B, first ? b->next : nullptr, first ? b->hist : nullptr, pos_dev, c.seq_len + 1,
+        s.keys + (size_t)s.rank * b->B);
+    PB_LAUNCHED(ctx, "k_argmax_merge");
+  }
   return PB_OK;
 }
 
