@@ -1209,7 +1209,7 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
   for (int b = warp; b < nblk && ok; b += AS_WARPS, ++it) {
     const int buf = it & 1;
     if (b + AS_WARPS < nblk) issue(b + AS_WARPS, buf ^ 1);
-    if (!(ok = pb_mbar_wait(&w->bar[buf], (it >> 1) & 1, err))) break;
+    if (!(ok = pb_mbar_wait_sleep(&w->bar[buf], (it >> 1) & 1, err))) break;
     const int jb = j0 + b * AS_BLK;
     const bool live = jb + p < j1;
     float dot[PER];
@@ -1283,7 +1283,7 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
   if (!ok) {
     // a copy that never completed: wait (bounded) for the warp's other buffer
     // too, so no bulk copy is in flight when the CTA exits
-    pb_mbar_wait(&w->bar[(it + 1) & 1], ((it + 1) >> 1) & 1, err);
+    pb_mbar_wait_sleep(&w->bar[(it + 1) & 1], ((it + 1) >> 1) & 1, err);
   }
   __syncthreads();  // every warp is done with its staging: reuse it for the merge
   float* mg = reinterpret_cast<float*>(stage);  // [warp][per][2 + 64]: max, sum, output
