@@ -62,34 +62,58 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons sampled during the timed region.
+    A reader thread stamps each sample on arrival; entering the block waits
+    for the first sample (nvidia-smi takes a while to start), and only the
+    samples that arrive between entering and leaving the block are kept."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
+    def __init__(self, index, interval_ms=50, cmd=None):
         self.index = index
+        self.interval = interval_ms / 1000.0
+        self.cmd = cmd or ["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                           "-lms", str(interval_ms)]
         self.p = None
+        self.stamped = []
+        self.lines = []
+
+    def _read(self):
+        for line in self.p.stdout:
+            if line.strip():
+                self.stamped.append((time.monotonic(), line))
 
     def __enter__(self):
+        import threading
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
-                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.p = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.p = None
+            return self
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+        deadline = time.monotonic() + 5.0
+        while not self.stamped and time.monotonic() < deadline and self.p.poll() is None:
+            time.sleep(0.01)
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *a):
         self.lines = []
-        if self.p:
-            self.p.terminate()
-            try:
-                out, _ = self.p.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.p.kill()
-                out, _ = self.p.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        if not self.p:
+            return
+        t1 = time.monotonic()
+        time.sleep(self.interval)  # the sample that covers the end of the region
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            self.p.wait()
+        self.reader.join(timeout=5)
+        inside = [l for t, l in self.stamped if self.t0 <= t <= t1 + self.interval]
+        self.lines = inside or [l for t, l in self.stamped if t >= self.t0][:1]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
