@@ -368,8 +368,9 @@ int pb_model_load_gguf(pb_ctx* ctx, const pb_gguf* g, int seq_len, pb_model** ou
 
 /* n_seqs (<= 256) independent sequences over a streaming model's weights
  * (Q4_0 embedding), each with its own KV cache.  The projections and the LM
- * head run as tensor-core GEMMs (pb_q4_gemm: f16 operands, f32 sums), so
- * logits agree with the one-sequence path within a relative tolerance. */
+ * head run as tensor-core GEMMs (pb_q4_gemm / pb_q4_gemm_f16: f16 operands,
+ * f32 sums; decode steps of up to 64 sequences take the decode-size kernel),
+ * so logits agree with the one-sequence path within a relative tolerance. */
 typedef struct pb_batch pb_batch;
 int pb_batch_create(pb_model* m, int n_seqs, pb_batch** out);
 int pb_batch_free(pb_batch* b);
@@ -386,7 +387,7 @@ int pb_batch_decode(pb_batch* b, int steps, int* tokens_host, float* logits_host
 /* row split over GPUs (thread-pool.js:165-246 splits a matvec's output   */
 /* rows over worker threads, thread-pool.js:174-203 for the row ranges;   */
 /* here one rank per GPU holds a row range of every projection and of    */
-/* the LM head, and NCCL all-gathers complete the activations)           */
+/* the LM head, and in-place all-gathers complete the activations)       */
 /* ------------------------------------------------------------------ */
 
 /* Which rows rank `rank` of `world` holds.  Query heads and kv heads are
@@ -433,17 +434,21 @@ typedef struct pb_peerbuf pb_peerbuf;
 int pb_comm_register(pb_comm* c, void* buf_dev, pb_peerbuf** out);
 int pb_comm_deregister(pb_comm* c, pb_peerbuf* pb);
 int pb_comm_allgather_inplace(pb_comm* c, pb_peerbuf* pb, size_t chunk_bytes);
-/* The peer exchange's bounded wait, on this device alone: a two-rank
- * exchange whose peer never signals.  Returns PB_OK with *raised_code =
- * the device error the kernel raised (PB_DEVERR_WAIT, 2, expected) after
- * about timeout_ms, and clears it; the context stays usable. */
+/* The peer exchange kernels' bounded waits, on this device alone: two-rank
+ * exchanges (the bulk kernel, then the low-latency one) whose peer never
+ * signals.  Returns PB_OK with *raised_code = PB_DEVERR_WAIT (2) when both
+ * waits gave up after about timeout_ms each (the device error word is then
+ * cleared and the context stays usable), else the first other code seen. */
 int pb_comm_selftest_wait(pb_ctx* ctx, int timeout_ms, int* raised_code);
 
 /* This process's rank of a row-split batch over comm's ranks: every rank
- * calls prefill / decode with the same arguments, and every rank gets the
- * same tokens and logits, with the same bits as pb_batch_create on one GPU.
- * The exchanges are in-place NCCL all-gathers on the context stream, four per
- * layer plus the argmax keys, recorded into the decode graph. */
+ * calls prefill / decode with the same arguments (asking for logits_host on
+ * every rank or on none: the logits are gathered collectively), and every
+ * rank gets the same tokens and logits, with the same bits as
+ * pb_batch_create on one GPU.  The exchanges are in-place all-gathers on the
+ * context stream, four per layer plus the argmax keys, recorded into the
+ * decode graph: one peer-memory kernel each when pb_comm_peer_access is 1,
+ * else NCCL all-gathers. */
 int pb_batch_create_split(pb_model* m, int n_seqs, pb_comm* comm, pb_batch** out);
 /* All `world` ranks of a row split in this process, on ctx's one device,
  * with device copies in place of the all-gathers: the split's arithmetic on
