@@ -1,6 +1,6 @@
 """Benchmark: Llama-3.2-1B-shape Q4_0 decode tok/s and Q4 matvec HBM GB/s on B200.
 
-Workload: Llama-3.2-1B-shaped model (dim 2048,
+Workload (the headline configuration): Llama-3.2-1B-shaped model (dim 2048,
 16 layers, 32/8 heads, FFN 8192, vocab 128256, tied Q4_0 embedding), random
 init N(0, 0.02) from a fixed seed, a 128-token seeded prompt prefilled
 untimed, then greedy batch-1 decode with the KV cache growing from position

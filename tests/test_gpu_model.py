@@ -1,5 +1,5 @@
 """Whole-model parity on the GPU: greedy token identity with the CPU oracle
-on the BASELINE configurations (stories15M / SmolLM2-135M / Llama-3.2-1B
+on the benchmark configurations (stories15M / SmolLM2-135M / Llama-3.2-1B
 shapes), logits within a stated tolerance, and device-resident properties.
 
 Tolerance for logits: 1e-5 relative to the largest |logit| (the reference's
@@ -21,7 +21,7 @@ import make_golden as mg  # noqa: E402
 LOGIT_RTOL = 1e-5
 
 CONFIGS = {
-    # stories15M shape, quantize.js Q8 layers, f32 embedding
+    # the reference's CPU-runnable case: stories15M shape, quantize.js Q8 layers, f32 embedding
     "stories15M": dict(kind=1, emb_type=0, dim=288, hidden_dim=768, n_layers=6, n_heads=6, n_kv_heads=6,
                        head_dim=48, vocab=32000, seq_len=256, rope_theta=10000.0, eps=1e-5),
     # SmolLM2-135M shape, Q4_0 layers, Q8_0 tied embedding
