@@ -153,7 +153,10 @@ extern "C" int pb_gguf_open(const char* path, pb_gguf** out) {
   g->version = r.get<uint32_t>();
   if (!r.ok || g->version < 2 || g->version > 3) return bad(PB_ERR_ARG, "unsupported GGUF version (supports v2-v3)");
   const uint64_t n_tensors = r.get<uint64_t>(), n_kv = r.get<uint64_t>();
-  if (!r.ok || n_tensors > (1u << 24) || n_kv > (1u << 24)) return bad(PB_ERR_ARG, "bad tensor or metadata count");
+  // every metadata entry takes at least 13 bytes (key length, type, one value
+  // byte) and every tensor entry 32, so the counts cannot exceed what is left
+  if (!r.ok || n_tensors > (r.size - r.pos) / 32 || n_kv > (r.size - r.pos) / 13)
+    return bad(PB_ERR_ARG, "bad tensor or metadata count");
   // metadata (gguf.js:159-167)
   g->meta.resize(n_kv);
   for (uint64_t i = 0; i < n_kv; ++i) {
@@ -197,19 +200,27 @@ extern "C" int pb_gguf_open(const char* path, pb_gguf** out) {
   }
   // data section start, aligned (streaming-loader.js:61-62)
   if (const Meta* a = g->find("general.alignment"))
-    if (a->type != GT_STRING && a->type != GT_ARRAY && a->i > 0) g->alignment = (uint64_t)a->i;
+    if (a->type != GT_STRING && a->type != GT_ARRAY && a->i > 0) {
+      if (a->i > (1 << 20)) return bad(PB_ERR_ARG, "general.alignment out of range");
+      g->alignment = (uint64_t)a->i;
+    }
   g->data_start = (r.pos + g->alignment - 1) / g->alignment * g->alignment;
   for (auto& t : g->tensors) {
     int64_t n = 1;
     for (int64_t d : t.dims) {
       if (d <= 0) return bad(PB_ERR_ARG, "non-positive tensor dimension");
-      n *= d;
+      if (__builtin_mul_overflow(n, d, &n) || n > ((int64_t)1 << 50))
+        return bad(PB_ERR_ARG, "tensor element count out of range");
     }
     const TypeSize* ts = type_size(t.type);
     t.bytes = ts ? (ts->block == 1 ? (uint64_t)n * ts->bytes : (uint64_t)((n + ts->block - 1) / ts->block) * ts->bytes)
                  : 0;
+    if (t.rel > g->size) {
+      std::string what = "tensor " + t.name + " starts past the end of the file";
+      return bad(PB_ERR_ARG, what.c_str());
+    }
     t.off = g->data_start + t.rel;
-    if (ts && t.off + t.bytes > g->size) {
+    if (ts && (t.bytes > g->size || t.off > g->size - t.bytes)) {
       std::string what = "tensor " + t.name + " runs past the end of the file";
       return bad(PB_ERR_ARG, what.c_str());
     }

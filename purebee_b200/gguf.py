@@ -128,7 +128,7 @@ class GGUFFile:
                 name, t, nd, off, nb = ctypes.c_char_p(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int64(), ctypes.c_int64()
                 _err(L.pb_gguf_tensor_info(self.h, i, ctypes.byref(name), ctypes.byref(t), ctypes.byref(nd), dims,
                                            ctypes.byref(off), ctypes.byref(nb)))
-                infos.append({"name": name.value.decode(), "dims": [dims[d] for d in range(nd.value)],
+                infos.append({"name": name.value.decode("utf-8", errors="replace"), "dims": [dims[d] for d in range(nd.value)],
                               "type": t.value, "offset": off.value, "byteSize": nb.value})
             self._infos = infos
         return self._infos

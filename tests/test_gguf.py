@@ -159,3 +159,67 @@ def test_malformed_files_raise(tmp_path, gg):
     W.write_gguf(p, md, [("output_norm.weight", [64], 0, bytes(256))])
     with gg.GGUFFile(p) as f, pytest.raises(gg.GGUFError, match="token_embd"):
         f.config()
+
+
+_FUZZ = r'''
+import os, sys, struct
+import numpy as np
+sys.path.insert(0, os.path.join(os.environ["PB_ROOT"], "tests"))
+sys.path.insert(0, os.environ["PB_ROOT"])
+import gguf_writer as W
+from purebee_b200 import gguf as gg
+
+rng = np.random.default_rng(int(os.environ["PB_SEED"]))
+dim, vocab = 64, 40
+md = W.llama_metadata(dim, 160, 3, 4, 2, 96, vocab)
+tensors = [("token_embd.weight", [dim, vocab], 2, rng.integers(0, 256, vocab * dim // 32 * 18, dtype=np.uint8).tobytes()),
+           ("output_norm.weight", [dim], 0, W.f32_bytes(np.ones(dim)))]
+path = os.path.join(os.environ["PB_TMP"], "fuzz.gguf")
+W.write_gguf(path, md, tensors)
+good = open(path, "rb").read()
+huge = [2**63 - 1, 2**62, 2**40, 2**32, 2**31, 2**24, 0xFFFFFFFF, 1 << 20]
+outcomes = {"ok": 0, "error": 0}
+for it in range(int(os.environ["PB_ITERS"])):
+    b = bytearray(good)
+    kind = it % 3
+    if kind == 0:    # a few random bytes anywhere before the tensor data
+        for _ in range(int(rng.integers(1, 9))):
+            b[int(rng.integers(0, len(b) - vocab * dim // 32 * 18))] = int(rng.integers(0, 256))
+    elif kind == 1:  # an 8-byte field set to a large value
+        off = int(rng.integers(0, len(b) - 8))
+        b[off:off + 8] = struct.pack("<Q", huge[int(rng.integers(0, len(huge)))])
+    else:            # truncated
+        b = b[:int(rng.integers(0, len(b)))]
+    open(path, "wb").write(bytes(b))
+    try:
+        with gg.GGUFFile(path) as f:
+            f.metadata
+            for t in f.tensorInfos:
+                try:
+                    f.readTensorRaw(t["name"])
+                except gg.GGUFError:
+                    pass
+            try:
+                f.config()
+                f.tokenizer()
+            except gg.GGUFError:
+                pass
+        outcomes["ok"] += 1
+    except gg.GGUFError:
+        outcomes["error"] += 1
+print(outcomes)
+'''
+
+
+def test_corrupted_files_error_or_parse(tmp_path, native):
+    """Random corruption of a valid file (flipped bytes, 8-byte fields set to
+    huge counts, offsets or sizes, truncation) either parses or raises
+    GGUFError: the parser never crashes, hangs or allocates without bound.  It
+    runs in a child process so that a crash fails this test alone."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, PB_ROOT=root, PB_TMP=str(tmp_path), PB_SEED="17", PB_ITERS="600")
+    r = subprocess.run([sys.executable, "-c", _FUZZ], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, f"parser crashed (rc {r.returncode}): {r.stderr[-2000:]}"
+    assert "'error'" in r.stdout
