@@ -61,3 +61,25 @@ def test_no_device_fails_loudly(native):
 
 def test_abi_version(native):
     assert native.lib().pb_abi_version() == 1
+
+
+def declared_arity():
+    """name -> number of parameters, from the prototypes in include/*.h."""
+    out = {}
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        txt = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        txt = re.sub(r"//[^\n]*", "", txt)
+        for name, params in re.findall(r"\b(pb_[a-z0-9_]+)\s*\(([^;{}]*?)\)\s*;", txt, flags=re.S):
+            p = params.strip()
+            out[name] = 0 if p in ("", "void") else p.count(",") + 1
+    return out
+
+
+def test_binding_arity_matches_header(native):
+    """Every ctypes signature passes as many arguments as the C prototype
+    takes (a mismatch would silently misread arguments at the C ABI)."""
+    ar = declared_arity()
+    assert set(ar) == declared_symbols()  # every prototype was parsed
+    wrong = {n: (k, len(native.SIGNATURES[n][1])) for n, k in ar.items()
+             if n in native.SIGNATURES and len(native.SIGNATURES[n][1]) != k}
+    assert not wrong, f"(header, binding) parameter counts differ: {wrong}"
