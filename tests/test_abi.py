@@ -83,3 +83,51 @@ def test_binding_arity_matches_header(native):
     wrong = {n: (k, len(native.SIGNATURES[n][1])) for n, k in ar.items()
              if n in native.SIGNATURES and len(native.SIGNATURES[n][1]) != k}
     assert not wrong, f"(header, binding) parameter counts differ: {wrong}"
+
+
+def _c_kind(decl):
+    d = decl.strip()
+    if "*" in d or "[" in d:
+        return "ptr"
+    d = re.sub(r"\b(const|unsigned|signed)\b", " ", d).split()
+    t = d[0] if d else ""
+    if t in ("double",):
+        return "f64"
+    if t in ("float",):
+        return "f32"
+    if t in ("size_t", "int64_t", "uint64_t", "long"):
+        return "i64"
+    if t in ("int", "int32_t", "uint32_t", "bool"):
+        return "i32"
+    return "other:" + t
+
+
+def _py_kind(ct):
+    import ctypes
+    if ct in (ctypes.c_void_p, ctypes.c_char_p) or (isinstance(ct, type) and issubclass(ct, ctypes._Pointer)):
+        return "ptr"
+    if ct is ctypes.c_double:
+        return "f64"
+    if ct is ctypes.c_float:
+        return "f32"
+    if ctypes.sizeof(ct) == 8:
+        return "i64"
+    if ctypes.sizeof(ct) == 4:
+        return "i32"
+    return "other"
+
+
+def test_binding_argument_kinds_match_header(native):
+    """Each argument's kind (pointer, 4- or 8-byte integer, float, double)
+    agrees between the prototype and the ctypes binding: a 4-byte int passed
+    where the C side reads a size_t leaves the upper half undefined."""
+    wrong = {}
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        txt = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        for name, params in re.findall(r"\b(pb_[a-z0-9_]+)\s*\(([^;{}]*?)\)\s*;", txt, flags=re.S):
+            p = params.strip()
+            kinds = [] if p in ("", "void") else [_c_kind(x) for x in p.split(",")]
+            got = [_py_kind(t) for t in native.SIGNATURES[name][1]]
+            if kinds != got:
+                wrong[name] = (kinds, got)
+    assert not wrong, f"(header, binding) argument kinds differ: {wrong}"
