@@ -131,3 +131,21 @@ def test_binding_argument_kinds_match_header(native):
             if kinds != got:
                 wrong[name] = (kinds, got)
     assert not wrong, f"(header, binding) argument kinds differ: {wrong}"
+
+
+def test_binding_return_kinds_match_header(native):
+    """Return kinds agree too (a pointer or 64-bit result read as a 4-byte int
+    would be truncated)."""
+    wrong, seen = {}, set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        txt = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        for ret, name in re.findall(r"(?:^|;|\})\s*((?:const\s+)?[a-z_0-9]+(?:\s*\*)?)\s*\b(pb_[a-z0-9_]+)\s*\([^;{}]*?\)\s*;",
+                                    txt, flags=re.S | re.M):
+            seen.add(name)
+            want = "void" if ret.strip() == "void" else _c_kind(ret)
+            rt = native.SIGNATURES[name][0]
+            got = "void" if rt is None else _py_kind(rt)
+            if want != got:
+                wrong[name] = (ret.strip(), want, got)
+    assert seen == declared_symbols()
+    assert not wrong, f"(header, binding) return kinds differ: {wrong}"
