@@ -105,3 +105,25 @@ def test_tokenizer_from_gguf_file(native, tmp_path):
     with GGUFFile(p) as f:
         tk = f.tokenizer()
     assert tk.encode("hi hi") == [7, 7] and tk.decode([1, 7, 7, 2]) == " hi hi"
+
+
+def test_gpt2_encoding_is_lossless_at_the_byte_level():
+    """Byte-level BPE keeps every byte: for any text the tokens' strings
+    concatenate to the byte-to-unicode image of its UTF-8 bytes, every merge
+    yields a vocabulary entry, and ASCII text decodes back exactly."""
+    from hypothesis import given, settings, strategies as st
+    b2u, _ = buildByteToUnicode()
+    extra = ["th", "he", "the", "Ġt", "Ġthe", "in", "ing", "Ã©", "ll", "ĠĠ"]
+    merges = ["t h", "h e", "th e", "Ġ t", "Ġt he", "i n", "in g", "Ã ©", "l l", "Ġ Ġ"]
+    tk, vocab = gpt2_vocab(extra, merges)
+
+    @settings(max_examples=300, deadline=None)
+    @given(st.text(max_size=40))
+    def check(text):
+        ids = tk.encode(text)
+        assert all(0 <= i < len(vocab) for i in ids)
+        assert "".join(vocab[i] for i in ids) == "".join(b2u[b] for b in text.encode("utf-8", "surrogatepass"))
+        if text.isascii():
+            assert tk.decode(ids) == text
+
+    check()
