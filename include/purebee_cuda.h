@@ -337,7 +337,9 @@ int pb_gguf_version(const pb_gguf* g);
 int64_t pb_gguf_data_start(const pb_gguf* g); /* aligned start of the tensor data */
 int64_t pb_gguf_alignment(const pb_gguf* g);  /* general.alignment, default 32 */
 /* Metadata: value types are GGUF's (0 u8 .. 12 f64; 8 string, 9 array).
- * Strings are returned as borrowed pointers with their byte length. */
+ * String values are returned as borrowed pointers with their byte length.
+ * Keys and tensor names are returned as NUL-terminated C strings: GGUF keys
+ * are ASCII identifiers, and a name with an embedded NUL byte reads up to it. */
 int pb_gguf_meta_count(const pb_gguf* g);
 int pb_gguf_meta_find(const pb_gguf* g, const char* key); /* index or -1 */
 int pb_gguf_meta_key(const pb_gguf* g, int i, const char** key);

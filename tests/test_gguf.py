@@ -223,3 +223,51 @@ def test_corrupted_files_error_or_parse(tmp_path, native):
     r = subprocess.run([sys.executable, "-c", _FUZZ], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, f"parser crashed (rc {r.returncode}): {r.stderr[-2000:]}"
     assert "'error'" in r.stdout
+
+
+def test_metadata_round_trip_property(tmp_path, gg):
+    """Any metadata the format can hold reads back as written: every scalar
+    type over its whole range, Unicode keys (without NUL: keys are C strings
+    at the ABI) and strings (with NUL: values carry their length), arrays of
+    scalars and of strings."""
+    from hypothesis import given, settings, strategies as st
+    ints = {W.U8: (0, 2**8 - 1), W.I8: (-2**7, 2**7 - 1), W.U16: (0, 2**16 - 1), W.I16: (-2**15, 2**15 - 1),
+            W.U32: (0, 2**32 - 1), W.I32: (-2**31, 2**31 - 1), W.U64: (0, 2**53), W.I64: (-2**53, 2**53)}
+    text = st.text(st.characters(blacklist_categories=("Cs",)), max_size=12)
+    keys = st.text(st.characters(blacklist_categories=("Cs",), blacklist_characters="\x00"), max_size=12)
+
+    def value(t):
+        if t in ints:
+            return st.integers(*ints[t])
+        if t == W.F32:
+            return st.floats(width=32, allow_nan=False)
+        if t == W.F64:
+            return st.floats(allow_nan=False)
+        if t == W.BOOL:
+            return st.booleans().map(int)
+        return text
+
+    scalar_t = st.sampled_from(sorted(ints) + [W.F32, W.F64, W.BOOL, W.STRING])
+    entry = scalar_t.flatmap(lambda t: st.one_of(
+        value(t).map(lambda v: (t, v)),
+        st.lists(value(t), max_size=5).map(lambda vs: (W.ARRAY, (t, vs)))))
+    path = str(tmp_path / "p.gguf")
+
+    @settings(max_examples=150, deadline=None)
+    @given(st.dictionaries(keys, entry, max_size=8))
+    def check(md):
+        W.write_gguf(path, [(k, t, v) for k, (t, v) in md.items()], [])
+        with gg.GGUFFile(path) as f:
+            got = f.metadata
+        assert set(got) == set(md)
+        for k, (t, v) in md.items():
+            if t == W.ARRAY:
+                et, vs = v
+                want = [bool(x) for x in vs] if et == W.BOOL else vs
+                assert got[k] == want, (k, et)
+            elif t == W.BOOL:
+                assert got[k] is bool(v)
+            else:
+                assert got[k] == v, (k, t)
+
+    check()
