@@ -46,6 +46,10 @@ extern "C" {
 #define PB_TYPE_Q4_0 2
 #define PB_TYPE_Q4_1 3
 #define PB_TYPE_Q8_0 8
+/* GGUF decode only (pb_gguf_dequant; a model loads a Q6_K embedding or
+ * output.weight as a dequantized f32 table, as streaming-loader.js:324-335
+ * does): 256-value blocks of 210 bytes, gguf.js:317-355. */
+#define PB_TYPE_Q6_K 14
 /* OR'ed into the type of pb_qmat_upload / pb_qmat_from_device: store the
  * matrix as a table read one row per lane (the layout pb_qmat_head needs)
  * instead of the matvec layout. */
@@ -190,8 +194,9 @@ int pb_attention(pb_ctx* ctx, const float* Q_dev, const float* K_dev, const floa
  * instead keeps the seqQ x seqK scores and probabilities in one fixed device
  * array of PB_NOALLOC_ATTN_BYTES per device, whose address pb_init looks up,
  * so the call itself makes no allocation and no set-up.
- * Limit: 2 * (4 * seqQ * seqK rounded up to 256) <= PB_NOALLOC_ATTN_BYTES
- * (seqQ * seqK <= 524224), else PB_ERR_ARG before anything is launched.
+ * Limits: 2 * (4 * seqQ * seqK rounded up to 256) <= PB_NOALLOC_ATTN_BYTES
+ * (seqQ * seqK <= 524288) and seqQ <= 65535, else PB_ERR_ARG before anything
+ * is launched (pb_attention has the same seqQ limit).
  * The array is shared by every context and stream on the device: calls that
  * overlap in time race on it, so the caller serialises them (one stream, or
  * an event between streams). */
@@ -218,7 +223,8 @@ int pb_quantize_q4a(pb_ctx* ctx, const float* x_dev, int64_t n, float* scales_de
 /* quantize.js:170-208 dequantize_q8 / dequantize_q4 */
 int pb_dequantize_q8a(pb_ctx* ctx, const float* scales_dev, const int8_t* q_dev, int64_t n, float* out_dev);
 int pb_dequantize_q4a(pb_ctx* ctx, const float* scales_dev, const uint8_t* q_dev, int64_t n, float* out_dev);
-/* gguf.js:219-315 loadTensorData for F32/F16/Q4_0/Q4_1/Q8_0 blocks */
+/* gguf.js:219-355 loadTensorData for F32/F16/Q4_0/Q4_1/Q8_0/Q6_K blocks
+ * (raw_dev holds ceil(n / block) whole blocks) */
 int pb_gguf_dequant(pb_ctx* ctx, int type, const void* raw_dev, int64_t n, float* out_dev);
 /* GGUF Q4_0 / Q8_0 block encoders (not in the reference, which only decodes
  * GGUF; used to build quantized synthetic models on the device). */
@@ -297,6 +303,21 @@ int pb_model_set_token(pb_model* m, int token);
 int pb_model_reset_cache(pb_model* m);             /* llama-streaming.js:828-837 */
 int pb_model_rollback_cache(pb_model* m, int pos); /* llama-streaming.js:845-862 */
 int pb_model_kv(pb_model* m, int layer, int which_v, float* host, size_t floats);
+/* Llama-3 RoPE frequency scaling, off by default.  The reference applies
+ * none: llama-streaming.js:316-336 rotates by pos / theta^(i/hd), and
+ * gguf.js:378-410 never maps rope_freqs.weight; so every parity check keeps
+ * it off.  A caller that wants the published Llama 3.1 / 3.2 rule (Llama-3.2-1B:
+ * factor 32, low_freq_factor 1, high_freq_factor 4, original_max_pos 8192)
+ * turns it on here; factor <= 0 turns it off.  Pair frequency f, wavelength
+ * w = 2 pi / f, C = original_max_pos: f if w < C / high; f / factor if
+ * w > C / low; else (1 - s) f / factor + s f with s = (C / w - low) / (high - low). */
+int pb_model_set_rope_scaling(pb_model* m, double factor, double low_freq_factor, double high_freq_factor,
+                              int original_max_pos);
+int pb_model_rope_scaling(const pb_model* m, double* factor_out); /* 0 when off */
+/* The pair frequencies freqs_out[head_dim / 2] of that rule (host only, no
+ * device needed; factor <= 0 gives the reference's 1 / theta^(i/hd)). */
+int pb_rope_freqs(double theta, int head_dim, double factor, double low_freq_factor, double high_freq_factor,
+                  int original_max_pos, double* freqs_out);
 /* Algorithmic bytes one decode step reads at cache length `pos+1`. */
 int64_t pb_model_decode_bytes(const pb_model* m, int pos);
 /* Kernel launches of one decode step. */

@@ -64,6 +64,7 @@ def lib():
         "orc_dequant_q4_1": (None, [U8P, c_i64, F32P]),
         "orc_dequant_q8_0": (None, [U8P, c_i64, F32P]),
         "orc_dequant_f16": (None, [U8P, c_i64, F32P]),
+        "orc_dequant_q6_k": (None, [U8P, c_i64, F32P]),
         "orc_quantize_gguf_q4_0": (None, [F32P, c_i64, U8P]),
         "orc_quantize_gguf_q8_0": (None, [F32P, c_i64, U8P]),
         "orc_q4_0_matvec_wasm": (None, [F32P, U8P, ctypes.c_int, ctypes.c_int, F32P]),
@@ -160,6 +161,12 @@ def dequant_q4_0(raw, n):
 def dequant_q4_1(raw, n):
     out = np.empty(n, np.float32)
     lib().orc_dequant_q4_1(_u8(raw), n, out)
+    return out
+
+
+def dequant_q6_k(raw, n):
+    out = np.empty(n, np.float32)
+    lib().orc_dequant_q6_k(_u8(raw), n, out)
     return out
 
 

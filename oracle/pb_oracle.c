@@ -155,6 +155,41 @@ void orc_dequant_f16(const uint8_t* raw, int64_t n, float* out) {
   for (int64_t i = 0; i < n; ++i) out[i] = orc_f16_exact(rd16(raw + 2 * i));
 }
 
+/* gguf.js:317-355 Q6_K: 210-byte blocks of 256 values, [ql 128][qh 64]
+ * [int8 scales 16][f16 d].  Two halves of 128; for l in 0..31 of a half the
+ * four values l, l+32, l+64, l+96 take the low nibble of ql[l], the low
+ * nibble of ql[l+32], the high nibble of ql[l], the high nibble of ql[l+32],
+ * each with two bits of qh[l] (bits 0-1, 2-3, 4-5, 6-7) on top, minus 32,
+ * times d times the scale is + 0, 2, 4, 6 (is = 8 half + l / 16).  JS
+ * computes d * sc * q in double and stores the f32. */
+void orc_dequant_q6_k(const uint8_t* raw, int64_t n, float* out) {
+  int64_t nb = (n + 255) / 256, idx = 0;
+  for (int64_t b = 0; b < nb; ++b) {
+    const uint8_t* blk = raw + b * 210;
+    const uint8_t* ql = blk;
+    const uint8_t* qh = blk + 128;
+    const int8_t* sc = (const int8_t*)(blk + 192);
+    const double d = orc_f16_exact(rd16(blk + 208));
+    for (int half = 0; half < 2; ++half) {
+      const uint8_t* qlb = ql + half * 64;
+      const uint8_t* qhb = qh + half * 32;
+      for (int l = 0; l < 32; ++l) {
+        const int is = half * 8 + l / 16;
+        const int q1 = ((qlb[l] & 0xF) | (((qhb[l] >> 0) & 3) << 4)) - 32;
+        const int q2 = ((qlb[l + 32] & 0xF) | (((qhb[l] >> 2) & 3) << 4)) - 32;
+        const int q3 = ((qlb[l] >> 4) | (((qhb[l] >> 4) & 3) << 4)) - 32;
+        const int q4 = ((qlb[l + 32] >> 4) | (((qhb[l] >> 6) & 3) << 4)) - 32;
+        const int64_t base = idx + half * 128;
+        if (base + l < n) out[base + l] = (float)(d * sc[is + 0] * q1);
+        if (base + l + 32 < n) out[base + l + 32] = (float)(d * sc[is + 2] * q2);
+        if (base + l + 64 < n) out[base + l + 64] = (float)(d * sc[is + 4] * q3);
+        if (base + l + 96 < n) out[base + l + 96] = (float)(d * sc[is + 6] * q4);
+      }
+    }
+    idx += 256;
+  }
+}
+
 /* ------------------------------------------------------------------ */
 /* GGUF encode: the build's own definition (the reference decodes only). */
 /* Q4_0: signed max-magnitude element m, d = m / -8, q = min(15,          */
@@ -1024,6 +1059,7 @@ int orc_model_set_head(orc_model* m, int emb_type, const uint8_t* raw) {
   if (!m->head_f32) m->head_f32 = (float*)malloc(sizeof(float) * (size_t)ne);
   if (emb_type == ORC_EMB_Q4_0) orc_dequant_q4_0(raw, ne, m->head_f32);
   else if (emb_type == ORC_EMB_Q8_0) orc_dequant_q8_0(raw, ne, m->head_f32);
+  else if (emb_type == ORC_EMB_F32) memcpy(m->head_f32, raw, sizeof(float) * (size_t)ne);
   else return -1;
   return 0;
 }

@@ -42,6 +42,7 @@ void orc_dequant_q4_0(const uint8_t* raw, int64_t n, float* out);
 void orc_dequant_q4_1(const uint8_t* raw, int64_t n, float* out);
 void orc_dequant_q8_0(const uint8_t* raw, int64_t n, float* out);
 void orc_dequant_f16(const uint8_t* raw, int64_t n, float* out);
+void orc_dequant_q6_k(const uint8_t* raw, int64_t n, float* out); /* gguf.js:317-355 */
 
 /* ---- GGUF block encode (not in the reference; the build's own definition) ---- */
 void orc_quantize_gguf_q4_0(const float* x, int64_t n, uint8_t* out);
@@ -115,7 +116,8 @@ uint8_t* orc_model_tensor(orc_model* m, int layer, int which, int64_t* nbytes);
 float* orc_model_q8a_scales(orc_model* m, int layer, int which, int64_t* count);
 /* Re-derive cached f32 tables after raw bytes were replaced. */
 void orc_model_refresh(orc_model* m);
-/* Untied LM head from GGUF bytes (emb_type ORC_EMB_Q4_0 / ORC_EMB_Q8_0). */
+/* Untied LM head from GGUF bytes (emb_type ORC_EMB_Q4_0 / ORC_EMB_Q8_0), or an
+ * f32 table (ORC_EMB_F32, already dequantized). */
 int orc_model_set_head(orc_model* m, int emb_type, const uint8_t* raw);
 /* llama-streaming.js:868-894 sample() with the uniform draw r given. */
 int orc_sample(const float* logits, int V, int topK, double temperature, double r);

@@ -154,6 +154,9 @@ SIGNATURES = {
     "pb_model_reset_cache": (I, [V]),
     "pb_model_rollback_cache": (I, [V, I]),
     "pb_model_kv": (I, [V, I, I, V, SZ]),
+    "pb_model_set_rope_scaling": (I, [V, D, D, D, I]),
+    "pb_model_rope_scaling": (I, [V, ctypes.POINTER(D)]),
+    "pb_rope_freqs": (I, [D, I, D, D, D, I, V]),
     "pb_model_decode_bytes": (I64, [V, I]),
     "pb_model_decode_launches": (I, [V]),
     "pb_q4_gemm_f16": (I, [V, V, V, I, V, I]),

@@ -459,10 +459,23 @@ __global__ void k_gguf_dequant(int type, const uint8_t* __restrict__ raw, int64_
       int byte = blk[4 + (j & 15)];
       int nib = j < 16 ? (byte & 15) : (byte >> 4);
       out[i] = (float)__dadd_rn(__dmul_rn((double)nib, d), m);
-    } else {  // Q8_0
+    } else if (type == PB_TYPE_Q8_0) {
       const uint8_t* blk = raw + b * 34;
       float d = pb_f16_exact((uint16_t)(blk[0] | (blk[1] << 8)));
       out[i] = __fmul_rn((float)(int8_t)blk[2 + j], d);  // exact: 8-bit x 11-bit
+    } else {  // Q6_K (gguf.js:317-355): [ql 128][qh 64][int8 scales 16][f16 d]
+      const int64_t bk = i / 256;
+      const int e = (int)(i % 256), half = e >> 7, r = e & 127, part = r >> 5, l = r & 31;
+      const uint8_t* blk = raw + bk * 210;
+      const uint8_t ql = blk[half * 64 + l + (part & 1) * 32];  // parts 0, 2 read byte l; 1, 3 byte l + 32
+      const uint8_t qh = blk[128 + half * 32 + l];
+      const int lo = (part < 2) ? (ql & 15) : (ql >> 4);
+      const int q = (lo | (((qh >> (2 * part)) & 3) << 4)) - 32;
+      const int sc = (int8_t)blk[192 + half * 8 + (l >> 4) + 2 * part];
+      const float d = pb_f16_exact((uint16_t)(blk[208] | (blk[209] << 8)));
+      // d * sc is exact in f32 (11 x 8 significant bits), so one rounding of
+      // the exact product, like the reference's double product stored to f32
+      out[i] = __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
     }
   }
 }
@@ -470,9 +483,9 @@ __global__ void k_gguf_dequant(int type, const uint8_t* __restrict__ raw, int64_
 extern "C" int pb_gguf_dequant(pb_ctx* ctx, int type, const void* raw, int64_t n, float* out) {
   if (!ctx || !raw || !out || n <= 0) return PB_ERR_ARG;
   if (type != PB_TYPE_F32 && type != PB_TYPE_F16 && type != PB_TYPE_Q4_0 && type != PB_TYPE_Q4_1 &&
-      type != PB_TYPE_Q8_0)
+      type != PB_TYPE_Q8_0 && type != PB_TYPE_Q6_K)
     return pb_set_error(ctx, PB_ERR_ARG, "unsupported tensor type %d", type);
-  if (type != PB_TYPE_F32 && type != PB_TYPE_F16 && n % 32)
+  if (type != PB_TYPE_F32 && type != PB_TYPE_F16 && type != PB_TYPE_Q6_K && n % 32)
     return pb_set_error(ctx, PB_ERR_ARG, "quantized tensors need n %% 32 == 0");
   k_gguf_dequant<<<pb_cdiv(n, 256), 256, 0, ctx->stream>>>(type, (const uint8_t*)raw, n, out);
   PB_LAUNCHED(ctx, "k_gguf_dequant");

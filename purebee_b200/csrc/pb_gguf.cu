@@ -12,6 +12,8 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <new>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -93,6 +95,18 @@ struct Reader {
   }
 };
 
+// Smallest encoded size of one array element of GGUF value type t (0: not
+// an element type).
+uint64_t elem_min_bytes(uint32_t t) {
+  switch (t) {
+    case GT_U8: case GT_I8: case GT_BOOL: return 1;
+    case GT_U16: case GT_I16: return 2;
+    case GT_U32: case GT_I32: case GT_F32: return 4;
+    case GT_U64: case GT_I64: case GT_F64: case GT_STRING: return 8;
+    default: return 0;
+  }
+}
+
 bool scalar(Reader& r, uint32_t t, Meta& m) {
   switch (t) {
     case GT_U8: m.i = r.get<uint8_t>(); break;
@@ -130,7 +144,7 @@ struct pb_gguf {
 
 extern "C" const char* pb_gguf_last_error(void) { return g_err.c_str(); }
 
-extern "C" int pb_gguf_open(const char* path, pb_gguf** out) {
+static int gguf_open(const char* path, pb_gguf** out) {
   if (!path || !out) return fail(PB_ERR_ARG, "pb_gguf_open: null argument");
   *out = nullptr;
   FILE* f = fopen(path, "rb");
@@ -167,8 +181,13 @@ extern "C" int pb_gguf_open(const char* path, pb_gguf** out) {
     if (m.type == GT_ARRAY) {  // gguf.js:137-144
       m.arr_type = r.get<uint32_t>();
       const uint64_t n = r.get<uint64_t>();
-      if (!r.ok || n > r.size - r.pos) return bad(PB_ERR_ARG, "bad metadata array");
       if (m.arr_type == GT_ARRAY) return bad(PB_ERR_ARG, "nested metadata arrays are not supported");
+      // each element takes at least its encoded size (a string its 8-byte
+      // length), so the count cannot exceed what is left of the file; this
+      // keeps a corrupt count from asking for more host memory than the
+      // file could describe
+      const uint64_t esz = elem_min_bytes(m.arr_type);
+      if (!r.ok || esz == 0 || n > (r.size - r.pos) / esz) return bad(PB_ERR_ARG, "bad metadata array");
       Meta e;
       if (m.arr_type == GT_STRING) {
         m.as.resize(n);
@@ -227,6 +246,18 @@ extern "C" int pb_gguf_open(const char* path, pb_gguf** out) {
   }
   *out = g;
   return PB_OK;
+}
+
+// No C++ exception may cross the C ABI: a host allocation that fails while
+// parsing becomes an error status.
+extern "C" int pb_gguf_open(const char* path, pb_gguf** out) {
+  try {
+    return gguf_open(path, out);
+  } catch (const std::bad_alloc&) {
+    return fail(PB_ERR_OOM, "%s: out of host memory while parsing", path ? path : "(null)");
+  } catch (const std::exception& e) {
+    return fail(PB_ERR_ARG, "%s: %s", path ? path : "(null)", e.what());
+  }
 }
 
 extern "C" int pb_gguf_close(pb_gguf* g) {
@@ -353,6 +384,12 @@ extern "C" int pb_gguf_tensor_read(const pb_gguf* g, int i, void* host, size_t b
 // (streaming-loader.js:57), else the embedding's row count.  kind and
 // emb_type come from the tensor types: Q4_0 layer weights make a streaming
 // model; its embedding is Q4_0 or Q8_0.
+// Embedding / output tables of these ggml types are kept as a dequantized f32
+// table (the reference dequantizes every table to f32 at load,
+// streaming-loader.js:324-335); Q4_0 and Q8_0 stay quantized and are
+// dequantized exactly inside the kernels.
+static bool table_as_f32(uint32_t t) { return t == 0 || t == 1 || t == PB_TYPE_Q6_K; }
+
 extern "C" int pb_gguf_config(const pb_gguf* g, pb_model_config* cfg) {
   if (!g || !cfg) return fail(PB_ERR_ARG, "pb_gguf_config: null argument");
   std::string arch = "llama";
@@ -386,7 +423,10 @@ extern "C" int pb_gguf_config(const pb_gguf* g, pb_model_config* cfg) {
   cfg->kind = PB_MODEL_STREAMING_Q4;
   if (e.type == 2) cfg->emb_type = PB_TYPE_Q4_0;
   else if (e.type == 8) cfg->emb_type = PB_TYPE_Q8_0;
-  else return fail(PB_ERR_ARG, "token_embd.weight has ggml type %u; the device model takes Q4_0 or Q8_0", e.type);
+  else if (table_as_f32(e.type)) cfg->emb_type = PB_TYPE_F32;  // dequantized, as streaming-loader.js:324-335
+  else
+    return fail(PB_ERR_ARG, "token_embd.weight has ggml type %u; the device model takes Q4_0, Q8_0, Q6_K, F16 or F32",
+                e.type);
   return PB_OK;
 }
 
@@ -470,19 +510,50 @@ extern "C" int pb_model_load_gguf(pb_ctx* ctx, const pb_gguf* g, int seq_len, pb
       return pb_set_error(ctx, PB_ERR_ARG, "%s has ggml type %u; the device model takes Q4_0 weights and F32/F16 norms",
                           t.name.c_str(), t.type);
   }
-  if (head >= 0 && g->tensors[head].type != 2 && g->tensors[head].type != 8)
-    return pb_set_error(ctx, PB_ERR_ARG, "output.weight has ggml type %u; the head takes Q4_0 or Q8_0",
-                        g->tensors[head].type);
+  const uint32_t ht = head >= 0 ? g->tensors[head].type : 2;
+  if (head >= 0 && ht != 2 && ht != 8 && !table_as_f32(ht))
+    return pb_set_error(ctx, PB_ERR_ARG, "output.weight has ggml type %u; the head takes Q4_0, Q8_0, Q6_K, F16 or F32",
+                        ht);
+  const int64_t n_table = (int64_t)cfg.vocab * cfg.dim;
+  for (int ti : {found[0], head}) {
+    if (ti < 0) continue;
+    int64_t n = 1;
+    for (int64_t d : g->tensors[ti].dims) n *= d;
+    if (n != n_table)
+      return pb_set_error(ctx, PB_ERR_ARG, "%s holds %lld values; vocab x dim is %lld", g->tensors[ti].name.c_str(),
+                          (long long)n, (long long)n_table);
+  }
   pb_model* m = nullptr;
   PB_TRY(pb_model_create(ctx, &cfg, &m));
   int rc = PB_OK;
-  if (head >= 0) rc = pb_model_attach_head(m, g->tensors[head].type == 2 ? PB_TYPE_Q4_0 : PB_TYPE_Q8_0);
+  if (head >= 0) rc = pb_model_attach_head(m, ht == 2 ? PB_TYPE_Q4_0 : ht == 8 ? PB_TYPE_Q8_0 : PB_TYPE_F32);
   std::vector<char> buf;
   std::vector<float> f32;
+  // a table kept as f32: decoded on the device (pb_gguf_dequant, gguf.js:219-355)
+  auto dequant_table = [&](const TensorInfo& t) -> int {
+    void* raw_dev = nullptr;
+    float* out_dev = nullptr;
+    int r = PB_OK;
+    if (cudaMalloc(&raw_dev, t.bytes) != cudaSuccess || cudaMalloc(&out_dev, (size_t)n_table * 4) != cudaSuccess)
+      r = pb_set_error(ctx, PB_ERR_OOM, "decoding %s", t.name.c_str());
+    if (r == PB_OK) r = pb_upload(ctx, raw_dev, buf.data(), t.bytes);
+    if (r == PB_OK) r = pb_gguf_dequant(ctx, (int)t.type, raw_dev, n_table, out_dev);
+    if (r == PB_OK) {
+      f32.resize((size_t)n_table);
+      r = pb_download(ctx, f32.data(), out_dev, (size_t)n_table * 4);
+    }
+    cudaFree(raw_dev);
+    cudaFree(out_dev);
+    return r;
+  };
   auto load = [&](int ti, int layer, int w) -> int {
     const TensorInfo& t = g->tensors[ti];
     buf.resize(t.bytes);
     if (pb_gguf_tensor_read(g, ti, buf.data(), t.bytes)) return pb_set_error(ctx, PB_ERR_ARG, "%s", g_err.c_str());
+    if ((w == 0 || w == 11) && table_as_f32(t.type)) {
+      if (int r = dequant_table(t)) return r;
+      return pb_model_set_tensor(m, layer, w, f32.data(), f32.size() * 4);
+    }
     if (w >= 8 && w <= 10 && t.type == 1) {  // F16 norm gains -> f32
       f32.resize(t.bytes / 2);
       f16_to_f32(reinterpret_cast<const uint16_t*>(buf.data()), f32.data(), f32.size());

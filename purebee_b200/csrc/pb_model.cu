@@ -18,6 +18,7 @@
 
 // from pb_ops.cu / pb_q4.cu
 void pb_rope_table(double theta, int hd, int start, int n, double2* out);
+void pb_rope_table_freqs(const double* freqs, int hd, int start, int n, double2* out);
 int pb_launch_attn_cached(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
                           int start_pos, const int* pos_dev, int n_heads, int n_kv, int hd, float* out, int max_len,
                           int nseq, pb_seq_geo geo);
@@ -60,12 +61,17 @@ struct pb_model {
   // llama.js weights
   float* emb_f32 = nullptr;               // tiles [V/32][dim][32]
   pb_qmat emb_f32_view;                   // head view of emb_f32
+  // a streaming model's dequantized tables (a GGUF embedding or output.weight
+  // of a type kept as f32, e.g. Q6_K, F16): emb_f32 above, and an untied head
+  float* head_f32 = nullptr;              // tiles [V/32][dim][32]
+  pb_qmat head_f32_view;
   std::vector<float*> q8s;                // scales per (layer, which 1..7)
   std::vector<int8_t*> q8q;
   // norms and cache
   float *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr;
   float *kc = nullptr, *vc = nullptr;
   double2* rope_tab = nullptr;
+  double rope_scaling[4] = {0, 0, 0, 0};  // factor, low, high, original context (factor 0: off)
   // activations (sized for max_m rows)
   int max_m = 0;
   float *x = nullptr, *xn = nullptr, *qkvo = nullptr, *att = nullptr, *guo = nullptr, *hb = nullptr, *proj = nullptr,
@@ -174,6 +180,7 @@ extern "C" int pb_model_free(pb_model* m) {
   for (auto* p : m->q8s) cudaFree(p);
   for (auto* p : m->q8q) cudaFree(p);
   cudaFree(m->emb_f32);
+  cudaFree(m->head_f32);
   cudaFree(m->rms_att); cudaFree(m->rms_ffn); cudaFree(m->rms_final);
   cudaFree(m->kc); cudaFree(m->vc); cudaFree(m->rope_tab);
   cudaFree(m->x); cudaFree(m->xn); cudaFree(m->qkvo); cudaFree(m->att); cudaFree(m->guo); cudaFree(m->hb);
@@ -190,6 +197,24 @@ __global__ void k_fill(float* p, int64_t n, float v) {
   if (i < n) p[i] = v;
 }
 
+// An f32 table [V][dim] stored as tiles [V/32][dim][32] (lanes = rows), with
+// the head view the head kernels take.
+static int alloc_f32_table(pb_model* m, float** tab, pb_qmat* view) {
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  const size_t ntile = (size_t)((c.vocab + 31) / 32) * 32;
+  if (cudaMalloc(tab, ntile * c.dim * 4) != cudaSuccess) return pb_set_error(ctx, PB_ERR_OOM, "f32 table");
+  cudaMemsetAsync(*tab, 0, ntile * c.dim * 4, ctx->stream);
+  *view = pb_qmat();
+  view->type = PB_TYPE_F32;
+  view->N = c.vocab;
+  view->K = c.dim;
+  view->N_pad = (int)ntile;
+  view->nb = c.dim / 32;
+  view->qs = (uint8_t*)*tab;
+  return PB_OK;
+}
+
 extern "C" int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model** out) {
   if (!ctx || !cfg || !out) return PB_ERR_ARG;
   *out = nullptr;
@@ -200,8 +225,9 @@ extern "C" int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model
     return pb_set_error(ctx, PB_ERR_ARG, "invalid model config");
   if (c.kind != PB_MODEL_STREAMING_Q4 && c.kind != PB_MODEL_LLAMA_Q8A)
     return pb_set_error(ctx, PB_ERR_ARG, "unknown model kind %d", c.kind);
-  if (c.kind == PB_MODEL_STREAMING_Q4 && c.emb_type != PB_TYPE_Q4_0 && c.emb_type != PB_TYPE_Q8_0)
-    return pb_set_error(ctx, PB_ERR_ARG, "streaming models take a Q4_0 or Q8_0 embedding");
+  if (c.kind == PB_MODEL_STREAMING_Q4 && c.emb_type != PB_TYPE_Q4_0 && c.emb_type != PB_TYPE_Q8_0 &&
+      c.emb_type != PB_TYPE_F32)
+    return pb_set_error(ctx, PB_ERR_ARG, "streaming models take a Q4_0, Q8_0 or f32 (dequantized) embedding");
   if (c.kind == PB_MODEL_LLAMA_Q8A && c.emb_type != PB_TYPE_F32)
     return pb_set_error(ctx, PB_ERR_ARG, "llama.js models take an f32 embedding");
   pb_model* m = new pb_model();
@@ -212,8 +238,12 @@ extern "C" int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model
   auto fail = [&](int code) { pb_model_free(m); return code; };
   const int L = c.n_layers;
   if (c.kind == PB_MODEL_STREAMING_Q4) {
-    rc = pb_qmat_alloc(ctx, c.emb_type, PB_LAYOUT_TILED8, c.vocab, c.dim, &m->emb);
-    if (rc) return fail(rc);
+    if (c.emb_type == PB_TYPE_F32) {
+      if ((rc = alloc_f32_table(m, &m->emb_f32, &m->emb_f32_view))) return fail(rc);
+    } else {
+      rc = pb_qmat_alloc(ctx, c.emb_type, PB_LAYOUT_TILED8, c.vocab, c.dim, &m->emb);
+      if (rc) return fail(rc);
+    }
     m->qkv.assign(L, nullptr); m->wo.assign(L, nullptr); m->gu.assign(L, nullptr); m->w2.assign(L, nullptr);
     for (int l = 0; l < L; ++l) {
       if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, PB_LAYOUT_ROWS, c.dim + 2 * m->kv_dim, c.dim, &m->qkv[l]))) return fail(rc);
@@ -222,15 +252,7 @@ extern "C" int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model
       if ((rc = pb_qmat_alloc(ctx, PB_TYPE_Q4_0, PB_LAYOUT_ROWS, c.dim, c.hidden_dim, &m->w2[l]))) return fail(rc);
     }
   } else {
-    size_t ntile = (size_t)((c.vocab + 31) / 32) * 32;
-    if (cudaMalloc(&m->emb_f32, ntile * c.dim * 4) != cudaSuccess) return fail(pb_set_error(ctx, PB_ERR_OOM, "embedding"));
-    cudaMemsetAsync(m->emb_f32, 0, ntile * c.dim * 4, ctx->stream);
-    m->emb_f32_view.type = PB_TYPE_F32;
-    m->emb_f32_view.N = c.vocab;
-    m->emb_f32_view.K = c.dim;
-    m->emb_f32_view.N_pad = (int)ntile;
-    m->emb_f32_view.nb = c.dim / 32;
-    m->emb_f32_view.qs = (uint8_t*)m->emb_f32;
+    if ((rc = alloc_f32_table(m, &m->emb_f32, &m->emb_f32_view))) return fail(rc);
     m->q8s.assign((size_t)L * 7, nullptr);
     m->q8q.assign((size_t)L * 7, nullptr);
     for (int l = 0; l < L; ++l)
@@ -352,7 +374,7 @@ extern "C" int pb_model_init_synthetic(pb_model* m, uint64_t seed, double stdev)
   auto gen = [&](uint64_t tid, int64_t n) { return pb_synth_weights(ctx, tmp, n, seed, tid, stdev); };
   // embedding (tensor id 0)
   if ((rc = gen(0, ne))) goto done;
-  if (c.kind == PB_MODEL_STREAMING_Q4) {
+  if (c.kind == PB_MODEL_STREAMING_Q4 && c.emb_type != PB_TYPE_F32) {
     if ((rc = pb_gguf_quantize(ctx, c.emb_type, tmp, ne, gg))) goto done;
     if ((rc = pack_rows(m, m->emb, gg, c.vocab, 0, 0))) goto done;
   } else {
@@ -382,29 +404,54 @@ done:
   return rc;
 }
 
-// The LM head table: output.weight when the file has one, else the tied
-// embedding (llama-streaming.js:616-679, streaming-loader.js sharedWeights).
-static pb_qmat* head_of(const pb_model* m) { return m->head ? m->head : m->emb; }
+// The quantized LM head table: output.weight when the file has one, else the
+// tied embedding (llama-streaming.js:616-679, streaming-loader.js
+// sharedWeights); nullptr when the head is an f32 table.
+static pb_qmat* head_of(const pb_model* m) {
+  if (m->head) return m->head;
+  return m->head_f32 ? nullptr : m->emb;
+}
+
+// The head table and the head kernel's arithmetic: batch_dot order with the
+// exact dequant over Q4_0 / Q8_0 tiles (mode 0), batch_dot order over a
+// dequantized f32 table (mode 2: what the reference keeps for every other
+// GGUF type, streaming-loader.js:324-335, e.g. Q6_K or F16), or llama.js's
+// double-precision dot over its f32 embedding (mode 1).
+static const pb_qmat* head_table(const pb_model* m, int* mode) {
+  if (m->c.kind == PB_MODEL_LLAMA_Q8A) { *mode = 1; return &m->emb_f32_view; }
+  if (m->head) { *mode = 0; return m->head; }
+  if (m->head_f32) { *mode = 2; return &m->head_f32_view; }
+  if (m->emb) { *mode = 0; return m->emb; }
+  *mode = 2;
+  return &m->emb_f32_view;
+}
 
 // Give a streaming model an untied LM head (GGUF output.weight) of `type`
-// (Q4_0 / Q8_0), set afterwards as tensor 11.
+// (Q4_0 / Q8_0 kept quantized, or PB_TYPE_F32 for a dequantized table), set
+// afterwards as tensor 11.
 extern "C" int pb_model_attach_head(pb_model* m, int type) {
   if (!m) return PB_ERR_ARG;
-  if (m->c.kind != PB_MODEL_STREAMING_Q4 || (type != PB_TYPE_Q4_0 && type != PB_TYPE_Q8_0))
-    return pb_set_error(m->ctx, PB_ERR_ARG, "an untied head needs a streaming model and a Q4_0 or Q8_0 table");
+  if (m->c.kind != PB_MODEL_STREAMING_Q4 || (type != PB_TYPE_Q4_0 && type != PB_TYPE_Q8_0 && type != PB_TYPE_F32))
+    return pb_set_error(m->ctx, PB_ERR_ARG, "an untied head needs a streaming model and a Q4_0, Q8_0 or f32 table");
   free_graph(m);
   pb_qmat_free(m->ctx, m->head);
   m->head = nullptr;
+  cudaFree(m->head_f32);
+  m->head_f32 = nullptr;
+  if (type == PB_TYPE_F32) return alloc_f32_table(m, &m->head_f32, &m->head_f32_view);
   return pb_qmat_alloc(m->ctx, type, PB_LAYOUT_TILED8, m->c.vocab, m->c.dim, &m->head);
 }
 
 static size_t tensor_bytes(const pb_model* m, int which) {
   const pb_model_config& c = m->c;
-  if (which == 11) return m->head ? (size_t)((int64_t)c.vocab * c.dim / 32) * (m->head->type == PB_TYPE_Q4_0 ? 18 : 34) : 0;
+  if (which == 11) {
+    if (m->head_f32) return (size_t)c.vocab * c.dim * 4;
+    return m->head ? (size_t)((int64_t)c.vocab * c.dim / 32) * (m->head->type == PB_TYPE_Q4_0 ? 18 : 34) : 0;
+  }
   if (which >= 8) return (size_t)c.dim * 4;
   if (which == 0) {
     int64_t ne = (int64_t)c.vocab * c.dim;
-    if (c.kind == PB_MODEL_LLAMA_Q8A) return (size_t)ne * 4;
+    if (c.kind == PB_MODEL_LLAMA_Q8A || c.emb_type == PB_TYPE_F32) return (size_t)ne * 4;
     return (size_t)(ne / 32) * (c.emb_type == PB_TYPE_Q4_0 ? 18 : 34);
   }
   int r, k;
@@ -420,7 +467,8 @@ static int model_tensor_io(pb_model* m, int layer, int which, void* host, size_t
   const pb_model_config& c = m->c;
   if (which < 0 || which > 11 || (which >= 1 && which <= 9 && (layer < 0 || layer >= c.n_layers)))
     return pb_set_error(ctx, PB_ERR_ARG, "bad tensor (layer %d, which %d)", layer, which);
-  if (which == 11 && !m->head) return pb_set_error(ctx, PB_ERR_ARG, "the model has no untied head (pb_model_attach_head)");
+  if (which == 11 && !m->head && !m->head_f32)
+    return pb_set_error(ctx, PB_ERR_ARG, "the model has no untied head (pb_model_attach_head)");
   size_t need = tensor_bytes(m, which);
   if (bytes != need) return pb_set_error(ctx, PB_ERR_ARG, "tensor %d needs %zu bytes, got %zu", which, need, bytes);
   if (!get) free_graph(m);
@@ -441,10 +489,12 @@ static int model_tensor_io(pb_model* m, int layer, int which, void* host, size_t
     return pb_upload(ctx, q, (const char*)host + nb * 4, nb * 32);
   }
   PB_TRY(pb_ensure_scratch(ctx, bytes));
-  if (c.kind == PB_MODEL_LLAMA_Q8A) {  // f32 embedding
+  float* f32_tab = which == 11 ? m->head_f32 : (which == 0 && (c.kind == PB_MODEL_LLAMA_Q8A || c.emb_type == PB_TYPE_F32))
+                                                  ? m->emb_f32 : nullptr;
+  if (f32_tab) {  // f32 table, stored as tiles
     int64_t ne = (int64_t)c.vocab * c.dim;
     if (!get) PB_TRY_CUDA(ctx, cudaMemcpyAsync(ctx->scratch, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
-    k_tile_f32<<<pb_cdiv(ne, 256), 256, 0, ctx->stream>>>((float*)ctx->scratch, c.vocab, c.dim, m->emb_f32, get);
+    k_tile_f32<<<pb_cdiv(ne, 256), 256, 0, ctx->stream>>>((float*)ctx->scratch, c.vocab, c.dim, f32_tab, get);
     PB_LAUNCHED(ctx, "k_tile_f32");
     if (get) PB_TRY_CUDA(ctx, cudaMemcpyAsync(host, ctx->scratch, bytes, cudaMemcpyDeviceToHost, ctx->stream));
     return pb_wait(ctx);
@@ -627,7 +677,7 @@ static int launch_embed(pb_model* m, const int* toks, int M) {
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
   dim3 grid(pb_cdiv(c.dim, 256), M);
-  if (c.kind == PB_MODEL_STREAMING_Q4)
+  if (m->emb)
     k_embed<<<grid, 256, 0, ctx->stream>>>(c.emb_type, m->emb->qs, m->emb->d, nullptr, c.vocab, c.dim, toks, nullptr,
                                            nullptr, nullptr, m->x, ctx->d_err);
   else
@@ -640,10 +690,9 @@ static int launch_embed(pb_model* m, const int* toks, int M) {
 // Final RMSNorm (fused into the head kernel) and the LM head with the greedy
 // argmax (llama-streaming.js:616-642, :899-909; llama.js:340-367).
 static int launch_head(pb_model* m, const float* last_x) {
-  pb_ctx* ctx = m->ctx;
-  if (m->c.kind == PB_MODEL_STREAMING_Q4)
-    return pb_launch_head_norm(ctx, head_of(m), last_x, m->rms_final, m->c.eps, m->logits, m->key, 0);
-  return pb_launch_head_norm(ctx, &m->emb_f32_view, last_x, m->rms_final, m->c.eps, m->logits, m->key, 1);
+  int mode = 0;
+  const pb_qmat* t = head_table(m, &mode);
+  return pb_launch_head_norm(m->ctx, t, last_x, m->rms_final, m->c.eps, m->logits, m->key, mode);
 }
 
 // Enqueue one decode step that reads token and position from m->tok_dev.
@@ -1000,6 +1049,43 @@ extern "C" int pb_model_rollback_cache(pb_model* m, int pos) {
   return pb_wait(ctx);
 }
 
+// Llama-3 RoPE frequency scaling (pb_rope_freqs) on the model's rotation
+// table; factor <= 0 restores the reference's unscaled table.  The table is
+// rebuilt in place, so recorded decode graphs pick it up.
+extern "C" int pb_rope_freqs(double theta, int hd, double factor, double low_freq_factor, double high_freq_factor,
+                             int original_max_pos, double* freqs_out);
+extern "C" int pb_model_set_rope_scaling(pb_model* m, double factor, double low_freq_factor, double high_freq_factor,
+                                         int original_max_pos) {
+  if (!m) return PB_ERR_ARG;
+  pb_ctx* ctx = m->ctx;
+  const pb_model_config& c = m->c;
+  std::vector<double> freqs((size_t)c.head_dim / 2);
+  if (pb_rope_freqs(c.rope_theta, c.head_dim, factor, low_freq_factor, high_freq_factor, original_max_pos,
+                    freqs.data()) != PB_OK)
+    return pb_set_error(ctx, PB_ERR_ARG,
+                        "RoPE scaling needs factor > 0, 0 < low_freq_factor < high_freq_factor and "
+                        "original_max_pos > 0 (or factor <= 0 to turn it off)");
+  std::vector<double2> tab((size_t)c.seq_len * (c.head_dim / 2));
+  pb_rope_table_freqs(freqs.data(), c.head_dim, 0, c.seq_len, tab.data());
+  PB_TRY(pb_wait(ctx));  // no replay may read the table while it changes
+  PB_TRY_CUDA(ctx, cudaMemcpy(m->rope_tab, tab.data(), tab.size() * sizeof(double2), cudaMemcpyHostToDevice));
+  if (factor > 0) {
+    m->rope_scaling[0] = factor;
+    m->rope_scaling[1] = low_freq_factor;
+    m->rope_scaling[2] = high_freq_factor;
+    m->rope_scaling[3] = original_max_pos;
+  } else {
+    m->rope_scaling[0] = m->rope_scaling[1] = m->rope_scaling[2] = m->rope_scaling[3] = 0;
+  }
+  return PB_OK;
+}
+
+extern "C" int pb_model_rope_scaling(const pb_model* m, double* factor_out) {
+  if (!m || !factor_out) return PB_ERR_ARG;
+  *factor_out = m->rope_scaling[0];
+  return PB_OK;
+}
+
 extern "C" int pb_model_kv(pb_model* m, int layer, int which_v, float* host, size_t floats) {
   if (!m || !host || layer < 0 || layer >= m->c.n_layers) return PB_ERR_ARG;
   size_t n = (size_t)m->c.seq_len * m->kv_dim;
@@ -1019,8 +1105,9 @@ extern "C" int64_t pb_model_decode_bytes(const pb_model* m, int pos) {
   }
   w *= c.n_layers;
   int64_t ne = (int64_t)c.vocab * c.dim;
-  const int ht = m->head ? m->head->type : c.emb_type;
-  int64_t head = c.kind == PB_MODEL_LLAMA_Q8A ? ne * 4 : ne / 32 * (ht == PB_TYPE_Q4_0 ? 18 : 34);
+  int mode = 0;
+  const int ht = head_table(m, &mode)->type;
+  int64_t head = ht == PB_TYPE_F32 ? ne * 4 : ne / 32 * (ht == PB_TYPE_Q4_0 ? 18 : 34);
   int64_t kvb = (int64_t)2 * c.n_layers * (pos + 1) * m->kv_dim * 4;
   return w + head + kvb;
 }
@@ -1426,7 +1513,8 @@ static int batch_create(pb_model* m, int n_seqs, int world, pb_comm* comm, pb_ba
   // decode steps run the fused-dequant GEMM, which needs no growable scratch
   // (the recorded decode graph relies on that)
   if (n_seqs > 256) return pb_set_error(ctx, PB_ERR_ARG, "at most 256 sequences per batch");
-  if (c.kind != PB_MODEL_STREAMING_Q4 || !m->emb || m->emb->type != PB_TYPE_Q4_0 || head_of(m)->type != PB_TYPE_Q4_0)
+  if (c.kind != PB_MODEL_STREAMING_Q4 || !m->emb || m->emb->type != PB_TYPE_Q4_0 || !head_of(m) ||
+      head_of(m)->type != PB_TYPE_Q4_0)
     return pb_set_error(ctx, PB_ERR_ARG, "batched serving needs a streaming model with a Q4_0 embedding and head");
   if (!pb_attn_decode_group_ok(c.n_heads / world, c.n_kv_heads / world, c.head_dim, c.seq_len))
     return pb_set_error(ctx, PB_ERR_ARG, "batched decode attention needs <= 8 query heads per kv head, head_dim %% 4 "

@@ -278,6 +278,8 @@ __global__ void k_attn_pv_generic(const float* __restrict__ W, const float* __re
 extern "C" int pb_attention(pb_ctx* ctx, const float* Q, const float* K, const float* V, int seqQ, int seqK, int dK,
                             int dV, int causal, float* out) {
   if (!ctx || !Q || !K || !V || !out || seqQ <= 0 || seqK <= 0 || dK <= 0 || dV <= 0) return PB_ERR_ARG;
+  // one CTA row per query: grid.y is limited to 65535
+  if (seqQ > 65535) return pb_set_error(ctx, PB_ERR_ARG, "seqQ = %d exceeds 65535", seqQ);
   size_t sb = (size_t)seqQ * seqK * 4;
   PB_TRY(pb_ensure_scratch(ctx, 2 * sb + 256));
   float* S = (float*)ctx->scratch;
@@ -321,6 +323,7 @@ extern "C" int pb_attention_noalloc(pb_ctx* ctx, const float* Q, const float* K,
                                     int dK, int dV, int causal, float* out) {
   if (!ctx || !Q || !K || !V || !out || seqQ <= 0 || seqK <= 0 || dK <= 0 || dV <= 0) return PB_ERR_ARG;
   if (!ctx->noalloc_attn) return pb_set_error(ctx, PB_ERR_STATE, "no-alloc scratch not set up");
+  if (seqQ > 65535) return pb_set_error(ctx, PB_ERR_ARG, "seqQ = %d exceeds 65535", seqQ);
   const size_t sb = (size_t)seqQ * seqK * 4, sb_al = (sb + 255) & ~(size_t)255;
   if (2 * sb_al > PB_NOALLOC_ATTN_BYTES)
     return pb_set_error(ctx, PB_ERR_ARG, "seqQ*seqK = %lld needs %zu bytes of scratch; the fixed array holds %u",
@@ -370,6 +373,53 @@ void pb_rope_table(double theta, int hd, int start, int n, double2* out) {
       out[(size_t)p * half + i / 2] = make_double2(cos(angle), sin(angle));
     }
   }
+}
+
+// Llama-3 RoPE frequency scaling, as Meta published it with Llama 3.1 / 3.2
+// (the `rope_freqs` factors a GGUF file may carry).  For a pair frequency f
+// with wavelength w = 2 pi / f, against the pre-training context C:
+//   w < C / high_freq_factor   -> f            (high frequencies kept)
+//   w > C / low_freq_factor    -> f / factor   (low frequencies stretched)
+//   otherwise, with s = (C / w - low_freq_factor) / (high_freq_factor - low_freq_factor),
+//                               -> (1 - s) f / factor + s f.
+// The reference never applies it: llama-streaming.js:316-336 uses
+// 1 / theta^(i / hd) as is, and gguf.js:378-410 never maps rope_freqs.weight.
+// So it is off unless a caller turns it on, and off in every parity check.
+extern "C" int pb_rope_freqs(double theta, int hd, double factor, double low_freq_factor, double high_freq_factor,
+                             int original_max_pos, double* freqs_out) {
+  if (hd <= 0 || (hd & 1) || !freqs_out || !(theta > 0)) return PB_ERR_ARG;
+  const bool on = factor > 0;
+  if (on && (!(low_freq_factor > 0) || !(high_freq_factor > low_freq_factor) || original_max_pos <= 0))
+    return PB_ERR_ARG;
+  const double two_pi = 6.283185307179586;
+  const double ctx_len = (double)original_max_pos;
+  for (int i = 0; i < hd; i += 2) {
+    const double f = 1.0 / pow(theta, (double)i / hd);
+    double g = f;
+    if (on) {
+      const double wavelen = two_pi / f;
+      if (wavelen < ctx_len / high_freq_factor) {
+        g = f;
+      } else if (wavelen > ctx_len / low_freq_factor) {
+        g = f / factor;
+      } else {
+        const double s = (ctx_len / wavelen - low_freq_factor) / (high_freq_factor - low_freq_factor);
+        g = (1.0 - s) * f / factor + s * f;
+      }
+    }
+    freqs_out[i / 2] = g;
+  }
+  return PB_OK;
+}
+
+// The rotation table for given pair frequencies (freqs[hd / 2]).
+void pb_rope_table_freqs(const double* freqs, int hd, int start, int n, double2* out) {
+  const int half = hd / 2;
+  for (int j = 0; j < half; ++j)
+    for (int p = 0; p < n; ++p) {
+      const double angle = (double)(start + p) * freqs[j];
+      out[(size_t)p * half + j] = make_double2(cos(angle), sin(angle));
+    }
 }
 
 extern "C" int pb_rope(pb_ctx* ctx, float* q, float* k, int seq, int start_pos, int n_heads, int n_kv, int hd,

@@ -937,6 +937,52 @@ k_head_f32_double(const float* __restrict__ E, int N, int D, const float* __rest
   }
 }
 
+// batch_dot (wasm-q4.js:467-549) over an f32 table stored as tiles
+// [V/32][D][32]: lanes = rows, acc[k % 4] += h[k] * E[v, k] with a separate
+// multiply and add, k ascending, then (acc1 + acc3) + (acc0 + acc2).  This is
+// the head of a streaming model whose table the reference dequantizes to f32
+// (streaming-loader.js:324-335) from a type the device keeps as f32 (Q6_K,
+// F16, F32).
+__global__ void __launch_bounds__(HD_WARPS * 32)
+k_head_f32_bd(const float* __restrict__ E, int N, int D, const float* __restrict__ h,
+              const float* __restrict__ norm_w, double eps, float* __restrict__ logits,
+              unsigned long long* __restrict__ amax) {
+  extern __shared__ __align__(16) float hs[];
+  pb_pdl_trigger();
+  pb_pdl_wait();
+  load_hidden(h, norm_w, eps, D, hs);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tile = blockIdx.x * HD_WARPS + warp;
+  const int row = tile * 32 + lane;
+  const int ntiles = (N + 31) >> 5;
+  float result = 0.0f;
+  if (tile < ntiles) {
+    const float* tp = E + (size_t)tile * D * 32 + lane;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int d = 0; d < D; d += 8) {  // D % 32 == 0
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldcs(tp + (size_t)(d + u) * 32);
+#pragma unroll
+      for (int u = 0; u < 8; u += 4) {
+        const float4 hv = *reinterpret_cast<const float4*>(hs + d + u);
+        head_acc(a0, a1, a2, a3, hv, make_float2(v[u], v[u + 1]), make_float2(v[u + 2], v[u + 3]));
+      }
+    }
+    result = __fadd_rn(__fadd_rn(a1, a3), __fadd_rn(a0, a2));
+    if (row < N) logits[row] = result;
+  }
+  if (amax) {
+    unsigned long long key = (tile < ntiles && row < N) ? pb_argmax_key(result, row) : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
+      key = t > key ? t : key;
+    }
+    if (lane == 0 && key) atomicMax(amax, key);
+  }
+}
+
 // wasm-q4.js:798-839 lmHead over a row-major f32 table (one-shot host API).
 __global__ void k_head_f32_rowmajor(const float* __restrict__ E, int N, int D, const float* __restrict__ h,
                                     float* __restrict__ logits) {
@@ -960,7 +1006,8 @@ __global__ void k_argmax_finish(const unsigned long long* key, int* idx) {
   if (threadIdx.x == 0 && blockIdx.x == 0) *idx = pb_argmax_index(*key);
 }
 
-// mode: 0 = batch_dot order over Q4_0/Q8_0 tiles; 1 = double order over f32 tiles
+// mode: 0 = batch_dot order over Q4_0/Q8_0 tiles; 1 = double order over f32
+// tiles (llama.js); 2 = batch_dot order over f32 tiles
 int pb_launch_head(pb_ctx* ctx, const pb_qmat* emb, const float* h, float* logits, unsigned long long* amax, int mode) {
   return pb_launch_head_norm(ctx, emb, h, nullptr, 0.0, logits, amax, mode);
 }
@@ -975,6 +1022,11 @@ int pb_launch_head_norm(pb_ctx* ctx, const pb_qmat* emb, const float* h, const f
   if (mode == 1) {
     k_head_f32_double<<<grid, HD_WARPS * 32, smem, ctx->stream>>>((const float*)emb->qs, emb->N, emb->K, h, norm_w, eps,
                                                                    logits, amax);
+  } else if (mode == 2) {
+    if (emb->type != PB_TYPE_F32 || (emb->K & 31))
+      return pb_set_error(ctx, PB_ERR_ARG, "f32 head table: type F32 and dim a multiple of 32");
+    return pb_launch(ctx, "k_head_f32_bd", true, k_head_f32_bd, dim3(grid), dim3(HD_WARPS * 32), smem,
+                     (const float*)emb->qs, emb->N, emb->K, h, norm_w, eps, logits, amax);
   } else if (emb->type == PB_TYPE_Q4_0 || emb->type == PB_TYPE_Q8_0) {
     if (emb->layout != PB_LAYOUT_TILED8)
       return pb_set_error(ctx, PB_ERR_ARG, "head table must be uploaded with PB_QMAT_TABLE");

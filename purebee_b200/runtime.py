@@ -77,12 +77,14 @@ class _DeviceModel:
         if which == 11:
             if self.head_type is None:
                 raise ValueError("the model has no untied head")
+            if self.head_type == N.TYPE_F32:
+                return c.vocabSize * c.dim * 4
             return c.vocabSize * c.dim // 32 * (18 if self.head_type == N.TYPE_Q4_0 else 34)
         if which >= 8:
             return c.dim * 4
         if which == 0:
             ne = c.vocabSize * c.dim
-            if self.kind == N.MODEL_LLAMA_Q8A:
+            if self.kind == N.MODEL_LLAMA_Q8A or self.emb_type == N.TYPE_F32:
                 return ne * 4
             return ne // 32 * (18 if self.emb_type == N.TYPE_Q4_0 else 34)
         kv = c.nKvHeads * c.headDim
@@ -167,6 +169,19 @@ class _DeviceModel:
 
     def rollback_cache(self, pos: int):
         self.ctx._check(N.lib().pb_model_rollback_cache(self.h, int(pos)))
+
+    def set_rope_scaling(self, factor: float, low_freq_factor: float = 1.0, high_freq_factor: float = 4.0,
+                         original_max_pos: int = 8192):
+        """Llama-3 RoPE frequency scaling on (factor > 0) or off (factor <= 0,
+        the default and the reference's behaviour)."""
+        self.ctx._check(N.lib().pb_model_set_rope_scaling(self.h, float(factor), float(low_freq_factor),
+                                                          float(high_freq_factor), int(original_max_pos)))
+
+    @property
+    def rope_scaling_factor(self) -> float:
+        f = ctypes.c_double()
+        self.ctx._check(N.lib().pb_model_rope_scaling(self.h, ctypes.byref(f)))
+        return f.value
 
     def kv(self, layer: int, which_v: int) -> np.ndarray:
         c = self.cfg
@@ -342,7 +357,8 @@ class _RuntimeBase:
 
 class StreamingLlamaRuntime(_RuntimeBase):
     """llama-streaming.js StreamingLlamaRuntime over GGUF Q4_0 layer weights and
-    a Q4_0 or Q8_0 tied embedding (emb_type)."""
+    a Q4_0 or Q8_0 tied embedding (emb_type), or an f32 one (TYPE_F32: the
+    dequantized table of a Q6_K / F16 / F32 token_embd.weight)."""
     KIND = N.MODEL_STREAMING_Q4
 
     @classmethod
@@ -368,7 +384,9 @@ class StreamingLlamaRuntime(_RuntimeBase):
         rt = cls.__new__(cls)
         rt.config = cfg
         rt.ctx = ctx
-        head_type = None if head is None else (N.TYPE_Q4_0 if head["type"] == 2 else N.TYPE_Q8_0)
+        # Q4_0 / Q8_0 tables stay quantized; any other type is held as a
+        # dequantized f32 table (streaming-loader.js:324-335)
+        head_type = None if head is None else {2: N.TYPE_Q4_0, 8: N.TYPE_Q8_0}.get(head["type"], N.TYPE_F32)
         rt.model = _DeviceModel(ctx, cfg, cls.KIND, extra["embType"], handle=h.value, head_type=head_type)
         rt._loaded = True
         rt._layersUsed = 0

@@ -149,13 +149,24 @@ def test_malformed_files_raise(tmp_path, gg):
     open(p, "wb").write(raw)
     with pytest.raises(gg.GGUFError, match="metadata value"):
         gg.GGUFFile(p)
-    # config needs the llama keys and a Q4_0/Q8_0 embedding
+    # a string array claiming more elements than the rest of the file can
+    # encode (8 bytes per string at least): rejected before any element is
+    # allocated
+    raw = (struct.pack("<IIQQ", 0x46554747, 3, 0, 1) + struct.pack("<Q", 1) + b"k"
+           + struct.pack("<IIQ", 9, 8, 1 << 20) + bytes(1 << 20))
+    open(p, "wb").write(raw)
+    with pytest.raises(gg.GGUFError, match="metadata array"):
+        gg.GGUFFile(p)
+    # config needs the llama keys and an embedding type the device model takes
     W.write_gguf(p, [("general.architecture", W.STRING, "llama")], t)
     with gg.GGUFFile(p) as f, pytest.raises(gg.GGUFError, match="embedding_length"):
         f.config()
-    W.write_gguf(p, md, [("token_embd.weight", [256, 40], 14, bytes(40 * 210))])
-    with gg.GGUFFile(p) as f, pytest.raises(gg.GGUFError, match="Q4_0 or Q8_0"):
+    W.write_gguf(p, md, [("token_embd.weight", [256, 40], 12, bytes(40 * 144))])  # Q4_K: not decoded
+    with gg.GGUFFile(p) as f, pytest.raises(gg.GGUFError, match="Q4_0, Q8_0, Q6_K"):
         f.config()
+    W.write_gguf(p, md, [("token_embd.weight", [256, 40], 14, bytes(40 * 210))])  # Q6_K: a dequantized f32 table
+    with gg.GGUFFile(p) as f:
+        assert f.config()[1]["embType"] == 0
     W.write_gguf(p, md, [("output_norm.weight", [64], 0, bytes(256))])
     with gg.GGUFFile(p) as f, pytest.raises(gg.GGUFError, match="token_embd"):
         f.config()

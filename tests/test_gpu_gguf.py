@@ -92,6 +92,60 @@ def test_gguf_untied_head(native, ctx, oracle, tmp_path):
     rt.shutdown()
 
 
+def _q6k_raw(rng, n):
+    raw = rng.integers(0, 256, n // 256 * 210, dtype=np.uint8)
+    d = (np.abs(rng.standard_normal(n // 256)) * 2e-4 + 1e-4).astype(np.float16)
+    raw.reshape(-1, 210)[:, 208:210] = d.view(np.uint8).reshape(-1, 2)
+    return raw
+
+
+@pytest.mark.parametrize("untied", [False, True])
+def test_gguf_q6_k_tables(native, ctx, oracle, tmp_path, untied):
+    """A Q6_K token_embd.weight (and a Q6_K output.weight when untied), the
+    type llama.cpp's quantizer commonly writes for these tables: the device
+    keeps them dequantized to f32, as streaming-loader.js:324-335 does, and
+    the head runs batch_dot over the f32 table.  Logits and greedy tokens
+    equal the oracle's, which holds the same dequantized tables."""
+    from purebee_b200.runtime import StreamingLlamaRuntime
+    rng = np.random.default_rng(7 + untied)
+    kw = dict(KW, emb_type=0)  # the oracle's f32 embedding (streaming kind)
+    om = oracle_model(oracle, dict(KW), 15)
+    n = kw["vocab"] * kw["dim"]
+    emb_q6 = _q6k_raw(rng, n)
+    emb_f32 = oracle.dequant_q6_k(emb_q6, n)
+    omf = oracle.Model(oracle.Config(**kw))
+    for l in range(kw["n_layers"]):
+        for w in range(1, 8):
+            omf.tensor(l, w)[:] = om.tensor(l, w)
+    omf.tensor(0, 0)[:] = emb_f32.view(np.uint8)
+    omf.refresh()
+    head = None
+    if untied:
+        head_q6 = _q6k_raw(rng, n)
+        omf.set_head(0, oracle.dequant_q6_k(head_q6, n).view(np.uint8))
+        head = (14, head_q6)
+    p = str(tmp_path / "q6.gguf")
+    t = write_model(p, om, KW, head=head)
+    t = [(nm, d, 14, emb_q6.tobytes()) if nm == "token_embd.weight" else (nm, d, ty, b) for nm, d, ty, b in t]
+    md = W.llama_metadata(kw["dim"], kw["hidden_dim"], kw["n_layers"], kw["n_heads"], kw["n_kv_heads"],
+                          kw["seq_len"], kw["vocab"], theta=kw["rope_theta"], eps=kw["eps"])
+    W.write_gguf(p, md, t)
+    rt = StreamingLlamaRuntime.fromGGUF(p, ctx=ctx)
+    assert rt.sharedWeights == (not untied)
+    # the device table is the decoded f32 table
+    assert np.array_equal(rt.getTensor(0, 0).view(np.float32), emb_f32)
+    prompt = oracle.synth_tokens(10, 21, 1, kw["vocab"]).tolist()
+    lg = rt.forward(prompt, 0)["logits"]
+    ref = omf.forward(prompt, 0)
+    assert np.max(np.abs(lg - ref)) <= 1e-5 * np.max(np.abs(ref))
+    rt.resetCache()
+    omf.reset_cache()
+    want = omf.generate(prompt, 24, eos_id=2)
+    got = rt.generate(prompt, 24, {"greedy": True, "eosId": 2})["tokens"]
+    assert got == want
+    rt.shutdown()
+
+
 def test_gguf_seq_len_override(native, ctx, oracle, tmp_path):
     from purebee_b200.runtime import StreamingLlamaRuntime
     om = oracle_model(oracle, KW, 13)

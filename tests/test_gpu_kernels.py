@@ -243,6 +243,24 @@ def test_gguf_encoders_and_decoders(native, ctx, oracle, golden):
     assert bits_equal(deq.download(count=64 * 32), oracle.dequant_q4_1(raw1, 64 * 32))
 
 
+def test_gguf_q6_k_decode(native, ctx, oracle):
+    """gguf.js:317-355 Q6_K on the device: bit for bit with the oracle,
+    including zero and subnormal scales and a partial last block."""
+    L = native.lib()
+    rng = np.random.default_rng(66)
+    nblk = 40
+    raw = rng.integers(0, 256, nblk * 210, dtype=np.uint8)
+    d = (rng.standard_normal(nblk) * 0.02).astype(np.float16)
+    d[3], d[4] = np.float16(0.0), np.float16(-6e-8)
+    raw.reshape(nblk, 210)[:, 208:210] = d.view(np.uint8).reshape(nblk, 2)
+    for n in (nblk * 256, nblk * 256 - 77):
+        r = dev(ctx, raw)
+        deq = out(ctx, n)
+        ctx._check(L.pb_gguf_dequant(ctx.h, 14, r.ptr, n, deq.ptr))
+        ctx.sync()
+        assert bits_equal(deq.download(count=n), oracle.dequant_q6_k(raw, n))
+
+
 def test_synth_device_equals_host(native, ctx, oracle):
     L = native.lib()
     n = 300001

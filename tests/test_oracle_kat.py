@@ -242,6 +242,66 @@ def test_gguf_q8_0_round_trip(oracle):
     assert np.all(np.abs(deq - x) <= 0.5 * d + 127 * 2.0 ** -11 * d + 1e-12)  # f16 rounding of d
 
 
+def q6k_block(ql, qh, sc, d_bits):
+    """One Q6_K block (gguf.js:317-355 layout): ql 128 B, qh 64 B, 16 int8 scales, f16 d."""
+    return np.concatenate([np.asarray(ql, np.uint8), np.asarray(qh, np.uint8), np.asarray(sc, np.int8).view(np.uint8),
+                           np.frombuffer(np.uint16(d_bits).tobytes(), np.uint8)])
+
+
+def py_dequant_q6_k(raw, n):
+    """Independent restatement of gguf.js:317-355 by element: value e of a
+    block is half h = e // 128, quarter t = (e % 128) // 32, l = e % 32; the
+    low four bits come from ql[64h + l + 32 (t & 1)] (t < 2: low nibble, else
+    high), the top two from qh[32h + l] >> 2t, the scale is sc[8h + l // 16 + 2t]."""
+    out = np.zeros(n, np.float32)
+    for e in range(n):
+        b, r = divmod(e, 256)
+        blk = raw[b * 210:(b + 1) * 210]
+        h, t, l = r // 128, (r % 128) // 32, r % 32
+        qlb = int(blk[64 * h + l + 32 * (t & 1)])
+        lo = qlb & 15 if t < 2 else qlb >> 4
+        q = (lo | (((int(blk[128 + 32 * h + l]) >> (2 * t)) & 3) << 4)) - 32
+        sc = int(np.int8(np.uint8(blk[192 + 8 * h + l // 16 + 2 * t])))
+        d = float(np.frombuffer(blk[208:210].tobytes(), np.float16)[0])
+        out[e] = f32(d * sc * q)
+    return out
+
+
+def test_q6_k_known_answers(oracle):
+    """gguf.js:317-355 on a hand-built block: d = 0.5, every scale = its
+    index + 1 (sign flipped for odd indices), chosen ql/qh bytes."""
+    ql = np.zeros(128, np.uint8)
+    qh = np.zeros(64, np.uint8)
+    ql[0] = 0x2F       # element 0: low nibble 15; element 64: high nibble 2
+    qh[0] = 0b11100100  # element 0 gets bits 00, element 32 bits 01, element 64 bits 10, element 96 bits 11
+    ql[32] = 0x71      # element 32: low nibble 1; element 96: high nibble 7
+    ql[64 + 17] = 0x0A  # second half, l = 17: element 128 + 17 low nibble 10
+    qh[32 + 17] = 0x03  # ... with top bits 11
+    sc = np.array([(i + 1) * (-1 if i % 2 else 1) for i in range(16)], np.int8)
+    raw = q6k_block(ql, qh, sc, 0x3800)  # d = 0.5
+    v = oracle.dequant_q6_k(raw, 256)
+    assert v[0] == 0.5 * 1 * (15 - 32)                   # is = 0, sc[0] = 1
+    assert v[32] == 0.5 * 3 * ((1 | (1 << 4)) - 32)      # sc[2] = 3
+    assert v[64] == 0.5 * 5 * ((2 | (2 << 4)) - 32)      # sc[4] = 5
+    assert v[96] == 0.5 * 7 * ((7 | (3 << 4)) - 32)      # sc[6] = 7
+    assert v[128 + 17] == 0.5 * (-10) * ((10 | (3 << 4)) - 32)  # half 1, l 17: is = 9, sc[9] = -10
+    assert v[1] == 0.5 * 1 * (0 - 32)                    # an all-zero element is -32 * d * sc
+    assert v[16] == 0.5 * (-2) * (0 - 32)                # l = 16 switches to sc[1]
+
+
+def test_q6_k_matches_python_restatement(oracle):
+    rng = np.random.default_rng(61)
+    nblk = 6
+    raw = rng.integers(0, 256, nblk * 210, dtype=np.uint8)
+    d = (rng.standard_normal(nblk) * 0.01).astype(np.float16)
+    d[1] = np.float16(0.0)
+    d[2] = np.float16(6e-8)  # subnormal
+    raw.reshape(nblk, 210)[:, 208:210] = d.view(np.uint8).reshape(nblk, 2)
+    n = nblk * 256 - 100  # a partial last block, as gguf.js allows
+    got = oracle.dequant_q6_k(raw, n)
+    assert np.array_equal(got.view(np.uint32), py_dequant_q6_k(raw, n).view(np.uint32))
+
+
 def test_synth_deterministic_and_normal(oracle):
     a = oracle.synth_weights(100000, 42, 3, 0.02)
     b = oracle.synth_weights(100000, 42, 3, 0.02)

@@ -51,7 +51,18 @@ def test_noalloc_attention_rejects_oversize(native, ctx):
     assert rc == native.PB_ERR_ARG
     assert b"fixed array" in native.lib().pb_last_error(ctx.h)
     assert ctx.launches == launches  # rejected before any launch
-    # the largest case that fits still runs and matches
+    # more queries than one grid dimension holds, although the scores fit:
+    # rejected by both entry points, again before any launch (buffers sized
+    # for the call all the same)
+    sq_big, sk_small = 65536, 1
+    Qb, Kb, Vb = _inputs(ctx, rng, sq_big, sk_small, 8, 8)
+    ob = ctx.alloc(sq_big * 8 * 4)
+    for fn in ("pb_attention_noalloc", "pb_attention"):
+        rc = getattr(native.lib(), fn)(ctx.h, Qb.ptr, Kb.ptr, Vb.ptr, sq_big, sk_small, 8, 8, 0, ob.ptr)
+        assert rc == native.PB_ERR_ARG, fn
+        assert b"65535" in native.lib().pb_last_error(ctx.h)
+    assert ctx.launches == launches
+    # the largest case that fits (seqQ * seqK = 524288) still runs and matches
     sk = 1024
     Q, K, V = _inputs(ctx, rng, sq, sk, 8, 8)
     o_na, o_ref = ctx.alloc(sq * 8 * 4), ctx.alloc(sq * 8 * 4)
