@@ -210,6 +210,14 @@ int pb_rope(pb_ctx* ctx, float* q_dev, float* k_dev, int seq, int start_pos, int
  * start_pos.. over a [seq_len, kv_dim] K/V cache (causal). */
 int pb_attn_cached(pb_ctx* ctx, const float* q_dev, const float* kc_dev, const float* vc_dev, int seq,
                    int start_pos, int n_heads, int n_kv, int head_dim, float* out_dev);
+/* llama-streaming.js:543-573: the attention of one query q [n_heads *
+ * head_dim] at position pos over a [max_len, n_kv * head_dim] K/V cache
+ * holding rows 0..pos, as the decode step runs it: the positions split over
+ * the GPU's SMs, double dots and sums, the splits merged in a fixed order.
+ * At most 8 query heads per kv head, head_dim % 4 == 0 and <= 128.  Blocks
+ * until done (the context scratch holds the per-split partials). */
+int pb_attn_decode(pb_ctx* ctx, const float* q_dev, const float* kc_dev, const float* vc_dev, int pos, int n_heads,
+                   int n_kv, int head_dim, int max_len, float* out_dev);
 /* llama-streaming.js:590-595 fused SiLU(gate)*up */
 int pb_swiglu(pb_ctx* ctx, const float* g_dev, const float* u_dev, int n, float* out_dev);
 

@@ -100,6 +100,7 @@ SIGNATURES = {
     "pb_attention_noalloc": (I, [V, V, V, V, I, I, I, I, I, V]),
     "pb_rope": (I, [V, V, V, I, I, I, I, I, D]),
     "pb_attn_cached": (I, [V, V, V, V, I, I, I, I, I, V]),
+    "pb_attn_decode": (I, [V, V, V, V, I, I, I, I, I, V]),
     "pb_swiglu": (I, [V, V, V, I, V]),
     "pb_quantize_q8a": (I, [V, V, I64, V, V]),
     "pb_quantize_q4a": (I, [V, V, I64, V, V]),

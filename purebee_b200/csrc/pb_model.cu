@@ -28,6 +28,13 @@ int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const fl
                           float* ws = nullptr, size_t ws_floats = 0, int* counters = nullptr,
                           __half* out16 = nullptr);
 
+int pb_attn_dec1_splits(int n_kv, int max_len, int sm_count);
+size_t pb_attn_dec1_ws_doubles(int n_heads, int n_kv, int hd, int nsplit);
+bool pb_attn_dec1_ok(int n_heads, int n_kv, int hd);
+int pb_launch_attn_dec1(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
+                        int n_heads, int n_kv, int hd, float* out, int max_len, int nsplit, double* ws,
+                        unsigned int* counters);
+
 int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
                                int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo);
 bool pb_attn_decode_ok(int n_heads, int n_kv, int hd, int max_len);
@@ -71,6 +78,11 @@ struct pb_model {
   float *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr;
   float *kc = nullptr, *vc = nullptr;
   double2* rope_tab = nullptr;
+  // one-sequence decode attention split over positions: per-split partials
+  // and the per-kv-head arrival counters (zero between launches)
+  int attn_splits = 0;
+  double* attn_ws = nullptr;
+  unsigned int* attn_cnt = nullptr;
   double rope_scaling[4] = {0, 0, 0, 0};  // factor, low, high, original context (factor 0: off)
   // activations (sized for max_m rows)
   int max_m = 0;
@@ -183,6 +195,7 @@ extern "C" int pb_model_free(pb_model* m) {
   cudaFree(m->head_f32);
   cudaFree(m->rms_att); cudaFree(m->rms_ffn); cudaFree(m->rms_final);
   cudaFree(m->kc); cudaFree(m->vc); cudaFree(m->rope_tab);
+  cudaFree(m->attn_ws); cudaFree(m->attn_cnt);
   cudaFree(m->x); cudaFree(m->xn); cudaFree(m->qkvo); cudaFree(m->att); cudaFree(m->guo); cudaFree(m->hb);
   cudaFree(m->proj); cudaFree(m->logits); cudaFree(m->toks); cudaFree(m->tok_dev); cudaFree(m->hist);
   cudaFree(m->key);
@@ -280,6 +293,13 @@ extern "C" int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model
   cudaMemsetAsync(m->key, 0, 16, ctx->stream);
   cudaMemsetAsync(m->tok_dev, 0, 16, ctx->stream);
   cudaMemsetAsync(m->hist, 0, (size_t)(c.seq_len + 1) * 4, ctx->stream);
+  if (pb_attn_dec1_ok(c.n_heads, c.n_kv_heads, c.head_dim)) {
+    m->attn_splits = pb_attn_dec1_splits(c.n_kv_heads, c.seq_len, ctx->sm_count);
+    const size_t wsd = pb_attn_dec1_ws_doubles(c.n_heads, c.n_kv_heads, c.head_dim, m->attn_splits);
+    if (cudaMalloc(&m->attn_ws, wsd * 8) != cudaSuccess || cudaMalloc(&m->attn_cnt, (size_t)c.n_kv_heads * 4))
+      return fail(pb_set_error(ctx, PB_ERR_OOM, "decode attention workspace"));
+    cudaMemsetAsync(m->attn_cnt, 0, (size_t)c.n_kv_heads * 4, ctx->stream);
+  }
   // RoPE rotation table built on the host as the reference builds it
   std::vector<double2> tab((size_t)c.seq_len * (c.head_dim / 2));
   pb_rope_table(c.rope_theta, c.head_dim, 0, c.seq_len, tab.data());
@@ -556,6 +576,18 @@ static void l2_hint(pb_mv_epi* e, int i, const pb_qmat* w, size_t cap = ~(size_t
   e->l2_next_bytes[i + 1] = (nblk * 2) & ~(size_t)15;
 }
 
+// Decode attention of the one sequence at *pos_dev (llama-streaming.js
+// :543-573): the position-split kernel when the shape fits it, else one CTA
+// per query head.
+static int launch_attn_decode1(pb_model* m, int l, const float* q, const int* pos_dev) {
+  const pb_model_config& c = m->c;
+  if (m->attn_ws)
+    return pb_launch_attn_dec1(m->ctx, q, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads, c.head_dim,
+                               m->att, c.seq_len, m->attn_splits, m->attn_ws, m->attn_cnt);
+  return pb_launch_attn_decode(m->ctx, q, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads, c.head_dim,
+                               m->att, c.seq_len, 1, pb_seq_geo());
+}
+
 // Decode layer (M == 1) of the streaming model: four fused matvecs and the
 // attention (llama-streaming.js:505-606).
 static int run_layer_decode_q4(pb_model* m, int l) {
@@ -582,8 +614,7 @@ static int run_layer_decode_q4(pb_model* m, int l) {
   l2_hint(&e, 0, m->wo[l]);
   l2_hint(&e, 2, m->w2[l]);
   PB_TRY(pb_launch_matvec(ctx, m->qkv[l], m->x, m->qkvo, 0, dim + 2 * kv, &e));
-  PB_TRY(pb_launch_attn_decode(ctx, m->qkvo, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads,
-                               c.head_dim, m->att, c.seq_len, 1, pb_seq_geo()));
+  PB_TRY(launch_attn_decode1(m, l, m->qkvo, pos_dev));
   // wo with the residual add
   pb_mv_epi r;
   r.kind = PB_EPI_RESIDUAL;
@@ -641,9 +672,8 @@ static int run_layer(pb_model* m, int l, int M, int start_pos, bool dev_pos) {
                                                                    ctx->d_err);
     PB_LAUNCHED(ctx, "k_rope_kv");
   }
-  if (M == 1 && pos_dev && pb_attn_decode_ok(c.n_heads, c.n_kv_heads, c.head_dim, c.seq_len))
-    PB_TRY(pb_launch_attn_decode(ctx, q, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads, c.head_dim,
-                                 m->att, c.seq_len, 1, pb_seq_geo()));
+  if (M == 1 && pos_dev && (m->attn_ws || pb_attn_decode_ok(c.n_heads, c.n_kv_heads, c.head_dim, c.seq_len)))
+    PB_TRY(launch_attn_decode1(m, l, q, pos_dev));
   else
     PB_TRY(pb_launch_attn_cached(ctx, q, qs_, kcache(m, l), vcache(m, l), M, start_pos, pos_dev, c.n_heads,
                                  c.n_kv_heads, c.head_dim, m->att, c.seq_len, 1, pb_seq_geo()));

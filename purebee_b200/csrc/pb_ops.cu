@@ -993,6 +993,218 @@ k_attn_dec(const float* __restrict__ q, const float* __restrict__ kc, const floa
   }
 }
 
+// ============================================================================
+// decode attention of one sequence split over positions (llama-streaming.js
+// :543-573 in double, as the reference computes it)
+// ============================================================================
+// k_attn_dec1<PER>: CTA (kv head g, split sp) over the positions
+// [sp * P, (sp + 1) * P) of the cache, P = ceil(cache_len / nsplit), for the
+// PER query heads of the group (each K and V row is read once).  The splits
+// fill one wave of the GPU (n_kv * nsplit ~ the SM count), so a layer's
+// attention is one short round of loads instead of a few CTAs walking the
+// whole cache.
+//   - before griddepcontrol.wait: the position (written by the step before),
+//     this split's K rows j < pos into registers and its V rows into L2
+//     (only row pos is written by the projection this step);
+//   - scores: thread per position, s_j = f32(dot * scale) with the double dot
+//     in the reference's order (d ascending, exact products);
+//   - per head the split's max m_c, e_j = f32(exp(s_j - m_c)) (the
+//     reference's f32 store), S_c = sum e_j and O_c[d] = sum_j e_j V[j, d]
+//     in double;
+//   - the last split of a kv head to finish (an atomic counter; no waiting)
+//     merges in split order: M = max m_c, S = sum S_c exp(m_c - M),
+//     out[d] = f32(sum O_c[d] exp(m_c - M) / S), and resets the counter.
+// Against the reference this moves the division by the sum after the
+// products and rescales a split's f32 e_j when its max is not the global
+// one: differences of an f32 rounding, within the attention tolerance.
+constexpr int AD1_THREADS = 128;
+constexpr int AD1_MAX_P = 512;   // positions per split
+constexpr int AD1_MAX_HD = 128;
+constexpr int AD1_GROUPS = AD1_THREADS / 16;  // PV position groups (16 float4 lanes cover hd <= 64 per pass)
+
+template <int PER>
+__global__ void __launch_bounds__(AD1_THREADS)
+k_attn_dec1(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+            const int* __restrict__ pos_dev, int n_kv, int hd, double scale, float* __restrict__ out, int max_len,
+            int nsplit, double* __restrict__ ws, unsigned int* __restrict__ counters, int* err) {
+  extern __shared__ __align__(16) double ad1_sm[];
+  const int g = blockIdx.x, sp = blockIdx.y, tid = threadIdx.x;
+  const int pos = *pos_dev;  // final: the step's first kernel starts after the previous step ended
+  const int cache_len = pos + 1;
+  if (pos < 0 || cache_len > max_len) {
+    pb_pdl_trigger();
+    if (tid == 0 && g == 0 && sp == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+    return;
+  }
+  const int kv_dim = n_kv * hd, h4 = hd >> 2;
+  const int P = (cache_len + nsplit - 1) / nsplit;
+  const int j0 = sp * P, j1 = min(j0 + P, cache_len);
+  const int n = j1 > j0 ? j1 - j0 : 0;
+  const float* kb = kc + (size_t)g * hd;
+  const float* vb = vc + (size_t)g * hd;
+  // K rows already in the cache (j < pos) into registers, V rows into L2
+  constexpr int KR = 16;  // float4 per thread held across the wait (hd <= 64)
+  float4 kr[KR];
+  const int jt = j0 + tid;
+  const bool has_row = tid < n;
+  if (has_row && jt < pos) {
+#pragma unroll
+    for (int u = 0; u < KR; ++u)
+      if (u < h4) kr[u] = reinterpret_cast<const float4*>(kb + (size_t)jt * kv_dim)[u];
+  }
+  for (int j = j0 + tid; j < j1 && j < pos; j += AD1_THREADS) pb_l2_prefetch(vb + (size_t)j * kv_dim, (uint32_t)hd * 4);
+  pb_pdl_trigger();
+  pb_pdl_wait();  // q and the cache row at pos come from the projection
+
+  double* e = ad1_sm;                                             // [PER][AD1_MAX_P]: e_j, then unused
+  double* pv = e + (size_t)PER * AD1_MAX_P;                       // [AD1_GROUPS][PER][hd]
+  float* qs = reinterpret_cast<float*>(pv + (size_t)AD1_GROUPS * PER * hd);  // [PER][hd]
+  __shared__ float smax[PER][AD1_THREADS / 32];
+  __shared__ double ssum[PER][AD1_THREADS / 32];
+  __shared__ unsigned int last_flag;
+  for (int i = tid; i < PER * h4; i += AD1_THREADS)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q + (size_t)g * PER * hd)[i];
+  __syncthreads();
+
+  // scores, thread per position
+  for (int t = tid; t < n; t += AD1_THREADS) {
+    const int j = j0 + t;
+    const float4* krow = reinterpret_cast<const float4*>(kb + (size_t)j * kv_dim);
+    double dot[PER];
+#pragma unroll
+    for (int h = 0; h < PER; ++h) dot[h] = 0.0;
+    for (int c0 = 0; c0 < h4; c0 += KR) {
+      float4 k4[KR];
+      const bool reg = t == tid && j < pos && c0 == 0;  // held from before the wait
+#pragma unroll
+      for (int u = 0; u < KR; ++u)
+        if (c0 + u < h4) k4[u] = reg ? kr[u] : krow[c0 + u];
+#pragma unroll
+      for (int u = 0; u < KR; ++u) {
+        if (c0 + u < h4) {
+#pragma unroll
+          for (int h = 0; h < PER; ++h) {
+            const float4 a = reinterpret_cast<const float4*>(qs + h * hd)[c0 + u];
+            dot[h] = __fma_rn((double)a.x, (double)k4[u].x, dot[h]);  // exact products, one rounding each
+            dot[h] = __fma_rn((double)a.y, (double)k4[u].y, dot[h]);
+            dot[h] = __fma_rn((double)a.z, (double)k4[u].z, dot[h]);
+            dot[h] = __fma_rn((double)a.w, (double)k4[u].w, dot[h]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < PER; ++h) {
+      const float s_ = (float)__dmul_rn(dot[h], scale);
+      e[h * AD1_MAX_P + t] = (double)s_;
+    }
+  }
+  // the split's max per head (`s > m` from -Infinity: NaN never wins)
+  const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+  for (int h = 0; h < PER; ++h) {
+    float m = -INFINITY;
+    for (int t = tid; t < n; t += AD1_THREADS) {
+      const float s_ = (float)e[h * AD1_MAX_P + t];
+      m = s_ > m ? s_ : m;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float o_ = __shfl_xor_sync(0xffffffffu, m, o);
+      m = o_ > m ? o_ : m;
+    }
+    if (lane == 0) smax[h][warp] = m;
+  }
+  __syncthreads();
+  float mc[PER];
+#pragma unroll
+  for (int h = 0; h < PER; ++h) {
+    float m = smax[h][0];
+    for (int w = 1; w < AD1_THREADS / 32; ++w) m = smax[h][w] > m ? smax[h][w] : m;
+    mc[h] = m;
+  }
+  // e_j = f32(exp(s_j - m_c)) and the split's double sum
+#pragma unroll
+  for (int h = 0; h < PER; ++h) {
+    double acc = 0.0;
+    for (int t = tid; t < n; t += AD1_THREADS) {
+      const float ej = (float)exp(__dsub_rn(e[h * AD1_MAX_P + t], (double)mc[h]));
+      e[h * AD1_MAX_P + t] = (double)ej;
+      acc = __dadd_rn(acc, (double)ej);
+    }
+    acc = pb_warp_sum_d(acc);
+    if (lane == 0) ssum[h][warp] = acc;
+  }
+  __syncthreads();
+  // O_c[h][d] = sum_j e_j V[j, d]: thread (float4 lane d4, position group jg)
+  const int d4 = tid & 15, jg = tid >> 4;
+  for (int dc = 0; dc < h4; dc += 16) {
+    const int dd = dc + d4;
+    double a[PER][4];
+#pragma unroll
+    for (int h = 0; h < PER; ++h) a[h][0] = a[h][1] = a[h][2] = a[h][3] = 0.0;
+    if (dd < h4) {
+      for (int t = jg; t < n; t += AD1_GROUPS) {
+        const float4 v = reinterpret_cast<const float4*>(vb + (size_t)(j0 + t) * kv_dim)[dd];
+#pragma unroll
+        for (int h = 0; h < PER; ++h) {
+          const double p = e[h * AD1_MAX_P + t];
+          a[h][0] = __fma_rn(p, (double)v.x, a[h][0]);
+          a[h][1] = __fma_rn(p, (double)v.y, a[h][1]);
+          a[h][2] = __fma_rn(p, (double)v.z, a[h][2]);
+          a[h][3] = __fma_rn(p, (double)v.w, a[h][3]);
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < PER; ++h)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) pv[((size_t)jg * PER + h) * hd + 4 * dd + c] = a[h][c];
+    }
+  }
+  __syncthreads();
+  // this split's partial: [m_c, S_c, O_c[hd]] per head, groups summed in order
+  double* wsp = ws + ((size_t)g * nsplit + sp) * PER * (2 + hd);
+  for (int i = tid; i < PER * hd; i += AD1_THREADS) {
+    const int h = i / hd, d = i - h * hd;
+    double o = pv[(size_t)h * hd + d];
+    for (int k = 1; k < AD1_GROUPS; ++k) o = __dadd_rn(o, pv[((size_t)k * PER + h) * hd + d]);
+    wsp[(size_t)h * (2 + hd) + 2 + d] = o;
+  }
+  if (tid < PER) {
+    double sacc = ssum[tid][0];
+    for (int w = 1; w < AD1_THREADS / 32; ++w) sacc = __dadd_rn(sacc, ssum[tid][w]);
+    wsp[(size_t)tid * (2 + hd)] = (double)mc[tid];
+    wsp[(size_t)tid * (2 + hd) + 1] = sacc;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last_flag = atomicAdd(counters + g, 1u) == (unsigned)nsplit - 1;
+  __syncthreads();
+  if (!last_flag) return;
+  __threadfence();
+  // the last split merges every split of this kv head, in split order
+  const double* wg = ws + (size_t)g * nsplit * PER * (2 + hd);
+  for (int i = tid; i < PER * hd; i += AD1_THREADS) {
+    const int h = i / hd, d = i - h * hd;
+    double M = -INFINITY;
+    for (int c = 0; c < nsplit; ++c) {
+      const double mcv = __ldcg(wg + ((size_t)c * PER + h) * (2 + hd));
+      M = mcv > M ? mcv : M;
+    }
+    double S = 0.0, O = 0.0;
+    for (int c = 0; c < nsplit; ++c) {
+      const double* w = wg + ((size_t)c * PER + h) * (2 + hd);
+      const double mcv = __ldcg(w), sc = __ldcg(w + 1);
+      if (sc == 0.0) continue;  // an empty split (fewer positions than splits); a non-empty one has S_c >= 1 or NaN
+      const double f = mcv == M ? 1.0 : exp(__dsub_rn(mcv, M));
+      S = __fma_rn(sc, f, S);
+      O = __fma_rn(__ldcg(w + 2 + d), f, O);
+    }
+    out[((size_t)g * PER + h) * hd + d] = (float)__ddiv_rn(O, S);
+  }
+  if (tid == 0) counters[g] = 0u;  // ready for the next launch
+}
+
 // k_attn_dec_group: the batched form (configs with many sequences), in f32 like
 // the batched prefill attention.  CTA (kv head g, sequence z), AG_THREADS
 // threads, all `per` query heads of the group at once so each K and V row is
@@ -1459,6 +1671,71 @@ int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const fl
                    pos_dev, n_heads, n_kv, hd, scale, out, max_len, geo, ctx->d_err);
 }
 
+// Splits of the one-sequence decode attention: about one CTA per SM in
+// total, at most AD1_MAX_P positions each.
+int pb_attn_dec1_splits(int n_kv, int max_len, int sm_count) {
+  int ns = sm_count / n_kv;
+  if (ns < 1) ns = 1;
+  const int need = (max_len + AD1_MAX_P - 1) / AD1_MAX_P;
+  return ns < need ? need : ns;
+}
+
+size_t pb_attn_dec1_ws_doubles(int n_heads, int n_kv, int hd, int nsplit) {
+  return (size_t)n_kv * nsplit * (n_heads / n_kv) * (2 + hd);
+}
+
+static size_t ad1_smem(int per, int hd) {
+  return (size_t)per * AD1_MAX_P * 8 + (size_t)AD1_GROUPS * per * hd * 8 + (size_t)per * hd * 4;
+}
+
+bool pb_attn_dec1_ok(int n_heads, int n_kv, int hd) {
+  return n_kv > 0 && n_heads % n_kv == 0 && n_heads / n_kv <= 8 && hd % 4 == 0 && hd <= AD1_MAX_HD &&
+         ad1_smem(n_heads / n_kv, hd) <= 200 * 1024;
+}
+
+// The position-split decode attention of one sequence; ws holds
+// pb_attn_dec1_ws_doubles doubles, counters n_kv zeroed words (the kernel
+// leaves them zero).
+int pb_launch_attn_dec1(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
+                        int n_heads, int n_kv, int hd, float* out, int max_len, int nsplit, double* ws,
+                        unsigned int* counters) {
+  if (!pb_attn_dec1_ok(n_heads, n_kv, hd) || nsplit <= 0 || (size_t)(max_len + nsplit - 1) / nsplit > AD1_MAX_P)
+    return pb_set_error(ctx, PB_ERR_ARG, "split decode attention: unsupported shape");
+  const double scale = 1.0 / sqrt((double)hd);  // llama-streaming.js:546
+  const dim3 grid(n_kv, nsplit);
+  const int per = n_heads / n_kv;
+  switch (per) {
+#define PB_AD1_CASE(P)                                                                                          \
+  case P:                                                                                                       \
+    return pb_launch(ctx, "k_attn_dec1", true, k_attn_dec1<P>, grid, dim3(AD1_THREADS), ad1_smem(P, hd), q, kc, \
+                     vc, pos_dev, n_kv, hd, scale, out, max_len, nsplit, ws, counters, ctx->d_err);
+    PB_AD1_CASE(1) PB_AD1_CASE(2) PB_AD1_CASE(3) PB_AD1_CASE(4) PB_AD1_CASE(5) PB_AD1_CASE(6) PB_AD1_CASE(7)
+    PB_AD1_CASE(8)
+#undef PB_AD1_CASE
+    default:
+      return pb_set_error(ctx, PB_ERR_ARG, "split decode attention: at most 8 query heads per kv head");
+  }
+}
+
+extern "C" int pb_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, int pos, int n_heads,
+                              int n_kv, int hd, int max_len, float* out) {
+  if (!ctx || !q || !kc || !vc || !out || n_heads <= 0 || n_kv <= 0 || hd <= 0 || pos < 0 || pos >= max_len)
+    return pb_set_error(ctx, PB_ERR_ARG, "pb_attn_decode: bad arguments (pos %d, max_len %d)", pos, max_len);
+  if (!pb_attn_dec1_ok(n_heads, n_kv, hd))
+    return pb_set_error(ctx, PB_ERR_ARG, "pb_attn_decode: needs n_heads %% n_kv == 0, at most 8 query heads per kv "
+                                         "head, head_dim %% 4 == 0 and head_dim <= %d", AD1_MAX_HD);
+  const int nsplit = pb_attn_dec1_splits(n_kv, max_len, ctx->sm_count);
+  const size_t wsb = pb_attn_dec1_ws_doubles(n_heads, n_kv, hd, nsplit) * 8;
+  PB_TRY(pb_ensure_scratch(ctx, wsb + 256 + (size_t)n_kv * 4 + 16));
+  double* ws = (double*)ctx->scratch;
+  unsigned int* cnt = (unsigned int*)((char*)ctx->scratch + ((wsb + 255) & ~(size_t)255));
+  int* pos_dev = (int*)(cnt + n_kv);
+  PB_TRY_CUDA(ctx, cudaMemsetAsync(cnt, 0, (size_t)n_kv * 4, ctx->stream));
+  PB_TRY_CUDA(ctx, cudaMemcpyAsync(pos_dev, &pos, 4, cudaMemcpyHostToDevice, ctx->stream));
+  PB_TRY(pb_launch_attn_dec1(ctx, q, kc, vc, pos_dev, n_heads, n_kv, hd, out, max_len, nsplit, ws, cnt));
+  return pb_wait(ctx);  // the position's host copy must outlive the transfer
+}
+
 int pb_setup_ops_kernels(void) {
   cudaError_t e = cudaFuncSetAttribute(k_attn_cached, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -1466,5 +1743,8 @@ int pb_setup_ops_kernels(void) {
   for (auto k : {k_attn_dec_split<1>, k_attn_dec_split<2>, k_attn_dec_split<3>, k_attn_dec_split<4>,
                  k_attn_dec_split<5>, k_attn_dec_split<6>, k_attn_dec_split<7>, k_attn_dec_split<8>})
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)as_smem());
+  for (auto k : {k_attn_dec1<1>, k_attn_dec1<2>, k_attn_dec1<3>, k_attn_dec1<4>, k_attn_dec1<5>, k_attn_dec1<6>,
+                 k_attn_dec1<7>, k_attn_dec1<8>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
 }

@@ -372,6 +372,35 @@ def test_attention_cached_and_generic(native, ctx, oracle, golden):
     assert close(o.download(count=30), oracle.attention(Q, K, V, 5, 5, 8, 6, True))
 
 
+@pytest.mark.parametrize("nh,nkv,hd,max_len,positions", [
+    (32, 8, 64, 2048, (0, 5, 128, 384, 639, 2047)),  # configs[3]: Llama-3.2-1B heads
+    (9, 3, 64, 512, (31, 287)),                       # configs[2]: SmolLM2-135M
+    (6, 6, 48, 256, (15, 143)),                       # configs[0]: stories15M
+])
+def test_split_decode_attention(native, ctx, oracle, nh, nkv, hd, max_len, positions):
+    """The decode step's position-split attention (pb_attn_decode) against
+    the oracle's llama-streaming.js:543-573 at cache lengths from 1 to the
+    maximum, within the reduction tolerance; a second call on the same
+    buffers gives the same bits (the split counters are left at zero)."""
+    L = native.lib()
+    rng = np.random.default_rng(52 + hd)
+    kv = nkv * hd
+    kk = rng.standard_normal((max_len, kv)).astype(f32)
+    vv = rng.standard_normal((max_len, kv)).astype(f32)
+    dkc, dvc = dev(ctx, kk), dev(ctx, vv)
+    for pos in positions:
+        qq = (rng.standard_normal(nh * hd) * 0.5).astype(f32)
+        dq, o = dev(ctx, qq), out(ctx, nh * hd)
+        ctx._check(L.pb_attn_decode(ctx.h, dq.ptr, dkc.ptr, dvc.ptr, pos, nh, nkv, hd, max_len, o.ptr))
+        got = o.download(count=nh * hd)
+        want = oracle.attn_cached(qq, kk[:pos + 1], vv[:pos + 1], 1, pos, nh * hd, nh, nkv, hd)
+        assert close(got, want), pos
+        ctx._check(L.pb_attn_decode(ctx.h, dq.ptr, dkc.ptr, dvc.ptr, pos, nh, nkv, hd, max_len, o.ptr))
+        assert bits_equal(o.download(count=nh * hd), got), pos
+    with pytest.raises(native.PureBeeError):
+        ctx._check(L.pb_attn_decode(ctx.h, dq.ptr, dkc.ptr, dvc.ptr, max_len, nh, nkv, hd, max_len, o.ptr))
+
+
 def test_capture_replay(native, ctx, oracle):
     """pb_capture_begin/end record device-pointer calls; a replay gives the same bits."""
     rng = np.random.default_rng(31)

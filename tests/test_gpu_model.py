@@ -129,26 +129,80 @@ def test_greedy_tokens_match_oracle(native, ctx, oracle, name, n_prompt, n_steps
     rt.shutdown()
 
 
-def test_llama1b_short_parity(native, ctx, oracle):
-    """configs[3] shape: prefill 16 + 8 decode steps, tokens and logits."""
-    kw = CONFIGS["llama1B"]
-    rt, om = make_pair(ctx, kw, 20261201, copy_weights_from_device=True)
-    prompt = oracle.synth_tokens(16, 20261201, 1, kw["vocab"]).tolist()
+def _top2_gap(lg):
+    v = np.sort(lg.astype(np.float64)[~np.isnan(lg)])
+    return float(v[-1] - v[-2])
+
+
+def _kv_rows_close(rt, om, layers, upto):
+    for l in layers:
+        for which in (0, 1):
+            kd, ko = rt.model.kv(l, which)[:upto], om.kv(l, which)[:upto]
+            assert np.max(np.abs(kd - ko)) <= LOGIT_RTOL * np.max(np.abs(ko)), (l, which)
+
+
+@pytest.mark.parametrize("name,n_prompt,n_steps", [("stories15M", 16, 128), ("smollm135M", 32, 256),
+                                                   ("llama1B", 128, 512)])
+def test_teacher_forced_full_workload(native, ctx, oracle, name, n_prompt, n_steps):
+    """Every configuration's whole BASELINE workload (configs[0] 16 + 128,
+    configs[2] 32 + 256, configs[3] 128 + 512 with the KV cache reaching
+    640 positions), teacher-forced: the prefill, then at every step the
+    device's decode step (the recorded graph the bench replays) and the
+    oracle run on the same token, the greedy token of the oracle's logits.
+    At every step: max |logit_dev - logit_oracle| <= LOGIT_RTOL * max |logit|,
+    and the device's greedy token equals the oracle's.  The worst relative
+    error and the smallest top-2 logit gap seen are printed (a gap far above
+    the error is what makes the greedy tokens robust)."""
+    kw = CONFIGS[name]
+    rt, om = make_pair(ctx, kw, 20261201, copy_weights_from_device=name == "llama1B")
+    prompt = oracle.synth_tokens(n_prompt, 20261201, 1, kw["vocab"]).tolist()
     lg_dev = rt.forward(prompt, 0)["logits"]
     lg_orc = om.forward(prompt, 0)
-    assert np.max(np.abs(lg_dev - lg_orc)) <= LOGIT_RTOL * np.max(np.abs(lg_orc))
+    scale = np.max(np.abs(lg_orc))
+    worst = float(np.max(np.abs(lg_dev - lg_orc)) / scale)
+    assert worst <= LOGIT_RTOL
     tok = oracle.argmax(lg_orc)
     assert rt.argmax(lg_dev) == tok
-    for step in range(8):
-        lg_dev = rt.forward([tok], 16 + step)["logits"]
-        lg_orc = om.forward([tok], 16 + step)
-        assert np.max(np.abs(lg_dev - lg_orc)) <= LOGIT_RTOL * np.max(np.abs(lg_orc))
-        nt = oracle.argmax(lg_orc)
-        assert rt.argmax(lg_dev) == nt
-        tok = nt
-    # the KV cache rows written so far agree
-    kd, ko = rt.model.kv(3, 0)[:24], om.kv(3, 0)[:24]
-    assert np.max(np.abs(kd - ko)) <= LOGIT_RTOL * np.max(np.abs(ko))
+    min_gap, gap_step, tokens = _top2_gap(lg_orc), -1, [tok]
+    for step in range(n_steps):
+        pos = n_prompt + step
+        nxt, lg_dev = rt.model.decode(tok, pos, True)
+        lg_orc = om.forward([tok], pos)
+        err = float(np.max(np.abs(lg_dev - lg_orc)) / np.max(np.abs(lg_orc)))
+        worst = max(worst, err)
+        assert err <= LOGIT_RTOL, (step, err)
+        want = oracle.argmax(lg_orc)
+        assert nxt == want and rt.argmax(lg_dev) == want, step
+        gap = _top2_gap(lg_orc)
+        if gap < min_gap:
+            min_gap, gap_step = gap, step
+        tok = want
+        tokens.append(tok)
+    last = n_prompt + n_steps
+    _kv_rows_close(rt, om, (0, kw["n_layers"] - 1), last)
+    print(f"\n[parity] {name} {n_prompt}+{n_steps}: worst max|dlogit|/max|logit| = {worst:.3e}, "
+          f"smallest top-2 gap = {min_gap:.4e} (step {gap_step}), {len(set(tokens))} distinct tokens, "
+          f"KV positions written = {last}")
+    rt.shutdown()
+
+
+@pytest.mark.parametrize("name,n_prompt,n_steps", [("smollm135M", 32, 96), ("llama1B", 16, 64)])
+def test_teacher_forced_random_tokens(native, ctx, oracle, name, n_prompt, n_steps):
+    """The same per-step check on seeded random input tokens instead of the
+    greedy ones (random-init models repeat a token under greedy decoding, so
+    this covers varied embeddings and attention patterns)."""
+    kw = CONFIGS[name]
+    rt, om = make_pair(ctx, kw, 7, copy_weights_from_device=name == "llama1B")
+    toks = oracle.synth_tokens(n_prompt + n_steps, 77, 1, kw["vocab"]).tolist()
+    lg_dev = rt.forward(toks[:n_prompt], 0)["logits"]
+    lg_orc = om.forward(toks[:n_prompt], 0)
+    assert np.max(np.abs(lg_dev - lg_orc)) <= LOGIT_RTOL * np.max(np.abs(lg_orc))
+    for step in range(n_steps):
+        pos = n_prompt + step
+        nxt, lg_dev = rt.model.decode(toks[pos], pos, True)
+        lg_orc = om.forward([toks[pos]], pos)
+        assert np.max(np.abs(lg_dev - lg_orc)) <= LOGIT_RTOL * np.max(np.abs(lg_orc)), step
+        assert nxt == oracle.argmax(lg_orc), step
     rt.shutdown()
 
 
