@@ -136,6 +136,21 @@ int pb_qmat_info(const pb_qmat* m, int* type, int* N, int* K);
  * multiple of 8 (rows are stored in 8-row tiles); anything else is
  * PB_ERR_ARG. */
 int pb_qmat_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, float* y_dev, int row0, int rows);
+/* Arithmetic of the resident Q4_0 matvec: pb_qmat_matvec and every model
+ * decode step on the context (a model re-records its step graph when the
+ * mode changes).
+ *   PB_MATVEC_FAST (default): the same exact (q - 8) * x products, summed
+ *     with one FMA per weight in a different order: y within an f32
+ *     relative tolerance of wasm-q4.js:118-267 (north_star's per-op bar),
+ *     greedy tokens unchanged (tests check both over whole workloads);
+ *   PB_MATVEC_EXACT: the WASM lane order with separate multiply and add,
+ *     bit for bit (the parity mode).
+ * pb_q4_0_matvec / pb_q4_1_matvec (the module functions) and Q4_1 matrices
+ * always run the exact kernel. */
+#define PB_MATVEC_FAST 0
+#define PB_MATVEC_EXACT 1
+int pb_set_matvec_mode(pb_ctx* ctx, int mode);
+int pb_matvec_mode(const pb_ctx* ctx);
 /* wasm-q4.js:716-747 q4_0_matvec(x, rawBuf, N, K): host buffers in and out. */
 int pb_q4_0_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, int N, int K, float* y_host);
 /* wasm-q4.js:758-785 q4_1_matvec(x, rawBuf, N, K) */

@@ -18,6 +18,7 @@ PB_OK, PB_ERR_ARG, PB_ERR_OOM, PB_ERR_CUDA, PB_ERR_TIMEOUT, PB_ERR_DEVICE, PB_ER
 TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q4_1, TYPE_Q8_0 = 0, 1, 2, 3, 8
 QMAT_TABLE = 0x100  # OR into the type: LM-head table layout (pb_qmat_head)
 MODEL_STREAMING_Q4, MODEL_LLAMA_Q8A = 0, 1
+MATVEC_FAST, MATVEC_EXACT = 0, 1  # pb_set_matvec_mode
 
 _ERRNAMES = {1: "PB_ERR_ARG", 2: "PB_ERR_OOM", 3: "PB_ERR_CUDA", 4: "PB_ERR_TIMEOUT", 5: "PB_ERR_DEVICE",
              6: "PB_ERR_STATE", 7: "PB_ERR_NOTFOUND"}
@@ -101,6 +102,8 @@ SIGNATURES = {
     "pb_rope": (I, [V, V, V, I, I, I, I, I, D]),
     "pb_attn_cached": (I, [V, V, V, V, I, I, I, I, I, V]),
     "pb_attn_decode": (I, [V, V, V, V, I, I, I, I, I, V]),
+    "pb_set_matvec_mode": (I, [V, I]),
+    "pb_matvec_mode": (I, [V]),
     "pb_swiglu": (I, [V, V, V, I, V]),
     "pb_quantize_q8a": (I, [V, V, I64, V, V]),
     "pb_quantize_q4a": (I, [V, V, I64, V, V]),
@@ -268,6 +271,14 @@ class Context:
 
     def sync(self) -> None:
         self._check(lib().pb_sync(self.h))
+
+    def set_matvec_mode(self, mode: int) -> None:
+        """MATVEC_FAST (default) or MATVEC_EXACT (the reference's lane order, bit for bit)."""
+        self._check(lib().pb_set_matvec_mode(self.h, int(mode)))
+
+    @property
+    def matvec_mode(self) -> int:
+        return int(lib().pb_matvec_mode(self.h))
 
     def set_timeout_ms(self, ms: int) -> None:
         self._check(lib().pb_set_timeout_ms(self.h, ms))

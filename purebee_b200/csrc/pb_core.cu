@@ -163,6 +163,14 @@ extern "C" int pb_shutdown(pb_ctx* ctx) {
 
 extern "C" const char* pb_last_error(const pb_ctx* ctx) { return ctx ? ctx->err.c_str() : "no context"; }
 
+extern "C" int pb_set_matvec_mode(pb_ctx* ctx, int mode) {
+  if (!ctx || (mode != PB_MATVEC_FAST && mode != PB_MATVEC_EXACT)) return PB_ERR_ARG;
+  ctx->matvec_mode = mode;
+  return PB_OK;
+}
+
+extern "C" int pb_matvec_mode(const pb_ctx* ctx) { return ctx ? ctx->matvec_mode : -1; }
+
 extern "C" int pb_set_timeout_ms(pb_ctx* ctx, int timeout_ms) {
   if (!ctx || timeout_ms <= 0) return PB_ERR_ARG;
   ctx->timeout_ms = timeout_ms;

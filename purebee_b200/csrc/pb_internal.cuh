@@ -12,6 +12,7 @@
 struct pb_ctx {
   int device = 0;
   int sm_count = 148;
+  int matvec_mode = PB_MATVEC_FAST;  // resident Q4_0 matvecs (pb_set_matvec_mode)
   size_t l2_bytes = 0;
   cudaStream_t stream = nullptr;
   int timeout_ms = 10000;

@@ -114,6 +114,7 @@ struct pb_model {
   std::vector<cudaGraph_t> lgraph;  // decode steps over the first L layers, index L
   std::vector<cudaGraphExec_t> lexec;
   int launches_per_step = 0;
+  int graph_mode = PB_MATVEC_FAST;  // matvec mode the recorded graphs were made with
   float* h_logits_pinned = nullptr;
   int* h_io_pinned = nullptr;
 };
@@ -745,7 +746,17 @@ static int ensure_sample_buffers(pb_model* m) {
   return PB_OK;
 }
 
+// Recorded graphs hold the matvec kernels of the context's matvec mode at
+// recording time; a mode change drops them so the next step records again.
+static void check_graph_mode(pb_model* m) {
+  if (m->graph_mode != m->ctx->matvec_mode) {
+    free_graph(m);
+    m->graph_mode = m->ctx->matvec_mode;
+  }
+}
+
 static int ensure_graph(pb_model* m) {
+  check_graph_mode(m);
   if (m->exec) return PB_OK;
   pb_ctx* ctx = m->ctx;
   PB_TRY(ensure_act(m, 1));
@@ -835,6 +846,7 @@ extern "C" int pb_model_sample(pb_model* m, int top_k, double temperature, uint6
 // Decode step graph over the first L < n_layers layers (the draft of
 // self-speculative decoding, forward(..., {maxLayers: L})).
 static int ensure_graph_layers(pb_model* m, int L) {
+  check_graph_mode(m);
   if ((int)m->lexec.size() < m->c.n_layers) {
     m->lexec.resize(m->c.n_layers, nullptr);
     m->lgraph.resize(m->c.n_layers, nullptr);
@@ -993,6 +1005,7 @@ extern "C" int pb_model_generate(pb_model* m, const int* prompt, int n_prompt, i
 static int ensure_sample_graph(pb_model* m, int top_k, double temperature, uint64_t seed) {
   pb_ctx* ctx = m->ctx;
   PB_TRY(ensure_sample_buffers(m));
+  check_graph_mode(m);
   if (m->sexec && m->s_topk == top_k && m->s_temp == temperature && m->s_seed == seed) return PB_OK;
   if (m->sexec) cudaGraphExecDestroy(m->sexec);
   if (m->sgraph) cudaGraphDestroy(m->sgraph);

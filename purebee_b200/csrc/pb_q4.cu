@@ -328,6 +328,9 @@ __device__ __forceinline__ void mv_load(MvBuf& R, const uint8_t* __restrict__ qs
   }
 }
 
+__device__ __forceinline__ void mv_epilogue(float v, int tile, int N, int row_end, float* __restrict__ y,
+                                            const pb_mv_epi& epi, int* err);
+
 // Chain of slot `slot`'s tile over the nb block partials, then the epilogue.
 // Lane = 4 * row + L.
 __device__ __forceinline__ void mv_chain(const float* __restrict__ pc, int nb, int tile, int N, int row_end,
@@ -350,6 +353,14 @@ __device__ __forceinline__ void mv_chain(const float* __restrict__ pc, int nb, i
   const float a2 = __shfl_sync(0xffffffffu, acc, base + 2);
   const float a3 = __shfl_sync(0xffffffffu, acc, base + 3);
   const float v = __fadd_rn(__fadd_rn(a1, a3), __fadd_rn(a0, a2));
+  mv_epilogue(v, tile, N, row_end, y, epi, err);
+}
+
+// The fused epilogue of an 8-row tile: every lane of quad r (lanes 4r ..
+// 4r + 3) holds row r's value v; the quad's lane 0 stores.
+__device__ __forceinline__ void mv_epilogue(float v, int tile, int N, int row_end, float* __restrict__ y,
+                                            const pb_mv_epi& epi, int* err) {
+  const int lane = threadIdx.x & 31, rr = lane >> 2, L = lane & 3;
   const int row = tile * 8 + rr;
   const bool live = L == 0 && row < row_end && row < N;
   if (epi.kind == PB_EPI_STORE) {
@@ -619,6 +630,221 @@ k_matvec_ws(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, co
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fast Q4_0 matvec (the default decode path).  The same products as the
+// reference, (q - 8) * x with q - 8 exact, summed with one FMA per weight
+// instead of the reference's separate multiply and add and in a different
+// order, so y agrees with wasm-q4.js:118-267 within an f32 tolerance, not
+// bit for bit (the exact kernels above stay the parity mode).
+//
+// A warp works on one (8-row tile, 32-block K chunk): lane l takes block
+// 32 c + l of the tile's 8 rows (16-byte coalesced loads, 512 contiguous
+// bytes per row), keeps that block's x as 16 f32 pairs, and forms per row
+// the block sum with packed f32x2 arithmetic: a nibble becomes the exact
+// float 2^k + q by one logic op, a packed add removes 2^k + 8, a packed FMA
+// accumulates.  That is one integer and two f32 lane operations per weight.
+// The block sum times the f16 scale (decoded the WASM way, wasm-q4.js
+// :88-109) is added into the row's partial.  The 8 row partials of the warp
+// are summed across lanes by a transposed butterfly (lane 4r ends with row
+// r), the K chunks of a tile are added in chunk order in shared memory, and
+// the tile's epilogue is the one of the exact kernels.  Each CTA prefetches
+// its tiles into L2 a few iterations ahead (bulk prefetch), so the register
+// loads find them there.
+// ---------------------------------------------------------------------------
+constexpr int MVF_MAX_WARPS = 16;
+constexpr int MVF_PF = 3;  // CTA iterations of L2 prefetch ahead
+
+__device__ __forceinline__ float q4_0_block_fast(uint4 p, const uint64_t (&xp)[16], const pb_magics& M) {
+  const uint64_t c_l01 = p2(-8388616.0f, -32776.0f), c_l23 = p2(-136.0f, -32776.0f);
+  const uint64_t c_h = p2(-524296.0f, -2056.0f);
+  uint64_t a = 0, b = 0;  // two independent FMA chains of f32 pairs
+  const uint32_t wv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t w = wv[g], w2 = w >> 16;
+    // elements 4g, 4g+1 (low nibbles of bytes 0, 1), 4g+2, 4g+3 (bytes 2, 3),
+    // then the high nibbles: elements 16 + 4g .. 16 + 4g + 3
+    const uint64_t l01 = p2add(p2(magr<0xFu>(w, M.m0), magr<0xF00u>(w, M.m8)), c_l01);
+    const uint64_t l23 = p2add(p2(magr<0xF0000u>(w, M.m16), magr<0xF00u>(w2, M.m8)), c_l23);
+    const uint64_t h01 = p2add(p2(magr<0xF0u>(w, M.m4), magr<0xF000u>(w, M.m12)), c_h);
+    const uint64_t h23 = p2add(p2(magr<0xF0u>(w2, M.m4), magr<0xF000u>(w2, M.m12)), c_h);
+    a = p2fma(l01, xp[2 * g], a);
+    b = p2fma(l23, xp[2 * g + 1], b);
+    a = p2fma(h01, xp[8 + 2 * g], a);
+    b = p2fma(h23, xp[9 + 2 * g], b);
+  }
+  const float2 s = up2(p2add(a, b));
+  return __fadd_rn(s.x, s.y);
+}
+
+// x (RMS-normalised when w is set) into shared memory, float4 chunks
+// swizzled within each 32-value block (bank-conflict-free reads of one block
+// per lane).  Any K: the threads loop over the chunks.
+// The sum of squares runs over a fixed partition (128 lanes, chunk c on lane
+// c % 128, then a fixed tree), so it does not depend on the CTA size: every
+// launch shape of the same vector normalises it to the same bits.
+__device__ __forceinline__ void mvf_stage_x(const float* __restrict__ x, const float* __restrict__ w, double eps, int K,
+                                            float4* xs4, double* red) {
+  const int tid = threadIdx.x, nt = blockDim.x, nc = K / 4;
+  double rms = 0.0;
+  if (w) {
+    if (tid < 128) {
+      double ss = 0.0;
+      for (int c = tid; c < nc; c += 128) {
+        const float4 v = reinterpret_cast<const float4*>(x)[c];
+        ss = __fma_rn((double)v.x, (double)v.x, ss);
+        ss = __fma_rn((double)v.y, (double)v.y, ss);
+        ss = __fma_rn((double)v.z, (double)v.z, ss);
+        ss = __fma_rn((double)v.w, (double)v.w, ss);
+      }
+      ss = pb_warp_sum_d(ss);
+      if ((tid & 31) == 0) red[tid >> 5] = ss;
+    }
+    __syncthreads();
+    const double ss = __dadd_rn(__dadd_rn(red[0], red[1]), __dadd_rn(red[2], red[3]));
+    rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)K), eps));
+  }
+  for (int c = tid; c < nc; c += nt) {
+    float4 v = reinterpret_cast<const float4*>(x)[c];
+    if (w) {
+      const float4 wv = reinterpret_cast<const float4*>(w)[c];
+      v.x = (float)__dmul_rn(__ddiv_rn((double)v.x, rms), (double)wv.x);
+      v.y = (float)__dmul_rn(__ddiv_rn((double)v.y, rms), (double)wv.y);
+      v.z = (float)__dmul_rn(__ddiv_rn((double)v.z, rms), (double)wv.z);
+      v.w = (float)__dmul_rn(__ddiv_rn((double)v.w, rms), (double)wv.w);
+    }
+    const int bj = c >> 3, ci = c & 7;
+    xs4[bj * 8 + (ci ^ (bj & 7))] = v;
+  }
+}
+
+// CTA of W warps = TPC tiles x KC chunks per iteration (TPC = W / KC).
+__global__ void __launch_bounds__(MVF_MAX_WARPS * 32, 1)
+k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, int nb, int tile_begin, int tile_end,
+      int row_end, const float* __restrict__ x, float* __restrict__ y, pb_mv_epi epi, pb_magics M, int* err) {
+  extern __shared__ __align__(16) unsigned char mvf_raw[];
+  __shared__ double red[MVF_MAX_WARPS];
+  const int K = nb * 32, KC = (nb + 31) >> 5, W = blockDim.x >> 5, TPC = W / KC;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tl = warp / KC, ch = warp - tl * KC;  // this warp's tile slot and K chunk
+  const bool active = tl < TPC;
+  const int b = ch * 32 + lane;
+  const bool has_b = active && b < nb;
+  float4* xs4 = reinterpret_cast<float4*>(mvf_raw);                  // [K / 4] swizzled
+  float* part = reinterpret_cast<float*>(mvf_raw + (size_t)K * 4);   // [2][TPC][KC][8]
+  const int per_iter = gridDim.x * TPC;
+  const int n_iter = (tile_end - tile_begin + per_iter - 1) / per_iter;  // CTA-uniform
+  const uint4* q4 = reinterpret_cast<const uint4*>(qs);
+  const size_t tq = (size_t)8 * nb * 16, td = (size_t)8 * nb * 2;
+  auto tile_of = [&](int it) { return tile_begin + it * per_iter + blockIdx.x * TPC + tl; };
+  // L2 prefetch: the chunk-0 warp of each tile slot fetches its tile (payload
+  // and scales are contiguous per tile) MVF_PF iterations ahead
+  auto prefetch = [&](int it) {
+    const int t = tile_of(it);
+    if (active && ch == 0 && lane == 0 && it < n_iter && t < tile_end) {
+      pb_l2_prefetch(qs + (size_t)t * tq, (uint32_t)tq);
+      pb_l2_prefetch(dsc + (size_t)t * td / 2, (uint32_t)td);
+    }
+  };
+  for (int i = 0; i < MVF_PF; ++i) prefetch(i);
+  if (tid == 0)
+    for (int i = 0; i < PB_MAX_L2_NEXT; ++i) pb_l2_prefetch_share(epi.l2_next[i], epi.l2_next_bytes[i], blockIdx.x, gridDim.x);
+  // the first tile's blocks (weights do not depend on the previous kernel)
+  uint4 pq[8];
+  uint32_t pd[8];
+  auto load = [&](int it) {
+    const int t = tile_of(it);
+    if (has_b && it < n_iter && t < tile_end) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const size_t slot = (size_t)(t * 8 + r) * nb + b;
+        pq[r] = __ldcs(q4 + slot);
+        pd[r] = __ldcs(dsc + slot);
+      }
+    }
+  };
+  load(0);
+  pb_pdl_trigger();
+  pb_pdl_wait();  // x (and the residual) come from the previous kernel
+  mvf_stage_x(x, epi.norm_w, epi.eps, K, xs4, red);
+  __syncthreads();
+  uint64_t xp[16];
+  if (has_b) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = xs4[b * 8 + (i ^ (b & 7))];
+      xp[2 * i] = p2(v.x, v.y);
+      xp[2 * i + 1] = p2(v.z, v.w);
+    }
+  }
+  for (int it = 0; it < n_iter; ++it) {
+    prefetch(it + MVF_PF);
+    const int t = tile_of(it);
+    float v[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) v[r] = 0.0f;
+    if (has_b && t < tile_end) {
+#pragma unroll
+      for (int r = 0; r < 8; ++r) v[r] = __fmul_rn(q4_0_block_fast(pq[r], xp, M), pb_f16_wasm(pd[r]));
+    }
+    load(it + 1);
+    // transposed butterfly over the lanes: lane 4r ends with row r's sum
+    float w4[4], w2[2];
+    const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = b16 ? v[i] : v[i + 4], keep = b16 ? v[i + 4] : v[i];
+      w4[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = b8 ? w4[i] : w4[i + 2], keep = b8 ? w4[i + 2] : w4[i];
+      w2[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+    }
+    float z;
+    {
+      const float send = b4 ? w2[0] : w2[1], keep = b4 ? w2[1] : w2[0];
+      z = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+    }
+    z = __fadd_rn(z, __shfl_xor_sync(0xffffffffu, z, 2));
+    z = __fadd_rn(z, __shfl_xor_sync(0xffffffffu, z, 1));
+    // lane 4r: row r = 4 bit4 + 2 bit3 + bit2 of the lane
+    const int row_of_lane = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    float* pbuf = part + (size_t)(it & 1) * TPC * KC * 8;
+    if (active && (lane & 3) == 0) pbuf[((size_t)tl * KC + ch) * 8 + row_of_lane] = z;
+    __syncthreads();
+    if (active && ch == 0 && t < tile_end) {
+      const int rr = lane >> 2;
+      float s_ = pbuf[(size_t)tl * KC * 8 + rr];
+      for (int c = 1; c < KC; ++c) s_ = __fadd_rn(s_, pbuf[((size_t)tl * KC + c) * 8 + rr]);
+      mv_epilogue(s_, t, N, row_end, y, epi, err);
+    }
+  }
+}
+
+// Warps per CTA: small matrices get small CTAs (more SMs share the rows),
+// large ones 16 warps; at least one warp per K chunk.
+static int mvf_warps(const pb_qmat* w, int ntiles, int sm_count) {
+  const int KC = (w->nb + 31) / 32;
+  int W = 4;
+  while (W < MVF_MAX_WARPS && (int64_t)ntiles * KC / W >= 2 * sm_count) W *= 2;
+  while (W < KC) W *= 2;
+  return W;
+}
+
+static int launch_mvf(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int tile_begin, int ntiles,
+                      int row_end, const pb_mv_epi& epi) {
+  const int KC = (w->nb + 31) / 32;
+  const int W = mvf_warps(w, ntiles, ctx->sm_count), TPC = W / KC;
+  const int groups = (ntiles + TPC - 1) / TPC;
+  const int cap = ctx->sm_count * (MVF_MAX_WARPS / W);  // CTAs resident at once (registers)
+  const int grid = groups < cap ? groups : cap;
+  const size_t smem = (size_t)w->K * 4 + (size_t)2 * TPC * KC * 8 * 4;
+  return pb_launch(ctx, "k_mvf", true, k_mvf, dim3(grid), dim3(W * 32), smem, (const uint8_t*)w->qs,
+                   (const uint16_t*)w->d, w->N, w->nb, tile_begin, tile_begin + ntiles, row_end, x, y, epi,
+                   pb_magics{PB_MAG0, PB_MAG4, PB_MAG8, PB_MAG12, PB_MAG16}, ctx->d_err);
+}
+
 static size_t mvw_smem(const pb_qmat* w) {
   return (size_t)2 * mvw_slots(w->nb) * w->nb * 32 * 4 + (size_t)w->nb * 32 * 4;
 }
@@ -670,6 +896,8 @@ int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, in
   pb_mv_epi epi = epi_in ? *epi_in : pb_mv_epi();
   if (!y && epi.kind != PB_EPI_SWIGLU4) return PB_ERR_ARG;
   const int tile_begin = row0 / 8, ntiles = pb_cdiv(rows, 8);
+  if (w->type == PB_TYPE_Q4_0 && ctx->matvec_mode == PB_MATVEC_FAST && w->nb <= 32 * MVF_MAX_WARPS)
+    return launch_mvf(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
   if (w->type == PB_TYPE_Q4_0) return launch_mv<PB_TYPE_Q4_0>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
   return launch_mv<PB_TYPE_Q4_1>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
 }
@@ -692,7 +920,12 @@ static int host_matvec(pb_ctx* ctx, int type, const float* x, const uint8_t* raw
     e = cudaMemcpyAsync(dx, x, (size_t)K * 4, cudaMemcpyHostToDevice, ctx->stream);
     if (e != cudaSuccess) rc = pb_cuda_error(ctx, e, "upload x");
   }
-  if (rc == PB_OK) rc = pb_launch_matvec(ctx, m, dx, dy, 0, N, nullptr);
+  if (rc == PB_OK) {  // the module functions keep the reference's exact lane order
+    const int mode = ctx->matvec_mode;
+    ctx->matvec_mode = PB_MATVEC_EXACT;
+    rc = pb_launch_matvec(ctx, m, dx, dy, 0, N, nullptr);
+    ctx->matvec_mode = mode;
+  }
   if (rc == PB_OK) {
     e = cudaMemcpyAsync(y, dy, (size_t)N * 4, cudaMemcpyDeviceToHost, ctx->stream);
     if (e != cudaSuccess) rc = pb_cuda_error(ctx, e, "download y");
@@ -1234,5 +1467,7 @@ int pb_setup_q4_kernels(void) {
   e = e ? e : cudaFuncSetAttribute(k_head<PB_TYPE_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_head<PB_TYPE_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_head_f32_double, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  e = e ? e : cudaFuncSetAttribute(k_head_f32_bd, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  e = e ? e : cudaFuncSetAttribute(k_mvf, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
 }

@@ -102,8 +102,17 @@ def test_q4_0_matvec_special_scales(native, ctx, oracle):
     assert bits_equal(wasm_q4.q4_0_matvec(x, raw, N, K), oracle.q4_0_matvec(x, raw, N, K))
 
 
-def test_resident_matvec_row_split(native, ctx, oracle):
-    """Rows split like thread-pool.js:174-203 give the same bits as one call."""
+@pytest.fixture
+def exact_mode(native, ctx):
+    """The resident matvec in the reference's exact lane order for one test."""
+    ctx.set_matvec_mode(native.MATVEC_EXACT)
+    yield
+    ctx.set_matvec_mode(native.MATVEC_FAST)
+
+
+def test_resident_matvec_row_split(native, ctx, oracle, exact_mode):
+    """Rows split like thread-pool.js:174-203 give the same bits as one call,
+    and in the exact mode the reference's bits."""
     rng = np.random.default_rng(12)
     N, K = 1024, 2048
     raw = rand_q4_0(rng, N, K)
@@ -116,6 +125,67 @@ def test_resident_matvec_row_split(native, ctx, oracle):
     ctx.sync()
     assert bits_equal(dy.download(count=N), oracle.q4_0_matvec(x, raw, N, K))
     assert bits_equal(m.gguf_bytes(), raw)  # device layout round trip
+
+
+# the fast resident matvec: exact (q - 8) * x products summed with one FMA
+# per weight in another order; per-op bar of the north star is an f32
+# relative tolerance, this is far inside it
+RTOL_MATVEC_FAST = 2e-6
+
+
+@pytest.mark.parametrize("N,K", [(64, 64), (136, 576), (512, 1536), (3072, 2048), (2048, 8192), (16384, 2048),
+                                 (1000, 4096), (40, 16384)])
+def test_fast_matvec_shapes(native, ctx, oracle, N, K):
+    """Every decode shape of configs[2]/[3] and ragged ones (N not a multiple
+    of 8, K with a partial last 32-block chunk): within RTOL_MATVEC_FAST of
+    the reference's lane order, and row splits give the same bits as one call."""
+    assert ctx.matvec_mode == native.MATVEC_FAST
+    rng = np.random.default_rng(N * 7 + K)
+    raw = rand_q4_0(rng, N, K)
+    x = rng.standard_normal(K).astype(f32)
+    m = native.QMat(ctx, native.TYPE_Q4_0, raw, N, K)
+    dx, dy, dz = dev(ctx, x), out(ctx, N), out(ctx, N)
+    L = native.lib()
+    ctx._check(L.pb_qmat_matvec(ctx.h, m.h, dx.ptr, dy.ptr, 0, 0))
+    y = dy.download(count=N)
+    assert close(y, oracle.q4_0_matvec(x, raw, N, K), RTOL_MATVEC_FAST)
+    step = max(8, (N // 3) // 8 * 8)
+    for r0 in range(0, N, step):
+        ctx._check(L.pb_qmat_matvec(ctx.h, m.h, dx.ptr, dz.ptr, r0, min(step, N - r0)))
+    assert bits_equal(dz.download(count=N), y)
+
+
+def test_fast_matvec_special_scales(native, ctx, oracle):
+    """Zero, -0, subnormal (decoded as 0 the WASM way) and exponent-31 scales."""
+    rng = np.random.default_rng(14)
+    N, K = 64, 512
+    raw = rand_q4_0(rng, N, K)
+    blk = raw.reshape(-1, 18)
+    for i, bits in enumerate([0x0000, 0x8000, 0x0001, 0x83FF, 0x7C00, 0xFBFF]):
+        blk[i * 7, 0], blk[i * 7, 1] = bits & 0xFF, bits >> 8
+    x = rng.standard_normal(K).astype(f32)
+    m = native.QMat(ctx, native.TYPE_Q4_0, raw, N, K)
+    dx, dy = dev(ctx, x), out(ctx, N)
+    ctx._check(native.lib().pb_qmat_matvec(ctx.h, m.h, dx.ptr, dy.ptr, 0, 0))
+    assert close(dy.download(count=N), oracle.q4_0_matvec(x, raw, N, K), RTOL_MATVEC_FAST)
+
+
+def test_matvec_mode_switch(native, ctx, oracle):
+    rng = np.random.default_rng(15)
+    N, K = 256, 2048
+    raw = rand_q4_0(rng, N, K)
+    x = rng.standard_normal(K).astype(f32)
+    m = native.QMat(ctx, native.TYPE_Q4_0, raw, N, K)
+    dx, dy = dev(ctx, x), out(ctx, N)
+    L = native.lib()
+    want = oracle.q4_0_matvec(x, raw, N, K)
+    for mode in (native.MATVEC_EXACT, native.MATVEC_FAST, native.MATVEC_EXACT):
+        ctx.set_matvec_mode(mode)
+        ctx._check(L.pb_qmat_matvec(ctx.h, m.h, dx.ptr, dy.ptr, 0, 0))
+        got = dy.download(count=N)
+        assert bits_equal(got, want) if mode == native.MATVEC_EXACT else close(got, want, RTOL_MATVEC_FAST)
+    ctx.set_matvec_mode(native.MATVEC_FAST)
+    assert L.pb_set_matvec_mode(ctx.h, 7) == native.PB_ERR_ARG
 
 
 def test_matvec_rejects_bad_rows(native, ctx):
@@ -411,12 +481,15 @@ def test_capture_replay(native, ctx, oracle):
     dx, dy = dev(ctx, x), out(ctx, N)
     L = native.lib()
     ctx.sync()
+    ctx._check(L.pb_qmat_matvec(ctx.h, m.h, dx.ptr, dy.ptr, 0, 0))
+    direct = dy.download(count=N)
     g = ctx.capture(lambda: ctx._check(L.pb_qmat_matvec(ctx.h, m.h, dx.ptr, dy.ptr, 0, 0)))
     ctx._check(L.pb_memset(ctx.h, dy.ptr, 0, N * 4))
     g.launch()
     g.launch()
     ctx.sync()
-    assert bits_equal(dy.download(count=N), oracle.q4_0_matvec(x, raw, N, K))
+    assert bits_equal(dy.download(count=N), direct)
+    assert close(direct, oracle.q4_0_matvec(x, raw, N, K), 2e-6)
     g.free()
     # a blocking call while recording is refused, and the context stays usable
     ctx._check(L.pb_capture_begin(ctx.h))

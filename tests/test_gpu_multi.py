@@ -40,6 +40,7 @@ def _rank(rank, world, port, n, k, outdir):
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=timedelta(seconds=60))
     ctx = N.Context(rank)
+    ctx.set_matvec_mode(N.MATVEC_EXACT)  # the row split against the reference's bits
     try:
         x, raw = _case(n, k, 3)
         rs = RowSplitMatvec(ctx, raw, N.TYPE_Q4_0, n, k)
