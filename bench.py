@@ -437,18 +437,16 @@ def run_ours(args, rank, world, torch, dist):
             "vs_baseline": None,
             "dtype": "u4 weights, f32 math (f64 for the reference's double ops)",
             "data": "synthetic (seeded N(0,0.02) weights, seeded prompt tokens)",
-            "config": {"workload": WORKLOAD, "model": "llama3.2-1B-shape", "global_batch": world, "seq_len": MAX_POS,
-                       "prompt": PROMPT, "parallelism": f"replicas{world}" if world > 1 else "single-gpu",
-                       "l2": "weights 695 MB per step > 126 MB L2 (no flush needed)"},
+            "config": config_line(world),
             "decode_step": {"bytes": step_bytes, "GBps": round(step_gbs, 1), "frac_of_hbm": round(step_gbs / peak, 3),
                             "launches": launches_per_step},
-            "roofline": {"bound": "hbm", "kernel": "k_matvec (Q4_0, WASM lane order)",
+            "roofline": {"bound": "hbm", "kernel": "k_mvf (Q4_0, fast decode matvec)",
                          "achieved": round(mv_agg, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(mv_agg / peak, 3),
                          "traffic": int(round(mv_bytes_avg * MV_DRAM_OVER_ALG)),
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gate-up launch "
-                                           "(16384x2048: 18948864 B against 18948096 algorithmic), scaled per launch; "
-                                           "profiles/k_matvec_gate_up_16384x2048.md",
+                                           f"(16384x2048), as a ratio to its algorithmic bytes ({MV_DRAM_OVER_ALG:.6f}) "
+                                           "times the bytes per launch",
                          "bytes_per_launch": int(mv_bytes_avg), "per_shape": mv},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
@@ -461,74 +459,97 @@ def run_ours(args, rank, world, torch, dist):
         if batched:
             result["batched"] = batched
         if world == 1 and not args.no_cpu_baseline:
-            result["cpu_baseline"] = cpu_baseline(rt, sample_tokens=2)
+            result["cpu_baseline"] = cpu_baseline(rt, prompt)
     rt.shutdown()
     ctx.close()
     return result
 
 
-def copy_to_oracle(rt):
-    """Oracle model holding the device's weights (same bits)."""
+def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    return O
+
+
+def oracle_prompt(O):
+    """The same seeded prompt as prompt_tokens() (one shared generator, pb_synth.h)."""
+    return O.synth_tokens(PROMPT, SEED, 1, CFG["vocab"]).tolist()
+
+
+def config_line(world):
+    return {"workload": WORKLOAD, "model": "llama3.2-1B-shape", "global_batch": world, "seq_len": MAX_POS,
+            "prompt": PROMPT, "parallelism": f"replicas{world}" if world > 1 else "single-gpu",
+            "rope_scaling": "off (the reference applies none)",
+            "l2": "weights 695 MB per step > 126 MB L2 (no flush needed)"}
+
+
+def cpu_baseline(rt, prompt, sample_tokens=32):
+    """The oracle (C restatement of the reference's decode, thread-pool.js row
+    split over every host thread) on the same model and the same workload
+    position: the device prefills the prompt, its weights and KV cache are
+    copied into the oracle, and `sample_tokens` greedy decode tokens from
+    position PROMPT are timed."""
+    O = _oracle()
+    rt.resetCache()
+    tok = O.argmax(rt.forward(prompt, 0)["logits"])
     om = O.Model(O.Config(**CFG))
     for w in range(8):
         for l in (range(CFG["n_layers"]) if w else [0]):
             om.tensor(l, w)[:] = rt.getTensor(l, w)
     om.refresh()
-    return O, om
-
-
-def cpu_baseline(rt, sample_tokens=2):
-    O, om = copy_to_oracle(rt)
+    for l in range(CFG["n_layers"]):
+        for v in (0, 1):
+            om.kv(l, v)[:PROMPT] = rt.model.kv(l, v)[:PROMPT]
     threads = os.cpu_count() or 1
     O.set_threads(threads)
-    om.forward([1], 0)  # warm
     t0 = time.perf_counter()
-    tok = 1
-    for i in range(sample_tokens):
-        lg = om.forward([tok], 1 + i)
-        tok = O.argmax(lg)
+    pos = PROMPT
+    for _ in range(sample_tokens):
+        tok = O.argmax(om.forward([tok], pos))
+        pos += 1
     dt = time.perf_counter() - t0
     return {"value": round(sample_tokens / dt, 4), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{sample_tokens} decode tokens of the same model at positions 1-{sample_tokens} "
-                      f"(oracle/pb_oracle.c, WASM-order Q4 matvec, {threads} threads row split)"}
+            "sample": f"{sample_tokens} greedy decode tokens at positions {PROMPT}-{PROMPT + sample_tokens - 1} after "
+                      f"the same {PROMPT}-token prompt, same weights (oracle/pb_oracle.c: WASM-order Q4 matvecs, "
+                      f"batch_dot head, double attention; {threads} threads row split as thread-pool.js)"}
 
 
 def run_reference(args):
-    """The reference algorithm on the host cores (C restatement; no JS engine)."""
-    from purebee_b200 import _native as N
-    ctx = N.Context(int(os.environ.get("LOCAL_RANK", 0)))
-    rt = build_model(ctx)
-    O, om = copy_to_oracle(rt)
-    rt.shutdown()
-    ctx.close()
+    """The reference algorithm on the host cores, on the same workload as the
+    GPU arm: the oracle (C restatement; the JavaScript reference has no engine
+    in this image) builds the same seeded weights with its own generator
+    (bit-identical to the device's), prefills the same 128-token prompt
+    (untimed), then decodes W warm-up and K timed greedy tokens from position
+    128, wrapping at 640 like the GPU arm.  Nothing of the product is loaded."""
+    O = _oracle()
     threads = os.cpu_count() or 1
     O.set_threads(threads)
-    prompt = prompt_tokens()[:8]
-    om.forward(prompt, 0)
-    pos = len(prompt)
-    tok = 1
-    # bounded: each timed step is one decode token; cap the count so the run
-    # stays within a few minutes
-    steps = min(args.steps, args.ref_max_steps)
-    warm = min(args.warmup, 1)
-    for _ in range(warm):
-        tok = O.argmax(om.forward([tok], pos))
-        pos += 1
+    om = O.Model(O.Config(**CFG))
+    om.init_synthetic(SEED)
+    prompt = oracle_prompt(O)
+    tok = O.argmax(om.forward(prompt, 0))
+    pos = PROMPT
+
+    def step(tok, pos):
+        if pos >= MAX_POS:
+            pos = PROMPT
+        return O.argmax(om.forward([tok], pos)), pos + 1
+
+    for _ in range(args.warmup):
+        tok, pos = step(tok, pos)
     t0 = time.perf_counter()
-    for _ in range(steps):
-        tok = O.argmax(om.forward([tok], pos))
-        pos += 1
+    for _ in range(args.steps):
+        tok, pos = step(tok, pos)
     dt = time.perf_counter() - t0
-    v = steps / dt
-    return {"metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": 0, "steps": steps,
-            "requested_steps": args.steps, "warmup": warm, "ms_per_step": round(dt / steps * 1e3, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (reference lane order)",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD, "model": "llama3.2-1B-shape", "global_batch": 1, "seq_len": MAX_POS},
+    v = args.steps / dt
+    return {"metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": 0, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (reference lane order), f64 reductions",
+            "data": "synthetic (seeded N(0,0.02) weights, seeded prompt tokens)", "impl": "reference",
+            "config": config_line(1),
             "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port",
-                             "sample": f"{steps} decode tokens after an 8-token prefill (oracle/pb_oracle.c; the "
+                             "sample": f"{args.steps} greedy decode tokens from position {PROMPT} after the same "
+                                       f"{PROMPT}-token prompt (oracle/pb_oracle.c, {threads} threads; the "
                                        f"JavaScript reference has no engine in this image)"},
             "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -600,7 +621,6 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--ref-max-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched configuration (configs[4])")
     ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK, head:VxD, gemm:MxNxK, or batched:BxP (batched prefill + 3 steps)")

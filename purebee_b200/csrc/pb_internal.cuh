@@ -266,6 +266,7 @@ __device__ __forceinline__ double pb_block_sum_d(double v, double* red) {
 #define PB_EPI_RESIDUAL 1  // y[row] = residual[row] + v   (llama-streaming.js:579-580, 601)
 #define PB_EPI_ROPE_KV 2   // rows [q | k | v]: RoPE q, k; k, v into the cache at pos (:531-541)
 #define PB_EPI_SWIGLU4 3   // tiles [g_4i..g_4i+3 | u_4i..u_4i+3]: h_i = silu(g_i)*u_i (:590-595)
+#define PB_EPI_ARGMAX 4    // logits y[row] = v and the greedy key atomicMax (:899-909)
 
 #define PB_MAX_L2_NEXT 4
 struct pb_mv_epi {
@@ -283,6 +284,7 @@ struct pb_mv_epi {
   float* kc = nullptr;
   float* vc = nullptr;
   float* h_out = nullptr;
+  unsigned long long* amax = nullptr;  // PB_EPI_ARGMAX
 };
 
 // Per-sequence strides (floats) of batched attention launches: blockIdx.z is
@@ -351,6 +353,8 @@ int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, in
                      const pb_mv_epi* epi);
 int pb_launch_head(pb_ctx* ctx, const pb_qmat* emb, const float* h, float* logits,
                    unsigned long long* argmax_key, int mode);
+int pb_launch_head_fast(pb_ctx* ctx, const pb_qmat* t, const float* h, const float* norm_w, double eps, float* logits,
+                        unsigned long long* amax);
 int pb_launch_head_norm(pb_ctx* ctx, const pb_qmat* emb, const float* h, const float* norm_w, double eps,
                         float* logits, unsigned long long* argmax_key, int mode);
 int pb_launch_argmax_finish(pb_ctx* ctx, const unsigned long long* key, int* idx);

@@ -723,6 +723,8 @@ static int launch_embed(pb_model* m, const int* toks, int M) {
 static int launch_head(pb_model* m, const float* last_x) {
   int mode = 0;
   const pb_qmat* t = head_table(m, &mode);
+  if (mode == 0 && m->ctx->matvec_mode == PB_MATVEC_FAST)
+    return pb_launch_head_fast(m->ctx, t, last_x, m->rms_final, m->c.eps, m->logits, m->key);
   return pb_launch_head_norm(m->ctx, t, last_x, m->rms_final, m->c.eps, m->logits, m->key, mode);
 }
 

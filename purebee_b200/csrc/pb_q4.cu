@@ -390,6 +390,15 @@ __device__ __forceinline__ void mv_epilogue(float v, int tile, int N, int row_en
         epi.vc[(size_t)pos * kvd + (row - epi.q_rows - kvd)] = v;
       }
     }
+  } else if (epi.kind == PB_EPI_ARGMAX) {  // logits and the greedy key (llama-streaming.js:899-909)
+    if (live) y[row] = v;
+    unsigned long long key = live ? pb_argmax_key(v, row) : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
+      key = t > key ? t : key;
+    }
+    if (lane == 0 && key) atomicMax(epi.amax, key);
   } else {  // PB_EPI_SWIGLU4: rows 0-3 gate, 4-7 up of indices 4*tile .. 4*tile+3
     const float u = __shfl_sync(0xffffffffu, v, (lane + 16) & 31);
     if (L == 0 && rr < 4 && row < N) {
@@ -677,6 +686,27 @@ __device__ __forceinline__ float q4_0_block_fast(uint4 p, const uint64_t (&xp)[1
   return __fadd_rn(s.x, s.y);
 }
 
+// Q8_0 block (gguf.js:239-257): byte j is element j; a byte becomes the
+// exact float 2^15 + (q + 128) by one byte permute with the exponent
+// pattern (q biased by 128 first), a packed add removes 2^15 + 128.
+__device__ __forceinline__ float q8_0_block_fast(uint4 p0, uint4 p1, const uint64_t (&xp)[16]) {
+  const uint64_t c = p2(-32896.0f, -32896.0f);
+  uint64_t a = 0, b = 0;
+  const uint32_t wv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t u = wv[i] ^ 0x80808080u;
+    const uint64_t e01 = p2add(p2(__uint_as_float(__byte_perm(u, PB_MAG8, 0x7504)),
+                                  __uint_as_float(__byte_perm(u, PB_MAG8, 0x7514))), c);
+    const uint64_t e23 = p2add(p2(__uint_as_float(__byte_perm(u, PB_MAG8, 0x7524)),
+                                  __uint_as_float(__byte_perm(u, PB_MAG8, 0x7534))), c);
+    a = p2fma(e01, xp[2 * i], a);
+    b = p2fma(e23, xp[2 * i + 1], b);
+  }
+  const float2 s = up2(p2add(a, b));
+  return __fadd_rn(s.x, s.y);
+}
+
 // x (RMS-normalised when w is set) into shared memory, float4 chunks
 // swizzled within each 32-value block (bank-conflict-free reads of one block
 // per lane).  Any K: the threads loop over the chunks.
@@ -719,9 +749,14 @@ __device__ __forceinline__ void mvf_stage_x(const float* __restrict__ x, const f
 }
 
 // CTA of W warps = TPC tiles x KC chunks per iteration (TPC = W / KC).
+// TYPE Q4_0 or Q8_0; LAYOUT ROWS (matvec weights) or TILED8 (a head table:
+// block b of the tile's 8 rows is 8 consecutive slots, so a lane's 8 rows
+// share 128-byte lines and the loads go through L1).
+template <int TYPE, int LAYOUT>
 __global__ void __launch_bounds__(MVF_MAX_WARPS * 32, 1)
 k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, int nb, int tile_begin, int tile_end,
       int row_end, const float* __restrict__ x, float* __restrict__ y, pb_mv_epi epi, pb_magics M, int* err) {
+  constexpr int QB = TYPE == PB_TYPE_Q8_0 ? 32 : 16;  // payload bytes per block
   extern __shared__ __align__(16) unsigned char mvf_raw[];
   __shared__ double red[MVF_MAX_WARPS];
   const int K = nb * 32, KC = (nb + 31) >> 5, W = blockDim.x >> 5, TPC = W / KC;
@@ -735,7 +770,7 @@ k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, i
   const int per_iter = gridDim.x * TPC;
   const int n_iter = (tile_end - tile_begin + per_iter - 1) / per_iter;  // CTA-uniform
   const uint4* q4 = reinterpret_cast<const uint4*>(qs);
-  const size_t tq = (size_t)8 * nb * 16, td = (size_t)8 * nb * 2;
+  const size_t tq = (size_t)8 * nb * QB, td = (size_t)8 * nb * 2;
   auto tile_of = [&](int it) { return tile_begin + it * per_iter + blockIdx.x * TPC + tl; };
   // L2 prefetch: the chunk-0 warp of each tile slot fetches its tile (payload
   // and scales are contiguous per tile) MVF_PF iterations ahead
@@ -750,16 +785,18 @@ k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, i
   if (tid == 0)
     for (int i = 0; i < PB_MAX_L2_NEXT; ++i) pb_l2_prefetch_share(epi.l2_next[i], epi.l2_next_bytes[i], blockIdx.x, gridDim.x);
   // the first tile's blocks (weights do not depend on the previous kernel)
-  uint4 pq[8];
+  constexpr int PL = QB / 16;  // uint4 per block payload
+  uint4 pq[8][PL];
   uint32_t pd[8];
   auto load = [&](int it) {
     const int t = tile_of(it);
     if (has_b && it < n_iter && t < tile_end) {
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
-        const size_t slot = (size_t)(t * 8 + r) * nb + b;
-        pq[r] = __ldcs(q4 + slot);
-        pd[r] = __ldcs(dsc + slot);
+        const size_t slot = LAYOUT == PB_LAYOUT_TILED8 ? ((size_t)t * nb + b) * 8 + r : (size_t)(t * 8 + r) * nb + b;
+#pragma unroll
+        for (int u = 0; u < PL; ++u) pq[r][u] = LAYOUT == PB_LAYOUT_TILED8 ? q4[slot * PL + u] : __ldcs(q4 + slot * PL + u);
+        pd[r] = LAYOUT == PB_LAYOUT_TILED8 ? dsc[slot] : __ldcs(dsc + slot);
       }
     }
   };
@@ -785,7 +822,15 @@ k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, i
     for (int r = 0; r < 8; ++r) v[r] = 0.0f;
     if (has_b && t < tile_end) {
 #pragma unroll
-      for (int r = 0; r < 8; ++r) v[r] = __fmul_rn(q4_0_block_fast(pq[r], xp, M), pb_f16_wasm(pd[r]));
+      for (int r = 0; r < 8; ++r) {
+        // the scale as the kernel being replaced decodes it: the WASM matvec's
+        // (wasm-q4.js:88-109) for matvec weights, the exact one of the table
+        // the reference's head reads (gguf.js:55-70)
+        const float d = LAYOUT == PB_LAYOUT_TILED8 ? pb_f16_exact(pd[r]) : pb_f16_wasm(pd[r]);
+        const float bs = TYPE == PB_TYPE_Q8_0 ? q8_0_block_fast(pq[r][0], pq[r][PL - 1], xp)
+                                              : q4_0_block_fast(pq[r][0], xp, M);
+        v[r] = __fmul_rn(bs, d);
+      }
     }
     load(it + 1);
     // transposed butterfly over the lanes: lane 4r ends with row r's sum
@@ -840,9 +885,27 @@ static int launch_mvf(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, i
   const int cap = ctx->sm_count * (MVF_MAX_WARPS / W);  // CTAs resident at once (registers)
   const int grid = groups < cap ? groups : cap;
   const size_t smem = (size_t)w->K * 4 + (size_t)2 * TPC * KC * 8 * 4;
-  return pb_launch(ctx, "k_mvf", true, k_mvf, dim3(grid), dim3(W * 32), smem, (const uint8_t*)w->qs,
+  auto kern = w->type == PB_TYPE_Q8_0
+                  ? (w->layout == PB_LAYOUT_TILED8 ? k_mvf<PB_TYPE_Q8_0, PB_LAYOUT_TILED8> : k_mvf<PB_TYPE_Q8_0, PB_LAYOUT_ROWS>)
+                  : (w->layout == PB_LAYOUT_TILED8 ? k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_TILED8> : k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS>);
+  return pb_launch(ctx, "k_mvf", true, kern, dim3(grid), dim3(W * 32), smem, (const uint8_t*)w->qs,
                    (const uint16_t*)w->d, w->N, w->nb, tile_begin, tile_begin + ntiles, row_end, x, y, epi,
                    pb_magics{PB_MAG0, PB_MAG4, PB_MAG8, PB_MAG12, PB_MAG16}, ctx->d_err);
+}
+
+// The LM head in the fast mode: the fast kernel over the head table (Q4_0 /
+// Q8_0, either layout) with the final RMSNorm prologue and the logits +
+// greedy argmax epilogue.  The exact kernel (k_head) keeps batch_dot's order.
+int pb_launch_head_fast(pb_ctx* ctx, const pb_qmat* t, const float* h, const float* norm_w, double eps, float* logits,
+                        unsigned long long* amax) {
+  if ((t->type != PB_TYPE_Q4_0 && t->type != PB_TYPE_Q8_0) || t->nb > 32 * MVF_MAX_WARPS)
+    return pb_set_error(ctx, PB_ERR_ARG, "fast head: Q4_0 or Q8_0 table, K <= %d", 32 * 32 * MVF_MAX_WARPS);
+  pb_mv_epi e;
+  e.kind = amax ? PB_EPI_ARGMAX : PB_EPI_STORE;
+  e.norm_w = norm_w;
+  e.eps = eps;
+  e.amax = amax;
+  return launch_mvf(ctx, t, h, logits, 0, (t->N + 7) / 8, t->N, e);
 }
 
 static size_t mvw_smem(const pb_qmat* w) {
@@ -1468,6 +1531,9 @@ int pb_setup_q4_kernels(void) {
   e = e ? e : cudaFuncSetAttribute(k_head<PB_TYPE_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_head_f32_double, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_head_f32_bd, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  e = e ? e : cudaFuncSetAttribute(k_mvf, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_TILED8>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q8_0, PB_LAYOUT_ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q8_0, PB_LAYOUT_TILED8>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
 }

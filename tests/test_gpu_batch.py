@@ -60,6 +60,47 @@ def test_batch_matches_single_sequence(native, ctx, n_seqs, n_prompt, hd, dim):
     rt.shutdown()
 
 
+def test_batch_llama1b_shape(native, ctx):
+    """configs[4] at its real shape: Llama-3.2-1B-shaped weights (N(0, 0.02),
+    Q4_0), 4 sequences of 512-token prompts (the prefill GEMMs take the same
+    persistent TMA path as 64 x 512, the decode steps the decode-size GEMM),
+    then teacher-forced decode steps; every sequence's logits against the
+    one-sequence exact path.  The relative error is printed."""
+    from purebee_b200.runtime import BatchedLlamaRuntime, LlamaConfig, StreamingLlamaRuntime
+    cfg = LlamaConfig(dim=2048, hiddenDim=8192, nLayers=16, nHeads=32, nKvHeads=8, vocabSize=128256, seqLen=640,
+                      headDim=64, ropeTheta=500000.0)
+    rt = StreamingLlamaRuntime(cfg, ctx=ctx, emb_type=native.TYPE_Q4_0)
+    rt.loadSynthetic(20261201, 0.02)
+    n_seqs, n_prompt = 4, 512
+    prompts = np.random.default_rng(9).integers(1, cfg.vocabSize, (n_seqs, n_prompt)).astype(np.int32)
+    bt = BatchedLlamaRuntime(rt, n_seqs)
+    nxt, lg = bt.prefill(prompts, want_logits=True)
+    errs = []
+    for s in range(n_seqs):
+        rt.resetCache()
+        want = rt.forward(prompts[s].tolist(), 0)["logits"]
+        ok, err = close(lg[s], want)
+        errs.append(err)
+        assert ok, f"prefill seq {s}: rel err {err:.2e}"
+    fed = [nxt.copy()]
+    for step in range(3):
+        toks, lgd = bt.decode(1, want_logits=True)
+        for s in range(n_seqs):
+            rt.resetCache()
+            rt.forward(prompts[s].tolist(), 0)
+            for i, t in enumerate(fed[:-1]):
+                rt.forward([int(t[s])], n_prompt + i)
+            want = rt.forward([int(fed[-1][s])], n_prompt + len(fed) - 1)["logits"]
+            ok, err = close(lgd[s], want)
+            errs.append(err)
+            assert ok, f"decode step {step} seq {s}: rel err {err:.2e}"
+        fed.append(toks[0].copy())
+    print(f"\n[batched parity] llama1B shape {n_seqs}x{n_prompt}: max rel logit err prefill "
+          f"{max(errs[:n_seqs]):.3e}, decode {max(errs[n_seqs:]):.3e}")
+    bt.free()
+    rt.shutdown()
+
+
 def test_batch_rejects(native, ctx):
     from purebee_b200.runtime import BatchedLlamaRuntime
     rt = make(native, ctx)
