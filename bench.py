@@ -214,11 +214,12 @@ def matvec_roofline(ctx, torch, stream, peak, reps=200):
 
 def row_split_vocab(ctx, torch, dist, world, peak, reps=40):
     """Config 2's vocab-head matvec (128256 x 2048 Q4_0) split by rows over the
-    ranks (thread-pool.js's row split, one GPU per worker) with the NCCL
-    all-gather of the y slices.  Each rank rotates over weight copies larger
-    than 4x L2 in total.  Times are device event times, max over ranks."""
+    ranks (thread-pool.js's row split, one GPU per worker) with the library's
+    NCCL all-gather of the y slices (pb_comm_allgather).  Each rank rotates
+    over weight copies larger than 4x L2 in total.  Times are device event
+    times on the library stream, max over ranks."""
     from purebee_b200 import _native as N
-    from purebee_b200.thread_pool import RowSplitMatvec, rows_per_rank
+    from purebee_b200.thread_pool import NcclComm, RowSplitMatvec, rows_per_rank
     n, k = 128256, 2048
     rng = np.random.default_rng(11)
     raw = rng.integers(0, 256, n * (k // 32) * 18, dtype=np.uint8)
@@ -227,15 +228,16 @@ def row_split_vocab(ctx, torch, dist, world, peak, reps=40):
     per = rows_per_rank(n, world)
     slice_bytes = per * (k // 32) * 18
     copies = max(2, int(np.ceil(4 * 126e6 / slice_bytes)))
-    mats = [RowSplitMatvec(ctx, raw, N.TYPE_Q4_0, n, k) for _ in range(copies)]
-    dev = mats[0].y_local.device
-    x = torch.randn(k, device=dev, dtype=torch.float32)
-    stream = mats[0].stream
+    comm = NcclComm.from_torch(ctx)
+    mats = [RowSplitMatvec(ctx, raw, N.TYPE_Q4_0, n, k, comm) for _ in range(copies)]
+    dev = torch.device("cuda", ctx.device)
+    x = ctx.to_device(rng.standard_normal(k).astype(np.float32))
+    stream = torch.cuda.ExternalStream(N.lib().pb_stream(ctx.h), device=dev)
 
     def timed(fn):
         for i in range(3):
             fn(i)
-        torch.cuda.synchronize(dev)
+        ctx.sync()
         dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -247,11 +249,12 @@ def row_split_vocab(ctx, torch, dist, world, peak, reps=40):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    stream.wait_stream(torch.cuda.current_stream(dev))
-    local_us = timed(lambda i: mats[i % copies].local(x))
-    full_us = timed(lambda i: mats[i % copies].matvec(x))
+    local_us = timed(lambda i: mats[i % copies].local(x.ptr))
+    full_us = timed(lambda i: mats[i % copies].matvec(x.ptr))
+    ctx.sync()
     for m in mats:
         m.free()
+    comm.free()
     alg = n * k // 32 * 18 + 4 * k + 4 * n
     return {"shape": "128256x2048 Q4_0 (vocab head)", "gpus": world, "rows_per_gpu": per, "copies_per_gpu": copies,
             "local_us": round(local_us, 3),
@@ -259,7 +262,8 @@ def row_split_vocab(ctx, torch, dist, world, peak, reps=40):
             "aggregate_GBps_local": round(alg / (local_us * 1e-6) / 1e9, 1),
             "with_allgather_us": round(full_us, 3),
             "aggregate_GBps_with_allgather": round(alg / (full_us * 1e-6) / 1e9, 1),
-            "frac_local_of_measured_peak_per_gpu": round((slice_bytes + 4 * k + 4 * per) / (local_us * 1e-6) / 1e9 / peak, 3)}
+            "frac_local_of_measured_peak_per_gpu": round((slice_bytes + 4 * k + 4 * per) / (local_us * 1e-6) / 1e9 / peak, 3),
+            "allgather": "pb_comm_allgather (NCCL, library stream)"}
 
 
 def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512, steps=256, dist=None):

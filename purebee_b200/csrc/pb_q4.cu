@@ -951,16 +951,17 @@ int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, in
   if (w->layout != PB_LAYOUT_ROWS)
     return pb_set_error(ctx, PB_ERR_ARG, "matrix was uploaded as a head table (PB_QMAT_TABLE); the matvec needs the "
                                          "row layout");
-  if (w->nb > MV_THREADS / 2)
-    return pb_set_error(ctx, PB_ERR_ARG, "K=%d exceeds the %d the matvec kernel supports", w->K, MV_THREADS * 16);
+  const bool fast = w->type == PB_TYPE_Q4_0 && ctx->matvec_mode == PB_MATVEC_FAST;
+  if (w->nb > (fast ? 32 * MVF_MAX_WARPS : MV_THREADS / 2))
+    return pb_set_error(ctx, PB_ERR_ARG, "K=%d exceeds the %d the matvec kernel supports", w->K,
+                        fast ? 1024 * MVF_MAX_WARPS : MV_THREADS * 16);
   if (rows <= 0) { row0 = 0; rows = w->N; }
   if (row0 < 0 || row0 + rows > w->N || (row0 & 7))
     return pb_set_error(ctx, PB_ERR_ARG, "row range [%d, %d) invalid (start must be a multiple of 8)", row0, row0 + rows);
   pb_mv_epi epi = epi_in ? *epi_in : pb_mv_epi();
   if (!y && epi.kind != PB_EPI_SWIGLU4) return PB_ERR_ARG;
   const int tile_begin = row0 / 8, ntiles = pb_cdiv(rows, 8);
-  if (w->type == PB_TYPE_Q4_0 && ctx->matvec_mode == PB_MATVEC_FAST && w->nb <= 32 * MVF_MAX_WARPS)
-    return launch_mvf(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
+  if (fast) return launch_mvf(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
   if (w->type == PB_TYPE_Q4_0) return launch_mv<PB_TYPE_Q4_0>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
   return launch_mv<PB_TYPE_Q4_1>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
 }

@@ -4,10 +4,11 @@ thread-pool.js's AtomicsThreadPool (thread-pool.js:57-345).
 The reference splits the rows of every matvec over worker threads
 (thread-pool.js:165-246: rowsPerThread = floor(N / T), the remainder to the
 first workers, the main thread takes the tail) and copies the per-thread row
-slices back into one output.  Here the workers are GPUs, one process per GPU
-(torch.distributed over NCCL): each rank keeps a contiguous slice of the rows
-resident on its device, computes it with the CUDA matvec, and an all-gather
-assembles y on every rank.  A row's result does not depend on which rows
+slices back into one output.  Here the workers are GPUs, one process per GPU:
+each rank keeps a contiguous slice of the rows resident on its device,
+computes it with the CUDA matvec, and the library's NCCL all-gather
+(pb_comm_allgather) assembles y on every rank.  torch.distributed only
+carries the communicator's unique id between the processes.  A row's result does not depend on which rows
 share its launch, so the gathered y has the same bits as a one-device matvec.
 
 Slices are whole 8-row tiles (the device layout's unit) and all but the last
@@ -43,39 +44,34 @@ def rows_per_rank(n_rows: int, world: int) -> int:
     return hi - lo
 
 
-def gather_rows(y_local, n_rows: int, group=None):
-    """All-gather the ranks' padded slices (each rows_per_rank long, in rank
-    order) and return the first n_rows values: the full y on every rank.
-    Works for any torch.distributed backend (NCCL on GPUs, gloo in tests)."""
-    import torch
-    import torch.distributed as dist
-    world = dist.get_world_size(group)
+def assemble_rows(slices, n_rows: int) -> np.ndarray:
+    """The full y from the ranks' padded slices in rank order (what the
+    all-gather leaves in its receive buffer): their concatenation cut to
+    n_rows.  Host-side statement of the layout the device gather produces."""
+    world = len(slices)
     per = rows_per_rank(n_rows, world)
-    if y_local.numel() != per:
-        raise ValueError(f"local slice has {y_local.numel()} values, expected {per}")
-    out = torch.empty(world * per, dtype=y_local.dtype, device=y_local.device)
-    dist.all_gather_into_tensor(out, y_local.contiguous(), group=group)
-    return out[:n_rows]
+    flat = np.concatenate([np.asarray(s, np.float32).reshape(-1)[:per] for s in slices])
+    return flat[:n_rows]
 
 
 class RowSplitMatvec:
-    """One Q4_0/Q4_1 matrix split by rows over the ranks of a process group.
+    """One Q4_0/Q4_1 matrix split by rows over the ranks of a communicator
+    (NcclComm: the library's pb_comm, one rank per process and GPU).
 
     `raw` is the whole matrix as GGUF bytes (row-major blocks, as the
-    reference's rawBuf); each rank uploads only its own rows.  `matvec(x)`
-    takes x on this rank's device and returns the full y (a torch tensor on
-    the same device) after the all-gather."""
+    reference's rawBuf); each rank uploads only its own rows.  `matvec(x_ptr)`
+    takes x (K floats) at a device address on this rank's device, runs the
+    rank's rows into its slice and all-gathers the slices with
+    pb_comm_allgather on the library stream; the first N floats of `y` are
+    the full result on every rank."""
 
-    def __init__(self, ctx: N_.Context, raw: np.ndarray, quant_type: int, n_rows: int, k: int, group=None):
-        import torch
-        import torch.distributed as dist
+    def __init__(self, ctx: N_.Context, raw: np.ndarray, quant_type: int, n_rows: int, k: int, comm):
         if quant_type not in _GGUF_BLOCK:
             raise ValueError("row-split matvec supports Q4_0 and Q4_1")
         if k % 32:
             raise ValueError("K must be a multiple of 32")
-        self.ctx, self.N, self.K, self.group = ctx, n_rows, k, group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        self.ctx, self.N, self.K, self.comm = ctx, n_rows, k, comm
+        self.rank, self.world = comm.rank, comm.world
         self.lo, self.hi = row_split(n_rows, self.world)[self.rank]
         self.per = rows_per_rank(n_rows, self.world)
         row_bytes = (k // 32) * _GGUF_BLOCK[quant_type]
@@ -85,34 +81,34 @@ class RowSplitMatvec:
         self.m = None
         if self.hi > self.lo:
             self.m = N_.QMat(ctx, quant_type, raw[self.lo * row_bytes:self.hi * row_bytes], self.hi - self.lo, k)
-        dev = torch.device("cuda", ctx.device)
-        self.y_local = torch.zeros(self.per, dtype=torch.float32, device=dev)
-        self.stream = torch.cuda.ExternalStream(N_.lib().pb_stream(ctx.h), device=dev)
+        self.y_local = ctx.alloc(self.per * 4)
+        self.y = ctx.alloc(self.world * self.per * 4)
+        ctx._check(N_.lib().pb_memset(ctx.h, self.y_local.ptr, 0, self.per * 4))
 
-    def local(self, x) -> None:
+    def local(self, x_ptr: int) -> None:
         """This rank's rows into y_local (enqueued on the library's stream)."""
         if self.m is not None:
-            self.ctx._check(N_.lib().pb_qmat_matvec(self.ctx.h, self.m.h, ctypes.c_void_p(x.data_ptr()),
-                                                    ctypes.c_void_p(self.y_local.data_ptr()), 0, 0))
+            self.ctx._check(N_.lib().pb_qmat_matvec(self.ctx.h, self.m.h, ctypes.c_void_p(x_ptr),
+                                                    ctypes.c_void_p(self.y_local.ptr), 0, 0))
 
-    def matvec(self, x):
-        """Full y on every rank: local rows, then the all-gather, both ordered
-        on the library's stream."""
-        import torch
-        if x.numel() != self.K or x.dtype != torch.float32 or not x.is_cuda:
-            raise ValueError("x must be a float32 CUDA tensor of K values")
-        caller = torch.cuda.current_stream(x.device)
-        self.stream.wait_stream(caller)  # x was produced on the caller's stream
-        with torch.cuda.stream(self.stream):
-            self.local(x)
-            y = gather_rows(self.y_local, self.N, self.group)
-        caller.wait_stream(self.stream)
-        return y
+    def gather(self) -> None:
+        """Every rank's slice into y (pb_comm_allgather, library stream)."""
+        self.comm.allgather(self.y_local.ptr, self.y.ptr, self.per * 4)
+
+    def matvec(self, x_ptr: int) -> N_.DeviceBuffer:
+        """Full y on every rank (device buffer; the first N floats), enqueued
+        on the library's stream: local rows, then the all-gather."""
+        self.local(x_ptr)
+        self.gather()
+        return self.y
 
     def free(self) -> None:
         if self.m is not None:
             self.m.free()
             self.m = None
+        for b in (getattr(self, "y_local", None), getattr(self, "y", None)):
+            if b is not None:
+                b.free()
 
 
 class AtomicsThreadPool:
@@ -121,20 +117,23 @@ class AtomicsThreadPool:
     reference, each call copies the weight slice in (here to the device); a
     runtime that keeps weights resident uses RowSplitMatvec instead."""
 
-    def __init__(self, ctx: N_.Context, group=None):
-        self.ctx, self.group = ctx, group
+    def __init__(self, ctx: N_.Context, comm):
+        self.ctx, self.comm = ctx, comm
 
     def matvec(self, x: np.ndarray, rawBuf: np.ndarray, quantType: int, N: int, K: int) -> np.ndarray:
-        import torch
-        rs = RowSplitMatvec(self.ctx, rawBuf, quantType, N, K, self.group)
+        rs = RowSplitMatvec(self.ctx, rawBuf, quantType, N, K, self.comm)
         try:
-            xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(rs.y_local.device)
-            torch.cuda.synchronize(rs.y_local.device)
-            y = rs.matvec(xd)
-            rs.stream.synchronize()
-            return y.cpu().numpy()
+            xd = self.ctx.to_device(np.ascontiguousarray(x, np.float32))
+            y = rs.matvec(xd.ptr)
+            out = y.download(np.float32, self.world_rows(rs))[:N]
+            xd.free()
+            return out
         finally:
             rs.free()
+
+    @staticmethod
+    def world_rows(rs: RowSplitMatvec) -> int:
+        return rs.world * rs.per
 
     def shutdown(self) -> None:
         pass

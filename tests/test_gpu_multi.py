@@ -1,6 +1,8 @@
 """Row-split matvec across GPUs (thread-pool.js:165-246 with GPUs as the
 workers): every rank's gathered y equals the one-device matvec bit for bit.
-One process per GPU over NCCL; the one-GPU case runs a world-size-1 group."""
+One process per GPU; the slices are all-gathered by the library's own NCCL
+communicator (pb_comm_allgather), torch.distributed only carries its id.
+The one-GPU case runs a world-size-1 communicator."""
 import os
 import socket
 
@@ -35,22 +37,27 @@ def _rank(rank, world, port, n, k, outdir):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, root)
     from purebee_b200 import _native as N
-    from purebee_b200.thread_pool import AtomicsThreadPool, RowSplitMatvec
+    from purebee_b200.thread_pool import AtomicsThreadPool, NcclComm, RowSplitMatvec
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=timedelta(seconds=60))
     ctx = N.Context(rank)
     ctx.set_matvec_mode(N.MATVEC_EXACT)  # the row split against the reference's bits
+    comm = None
     try:
+        comm = NcclComm.from_torch(ctx)
         x, raw = _case(n, k, 3)
-        rs = RowSplitMatvec(ctx, raw, N.TYPE_Q4_0, n, k)
-        y = rs.matvec(torch.from_numpy(x).cuda(rank))
-        np.save(os.path.join(outdir, f"y{rank}.npy"), y.cpu().numpy())
+        rs = RowSplitMatvec(ctx, raw, N.TYPE_Q4_0, n, k, comm)
+        xd = ctx.to_device(x)
+        y = rs.matvec(xd.ptr).download(np.float32, rs.world * rs.per)[:n]
+        np.save(os.path.join(outdir, f"y{rank}.npy"), y)
         rs.free()
-        y2 = AtomicsThreadPool(ctx).matvec(x, raw, N.TYPE_Q4_0, n, k)
+        y2 = AtomicsThreadPool(ctx, comm).matvec(x, raw, N.TYPE_Q4_0, n, k)
         np.save(os.path.join(outdir, f"z{rank}.npy"), y2)
         dist.barrier()
     finally:
+        if comm is not None:
+            comm.free()
         ctx.close()
         dist.destroy_process_group()
 

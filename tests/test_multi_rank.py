@@ -1,6 +1,7 @@
 """The multi-GPU row split's host logic on CPU: world-size-2 gloo ranks on
 127.0.0.1, each computing its rows with the oracle (standing in for the
-device matvec), all-gathered with purebee_b200.thread_pool.gather_rows."""
+device matvec); a gloo all-gather stands in for the device's NCCL one, and
+purebee_b200.thread_pool.assemble_rows cuts the gathered slices to y."""
 import os
 import socket
 
@@ -44,7 +45,7 @@ def _rank(rank, world, port, n, k, seed, outdir):
     sys.path.insert(0, root)
     sys.path.insert(0, os.path.join(root, "oracle"))
     import oracle as O
-    from purebee_b200.thread_pool import gather_rows, row_split, rows_per_rank
+    from purebee_b200.thread_pool import assemble_rows, row_split, rows_per_rank
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
         rng = np.random.default_rng(seed)
@@ -57,7 +58,9 @@ def _rank(rank, world, port, n, k, seed, outdir):
         y_local = torch.zeros(rows_per_rank(n, world), dtype=torch.float32)
         if hi > lo:
             y_local[:hi - lo] = torch.from_numpy(O.q4_0_matvec(x, raw[lo * rb:hi * rb], hi - lo, k))
-        y = gather_rows(y_local, n).numpy()
+        parts = [torch.zeros_like(y_local) for _ in range(world)]
+        dist.all_gather(parts, y_local)
+        y = assemble_rows([p.numpy() for p in parts], n)
         np.save(os.path.join(outdir, f"y{rank}.npy"), y)
         if rank == 0:
             np.save(os.path.join(outdir, "full.npy"), O.q4_0_matvec(x, raw, n, k))
