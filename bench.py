@@ -391,6 +391,18 @@ def run_ours(args, rank, world, torch, dist):
         ms = float(t.item())
         dist.barrier()
     clocks = clk.summary()
+    # the whole configs[3] decode window (positions 128 -> 640, one pass) and
+    # the step time around three positions of it
+    def window_ms(p0, n):
+        ctx.sync()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ctx._check(N.lib().pb_model_decode_loop(m.h, p0, n, None))
+        b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b)
+    full_ms = window_ms(PROMPT, MAX_POS - PROMPT)
+    by_pos = {str(p): round(window_ms(p, 8) / 8, 4) for p in (PROMPT, 384, MAX_POS - 8)}
     # algorithmic bytes per token at the mean position of the timed steps
     mid = min(pos + args.steps // 2, MAX_POS - 1)
     step_bytes = int(N.lib().pb_model_decode_bytes(m.h, mid))
@@ -443,7 +455,10 @@ def run_ours(args, rank, world, torch, dist):
             "data": "synthetic (seeded N(0,0.02) weights, seeded prompt tokens)",
             "config": config_line(world),
             "decode_step": {"bytes": step_bytes, "GBps": round(step_gbs, 1), "frac_of_hbm": round(step_gbs / peak, 3),
-                            "launches": launches_per_step},
+                            "launches": launches_per_step, "ms_by_position": by_pos,
+                            "full_window": {"positions": f"{PROMPT}-{MAX_POS - 1}", "steps": MAX_POS - PROMPT,
+                                            "ms": round(full_ms, 3),
+                                            "tok_s": round((MAX_POS - PROMPT) / (full_ms / 1e3), 2)}},
             "roofline": {"bound": "hbm", "kernel": "k_mvf (Q4_0, fast decode matvec)",
                          "achieved": round(mv_agg, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(mv_agg / peak, 3),
@@ -582,6 +597,30 @@ def run_case(args):
         rt.shutdown()
         ctx.close()
         return
+    if kind == "decode":  # decode:N[@POS] -> N decode steps of the headline model from POS (default 128)
+        import torch
+        from purebee_b200 import _native as N
+        steps, _, pos0 = shape.partition("@")
+        steps, pos0 = int(steps), int(pos0 or PROMPT)
+        ctx = N.Context(0)
+        torch.cuda.set_device(0)
+        stream = torch.cuda.ExternalStream(N.lib().pb_stream(ctx.h), device=0)
+        rt = build_model(ctx)
+        rt.forward(prompt_tokens(), 0)
+        ctx._check(N.lib().pb_model_decode_loop(rt.model.h, PROMPT, args.warmup, None))
+        ctx.sync()
+        torch.cuda.profiler.start()  # ncu --profile-from-start off captures these steps only
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ctx._check(N.lib().pb_model_decode_loop(rt.model.h, pos0, steps, None))
+        b.record(stream)
+        b.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"case": args.case, "ms_per_step": round(a.elapsed_time(b) / steps, 4),
+                          "launches_per_step": int(N.lib().pb_model_decode_launches(rt.model.h))}), flush=True)
+        rt.shutdown()
+        ctx.close()
+        return
     mtok = 1
     if kind == "gemm":  # gemm:MxNxK
         mtok, n, k = (int(v) for v in shape.lower().split("x"))
@@ -627,7 +666,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched configuration (configs[4])")
-    ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK, head:VxD, gemm:MxNxK, or batched:BxP (batched prefill + 3 steps)")
+    ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK, head:VxD, gemm:MxNxK, batched:BxP "
+                                                 "(batched prefill + 3 steps), or decode:N[@POS] (N decode steps)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.case:

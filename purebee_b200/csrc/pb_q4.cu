@@ -711,21 +711,34 @@ __device__ __forceinline__ float q8_0_block_fast(uint4 p0, uint4 p1, const uint6
 // swizzled within each 32-value block (bank-conflict-free reads of one block
 // per lane).  Any K: the threads loop over the chunks.
 // The sum of squares runs over a fixed partition (128 lanes, chunk c on lane
-// c % 128, then a fixed tree), so it does not depend on the CTA size: every
-// launch shape of the same vector normalises it to the same bits.
+// c % 128 in ascending order, then a fixed tree), so it does not depend on
+// the CTA size: every launch shape of the same vector normalises it to the
+// same bits.  Loads go out in batches of 4 per thread before any is used, so
+// staging costs one memory latency per batch, not one per chunk.
+constexpr int MVF_XB = 4;
 __device__ __forceinline__ void mvf_stage_x(const float* __restrict__ x, const float* __restrict__ w, double eps, int K,
                                             float4* xs4, double* red) {
   const int tid = threadIdx.x, nt = blockDim.x, nc = K / 4;
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
   double rms = 0.0;
   if (w) {
     if (tid < 128) {
       double ss = 0.0;
-      for (int c = tid; c < nc; c += 128) {
-        const float4 v = reinterpret_cast<const float4*>(x)[c];
-        ss = __fma_rn((double)v.x, (double)v.x, ss);
-        ss = __fma_rn((double)v.y, (double)v.y, ss);
-        ss = __fma_rn((double)v.z, (double)v.z, ss);
-        ss = __fma_rn((double)v.w, (double)v.w, ss);
+      for (int c0 = tid; c0 < nc; c0 += 128 * MVF_XB) {
+        float4 v[MVF_XB];
+#pragma unroll
+        for (int j = 0; j < MVF_XB; ++j)
+          if (c0 + 128 * j < nc) v[j] = x4[c0 + 128 * j];
+#pragma unroll
+        for (int j = 0; j < MVF_XB; ++j) {
+          if (c0 + 128 * j < nc) {
+            ss = __fma_rn((double)v[j].x, (double)v[j].x, ss);
+            ss = __fma_rn((double)v[j].y, (double)v[j].y, ss);
+            ss = __fma_rn((double)v[j].z, (double)v[j].z, ss);
+            ss = __fma_rn((double)v[j].w, (double)v[j].w, ss);
+          }
+        }
       }
       ss = pb_warp_sum_d(ss);
       if ((tid & 31) == 0) red[tid >> 5] = ss;
@@ -734,17 +747,31 @@ __device__ __forceinline__ void mvf_stage_x(const float* __restrict__ x, const f
     const double ss = __dadd_rn(__dadd_rn(red[0], red[1]), __dadd_rn(red[2], red[3]));
     rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)K), eps));
   }
-  for (int c = tid; c < nc; c += nt) {
-    float4 v = reinterpret_cast<const float4*>(x)[c];
-    if (w) {
-      const float4 wv = reinterpret_cast<const float4*>(w)[c];
-      v.x = (float)__dmul_rn(__ddiv_rn((double)v.x, rms), (double)wv.x);
-      v.y = (float)__dmul_rn(__ddiv_rn((double)v.y, rms), (double)wv.y);
-      v.z = (float)__dmul_rn(__ddiv_rn((double)v.z, rms), (double)wv.z);
-      v.w = (float)__dmul_rn(__ddiv_rn((double)v.w, rms), (double)wv.w);
+  for (int c0 = tid; c0 < nc; c0 += nt * MVF_XB) {
+    float4 v[MVF_XB], wv[MVF_XB];
+#pragma unroll
+    for (int j = 0; j < MVF_XB; ++j) {
+      const int c = c0 + nt * j;
+      if (c < nc) {
+        v[j] = x4[c];
+        if (w) wv[j] = w4[c];
+      }
     }
-    const int bj = c >> 3, ci = c & 7;
-    xs4[bj * 8 + (ci ^ (bj & 7))] = v;
+#pragma unroll
+    for (int j = 0; j < MVF_XB; ++j) {
+      const int c = c0 + nt * j;
+      if (c < nc) {
+        float4 o = v[j];
+        if (w) {
+          o.x = (float)__dmul_rn(__ddiv_rn((double)o.x, rms), (double)wv[j].x);
+          o.y = (float)__dmul_rn(__ddiv_rn((double)o.y, rms), (double)wv[j].y);
+          o.z = (float)__dmul_rn(__ddiv_rn((double)o.z, rms), (double)wv[j].z);
+          o.w = (float)__dmul_rn(__ddiv_rn((double)o.w, rms), (double)wv[j].w);
+        }
+        const int bj = c >> 3, ci = c & 7;
+        xs4[bj * 8 + (ci ^ (bj & 7))] = o;
+      }
+    }
   }
 }
 
