@@ -72,6 +72,9 @@ struct pb_model {
   // of a type kept as f32, e.g. Q6_K, F16): emb_f32 above, and an untied head
   float* head_f32 = nullptr;              // tiles [V/32][dim][32]
   pb_qmat head_f32_view;
+  // the quantized head table in the matvec (row) layout, for the fast
+  // kernel's coalesced loads; built on first use, dropped when the table changes
+  pb_qmat* head_rows = nullptr;
   std::vector<float*> q8s;                // scales per (layer, which 1..7)
   std::vector<int8_t*> q8q;
   // norms and cache
@@ -186,6 +189,7 @@ extern "C" int pb_model_free(pb_model* m) {
   cudaFree(m->exit_prob);
   pb_qmat_free(nullptr, m->emb);
   pb_qmat_free(nullptr, m->head);
+  pb_qmat_free(nullptr, m->head_rows);
   for (auto* p : m->qkv) pb_qmat_free(nullptr, p);
   for (auto* p : m->wo) pb_qmat_free(nullptr, p);
   for (auto* p : m->gu) pb_qmat_free(nullptr, p);
@@ -380,6 +384,8 @@ extern "C" int pb_model_init_synthetic(pb_model* m, uint64_t seed, double stdev)
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
   free_graph(m);
+  pb_qmat_free(ctx, m->head_rows);
+  m->head_rows = nullptr;
   // largest tensor: embedding or an FFN matrix
   int64_t ne = (int64_t)c.vocab * c.dim;
   int64_t nf = (int64_t)c.hidden_dim * c.dim;
@@ -457,6 +463,8 @@ extern "C" int pb_model_attach_head(pb_model* m, int type) {
   free_graph(m);
   pb_qmat_free(m->ctx, m->head);
   m->head = nullptr;
+  pb_qmat_free(m->ctx, m->head_rows);
+  m->head_rows = nullptr;
   cudaFree(m->head_f32);
   m->head_f32 = nullptr;
   if (type == PB_TYPE_F32) return alloc_f32_table(m, &m->head_f32, &m->head_f32_view);
@@ -493,6 +501,10 @@ static int model_tensor_io(pb_model* m, int layer, int which, void* host, size_t
   size_t need = tensor_bytes(m, which);
   if (bytes != need) return pb_set_error(ctx, PB_ERR_ARG, "tensor %d needs %zu bytes, got %zu", which, need, bytes);
   if (!get) free_graph(m);
+  if (!get && (which == 0 || which == 11)) {
+    pb_qmat_free(ctx, m->head_rows);
+    m->head_rows = nullptr;
+  }
   if (which >= 8 && which <= 10) {
     float* p = which == 8 ? m->rms_att + (size_t)layer * c.dim : which == 9 ? m->rms_ffn + (size_t)layer * c.dim
                                                                             : m->rms_final;
@@ -718,13 +730,32 @@ static int launch_embed(pb_model* m, const int* toks, int M) {
   return PB_OK;
 }
 
+// The row-layout copy of the quantized head table the fast head reads (the
+// tiled table serves the exact batch_dot kernel and the embedding lookup).
+// Allocates: called before any recording.
+static int ensure_head_rows(pb_model* m) {
+  pb_ctx* ctx = m->ctx;
+  if (m->head_rows || ctx->matvec_mode != PB_MATVEC_FAST || m->c.kind != PB_MODEL_STREAMING_Q4) return PB_OK;
+  const pb_qmat* t = head_of(m);
+  if (!t || (t->type != PB_TYPE_Q4_0 && t->type != PB_TYPE_Q8_0)) return PB_OK;
+  const size_t bytes = (size_t)t->N * t->nb * (t->type == PB_TYPE_Q4_0 ? 18 : 34);
+  PB_TRY(pb_ensure_scratch(ctx, bytes));
+  const int64_t tot = (int64_t)t->N * t->nb;
+  k_pack_rows<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>((const uint8_t*)ctx->scratch, t->N, 0, 0, t->nb, t->type,
+                                                          t->layout, t->qs, t->d, 1);
+  PB_LAUNCHED(ctx, "k_pack_rows");
+  PB_TRY(pb_qmat_from_device(ctx, t->type, ctx->scratch, t->N, t->K, &m->head_rows));
+  return pb_wait(ctx);
+}
+
 // Final RMSNorm (fused into the head kernel) and the LM head with the greedy
 // argmax (llama-streaming.js:616-642, :899-909; llama.js:340-367).
 static int launch_head(pb_model* m, const float* last_x) {
   int mode = 0;
   const pb_qmat* t = head_table(m, &mode);
   if (mode == 0 && m->ctx->matvec_mode == PB_MATVEC_FAST)
-    return pb_launch_head_fast(m->ctx, t, last_x, m->rms_final, m->c.eps, m->logits, m->key);
+    return pb_launch_head_fast(m->ctx, m->head_rows ? m->head_rows : t, last_x, m->rms_final, m->c.eps, m->logits,
+                               m->key);
   return pb_launch_head_norm(m->ctx, t, last_x, m->rms_final, m->c.eps, m->logits, m->key, mode);
 }
 
@@ -760,6 +791,7 @@ static void check_graph_mode(pb_model* m) {
 static int ensure_graph(pb_model* m) {
   check_graph_mode(m);
   if (m->exec) return PB_OK;
+  PB_TRY(ensure_head_rows(m));
   pb_ctx* ctx = m->ctx;
   PB_TRY(ensure_act(m, 1));
   int64_t before = ctx->launches;
@@ -789,6 +821,7 @@ extern "C" int pb_model_forward_ex(pb_model* m, const int* tokens, int n, int st
     int next;
     return pb_model_decode_ex(m, tokens[0], start_pos, max_layers, &next, logits_host, layers_used);
   }
+  PB_TRY(ensure_head_rows(m));
   const int L = max_layers <= 0 || max_layers > c.n_layers ? c.n_layers : max_layers;
   PB_TRY(ensure_act(m, n));
   PB_TRY_CUDA(ctx, cudaMemcpyAsync(m->toks, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
@@ -849,6 +882,7 @@ extern "C" int pb_model_sample(pb_model* m, int top_k, double temperature, uint6
 // self-speculative decoding, forward(..., {maxLayers: L})).
 static int ensure_graph_layers(pb_model* m, int L) {
   check_graph_mode(m);
+  PB_TRY(ensure_head_rows(m));
   if ((int)m->lexec.size() < m->c.n_layers) {
     m->lexec.resize(m->c.n_layers, nullptr);
     m->lgraph.resize(m->c.n_layers, nullptr);
@@ -1008,6 +1042,7 @@ static int ensure_sample_graph(pb_model* m, int top_k, double temperature, uint6
   pb_ctx* ctx = m->ctx;
   PB_TRY(ensure_sample_buffers(m));
   check_graph_mode(m);
+  PB_TRY(ensure_head_rows(m));
   if (m->sexec && m->s_topk == top_k && m->s_temp == temperature && m->s_seed == seed) return PB_OK;
   if (m->sexec) cudaGraphExecDestroy(m->sexec);
   if (m->sgraph) cudaGraphDestroy(m->sgraph);

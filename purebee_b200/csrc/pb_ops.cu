@@ -1182,25 +1182,53 @@ k_attn_dec1(const float* __restrict__ q, const float* __restrict__ kc, const flo
   __syncthreads();
   if (!last_flag) return;
   __threadfence();
-  // the last split merges every split of this kv head, in split order
+  // the last split merges every split of this kv head, in split order:
+  // the splits' maxima and sums into shared memory, one scale factor
+  // f_c = exp(m_c - M) per (head, split), then the partial outputs in
+  // batches of loads issued before use
   const double* wg = ws + (size_t)g * nsplit * PER * (2 + hd);
+  double* fm = e;                          // [PER][nsplit]: m_c, then f_c
+  double* fs = e + (size_t)PER * nsplit;   // [PER][nsplit]: S_c (0: an empty split)
+  __shared__ double mh[PER], sh[PER];
+  for (int i = tid; i < PER * nsplit; i += AD1_THREADS) {
+    const int h = i / nsplit, c = i - h * nsplit;
+    const double* w = wg + ((size_t)c * PER + h) * (2 + hd);
+    fm[i] = __ldcg(w);
+    fs[i] = __ldcg(w + 1);
+  }
+  __syncthreads();
+  if (tid < PER) {
+    double M = -INFINITY;
+    for (int c = 0; c < nsplit; ++c)
+      if (fs[tid * nsplit + c] != 0.0 && fm[tid * nsplit + c] > M) M = fm[tid * nsplit + c];
+    mh[tid] = M;
+  }
+  __syncthreads();
+  for (int i = tid; i < PER * nsplit; i += AD1_THREADS) {
+    const double M = mh[i / nsplit], m_ = fm[i];
+    fm[i] = fs[i] == 0.0 ? 0.0 : (m_ == M ? 1.0 : exp(__dsub_rn(m_, M)));
+  }
+  __syncthreads();
+  if (tid < PER) {  // a non-empty split has S_c >= 1 or NaN (which then reaches the output)
+    double S = 0.0;
+    for (int c = 0; c < nsplit; ++c)
+      if (fs[tid * nsplit + c] != 0.0) S = __fma_rn(fs[tid * nsplit + c], fm[tid * nsplit + c], S);
+    sh[tid] = S;
+  }
+  __syncthreads();
   for (int i = tid; i < PER * hd; i += AD1_THREADS) {
     const int h = i / hd, d = i - h * hd;
-    double M = -INFINITY;
-    for (int c = 0; c < nsplit; ++c) {
-      const double mcv = __ldcg(wg + ((size_t)c * PER + h) * (2 + hd));
-      M = mcv > M ? mcv : M;
+    double O = 0.0;
+    for (int c0 = 0; c0 < nsplit; c0 += 8) {
+      double v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[j] = c0 + j < nsplit ? __ldcg(wg + ((size_t)(c0 + j) * PER + h) * (2 + hd) + 2 + d) : 0.0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (c0 + j < nsplit && fs[h * nsplit + c0 + j] != 0.0) O = __fma_rn(v[j], fm[h * nsplit + c0 + j], O);
     }
-    double S = 0.0, O = 0.0;
-    for (int c = 0; c < nsplit; ++c) {
-      const double* w = wg + ((size_t)c * PER + h) * (2 + hd);
-      const double mcv = __ldcg(w), sc = __ldcg(w + 1);
-      if (sc == 0.0) continue;  // an empty split (fewer positions than splits); a non-empty one has S_c >= 1 or NaN
-      const double f = mcv == M ? 1.0 : exp(__dsub_rn(mcv, M));
-      S = __fma_rn(sc, f, S);
-      O = __fma_rn(__ldcg(w + 2 + d), f, O);
-    }
-    out[((size_t)g * PER + h) * hd + d] = (float)__ddiv_rn(O, S);
+    out[((size_t)g * PER + h) * hd + d] = (float)__ddiv_rn(O, sh[h]);
   }
   if (tid == 0) counters[g] = 0u;  // ready for the next launch
 }
@@ -1699,7 +1727,8 @@ bool pb_attn_dec1_ok(int n_heads, int n_kv, int hd) {
 int pb_launch_attn_dec1(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
                         int n_heads, int n_kv, int hd, float* out, int max_len, int nsplit, double* ws,
                         unsigned int* counters) {
-  if (!pb_attn_dec1_ok(n_heads, n_kv, hd) || nsplit <= 0 || (size_t)(max_len + nsplit - 1) / nsplit > AD1_MAX_P)
+  if (!pb_attn_dec1_ok(n_heads, n_kv, hd) || nsplit <= 0 || nsplit > AD1_MAX_P / 2 ||
+      (size_t)(max_len + nsplit - 1) / nsplit > AD1_MAX_P)
     return pb_set_error(ctx, PB_ERR_ARG, "split decode attention: unsupported shape");
   const double scale = 1.0 / sqrt((double)hd);  // llama-streaming.js:546
   const dim3 grid(n_kv, nsplit);
