@@ -9,6 +9,7 @@
 // then the final rmsnorm and the head with the fused argmax.  Position and
 // token live in device memory, so one captured graph replays every step.
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <vector>
@@ -300,6 +301,11 @@ extern "C" int pb_model_create(pb_ctx* ctx, const pb_model_config* cfg, pb_model
   cudaMemsetAsync(m->hist, 0, (size_t)(c.seq_len + 1) * 4, ctx->stream);
   if (pb_attn_dec1_ok(c.n_heads, c.n_kv_heads, c.head_dim)) {
     m->attn_splits = pb_attn_dec1_splits(c.n_kv_heads, c.seq_len, ctx->sm_count);
+    // tuning override of the split count (positions per split stay within the kernel's bound)
+    if (const char* e = getenv("PB_ATTN_SPLITS")) {
+      const int v = atoi(e);
+      if (v > 0 && v >= pb_attn_dec1_splits(c.n_kv_heads, c.seq_len, 1)) m->attn_splits = v;
+    }
     const size_t wsd = pb_attn_dec1_ws_doubles(c.n_heads, c.n_kv_heads, c.head_dim, m->attn_splits);
     if (cudaMalloc(&m->attn_ws, wsd * 8) != cudaSuccess || cudaMalloc(&m->attn_cnt, (size_t)c.n_kv_heads * 4))
       return fail(pb_set_error(ctx, PB_ERR_OOM, "decode attention workspace"));

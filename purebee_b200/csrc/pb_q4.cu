@@ -775,15 +775,30 @@ __device__ __forceinline__ void mvf_stage_x(const float* __restrict__ x, const f
   }
 }
 
+constexpr int MVF_NS = 2;  // shared-memory stages of weight payload per warp
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
 // CTA of W warps = TPC tiles x KC chunks per iteration (TPC = W / KC).
 // TYPE Q4_0 or Q8_0; LAYOUT ROWS (matvec weights) or TILED8 (a head table:
-// block b of the tile's 8 rows is 8 consecutive slots, so a lane's 8 rows
-// share 128-byte lines and the loads go through L1).
+// block b of the tile's 8 rows is 8 consecutive slots).
+// The payload streams through shared memory: each lane copies its own 16-byte
+// pieces with cp.async into its warp's stage buffer, MVF_NS units ahead, and
+// reads back only what it copied (no cross-lane hand-off, so no barrier); the
+// scales are loaded into registers one unit ahead.  The loads of the next
+// units are therefore in flight while a unit is computed, and the CTA's
+// later tiles are bulk-prefetched into L2 further ahead still.
 template <int TYPE, int LAYOUT>
 __global__ void __launch_bounds__(MVF_MAX_WARPS * 32, 1)
 k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, int nb, int tile_begin, int tile_end,
       int row_end, const float* __restrict__ x, float* __restrict__ y, pb_mv_epi epi, pb_magics M, int* err) {
   constexpr int QB = TYPE == PB_TYPE_Q8_0 ? 32 : 16;  // payload bytes per block
+  constexpr int PL = QB / 16;                          // 16-byte pieces per block
+  constexpr int STAGE = 8 * 32 * QB;                   // one unit: 8 rows x 32 lanes
   extern __shared__ __align__(16) unsigned char mvf_raw[];
   __shared__ double red[MVF_MAX_WARPS];
   const int K = nb * 32, KC = (nb + 31) >> 5, W = blockDim.x >> 5, TPC = W / KC;
@@ -794,11 +809,17 @@ k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, i
   const bool has_b = active && b < nb;
   float4* xs4 = reinterpret_cast<float4*>(mvf_raw);                  // [K / 4] swizzled
   float* part = reinterpret_cast<float*>(mvf_raw + (size_t)K * 4);   // [2][TPC][KC][8]
+  unsigned char* wst = mvf_raw + (size_t)K * 4 + (((size_t)2 * TPC * KC * 8 * 4 + 15) & ~(size_t)15) +
+                       (size_t)warp * MVF_NS * STAGE;                // this warp's stages
   const int per_iter = gridDim.x * TPC;
   const int n_iter = (tile_end - tile_begin + per_iter - 1) / per_iter;  // CTA-uniform
   const uint4* q4 = reinterpret_cast<const uint4*>(qs);
   const size_t tq = (size_t)8 * nb * QB, td = (size_t)8 * nb * 2;
   auto tile_of = [&](int it) { return tile_begin + it * per_iter + blockIdx.x * TPC + tl; };
+  auto live = [&](int it) { return has_b && it < n_iter && tile_of(it) < tile_end; };
+  auto slot_of = [&](int t, int r) {
+    return LAYOUT == PB_LAYOUT_TILED8 ? ((size_t)t * nb + b) * 8 + r : (size_t)(t * 8 + r) * nb + b;
+  };
   // L2 prefetch: the chunk-0 warp of each tile slot fetches its tile (payload
   // and scales are contiguous per tile) MVF_PF iterations ahead
   auto prefetch = [&](int it) {
@@ -808,26 +829,36 @@ k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, i
       pb_l2_prefetch(dsc + (size_t)t * td / 2, (uint32_t)td);
     }
   };
+  // unit `it`'s payload into stage it % MVF_NS (one commit group per unit,
+  // empty when the unit is past the end, so the group count stays regular)
+  auto issue = [&](int it) {
+    if (live(it)) {
+      const int t = tile_of(it);
+      unsigned char* st = wst + (size_t)(it % MVF_NS) * STAGE;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const size_t slot = slot_of(t, r);
+#pragma unroll
+        for (int u = 0; u < PL; ++u) cp_async16(st + ((size_t)(r * 32 + lane) * PL + u) * 16, q4 + slot * PL + u);
+      }
+    }
+    cp_async_commit();
+  };
+  auto scales = [&](int it, uint32_t (&pd)[8]) {
+    if (live(it)) {
+      const int t = tile_of(it);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) pd[r] = __ldcs(dsc + slot_of(t, r));
+    }
+  };
   for (int i = 0; i < MVF_PF; ++i) prefetch(i);
   if (tid == 0)
     for (int i = 0; i < PB_MAX_L2_NEXT; ++i) pb_l2_prefetch_share(epi.l2_next[i], epi.l2_next_bytes[i], blockIdx.x, gridDim.x);
-  // the first tile's blocks (weights do not depend on the previous kernel)
-  constexpr int PL = QB / 16;  // uint4 per block payload
-  uint4 pq[8][PL];
-  uint32_t pd[8];
-  auto load = [&](int it) {
-    const int t = tile_of(it);
-    if (has_b && it < n_iter && t < tile_end) {
+  // weights do not depend on the previous kernel: the first units go out before the wait
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const size_t slot = LAYOUT == PB_LAYOUT_TILED8 ? ((size_t)t * nb + b) * 8 + r : (size_t)(t * 8 + r) * nb + b;
-#pragma unroll
-        for (int u = 0; u < PL; ++u) pq[r][u] = LAYOUT == PB_LAYOUT_TILED8 ? q4[slot * PL + u] : __ldcs(q4 + slot * PL + u);
-        pd[r] = LAYOUT == PB_LAYOUT_TILED8 ? dsc[slot] : __ldcs(dsc + slot);
-      }
-    }
-  };
-  load(0);
+  for (int i = 0; i < MVF_NS; ++i) issue(i);
+  uint32_t pd[8], pdn[8];
+  scales(0, pd);
   pb_pdl_trigger();
   pb_pdl_wait();  // x (and the residual) come from the previous kernel
   mvf_stage_x(x, epi.norm_w, epi.eps, K, xs4, red);
@@ -843,23 +874,28 @@ k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, i
   }
   for (int it = 0; it < n_iter; ++it) {
     prefetch(it + MVF_PF);
+    scales(it + 1, pdn);
+    asm volatile("cp.async.wait_group %0;" ::"n"(MVF_NS - 1) : "memory");  // unit it has landed
     const int t = tile_of(it);
     float v[8];
 #pragma unroll
     for (int r = 0; r < 8; ++r) v[r] = 0.0f;
-    if (has_b && t < tile_end) {
+    if (live(it)) {
+      const unsigned char* st = wst + (size_t)(it % MVF_NS) * STAGE;
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
+        const uint4* pp = reinterpret_cast<const uint4*>(st + (size_t)(r * 32 + lane) * QB);
         // the scale as the kernel being replaced decodes it: the WASM matvec's
         // (wasm-q4.js:88-109) for matvec weights, the exact one of the table
         // the reference's head reads (gguf.js:55-70)
         const float d = LAYOUT == PB_LAYOUT_TILED8 ? pb_f16_exact(pd[r]) : pb_f16_wasm(pd[r]);
-        const float bs = TYPE == PB_TYPE_Q8_0 ? q8_0_block_fast(pq[r][0], pq[r][PL - 1], xp)
-                                              : q4_0_block_fast(pq[r][0], xp, M);
+        const float bs = TYPE == PB_TYPE_Q8_0 ? q8_0_block_fast(pp[0], pp[PL - 1], xp) : q4_0_block_fast(pp[0], xp, M);
         v[r] = __fmul_rn(bs, d);
       }
     }
-    load(it + 1);
+    issue(it + MVF_NS);  // this lane read its own pieces of the stage: refill it
+#pragma unroll
+    for (int r = 0; r < 8; ++r) pd[r] = pdn[r];
     // transposed butterfly over the lanes: lane 4r ends with row r's sum
     float w4[4], w2[2];
     const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4;
@@ -892,15 +928,23 @@ k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, i
       mv_epilogue(s_, t, N, row_end, y, epi, err);
     }
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");  // no copy outlives the CTA
+}
+
+static size_t mvf_smem(const pb_qmat* w, int W) {
+  const int KC = (w->nb + 31) / 32, TPC = W / KC, QB = w->type == PB_TYPE_Q8_0 ? 32 : 16;
+  return (size_t)w->K * 4 + (((size_t)2 * TPC * KC * 8 * 4 + 15) & ~(size_t)15) + (size_t)W * MVF_NS * 8 * 32 * QB;
 }
 
 // Warps per CTA: small matrices get small CTAs (more SMs share the rows),
-// large ones 16 warps; at least one warp per K chunk.
+// large ones up to 16 warps; at least one warp per K chunk; within the
+// shared-memory budget.
 static int mvf_warps(const pb_qmat* w, int ntiles, int sm_count) {
   const int KC = (w->nb + 31) / 32;
   int W = 4;
   while (W < MVF_MAX_WARPS && (int64_t)ntiles * KC / W >= 2 * sm_count) W *= 2;
   while (W < KC) W *= 2;
+  while (W > KC && W > 4 && mvf_smem(w, W) > (size_t)200 * 1024) W /= 2;
   return W;
 }
 
@@ -908,10 +952,16 @@ static int launch_mvf(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, i
                       int row_end, const pb_mv_epi& epi) {
   const int KC = (w->nb + 31) / 32;
   const int W = mvf_warps(w, ntiles, ctx->sm_count), TPC = W / KC;
+  const size_t smem = mvf_smem(w, W);
+  if (smem > (size_t)200 * 1024)
+    return pb_set_error(ctx, PB_ERR_ARG, "fast matvec: K=%d needs %zu bytes of shared memory", w->K, smem);
   const int groups = (ntiles + TPC - 1) / TPC;
-  const int cap = ctx->sm_count * (MVF_MAX_WARPS / W);  // CTAs resident at once (registers)
+  int per_sm = MVF_MAX_WARPS / W;  // CTAs resident at once: registers ...
+  const int by_smem = (int)((size_t)220 * 1024 / (smem + 1024));
+  per_sm = per_sm < by_smem ? per_sm : by_smem;  // ... and shared memory
+  if (per_sm < 1) per_sm = 1;
+  const int cap = ctx->sm_count * per_sm;
   const int grid = groups < cap ? groups : cap;
-  const size_t smem = (size_t)w->K * 4 + (size_t)2 * TPC * KC * 8 * 4;
   auto kern = w->type == PB_TYPE_Q8_0
                   ? (w->layout == PB_LAYOUT_TILED8 ? k_mvf<PB_TYPE_Q8_0, PB_LAYOUT_TILED8> : k_mvf<PB_TYPE_Q8_0, PB_LAYOUT_ROWS>)
                   : (w->layout == PB_LAYOUT_TILED8 ? k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_TILED8> : k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS>);
