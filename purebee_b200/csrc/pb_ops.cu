@@ -999,10 +999,10 @@ k_attn_dec(const float* __restrict__ q, const float* __restrict__ kc, const floa
 // ============================================================================
 // k_attn_dec1<PER>: CTA (kv head g, split sp) over the positions
 // [sp * P, (sp + 1) * P) of the cache, P = ceil(cache_len / nsplit), for the
-// PER query heads of the group (each K and V row is read once).  The splits
-// fill one wave of the GPU (n_kv * nsplit ~ the SM count), so a layer's
-// attention is one short round of loads instead of a few CTAs walking the
-// whole cache.
+// PER query heads of the group (each K and V row is read once).  Up to 8
+// splits per kv head (64 CTAs for 8 kv heads): each CTA walks an eighth of
+// the cache instead of one CTA per head walking all of it, and the merge
+// stays short.
 //   - before griddepcontrol.wait: the position (written by the step before),
 //     this split's K rows j < pos into registers and its V rows into L2
 //     (only row pos is written by the projection this step);
@@ -1699,10 +1699,13 @@ int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const fl
                    pos_dev, n_heads, n_kv, hd, scale, out, max_len, geo, ctx->d_err);
 }
 
-// Splits of the one-sequence decode attention: about one CTA per SM in
-// total, at most AD1_MAX_P positions each.
+// Splits of the one-sequence decode attention: at most 8 per kv head and at
+// most AD1_MAX_P positions each.
 int pb_attn_dec1_splits(int n_kv, int max_len, int sm_count) {
+  // up to 8 splits per kv head: more splits shorten each CTA's walk over the
+  // cache but lengthen the merge; 8 measured best at 128-640 positions
   int ns = sm_count / n_kv;
+  if (ns > 8) ns = 8;
   if (ns < 1) ns = 1;
   const int need = (max_len + AD1_MAX_P - 1) / AD1_MAX_P;
   return ns < need ? need : ns;

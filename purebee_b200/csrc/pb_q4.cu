@@ -686,6 +686,59 @@ __device__ __forceinline__ float q4_0_block_fast(uint4 p, const uint64_t (&xp)[1
   return __fadd_rn(s.x, s.y);
 }
 
+// Two nibbles into one f32 pair and the magic offsets removed, in one asm
+// block, so the pair is built in place rather than moved together.
+template <uint32_t MA, uint32_t MB>
+__device__ __forceinline__ uint64_t nib_pair(uint32_t wa, uint32_t wb, uint32_t ea, uint32_t eb, uint64_t c) {
+  uint64_t r;
+  asm("{\n\t.reg .b32 a, b;\n\t.reg .b64 t;\n\t"
+      "lop3.b32 a, %1, %5, %3, 0xEA;\n\t"
+      "lop3.b32 b, %2, %6, %4, 0xEA;\n\t"
+      "mov.b64 t, {a, b};\n\t"
+      "add.rn.f32x2 %0, t, %7;\n\t}"
+      : "=l"(r)
+      : "r"(wa), "r"(wb), "r"(ea), "r"(eb), "n"(MA), "n"(MB), "l"(c));
+  return r;
+}
+
+// The same block sum with the pairs built by nib_pair.
+__device__ __forceinline__ float q4_0_block_fast2(uint4 p, const uint64_t (&xp)[16], const pb_magics& M) {
+  const uint64_t c_l01 = p2(-8388616.0f, -32776.0f), c_l23 = p2(-136.0f, -32776.0f);
+  const uint64_t c_h = p2(-524296.0f, -2056.0f);
+  uint64_t a = 0, b = 0;
+  const uint32_t wv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t w = wv[g], w2 = w >> 16;
+    a = p2fma(nib_pair<0xFu, 0xF00u>(w, w, M.m0, M.m8, c_l01), xp[2 * g], a);
+    b = p2fma(nib_pair<0xF0000u, 0xF00u>(w, w2, M.m16, M.m8, c_l23), xp[2 * g + 1], b);
+    a = p2fma(nib_pair<0xF0u, 0xF000u>(w, w, M.m4, M.m12, c_h), xp[8 + 2 * g], a);
+    b = p2fma(nib_pair<0xF0u, 0xF000u>(w2, w2, M.m4, M.m12, c_h), xp[9 + 2 * g], b);
+  }
+  const float2 s = up2(p2add(a, b));
+  return __fadd_rn(s.x, s.y);
+}
+
+// Scalar form: one logic op, one add and one FMA per weight, no pairs.
+__device__ __forceinline__ float q4_0_block_scalar(uint4 p, const uint64_t (&xp)[16], const pb_magics& M) {
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  const uint32_t wv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t w = wv[g], w2 = w >> 16;
+    const float2 xl01 = up2(xp[2 * g]), xl23 = up2(xp[2 * g + 1]), xh01 = up2(xp[8 + 2 * g]), xh23 = up2(xp[9 + 2 * g]);
+    a0 = __fmaf_rn(__fadd_rn(magr<0xFu>(w, M.m0), -8388616.0f), xl01.x, a0);
+    a1 = __fmaf_rn(__fadd_rn(magr<0xF00u>(w, M.m8), -32776.0f), xl01.y, a1);
+    a2 = __fmaf_rn(__fadd_rn(magr<0xF0000u>(w, M.m16), -136.0f), xl23.x, a2);
+    a3 = __fmaf_rn(__fadd_rn(magr<0xF00u>(w2, M.m8), -32776.0f), xl23.y, a3);
+    a0 = __fmaf_rn(__fadd_rn(magr<0xF0u>(w, M.m4), -524296.0f), xh01.x, a0);
+    a1 = __fmaf_rn(__fadd_rn(magr<0xF000u>(w, M.m12), -2056.0f), xh01.y, a1);
+    a2 = __fmaf_rn(__fadd_rn(magr<0xF0u>(w2, M.m4), -524296.0f), xh23.x, a2);
+    a3 = __fmaf_rn(__fadd_rn(magr<0xF000u>(w2, M.m12), -2056.0f), xh23.y, a3);
+  }
+  return __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+}
+
 // Q8_0 block (gguf.js:239-257): byte j is element j; a byte becomes the
 // exact float 2^15 + (q + 128) by one byte permute with the exponent
 // pattern (q biased by 128 first), a packed add removes 2^15 + 128.
@@ -747,6 +800,9 @@ __device__ __forceinline__ void mvf_stage_x(const float* __restrict__ x, const f
     const double ss = __dadd_rn(__dadd_rn(red[0], red[1]), __dadd_rn(red[2], red[3]));
     rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)K), eps));
   }
+  // the fast path scales in f32 by 1 / rms (rms itself in double): two f32
+  // roundings per element instead of the reference's double (x / rms) * w
+  const float inv = w ? (float)(1.0 / rms) : 1.0f;
   for (int c0 = tid; c0 < nc; c0 += nt * MVF_XB) {
     float4 v[MVF_XB], wv[MVF_XB];
 #pragma unroll
@@ -763,10 +819,10 @@ __device__ __forceinline__ void mvf_stage_x(const float* __restrict__ x, const f
       if (c < nc) {
         float4 o = v[j];
         if (w) {
-          o.x = (float)__dmul_rn(__ddiv_rn((double)o.x, rms), (double)wv[j].x);
-          o.y = (float)__dmul_rn(__ddiv_rn((double)o.y, rms), (double)wv[j].y);
-          o.z = (float)__dmul_rn(__ddiv_rn((double)o.z, rms), (double)wv[j].z);
-          o.w = (float)__dmul_rn(__ddiv_rn((double)o.w, rms), (double)wv[j].w);
+          o.x = __fmul_rn(__fmul_rn(o.x, inv), wv[j].x);
+          o.y = __fmul_rn(__fmul_rn(o.y, inv), wv[j].y);
+          o.z = __fmul_rn(__fmul_rn(o.z, inv), wv[j].z);
+          o.w = __fmul_rn(__fmul_rn(o.w, inv), wv[j].w);
         }
         const int bj = c >> 3, ci = c & 7;
         xs4[bj * 8 + (ci ^ (bj & 7))] = o;
@@ -792,7 +848,7 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 // scales are loaded into registers one unit ahead.  The loads of the next
 // units are therefore in flight while a unit is computed, and the CTA's
 // later tiles are bulk-prefetched into L2 further ahead still.
-template <int TYPE, int LAYOUT>
+template <int TYPE, int LAYOUT, int VAR = 0>
 __global__ void __launch_bounds__(MVF_MAX_WARPS * 32, 1)
 k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, int nb, int tile_begin, int tile_end,
       int row_end, const float* __restrict__ x, float* __restrict__ y, pb_mv_epi epi, pb_magics M, int* err) {
@@ -889,7 +945,10 @@ k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, i
         // (wasm-q4.js:88-109) for matvec weights, the exact one of the table
         // the reference's head reads (gguf.js:55-70)
         const float d = LAYOUT == PB_LAYOUT_TILED8 ? pb_f16_exact(pd[r]) : pb_f16_wasm(pd[r]);
-        const float bs = TYPE == PB_TYPE_Q8_0 ? q8_0_block_fast(pp[0], pp[PL - 1], xp) : q4_0_block_fast(pp[0], xp, M);
+        const float bs = TYPE == PB_TYPE_Q8_0 ? q8_0_block_fast(pp[0], pp[PL - 1], xp)
+                         : VAR == 1 ? q4_0_block_fast2(pp[0], xp, M)
+                         : VAR == 2 ? q4_0_block_scalar(pp[0], xp, M)
+                                    : q4_0_block_fast(pp[0], xp, M);
         v[r] = __fmul_rn(bs, d);
       }
     }
@@ -962,9 +1021,12 @@ static int launch_mvf(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, i
   if (per_sm < 1) per_sm = 1;
   const int cap = ctx->sm_count * per_sm;
   const int grid = groups < cap ? groups : cap;
+  static const int var = getenv("PB_MVF_VARIANT") ? atoi(getenv("PB_MVF_VARIANT")) : 0;  // arithmetic form (tuning)
   auto kern = w->type == PB_TYPE_Q8_0
                   ? (w->layout == PB_LAYOUT_TILED8 ? k_mvf<PB_TYPE_Q8_0, PB_LAYOUT_TILED8> : k_mvf<PB_TYPE_Q8_0, PB_LAYOUT_ROWS>)
-                  : (w->layout == PB_LAYOUT_TILED8 ? k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_TILED8> : k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS>);
+                  : w->layout == PB_LAYOUT_TILED8 ? k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_TILED8>
+                  : var == 1 ? k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS, 1>
+                  : var == 2 ? k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS, 2> : k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS>;
   return pb_launch(ctx, "k_mvf", true, kern, dim3(grid), dim3(W * 32), smem, (const uint8_t*)w->qs,
                    (const uint16_t*)w->d, w->N, w->nb, tile_begin, tile_begin + ntiles, row_end, x, y, epi,
                    pb_magics{PB_MAG0, PB_MAG4, PB_MAG8, PB_MAG12, PB_MAG16}, ctx->d_err);
@@ -1610,6 +1672,8 @@ int pb_setup_q4_kernels(void) {
   e = e ? e : cudaFuncSetAttribute(k_head_f32_double, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_head_f32_bd, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_TILED8>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q8_0, PB_LAYOUT_ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q8_0, PB_LAYOUT_TILED8>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
