@@ -124,6 +124,7 @@ extern "C" int pb_init(int device, pb_ctx** out) {
   cudaMemset(ctx->d_err, 0, sizeof(int));
   cudaDeviceSynchronize();
   if (pb_setup_q4_kernels() != PB_OK || pb_setup_ops_kernels() != PB_OK || pb_setup_gemm_kernels() != PB_OK ||
+      pb_setup_mvi_kernels() != PB_OK ||
       pb_setup_sample_kernels() != PB_OK ||
       pb_setup_noalloc(ctx) != PB_OK) {
     pb_shutdown(ctx);
@@ -635,6 +636,9 @@ int pb_qmat_pack_from_device(pb_ctx* ctx, pb_qmat* m, const void* gguf_dev) {
   k_qmat_pack<<<pb_cdiv(total, 256), 256, 0, ctx->stream>>>(m->type, m->layout, (const uint8_t*)gguf_dev, m->N,
                                                             m->nb, m->qs, m->d, m->m, 0);
   PB_LAUNCHED(ctx, "k_qmat_pack");
+  m->mma_ok = false;
+  // matvec weights also get the tensor-core copy the fast matvec reads
+  if (m->type == PB_TYPE_Q4_0 && m->layout == PB_LAYOUT_ROWS) return pb_qmat_build_mma(ctx, m);
   return PB_OK;
 }
 
@@ -679,6 +683,8 @@ extern "C" int pb_qmat_free(pb_ctx* ctx, pb_qmat* m) {
   cudaFree(m->qs);
   cudaFree(m->d);
   cudaFree(m->m);
+  cudaFree(m->mq);
+  cudaFree(m->md);
   delete m;
   return PB_OK;
 }

@@ -49,7 +49,16 @@ struct pb_qmat {
   uint8_t* qs = nullptr;
   uint16_t* d = nullptr;
   uint16_t* m = nullptr;  // Q4_1 min
+  // A second copy of a Q4_0 matrix for the int8 tensor-core matvec (k_mvi,
+  // the fast mode): 16-row tiles, nibbles placed for the mma fragments, the
+  // blocks padded to whole spans of 8 (see pb_mvi.cu).  mma_ok: it mirrors
+  // the current contents (a writer of qs/d clears it; pb_qmat_build_mma sets it).
+  uint8_t* mq = nullptr;
+  uint16_t* md = nullptr;
+  int nbp = 0;  // blocks per row in the copy (a multiple of 8)
+  bool mma_ok = false;
 };
+int pb_qmat_build_mma(pb_ctx* ctx, pb_qmat* m);  // (re)build the tensor-core copy
 
 // ---- host helpers ---------------------------------------------------------
 
@@ -287,6 +296,61 @@ struct pb_mv_epi {
   unsigned long long* amax = nullptr;  // PB_EPI_ARGMAX
 };
 
+// The fused epilogue of an 8-row tile of a matvec: every lane of quad r
+// (lanes 4r .. 4r + 3) holds row r's value v; the quad's lane 0 stores rows
+// in [row_begin, row_end).
+__device__ __forceinline__ void pb_mv_epilogue(float v, int tile, int N, int row_begin, int row_end,
+                                               float* __restrict__ y, const pb_mv_epi& epi, int* err) {
+  const int lane = threadIdx.x & 31, rr = lane >> 2, L = lane & 3;
+  const int row = tile * 8 + rr;
+  const bool live = L == 0 && row >= row_begin && row < row_end && row < N;
+  if (epi.kind == PB_EPI_STORE) {
+    if (live) y[row] = v;
+  } else if (epi.kind == PB_EPI_RESIDUAL) {
+    if (live) y[row] = __fadd_rn(epi.residual[row], v);
+  } else if (epi.kind == PB_EPI_ROPE_KV) {
+    // rows of a tile are all q, all k or all v (q_rows, kv_rows % 8 == 0)
+    const float vp = __shfl_sync(0xffffffffu, v, lane ^ 4);  // partner row rr ^ 1
+    const int pos = epi.pos_dev ? *epi.pos_dev : epi.start_pos;
+    const bool in_range = pos >= 0 && pos < epi.max_len;
+    if (live && !in_range && rr == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+    if (live && in_range) {
+      const int kvd = epi.kv_rows;
+      if (row < epi.q_rows + kvd) {  // q or k: rotate the pair (2i, 2i+1)
+        const bool isq = row < epi.q_rows;
+        const int rel = isq ? row : row - epi.q_rows;
+        const int pr = (rel % epi.head_dim) >> 1;
+        const double2 cs = epi.rope_tab[(size_t)pos * (epi.head_dim >> 1) + pr];
+        const bool even = (rr & 1) == 0;
+        const double x0 = even ? (double)v : (double)vp, x1 = even ? (double)vp : (double)v;
+        const float o = even ? (float)__dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y))
+                             : (float)__dadd_rn(__dmul_rn(x0, cs.y), __dmul_rn(x1, cs.x));
+        if (isq) y[row] = o;
+        else epi.kc[(size_t)pos * kvd + rel] = o;
+      } else {
+        epi.vc[(size_t)pos * kvd + (row - epi.q_rows - kvd)] = v;
+      }
+    }
+  } else if (epi.kind == PB_EPI_ARGMAX) {  // logits and the greedy key (llama-streaming.js:899-909)
+    if (live) y[row] = v;
+    unsigned long long key = live ? pb_argmax_key(v, row) : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
+      key = t > key ? t : key;
+    }
+    if (lane == 0 && key) atomicMax(epi.amax, key);
+  } else {  // PB_EPI_SWIGLU4: rows 0-3 gate, 4-7 up of indices 4*tile .. 4*tile+3
+    const float u = __shfl_sync(0xffffffffu, v, (lane + 16) & 31);
+    if (L == 0 && rr < 4 && row < N) {
+      const double g = v;
+      const double silu = __ddiv_rn(g, __dadd_rn(1.0, exp(-g)));
+      epi.h_out[tile * 4 + rr] = (float)__dmul_rn(silu, (double)u);
+    }
+  }
+}
+
+
 // Per-sequence strides (floats) of batched attention launches: blockIdx.z is
 // the sequence; its query rows, cache and output rows sit these far apart.
 struct pb_seq_geo {
@@ -361,6 +425,8 @@ int pb_launch_argmax_finish(pb_ctx* ctx, const unsigned long long* key, int* idx
 int pb_qmat_alloc(pb_ctx* ctx, int type, int layout, int N, int K, pb_qmat** out);
 int pb_qmat_pack_from_device(pb_ctx* ctx, pb_qmat* m, const void* gguf_dev);
 int pb_setup_q4_kernels(void);
+int pb_setup_mvi_kernels(void);
+int pb_launch_mvi(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows, const pb_mv_epi& epi);
 int pb_setup_ops_kernels(void);
 int pb_setup_gemm_kernels(void);
 int pb_setup_sample_kernels(void);

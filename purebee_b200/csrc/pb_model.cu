@@ -378,6 +378,7 @@ __global__ void k_tile_f32(const float* __restrict__ src, int V, int dim, float*
 
 static int pack_rows(pb_model* m, pb_qmat* dst, const void* gguf_dev, int rows, int row_off, int interleave4) {
   pb_ctx* ctx = m->ctx;
+  dst->mma_ok = false;  // the tensor-core copy no longer mirrors the matrix
   int64_t tot = (int64_t)rows * dst->nb;
   k_pack_rows<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>((const uint8_t*)gguf_dev, rows, row_off, interleave4,
                                                           dst->nb, dst->type, dst->layout, dst->qs, dst->d, 0);
@@ -548,7 +549,10 @@ static int model_tensor_io(pb_model* m, int layer, int which, void* host, size_t
     mshape(c, which, &rows, &k);
     dst = fused_target(m, layer, which, &off, &il);
   }
-  if (!get) PB_TRY_CUDA(ctx, cudaMemcpyAsync(ctx->scratch, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  if (!get) {
+    PB_TRY_CUDA(ctx, cudaMemcpyAsync(ctx->scratch, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    dst->mma_ok = false;
+  }
   int64_t tot = (int64_t)rows * dst->nb;
   k_pack_rows<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>((const uint8_t*)ctx->scratch, rows, off, il, dst->nb,
                                                           dst->type, dst->layout, dst->qs, dst->d, get);
@@ -736,12 +740,18 @@ static int launch_embed(pb_model* m, const int* toks, int M) {
   return PB_OK;
 }
 
-// The row-layout copy of the quantized head table the fast head reads (the
-// tiled table serves the exact batch_dot kernel and the embedding lookup).
-// Allocates: called before any recording.
+// The copies the fast mode reads: the layer matrices' tensor-core copies and
+// the row-layout copy of the quantized head table (the tiled table serves
+// the exact batch_dot kernel and the embedding lookup; its row copy gets a
+// tensor-core copy of its own).  Allocates: called before any recording.
 static int ensure_head_rows(pb_model* m) {
   pb_ctx* ctx = m->ctx;
-  if (m->head_rows || ctx->matvec_mode != PB_MATVEC_FAST || m->c.kind != PB_MODEL_STREAMING_Q4) return PB_OK;
+  if (ctx->matvec_mode != PB_MATVEC_FAST || m->c.kind != PB_MODEL_STREAMING_Q4) return PB_OK;
+  // the layer matrices' tensor-core copies (rebuilt after their weights change)
+  for (auto* v : {&m->qkv, &m->wo, &m->gu, &m->w2})
+    for (pb_qmat* w : *v)
+      if (w && !w->mma_ok) PB_TRY(pb_qmat_build_mma(ctx, w));
+  if (m->head_rows) return PB_OK;
   const pb_qmat* t = head_of(m);
   if (!t || (t->type != PB_TYPE_Q4_0 && t->type != PB_TYPE_Q8_0)) return PB_OK;
   const size_t bytes = (size_t)t->N * t->nb * (t->type == PB_TYPE_Q4_0 ? 18 : 34);

@@ -328,9 +328,6 @@ __device__ __forceinline__ void mv_load(MvBuf& R, const uint8_t* __restrict__ qs
   }
 }
 
-__device__ __forceinline__ void mv_epilogue(float v, int tile, int N, int row_end, float* __restrict__ y,
-                                            const pb_mv_epi& epi, int* err);
-
 // Chain of slot `slot`'s tile over the nb block partials, then the epilogue.
 // Lane = 4 * row + L.
 __device__ __forceinline__ void mv_chain(const float* __restrict__ pc, int nb, int tile, int N, int row_end,
@@ -353,60 +350,7 @@ __device__ __forceinline__ void mv_chain(const float* __restrict__ pc, int nb, i
   const float a2 = __shfl_sync(0xffffffffu, acc, base + 2);
   const float a3 = __shfl_sync(0xffffffffu, acc, base + 3);
   const float v = __fadd_rn(__fadd_rn(a1, a3), __fadd_rn(a0, a2));
-  mv_epilogue(v, tile, N, row_end, y, epi, err);
-}
-
-// The fused epilogue of an 8-row tile: every lane of quad r (lanes 4r ..
-// 4r + 3) holds row r's value v; the quad's lane 0 stores.
-__device__ __forceinline__ void mv_epilogue(float v, int tile, int N, int row_end, float* __restrict__ y,
-                                            const pb_mv_epi& epi, int* err) {
-  const int lane = threadIdx.x & 31, rr = lane >> 2, L = lane & 3;
-  const int row = tile * 8 + rr;
-  const bool live = L == 0 && row < row_end && row < N;
-  if (epi.kind == PB_EPI_STORE) {
-    if (live) y[row] = v;
-  } else if (epi.kind == PB_EPI_RESIDUAL) {
-    if (live) y[row] = __fadd_rn(epi.residual[row], v);
-  } else if (epi.kind == PB_EPI_ROPE_KV) {
-    // rows of a tile are all q, all k or all v (q_rows, kv_rows % 8 == 0)
-    const float vp = __shfl_sync(0xffffffffu, v, lane ^ 4);  // partner row rr ^ 1
-    const int pos = epi.pos_dev ? *epi.pos_dev : epi.start_pos;
-    const bool in_range = pos >= 0 && pos < epi.max_len;
-    if (live && !in_range && rr == 0) pb_raise(err, PB_DEVERR_BOUNDS);
-    if (live && in_range) {
-      const int kvd = epi.kv_rows;
-      if (row < epi.q_rows + kvd) {  // q or k: rotate the pair (2i, 2i+1)
-        const bool isq = row < epi.q_rows;
-        const int rel = isq ? row : row - epi.q_rows;
-        const int pr = (rel % epi.head_dim) >> 1;
-        const double2 cs = epi.rope_tab[(size_t)pos * (epi.head_dim >> 1) + pr];
-        const bool even = (rr & 1) == 0;
-        const double x0 = even ? (double)v : (double)vp, x1 = even ? (double)vp : (double)v;
-        const float o = even ? (float)__dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y))
-                             : (float)__dadd_rn(__dmul_rn(x0, cs.y), __dmul_rn(x1, cs.x));
-        if (isq) y[row] = o;
-        else epi.kc[(size_t)pos * kvd + rel] = o;
-      } else {
-        epi.vc[(size_t)pos * kvd + (row - epi.q_rows - kvd)] = v;
-      }
-    }
-  } else if (epi.kind == PB_EPI_ARGMAX) {  // logits and the greedy key (llama-streaming.js:899-909)
-    if (live) y[row] = v;
-    unsigned long long key = live ? pb_argmax_key(v, row) : 0ull;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long t = __shfl_xor_sync(0xffffffffu, key, o);
-      key = t > key ? t : key;
-    }
-    if (lane == 0 && key) atomicMax(epi.amax, key);
-  } else {  // PB_EPI_SWIGLU4: rows 0-3 gate, 4-7 up of indices 4*tile .. 4*tile+3
-    const float u = __shfl_sync(0xffffffffu, v, (lane + 16) & 31);
-    if (L == 0 && rr < 4 && row < N) {
-      const double g = v;
-      const double silu = __ddiv_rn(g, __dadd_rn(1.0, exp(-g)));
-      epi.h_out[tile * 4 + rr] = (float)__dmul_rn(silu, (double)u);
-    }
-  }
+  pb_mv_epilogue(v, tile, N, 0, row_end, y, epi, err);
 }
 
 template <int TYPE, int NT>
@@ -984,7 +928,7 @@ k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, i
       const int rr = lane >> 2;
       float s_ = pbuf[(size_t)tl * KC * 8 + rr];
       for (int c = 1; c < KC; ++c) s_ = __fadd_rn(s_, pbuf[((size_t)tl * KC + c) * 8 + rr]);
-      mv_epilogue(s_, t, N, row_end, y, epi, err);
+      pb_mv_epilogue(s_, t, N, 0, row_end, y, epi, err);
     }
   }
   asm volatile("cp.async.wait_all;" ::: "memory");  // no copy outlives the CTA
@@ -1044,6 +988,8 @@ int pb_launch_head_fast(pb_ctx* ctx, const pb_qmat* t, const float* h, const flo
   e.norm_w = norm_w;
   e.eps = eps;
   e.amax = amax;
+  if (t->mq && t->mma_ok && t->layout == PB_LAYOUT_ROWS && t->type == PB_TYPE_Q4_0)
+    return pb_launch_mvi(ctx, t, h, logits, 0, t->N, e);
   return launch_mvf(ctx, t, h, logits, 0, (t->N + 7) / 8, t->N, e);
 }
 
@@ -1100,7 +1046,11 @@ int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, in
   pb_mv_epi epi = epi_in ? *epi_in : pb_mv_epi();
   if (!y && epi.kind != PB_EPI_SWIGLU4) return PB_ERR_ARG;
   const int tile_begin = row0 / 8, ntiles = pb_cdiv(rows, 8);
-  if (fast) return launch_mvf(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
+  if (fast) {
+    // the int8 tensor-core kernel on the matrix's current tensor-core copy, else the f32 one
+    if (w->mq && w->mma_ok && w->layout == PB_LAYOUT_ROWS) return pb_launch_mvi(ctx, w, x, y, row0, rows, epi);
+    return launch_mvf(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
+  }
   if (w->type == PB_TYPE_Q4_0) return launch_mv<PB_TYPE_Q4_0>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
   return launch_mv<PB_TYPE_Q4_1>(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);
 }
