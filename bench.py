@@ -266,7 +266,8 @@ def row_split_vocab(ctx, torch, dist, world, peak, reps=40):
             "allgather": "pb_comm_allgather (NCCL, library stream)"}
 
 
-def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512, steps=256, dist=None):
+def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512, steps=256, dist=None, warm=2,
+                clk=None, e2e=False):
     """n_seqs seeded prompts of n_prompt tokens prefilled as one
     batch (tensor-core GEMMs), then `steps` greedy decode steps of every
     sequence (one replayed graph per step).  With N ranks the model is row
@@ -303,15 +304,40 @@ def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512
     e1.record(stream)
     e1.synchronize()
     prefill_ms = max_over_ranks(e0.elapsed_time(e1))
-    bt.decode(2)  # warm: records the decode graph
+    l0 = ctx.launches
+    bt.decode(1)  # records the decode graph (its launches are counted once, here)
+    launches_per_step = ctx.launches - l0
+    if warm > 1:
+        bt.decode(warm - 1)
     ctx.sync()
     if dist:
         dist.barrier()
-    e1.record(stream)
-    toks = bt.decode(steps)
-    e2.record(stream)
-    e2.synchronize()
+    from contextlib import nullcontext
+    with clk if clk is not None else nullcontext():
+        e1.record(stream)
+        toks = bt.decode(steps)
+        e2.record(stream)
+        e2.synchronize()
     decode_ms = max_over_ranks(e1.elapsed_time(e2))
+    e2e_line = None
+    if e2e:
+        # through the public calls with host buffers: the seeded prompts in,
+        # `steps` greedy steps with every step's tokens copied out
+        ctx.sync()
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        bt.prefill(prompts)
+        bt.decode(steps)
+        wall = time.perf_counter() - t0
+        if dist:
+            t = torch.tensor([wall], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            wall = float(t.item())
+        e2e_line = {"value": round(n_seqs * steps / wall, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": int(prompts.nbytes // steps), "d2h_bytes_per_step": 4 * n_seqs,
+                    "api": "BatchedLlamaRuntime.prefill (host prompts) + decode (tokens to the host every step), "
+                           "wall clock, generated tokens / s"}
     bt.free()  # before the communicator: the decode graph holds its NCCL work
     if comm is not None:
         comm.free()
@@ -339,8 +365,75 @@ def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512
             "decode_frac_of_hbm": round(step_bytes / dec_s / 1e9 / (world * peak), 3),
             "decode_allgather_bytes_per_step": int(gathered) if world > 1 else 0,
             "tokens_sample": toks[-1][:4].tolist(),
+            "decode_launches_per_step": int(launches_per_step),
+            "e2e": e2e_line,
             "arithmetic": "projections and head: f16 operands, f32 accumulation (tcgen05); prefill attention: f16 "
                           "operands, f32 accumulation (mma.sync)"}
+
+
+def run_split(args, rank, world, torch, dist):
+    """N > 1: the batched configuration row-split over the N GPUs
+    (north_star: batch-1 decode is a one-GPU figure, the batched config is the
+    one reported at 1/2/4/8 GPUs).  A step is one batched decode step of all
+    64 sequences; W warm-up and K timed steps after the 512-token prefill,
+    device event time, max over ranks; the work is fixed, so the scaling is
+    strong.  Rank 0 first times the same workload on its GPU alone, the
+    one-GPU reference the speed-up is read against.  Config 2's vocab-head
+    row split is reported alongside."""
+    from purebee_b200 import _native as N
+    dev = int(os.environ.get("LOCAL_RANK", 0))
+    ctx = N.Context(dev)
+    ctx.set_timeout_ms(120000)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.ExternalStream(N.lib().pb_stream(ctx.h), device=dev)
+    peak, peak_kind = load_peaks()
+    flop_peak = load_flop_peak()
+    rt = build_model(ctx)
+    one = None
+    if rank == 0:
+        one = run_batched(ctx, torch, stream, rt, peak, flop_peak, steps=args.steps, warm=args.warmup, dist=None)
+    dist.barrier()
+    clk = ClockSampler(dev)
+    sp = run_batched(ctx, torch, stream, rt, peak, flop_peak, steps=args.steps, warm=args.warmup, dist=dist, clk=clk,
+                     e2e=True)
+    split = row_split_vocab(ctx, torch, dist, world, peak)
+    result = None
+    if rank == 0:
+        n_seqs = 64
+        result = {
+            "metric": METRIC,
+            "value": sp["decode_tok_s"],
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": sp["decode_ms_per_step"],
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "u4 weights; f16 tensor-core operands, f32 accumulation",
+            "data": "synthetic (seeded N(0,0.02) weights, seeded prompt tokens)",
+            "config": {"workload": "llama3.2-1B-shape Q4_0 batched serving, 64 seqs x 512-token prompts, greedy "
+                                   "decode steps (configs[4])", "model": "llama3.2-1B-shape", "global_batch": n_seqs,
+                       "seq_len": 2048, "prompt": 512, "parallelism": f"rowsplit{world}",
+                       "rope_scaling": "off (the reference applies none)",
+                       "l2": "a decode step reads the weights once plus every sequence's KV (> 126 MB L2)"},
+            "one_gpu_same_workload": {"decode_tok_s": one["decode_tok_s"], "decode_ms_per_step":
+                                      one["decode_ms_per_step"], "prefill_ms": one["prefill_ms"]},
+            "batched": sp,
+            "roofline": {"bound": "hbm", "kernel": "the batched decode step (every kernel; weights / N and the "
+                                                  "rank's KV per GPU)",
+                         "achieved": round(sp["decode_step_bytes"] / (sp["decode_ms_per_step"] / 1e3) / 1e9 / world, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": sp["decode_frac_of_hbm"],
+                         "traffic": None},
+            "row_split": split,
+            "gpu_launches": sp["decode_launches_per_step"] * args.steps,
+            "clocks": clk.summary(),
+            "e2e": sp["e2e"],
+        }
+    rt.shutdown()
+    ctx.close()
+    return result
 
 
 def run_ours(args, rank, world, torch, dist):
@@ -688,7 +781,7 @@ def main():
         td.init_process_group("nccl", timeout=timedelta(seconds=180),
                               device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))))
         dist = td
-    res = run_ours(args, rank, world, torch, dist)
+    res = run_split(args, rank, world, torch, dist) if world > 1 else run_ours(args, rank, world, torch, dist)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if dist:

@@ -8,11 +8,11 @@
 // The 4-bit codes go to the tensor cores as unsigned bytes and x as signed
 // bytes: mma.sync m16n8k32 (u8 x s8 -> s32) sums exact integer products.  x
 // is written per 32-value block b as three signed digits,
-//     x[k] ~= 2^e_b / 127 * (d0 + d1 / 128 + d2 / 16384),
-// d0 in [-127, 127], d1 and d2 in [-64, 64] (e_b: the block maximum's binary
-// exponent, so 2^-e_b scales exactly); the representation error is below
-// 2^-22 of the block's largest |x|.  The -8 of the codes is applied through
-// T_b = sum of each digit over the block, also exact.
+//     x[k] ~= 2^e_b / 127 * (d0 + d1 / 254 + d2 / 254^2),
+// each in [-127, 127] (e_b: the block maximum's binary exponent, so 2^-e_b
+// scales exactly); the representation error is about 1e-7 of the block's
+// largest |x|.  The -8 of the codes is applied through T_b = the sum of
+// each digit over the block, also exact.
 //
 // Fragments: a warp takes a 16-row tile.  For the 8 blocks of a span (256 k)
 // the MMA's 8 columns are the 8 blocks: at step j (block 8s + j) only the
@@ -164,10 +164,10 @@ __device__ __forceinline__ void mvi_stage(const float* __restrict__ x, const flo
       int e = 0;
       if (m > 0.0f && m <= 3.402823466e38f) frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1): |x| * 2^-e < 1
       const float v = m <= 3.402823466e38f ? __fmul_rn(ldexpf(xv[u], -e), 127.0f) : 0.0f;
-      const float d0 = rintf(v);
-      const float r1 = __fmul_rn(__fsub_rn(v, d0), 128.0f);  // v - d0 is exact; * 128 too
+      const float d0 = rintf(v);                              // |v| < 127: d0 in [-127, 127]
+      const float r1 = __fmul_rn(__fsub_rn(v, d0), 254.0f);  // v - d0 in [-0.5, 0.5] (exact): r1 in [-127, 127]
       const float d1 = rintf(r1);
-      const float d2 = rintf(__fmul_rn(__fsub_rn(r1, d1), 128.0f));
+      const float d2 = rintf(__fmul_rn(__fsub_rn(r1, d1), 254.0f));
       const int i0 = (int)d0, i1 = (int)d1, i2 = (int)d2;
       // byte `lane` of each digit: word lane / 4; lane t of the fragment keeps words t and 4 + t
       const int wd = lane >> 2, tt = wd & 3, hh = wd >> 2;
@@ -272,7 +272,7 @@ k_mvi(const uint8_t* __restrict__ mq, const uint16_t* __restrict__ md, int N, in
           const int4 ti = (c & 1) ? ti1 : ti0;
           const int off = c < 2 ? 8 : 128;  // 8 * T, and 16 * 8 * T for the rows carrying 16 q
           const int e0 = D0[c] - off * ti.x, e1 = D1[c] - off * ti.y, e2 = D2[c] - off * ti.z;
-          float v = __fmaf_rn((float)e2, 1.0f / 16384.0f, __fmaf_rn((float)e1, 1.0f / 128.0f, (float)e0));
+          float v = __fmaf_rn((float)e2, 1.0f / 64516.0f, __fmaf_rn((float)e1, 1.0f / 254.0f, (float)e0));
           if (c >= 2) v = __fmul_rn(v, 1.0f / 16.0f);
           const float sc = __fmul_rn(pb_f16_wasm(dw[c]), __int_as_float(ti.w));
           if (c < 2) acc_lo = __fmaf_rn(v, sc, acc_lo);
