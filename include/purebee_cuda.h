@@ -151,6 +151,13 @@ int pb_qmat_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, float* y_d
 #define PB_MATVEC_EXACT 1
 int pb_set_matvec_mode(pb_ctx* ctx, int mode);
 int pb_matvec_mode(const pb_ctx* ctx);
+/* Fast mode, Q4_0 matrices in the row layout with a tensor-core copy: the
+ * int8 tensor-core kernel runs the matvecs of a matrix of at least `rows`
+ * rows, the f32 kernel those of smaller ones (default 32768: the LM head;
+ * environment PB_MVI_MIN_ROWS at pb_init).  Both agree with the exact kernel
+ * within the fast mode's tolerance.  A tuning knob with no counterpart in
+ * the reference. */
+int pb_set_mvi_min_rows(pb_ctx* ctx, int rows);
 /* wasm-q4.js:716-747 q4_0_matvec(x, rawBuf, N, K): host buffers in and out. */
 int pb_q4_0_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, int N, int K, float* y_host);
 /* wasm-q4.js:758-785 q4_1_matvec(x, rawBuf, N, K) */

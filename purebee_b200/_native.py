@@ -104,6 +104,7 @@ SIGNATURES = {
     "pb_attn_decode": (I, [V, V, V, V, I, I, I, I, I, V]),
     "pb_set_matvec_mode": (I, [V, I]),
     "pb_matvec_mode": (I, [V]),
+    "pb_set_mvi_min_rows": (I, [V, I]),
     "pb_swiglu": (I, [V, V, V, I, V]),
     "pb_quantize_q8a": (I, [V, V, I64, V, V]),
     "pb_quantize_q4a": (I, [V, V, I64, V, V]),
@@ -279,6 +280,10 @@ class Context:
     @property
     def matvec_mode(self) -> int:
         return int(lib().pb_matvec_mode(self.h))
+
+    def set_mvi_min_rows(self, rows: int) -> None:
+        """Fast mode: matrix rows from which Q4_0 matvecs take the int8 tensor-core kernel."""
+        self._check(lib().pb_set_mvi_min_rows(self.h, int(rows)))
 
     def set_timeout_ms(self, ms: int) -> None:
         self._check(lib().pb_set_timeout_ms(self.h, ms))

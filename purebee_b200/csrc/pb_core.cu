@@ -115,6 +115,8 @@ extern "C" int pb_init(int device, pb_ctx** out) {
     return PB_ERR_STATE;
   }
   ctx->sm_count = prop.multiProcessorCount;
+  // tuning override: matrix rows from which the fast mode takes the int8 tensor-core matvec
+  if (const char* ev = getenv("PB_MVI_MIN_ROWS")) ctx->mvi_min_rows = atoi(ev);
   const char* nopdl = getenv("PB_NO_PDL");  // programmatic dependent launch off (debugging aid)
   ctx->pdl = !(nopdl && nopdl[0] == '1');
 
@@ -171,6 +173,12 @@ extern "C" int pb_set_matvec_mode(pb_ctx* ctx, int mode) {
 }
 
 extern "C" int pb_matvec_mode(const pb_ctx* ctx) { return ctx ? ctx->matvec_mode : -1; }
+
+extern "C" int pb_set_mvi_min_rows(pb_ctx* ctx, int rows) {
+  if (!ctx || rows < 0) return PB_ERR_ARG;
+  ctx->mvi_min_rows = rows;
+  return PB_OK;
+}
 
 extern "C" int pb_set_timeout_ms(pb_ctx* ctx, int timeout_ms) {
   if (!ctx || timeout_ms <= 0) return PB_ERR_ARG;

@@ -19,6 +19,7 @@ struct pb_ctx {
   int* d_err = nullptr;         // device error word: 0 = ok
   int64_t launches = 0;
   bool pdl = true;              // launch matvecs with programmatic stream serialization
+  int mvi_min_rows = 32768;     // fast mode: matrices of this many rows on take the int8 tensor-core matvec
   std::string err;
   // scratch for one-shot host-buffer calls (grown on demand)
   void* scratch = nullptr;

@@ -133,9 +133,18 @@ def test_resident_matvec_row_split(native, ctx, oracle, exact_mode):
 RTOL_MATVEC_FAST = 2e-6
 
 
+@pytest.fixture(params=["f32", "int8"])
+def fast_kernel(request, native, ctx):
+    """Each fast-mode Q4_0 kernel in turn: the f32 one, and the int8
+    tensor-core one (taken for every matrix size for the test)."""
+    ctx.set_mvi_min_rows(1 << 30 if request.param == "f32" else 0)
+    yield request.param
+    ctx.set_mvi_min_rows(32768)
+
+
 @pytest.mark.parametrize("N,K", [(64, 64), (136, 576), (512, 1536), (3072, 2048), (2048, 8192), (16384, 2048),
                                  (1000, 4096), (40, 16384)])
-def test_fast_matvec_shapes(native, ctx, oracle, N, K):
+def test_fast_matvec_shapes(native, ctx, oracle, fast_kernel, N, K):
     """Every decode shape of configs[2]/[3] and ragged ones (N not a multiple
     of 8, K with a partial last 32-block chunk): within RTOL_MATVEC_FAST of
     the reference's lane order, and row splits give the same bits as one call."""
@@ -155,7 +164,7 @@ def test_fast_matvec_shapes(native, ctx, oracle, N, K):
     assert bits_equal(dz.download(count=N), y)
 
 
-def test_fast_matvec_special_scales(native, ctx, oracle):
+def test_fast_matvec_special_scales(native, ctx, oracle, fast_kernel):
     """Zero, -0, subnormal (decoded as 0 the WASM way) and exponent-31 scales."""
     rng = np.random.default_rng(14)
     N, K = 64, 512
