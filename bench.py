@@ -666,6 +666,54 @@ def run_reference(args):
             "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_exchange_case(args):
+    """`--case exchange:BYTES` under torchrun: the row split's exchange step
+    alone, an in-place all-gather of BYTES per rank over a registered buffer
+    (pb_comm_allgather_inplace: the peer-memory kernel when the ranks have
+    peer access, else NCCL).  W untimed calls, then K back to back on the
+    context stream, timed with CUDA events; rank 0 prints the max over ranks
+    in microseconds per exchange."""
+    import ctypes
+    import torch
+    import torch.distributed as td
+    from datetime import timedelta
+    from purebee_b200 import _native as N
+    from purebee_b200.thread_pool import NcclComm
+    nbytes = int(args.case.split(":", 1)[1])
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    td.init_process_group("gloo", timeout=timedelta(seconds=120))
+    ctx = N.Context(local)
+    stream = torch.cuda.ExternalStream(N.lib().pb_stream(ctx.h), device=local)
+    comm = NcclComm.from_torch(ctx)
+    buf = ctx.alloc(nbytes * world)
+    pb = ctypes.c_void_p()
+    ctx._check(N.lib().pb_comm_register(comm.h, buf.ptr, ctypes.byref(pb)))
+    call = lambda: ctx._check(N.lib().pb_comm_allgather_inplace(comm.h, pb.value, nbytes))
+    for _ in range(args.warmup):
+        call()
+    ctx.sync()
+    td.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        call()
+    b.record(stream)
+    b.synchronize()
+    us = torch.tensor([a.elapsed_time(b) * 1e3 / args.steps])
+    td.all_reduce(us, op=td.ReduceOp.MAX)
+    if rank == 0:
+        print(json.dumps({"case": args.case, "n_gpus": world, "us_per_exchange": round(float(us[0]), 3),
+                          "bytes_per_rank": nbytes, "transport": "peer memory" if comm.peer_access else "NCCL",
+                          "steps": args.steps}), flush=True)
+    ctx._check(N.lib().pb_comm_deregister(comm.h, pb.value))
+    comm.free()
+    td.barrier()
+    td.destroy_process_group()
+    ctx.close()
+
+
 def run_case(args):
     """One kernel on a small case, for profiler captures: `--case matvec:NxK`
     runs the Q4_0 matvec on one seeded N x K matrix (W plain launches, then K
@@ -675,6 +723,9 @@ def run_case(args):
     from purebee_b200 import _native as N
     L = N.lib()
     kind, shape = args.case.split(":", 1)
+    if kind == "exchange":
+        run_exchange_case(args)
+        return
     if kind == "batched":  # batched:BxP -> one batched prefill of B x P seeded tokens, 3 decode steps
         from purebee_b200 import _native as N
         from purebee_b200.runtime import BatchedLlamaRuntime
@@ -760,7 +811,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched configuration (configs[4])")
     ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK, head:VxD, gemm:MxNxK, batched:BxP "
-                                                 "(batched prefill + 3 steps), or decode:N[@POS] (N decode steps)")
+                                                 "(batched prefill + 3 steps), decode:N[@POS] (N decode steps), or exchange:BYTES "
+                                                 "(under torchrun: in-place all-gathers of BYTES per rank)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.case:

@@ -175,6 +175,22 @@ int pb_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int M, int ldx
  * fused kernel), M >= 512 the persistent TMA kernel.  With the activations
  * already rounded to f16, M <= 64 gives the same bits as pb_q4_gemm. */
 int pb_q4_gemm_f16(pb_ctx* ctx, const pb_qmat* w, const void* x16_dev, int M, float* c_dev, int ldc);
+/* pb_q4_gemm with a precision choice: terms == 1 is pb_q4_gemm; terms == 3
+ * splits both operands into f16 pairs, hi = f16(v) and lo = f16(v - hi) (the
+ * weight value (q-8)*d splits exactly, x keeps about 22 bits), and sums
+ * hi*hi + hi*lo + lo*hi on the tensor cores, for three times the tensor-core
+ * work.  C then agrees with the reference's f32 arithmetic within the
+ * tensor cores' f32 accumulation error.  The batched model uses terms == 3.
+ * Both forms decode the block scale as wasm-q4.js:88-109 does (a zero
+ * exponent is +0). */
+int pb_q4_gemm_ex(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int M, int ldx, float* c_dev, int ldc,
+                  int terms);
+/* The three-term product with activations already split: xhl_dev holds each
+ * row of K values as 2K halves, per 64-wide K group its 64 hi halves then its
+ * 64 lo halves (the layout the batched model's producers write).  M <= 64 or
+ * M >= 512 with K % 64 == 0; the same bits as pb_q4_gemm_ex(terms = 3) on the
+ * f32 activations the pairs came from. */
+int pb_q4_gemm_hl(pb_ctx* ctx, const pb_qmat* w, const void* xhl_dev, int M, float* c_dev, int ldc);
 /* wasm-q4.js:798-839 lmHead(hidden, embData, V, D): f32 row-major table on
  * the host, batch_dot lane order (wasm-q4.js:447-566). */
 int pb_lm_head(pb_ctx* ctx, const float* h_host, const float* emb_host, int V, int D, float* logits_host);
@@ -435,6 +451,12 @@ int pb_batch_prefill(pb_batch* b, const int* tokens_host, int n_prompt, int* nex
  * step); tokens_host [steps][n_seqs] (optional) gets the generated tokens,
  * logits_host [n_seqs][vocab] (optional) the last step's logits. */
 int pb_batch_decode(pb_batch* b, int steps, int* tokens_host, float* logits_host);
+/* GEMM precision of the batch: 3 (the default) runs every projection and the
+ * head as the three-term product of pb_q4_gemm_ex; 1 rounds each operand to
+ * f16 once (a third of the tensor-core work, logits about 3e-3 of their
+ * scale from the one-sequence path at the Llama-3.2-1B shape).  Set between
+ * steps.  No counterpart in the reference, which serves one sequence. */
+int pb_batch_set_precision(pb_batch* b, int terms);
 
 /* ------------------------------------------------------------------ */
 /* row split over GPUs (thread-pool.js:165-246 splits a matvec's output   */

@@ -165,10 +165,13 @@ SIGNATURES = {
     "pb_model_decode_bytes": (I64, [V, I]),
     "pb_model_decode_launches": (I, [V]),
     "pb_q4_gemm_f16": (I, [V, V, V, I, V, I]),
+    "pb_q4_gemm_ex": (I, [V, V, V, I, I, V, I, I]),
+    "pb_q4_gemm_hl": (I, [V, V, V, I, V, I]),
     "pb_batch_create": (I, [V, I, ctypes.POINTER(V)]),
     "pb_batch_free": (I, [V]),
     "pb_batch_prefill": (I, [V, V, I, V, V]),
     "pb_batch_decode": (I, [V, I, V, V]),
+    "pb_batch_set_precision": (I, [V, I]),
     "pb_batch_split_plan": (I, [ctypes.POINTER(ModelConfig), I, I, ctypes.POINTER(SplitPlan)]),
     "pb_batch_create_split": (I, [V, I, V, ctypes.POINTER(V)]),
     "pb_batch_create_group": (I, [V, I, I, ctypes.POINTER(V)]),

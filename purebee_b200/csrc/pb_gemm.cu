@@ -4,11 +4,18 @@
 // device layout; the batched LM head runs it over the tiled table).  This is the batched prefill / batched decode form of the
 // reference's per-row matvec (wasm-q4.js:118-267) and of its prefill matmul
 // (llama-streaming.js:398 -> wasm-simd.js:71-91).  It does not reproduce the
-// reference's f32 operation order: each operand is rounded to f16 once (the
-// weight value (q-8)*d is exact in f32 and rounded once; x is rounded once),
-// products are exact and the sums run in f32 on the tensor cores.  Results
-// therefore agree with the reference within a stated relative tolerance, not
-// bit for bit; the batch-1 decode path keeps the exact kernels.
+// reference's f32 operation order.  The scale is decoded as the reference
+// decodes it (wasm-q4.js:88-109: a zero exponent is +0), and the weight value
+// (q-8)*d is exact in f32.  One term (pb_gemm_epi terms == 1): each operand
+// is rounded to f16 once.  Three terms (the batched model's default): each
+// operand v becomes the f16 pair hi = f16(v), lo = f16(v - hi) -- exact for
+// the weights, about 22 bits for x -- and hi*hi + hi*lo + lo*hi run on the
+// tensor cores.  Products are exact and the sums run in f32 on the tensor
+// cores, so results agree with the reference within a stated relative
+// tolerance (about 3e-3 with one term, the accumulation bound with three),
+// not bit for bit; the batch-1 decode path keeps the exact kernels.  Values
+// past the f16 range (a scale with exponent 31, |x| > 65504) overflow the
+// operands.
 //
 // One CTA computes a 128-row x 128-token tile with tcgen05.mma (kind::f16,
 // M = 128, N = 128, K = 16 per instruction), the accumulator in 128 TMEM
@@ -91,6 +98,13 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// The lo halves of (a, b) given their hi pair: f16(a - hi_a), f16(b - hi_b)
+// (each difference exact in f32).
+__device__ __forceinline__ uint32_t pack_lo2(float a, float b, uint32_t hi) {
+  const __half2 h = *reinterpret_cast<const __half2*>(&hi);
+  return pack_h2(__fsub_rn(a, __low2float(h)), __fsub_rn(b, __high2float(h)));
+}
+
 }  // namespace
 
 // One TMEM row (weight row `row`) of 32 token columns m0c .. m0c+31 through
@@ -107,9 +121,10 @@ __device__ __forceinline__ void gemm_emit32(const uint32_t (&v)[32], bool zero, 
       if (row < N && m < M && (row & 4) == 0) {
         const float silu = __fdividef(r, 1.0f + __expf(-r));
         const float h = __fmul_rn(silu, partner);
-        const size_t o = (size_t)m * (N / 2) + 4 * (row >> 3) + (row & 3);
-        if (epi.h16) epi.h16[o] = __float2half_rn(h);
-        else epi.h32[o] = h;
+        const int f = 4 * (row >> 3) + (row & 3);
+        if (epi.h16 && epi.terms == 3) pb_store_hl(epi.h16, pb_hl_index((size_t)m * N, f), h);
+        else if (epi.h16) epi.h16[(size_t)m * (N / 2) + f] = __float2half_rn(h);
+        else epi.h32[(size_t)m * (N / 2) + f] = h;
       }
     } else if (row < N && m < M) {
       float* c = C + (size_t)m * ldc + row;
@@ -121,7 +136,10 @@ __device__ __forceinline__ void gemm_emit32(const uint32_t (&v)[32], bool zero, 
 // TOK tokens per CTA (MMA N = 64 or 128).  grid.z splits K: CTA z covers K
 // steps [z*kper, (z+1)*kper) and, when gridDim.z > 1, writes its partial tile
 // to C + z*M*ldc (a workspace the reduce kernel sums in order of z).
-template <int TOK, bool XCH>
+// TERMS == 3: a stage holds the hi and lo tiles of both operands (the weight
+// value splits exactly, x to about 22 bits) and each 16-wide K slice issues
+// hi*hi, hi*lo and lo*hi into the accumulator.
+template <int TOK, bool XCH, int TERMS>
 __global__ void __launch_bounds__(GM_THREADS, 1)
 k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int layout, int N, int N_pad, int nb,
              const float* __restrict__ X, int ldx, int M, float* __restrict__ C, int ldc, int kper, pb_gemm_epi epi,
@@ -174,7 +192,7 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
     if (b < nb && row < N_pad) {
       const size_t slot = (size_t)pb_slot(layout, row, b, nb);
       pl = __ldg(reinterpret_cast<const uint4*>(qs) + slot);
-      dsv = pb_f16_exact(__ldg(dsc + slot));
+      dsv = pb_f16_wasm(__ldg(dsc + slot));  // the reference's scale decode
     }
     const int k = kg * GM_KSTEP + xh * 32;
     const bool live = xlive_row && k < K;
@@ -188,10 +206,14 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
   if (ksteps > 0) load_step(kbeg);
 
   bool ok = true;
+  // stage tiles: A hi, B hi, then (TERMS == 3) A lo, B lo
+  constexpr int STAGE = (TERMS == 3 ? 4 : 2) * GM_TILE_BYTES;
   for (int ks = 0; ks < ksteps && ok; ++ks) {
     const int st = ks & 1;
-    unsigned char* sA = ring + st * GM_STAGE_BYTES;
+    unsigned char* sA = ring + st * STAGE;
     unsigned char* sB = sA + GM_TILE_BYTES;
+    unsigned char* sAl = sA + 2 * GM_TILE_BYTES;
+    unsigned char* sBl = sA + 3 * GM_TILE_BYTES;
     if (ks >= 2) ok = pb_mbar_wait(&bars[st], ((ks >> 1) - 1) & 1, err);  // MMAs of step ks-2 are done with it
     if (!ok) break;
     {
@@ -211,6 +233,14 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
         v.z = pack_h2(e[8 * c + 4], e[8 * c + 5]);
         v.w = pack_h2(e[8 * c + 6], e[8 * c + 7]);
         *reinterpret_cast<uint4*>(sA + sw128(wr, wblk * 4 + c)) = v;
+        if (TERMS == 3) {
+          uint4 l;
+          l.x = pack_lo2(e[8 * c + 0], e[8 * c + 1], v.x);
+          l.y = pack_lo2(e[8 * c + 2], e[8 * c + 3], v.y);
+          l.z = pack_lo2(e[8 * c + 4], e[8 * c + 5], v.z);
+          l.w = pack_lo2(e[8 * c + 6], e[8 * c + 7], v.w);
+          *reinterpret_cast<uint4*>(sAl + sw128(wr, wblk * 4 + c)) = l;
+        }
       }
     }
     if (xr_ < TOK) {
@@ -222,6 +252,14 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
         v.z = pack_h2(xa[2 * c + 1].x, xa[2 * c + 1].y);
         v.w = pack_h2(xa[2 * c + 1].z, xa[2 * c + 1].w);
         *reinterpret_cast<uint4*>(sB + sw128(xr_, xh * 4 + c)) = v;
+        if (TERMS == 3) {
+          uint4 l;
+          l.x = pack_lo2(xa[2 * c].x, xa[2 * c].y, v.x);
+          l.y = pack_lo2(xa[2 * c].z, xa[2 * c].w, v.y);
+          l.z = pack_lo2(xa[2 * c + 1].x, xa[2 * c + 1].y, v.z);
+          l.w = pack_lo2(xa[2 * c + 1].z, xa[2 * c + 1].w, v.w);
+          *reinterpret_cast<uint4*>(sBl + sw128(xr_, xh * 4 + c)) = l;
+        }
       }
     }
     if (ks + 1 < ksteps) load_step(kbeg + ks + 1);
@@ -231,9 +269,15 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
     if (tid == 0) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sB));
+      const uint64_t dal = sw128_desc(smem_addr(sAl)), dbl = sw128_desc(smem_addr(sBl));
 #pragma unroll
-      for (int kk = 0; kk < GM_KSTEP / 16; ++kk)  // +32 bytes (16 f16) along K per MMA
+      for (int kk = 0; kk < GM_KSTEP / 16; ++kk) {  // +32 bytes (16 f16) along K per MMA
         mma_f16(tmem_d, da + 2 * kk, db + 2 * kk, gm_idesc(TOK), (ks > 0 || kk > 0) ? 1u : 0u);
+        if (TERMS == 3) {
+          mma_f16(tmem_d, da + 2 * kk, dbl + 2 * kk, gm_idesc(TOK), 1u);
+          mma_f16(tmem_d, dal + 2 * kk, db + 2 * kk, gm_idesc(TOK), 1u);
+        }
+      }
       mma_commit(&bars[st]);
     }
   }
@@ -259,7 +303,7 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
   }
 }
 
-static size_t gm_smem() { return 2 * GM_STAGE_BYTES + 1024; }
+static size_t gm_smem(int terms) { return (size_t)2 * (terms == 3 ? 2 : 1) * GM_STAGE_BYTES + 1024; }
 
 // ---------------------------------------------------------------------------
 // Large batches: a plain f16 GEMM fed by TMA.  The Q4_0 weights are first
@@ -309,44 +353,70 @@ __device__ __forceinline__ void mma_f16_n256(uint32_t tmem_d, uint64_t adesc, ui
 
 }  // namespace
 
+// terms == 3: the row is written as hi/lo pairs in 64-wide groups
+// (pb_hl_index), [N_pad][2K] halves; the pair is exact: hi + lo == (q-8)*d.
 __global__ void k_dequant_q4_f16(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int layout, int nb,
-                                 int64_t nblocks, __half* __restrict__ out) {
+                                 int64_t nblocks, __half* __restrict__ out, int terms) {
   const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // output block (row-major) per thread
   if (b >= nblocks) return;
-  const int64_t slot = pb_slot(layout, (int)(b / nb), (int)(b % nb), nb);
+  const int row = (int)(b / nb), blk = (int)(b % nb);
+  const int64_t slot = pb_slot(layout, row, blk, nb);
   const uint4 pl = __ldg(reinterpret_cast<const uint4*>(qs) + slot);
-  const float d = pb_f16_exact(__ldg(dsc + slot));
+  const float d = pb_f16_wasm(__ldg(dsc + slot));  // the reference's scale decode
   const uint32_t wv[4] = {pl.x, pl.y, pl.z, pl.w};
-  uint32_t lo[8], hi[8];
+  float e[32];
 #pragma unroll
-  for (int j = 0; j < 16; j += 2) {
-    const uint32_t b0 = (wv[j >> 2] >> (8 * (j & 3))) & 0xFFu, b1 = (wv[(j + 1) >> 2] >> (8 * ((j + 1) & 3))) & 0xFFu;
-    lo[j >> 1] = pack_h2((float)((int)(b0 & 15u) - 8) * d, (float)((int)(b1 & 15u) - 8) * d);
-    hi[j >> 1] = pack_h2((float)((int)(b0 >> 4) - 8) * d, (float)((int)(b1 >> 4) - 8) * d);
+  for (int j = 0; j < 16; ++j) {
+    const uint32_t byte = (wv[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+    e[j] = (float)((int)(byte & 15u) - 8) * d;  // exact in f32
+    e[16 + j] = (float)((int)(byte >> 4) - 8) * d;
   }
-  uint4* o = reinterpret_cast<uint4*>(out + b * 32);
-  o[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-  o[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-  o[2] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-  o[3] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+  uint32_t h[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) h[j] = pack_h2(e[2 * j], e[2 * j + 1]);
+  uint4* o = reinterpret_cast<uint4*>(
+      terms == 3 ? out + (size_t)row * 2 * nb * 32 + (size_t)(blk >> 1) * 128 + (blk & 1) * 32 : out + b * 32);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) o[c] = make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+  if (terms == 3) {
+    uint32_t l[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) l[j] = pack_lo2(e[2 * j], e[2 * j + 1], h[j]);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) o[8 + c] = make_uint4(l[4 * c], l[4 * c + 1], l[4 * c + 2], l[4 * c + 3]);  // +64 halves
+  }
 }
 
 // f32 X (row-major with stride ldx, or in column chunks of width kc) ->
-// row-major f16 [M][K]
-__global__ void k_f32_to_f16(const float* __restrict__ x, int M, int K, int ldx, int kc, __half* __restrict__ out) {
+// row-major f16 [M][K], or (terms == 3) hi/lo pairs [M][2K] (pb_hl_index)
+__global__ void k_f32_to_f16(const float* __restrict__ x, int M, int K, int ldx, int kc, __half* __restrict__ out,
+                             int terms) {
   const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;  // 4 values per thread
   if (i >= (int64_t)M * K) return;
   const int m = (int)(i / K), k = (int)(i % K);
   const float* src = kc ? x + (size_t)(k / kc) * M * kc + (size_t)m * kc + k % kc : x + (size_t)m * ldx + k;
   const float4 v = __ldg(reinterpret_cast<const float4*>(src));
-  reinterpret_cast<uint2*>(out)[i / 4] = make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
+  const uint2 hi = make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
+  if (terms != 3) {
+    reinterpret_cast<uint2*>(out)[i / 4] = hi;
+    return;
+  }
+  const size_t o = (size_t)m * 2 * K + (size_t)(k >> 6) * 128 + (k & 63);  // k % 4 == 0: 8-byte stores
+  *reinterpret_cast<uint2*>(out + o) = hi;
+  *reinterpret_cast<uint2*>(out + o + 64) = make_uint2(pack_lo2(v.x, v.y, hi.x), pack_lo2(v.z, v.w, hi.y));
 }
 
+// TERMS == 3: both operands are hi/lo pair rows ([rows][2K] halves, 64-wide
+// groups), a stage holds A hi, B hi, A lo, B lo (two stages fit), and each
+// 16-wide K slice issues hi*hi, hi*lo and lo*hi.
+template <int TERMS>
 __global__ void __launch_bounds__(TG_THREADS, 1)
 k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, int N, int M,
                int K, int xkc, float* __restrict__ C, int ldc, pb_gemm_epi epi, int* err) {
+  constexpr int NST = TERMS == 3 ? 2 : TG_STAGES;
+  constexpr int SB = TERMS == 3 ? 2 * TG_STAGE_BYTES : TG_STAGE_BYTES;
   extern __shared__ __align__(1024) unsigned char tg_raw[];
-  __shared__ uint64_t full[TG_STAGES], empty[TG_STAGES], acc_full[2], acc_empty[2];
+  __shared__ uint64_t full[NST], empty[NST], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   unsigned char* ring = tg_raw + ((1024 - (smem_addr(tg_raw) & 1023)) & 1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -360,7 +430,7 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 32) {
-    for (int s = 0; s < TG_STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       pb_mbar_init(&full[s], 1);
       pb_mbar_init(&empty[s], 1);
     }
@@ -382,13 +452,22 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
       const int n0 = (t % ntn) * TG_ROWS, m0 = (t / ntn) * TG_TOK;
       for (int ks = 0; ks < ksteps; ++ks, ++g) {
-        const int s = g % TG_STAGES;
-        if (g >= TG_STAGES && !(ok = pb_mbar_wait(&empty[s], ((g / TG_STAGES) - 1) & 1, err))) break;
-        unsigned char* sA = ring + s * TG_STAGE_BYTES;
-        pb_mbar_arrive_tx(&full[s], TG_STAGE_BYTES);
-        tma_load_2d(sA, &map_w, ks * TG_K, n0, &full[s]);
-        // X: column chunk (k / xkc), x coordinate k % xkc (a multiple of 64 elements)
-        tma_load_3d(sA + TG_A_BYTES, &map_x, (ks * TG_K) % xkc, m0, (ks * TG_K) / xkc, &full[s]);
+        const int s = g % NST;
+        if (g >= NST && !(ok = pb_mbar_wait(&empty[s], ((g / NST) - 1) & 1, err))) break;
+        unsigned char* sA = ring + s * SB;
+        pb_mbar_arrive_tx(&full[s], SB);
+        // X: column chunk (k / xkc), x coordinate k % xkc (a multiple of 64 elements);
+        // hi/lo rows: the hi group at 2x, the lo group 64 halves after it
+        const int xk = (ks * TG_K) % xkc, xz = (ks * TG_K) / xkc;
+        if (TERMS == 3) {
+          tma_load_2d(sA, &map_w, 2 * ks * TG_K, n0, &full[s]);
+          tma_load_3d(sA + TG_A_BYTES, &map_x, 2 * xk, m0, xz, &full[s]);
+          tma_load_2d(sA + TG_STAGE_BYTES, &map_w, 2 * ks * TG_K + 64, n0, &full[s]);
+          tma_load_3d(sA + TG_STAGE_BYTES + TG_A_BYTES, &map_x, 2 * xk + 64, m0, xz, &full[s]);
+        } else {
+          tma_load_2d(sA, &map_w, ks * TG_K, n0, &full[s]);
+          tma_load_3d(sA + TG_A_BYTES, &map_x, xk, m0, xz, &full[s]);
+        }
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -401,13 +480,21 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t acc = tmem_d + (uint32_t)(b * TG_TOK);
       for (int ks = 0; ks < ksteps; ++ks, ++g) {
-        const int s = g % TG_STAGES;
-        if (!(ok = pb_mbar_wait(&full[s], (g / TG_STAGES) & 1, err))) break;
+        const int s = g % NST;
+        if (!(ok = pb_mbar_wait(&full[s], (g / NST) & 1, err))) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        unsigned char* sA = ring + s * TG_STAGE_BYTES;
+        unsigned char* sA = ring + s * SB;
         const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sA + TG_A_BYTES));
+        const uint64_t dal = sw128_desc(smem_addr(sA + TG_STAGE_BYTES));
+        const uint64_t dbl = sw128_desc(smem_addr(sA + TG_STAGE_BYTES + TG_A_BYTES));
 #pragma unroll
-        for (int kk = 0; kk < TG_K / 16; ++kk) mma_f16_n256(acc, da + 2 * kk, db + 2 * kk, (ks > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < TG_K / 16; ++kk) {
+          mma_f16_n256(acc, da + 2 * kk, db + 2 * kk, (ks > 0 || kk > 0) ? 1u : 0u);
+          if (TERMS == 3) {
+            mma_f16_n256(acc, da + 2 * kk, dbl + 2 * kk, 1u);
+            mma_f16_n256(acc, dal + 2 * kk, db + 2 * kk, 1u);
+          }
+        }
         mma_commit(&empty[s]);
       }
       mma_commit(&acc_full[b]);  // fires when every MMA of the tile has completed
@@ -441,7 +528,9 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   }
 }
 
-static size_t tg_smem() { return (size_t)TG_STAGES * TG_STAGE_BYTES + 1024; }
+static size_t tg_smem(int terms) {
+  return (terms == 3 ? (size_t)2 * 2 * TG_STAGE_BYTES : (size_t)TG_STAGES * TG_STAGE_BYTES) + 1024;
+}
 
 static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder(pb_ctx* ctx) {
   static std::once_flag once;
@@ -490,30 +579,32 @@ static int make_map_x(pb_ctx* ctx, CUtensorMap* map, const void* base, int rows,
 
 static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, const __half* Xh, int ldx, int M, float* C,
                            int ldc, const pb_gemm_epi& epi) {
-  const int K = w->K;
-  const size_t wbytes = (size_t)w->N_pad * K * 2, xbytes = Xh ? 0 : (size_t)M * K * 2;
+  const int K = w->K, tw = epi.terms == 3 ? 2 : 1;  // halves per value: hi (and lo)
+  const size_t wbytes = (size_t)w->N_pad * K * 2 * tw, xbytes = Xh ? 0 : (size_t)M * K * 2 * tw;
   const size_t off_x = (wbytes + 1023) & ~(size_t)1023;
   PB_TRY(pb_ensure_gemm_scratch(ctx, off_x + xbytes));
   __half* w16 = reinterpret_cast<__half*>(ctx->gemm_scratch);
   const __half* x16 = Xh;
   const int64_t nblk = (int64_t)w->N_pad * w->nb;
-  k_dequant_q4_f16<<<pb_cdiv(nblk, 256), 256, 0, ctx->stream>>>(w->qs, w->d, w->layout, w->nb, nblk, w16);
+  k_dequant_q4_f16<<<pb_cdiv(nblk, 256), 256, 0, ctx->stream>>>(w->qs, w->d, w->layout, w->nb, nblk, w16, epi.terms);
   PB_LAUNCHED(ctx, "k_dequant_q4_f16");
-  if (!Xh) {  // the activations rounded to f16 once
+  if (!Xh) {  // the activations rounded to f16 once (or split into hi/lo pairs)
     __half* xs = reinterpret_cast<__half*>(static_cast<char*>(ctx->gemm_scratch) + off_x);
-    k_f32_to_f16<<<pb_cdiv((int64_t)M * K / 4, 256), 256, 0, ctx->stream>>>(X, M, K, ldx, epi.x_chunk, xs);
+    k_f32_to_f16<<<pb_cdiv((int64_t)M * K / 4, 256), 256, 0, ctx->stream>>>(X, M, K, ldx, epi.x_chunk, xs,
+                                                                             epi.terms);
     PB_LAUNCHED(ctx, "k_f32_to_f16");
     x16 = xs;
   }
-  // the f32 conversion writes row-major f16; an f16 operand keeps its chunks
+  // the f32 conversion writes whole rows; an f16 operand keeps its chunks
   const int xkc = (Xh && epi.x_chunk) ? epi.x_chunk : K;
   CUtensorMap mw, mx;
-  PB_TRY(make_map(ctx, &mw, w16, w->N_pad, K, TG_ROWS));
-  PB_TRY(make_map_x(ctx, &mx, const_cast<__half*>(x16), M, K, xkc, TG_TOK));
+  PB_TRY(make_map(ctx, &mw, w16, w->N_pad, K * tw, TG_ROWS));
+  PB_TRY(make_map_x(ctx, &mx, const_cast<__half*>(x16), M, K * tw, xkc * tw, TG_TOK));
   const int64_t ntiles = (int64_t)pb_cdiv(w->N, TG_ROWS) * pb_cdiv(M, TG_TOK);
   if (ntiles > (1ll << 30)) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
   const int grid = (int)(ntiles < ctx->sm_count ? ntiles : ctx->sm_count);  // persistent: one CTA per SM
-  k_gemm_f16_tma<<<grid, TG_THREADS, tg_smem(), ctx->stream>>>(mw, mx, w->N, M, K, xkc, C, ldc, epi, ctx->d_err);
+  auto kern = epi.terms == 3 ? k_gemm_f16_tma<3> : k_gemm_f16_tma<1>;
+  kern<<<grid, TG_THREADS, tg_smem(epi.terms), ctx->stream>>>(mw, mx, w->N, M, K, xkc, C, ldc, epi, ctx->d_err);
   PB_LAUNCHED(ctx, "k_gemm_f16_tma");
   return PB_OK;
 }
@@ -533,7 +624,8 @@ __global__ void k_splitk_reduce(const float* __restrict__ ws, int splits, int M,
       u += ws[((size_t)z * M + m) * N + nu];
     }
     const float h = __fdividef(g, 1.0f + __expf(-g)) * u;
-    if (epi.h16) epi.h16[(size_t)m * (N / 2) + i] = __float2half_rn(h);
+    if (epi.h16 && epi.terms == 3) pb_store_hl(epi.h16, pb_hl_index((size_t)m * N, i), h);
+    else if (epi.h16) epi.h16[(size_t)m * (N / 2) + i] = __float2half_rn(h);
     else epi.h32[(size_t)m * (N / 2) + i] = h;
     return;
   }
@@ -595,9 +687,12 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
     kepi.h16 = nullptr;
     kepi.h32 = nullptr;
   }
-  auto kern = tok == 64 ? (epi.x_chunk ? k_q4_gemm_tc<64, true> : k_q4_gemm_tc<64, false>)
-                        : (epi.x_chunk ? k_q4_gemm_tc<128, true> : k_q4_gemm_tc<128, false>);
-  kern<<<grid, GM_THREADS, gm_smem(), ctx->stream>>>(w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, X, ldx, M, dst, ldd,
+  auto kern = epi.terms == 3
+                  ? (tok == 64 ? (epi.x_chunk ? k_q4_gemm_tc<64, true, 3> : k_q4_gemm_tc<64, false, 3>)
+                               : (epi.x_chunk ? k_q4_gemm_tc<128, true, 3> : k_q4_gemm_tc<128, false, 3>))
+                  : (tok == 64 ? (epi.x_chunk ? k_q4_gemm_tc<64, true, 1> : k_q4_gemm_tc<64, false, 1>)
+                               : (epi.x_chunk ? k_q4_gemm_tc<128, true, 1> : k_q4_gemm_tc<128, false, 1>));
+  kern<<<grid, GM_THREADS, gm_smem(epi.terms), ctx->stream>>>(w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, X, ldx, M, dst, ldd,
                                                     kper, kepi, ctx->d_err);
   PB_LAUNCHED(ctx, "k_q4_gemm_tc");
   if (splits > 1) {
@@ -619,9 +714,27 @@ extern "C" int pb_q4_gemm_f16(pb_ctx* ctx, const pb_qmat* w, const void* x16_dev
 }
 
 extern "C" int pb_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int M, int ldx, float* c_dev, int ldc) {
-  if (!w) return PB_ERR_ARG;
+  return pb_q4_gemm_ex(ctx, w, x_dev, M, ldx, c_dev, ldc, 1);
+}
+
+extern "C" int pb_q4_gemm_ex(pb_ctx* ctx, const pb_qmat* w, const float* x_dev, int M, int ldx, float* c_dev, int ldc,
+                             int terms) {
+  if (!w || (terms != 1 && terms != 3)) return PB_ERR_ARG;
   if (ldx < w->K || ldc < w->N) return pb_set_error(ctx, PB_ERR_ARG, "row strides smaller than the matrix");
-  return pb_launch_q4_gemm(ctx, w, x_dev, ldx, M, c_dev, ldc, nullptr, 0);
+  pb_gemm_epi e;
+  e.terms = terms;
+  return pb_launch_q4_gemm(ctx, w, x_dev, ldx, M, c_dev, ldc, nullptr, 0, &e);
+}
+
+extern "C" int pb_q4_gemm_hl(pb_ctx* ctx, const pb_qmat* w, const void* xhl_dev, int M, float* c_dev, int ldc) {
+  if (!ctx || !w || !xhl_dev || !c_dev || M <= 0) return PB_ERR_ARG;
+  if (ldc < w->N) return pb_set_error(ctx, PB_ERR_ARG, "row stride smaller than the matrix");
+  if (!pb_gemm_uses_ws(w, M) && !pb_gemm_uses_tma(w, M))
+    return pb_set_error(ctx, PB_ERR_ARG, "hi/lo activations take M <= 64 or M >= %d rows and K %% 64 == 0",
+                        PB_GEMM_TMA_MIN_M);
+  pb_gemm_epi e;
+  e.terms = 3;
+  return pb_launch_q4_gemm(ctx, w, nullptr, w->K, M, c_dev, ldc, nullptr, 0, &e, static_cast<const __half*>(xhl_dev));
 }
 
 // ---------------------------------------------------------------------------
@@ -648,8 +761,12 @@ constexpr int GW_RAW_BYTES = GW_ROWS * 32;               // 2 Q4_0 payloads (16 
 constexpr int GW_X_BYTES = GW_TOK * GW_K * 2;            // f16 activations, swizzled
 constexpr int GW_A_BYTES = GW_ROWS * GW_K * 2;           // f16 weights, swizzled
 constexpr int GW_STAGE_BYTES = GW_X_BYTES + GW_RAW_BYTES;  // X first: 1024-aligned
-// [GW_ABUF dequantized tiles][GW_STAGES (activations, payload) stages]
-static size_t gw_smem() { return (size_t)GW_ABUF * GW_A_BYTES + (size_t)GW_STAGES * GW_STAGE_BYTES + 1024; }
+// [GW_ABUF dequantized tiles][GW_STAGES (activations, payload) stages]; with
+// three terms each weight tile and each activation tile is a hi, lo pair
+static size_t gw_smem(int terms) {
+  const int t = terms == 3 ? 2 : 1;
+  return (size_t)GW_ABUF * GW_A_BYTES * t + (size_t)GW_STAGES * (GW_X_BYTES * t + GW_RAW_BYTES) + 1024;
+}
 
 namespace {
 __device__ __forceinline__ uint32_t h2_sub_mul(uint32_t v, uint32_t magic, uint32_t d2) {
@@ -660,12 +777,30 @@ __device__ __forceinline__ uint32_t h2_sub_mul(uint32_t v, uint32_t magic, uint3
       : "r"(v), "r"(magic), "r"(d2));
   return r;
 }
+
+// hi = f16((v - magic) * d2) and lo = (v - magic) * d2 - hi on f16 pairs.  The
+// fused multiply-add rounds once, and the remainder is exact in f16: the
+// product is an integer multiple of d's last place with at most 14
+// significant bits, so hi (11 bits) leaves a multiple of that place of at
+// most 4 bits.
+__device__ __forceinline__ void h2_sub_mul_hl(uint32_t v, uint32_t magic, uint32_t d2, uint32_t& hi, uint32_t& lo) {
+  asm("{\n\t.reg .b32 t, n;\n\tsub.rn.f16x2 t, %2, %3;\n\tmul.rn.f16x2 %0, t, %4;\n\t"
+      "neg.f16x2 n, %0;\n\tfma.rn.f16x2 %1, t, %4, n;\n\t}"
+      : "=r"(hi), "=r"(lo)
+      : "r"(v), "r"(magic), "r"(d2));
+}
 }  // namespace
 
+// TERMS == 3: the activations are hi/lo pair rows (two TMA boxes per step),
+// the dequant warps write the weight tile's hi and lo halves, and each
+// 16-wide K slice issues hi*hi, hi*lo and lo*hi.
+template <int TERMS>
 __global__ void __launch_bounds__(GW_THREADS, 1)
 k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_x,
              const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int layout, int N, int N_pad, int nb, int M, int xkc,
              float* __restrict__ C, int ldc, int kper, pb_gemm_epi epi, int* err) {
+  constexpr int TW = TERMS == 3 ? 2 : 1;
+  constexpr int XB = GW_X_BYTES * TW, SB = XB + GW_RAW_BYTES, AB = GW_A_BYTES * TW;
   extern __shared__ __align__(1024) unsigned char gw_raw[];
   __shared__ uint64_t full[GW_STAGES], empty[GW_STAGES], aready[GW_ABUF], afree[GW_ABUF], accf;
   __shared__ uint32_t tmem_base;
@@ -706,18 +841,20 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       for (int g = 0; g < ksteps && ok; ++g) {
         const int st = g % GW_STAGES;
         if (g >= GW_STAGES && !(ok = pb_mbar_wait_sleep(&empty[st], ((g / GW_STAGES) - 1) & 1, err))) break;
-        unsigned char* sX = ring + GW_ABUF * GW_A_BYTES + st * GW_STAGE_BYTES;
-        pb_mbar_arrive_tx(&full[st], GW_X_BYTES + GW_RAW_BYTES);
+        unsigned char* sX = ring + GW_ABUF * AB + st * SB;
+        pb_mbar_arrive_tx(&full[st], SB);
         const int ks = kbeg + g;
         if (layout == PB_LAYOUT_TILED8)
           asm volatile(
               "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-              "[%5];" ::"r"(smem_addr(sX + GW_X_BYTES)),
+              "[%5];" ::"r"(smem_addr(sX + XB)),
               "l"(&map_q), "r"(0), "r"(2 * ks), "r"(n0 >> 3), "r"(smem_addr(&full[st]))
               : "memory");
         else
-          tma_load_2d(sX + GW_X_BYTES, &map_q, 32 * ks, n0, &full[st]);
-        tma_load_3d(sX, &map_x, (ks * GW_K) % xkc, m0, (ks * GW_K) / xkc, &full[st]);
+          tma_load_2d(sX + XB, &map_q, 32 * ks, n0, &full[st]);
+        const int xk = (ks * GW_K) % xkc, xz = (ks * GW_K) / xkc;
+        tma_load_3d(sX, &map_x, TW * xk, m0, xz, &full[st]);
+        if (TERMS == 3) tma_load_3d(sX + GW_X_BYTES, &map_x, 2 * xk + 64, m0, xz, &full[st]);
       }
     }
   } else if (warp == 1) {
@@ -728,12 +865,18 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
         // the weight tile of step g is written after the payload and activations landed
         if (!(ok = pb_mbar_wait_sleep(&aready[ab], (g / GW_ABUF) & 1, err))) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        unsigned char* sA = ring + ab * GW_A_BYTES;
-        unsigned char* sX = ring + GW_ABUF * GW_A_BYTES + st * GW_STAGE_BYTES;
+        unsigned char* sA = ring + ab * AB;
+        unsigned char* sX = ring + GW_ABUF * AB + st * SB;
         const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sX));
+        const uint64_t dal = sw128_desc(smem_addr(sA + GW_A_BYTES)), dbl = sw128_desc(smem_addr(sX + GW_X_BYTES));
 #pragma unroll
-        for (int kk = 0; kk < GW_K / 16; ++kk)
+        for (int kk = 0; kk < GW_K / 16; ++kk) {
           mma_f16(tmem_d, da + 2 * kk, db + 2 * kk, gm_idesc(GW_TOK), (g > 0 || kk > 0) ? 1u : 0u);
+          if (TERMS == 3) {
+            mma_f16(tmem_d, da + 2 * kk, dbl + 2 * kk, gm_idesc(GW_TOK), 1u);
+            mma_f16(tmem_d, dal + 2 * kk, db + 2 * kk, gm_idesc(GW_TOK), 1u);
+          }
+        }
         mma_commit(&empty[st]);
         mma_commit(&afree[ab]);
       }
@@ -761,7 +904,11 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       d[0] = d[1] = 0u;
       if (live_row && ks < kend) {
 #pragma unroll
-        for (int bb = 0; bb < 2; ++bb) d[bb] = __ldg(dsc + pb_slot(layout, row, 2 * ks + bb, nb));
+        for (int bb = 0; bb < 2; ++bb) {
+          // the reference's scale decode: a zero exponent is +0 (subnormal scales flushed)
+          const uint32_t bits = __ldg(dsc + pb_slot(layout, row, 2 * ks + bb, nb));
+          d[bb] = (bits & 0x7C00u) ? bits : 0u;
+        }
       }
     };
     uint32_t dnext[2];
@@ -774,27 +921,36 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       if (!(ok = pb_mbar_wait_sleep(&full[st], (g / GW_STAGES) & 1, err))) break;
       // the weight buffer is free once the MMAs of step g - GW_ABUF completed
       if (g >= GW_ABUF && !(ok = pb_mbar_wait_sleep(&afree[ab], ((g / GW_ABUF) - 1) & 1, err))) break;
-      unsigned char* sA = ring + ab * GW_A_BYTES;
-      const unsigned char* raw = ring + GW_ABUF * GW_A_BYTES + st * GW_STAGE_BYTES + GW_X_BYTES;
+      unsigned char* sA = ring + ab * AB;
+      const unsigned char* raw = ring + GW_ABUF * AB + st * SB + XB;
 #pragma unroll
       for (int bb = 0; bb < 2; ++bb) {
         const uint32_t off =
             layout == PB_LAYOUT_TILED8 ? (uint32_t)((((t >> 3) * 2 + bb) * 8 + (t & 7)) * 16) : (uint32_t)(t * 32 + bb * 16);
         const uint4 q = *reinterpret_cast<const uint4*>(raw + off);
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-        uint32_t lo[8], hi[8];  // f16 pairs (k, k+1): lo nibbles are k 0..15, hi nibbles k 16..31
+        // f16 pairs (k, k+1): v[0..7] from the low nibbles (k 0..15), v[8..15] the high ones (k 16..31)
+        uint32_t v[16], h[16], r[16];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const uint32_t a = __byte_perm(w[i], 0u, 0x4140u), b = __byte_perm(w[i], 0u, 0x4342u);
-          lo[2 * i] = h2_sub_mul((a & 0x000F000Fu) | 0x64006400u, magic, d2[bb]);
-          lo[2 * i + 1] = h2_sub_mul((b & 0x000F000Fu) | 0x64006400u, magic, d2[bb]);
-          hi[2 * i] = h2_sub_mul(((a >> 4) & 0x000F000Fu) | 0x64006400u, magic, d2[bb]);
-          hi[2 * i + 1] = h2_sub_mul(((b >> 4) & 0x000F000Fu) | 0x64006400u, magic, d2[bb]);
+          v[2 * i] = (a & 0x000F000Fu) | 0x64006400u;
+          v[2 * i + 1] = (b & 0x000F000Fu) | 0x64006400u;
+          v[8 + 2 * i] = ((a >> 4) & 0x000F000Fu) | 0x64006400u;
+          v[8 + 2 * i + 1] = ((b >> 4) & 0x000F000Fu) | 0x64006400u;
         }
-        *reinterpret_cast<uint4*>(sA + sw128(t, 4 * bb + 0)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        *reinterpret_cast<uint4*>(sA + sw128(t, 4 * bb + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-        *reinterpret_cast<uint4*>(sA + sw128(t, 4 * bb + 2)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(sA + sw128(t, 4 * bb + 3)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if (TERMS == 3) h2_sub_mul_hl(v[i], magic, d2[bb], h[i], r[i]);
+          else h[i] = h2_sub_mul(v[i], magic, d2[bb]);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          *reinterpret_cast<uint4*>(sA + sw128(t, 4 * bb + c)) = make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+          if (TERMS == 3)
+            *reinterpret_cast<uint4*>(sA + GW_A_BYTES + sw128(t, 4 * bb + c)) =
+                make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+        }
       }
       // generic-proxy reads of the payload and writes of the tile -> the async proxy
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -878,12 +1034,13 @@ static int launch_gemm_ws(pb_ctx* ctx, const pb_qmat* w, const __half* Xh, int M
     kepi.h16 = nullptr;
     kepi.h32 = nullptr;
   }
-  const int xkc = epi.x_chunk ? epi.x_chunk : w->K;
+  const int xkc = epi.x_chunk ? epi.x_chunk : w->K, tw = epi.terms == 3 ? 2 : 1;
   CUtensorMap mq, mx;
   PB_TRY(make_map_q(ctx, &mq, w));
-  PB_TRY(make_map_x(ctx, &mx, Xh, M, w->K, xkc, GW_TOK));
-  k_q4_gemm_ws<<<grid, GW_THREADS, gw_smem(), ctx->stream>>>(mq, mx, w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, M, xkc,
-                                                             dst, ldd, kper, kepi, ctx->d_err);
+  PB_TRY(make_map_x(ctx, &mx, Xh, M, w->K * tw, xkc * tw, GW_TOK));
+  auto kern = epi.terms == 3 ? k_q4_gemm_ws<3> : k_q4_gemm_ws<1>;
+  kern<<<grid, GW_THREADS, gw_smem(epi.terms), ctx->stream>>>(mq, mx, w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, M,
+                                                              xkc, dst, ldd, kper, kepi, ctx->d_err);
   PB_LAUNCHED(ctx, "k_q4_gemm_ws");
   if (splits > 1) {
     const int cols = epi.mode == PB_GEMM_SWIGLU ? w->N / 2 : w->N;
@@ -895,11 +1052,19 @@ static int launch_gemm_ws(pb_ctx* ctx, const pb_qmat* w, const __half* Xh, int M
 
 int pb_setup_gemm_kernels(void) {
   cudaError_t e = cudaSuccess;
-  for (auto k : {k_q4_gemm_tc<64, false>, k_q4_gemm_tc<64, true>, k_q4_gemm_tc<128, false>, k_q4_gemm_tc<128, true>})
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gm_smem());
+  for (auto k : {k_q4_gemm_tc<64, false, 1>, k_q4_gemm_tc<64, true, 1>, k_q4_gemm_tc<128, false, 1>,
+                 k_q4_gemm_tc<128, true, 1>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gm_smem(1));
+  for (auto k : {k_q4_gemm_tc<64, false, 3>, k_q4_gemm_tc<64, true, 3>, k_q4_gemm_tc<128, false, 3>,
+                 k_q4_gemm_tc<128, true, 3>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gm_smem(3));
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_q4_gemm_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gw_smem());
+    e = cudaFuncSetAttribute(k_q4_gemm_ws<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gw_smem(1));
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(k_gemm_f16_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tg_smem());
+    e = cudaFuncSetAttribute(k_q4_gemm_ws<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gw_smem(3));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_gemm_f16_tma<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tg_smem(1));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(k_gemm_f16_tma<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tg_smem(3));
   return e == cudaSuccess ? PB_OK : PB_ERR_CUDA;
 }

@@ -380,9 +380,27 @@ struct pb_gemm_epi {
   float* h32 = nullptr;
   int x_chunk = 0;
   int split_n = 0;
+  // 1: each operand rounded to f16 once; 3: both split into f16 hi + lo and
+  // the three products hi*hi + hi*lo + lo*hi summed (f16 operands then come,
+  // and h16 goes out, in the hi/lo layout below)
+  int terms = 1;
 };
+
+// The hi/lo f16 layout of the three-term GEMM operands: a value v is the
+// pair hi = f16(v), lo = f16(v - hi) (v - hi is exact in f32, so hi + lo
+// carries about 22 bits of v); along K each 64-wide group is stored as its
+// 64 hi halves, then its 64 lo halves.  A row of K values takes 2K halves:
+// the bytes of the f32 row, so a buffer sized for f32 holds it.
+__device__ __forceinline__ size_t pb_hl_index(size_t row_base, int k) {
+  return row_base + (size_t)(k >> 6) * 128 + (k & 63);
+}
+__device__ __forceinline__ void pb_store_hl(__half* p, size_t i, float v) {
+  const __half hi = __float2half_rn(v);
+  p[i] = hi;
+  p[i + 64] = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+}
 void pb_launch_rmsnorm(cudaStream_t st, const float* x, int rows, int dim, const float* w, double eps, float* out,
-                       __half* out16, int xc);
+                       __half* out16, int xc, int hl = 0);
 int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
                       size_t ws_bytes, const pb_gemm_epi* epi = nullptr, const __half* Xh = nullptr);
 bool pb_gemm_uses_tma(const pb_qmat* w, int M);  // the f16-operand TMA path (takes Xh)

@@ -27,7 +27,7 @@ int pb_launch_prefill_q4(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx,
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
                           int n_heads, int n_kv, int hd, float* out, int max_len, int nseq, pb_seq_geo geo,
                           float* ws = nullptr, size_t ws_floats = 0, int* counters = nullptr,
-                          __half* out16 = nullptr);
+                          __half* out16 = nullptr, int hl16 = 0);
 
 int pb_attn_dec1_splits(int n_kv, int max_len, int sm_count);
 size_t pb_attn_dec1_ws_doubles(int n_heads, int n_kv, int hd, int nsplit);
@@ -37,11 +37,9 @@ int pb_launch_attn_dec1(pb_ctx* ctx, const float* q, const float* kc, const floa
                         unsigned int* counters);
 
 int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
-                               int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo);
+                               int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo, int terms = 1);
 bool pb_attn_decode_ok(int n_heads, int n_kv, int hd, int max_len);
 bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len);
-void pb_launch_rmsnorm(cudaStream_t st, const float* x, int rows, int dim, const float* w, double eps, float* out,
-                       __half* out16, int xc);
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
                           const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
                           const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
@@ -575,8 +573,8 @@ extern "C" int pb_model_get_tensor(pb_model* m, int layer, int which, void* host
 // ---------------------------------------------------------------------------
 
 static int launch_norm(pb_model* m, const float* x, int M, const float* w, float* out, __half* out16 = nullptr,
-                       int xc = 0) {
-  pb_launch_rmsnorm(m->ctx->stream, x, M, m->c.dim, w, m->c.eps, out, out16, xc);
+                       int xc = 0, int hl = 0) {
+  pb_launch_rmsnorm(m->ctx->stream, x, M, m->c.dim, w, m->c.eps, out, out16, xc, hl);
   PB_LAUNCHED(m->ctx, "k_rmsnorm");
   return PB_OK;
 }
@@ -1289,7 +1287,13 @@ struct pb_batch {
   bool p2p_ll = false;
   void* ll_mem = nullptr;  // this rank's slots, then its epoch and done counters
   bool decoding = false;   // the layer being enqueued is a decode step (one row per sequence)
+  // GEMM precision: 3 = f16 hi/lo pairs of both operands, three tensor-core
+  // products (the default); 1 = each operand rounded to f16 once
+  int terms = 3;
 };
+
+// halves per value of an f16 GEMM operand the batch writes: hi and lo, or hi alone
+static int op_halves(const pb_batch* b) { return b->terms == 3 ? 2 : 1; }
 
 // the buffers the row split exchanges
 enum { XG_X = 0, XG_ATT = 1, XG_HB = 2, XG_KEYS = 3, XG_LOGITS = 4 };
@@ -1581,6 +1585,13 @@ static int batch_ensure_rows(pb_batch* b, int rows) {
   return batch_share(b, XG_ROWS, 3, &b->p2p_rows);
 }
 
+extern "C" int pb_batch_set_precision(pb_batch* b, int terms) {
+  if (!b || (terms != 1 && terms != 3)) return PB_ERR_ARG;
+  if (terms != b->terms) batch_free_graph(b);  // the recorded decode step holds the other kernels
+  b->terms = terms;
+  return PB_OK;
+}
+
 extern "C" int pb_batch_free(pb_batch* b) {
   if (!b) return PB_OK;
   pb_ctx* ctx = b->m ? b->m->ctx : nullptr;
@@ -1714,11 +1725,12 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
   float* vc = s.vc + (size_t)l * b->B * cache_seq;
   pb_gemm_epi st;
   st.split_n = dim + 2 * m->kv_dim;
+  st.terms = b->terms;
   // the norm writes the GEMM's f16 operand directly on the TMA and decode paths
   __half* xn16 = reinterpret_cast<__half*>(s.xn);
   const bool d16 = dec16(b, s, l, rows);
   if (pb_gemm_uses_tma(s.qkv[l], rows) || d16) {
-    PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, nullptr, xn16, dc));
+    PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, nullptr, xn16, dc, b->terms == 3));
     PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], nullptr, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st, xn16));
   } else {
     PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, s.xn, nullptr, dc));
@@ -1737,15 +1749,15 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
   if (rows_per_seq == 1 && pos_dev) {
     geo.q = qw;
     geo.out = dc;
-    __half* att16 = d16 ? reinterpret_cast<__half*>(s.att) + (size_t)s.rank * rows * dc : nullptr;
+    __half* att16 = d16 ? reinterpret_cast<__half*>(s.att) + (size_t)s.rank * rows * dc * op_halves(b) : nullptr;
     return pb_launch_attn_decode(ctx, s.qkvo, kc, vc, pos_dev, p.n_heads, p.n_kv_heads, hd, att, c.seq_len, b->B, geo,
-                                 b->ws, b->ws_bytes / 4, b->attn_cnt, att16);
+                                 b->ws, b->ws_bytes / 4, b->attn_cnt, att16, b->terms == 3);
   }
   geo.q = (int64_t)rows_per_seq * qw;
   geo.out = (int64_t)rows_per_seq * dc;
   if (hd == 64 && !pos_dev)
     return pb_launch_attn_prefill(ctx, s.qkvo, qw, kc, vc, rows_per_seq, start_pos, p.n_heads, p.n_kv_heads, hd, att,
-                                  b->B, geo);
+                                  b->B, geo, b->terms);
   return pb_launch_attn_cached(ctx, s.qkvo, qw, kc, vc, rows_per_seq, start_pos, pos_dev, p.n_heads, p.n_kv_heads, hd,
                                att, c.seq_len, b->B, geo);
 }
@@ -1759,6 +1771,7 @@ static int shard_wo(pb_batch* b, pb_shard& s, int l, int rows) {
   add.mode = PB_GEMM_ADD;
   add.x_chunk = chunk_of(b, dc);
   add.split_n = m->c.dim;
+  add.terms = b->terms;
   if (dec16(b, s, l, rows))
     return pb_launch_q4_gemm(m->ctx, s.wo[l], nullptr, m->c.dim, rows, s.x + (size_t)s.rank * rows * dc, dc, b->ws,
                              b->ws_bytes, &add, reinterpret_cast<const __half*>(s.att));
@@ -1779,11 +1792,12 @@ static int shard_gate_up(pb_batch* b, pb_shard& s, int l, int rows) {
   const bool gu16 = pb_gemm_uses_tma(s.gu[l], rows) || dec16(b, s, l, rows);
   __half* xn16 = reinterpret_cast<__half*>(s.xn);
   PB_TRY(launch_norm(m, s.x, rows, m->rms_ffn + (size_t)l * dim, gu16 ? nullptr : s.xn, gu16 ? xn16 : nullptr,
-                     s.p.dim_chunk));
+                     s.p.dim_chunk, b->terms == 3));
   pb_gemm_epi glu;
   glu.mode = PB_GEMM_SWIGLU;
   glu.split_n = 2 * m->c.hidden_dim;
-  const size_t off = (size_t)s.rank * rows * fc;
+  glu.terms = b->terms;
+  const size_t off = (size_t)s.rank * rows * fc * (hidden_f16(b, s, l, rows) ? op_halves(b) : 1);
   if (hidden_f16(b, s, l, rows)) glu.h16 = reinterpret_cast<__half*>(s.hb) + off;
   else glu.h32 = s.hb + off;
   if (gu16) return pb_launch_q4_gemm(ctx, s.gu[l], nullptr, dim, rows, nullptr, 2 * fc, b->ws, b->ws_bytes, &glu, xn16);
@@ -1798,6 +1812,7 @@ static int shard_down(pb_batch* b, pb_shard& s, int l, int rows) {
   add.mode = PB_GEMM_ADD;
   add.x_chunk = chunk_of(b, s.p.hidden_chunk);
   add.split_n = m->c.dim;
+  add.terms = b->terms;
   float* C = s.x + (size_t)s.rank * rows * dc;
   if (hidden_f16(b, s, l, rows))
     return pb_launch_q4_gemm(m->ctx, s.w2[l], nullptr, F, rows, C, dc, b->ws, b->ws_bytes, &add,
@@ -1812,13 +1827,15 @@ static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start
   const pb_model_config& c = b->m->c;
   b->decoding = rows_per_seq == 1 && pos_dev != nullptr;
   const size_t dchunk = (size_t)rows * (c.dim / b->world) * 4;
-  const size_t achunk = dec16(b, b->sh[0], l, rows) ? dchunk / 2 : dchunk;  // f16 attention output
+  // f16 attention output (hi/lo pairs take the bytes of f32)
+  const size_t achunk = dec16(b, b->sh[0], l, rows) ? dchunk / 2 * op_halves(b) : dchunk;
   for (auto& s : b->sh) PB_TRY(shard_attention(b, s, l, rows, rows_per_seq, start_pos, pos_dev));
   PB_TRY(batch_gather(b, XG_ATT, achunk));
   for (auto& s : b->sh) PB_TRY(shard_wo(b, s, l, rows));
   PB_TRY(batch_gather(b, XG_X, dchunk));
   for (auto& s : b->sh) PB_TRY(shard_gate_up(b, s, l, rows));
-  const size_t hchunk = (size_t)rows * (c.hidden_dim / b->world) * (hidden_f16(b, b->sh[0], l, rows) ? 2 : 4);
+  const size_t hchunk =
+      (size_t)rows * (c.hidden_dim / b->world) * (hidden_f16(b, b->sh[0], l, rows) ? 2 * op_halves(b) : 4);
   PB_TRY(batch_gather(b, XG_HB, hchunk));
   for (auto& s : b->sh) PB_TRY(shard_down(b, s, l, rows));
   return batch_gather(b, XG_X, dchunk);
@@ -1834,12 +1851,15 @@ static int batch_head(pb_batch* b, bool from_x, const int* pos_dev) {
   for (auto& s : b->sh) {
     const bool h16 = pb_gemm_uses_ws(s.head, b->B);
     __half* xn16 = h16 ? reinterpret_cast<__half*>(s.xn) : nullptr;
-    if (from_x) PB_TRY(launch_norm(m, s.x, b->B, m->rms_final, h16 ? nullptr : s.xn, xn16, s.p.dim_chunk));
-    else PB_TRY(launch_norm(m, s.xl, b->B, m->rms_final, h16 ? nullptr : s.xn, xn16));
+    const int hl = b->terms == 3;
+    if (from_x) PB_TRY(launch_norm(m, s.x, b->B, m->rms_final, h16 ? nullptr : s.xn, xn16, s.p.dim_chunk, hl));
+    else PB_TRY(launch_norm(m, s.xl, b->B, m->rms_final, h16 ? nullptr : s.xn, xn16, 0, hl));
     const int vc = s.p.vocab_chunk;
     float* lg = s.logits + (size_t)s.rank * b->B * vc;
-    if (h16) PB_TRY(pb_launch_q4_gemm(ctx, s.head, nullptr, c.dim, b->B, lg, vc, nullptr, 0, nullptr, xn16));
-    else PB_TRY(pb_launch_q4_gemm(ctx, s.head, s.xn, c.dim, b->B, lg, vc, nullptr, 0));
+    pb_gemm_epi he;
+    he.terms = b->terms;
+    if (h16) PB_TRY(pb_launch_q4_gemm(ctx, s.head, nullptr, c.dim, b->B, lg, vc, nullptr, 0, &he, xn16));
+    else PB_TRY(pb_launch_q4_gemm(ctx, s.head, s.xn, c.dim, b->B, lg, vc, nullptr, 0, &he));
     // this rank's keys (zero: cleared by the previous merge or at creation)
     k_argmax_chunks<<<dim3(pb_cdiv(s.p.vocab_rows, AMX_CHUNK), b->B), 256, 0, ctx->stream>>>(
         lg, s.p.vocab_rows, vc, s.p.vocab_row0, s.keys + (size_t)s.rank * b->B);

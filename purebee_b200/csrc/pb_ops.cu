@@ -29,7 +29,7 @@
 // output rows are row-major either way.
 template <bool CH>
 __global__ void k_rmsnorm_t(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
-                            float* __restrict__ out, __half* __restrict__ out16, int xc) {
+                            float* __restrict__ out, __half* __restrict__ out16, int xc, int hl) {
   __shared__ double red[32];
   const size_t row = blockIdx.x;
   const float* xr = x + row * (CH ? xc : dim);
@@ -44,6 +44,11 @@ __global__ void k_rmsnorm_t(const float* __restrict__ x, int dim, const float* _
   double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)dim), eps));
   if (out16) {
     const float inv = (float)(1.0 / rms);
+    if (hl) {  // the three-term GEMM operand: hi/lo pairs (pb_hl_index)
+      for (int d = threadIdx.x; d < dim; d += blockDim.x)
+        pb_store_hl(out16, pb_hl_index((size_t)row * 2 * dim, d), X(d) * inv * w[d]);
+      return;
+    }
     for (int d = threadIdx.x; d < dim; d += blockDim.x) out16[row * dim + d] = __float2half_rn(X(d) * inv * w[d]);
     return;
   }
@@ -52,9 +57,9 @@ __global__ void k_rmsnorm_t(const float* __restrict__ x, int dim, const float* _
 }
 
 void pb_launch_rmsnorm(cudaStream_t st, const float* x, int rows, int dim, const float* w, double eps, float* out,
-                       __half* out16, int xc) {
-  if (xc > 0 && xc < dim) k_rmsnorm_t<true><<<rows, 256, 0, st>>>(x, dim, w, eps, out, out16, xc);
-  else k_rmsnorm_t<false><<<rows, 256, 0, st>>>(x, dim, w, eps, out, out16, 0);
+                       __half* out16, int xc, int hl) {
+  if (xc > 0 && xc < dim) k_rmsnorm_t<true><<<rows, 256, 0, st>>>(x, dim, w, eps, out, out16, xc, hl);
+  else k_rmsnorm_t<false><<<rows, 256, 0, st>>>(x, dim, w, eps, out, out16, 0, hl);
 }
 
 extern "C" int pb_rmsnorm(pb_ctx* ctx, const float* x, int seq, int dim, const float* w, double eps, float* out) {
@@ -526,6 +531,10 @@ __global__ void k_attn_cached(const float* __restrict__ q, const float* __restri
 // accumulation).  CTA = (64 queries, head, sequence), four warps of 16 query
 // rows.  Q, K and V tiles are converted from the f32 activations and cache to
 // f16 in shared memory (rows padded to 72 halves so ldmatrix is conflict-free).
+// TERMS == 3 (the batched model's default precision): every operand is kept
+// as an f16 pair hi = f16(v), lo = f16(v - hi) -- Q, K and V in two tiles
+// each, P split in registers -- and both products run as hi*hi + hi*lo +
+// lo*hi, so the scores and the output carry about 22 bits instead of 11.
 // Per 64-key tile: S = Q K^T in registers, scaled by log2(e)/sqrt(hd), causal
 // mask, online softmax (running max and sum per row, exp2), P packed to f16
 // straight from the S accumulators into A fragments, O += P V with V read by
@@ -563,14 +572,33 @@ __device__ __forceinline__ void ft_store4(__half* dst, float4 v) {
   u.y = ft_h2(v.z, v.w);
   *reinterpret_cast<uint2*>(dst) = u;
 }
+// the lo halves of (a, b) given their hi pair (each difference exact in f32)
+__device__ __forceinline__ uint32_t ft_lo2(float a, float b, uint32_t hi) {
+  const __half2 h = *reinterpret_cast<const __half2*>(&hi);
+  return ft_h2(__fsub_rn(a, __low2float(h)), __fsub_rn(b, __high2float(h)));
+}
+// 4 consecutive f32 -> their hi halves at dst, their lo halves at dst_lo
+__device__ __forceinline__ void ft_store4_hl(__half* dst, __half* dst_lo, float4 v) {
+  uint2 u, l;
+  u.x = ft_h2(v.x, v.y);
+  u.y = ft_h2(v.z, v.w);
+  l.x = ft_lo2(v.x, v.y, u.x);
+  l.y = ft_lo2(v.z, v.w, u.y);
+  *reinterpret_cast<uint2*>(dst) = u;
+  *reinterpret_cast<uint2*>(dst_lo) = l;
+}
 
+template <int TERMS>
 __global__ void __launch_bounds__(FT_THREADS)
 k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __restrict__ kc,
                   const float* __restrict__ vc, int seq, int start_pos, int n_heads, int n_kv, float scale,
                   float* __restrict__ out, pb_seq_geo geo) {
-  __shared__ __align__(16) __half Qs[FT_Q][FT_LD];
-  __shared__ __align__(16) __half Ks[FT_KT][FT_LD];
-  __shared__ __align__(16) __half Vs[FT_KT][FT_LD];
+  // [hi, lo] tiles of Q, K, V (the lo tiles only with three terms)
+  constexpr int T = TERMS == 3 ? 2 : 1;
+  extern __shared__ __align__(16) unsigned char ft_raw[];
+  __half(*Qs)[FT_LD] = reinterpret_cast<__half(*)[FT_LD]>(ft_raw);
+  __half(*Ks)[FT_LD] = Qs + T * FT_Q;
+  __half(*Vs)[FT_LD] = Ks + T * FT_KT;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int q0 = blockIdx.x * FT_Q, h = blockIdx.y, z = blockIdx.z;
   const int per = n_heads / n_kv, kh = h / per, kv_dim = n_kv * FT_HD, dim = n_heads * FT_HD;
@@ -582,14 +610,17 @@ k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __rest
     const int qr = i / (FT_HD / 4), d4 = i % (FT_HD / 4);
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (q0 + qr < seq) v = *reinterpret_cast<const float4*>(q + (size_t)(q0 + qr) * q_stride + (size_t)h * FT_HD + 4 * d4);
-    ft_store4(&Qs[qr][4 * d4], v);
+    if (TERMS == 3) ft_store4_hl(&Qs[qr][4 * d4], &Qs[FT_Q + qr][4 * d4], v);
+    else ft_store4(&Qs[qr][4 * d4], v);
   }
   __syncthreads();
-  uint32_t qa[4][4];  // A fragments of this warp's 16 rows, 4 steps of 16 dims
+  uint32_t qa[4][4], ql[4][4];  // A fragments (hi, lo) of this warp's 16 rows, 4 steps of 16 dims
 #pragma unroll
-  for (int kk = 0; kk < 4; ++kk)
-    ft_ldsm_x4(&Qs[warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8][kk * 16 + (lane >> 4) * 8], qa[kk][0], qa[kk][1],
-               qa[kk][2], qa[kk][3]);
+  for (int kk = 0; kk < 4; ++kk) {
+    const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, cc = kk * 16 + (lane >> 4) * 8;
+    ft_ldsm_x4(&Qs[r][cc], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+    if (TERMS == 3) ft_ldsm_x4(&Qs[FT_Q + r][cc], ql[kk][0], ql[kk][1], ql[kk][2], ql[kk][3]);
+  }
   float o[8][4];
 #pragma unroll
   for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
@@ -607,8 +638,13 @@ k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __rest
         kv4 = *reinterpret_cast<const float4*>(kc + (size_t)(k0 + kr) * kv_dim + (size_t)kh * FT_HD + 4 * d4);
         vv4 = *reinterpret_cast<const float4*>(vc + (size_t)(k0 + kr) * kv_dim + (size_t)kh * FT_HD + 4 * d4);
       }
-      ft_store4(&Ks[kr][4 * d4], kv4);
-      ft_store4(&Vs[kr][4 * d4], vv4);
+      if (TERMS == 3) {
+        ft_store4_hl(&Ks[kr][4 * d4], &Ks[FT_KT + kr][4 * d4], kv4);
+        ft_store4_hl(&Vs[kr][4 * d4], &Vs[FT_KT + kr][4 * d4], vv4);
+      } else {
+        ft_store4(&Ks[kr][4 * d4], kv4);
+        ft_store4(&Vs[kr][4 * d4], vv4);
+      }
     }
     __syncthreads();
     float s[8][4];
@@ -619,9 +655,18 @@ k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __rest
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
         uint32_t b0, b1, b2, b3;
-        ft_ldsm_x4(&Ks[np * 16 + (lane & 7) + (lane >> 4) * 8][kk * 16 + ((lane >> 3) & 1) * 8], b0, b1, b2, b3);
+        const int r = np * 16 + (lane & 7) + (lane >> 4) * 8, cc = kk * 16 + ((lane >> 3) & 1) * 8;
+        ft_ldsm_x4(&Ks[r][cc], b0, b1, b2, b3);
         ft_mma(s[2 * np], qa[kk], b0, b1);
         ft_mma(s[2 * np + 1], qa[kk], b2, b3);
+        if (TERMS == 3) {
+          uint32_t l0, l1, l2, l3;
+          ft_ldsm_x4(&Ks[FT_KT + r][cc], l0, l1, l2, l3);
+          ft_mma(s[2 * np], qa[kk], l0, l1);
+          ft_mma(s[2 * np + 1], qa[kk], l2, l3);
+          ft_mma(s[2 * np], ql[kk], b0, b1);
+          ft_mma(s[2 * np + 1], ql[kk], b2, b3);
+        }
       }
     }
     float mt0 = -INFINITY, mt1 = -INFINITY;
@@ -668,12 +713,28 @@ k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __rest
     for (int kk = 0; kk < 4; ++kk) {  // 16 keys per step: S n-tiles 2kk, 2kk+1 as the A fragment
       const uint32_t pa[4] = {ft_h2(s[2 * kk][0], s[2 * kk][1]), ft_h2(s[2 * kk][2], s[2 * kk][3]),
                               ft_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]), ft_h2(s[2 * kk + 1][2], s[2 * kk + 1][3])};
+      uint32_t pl[4] = {0u, 0u, 0u, 0u};
+      if (TERMS == 3) {
+        pl[0] = ft_lo2(s[2 * kk][0], s[2 * kk][1], pa[0]);
+        pl[1] = ft_lo2(s[2 * kk][2], s[2 * kk][3], pa[1]);
+        pl[2] = ft_lo2(s[2 * kk + 1][0], s[2 * kk + 1][1], pa[2]);
+        pl[3] = ft_lo2(s[2 * kk + 1][2], s[2 * kk + 1][3], pa[3]);
+      }
 #pragma unroll
       for (int np = 0; np < 4; ++np) {
         uint32_t b0, b1, b2, b3;
-        ft_ldsm_x4_t(&Vs[kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8][np * 16 + (lane >> 4) * 8], b0, b1, b2, b3);
+        const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, cc = np * 16 + (lane >> 4) * 8;
+        ft_ldsm_x4_t(&Vs[r][cc], b0, b1, b2, b3);
         ft_mma(o[2 * np], pa, b0, b1);
         ft_mma(o[2 * np + 1], pa, b2, b3);
+        if (TERMS == 3) {
+          uint32_t l0, l1, l2, l3;
+          ft_ldsm_x4_t(&Vs[FT_KT + r][cc], l0, l1, l2, l3);
+          ft_mma(o[2 * np], pa, l0, l1);
+          ft_mma(o[2 * np + 1], pa, l2, l3);
+          ft_mma(o[2 * np], pl, b0, b1);
+          ft_mma(o[2 * np + 1], pl, b2, b3);
+        }
       }
     }
   }
@@ -696,10 +757,14 @@ k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __rest
   }
 }
 
+static size_t ft_smem(int terms) { return (size_t)(terms == 3 ? 2 : 1) * (FT_Q + 2 * FT_KT) * FT_LD * 2; }
+
 int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
-                           int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo) {
-  if (hd != FT_HD || (q_stride & 3)) return PB_ERR_ARG;
-  k_attn_prefill_tc<<<dim3(pb_cdiv(seq, FT_Q), n_heads, nseq), FT_THREADS, 0, ctx->stream>>>(
+                           int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo,
+                           int terms) {
+  if (hd != FT_HD || (q_stride & 3) || (terms != 1 && terms != 3)) return PB_ERR_ARG;
+  auto kern = terms == 3 ? k_attn_prefill_tc<3> : k_attn_prefill_tc<1>;
+  kern<<<dim3(pb_cdiv(seq, FT_Q), n_heads, nseq), FT_THREADS, ft_smem(terms), ctx->stream>>>(
       q, q_stride, kc, vc, seq, start_pos, n_heads, n_kv, (float)(1.0 / sqrt((double)hd)), out, geo);
   PB_LAUNCHED(ctx, "k_attn_prefill_tc");
   return PB_OK;
@@ -1438,7 +1503,7 @@ template <int PER>
 __global__ void __launch_bounds__(AS_WARPS * 32)
 k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                  const int* __restrict__ pos_dev, int n_kv, float scale, float* __restrict__ out,
-                 __half* __restrict__ out16, int max_len, pb_seq_geo geo, float* __restrict__ ws,
+                 __half* __restrict__ out16, int hl, int max_len, pb_seq_geo geo, float* __restrict__ ws,
                  int* __restrict__ counters, int* err) {
   extern __shared__ __align__(16) unsigned char as_raw[];
   float* qs = reinterpret_cast<float*>(as_raw);  // [per][64]
@@ -1603,9 +1668,10 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
       O = __fmaf_rn(r[2 + d], f, O);
     }
     if (!split) {
-      const size_t o = z * geo.out + (size_t)g * per * AS_HD + i;
-      if (out16) out16[o] = __float2half_rn(__fdiv_rn(O, L));
-      else out[o] = __fdiv_rn(O, L);
+      const int c = g * per * AS_HD + i;
+      if (out16 && hl) pb_store_hl(out16, pb_hl_index(z * 2 * geo.out, c), __fdiv_rn(O, L));
+      else if (out16) out16[z * geo.out + c] = __float2half_rn(__fdiv_rn(O, L));
+      else out[z * geo.out + c] = __fdiv_rn(O, L);
     } else {
       if (d == 0) {
         part[(size_t)h * rec] = M;
@@ -1633,9 +1699,10 @@ k_attn_dec_split(const float* __restrict__ q, const float* __restrict__ kc, cons
       L = __fmaf_rn(__ldcg(r + 1), f, L);
       O = __fmaf_rn(__ldcg(r + 2 + d), f, O);
     }
-    const size_t o = z * geo.out + (size_t)g * per * AS_HD + i;
-    if (out16) out16[o] = __float2half_rn(__fdiv_rn(O, L));
-    else out[o] = __fdiv_rn(O, L);
+    const int c = g * per * AS_HD + i;
+    if (out16 && hl) pb_store_hl(out16, pb_hl_index(z * 2 * geo.out, c), __fdiv_rn(O, L));
+    else if (out16) out16[z * geo.out + c] = __float2half_rn(__fdiv_rn(O, L));
+    else out[z * geo.out + c] = __fdiv_rn(O, L);
   }
   if (tid == 0) counters[(size_t)z * n_kv + g] = 0;  // for the next launch
 }
@@ -1669,7 +1736,7 @@ bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len) {
 // of a batched launch, `geo` apart).
 int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
                           int n_heads, int n_kv, int hd, float* out, int max_len, int nseq, pb_seq_geo geo,
-                          float* ws, size_t ws_floats, int* counters, __half* out16) {
+                          float* ws, size_t ws_floats, int* counters, __half* out16, int hl16) {
   if (!(nseq > 1 ? pb_attn_decode_group_ok(n_heads, n_kv, hd, max_len) : pb_attn_decode_ok(n_heads, n_kv, hd, max_len)))
     return pb_set_error(ctx, PB_ERR_ARG, "decode attention needs n_heads %% n_kv == 0, head_dim %% 4 == 0, "
                                          "head_dim <= %d and max_len <= %d", AF_MAX_HD, (200 * 1024 - AF_PART * 8) / 4);
@@ -1682,7 +1749,7 @@ int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const fl
 #define PB_AS_CASE(P)                                                                                              \
   case P:                                                                                                          \
     return pb_launch(ctx, "k_attn_dec_split", true, k_attn_dec_split<P>, grid, dim3(AS_WARPS * 32), as_smem(), q, \
-                     kc, vc, pos_dev, n_kv, (float)scale, out, out16, max_len, geo, ws, counters, ctx->d_err);
+                     kc, vc, pos_dev, n_kv, (float)scale, out, out16, hl16, max_len, geo, ws, counters, ctx->d_err);
         PB_AS_CASE(1) PB_AS_CASE(2) PB_AS_CASE(3) PB_AS_CASE(4) PB_AS_CASE(5) PB_AS_CASE(6) PB_AS_CASE(7)
         PB_AS_CASE(8)
 #undef PB_AS_CASE
@@ -1769,6 +1836,9 @@ extern "C" int pb_attn_decode(pb_ctx* ctx, const float* q, const float* kc, cons
 }
 
 int pb_setup_ops_kernels(void) {
+  for (auto k : {k_attn_prefill_tc<1>, k_attn_prefill_tc<3>})
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ft_smem(3)) != cudaSuccess)
+      return PB_ERR_CUDA;
   cudaError_t e = cudaFuncSetAttribute(k_attn_cached, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attn_dec_group, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);

@@ -408,8 +408,9 @@ class LlamaRuntime(_RuntimeBase):
 class BatchedLlamaRuntime:
     """n_seqs sequences decoded together over one StreamingLlamaRuntime's
     weights (the batched configuration).  The projections and the LM head
-    run as tensor-core GEMMs with f16 operands, so logits agree with the
-    one-sequence runtime within a relative tolerance, not bit for bit.
+    run as tensor-core GEMMs over f16 hi/lo operand pairs, so logits agree
+    with the one-sequence runtime within a relative tolerance, not bit for
+    bit.
 
     comm (thread_pool.NcclComm): this process is one rank of a row split
     over comm's GPUs (pb_batch_create_split); every rank calls prefill and
@@ -435,6 +436,11 @@ class BatchedLlamaRuntime:
             self.ctx._check(N.lib().pb_batch_create(base.model.h, n_seqs, ctypes.byref(h)))
         self.h = h.value
         self.n_prompt = 0
+
+    def set_precision(self, terms: int) -> None:
+        """3 (default): hi/lo f16 operand pairs, three tensor-core products per
+        GEMM; 1: each operand rounded to f16 once (faster, about 3e-3)."""
+        self.ctx._check(N.lib().pb_batch_set_precision(self.h, int(terms)))
 
     def prefill(self, prompts, want_logits: bool = False):
         """prompts: [n_seqs][n_prompt] token ids -> next greedy token per sequence."""

@@ -1,12 +1,14 @@
 """Batched serving (pb_batch_*): every sequence's prefill and decode logits
 match the one-sequence device path (which matches the reference oracle) within
-the f16-GEMM tolerance; greedy tokens follow those logits."""
+the batched GEMMs' tolerance; greedy tokens follow those logits."""
 import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
-# f16 operands in every projection: relative to the largest logit of the row
-RTOL_LOGITS = 2e-2
+# relative to the largest logit of the row: the north star's per-op bar with
+# the three-term GEMMs (the default), and the bound of the one-rounding form
+RTOL_LOGITS = 1e-3
+RTOL_LOGITS_ONE_TERM = 2e-2
 
 
 def make(native, ctx, seed=5, **kw):
@@ -19,29 +21,35 @@ def make(native, ctx, seed=5, **kw):
     return rt
 
 
-def close(a, b):
+def close(a, b, rtol=RTOL_LOGITS):
     a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
     err = np.max(np.abs(a - b)) / np.max(np.abs(b))
-    return err <= RTOL_LOGITS, err
+    return err <= rtol, err
 
 
-@pytest.mark.parametrize("n_seqs,n_prompt,hd,dim", [(3, 5, 32, 128), (4, 130, 32, 128), (3, 70, 64, 128),
-                                                    (2, 300, 64, 128), (4, 9, 64, 512)])
-def test_batch_matches_single_sequence(native, ctx, n_seqs, n_prompt, hd, dim):
+@pytest.mark.parametrize("n_seqs,n_prompt,hd,dim,terms", [(3, 5, 32, 128, 3), (4, 130, 32, 128, 3),
+                                                          (3, 70, 64, 128, 3), (2, 300, 64, 128, 3),
+                                                          (4, 9, 64, 512, 3), (3, 70, 64, 128, 1),
+                                                          (2, 300, 64, 128, 1)])
+def test_batch_matches_single_sequence(native, ctx, n_seqs, n_prompt, hd, dim, terms):
     """15 / 210 rows run the fused-dequant GEMM, 520 / 600 the TMA one; head_dim 64
-    takes the f32 tiled prefill attention, 32 the per-query kernel; dim 512
-    makes the decode GEMMs split K over CTAs."""
+    takes the tiled prefill attention, 32 the per-query kernel; dim 512
+    makes the decode GEMMs split K over CTAs.  terms: the GEMM precision."""
     from purebee_b200.runtime import BatchedLlamaRuntime
     rt = make(native, ctx, dim=dim, hiddenDim=2 * dim, headDim=hd, nHeads=dim // hd, nKvHeads=max(1, dim // (2 * hd)),
               seqLen=400)
     rng = np.random.default_rng(n_seqs * 100 + n_prompt)
     prompts = rng.integers(1, 512, (n_seqs, n_prompt)).astype(np.int32)
     bt = BatchedLlamaRuntime(rt, n_seqs)
+    bt.set_precision(terms)
+    rtol = RTOL_LOGITS if terms == 3 else RTOL_LOGITS_ONE_TERM
     nxt, lg = bt.prefill(prompts, want_logits=True)
+    errs = []
     for s in range(n_seqs):
         rt.resetCache()
         want = rt.forward(prompts[s].tolist(), 0)["logits"]
-        ok, err = close(lg[s], want)
+        ok, err = close(lg[s], want, rtol)
+        errs.append(err)
         assert ok, f"prefill seq {s}: rel err {err:.2e}"
         assert nxt[s] == int(np.argmax(lg[s]))
     # teacher-forced decode: the one-sequence path fed the batch's own tokens
@@ -52,10 +60,12 @@ def test_batch_matches_single_sequence(native, ctx, n_seqs, n_prompt, hd, dim):
             rt.resetCache()
             seq = prompts[s].tolist() + [int(t[s]) for t in fed]
             want = rt.forward(seq, 0)["logits"]
-            ok, err = close(lgd[s], want)
+            ok, err = close(lgd[s], want, rtol)
+            errs.append(err)
             assert ok, f"decode step {step} seq {s}: rel err {err:.2e}"
             assert toks[0][s] == int(np.argmax(lgd[s]))
         fed.append(toks[0].copy())
+    print(f"\n[batched parity] {n_seqs}x{n_prompt} hd {hd} dim {dim} terms {terms}: max rel logit err {max(errs):.3e}")
     bt.free()
     rt.shutdown()
 
