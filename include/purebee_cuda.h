@@ -251,9 +251,12 @@ int pb_attn_cached(pb_ctx* ctx, const float* q_dev, const float* kc_dev, const f
 /* llama-streaming.js:543-573: the attention of one query q [n_heads *
  * head_dim] at position pos over a [max_len, n_kv * head_dim] K/V cache
  * holding rows 0..pos, as the decode step runs it: the positions split over
- * the GPU's SMs, double dots and sums, the splits merged in a fixed order.
- * At most 8 query heads per kv head, head_dim % 4 == 0 and <= 128.  Blocks
- * until done (the context scratch holds the per-split partials). */
+ * the GPU's SMs, the splits merged in a fixed order.  In the exact matvec
+ * mode, and for head_dim != 64, dots and sums run in double (the
+ * reference's arithmetic, within an f32 rounding); in the fast mode
+ * (head_dim 64, max_len <= 2048) in f32 with the splits of a kv head merged
+ * through one thread-block cluster.  At most 8 query heads per kv head,
+ * head_dim % 4 == 0 and <= 128.  Blocks until done. */
 int pb_attn_decode(pb_ctx* ctx, const float* q_dev, const float* kc_dev, const float* vc_dev, int pos, int n_heads,
                    int n_kv, int head_dim, int max_len, float* out_dev);
 /* llama-streaming.js:590-595 fused SiLU(gate)*up */

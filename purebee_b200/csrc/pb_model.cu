@@ -30,6 +30,9 @@ int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const fl
                           __half* out16 = nullptr, int hl16 = 0);
 
 int pb_attn_dec1_splits(int n_kv, int max_len, int sm_count);
+bool pb_attn_dec_fast_ok(int n_heads, int n_kv, int hd, int max_len);
+int pb_launch_attn_dec_fast(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
+                            int n_heads, int n_kv, int hd, float* out, int max_len);
 size_t pb_attn_dec1_ws_doubles(int n_heads, int n_kv, int hd, int nsplit);
 bool pb_attn_dec1_ok(int n_heads, int n_kv, int hd);
 int pb_launch_attn_dec1(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
@@ -602,6 +605,10 @@ static void l2_hint(pb_mv_epi* e, int i, const pb_qmat* w, size_t cap = ~(size_t
 // per query head.
 static int launch_attn_decode1(pb_model* m, int l, const float* q, const int* pos_dev) {
   const pb_model_config& c = m->c;
+  // fast mode: the f32, cluster-merged form
+  if (m->ctx->matvec_mode == PB_MATVEC_FAST && pb_attn_dec_fast_ok(c.n_heads, c.n_kv_heads, c.head_dim, c.seq_len))
+    return pb_launch_attn_dec_fast(m->ctx, q, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads,
+                                   c.head_dim, m->att, c.seq_len);
   if (m->attn_ws)
     return pb_launch_attn_dec1(m->ctx, q, kcache(m, l), vcache(m, l), pos_dev, c.n_heads, c.n_kv_heads, c.head_dim,
                                m->att, c.seq_len, m->attn_splits, m->attn_ws, m->attn_cnt);

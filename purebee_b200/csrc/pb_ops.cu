@@ -15,6 +15,8 @@
 
 #include <mutex>
 
+#include <cooperative_groups.h>
+
 #include "pb_internal.cuh"
 
 // ============================================================================
@@ -1816,6 +1818,230 @@ int pb_launch_attn_dec1(pb_ctx* ctx, const float* q, const float* kc, const floa
   }
 }
 
+// k_attn_dec_fast<PER>: the fast mode's decode attention for one query
+// (head_dim 64), the f32 form of k_attn_dec1 above.  CTA (kv head g, split
+// sp) over the positions [sp * P, (sp + 1) * P), P = ceil(cache_len / nsplit),
+// for the PER query heads of the group; the nsplit CTAs of a kv head are one
+// thread-block cluster.
+//   - before griddepcontrol.wait: the split's K and V rows j < pos (final:
+//     written by earlier steps) into shared memory by cp.async, so their
+//     latency overlaps the projection that is still running;
+//   - after it: q and the row at pos (this step's), then scores (thread per
+//     position, f32 dots of the four 16-dim quarters), per head the split's
+//     max m_c, p_j = exp(s_j - m_c), S_c = sum p_j, O_c = sum p_j V_j (four
+//     position groups, summed in order);
+//   - cluster barrier, then CTA sp merges a slice of the PER x 64 outputs
+//     from every split's shared memory (distributed shared memory), in split
+//     order: M = max m_c, out = sum O_c e^(m_c - M) / sum S_c e^(m_c - M);
+//     a second barrier keeps each CTA's shared memory alive until read.
+// f32 throughout (the reference sums in double): the differences are of f32
+// rounding, within the fast mode's tolerance; the split depends only on the
+// cache length, so results do not depend on scheduling.
+constexpr int AQ_THREADS = 128, AQ_HD = 64, AQ_KLD = 68, AQ_MAXP = 256, AQ_MAX_SPLIT = 8;
+
+static size_t aq_smem(int per, int pmax) {
+  return ((size_t)pmax * AQ_KLD + (size_t)pmax * AQ_HD + (size_t)per * pmax + (size_t)per * AQ_HD +
+          (size_t)4 * per * AQ_HD) * 4;
+}
+
+template <int PER>
+__global__ void __launch_bounds__(AQ_THREADS)
+k_attn_dec_fast(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                const int* __restrict__ pos_dev, int n_kv, float scale, float* __restrict__ out, int max_len, int pmax,
+                int* err) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  extern __shared__ __align__(16) float aq_sm[];
+  float* ks = aq_sm;                                  // [pmax][AQ_KLD] (padded: conflict-free row reads)
+  float* vs = ks + (size_t)pmax * AQ_KLD;             // [pmax][64]
+  float* sc = vs + (size_t)pmax * AQ_HD;              // [PER][pmax]: scores, then p
+  float* qs = sc + (size_t)PER * pmax;                // [PER][64]
+  float* gp = qs + PER * AQ_HD;                       // [4][PER][64]: PV partials of the position groups
+  __shared__ float red_m[PER][AQ_THREADS / 32], red_s[PER][AQ_THREADS / 32];
+  __shared__ float part_m[PER], part_s[PER];
+  __shared__ __align__(16) float part_o[PER * AQ_HD];
+  const int g = blockIdx.x, sp = (int)cl.block_rank(), nsplit = (int)cl.num_blocks(), tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int pos = *pos_dev;  // final: the step's first kernel starts after the previous step ended
+  const int cache_len = pos + 1;
+  const int P = (cache_len + nsplit - 1) / nsplit;
+  if (pos < 0 || cache_len > max_len || P > pmax) {  // the same for every CTA: all leave before any barrier
+    pb_pdl_trigger();
+    if (tid == 0 && g == 0 && sp == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+    return;
+  }
+  const int kv_dim = n_kv * AQ_HD;
+  const int j0 = sp * P;
+  const int n = cache_len - j0 < 0 ? 0 : (cache_len - j0 < P ? cache_len - j0 : P);
+  const bool has_pos = pos >= j0 && pos < j0 + n;
+  const int npre = has_pos ? n - 1 : n;  // rows before pos: final already
+  const float* kb = kc + (size_t)g * AQ_HD;
+  const float* vb = vc + (size_t)g * AQ_HD;
+  for (int i = tid; i < npre * 16; i += AQ_THREADS) {
+    const int r = i >> 4, c = i & 15;
+    const size_t src = (size_t)(j0 + r) * kv_dim + 4 * c;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(pb_smem_addr(ks + r * AQ_KLD + 4 * c)),
+                 "l"(kb + src) : "memory");
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(pb_smem_addr(vs + r * AQ_HD + 4 * c)),
+                 "l"(vb + src) : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  pb_pdl_trigger();
+  pb_pdl_wait();  // q and the cache row at pos come from the projection
+  if (has_pos && tid < 32) {
+    const int r = pos - j0, c = tid & 15;
+    const float* src = (tid < 16 ? kb : vb) + (size_t)pos * kv_dim + 4 * c;
+    float* dst = tid < 16 ? ks + r * AQ_KLD + 4 * c : vs + r * AQ_HD + 4 * c;
+    *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(src);
+  }
+  for (int i = tid; i < PER * AQ_HD / 4; i += AQ_THREADS)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q + (size_t)g * PER * AQ_HD)[i];
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+
+  // scores: thread per position, four independent 16-dim chains per head
+  for (int t = tid; t < n; t += AQ_THREADS) {
+    const float4* kr = reinterpret_cast<const float4*>(ks + t * AQ_KLD);
+    float a[PER][4];
+#pragma unroll
+    for (int h = 0; h < PER; ++h) a[h][0] = a[h][1] = a[h][2] = a[h][3] = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const float4 k4 = kr[u];
+#pragma unroll
+      for (int h = 0; h < PER; ++h) {
+        const float4 q4 = reinterpret_cast<const float4*>(qs + h * AQ_HD)[u];
+        float& acc = a[h][u & 3];
+        acc = fmaf(q4.x, k4.x, acc);
+        acc = fmaf(q4.y, k4.y, acc);
+        acc = fmaf(q4.z, k4.z, acc);
+        acc = fmaf(q4.w, k4.w, acc);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < PER; ++h) sc[h * pmax + t] = ((a[h][0] + a[h][1]) + (a[h][2] + a[h][3])) * scale;
+  }
+  __syncthreads();
+  // per head: the split's max (`s > m` from -Infinity: NaN never wins), then p and its sum
+  float mh[PER];
+#pragma unroll
+  for (int h = 0; h < PER; ++h) {
+    float m = -INFINITY;
+    for (int t = tid; t < n; t += AQ_THREADS) m = sc[h * pmax + t] > m ? sc[h * pmax + t] : m;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float o_ = __shfl_xor_sync(0xffffffffu, m, o);
+      m = o_ > m ? o_ : m;
+    }
+    if (lane == 0) red_m[h][warp] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int h = 0; h < PER; ++h) {
+    float m = red_m[h][0];
+    for (int w = 1; w < AQ_THREADS / 32; ++w) m = red_m[h][w] > m ? red_m[h][w] : m;
+    mh[h] = m;
+    float s_ = 0.0f;
+    for (int t = tid; t < n; t += AQ_THREADS) {
+      const float p = expf(sc[h * pmax + t] - m);
+      sc[h * pmax + t] = p;
+      s_ += p;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s_ += __shfl_xor_sync(0xffffffffu, s_, o);
+    if (lane == 0) red_s[h][warp] = s_;
+  }
+  __syncthreads();
+  // PV: thread (dim pair dp, position group jg), positions jg, jg + 4, ...
+  {
+    const int dp = tid & 31, jg = tid >> 5;
+    float2 acc[PER];
+#pragma unroll
+    for (int h = 0; h < PER; ++h) acc[h] = make_float2(0.0f, 0.0f);
+    for (int t = jg; t < n; t += 4) {
+      const float2 v = reinterpret_cast<const float2*>(vs + t * AQ_HD)[dp];
+#pragma unroll
+      for (int h = 0; h < PER; ++h) {
+        const float p = sc[h * pmax + t];
+        acc[h].x = fmaf(p, v.x, acc[h].x);
+        acc[h].y = fmaf(p, v.y, acc[h].y);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < PER; ++h) reinterpret_cast<float2*>(gp + ((size_t)jg * PER + h) * AQ_HD)[dp] = acc[h];
+  }
+  __syncthreads();
+  for (int i = tid; i < PER * AQ_HD; i += AQ_THREADS)
+    part_o[i] = ((gp[i] + gp[PER * AQ_HD + i]) + gp[2 * PER * AQ_HD + i]) + gp[3 * PER * AQ_HD + i];
+  if (tid < PER) {  // (from shared memory: mh indexed by tid would go to local memory)
+    float m = red_m[tid][0];
+    for (int w = 1; w < AQ_THREADS / 32; ++w) m = red_m[tid][w] > m ? red_m[tid][w] : m;
+    part_m[tid] = n > 0 ? m : -INFINITY;
+    part_s[tid] = n > 0 ? ((red_s[tid][0] + red_s[tid][1]) + red_s[tid][2]) + red_s[tid][3] : 0.0f;
+  }
+  cl.sync();  // every split's partial is written
+  // this CTA's slice of the outputs, merged over the splits in order
+  const int per_cta = (PER * AQ_HD + nsplit - 1) / nsplit;
+  const int i = sp * per_cta + tid;
+  if (tid < per_cta && i < PER * AQ_HD) {
+    const int h = i / AQ_HD;
+    float M = -INFINITY;
+    for (int c = 0; c < nsplit; ++c) {
+      const float s_ = *cl.map_shared_rank(&part_s[h], c), m_ = *cl.map_shared_rank(&part_m[h], c);
+      if (s_ != 0.0f && m_ > M) M = m_;
+    }
+    float S = 0.0f, O = 0.0f;
+    for (int c = 0; c < nsplit; ++c) {
+      const float s_ = *cl.map_shared_rank(&part_s[h], c);
+      if (s_ == 0.0f) continue;  // an empty split
+      const float f = expf(*cl.map_shared_rank(&part_m[h], c) - M);
+      S = fmaf(s_, f, S);
+      O = fmaf(*cl.map_shared_rank(&part_o[i], c), f, O);
+    }
+    out[(size_t)g * PER * AQ_HD + i] = O / S;
+  }
+  cl.sync();  // the other CTAs have read this one's partial
+}
+
+// Whether the fast decode attention takes this shape (max_len positions in
+// at most AQ_MAX_SPLIT splits of at most AQ_MAXP).
+bool pb_attn_dec_fast_ok(int n_heads, int n_kv, int hd, int max_len) {
+  return n_kv > 0 && n_heads % n_kv == 0 && n_heads / n_kv <= 8 && hd == AQ_HD &&
+         (max_len + AQ_MAX_SPLIT - 1) / AQ_MAX_SPLIT <= AQ_MAXP;
+}
+
+int pb_launch_attn_dec_fast(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
+                            int n_heads, int n_kv, int hd, float* out, int max_len) {
+  if (!pb_attn_dec_fast_ok(n_heads, n_kv, hd, max_len))
+    return pb_set_error(ctx, PB_ERR_ARG, "fast decode attention: unsupported shape");
+  const int nsplit = AQ_MAX_SPLIT, pmax = (max_len + nsplit - 1) / nsplit, per = n_heads / n_kv;
+  const float scale = (float)(1.0 / sqrt((double)hd));  // llama-streaming.js:546
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_kv, nsplit);
+  cfg.blockDim = dim3(AQ_THREADS);
+  cfg.dynamicSmemBytes = aq_smem(per, pmax);
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = nsplit;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = ctx->pdl ? 2 : 1;
+  cudaError_t e = cudaErrorInvalidValue;
+  switch (per) {
+#define PB_AQ_CASE(P) \
+  case P: e = cudaLaunchKernelEx(&cfg, k_attn_dec_fast<P>, q, kc, vc, pos_dev, n_kv, scale, out, max_len, pmax, ctx->d_err); break;
+    PB_AQ_CASE(1) PB_AQ_CASE(2) PB_AQ_CASE(3) PB_AQ_CASE(4) PB_AQ_CASE(5) PB_AQ_CASE(6) PB_AQ_CASE(7) PB_AQ_CASE(8)
+#undef PB_AQ_CASE
+    default: break;
+  }
+  if (e != cudaSuccess) return pb_cuda_error(ctx, e, "k_attn_dec_fast");
+  return pb_check_launch(ctx, "k_attn_dec_fast");
+}
+
 extern "C" int pb_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const float* vc, int pos, int n_heads,
                               int n_kv, int hd, int max_len, float* out) {
   if (!ctx || !q || !kc || !vc || !out || n_heads <= 0 || n_kv <= 0 || hd <= 0 || pos < 0 || pos >= max_len)
@@ -1823,15 +2049,17 @@ extern "C" int pb_attn_decode(pb_ctx* ctx, const float* q, const float* kc, cons
   if (!pb_attn_dec1_ok(n_heads, n_kv, hd))
     return pb_set_error(ctx, PB_ERR_ARG, "pb_attn_decode: needs n_heads %% n_kv == 0, at most 8 query heads per kv "
                                          "head, head_dim %% 4 == 0 and head_dim <= %d", AD1_MAX_HD);
+  const bool fast = ctx->matvec_mode == PB_MATVEC_FAST && pb_attn_dec_fast_ok(n_heads, n_kv, hd, max_len);
   const int nsplit = pb_attn_dec1_splits(n_kv, max_len, ctx->sm_count);
-  const size_t wsb = pb_attn_dec1_ws_doubles(n_heads, n_kv, hd, nsplit) * 8;
+  const size_t wsb = fast ? 0 : pb_attn_dec1_ws_doubles(n_heads, n_kv, hd, nsplit) * 8;
   PB_TRY(pb_ensure_scratch(ctx, wsb + 256 + (size_t)n_kv * 4 + 16));
   double* ws = (double*)ctx->scratch;
   unsigned int* cnt = (unsigned int*)((char*)ctx->scratch + ((wsb + 255) & ~(size_t)255));
   int* pos_dev = (int*)(cnt + n_kv);
   PB_TRY_CUDA(ctx, cudaMemsetAsync(cnt, 0, (size_t)n_kv * 4, ctx->stream));
   PB_TRY_CUDA(ctx, cudaMemcpyAsync(pos_dev, &pos, 4, cudaMemcpyHostToDevice, ctx->stream));
-  PB_TRY(pb_launch_attn_dec1(ctx, q, kc, vc, pos_dev, n_heads, n_kv, hd, out, max_len, nsplit, ws, cnt));
+  if (fast) PB_TRY(pb_launch_attn_dec_fast(ctx, q, kc, vc, pos_dev, n_heads, n_kv, hd, out, max_len));
+  else PB_TRY(pb_launch_attn_dec1(ctx, q, kc, vc, pos_dev, n_heads, n_kv, hd, out, max_len, nsplit, ws, cnt));
   return pb_wait(ctx);  // the position's host copy must outlive the transfer
 }
 
@@ -1845,6 +2073,9 @@ int pb_setup_ops_kernels(void) {
   for (auto k : {k_attn_dec_split<1>, k_attn_dec_split<2>, k_attn_dec_split<3>, k_attn_dec_split<4>,
                  k_attn_dec_split<5>, k_attn_dec_split<6>, k_attn_dec_split<7>, k_attn_dec_split<8>})
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)as_smem());
+  for (auto k : {k_attn_dec_fast<1>, k_attn_dec_fast<2>, k_attn_dec_fast<3>, k_attn_dec_fast<4>,
+                 k_attn_dec_fast<5>, k_attn_dec_fast<6>, k_attn_dec_fast<7>, k_attn_dec_fast<8>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   for (auto k : {k_attn_dec1<1>, k_attn_dec1<2>, k_attn_dec1<3>, k_attn_dec1<4>, k_attn_dec1<5>, k_attn_dec1<6>,
                  k_attn_dec1<7>, k_attn_dec1<8>})
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);

@@ -5,12 +5,19 @@
 //     blockAcc[L] = sum over g in {0,4,8,12} of  (lo-8)*x[g+L], (hi-8)*x[g+16+L]
 // in f32 with a separate multiply and add, then the in-order chain
 //     acc[L] = acc[L] + blockAcc[L]*d        (blocks b = 0, 1, 2, ...)
-// and y = (acc1 + acc3) + (acc0 + acc2).  The per-block partials are
-// independent, so eight producer warps compute them for all (row, block)
-// pairs of a row tile in parallel (lanes = rows, one coalesced 16 B load per
-// lane); one consumer warp runs the in-order chains from a shared-memory ring
-// as chunks of blocks complete (mbarrier handshake, bounded waits).  The
-// result is bit-identical to the reference's WASM kernel.
+// and y = (acc1 + acc3) + (acc0 + acc2).  Two modes run it (pb_set_matvec_mode):
+//   - exact (k_matvec, k_matvec_ws): the per-block partials are independent,
+//     so warps compute them for all (row, block) pairs of an 8-row tile in
+//     parallel and the in-order acc[L] chains run over them from shared
+//     memory: bit-identical to the reference's WASM kernel;
+//   - fast, the default (k_mvf here; k_mvi, the int8 tensor-core kernel in
+//     pb_mvi.cu, for matrices of at least ctx->mvi_min_rows rows): the same
+//     exact (q-8)*x products summed in another order with one FMA per
+//     weight, a warp per (8-row tile, 32-block chunk) unit with the payload
+//     streamed through per-warp cp.async stages, chunk partials summed in
+//     order: within an f32 relative tolerance of the reference.
+// Both take the same fused prologues (RMSNorm of x) and epilogues (residual
+// add, RoPE + KV append, SwiGLU of interleaved gate|up tiles, argmax).
 //
 // Head (wasm-q4.js:447-566 batch_dot over the table gguf.js:239-286
 // dequantizes).  The reference's lane L chain runs over k = L, L+4, ... of

@@ -131,6 +131,9 @@ def test_resident_matvec_row_split(native, ctx, oracle, exact_mode):
 # per weight in another order; per-op bar of the north star is an f32
 # relative tolerance, this is far inside it
 RTOL_MATVEC_FAST = 2e-6
+# the fast mode's decode attention: f32 dots, exponentials and sums where the
+# reference uses double
+RTOL_ATTN_FAST = 5e-6
 
 
 @pytest.fixture(params=["f32", "int8"])
@@ -456,12 +459,17 @@ def test_attention_cached_and_generic(native, ctx, oracle, golden):
     (9, 3, 64, 512, (31, 287)),                       # configs[2]: SmolLM2-135M
     (6, 6, 48, 256, (15, 143)),                       # configs[0]: stories15M
 ])
-def test_split_decode_attention(native, ctx, oracle, nh, nkv, hd, max_len, positions):
+@pytest.mark.parametrize("mode", ["fast", "exact"])
+def test_split_decode_attention(native, ctx, oracle, nh, nkv, hd, max_len, positions, mode):
     """The decode step's position-split attention (pb_attn_decode) against
     the oracle's llama-streaming.js:543-573 at cache lengths from 1 to the
-    maximum, within the reduction tolerance; a second call on the same
-    buffers gives the same bits (the split counters are left at zero)."""
+    maximum, within the reduction tolerance (the fast mode's f32 form within
+    RTOL_ATTN_FAST); a second call on the same buffers gives the same bits
+    (the split counters are left at zero)."""
     L = native.lib()
+    ctx.set_matvec_mode(native.MATVEC_FAST if mode == "fast" else native.MATVEC_EXACT)
+    rtol = RTOL_ATTN_FAST if mode == "fast" else RTOL_REDUCE
+    worst = 0.0
     rng = np.random.default_rng(52 + hd)
     kv = nkv * hd
     kk = rng.standard_normal((max_len, kv)).astype(f32)
@@ -473,11 +481,14 @@ def test_split_decode_attention(native, ctx, oracle, nh, nkv, hd, max_len, posit
         ctx._check(L.pb_attn_decode(ctx.h, dq.ptr, dkc.ptr, dvc.ptr, pos, nh, nkv, hd, max_len, o.ptr))
         got = o.download(count=nh * hd)
         want = oracle.attn_cached(qq, kk[:pos + 1], vv[:pos + 1], 1, pos, nh * hd, nh, nkv, hd)
-        assert close(got, want), pos
+        worst = max(worst, np.max(np.abs(got.astype(np.float64) - want)) / np.max(np.abs(want)))
+        assert close(got, want, rtol), pos
         ctx._check(L.pb_attn_decode(ctx.h, dq.ptr, dkc.ptr, dvc.ptr, pos, nh, nkv, hd, max_len, o.ptr))
         assert bits_equal(o.download(count=nh * hd), got), pos
+    print(f"[decode attention] {mode} {nh}/{nkv}x{hd} max_len {max_len}: worst rel err {worst:.3e}")
     with pytest.raises(native.PureBeeError):
         ctx._check(L.pb_attn_decode(ctx.h, dq.ptr, dkc.ptr, dvc.ptr, max_len, nh, nkv, hd, max_len, o.ptr))
+    ctx.set_matvec_mode(native.MATVEC_FAST)
 
 
 def test_capture_replay(native, ctx, oracle):
