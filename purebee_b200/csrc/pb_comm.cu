@@ -107,6 +107,8 @@ __global__ void __launch_bounds__(256)
 k_peer_gather(pb_peer_bufs bufs, size_t chunk_bytes, int rank, int world, pb_peer_sync sync,
               unsigned long long* __restrict__ epoch, unsigned int* __restrict__ done, unsigned long long limit_ns,
               int vec16, int* err) {
+  pb_pdl_trigger();
+  pb_pdl_wait();  // this rank's chunk (and the epoch) come from the kernels before
   const size_t off = (size_t)rank * chunk_bytes;
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   if (vec16) {
@@ -159,10 +161,8 @@ static int launch_peer_gather(pb_ctx* ctx, const pb_peer_bufs& bufs, size_t chun
   int grid = (int)((units + 256 * 4 - 1) / (256 * 4));
   grid = grid < 1 ? 1 : grid > 2 * ctx->sm_count ? 2 * ctx->sm_count : grid;
   const unsigned long long limit = (unsigned long long)ctx->timeout_ms * 1000000ull;
-  k_peer_gather<<<grid, 256, 0, ctx->stream>>>(bufs, chunk_bytes, rank, world, sync, epoch, done, limit, vec16 ? 1 : 0,
-                                              ctx->d_err);
-  PB_LAUNCHED(ctx, "k_peer_gather");
-  return PB_OK;
+  return pb_launch(ctx, "k_peer_gather", true, k_peer_gather, dim3(grid), dim3(256), 0, bufs, chunk_bytes, rank, world,
+                   sync, epoch, done, limit, vec16 ? 1 : 0, ctx->d_err);
 }
 
 // ---------------------------------------------------------------------------
@@ -181,6 +181,8 @@ static int launch_peer_gather(pb_ctx* ctx, const pb_peer_bufs& bufs, size_t chun
 __global__ void __launch_bounds__(256)
 k_ll_gather(char* __restrict__ buf, size_t chunk_bytes, int rank, int world, pb_ll_slots slots, size_t cap_units,
             unsigned int* __restrict__ epoch, unsigned int* __restrict__ done, unsigned long long limit_ns, int* err) {
+  pb_pdl_trigger();
+  pb_pdl_wait();  // this rank's chunk (and the epoch) come from the kernels before
   const unsigned int e = *epoch + 1u;
   const size_t half = e & 1u, n = chunk_bytes / 8;
   const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
@@ -233,10 +235,8 @@ int pb_comm_ll_gather(pb_comm* c, const pb_ll_slots& slots, size_t cap_units, ch
   int grid = (int)((n + 255) / 256);
   grid = grid < 1 ? 1 : grid > ctx->sm_count ? ctx->sm_count : grid;  // all CTAs resident
   const unsigned long long limit = (unsigned long long)ctx->timeout_ms * 1000000ull;
-  k_ll_gather<<<grid, 256, 0, ctx->stream>>>(buf, chunk_bytes, c->rank, c->world, slots, cap_units, epoch, done, limit,
-                                            ctx->d_err);
-  PB_LAUNCHED(ctx, "k_ll_gather");
-  return PB_OK;
+  return pb_launch(ctx, "k_ll_gather", true, k_ll_gather, dim3(grid), dim3(256), 0, buf, chunk_bytes, c->rank, c->world,
+                   slots, cap_units, epoch, done, limit, ctx->d_err);
 }
 
 extern "C" int pb_comm_id(void* id_out) {

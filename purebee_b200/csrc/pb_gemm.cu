@@ -182,6 +182,8 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
   const int wr = tid >> 1, wblk = tid & 1;  // weights: (row, block) of the two Q4_0 blocks of a step
   const int xr_ = tid >> 1, xh = tid & 1;   // activations: (token, half of the 64-wide step)
   const bool xlive_row = xr_ < TOK && m0 + xr_ < M;
+  pb_pdl_trigger();
+  pb_pdl_wait();  // the activations (and C) come from the previous kernels
   uint4 pl;
   float dsv;
   float4 xa[8];
@@ -358,6 +360,8 @@ __device__ __forceinline__ void mma_f16_n256(uint32_t tmem_d, uint64_t adesc, ui
 __global__ void k_dequant_q4_f16(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int layout, int nb,
                                  int64_t nblocks, __half* __restrict__ out, int terms) {
   const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // output block (row-major) per thread
+  pb_pdl_trigger();
+  pb_pdl_wait();  // the scratch it writes may still be read by the GEMM before
   if (b >= nblocks) return;
   const int row = (int)(b / nb), blk = (int)(b % nb);
   const int64_t slot = pb_slot(layout, row, blk, nb);
@@ -392,6 +396,8 @@ __global__ void k_dequant_q4_f16(const uint8_t* __restrict__ qs, const uint16_t*
 __global__ void k_f32_to_f16(const float* __restrict__ x, int M, int K, int ldx, int kc, __half* __restrict__ out,
                              int terms) {
   const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;  // 4 values per thread
+  pb_pdl_trigger();
+  pb_pdl_wait();
   if (i >= (int64_t)M * K) return;
   const int m = (int)(i / K), k = (int)(i % K);
   const float* src = kc ? x + (size_t)(k / kc) * M * kc + (size_t)m * kc + k % kc : x + (size_t)m * ldx + k;
@@ -444,6 +450,8 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem_d = tmem_base;
+  pb_pdl_trigger();
+  pb_pdl_wait();  // both operands and C come from the previous kernels
 
   if (warp == 0 && lane == 0) {
     // producer: stage s is free once the MMAs that read it committed to empty[s]
@@ -586,13 +594,12 @@ static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, const 
   __half* w16 = reinterpret_cast<__half*>(ctx->gemm_scratch);
   const __half* x16 = Xh;
   const int64_t nblk = (int64_t)w->N_pad * w->nb;
-  k_dequant_q4_f16<<<pb_cdiv(nblk, 256), 256, 0, ctx->stream>>>(w->qs, w->d, w->layout, w->nb, nblk, w16, epi.terms);
-  PB_LAUNCHED(ctx, "k_dequant_q4_f16");
+  PB_TRY(pb_launch(ctx, "k_dequant_q4_f16", true, k_dequant_q4_f16, dim3((unsigned)pb_cdiv(nblk, 256)), dim3(256), 0,
+                   (const uint8_t*)w->qs, (const uint16_t*)w->d, w->layout, w->nb, nblk, w16, epi.terms));
   if (!Xh) {  // the activations rounded to f16 once (or split into hi/lo pairs)
     __half* xs = reinterpret_cast<__half*>(static_cast<char*>(ctx->gemm_scratch) + off_x);
-    k_f32_to_f16<<<pb_cdiv((int64_t)M * K / 4, 256), 256, 0, ctx->stream>>>(X, M, K, ldx, epi.x_chunk, xs,
-                                                                             epi.terms);
-    PB_LAUNCHED(ctx, "k_f32_to_f16");
+    PB_TRY(pb_launch(ctx, "k_f32_to_f16", true, k_f32_to_f16, dim3((unsigned)pb_cdiv((int64_t)M * K / 4, 256)),
+                     dim3(256), 0, X, M, K, ldx, epi.x_chunk, xs, epi.terms));
     x16 = xs;
   }
   // the f32 conversion writes whole rows; an f16 operand keeps its chunks
@@ -604,9 +611,8 @@ static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, const 
   if (ntiles > (1ll << 30)) return pb_set_error(ctx, PB_ERR_ARG, "M=%d too large", M);
   const int grid = (int)(ntiles < ctx->sm_count ? ntiles : ctx->sm_count);  // persistent: one CTA per SM
   auto kern = epi.terms == 3 ? k_gemm_f16_tma<3> : k_gemm_f16_tma<1>;
-  kern<<<grid, TG_THREADS, tg_smem(epi.terms), ctx->stream>>>(mw, mx, w->N, M, K, xkc, C, ldc, epi, ctx->d_err);
-  PB_LAUNCHED(ctx, "k_gemm_f16_tma");
-  return PB_OK;
+  return pb_launch(ctx, "k_gemm_f16_tma", true, kern, dim3(grid), dim3(TG_THREADS), tg_smem(epi.terms), mw, mx, w->N, M,
+                   K, xkc, C, ldc, epi, ctx->d_err);
 }
 
 // C[m][n] = sum over z (ascending) of the split-K partials ws[z][m][n], then
@@ -615,6 +621,8 @@ static int launch_gemm_tma(pb_ctx* ctx, const pb_qmat* w, const float* X, const 
 __global__ void k_splitk_reduce(const float* __restrict__ ws, int splits, int M, int N, float* __restrict__ C,
                                 int ldc, pb_gemm_epi epi) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
+  pb_pdl_trigger();
+  pb_pdl_wait();  // the partials come from the GEMM before
   if (epi.mode == PB_GEMM_SWIGLU) {
     if (i >= N / 2) return;
     const int ng = 8 * (i >> 2) + (i & 3), nu = ng + 4;
@@ -692,13 +700,13 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
                                : (epi.x_chunk ? k_q4_gemm_tc<128, true, 3> : k_q4_gemm_tc<128, false, 3>))
                   : (tok == 64 ? (epi.x_chunk ? k_q4_gemm_tc<64, true, 1> : k_q4_gemm_tc<64, false, 1>)
                                : (epi.x_chunk ? k_q4_gemm_tc<128, true, 1> : k_q4_gemm_tc<128, false, 1>));
-  kern<<<grid, GM_THREADS, gm_smem(epi.terms), ctx->stream>>>(w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, X, ldx, M, dst, ldd,
-                                                    kper, kepi, ctx->d_err);
-  PB_LAUNCHED(ctx, "k_q4_gemm_tc");
+  PB_TRY(pb_launch(ctx, "k_q4_gemm_tc", true, kern, grid, dim3(GM_THREADS), gm_smem(epi.terms), (const uint8_t*)w->qs,
+                   (const uint16_t*)w->d, w->layout, w->N, w->N_pad, w->nb, X, ldx, M, dst, ldd, kper, kepi,
+                   ctx->d_err));
   if (splits > 1) {
     const int cols = epi.mode == PB_GEMM_SWIGLU ? w->N / 2 : w->N;
-    k_splitk_reduce<<<dim3(pb_cdiv(cols, 256), M), 256, 0, ctx->stream>>>(ws, splits, M, w->N, C, ldc, epi);
-    PB_LAUNCHED(ctx, "k_splitk_reduce");
+    PB_TRY(pb_launch(ctx, "k_splitk_reduce", true, k_splitk_reduce, dim3(pb_cdiv(cols, 256), M), dim3(256), 0,
+                     (const float*)ws, splits, M, w->N, C, ldc, epi));
   }
   return PB_OK;
 }
@@ -811,6 +819,11 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
   const int kbeg = blockIdx.z * kper, kend = kbeg + kper < ktot ? kbeg + kper : ktot;
   const int ksteps = kend > kbeg ? kend - kbeg : 0;
   C += (size_t)blockIdx.z * M * ldc;
+  // programmatic dependent launch: the next kernel may start its own weight
+  // loads now; this grid reads activations and writes C only after the
+  // dependency wait (the producer before its activation loads, the other
+  // threads below)
+  pb_pdl_trigger();
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
@@ -837,13 +850,10 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
 
   if (warp == 0) {
     if (lane == 0) {  // producer
-      bool ok = true;
-      for (int g = 0; g < ksteps && ok; ++g) {
-        const int st = g % GW_STAGES;
-        if (g >= GW_STAGES && !(ok = pb_mbar_wait_sleep(&empty[st], ((g / GW_STAGES) - 1) & 1, err))) break;
+      // the Q4_0 payload of step g into stage g % GW_STAGES (weights: final before this grid)
+      auto payload = [&](int g) {
+        const int st = g % GW_STAGES, ks = kbeg + g;
         unsigned char* sX = ring + GW_ABUF * AB + st * SB;
-        pb_mbar_arrive_tx(&full[st], SB);
-        const int ks = kbeg + g;
         if (layout == PB_LAYOUT_TILED8)
           asm volatile(
               "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
@@ -852,9 +862,30 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
               : "memory");
         else
           tma_load_2d(sX + XB, &map_q, 32 * ks, n0, &full[st]);
+      };
+      // the activations of step g (written by the previous kernels)
+      auto acts = [&](int g) {
+        const int st = g % GW_STAGES, ks = kbeg + g;
+        unsigned char* sX = ring + GW_ABUF * AB + st * SB;
         const int xk = (ks * GW_K) % xkc, xz = (ks * GW_K) / xkc;
         tma_load_3d(sX, &map_x, TW * xk, m0, xz, &full[st]);
         if (TERMS == 3) tma_load_3d(sX + GW_X_BYTES, &map_x, 2 * xk + 64, m0, xz, &full[st]);
+      };
+      // the first ring's payloads go out before the dependency wait, their activations after it
+      const int first = ksteps < GW_STAGES ? ksteps : GW_STAGES;
+      for (int g = 0; g < first; ++g) {
+        pb_mbar_arrive_tx(&full[g], SB);
+        payload(g);
+      }
+      pb_pdl_wait();
+      for (int g = 0; g < first; ++g) acts(g);
+      bool ok = true;
+      for (int g = first; g < ksteps && ok; ++g) {
+        const int st = g % GW_STAGES;
+        if (!(ok = pb_mbar_wait_sleep(&empty[st], ((g / GW_STAGES) - 1) & 1, err))) break;
+        pb_mbar_arrive_tx(&full[st], SB);
+        payload(g);
+        acts(g);
       }
     }
   } else if (warp == 1) {
@@ -913,6 +944,7 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
     };
     uint32_t dnext[2];
     scales(kbeg, dnext);
+    pb_pdl_wait();  // before the epilogue reads or writes C
     for (int g = 0; g < ksteps && ok; ++g) {
       const int st = g % GW_STAGES, ks = kbeg + g;
       const uint32_t d2[2] = {dnext[0] | (dnext[0] << 16), dnext[1] | (dnext[1] << 16)};
@@ -1039,13 +1071,13 @@ static int launch_gemm_ws(pb_ctx* ctx, const pb_qmat* w, const __half* Xh, int M
   PB_TRY(make_map_q(ctx, &mq, w));
   PB_TRY(make_map_x(ctx, &mx, Xh, M, w->K * tw, xkc * tw, GW_TOK));
   auto kern = epi.terms == 3 ? k_q4_gemm_ws<3> : k_q4_gemm_ws<1>;
-  kern<<<grid, GW_THREADS, gw_smem(epi.terms), ctx->stream>>>(mq, mx, w->qs, w->d, w->layout, w->N, w->N_pad, w->nb, M,
-                                                              xkc, dst, ldd, kper, kepi, ctx->d_err);
-  PB_LAUNCHED(ctx, "k_q4_gemm_ws");
+  PB_TRY(pb_launch(ctx, "k_q4_gemm_ws", true, kern, grid, dim3(GW_THREADS), gw_smem(epi.terms), mq, mx,
+                   (const uint8_t*)w->qs, (const uint16_t*)w->d, w->layout, w->N, w->N_pad, w->nb, M, xkc, dst, ldd,
+                   kper, kepi, ctx->d_err));
   if (splits > 1) {
     const int cols = epi.mode == PB_GEMM_SWIGLU ? w->N / 2 : w->N;
-    k_splitk_reduce<<<dim3(pb_cdiv(cols, 256), M), 256, 0, ctx->stream>>>(ws, splits, M, w->N, C, ldc, epi);
-    PB_LAUNCHED(ctx, "k_splitk_reduce");
+    PB_TRY(pb_launch(ctx, "k_splitk_reduce", true, k_splitk_reduce, dim3(pb_cdiv(cols, 256), M), dim3(256), 0,
+                     (const float*)ws, splits, M, w->N, C, ldc, epi));
   }
   return PB_OK;
 }

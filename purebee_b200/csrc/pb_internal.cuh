@@ -399,8 +399,10 @@ __device__ __forceinline__ void pb_store_hl(__half* p, size_t i, float v) {
   p[i] = hi;
   p[i + 64] = __float2half_rn(__fsub_rn(v, __half2float(hi)));
 }
+// pdl: launched as a programmatic dependent of the previous kernel (the
+// kernel waits for it before reading x)
 void pb_launch_rmsnorm(cudaStream_t st, const float* x, int rows, int dim, const float* w, double eps, float* out,
-                       __half* out16, int xc, int hl = 0);
+                       __half* out16, int xc, int hl = 0, bool pdl = false);
 int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
                       size_t ws_bytes, const pb_gemm_epi* epi = nullptr, const __half* Xh = nullptr);
 bool pb_gemm_uses_tma(const pb_qmat* w, int M);  // the f16-operand TMA path (takes Xh)

@@ -577,7 +577,7 @@ extern "C" int pb_model_get_tensor(pb_model* m, int layer, int which, void* host
 
 static int launch_norm(pb_model* m, const float* x, int M, const float* w, float* out, __half* out16 = nullptr,
                        int xc = 0, int hl = 0) {
-  pb_launch_rmsnorm(m->ctx->stream, x, M, m->c.dim, w, m->c.eps, out, out16, xc, hl);
+  pb_launch_rmsnorm(m->ctx->stream, x, M, m->c.dim, w, m->c.eps, out, out16, xc, hl, m->ctx->pdl);
   PB_LAUNCHED(m->ctx, "k_rmsnorm");
   return PB_OK;
 }
@@ -1512,6 +1512,8 @@ __global__ void k_batch_embed(int type, const uint8_t* __restrict__ qs, const ui
 constexpr int AMX_CHUNK = 8192;
 __global__ void __launch_bounds__(256)
 k_argmax_chunks(const float* __restrict__ logits, int n, int ld, int v0, unsigned long long* __restrict__ keys) {
+  pb_pdl_trigger();
+  pb_pdl_wait();  // the logits come from the head
   __shared__ unsigned long long red[8];
   const int r = blockIdx.y, c0 = blockIdx.x * AMX_CHUNK, c1 = min(n, c0 + AMX_CHUNK);
   unsigned long long key = 0ull;
@@ -1538,6 +1540,8 @@ k_argmax_chunks(const float* __restrict__ logits, int n, int ld, int v0, unsigne
 __global__ void k_argmax_merge(unsigned long long* __restrict__ keys, int world, int B, int* __restrict__ next,
                                int* __restrict__ hist, const int* __restrict__ pos_dev, int hist_len,
                                unsigned long long* __restrict__ reset) {
+  pb_pdl_trigger();
+  pb_pdl_wait();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= B) return;
   unsigned long long best = 0ull;
@@ -1553,6 +1557,7 @@ __global__ void k_argmax_merge(unsigned long long* __restrict__ keys, int world,
 }
 
 __global__ void k_batch_step_end(int* __restrict__ pos_dev) {
+  pb_pdl_wait();
   if (threadIdx.x == 0 && blockIdx.x == 0) *pos_dev += 1;
 }
 
@@ -1745,10 +1750,11 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
   }
   {
     const int tot = (p.n_heads + p.n_kv_heads) * (hd / 2) + kvl;
-    k_rope_kv<<<dim3(pb_cdiv(tot, 128), rows), 128, 0, ctx->stream>>>(
-        s.qkvo, qw, s.qkvo + p.n_heads * hd, qw, s.qkvo + (p.n_heads + p.n_kv_heads) * hd, qw, p.n_heads,
-        p.n_kv_heads, hd, m->rope_tab, start_pos, pos_dev, kc, vc, c.seq_len, rows_per_seq, cache_seq, ctx->d_err);
-    PB_LAUNCHED(ctx, "k_rope_kv");
+    PB_TRY(pb_launch(ctx, "k_rope_kv", true, k_rope_kv, dim3(pb_cdiv(tot, 128), rows), dim3(128), 0, s.qkvo, qw,
+                     (const float*)(s.qkvo + p.n_heads * hd), qw,
+                     (const float*)(s.qkvo + (p.n_heads + p.n_kv_heads) * hd), qw, p.n_heads, p.n_kv_heads, hd,
+                     (const double2*)m->rope_tab, start_pos, pos_dev, kc, vc, c.seq_len, rows_per_seq, cache_seq,
+                     ctx->d_err));
   }
   float* att = s.att + (size_t)s.rank * rows * dc;
   pb_seq_geo geo;
@@ -1868,9 +1874,9 @@ static int batch_head(pb_batch* b, bool from_x, const int* pos_dev) {
     if (h16) PB_TRY(pb_launch_q4_gemm(ctx, s.head, nullptr, c.dim, b->B, lg, vc, nullptr, 0, &he, xn16));
     else PB_TRY(pb_launch_q4_gemm(ctx, s.head, s.xn, c.dim, b->B, lg, vc, nullptr, 0, &he));
     // this rank's keys (zero: cleared by the previous merge or at creation)
-    k_argmax_chunks<<<dim3(pb_cdiv(s.p.vocab_rows, AMX_CHUNK), b->B), 256, 0, ctx->stream>>>(
-        lg, s.p.vocab_rows, vc, s.p.vocab_row0, s.keys + (size_t)s.rank * b->B);
-    PB_LAUNCHED(ctx, "k_argmax_chunks");
+    PB_TRY(pb_launch(ctx, "k_argmax_chunks", true, k_argmax_chunks, dim3(pb_cdiv(s.p.vocab_rows, AMX_CHUNK), b->B),
+                     dim3(256), 0, (const float*)lg, s.p.vocab_rows, vc, s.p.vocab_row0,
+                     s.keys + (size_t)s.rank * b->B));
   }
   PB_TRY(batch_gather(b, XG_KEYS, (size_t)b->B * 8));
   for (auto& s : b->sh) {  // every shard reads the gathered keys and clears its own for the next step

@@ -33,6 +33,8 @@ template <bool CH>
 __global__ void k_rmsnorm_t(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
                             float* __restrict__ out, __half* __restrict__ out16, int xc, int hl) {
   __shared__ double red[32];
+  pb_pdl_trigger();
+  pb_pdl_wait();  // x comes from the previous kernel
   const size_t row = blockIdx.x;
   const float* xr = x + row * (CH ? xc : dim);
   const size_t cs = (size_t)gridDim.x * xc;
@@ -59,9 +61,18 @@ __global__ void k_rmsnorm_t(const float* __restrict__ x, int dim, const float* _
 }
 
 void pb_launch_rmsnorm(cudaStream_t st, const float* x, int rows, int dim, const float* w, double eps, float* out,
-                       __half* out16, int xc, int hl) {
-  if (xc > 0 && xc < dim) k_rmsnorm_t<true><<<rows, 256, 0, st>>>(x, dim, w, eps, out, out16, xc, hl);
-  else k_rmsnorm_t<false><<<rows, 256, 0, st>>>(x, dim, w, eps, out, out16, 0, hl);
+                       __half* out16, int xc, int hl, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (xc > 0 && xc < dim) cudaLaunchKernelEx(&cfg, k_rmsnorm_t<true>, x, dim, w, eps, out, out16, xc, hl);
+  else cudaLaunchKernelEx(&cfg, k_rmsnorm_t<false>, x, dim, w, eps, out, out16, 0, hl);
 }
 
 extern "C" int pb_rmsnorm(pb_ctx* ctx, const float* x, int seq, int dim, const float* w, double eps, float* out) {
@@ -809,6 +820,8 @@ __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __re
                           float* __restrict__ kc, float* __restrict__ vc, int max_len, int rows_per_seq,
                           int64_t cache_seq_stride, int* err) {
   int t = blockIdx.y;  // row; rows of sequence s are s*rows_per_seq .. +rows_per_seq-1
+  pb_pdl_trigger();
+  pb_pdl_wait();  // q, k, v come from the projection
   const int sq = t / rows_per_seq;
   kc += sq * cache_seq_stride;
   vc += sq * cache_seq_stride;
@@ -1100,6 +1113,7 @@ k_attn_dec1(const float* __restrict__ q, const float* __restrict__ kc, const flo
   const int cache_len = pos + 1;
   if (pos < 0 || cache_len > max_len) {
     pb_pdl_trigger();
+    pb_pdl_wait();  // a dependent grid ends after the one before it, on every path
     if (tid == 0 && g == 0 && sp == 0) pb_raise(err, PB_DEVERR_BOUNDS);
     return;
   }
@@ -1867,6 +1881,7 @@ k_attn_dec_fast(const float* __restrict__ q, const float* __restrict__ kc, const
   const int P = (cache_len + nsplit - 1) / nsplit;
   if (pos < 0 || cache_len > max_len || P > pmax) {  // the same for every CTA: all leave before any barrier
     pb_pdl_trigger();
+    pb_pdl_wait();  // a dependent grid ends after the one before it, on every path
     if (tid == 0 && g == 0 && sp == 0) pb_raise(err, PB_DEVERR_BOUNDS);
     return;
   }
