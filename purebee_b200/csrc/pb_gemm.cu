@@ -126,9 +126,17 @@ __device__ __forceinline__ void gemm_emit32(const uint32_t (&v)[32], bool zero, 
         else if (epi.h16) epi.h16[(size_t)m * (N / 2) + f] = __float2half_rn(h);
         else epi.h32[(size_t)m * (N / 2) + f] = h;
       }
-    } else if (row < N && m < M) {
-      float* c = C + (size_t)m * ldc + row;
-      *c = epi.mode == PB_GEMM_ADD ? __fadd_rn(*c, r) : r;
+    } else {
+      float v = r;
+      if (row < N && m < M) {
+        float* c = C + (size_t)m * ldc + row;
+        v = epi.mode == PB_GEMM_ADD ? __fadd_rn(*c, r) : r;
+        *c = v;
+      }
+      if (epi.xs.world > 0) {  // the fused residual exchange: lanes (row, row ^ 1) form a packet
+        const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
+        if (row < N && m < M && (row & 1) == 0) pb_xsend_pair(epi.xs, m, row, v, partner);
+      }
     }
   }
 }
@@ -637,11 +645,18 @@ __global__ void k_splitk_reduce(const float* __restrict__ ws, int splits, int M,
     else epi.h32[(size_t)m * (N / 2) + i] = h;
     return;
   }
-  if (i >= N) return;
-  float acc = 0.0f;
-  for (int z = 0; z < splits; ++z) acc += ws[((size_t)z * M + m) * N + i];
-  float* c = C + (size_t)m * ldc + i;
-  *c = epi.mode == PB_GEMM_ADD ? __fadd_rn(*c, acc) : acc;
+  float v = 0.0f;
+  if (i < N) {
+    float acc = 0.0f;
+    for (int z = 0; z < splits; ++z) acc += ws[((size_t)z * M + m) * N + i];
+    float* c = C + (size_t)m * ldc + i;
+    v = epi.mode == PB_GEMM_ADD ? __fadd_rn(*c, acc) : acc;
+    *c = v;
+  }
+  if (epi.xs.world > 0) {  // the fused residual exchange: threads (i, i ^ 1) form a packet
+    const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
+    if (i < N && (i & 1) == 0) pb_xsend_pair(epi.xs, m, i, v, partner);
+  }
 }
 
 bool pb_gemm_uses_tma(const pb_qmat* w, int M) { return M >= PB_GEMM_TMA_MIN_M && w->K % TG_K == 0; }
@@ -694,6 +709,7 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
     kepi.mode = PB_GEMM_STORE;
     kepi.h16 = nullptr;
     kepi.h32 = nullptr;
+    kepi.xs.world = 0;  // the reduce sends the finished values
   }
   auto kern = epi.terms == 3
                   ? (tok == 64 ? (epi.x_chunk ? k_q4_gemm_tc<64, true, 3> : k_q4_gemm_tc<64, false, 3>)
@@ -1065,6 +1081,7 @@ static int launch_gemm_ws(pb_ctx* ctx, const pb_qmat* w, const __half* Xh, int M
     kepi.mode = PB_GEMM_STORE;
     kepi.h16 = nullptr;
     kepi.h32 = nullptr;
+    kepi.xs.world = 0;  // the reduce sends the finished values
   }
   const int xkc = epi.x_chunk ? epi.x_chunk : w->K, tw = epi.terms == 3 ? 2 : 1;
   CUtensorMap mq, mx;

@@ -160,6 +160,12 @@ __device__ __forceinline__ void pb_pdl_trigger() { asm volatile("griddepcontrol.
 __device__ __forceinline__ void pb_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // Record the first device-side error; the host reads it with pb_device_error.
+__device__ __forceinline__ unsigned long long pb_globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
 __device__ __forceinline__ void pb_raise(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
@@ -374,6 +380,33 @@ struct pb_seq_geo {
 //   split_n > 0: the split-K count is chosen as for a matrix of split_n rows,
 //     so a row slice of a matrix sums its K partials in the same order as the
 //     whole matrix (and gives the same bits).
+// The row split's residual exchange folded into the GEMM that adds into this
+// rank's chunk of x (decode steps over peer memory): besides storing the new
+// value, the epilogue stores it, two values per 16-byte packet with the
+// exchange's epoch twice ({v0, e, v1, e}, the low-latency exchange's format),
+// into every peer's slots; the next RMSNorm reads the peers' chunks from its
+// own slots (k_rmsnorm_xrecv).  world == 0: off.
+struct pb_xsend {
+  uint4* slots[8];              // every rank's slot array (PB_MAX_RANKS)
+  size_t cap_units = 0;         // packets per (half, sender)
+  const unsigned int* epoch = nullptr;  // exchange counter: this exchange is *epoch + 1
+  int rank = 0, world = 0;
+  int width = 0;                // chunk width: (token m, column c) is unit (m * width + c) / 2
+};
+
+// One packet of the fused exchange: columns (c, c + 1) of token m, c even.
+__device__ __forceinline__ void pb_xsend_pair(const pb_xsend& xs, int m, int c, float v0, float v1) {
+  const unsigned int e = *xs.epoch + 1u;
+  const size_t half = e & 1u, u = ((size_t)m * xs.width + c) >> 1;
+  for (int q = 0; q < xs.world; ++q) {
+    if (q == xs.rank) continue;
+    uint4* dst = xs.slots[q] + (half * xs.world + xs.rank) * xs.cap_units + u;
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(__float_as_uint(v0)), "r"(e),
+                 "r"(__float_as_uint(v1)), "r"(e)
+                 : "memory");
+  }
+}
+
 struct pb_gemm_epi {
   int mode = PB_GEMM_STORE;
   __half* h16 = nullptr;
@@ -384,6 +417,7 @@ struct pb_gemm_epi {
   // the three products hi*hi + hi*lo + lo*hi summed (f16 operands then come,
   // and h16 goes out, in the hi/lo layout below)
   int terms = 1;
+  pb_xsend xs;  // PB_GEMM_ADD: the fused residual exchange (row split, decode steps)
 };
 
 // The hi/lo f16 layout of the three-term GEMM operands: a value v is the
@@ -414,6 +448,7 @@ int pb_comm_gather_inplace(pb_comm* c, void* base, size_t chunk_bytes);
 pb_ctx* pb_comm_ctx(const pb_comm* c);
 // Peer memory of the ranks (CUDA IPC): tables of every rank's copy of a buffer
 #define PB_MAX_RANKS 8
+static_assert(sizeof(pb_xsend::slots) / sizeof(uint4*) == PB_MAX_RANKS, "pb_xsend holds one slot array per rank");
 struct pb_peer_bufs {
   char* p[PB_MAX_RANKS];
 };
@@ -433,6 +468,20 @@ struct pb_ll_slots {
 };
 int pb_comm_ll_gather(pb_comm* c, const pb_ll_slots& slots, size_t cap_units, char* buf, size_t chunk_bytes,
                       unsigned int* epoch, unsigned int* done);
+
+// The receiving end of the fused residual exchange (pb_xsend): this rank's
+// slot array and the exchange's counters.
+struct pb_xrecv {
+  const uint4* mine = nullptr;
+  size_t cap_units = 0;
+  unsigned int* epoch = nullptr;
+  unsigned int* done = nullptr;
+  int rank = 0, world = 0;
+  unsigned long long limit_ns = 0;  // set by the launcher from the context timeout
+  int* err = nullptr;
+};
+int pb_launch_rmsnorm_xrecv(pb_ctx* ctx, float* x, int rows, int dim, const float* w, double eps, float* out,
+                            __half* out16, int xc, int hl, const pb_xrecv& xr);
 
 int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows,
                      const pb_mv_epi* epi);

@@ -1714,6 +1714,37 @@ static int batch_gather(pb_batch* b, int id, size_t chunk_bytes) {
 // The x_chunk of an operand stored in `width`-wide chunks (0 when unsplit).
 static int chunk_of(const pb_batch* b, int width) { return b->world > 1 ? width : 0; }
 
+// Whether this step's residual exchanges are fused into their producers and
+// consumers: decode steps of a row split whose ranks exchange over peer
+// memory, the residual chunk within the low-latency slots.  The GEMM that adds
+// into this rank's chunk of x sends it (pb_xsend), the next RMSNorm receives
+// the peers' chunks (k_rmsnorm_xrecv): no exchange kernel in between.
+static bool fused_x(const pb_batch* b, int rows) {
+  const size_t chunk = (size_t)rows * (b->m->c.dim / b->world) * 4;
+  return b->decoding && b->comm && b->p2p_ll && b->world > 1 && chunk % 8 == 0 && chunk / 8 <= b->ll_cap &&
+         (b->m->c.dim / b->world) % 2 == 0 && (size_t)b->m->c.dim * 4 <= 48 * 1024;
+}
+static pb_xsend xsend_of(pb_batch* b, int width) {
+  pb_xsend xs;
+  for (int q = 0; q < PB_MAX_RANKS; ++q) xs.slots[q] = q < b->world ? b->ll.s[q] : nullptr;
+  xs.cap_units = b->ll_cap;
+  xs.epoch = ll_counters(b);
+  xs.rank = b->sh[0].rank;
+  xs.world = b->world;
+  xs.width = width;
+  return xs;
+}
+static pb_xrecv xrecv_of(pb_batch* b) {
+  pb_xrecv xr;
+  xr.mine = b->ll.s[b->sh[0].rank];
+  xr.cap_units = b->ll_cap;
+  xr.epoch = ll_counters(b);
+  xr.done = xr.epoch + 1;
+  xr.rank = b->sh[0].rank;
+  xr.world = b->world;
+  return xr;
+}
+
 // Decode-size steps (<= 64 token rows, head_dim 64): every GEMM takes f16
 // activations (the warp-specialised decode GEMM), which the norms, the split
 // attention and the SwiGLU epilogue write directly.
@@ -1726,7 +1757,7 @@ static bool dec16(const pb_batch* b, const pb_shard& s, int l, int rows) {
 // norm -> this rank's q | k | v -> RoPE + KV append -> attention of its heads
 // into its chunk of att.
 static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_per_seq, int start_pos,
-                           const int* pos_dev) {
+                           const int* pos_dev, bool recv_x = false) {
   pb_model* m = b->m;
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
@@ -1741,7 +1772,13 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
   // the norm writes the GEMM's f16 operand directly on the TMA and decode paths
   __half* xn16 = reinterpret_cast<__half*>(s.xn);
   const bool d16 = dec16(b, s, l, rows);
-  if (pb_gemm_uses_tma(s.qkv[l], rows) || d16) {
+  if (recv_x) {  // x's other chunks arrive with the norm (fused exchange)
+    const bool f16 = pb_gemm_uses_tma(s.qkv[l], rows) || d16;
+    PB_TRY(pb_launch_rmsnorm_xrecv(ctx, s.x, rows, dim, m->rms_att + (size_t)l * dim, c.eps, f16 ? nullptr : s.xn,
+                                   f16 ? xn16 : nullptr, dc, f16 && b->terms == 3, xrecv_of(b)));
+    if (f16) PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], nullptr, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st, xn16));
+    else PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], s.xn, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st));
+  } else if (pb_gemm_uses_tma(s.qkv[l], rows) || d16) {
     PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, nullptr, xn16, dc, b->terms == 3));
     PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], nullptr, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st, xn16));
   } else {
@@ -1777,7 +1814,7 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
 
 // this rank's rows of wo with the residual add into its chunk of x
 // (llama-streaming.js:579-580)
-static int shard_wo(pb_batch* b, pb_shard& s, int l, int rows) {
+static int shard_wo(pb_batch* b, pb_shard& s, int l, int rows, bool send_x = false) {
   pb_model* m = b->m;
   const int dc = s.p.dim_chunk;
   pb_gemm_epi add;
@@ -1785,6 +1822,7 @@ static int shard_wo(pb_batch* b, pb_shard& s, int l, int rows) {
   add.x_chunk = chunk_of(b, dc);
   add.split_n = m->c.dim;
   add.terms = b->terms;
+  if (send_x) add.xs = xsend_of(b, dc);
   if (dec16(b, s, l, rows))
     return pb_launch_q4_gemm(m->ctx, s.wo[l], nullptr, m->c.dim, rows, s.x + (size_t)s.rank * rows * dc, dc, b->ws,
                              b->ws_bytes, &add, reinterpret_cast<const __half*>(s.att));
@@ -1798,14 +1836,18 @@ static bool hidden_f16(const pb_batch* b, const pb_shard& s, int l, int rows) {
 
 // norm -> this rank's gate|up rows with SwiGLU in the epilogue, h into its
 // chunk of hb (f16 for the TMA path of w2, f32 otherwise)
-static int shard_gate_up(pb_batch* b, pb_shard& s, int l, int rows) {
+static int shard_gate_up(pb_batch* b, pb_shard& s, int l, int rows, bool recv_x = false) {
   pb_model* m = b->m;
   pb_ctx* ctx = m->ctx;
   const int dim = m->c.dim, fc = s.p.hidden_chunk;
   const bool gu16 = pb_gemm_uses_tma(s.gu[l], rows) || dec16(b, s, l, rows);
   __half* xn16 = reinterpret_cast<__half*>(s.xn);
-  PB_TRY(launch_norm(m, s.x, rows, m->rms_ffn + (size_t)l * dim, gu16 ? nullptr : s.xn, gu16 ? xn16 : nullptr,
-                     s.p.dim_chunk, b->terms == 3));
+  if (recv_x)  // x's other chunks arrive with the norm (fused exchange)
+    PB_TRY(pb_launch_rmsnorm_xrecv(ctx, s.x, rows, dim, m->rms_ffn + (size_t)l * dim, m->c.eps, gu16 ? nullptr : s.xn,
+                                   gu16 ? xn16 : nullptr, s.p.dim_chunk, gu16 && b->terms == 3, xrecv_of(b)));
+  else
+    PB_TRY(launch_norm(m, s.x, rows, m->rms_ffn + (size_t)l * dim, gu16 ? nullptr : s.xn, gu16 ? xn16 : nullptr,
+                       s.p.dim_chunk, b->terms == 3));
   pb_gemm_epi glu;
   glu.mode = PB_GEMM_SWIGLU;
   glu.split_n = 2 * m->c.hidden_dim;
@@ -1818,7 +1860,7 @@ static int shard_gate_up(pb_batch* b, pb_shard& s, int l, int rows) {
 }
 
 // this rank's rows of w2 with the residual add into its chunk of x (:601)
-static int shard_down(pb_batch* b, pb_shard& s, int l, int rows) {
+static int shard_down(pb_batch* b, pb_shard& s, int l, int rows, bool send_x = false) {
   pb_model* m = b->m;
   const int F = m->c.hidden_dim, dc = s.p.dim_chunk;
   pb_gemm_epi add;
@@ -1826,6 +1868,7 @@ static int shard_down(pb_batch* b, pb_shard& s, int l, int rows) {
   add.x_chunk = chunk_of(b, s.p.hidden_chunk);
   add.split_n = m->c.dim;
   add.terms = b->terms;
+  if (send_x) add.xs = xsend_of(b, dc);
   float* C = s.x + (size_t)s.rank * rows * dc;
   if (hidden_f16(b, s, l, rows))
     return pb_launch_q4_gemm(m->ctx, s.w2[l], nullptr, F, rows, C, dc, b->ws, b->ws_bytes, &add,
@@ -1842,16 +1885,18 @@ static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start
   const size_t dchunk = (size_t)rows * (c.dim / b->world) * 4;
   // f16 attention output (hi/lo pairs take the bytes of f32)
   const size_t achunk = dec16(b, b->sh[0], l, rows) ? dchunk / 2 * op_halves(b) : dchunk;
-  for (auto& s : b->sh) PB_TRY(shard_attention(b, s, l, rows, rows_per_seq, start_pos, pos_dev));
+  // fused residual exchanges: the wo / down GEMMs send, the next norm receives
+  const bool fx = fused_x(b, rows);
+  for (auto& s : b->sh) PB_TRY(shard_attention(b, s, l, rows, rows_per_seq, start_pos, pos_dev, fx && l > 0));
   PB_TRY(batch_gather(b, XG_ATT, achunk));
-  for (auto& s : b->sh) PB_TRY(shard_wo(b, s, l, rows));
-  PB_TRY(batch_gather(b, XG_X, dchunk));
-  for (auto& s : b->sh) PB_TRY(shard_gate_up(b, s, l, rows));
+  for (auto& s : b->sh) PB_TRY(shard_wo(b, s, l, rows, fx));
+  if (!fx) PB_TRY(batch_gather(b, XG_X, dchunk));
+  for (auto& s : b->sh) PB_TRY(shard_gate_up(b, s, l, rows, fx));
   const size_t hchunk =
       (size_t)rows * (c.hidden_dim / b->world) * (hidden_f16(b, b->sh[0], l, rows) ? 2 * op_halves(b) : 4);
   PB_TRY(batch_gather(b, XG_HB, hchunk));
-  for (auto& s : b->sh) PB_TRY(shard_down(b, s, l, rows));
-  return batch_gather(b, XG_X, dchunk);
+  for (auto& s : b->sh) PB_TRY(shard_down(b, s, l, rows, fx));
+  return fx ? PB_OK : batch_gather(b, XG_X, dchunk);
 }
 
 // Final RMSNorm of each sequence's last row (xl, or x itself when every row
@@ -1865,7 +1910,10 @@ static int batch_head(pb_batch* b, bool from_x, const int* pos_dev) {
     const bool h16 = pb_gemm_uses_ws(s.head, b->B);
     __half* xn16 = h16 ? reinterpret_cast<__half*>(s.xn) : nullptr;
     const int hl = b->terms == 3;
-    if (from_x) PB_TRY(launch_norm(m, s.x, b->B, m->rms_final, h16 ? nullptr : s.xn, xn16, s.p.dim_chunk, hl));
+    if (from_x && fused_x(b, b->B))  // the last layer's down GEMM sent its residual chunk
+      PB_TRY(pb_launch_rmsnorm_xrecv(ctx, s.x, b->B, c.dim, m->rms_final, c.eps, h16 ? nullptr : s.xn, xn16,
+                                     s.p.dim_chunk, h16 && hl, xrecv_of(b)));
+    else if (from_x) PB_TRY(launch_norm(m, s.x, b->B, m->rms_final, h16 ? nullptr : s.xn, xn16, s.p.dim_chunk, hl));
     else PB_TRY(launch_norm(m, s.xl, b->B, m->rms_final, h16 ? nullptr : s.xn, xn16, 0, hl));
     const int vc = s.p.vocab_chunk;
     float* lg = s.logits + (size_t)s.rank * b->B * vc;

@@ -60,6 +60,88 @@ __global__ void k_rmsnorm_t(const float* __restrict__ x, int dim, const float* _
     out[row * dim + d] = (float)__dmul_rn(__ddiv_rn((double)X(d), rms), (double)w[d]);
 }
 
+// The RMSNorm that ends the row split's fused residual exchange (decode
+// steps): row `row` of x is stored in column chunks of width xc (chunk c at
+// x + c * rows * xc); this rank's chunk is local, every peer's arrives in
+// this rank's slots as {v0, e, v1, e} packets from the peer's add epilogue
+// (pb_xsend_pair).  The row goes to shared memory first -- the peers' values
+// also into the local chunks -- then the arithmetic is k_rmsnorm_t's, so the
+// output has the same bits as the unfused exchange followed by the norm.
+// The last CTA advances the exchange counter.  Every poll is bounded by the
+// context timeout (PB_DEVERR_WAIT).
+__global__ void k_rmsnorm_xrecv(float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
+                                float* __restrict__ out, __half* __restrict__ out16, int xc, int hl, pb_xrecv xr) {
+  extern __shared__ float xrow[];
+  __shared__ double red[32];
+  pb_pdl_trigger();
+  pb_pdl_wait();  // this rank's chunk (and the exchange counter) come from the kernels before
+  const int row = blockIdx.x, rows = gridDim.x;
+  const unsigned int e = *xr.epoch + 1u;
+  const size_t half = e & 1u;
+  const unsigned long long t0 = pb_globaltimer_ns();
+  bool ok = true;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    const int c = d / xc, k = d - c * xc;
+    float* xl = x + (size_t)c * rows * xc + (size_t)row * xc + k;
+    if (c == xr.rank) {
+      xrow[d] = *xl;
+      continue;
+    }
+    const uint4* src = xr.mine + (half * xr.world + c) * xr.cap_units + (((size_t)row * xc + k) >> 1);
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    for (uint32_t it = 0; ok; ++it) {
+      asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                   : "l"(src)
+                   : "memory");
+      if (v.y == e && v.w == e) break;
+      if ((it & 63) == 63 && pb_globaltimer_ns() - t0 > xr.limit_ns) {
+        pb_raise(xr.err, PB_DEVERR_WAIT);
+        ok = false;
+      }
+    }
+    const float val = __uint_as_float((k & 1) ? v.z : v.x);
+    xrow[d] = val;
+    *xl = val;  // the local copy of the peer's chunk
+  }
+  __syncthreads();
+  double ss = 0.0;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    const double v = (double)xrow[d];
+    ss = __fma_rn(v, v, ss);
+  }
+  ss = pb_block_sum_d(ss, red);
+  double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)dim), eps));
+  if (out16) {
+    const float inv = (float)(1.0 / rms);
+    if (hl) {
+      for (int d = threadIdx.x; d < dim; d += blockDim.x)
+        pb_store_hl(out16, pb_hl_index((size_t)row * 2 * dim, d), xrow[d] * inv * w[d]);
+    } else {
+      for (int d = threadIdx.x; d < dim; d += blockDim.x) out16[(size_t)row * dim + d] = __float2half_rn(xrow[d] * inv * w[d]);
+    }
+  } else {
+    for (int d = threadIdx.x; d < dim; d += blockDim.x)
+      out[(size_t)row * dim + d] = (float)__dmul_rn(__ddiv_rn((double)xrow[d], rms), (double)w[d]);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(xr.done, 1u) == (unsigned)rows - 1) {
+    *xr.done = 0u;
+    *xr.epoch = e;
+  }
+}
+
+int pb_launch_rmsnorm_xrecv(pb_ctx* ctx, float* x, int rows, int dim, const float* w, double eps, float* out,
+                            __half* out16, int xc, int hl, const pb_xrecv& xr) {
+  if (xc <= 0 || dim % xc || xc % 2 || (size_t)dim * 4 > 48 * 1024)
+    return pb_set_error(ctx, PB_ERR_ARG, "fused residual exchange: chunks of %d over dim %d", xc, dim);
+  pb_xrecv r = xr;
+  r.limit_ns = (unsigned long long)ctx->timeout_ms * 1000000ull;
+  r.err = ctx->d_err;
+  return pb_launch(ctx, "k_rmsnorm_xrecv", true, k_rmsnorm_xrecv, dim3(rows), dim3(256), (size_t)dim * 4, x, dim, w,
+                   eps, out, out16, xc, hl, r);
+}
+
 void pb_launch_rmsnorm(cudaStream_t st, const float* x, int rows, int dim, const float* w, double eps, float* out,
                        __half* out16, int xc, int hl, bool pdl) {
   cudaLaunchConfig_t cfg = {};
