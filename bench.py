@@ -353,8 +353,10 @@ def run_batched(ctx, torch, stream, rt, peak, flop_peak, n_seqs=64, n_prompt=512
     gathered = c["n_layers"] * (3 * hd_bytes + n_seqs * F * 4) + n_seqs * 8  # per step, whole buffers
     return {"workload": f"configs[4]: {n_seqs} seqs x {n_prompt}-token seeded prompts, then {steps} greedy steps",
             "n_gpus": world, "scaling": "strong",
-            "parallelism": (f"rowsplit{world}: {4 * c['n_layers'] + 1} all-gathers per decode step over "
-                            + ("NVLink peer memory (low-latency exchange)" if comm_p2p else "NCCL"))
+            "parallelism": (f"rowsplit{world}: " + (
+                f"{2 * c['n_layers'] + 1} exchange kernels per decode step over NVLink peer memory (low-latency "
+                f"exchange) and {2 * c['n_layers']} residual exchanges fused into the add epilogues and the next "
+                f"norms" if comm_p2p else f"{4 * c['n_layers'] + 1} NCCL all-gathers per decode step"))
             if world > 1 else "single-gpu",
             "prefill_ms": round(prefill_ms, 2), "prefill_tok_s": round(tokens / (prefill_ms / 1e3), 1),
             "prefill_linear_TFLOPs": round(lin_flops / (prefill_ms / 1e3) / 1e12, 1),
