@@ -158,32 +158,35 @@ __device__ __forceinline__ void mvi_stage(const float* __restrict__ x, const flo
     for (int u = 0; u < 4; ++u) {
       const int b = b0 + W * u;
       if (b >= nbp) break;
-      float m = fabsf(xv[u]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      int e = 0;
-      if (m > 0.0f && m <= 3.402823466e38f) frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1): |x| * 2^-e < 1
-      const float v = m <= 3.402823466e38f ? __fmul_rn(ldexpf(xv[u], -e), 127.0f) : 0.0f;
-      const float d0 = rintf(v);                              // |v| < 127: d0 in [-127, 127]
-      const float r1 = __fmul_rn(__fsub_rn(v, d0), 254.0f);  // v - d0 in [-0.5, 0.5] (exact): r1 in [-127, 127]
-      const float d1 = rintf(r1);
-      const float d2 = rintf(__fmul_rn(__fsub_rn(r1, d1), 254.0f));
-      const int i0 = (int)d0, i1 = (int)d1, i2 = (int)d2;
+      // the block maximum of |x| as bits (order-preserving for non-negative floats)
+      const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(xv[u]) & 0x7FFFFFFFu);
+      const uint32_t E = mb >> 23;  // biased exponent of the maximum
+      int e = 0;                    // m = f * 2^e, f in [0.5, 1): |x| * 2^-e < 1
+      float v = 0.0f, f = 0.0f;     // v = x * 127 * 2^-e, f = 2^e / 127
+      if (mb > 0x7F7FFFFFu) {       // inf or NaN in the block: its rows become NaN
+        f = __int_as_float(0x7fc00000);
+      } else if (E >= 1 && E <= 252) {
+        e = (int)E - 126;
+        // 127 * 2^-e is exact, so v is x * 2^-e * 127 rounded once; 2^e * f32(1/127) is f32(2^e / 127)
+        v = __fmul_rn(xv[u], __fmul_rn(__uint_as_float((uint32_t)(127 - e) << 23), 127.0f));
+        f = __fmul_rn(__uint_as_float((uint32_t)(127 + e) << 23), 1.0f / 127.0f);
+      } else if (mb != 0) {  // a subnormal maximum, or one near the top of the range
+        frexpf(__uint_as_float(mb), &e);
+        v = __fmul_rn(ldexpf(xv[u], -e), 127.0f);
+        f = __fdiv_rn(ldexpf(1.0f, e), 127.0f);
+      }
+      const int i0 = __float2int_rn(v);                            // |v| <= 127
+      const float r1 = __fmul_rn(__fsub_rn(v, (float)i0), 254.0f);  // v - i0 in [-0.5, 0.5], exact
+      const int i1 = __float2int_rn(r1);
+      const int i2 = __float2int_rn(__fmul_rn(__fsub_rn(r1, (float)i1), 254.0f));
       // byte `lane` of each digit: word lane / 4; lane t of the fragment keeps words t and 4 + t
       const int wd = lane >> 2, tt = wd & 3, hh = wd >> 2;
       unsigned char* base = reinterpret_cast<unsigned char*>(dig + (size_t)b * 12);
       base[(0 * 4 + tt) * 8 + hh * 4 + (lane & 3)] = (unsigned char)(int8_t)i0;
       base[(1 * 4 + tt) * 8 + hh * 4 + (lane & 3)] = (unsigned char)(int8_t)i1;
       base[(2 * 4 + tt) * 8 + hh * 4 + (lane & 3)] = (unsigned char)(int8_t)i2;
-      int s0 = i0, s1 = i1, s2 = i2;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-      }
-      // a block holding inf or NaN makes its rows NaN (the digits are then meaningless)
-      const float f = m <= 3.402823466e38f ? __fdiv_rn(ldexpf(1.0f, e), 127.0f) : __int_as_float(0x7fc00000);
+      const int s0 = __reduce_add_sync(0xffffffffu, i0), s1 = __reduce_add_sync(0xffffffffu, i1),
+                s2 = __reduce_add_sync(0xffffffffu, i2);
       if (lane == 0) tinfo[b] = make_int4(s0, s1, s2, __float_as_int(f));
     }
   }
