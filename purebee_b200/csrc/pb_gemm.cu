@@ -31,6 +31,8 @@
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
+#include <stdlib.h>
+
 #include <mutex>
 
 #include "pb_internal.cuh"
@@ -1060,9 +1062,13 @@ static int launch_gemm_ws(pb_ctx* ctx, const pb_qmat* w, const __half* Xh, int M
   const int ktot = w->K / GW_K;
   dim3 grid(pb_cdiv(w->N, GW_ROWS), 1, 1);
   int splits = 1;
-  if (ws) {  // split K while the grid fits one wave of two CTAs per SM
+  if (ws) {  // split K while the grid fits one wave of the CTAs an SM holds (shared memory)
     const int plan_n = epi.split_n > 0 ? epi.split_n : w->N;
-    splits = 2 * ctx->sm_count / pb_cdiv(plan_n, GW_ROWS);
+    static const int per_sm_env = getenv("PB_WS_PER_SM") ? atoi(getenv("PB_WS_PER_SM")) : 0;  // tuning override
+    int per_sm = (int)((size_t)227 * 1024 / (gw_smem(epi.terms) + 1024));
+    if (per_sm < 1) per_sm = 1;
+    if (per_sm_env > 0) per_sm = per_sm_env;
+    splits = per_sm * ctx->sm_count / pb_cdiv(plan_n, GW_ROWS);
     const int max_by_k = ktot / 4 > 1 ? ktot / 4 : 1;
     const int max_by_ws = (int)(ws_bytes / ((size_t)M * plan_n * 4));
     const int fit = (int)(ws_bytes / ((size_t)M * w->N * 4));
