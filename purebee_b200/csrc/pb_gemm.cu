@@ -692,7 +692,8 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
     // planned for split_n rows when set (a row slice keeps the whole matrix's plan)
     const int plan_n = epi.split_n > 0 ? epi.split_n : w->N;
     const int base = pb_cdiv(plan_n, GM_ROWS) * grid.y;
-    splits = pb_cdiv(2 * ctx->sm_count, base);
+    // until the grid covers the SMs twice, or once with the three-term stages (one CTA per SM)
+    splits = pb_cdiv((epi.terms == 3 ? 1 : 2) * ctx->sm_count, base);
     const int max_by_k = ktot / 4 > 1 ? ktot / 4 : 1;
     const int max_by_ws = (int)(ws_bytes / ((size_t)M * plan_n * 4));
     const int fit = (int)(ws_bytes / ((size_t)M * w->N * 4));  // the partials of this matrix must fit
