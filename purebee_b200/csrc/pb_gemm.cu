@@ -783,13 +783,16 @@ extern "C" int pb_q4_gemm_hl(pb_ctx* ctx, const pb_qmat* w, const void* xhl_dev,
 // in the same order, so both kernels give the same partial sums.
 // ---------------------------------------------------------------------------
 
-constexpr int GW_ROWS = 128, GW_TOK = 64, GW_K = 64, GW_STAGES = 6, GW_ABUF = 2, GW_THREADS = 192;
+constexpr int GW_ROWS = 128, GW_TOK = 64, GW_K = 64, GW_STAGES = 6, GW_ABUF = 2, GW_THREADS = 320;
+constexpr int GW_DQ = GW_THREADS - 64;  // dequant threads: one per (row, block) of a 64-wide K step
+static_assert(GW_DQ == 2 * GW_ROWS && GW_TOK == 64 && GW_K == 64,
+              "the dequant threads cover a step's two blocks of every row; two warps share a TMEM quadrant's columns");
 constexpr int GW_RAW_BYTES = GW_ROWS * 32;               // 2 Q4_0 payloads (16 B) per row
 constexpr int GW_X_BYTES = GW_TOK * GW_K * 2;            // f16 activations, swizzled
 constexpr int GW_A_BYTES = GW_ROWS * GW_K * 2;           // f16 weights, swizzled
-constexpr int GW_STAGE_BYTES = GW_X_BYTES + GW_RAW_BYTES;  // X first: 1024-aligned
-// [GW_ABUF dequantized tiles][GW_STAGES (activations, payload) stages]; with
-// three terms each weight tile and each activation tile is a hi, lo pair
+// [GW_ABUF dequantized tiles][GW_STAGES (activations, payload) stages], the
+// activations first in a stage (1024-aligned); with three terms each weight
+// tile and each activation tile is a hi, lo pair
 static size_t gw_smem(int terms) {
   const int t = terms == 3 ? 2 : 1;
   return (size_t)GW_ABUF * GW_A_BYTES * t + (size_t)GW_STAGES * (GW_X_BYTES * t + GW_RAW_BYTES) + 1024;
@@ -856,7 +859,7 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       pb_mbar_init(&empty[st], 1);
     }
     for (int ab = 0; ab < GW_ABUF; ++ab) {
-      pb_mbar_init(&aready[ab], 128);
+      pb_mbar_init(&aready[ab], GW_DQ);
       pb_mbar_init(&afree[ab], 1);
     }
     pb_mbar_init(&accf, 1);
@@ -933,12 +936,13 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       if (ok && ksteps > 0) mma_commit(&accf);
     }
   } else {
-    // dequant: thread t = weight row n0 + t
-    const int t = tid - 64, row = n0 + t;
+    // dequant: thread t = (block bb = t / 128 of the step, weight row n0 + t % 128); two
+    // warps per sub-partition, so one warp's latency hides behind the other's
+    const int t = (tid - 64) & (GW_ROWS - 1), bb = (tid - 64) >> 7, row = n0 + t;
     const bool live_row = row < N_pad;
     const uint32_t magic = 0x64086408u;  // f16 1032.0 twice
     // the CTA's payload slice into L2 first (one run per row, or per 8-row tile)
-    if (ksteps > 0) {
+    if (ksteps > 0 && bb == 0) {
       const int b0 = 2 * kbeg, b1 = 2 * kend < nb ? 2 * kend : nb;
       if (layout == PB_LAYOUT_TILED8) {
         const int tile = (n0 >> 3) + t;
@@ -949,33 +953,26 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       }
     }
     bool ok = true;
-    // the two scales of a step, loaded one step ahead (L2-resident after the prefetch)
-    auto scales = [&](int ks, uint32_t (&d)[2]) {
-      d[0] = d[1] = 0u;
-      if (live_row && ks < kend) {
-#pragma unroll
-        for (int bb = 0; bb < 2; ++bb) {
-          // the reference's scale decode: a zero exponent is +0 (subnormal scales flushed)
-          const uint32_t bits = __ldg(dsc + pb_slot(layout, row, 2 * ks + bb, nb));
-          d[bb] = (bits & 0x7C00u) ? bits : 0u;
-        }
-      }
+    // the thread's scale of a step, loaded one step ahead (L2-resident after the prefetch)
+    auto scales = [&](int ks) -> uint32_t {
+      if (!live_row || ks >= kend) return 0u;
+      // the reference's scale decode: a zero exponent is +0 (subnormal scales flushed)
+      const uint32_t bits = __ldg(dsc + pb_slot(layout, row, 2 * ks + bb, nb));
+      return (bits & 0x7C00u) ? bits : 0u;
     };
-    uint32_t dnext[2];
-    scales(kbeg, dnext);
+    uint32_t dnext = scales(kbeg);
     pb_pdl_wait();  // before the epilogue reads or writes C
     for (int g = 0; g < ksteps && ok; ++g) {
       const int st = g % GW_STAGES, ks = kbeg + g;
-      const uint32_t d2[2] = {dnext[0] | (dnext[0] << 16), dnext[1] | (dnext[1] << 16)};
-      scales(ks + 1, dnext);
+      const uint32_t d2 = dnext | (dnext << 16);
+      dnext = scales(ks + 1);
       const int ab = g % GW_ABUF;
       if (!(ok = pb_mbar_wait_sleep(&full[st], (g / GW_STAGES) & 1, err))) break;
       // the weight buffer is free once the MMAs of step g - GW_ABUF completed
       if (g >= GW_ABUF && !(ok = pb_mbar_wait_sleep(&afree[ab], ((g / GW_ABUF) - 1) & 1, err))) break;
       unsigned char* sA = ring + ab * AB;
       const unsigned char* raw = ring + GW_ABUF * AB + st * SB + XB;
-#pragma unroll
-      for (int bb = 0; bb < 2; ++bb) {
+      {
         const uint32_t off =
             layout == PB_LAYOUT_TILED8 ? (uint32_t)((((t >> 3) * 2 + bb) * 8 + (t & 7)) * 16) : (uint32_t)(t * 32 + bb * 16);
         const uint4 q = *reinterpret_cast<const uint4*>(raw + off);
@@ -992,8 +989,8 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          if (TERMS == 3) h2_sub_mul_hl(v[i], magic, d2[bb], h[i], r[i]);
-          else h[i] = h2_sub_mul(v[i], magic, d2[bb]);
+          if (TERMS == 3) h2_sub_mul_hl(v[i], magic, d2, h[i], r[i]);
+          else h[i] = h2_sub_mul(v[i], magic, d2);
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -1007,18 +1004,16 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&aready[ab])) : "memory");
     }
-    // epilogue: TMEM lanes of this warp's quadrant, 64 token columns
+    // epilogue: TMEM lanes of this warp's quadrant (warp % 4), two warps per quadrant, each
+    // 32 of the 64 token columns
     const bool empty_split = ksteps == 0;
     if (ok && !empty_split) ok = pb_mbar_wait_sleep(&accf, 0, err);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok) {
-      const int q4 = warp & 3, erow = n0 + q4 * 32 + lane;
-#pragma unroll 1
-      for (int c0 = 0; c0 < GW_TOK; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem_d + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
-        gemm_emit32(v, empty_split, erow, N, m0 + c0, M, C, ldc, epi);
-      }
+      const int q4 = warp & 3, erow = n0 + q4 * 32 + lane, c0 = bb * 32;
+      uint32_t v[32];
+      tmem_ld32(tmem_d + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
+      gemm_emit32(v, empty_split, erow, N, m0 + c0, M, C, ldc, epi);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
