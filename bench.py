@@ -773,7 +773,7 @@ def run_case(args):
         ctx.close()
         return
     mtok = 1
-    if kind in ("gemm", "gemmhl"):  # gemm:MxNxK (f32 activations), gemmhl:MxNxK (hi/lo pairs, three terms)
+    if kind in ("gemm", "gemm3", "gemmhl"):  # gemm / gemm3:MxNxK (f32 activations, one / three terms), gemmhl:MxNxK
         mtok, n, k = (int(v) for v in shape.lower().split("x"))
     else:
         n, k = (int(v) for v in shape.lower().split("x"))
@@ -792,6 +792,10 @@ def run_case(args):
         X = ctx.to_device(rng.standard_normal((mtok, k)).astype(np.float32))
         Cb = ctx.alloc(mtok * n * 4)
         call = lambda: ctx._check(L.pb_q4_gemm(ctx.h, m.h, X.ptr, mtok, k, Cb.ptr, n))
+    elif kind == "gemm3":  # the three-term product (M >= 512: hi/lo copies and the persistent TMA kernel)
+        X = ctx.to_device(rng.standard_normal((mtok, k)).astype(np.float32))
+        Cb = ctx.alloc(mtok * n * 4)
+        call = lambda: ctx._check(L.pb_q4_gemm_ex(ctx.h, m.h, X.ptr, mtok, k, Cb.ptr, n, 3))
     elif kind == "gemmhl":  # the batched decode GEMM's three-term form (M <= 64: the warp-specialised kernel)
         Xf = rng.standard_normal((mtok, k)).astype(np.float32)
         hi = Xf.astype(np.float16)
@@ -810,7 +814,7 @@ def run_case(args):
         call()
     us = graph_time_us(ctx, torch, stream, lambda i: call(), args.steps)
     line = {"case": args.case, "us_per_launch": round(us, 3), "bytes": int(raw.nbytes)}
-    if kind in ("gemm", "gemmhl"):
+    if kind in ("gemm", "gemm3", "gemmhl"):
         line["TFLOPs"] = round(2.0 * mtok * n * k / (us * 1e-6) / 1e12, 1)
     print(json.dumps(line), flush=True)
     m.free()
@@ -825,7 +829,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched configuration (configs[4])")
-    ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK, head:VxD, gemm:MxNxK, gemmhl:MxNxK, batched:BxP "
+    ap.add_argument("--case", default=None, help="profile one kernel: matvec:NxK, head:VxD, gemm:MxNxK, gemm3:MxNxK, gemmhl:MxNxK, batched:BxP "
                                                  "(batched prefill + 3 steps), decode:N[@POS] (N decode steps), or exchange:BYTES "
                                                  "(under torchrun: in-place all-gathers of BYTES per rank)")
     args = ap.parse_args()

@@ -158,6 +158,15 @@ int pb_matvec_mode(const pb_ctx* ctx);
  * within the fast mode's tolerance.  A tuning knob with no counterpart in
  * the reference. */
 int pb_set_mvi_min_rows(pb_ctx* ctx, int rows);
+/* Fast mode: on = 1 runs the Q4_0 row-layout matvecs with K % 128 == 0 and
+ * K <= 16384 on the tcgen05 int8 kernel (the same integer digits as the int8
+ * kernel above, the products on the 5th-generation tensor cores) for the
+ * matrices uploaded while it is on (they get the kernel's tile-contiguous
+ * copy); other matrices, and every matrix with on = 0 (the default, as it
+ * measures slower than the kernels above; environment PB_MVT=1 at pb_init
+ * turns it on), take the choice pb_set_mvi_min_rows makes.  A tuning knob
+ * with no counterpart in the reference. */
+int pb_set_mvt(pb_ctx* ctx, int on);
 /* wasm-q4.js:716-747 q4_0_matvec(x, rawBuf, N, K): host buffers in and out. */
 int pb_q4_0_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, int N, int K, float* y_host);
 /* wasm-q4.js:758-785 q4_1_matvec(x, rawBuf, N, K) */

@@ -117,6 +117,7 @@ extern "C" int pb_init(int device, pb_ctx** out) {
   ctx->sm_count = prop.multiProcessorCount;
   // tuning override: matrix rows from which the fast mode takes the int8 tensor-core matvec
   if (const char* ev = getenv("PB_MVI_MIN_ROWS")) ctx->mvi_min_rows = atoi(ev);
+  if (const char* ev = getenv("PB_MVT")) ctx->mvt = ev[0] == '1';  // tuning override: the tcgen05 matvec on
   const char* nopdl = getenv("PB_NO_PDL");  // programmatic dependent launch off (debugging aid)
   ctx->pdl = !(nopdl && nopdl[0] == '1');
 
@@ -126,7 +127,7 @@ extern "C" int pb_init(int device, pb_ctx** out) {
   cudaMemset(ctx->d_err, 0, sizeof(int));
   cudaDeviceSynchronize();
   if (pb_setup_q4_kernels() != PB_OK || pb_setup_ops_kernels() != PB_OK || pb_setup_gemm_kernels() != PB_OK ||
-      pb_setup_mvi_kernels() != PB_OK ||
+      pb_setup_mvi_kernels() != PB_OK || pb_setup_mvt_kernels() != PB_OK ||
       pb_setup_sample_kernels() != PB_OK ||
       pb_setup_noalloc(ctx) != PB_OK) {
     pb_shutdown(ctx);
@@ -177,6 +178,12 @@ extern "C" int pb_matvec_mode(const pb_ctx* ctx) { return ctx ? ctx->matvec_mode
 extern "C" int pb_set_mvi_min_rows(pb_ctx* ctx, int rows) {
   if (!ctx || rows < 0) return PB_ERR_ARG;
   ctx->mvi_min_rows = rows;
+  return PB_OK;
+}
+
+extern "C" int pb_set_mvt(pb_ctx* ctx, int on) {
+  if (!ctx || (on != 0 && on != 1)) return PB_ERR_ARG;
+  ctx->mvt = on == 1;
   return PB_OK;
 }
 
@@ -693,6 +700,7 @@ extern "C" int pb_qmat_free(pb_ctx* ctx, pb_qmat* m) {
   cudaFree(m->m);
   cudaFree(m->mq);
   cudaFree(m->md);
+  cudaFree(m->tq);
   delete m;
   return PB_OK;
 }

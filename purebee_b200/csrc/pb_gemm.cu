@@ -27,15 +27,11 @@
 // the stage is rewritten only after that mbarrier's phase completes.  Every
 // wait is bounded and records PB_DEVERR_WAIT instead of hanging.
 
-#include <cuda.h>
-#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
 #include <stdlib.h>
 
-#include <mutex>
-
-#include "pb_internal.cuh"
+#include "pb_tc.cuh"
 
 namespace {
 
@@ -46,22 +42,6 @@ constexpr int GM_THREADS = 256;
 constexpr int GM_TILE_BYTES = GM_ROWS * GM_KSTEP * 2;  // 16 KB, A and B alike
 constexpr int GM_STAGE_BYTES = 2 * GM_TILE_BYTES;
 constexpr int PB_GEMM_TMA_MIN_M = 512;  // from here on the f16 copy of W pays for itself
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-// Byte offset of 16-byte chunk c (K elements 8c .. 8c+7) of row r in a
-// K-major, 128-byte-swizzled tile: 8-row groups of 1024 bytes, rows of 128
-// bytes, chunk index XOR (row mod 8).
-__device__ __forceinline__ uint32_t sw128(int r, int c) {
-  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
-}
-
-// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024
-// bytes apart (stride byte offset), sm100 descriptor version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
 
 // Instruction descriptor: D f32, A and B f16, both K-major, M = 128, N = tok.
 __host__ __device__ constexpr uint32_t gm_idesc(int tok) {
@@ -76,23 +56,6 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
       ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
       : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
@@ -158,7 +121,7 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
   __shared__ uint64_t bars[2];
   __shared__ uint32_t tmem_base;
   // 1024-byte alignment of the swizzled tiles (the swizzle repeats every 1024 bytes)
-  unsigned char* ring = gm_raw + ((1024 - (smem_addr(gm_raw) & 1023)) & 1023);
+  unsigned char* ring = gm_raw + ((1024 - (pb_smem_addr(gm_raw) & 1023)) & 1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * GM_ROWS, m0 = blockIdx.y * TOK;
   const int K = nb * 32, ktot = (K + GM_KSTEP - 1) / GM_KSTEP;
@@ -167,7 +130,7 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
   C += (size_t)blockIdx.z * M * ldc;
 
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(pb_smem_addr(&tmem_base)),
                  "r"(TOK)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -244,14 +207,14 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
         v.y = pack_h2(e[8 * c + 2], e[8 * c + 3]);
         v.z = pack_h2(e[8 * c + 4], e[8 * c + 5]);
         v.w = pack_h2(e[8 * c + 6], e[8 * c + 7]);
-        *reinterpret_cast<uint4*>(sA + sw128(wr, wblk * 4 + c)) = v;
+        *reinterpret_cast<uint4*>(sA + pb_sw128(wr, wblk * 4 + c)) = v;
         if (TERMS == 3) {
           uint4 l;
           l.x = pack_lo2(e[8 * c + 0], e[8 * c + 1], v.x);
           l.y = pack_lo2(e[8 * c + 2], e[8 * c + 3], v.y);
           l.z = pack_lo2(e[8 * c + 4], e[8 * c + 5], v.z);
           l.w = pack_lo2(e[8 * c + 6], e[8 * c + 7], v.w);
-          *reinterpret_cast<uint4*>(sAl + sw128(wr, wblk * 4 + c)) = l;
+          *reinterpret_cast<uint4*>(sAl + pb_sw128(wr, wblk * 4 + c)) = l;
         }
       }
     }
@@ -263,14 +226,14 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
         v.y = pack_h2(xa[2 * c].z, xa[2 * c].w);
         v.z = pack_h2(xa[2 * c + 1].x, xa[2 * c + 1].y);
         v.w = pack_h2(xa[2 * c + 1].z, xa[2 * c + 1].w);
-        *reinterpret_cast<uint4*>(sB + sw128(xr_, xh * 4 + c)) = v;
+        *reinterpret_cast<uint4*>(sB + pb_sw128(xr_, xh * 4 + c)) = v;
         if (TERMS == 3) {
           uint4 l;
           l.x = pack_lo2(xa[2 * c].x, xa[2 * c].y, v.x);
           l.y = pack_lo2(xa[2 * c].z, xa[2 * c].w, v.y);
           l.z = pack_lo2(xa[2 * c + 1].x, xa[2 * c + 1].y, v.z);
           l.w = pack_lo2(xa[2 * c + 1].z, xa[2 * c + 1].w, v.w);
-          *reinterpret_cast<uint4*>(sBl + sw128(xr_, xh * 4 + c)) = l;
+          *reinterpret_cast<uint4*>(sBl + pb_sw128(xr_, xh * 4 + c)) = l;
         }
       }
     }
@@ -280,8 +243,8 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
     __syncthreads();
     if (tid == 0) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sB));
-      const uint64_t dal = sw128_desc(smem_addr(sAl)), dbl = sw128_desc(smem_addr(sBl));
+      const uint64_t da = pb_sw128_desc(pb_smem_addr(sA)), db = pb_sw128_desc(pb_smem_addr(sB));
+      const uint64_t dal = pb_sw128_desc(pb_smem_addr(sAl)), dbl = pb_sw128_desc(pb_smem_addr(sBl));
 #pragma unroll
       for (int kk = 0; kk < GM_KSTEP / 16; ++kk) {  // +32 bytes (16 f16) along K per MMA
         mma_f16(tmem_d, da + 2 * kk, db + 2 * kk, gm_idesc(TOK), (ks > 0 || kk > 0) ? 1u : 0u);
@@ -290,7 +253,7 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
           mma_f16(tmem_d, dal + 2 * kk, db + 2 * kk, gm_idesc(TOK), 1u);
         }
       }
-      mma_commit(&bars[st]);
+      pb_umma_commit(&bars[st]);
     }
   }
   // the last step's commit covers every MMA issued before it
@@ -303,7 +266,7 @@ k_q4_gemm_tc(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, i
 #pragma unroll 1
     for (int c0 = 0; c0 < TOK; c0 += 32) {
       uint32_t v[32];
-      tmem_ld32(tmem_d + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+      pb_tmem_ld32(tmem_d + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
       gemm_emit32(v, empty_split, row, N, m0 + c0, M, C, ldc, epi);  // split-K partials always STORE
     }
   }
@@ -339,20 +302,6 @@ constexpr int TG_STAGE_BYTES = TG_A_BYTES + TG_B_BYTES;
 constexpr uint32_t TG_IDESC = (1u << 4) | ((uint32_t)(TG_TOK >> 3) << 17) | ((uint32_t)(TG_ROWS >> 4) << 24);
 
 namespace {
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-      ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
-      : "memory");
-}
 
 __device__ __forceinline__ void mma_f16_n256(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
@@ -434,13 +383,13 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
   extern __shared__ __align__(1024) unsigned char tg_raw[];
   __shared__ uint64_t full[NST], empty[NST], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
-  unsigned char* ring = tg_raw + ((1024 - (smem_addr(tg_raw) & 1023)) & 1023);
+  unsigned char* ring = tg_raw + ((1024 - (pb_smem_addr(tg_raw) & 1023)) & 1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ksteps = K / TG_K;
   const int ntn = (N + TG_ROWS - 1) / TG_ROWS, ntm = (M + TG_TOK - 1) / TG_TOK, ntiles = ntn * ntm;
 
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(pb_smem_addr(&tmem_base)),
                  "r"(2 * TG_TOK)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -478,13 +427,13 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
         // hi/lo rows: the hi group at 2x, the lo group 64 halves after it
         const int xk = (ks * TG_K) % xkc, xz = (ks * TG_K) / xkc;
         if (TERMS == 3) {
-          tma_load_2d(sA, &map_w, 2 * ks * TG_K, n0, &full[s]);
-          tma_load_3d(sA + TG_A_BYTES, &map_x, 2 * xk, m0, xz, &full[s]);
-          tma_load_2d(sA + TG_STAGE_BYTES, &map_w, 2 * ks * TG_K + 64, n0, &full[s]);
-          tma_load_3d(sA + TG_STAGE_BYTES + TG_A_BYTES, &map_x, 2 * xk + 64, m0, xz, &full[s]);
+          pb_tma_load_2d(sA, &map_w, 2 * ks * TG_K, n0, &full[s]);
+          pb_tma_load_3d(sA + TG_A_BYTES, &map_x, 2 * xk, m0, xz, &full[s]);
+          pb_tma_load_2d(sA + TG_STAGE_BYTES, &map_w, 2 * ks * TG_K + 64, n0, &full[s]);
+          pb_tma_load_3d(sA + TG_STAGE_BYTES + TG_A_BYTES, &map_x, 2 * xk + 64, m0, xz, &full[s]);
         } else {
-          tma_load_2d(sA, &map_w, ks * TG_K, n0, &full[s]);
-          tma_load_3d(sA + TG_A_BYTES, &map_x, xk, m0, xz, &full[s]);
+          pb_tma_load_2d(sA, &map_w, ks * TG_K, n0, &full[s]);
+          pb_tma_load_3d(sA + TG_A_BYTES, &map_x, xk, m0, xz, &full[s]);
         }
       }
     }
@@ -502,9 +451,9 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
         if (!(ok = pb_mbar_wait(&full[s], (g / NST) & 1, err))) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         unsigned char* sA = ring + s * SB;
-        const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sA + TG_A_BYTES));
-        const uint64_t dal = sw128_desc(smem_addr(sA + TG_STAGE_BYTES));
-        const uint64_t dbl = sw128_desc(smem_addr(sA + TG_STAGE_BYTES + TG_A_BYTES));
+        const uint64_t da = pb_sw128_desc(pb_smem_addr(sA)), db = pb_sw128_desc(pb_smem_addr(sA + TG_A_BYTES));
+        const uint64_t dal = pb_sw128_desc(pb_smem_addr(sA + TG_STAGE_BYTES));
+        const uint64_t dbl = pb_sw128_desc(pb_smem_addr(sA + TG_STAGE_BYTES + TG_A_BYTES));
 #pragma unroll
         for (int kk = 0; kk < TG_K / 16; ++kk) {
           mma_f16_n256(acc, da + 2 * kk, db + 2 * kk, (ks > 0 || kk > 0) ? 1u : 0u);
@@ -513,9 +462,9 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
             mma_f16_n256(acc, dal + 2 * kk, db + 2 * kk, 1u);
           }
         }
-        mma_commit(&empty[s]);
+        pb_umma_commit(&empty[s]);
       }
-      mma_commit(&acc_full[b]);  // fires when every MMA of the tile has completed
+      pb_umma_commit(&acc_full[b]);  // fires when every MMA of the tile has completed
     }
   } else if (warp >= 4) {
     // epilogue: lane quadrant q of the accumulator, half of its 256 columns
@@ -530,12 +479,12 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
 #pragma unroll 1
       for (int c0 = half * (TG_TOK / 2); c0 < (half + 1) * (TG_TOK / 2); c0 += 32) {
         uint32_t v[32];
-        tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * TG_TOK + c0), v);
+        pb_tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * TG_TOK + c0), v);
         gemm_emit32(v, false, row, N, m0 + c0, M, C, ldc, epi);
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&acc_empty[b])) : "memory");
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(pb_smem_addr(&acc_empty[b])) : "memory");
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -550,23 +499,9 @@ static size_t tg_smem(int terms) {
   return (terms == 3 ? (size_t)2 * 2 * TG_STAGE_BYTES : (size_t)TG_STAGES * TG_STAGE_BYTES) + 1024;
 }
 
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder(pb_ctx* ctx) {
-  static std::once_flag once;
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  if (!fn) pb_set_error(ctx, PB_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
-  return fn;
-}
-
 // Row-major f16 [rows][K] with a box of box_rows x 64 elements, 128-byte swizzle.
 static int make_map(pb_ctx* ctx, CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
-  auto enc = tensor_map_encoder(ctx);
+  auto enc = pb_tensor_map_encoder(ctx);
   if (!enc) return PB_ERR_CUDA;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)K * 2};
@@ -582,7 +517,7 @@ static int make_map(pb_ctx* ctx, CUtensorMap* map, const void* base, int rows, i
 // f16 X as [K / kc][rows][kc] (kc == K: plain row-major [rows][K]) with a box
 // of box_rows x 64 elements of one chunk, 128-byte swizzle.
 static int make_map_x(pb_ctx* ctx, CUtensorMap* map, const void* base, int rows, int K, int kc, int box_rows) {
-  auto enc = tensor_map_encoder(ctx);
+  auto enc = pb_tensor_map_encoder(ctx);
   if (!enc) return PB_ERR_CUDA;
   cuuint64_t dims[3] = {(cuuint64_t)kc, (cuuint64_t)rows, (cuuint64_t)(K / kc)};
   cuuint64_t strides[2] = {(cuuint64_t)kc * 2, (cuuint64_t)rows * kc * 2};
@@ -834,7 +769,7 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
   extern __shared__ __align__(1024) unsigned char gw_raw[];
   __shared__ uint64_t full[GW_STAGES], empty[GW_STAGES], aready[GW_ABUF], afree[GW_ABUF], accf;
   __shared__ uint32_t tmem_base;
-  unsigned char* ring = gw_raw + ((1024 - (smem_addr(gw_raw) & 1023)) & 1023);
+  unsigned char* ring = gw_raw + ((1024 - (pb_smem_addr(gw_raw) & 1023)) & 1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * GW_ROWS, m0 = blockIdx.y * GW_TOK;
   const int ktot = nb / 2;  // K / 64
@@ -848,7 +783,7 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
   pb_pdl_trigger();
 
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(pb_smem_addr(&tmem_base)),
                  "r"(GW_TOK)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -879,19 +814,19 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
         if (layout == PB_LAYOUT_TILED8)
           asm volatile(
               "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-              "[%5];" ::"r"(smem_addr(sX + XB)),
-              "l"(&map_q), "r"(0), "r"(2 * ks), "r"(n0 >> 3), "r"(smem_addr(&full[st]))
+              "[%5];" ::"r"(pb_smem_addr(sX + XB)),
+              "l"(&map_q), "r"(0), "r"(2 * ks), "r"(n0 >> 3), "r"(pb_smem_addr(&full[st]))
               : "memory");
         else
-          tma_load_2d(sX + XB, &map_q, 32 * ks, n0, &full[st]);
+          pb_tma_load_2d(sX + XB, &map_q, 32 * ks, n0, &full[st]);
       };
       // the activations of step g (written by the previous kernels)
       auto acts = [&](int g) {
         const int st = g % GW_STAGES, ks = kbeg + g;
         unsigned char* sX = ring + GW_ABUF * AB + st * SB;
         const int xk = (ks * GW_K) % xkc, xz = (ks * GW_K) / xkc;
-        tma_load_3d(sX, &map_x, TW * xk, m0, xz, &full[st]);
-        if (TERMS == 3) tma_load_3d(sX + GW_X_BYTES, &map_x, 2 * xk + 64, m0, xz, &full[st]);
+        pb_tma_load_3d(sX, &map_x, TW * xk, m0, xz, &full[st]);
+        if (TERMS == 3) pb_tma_load_3d(sX + GW_X_BYTES, &map_x, 2 * xk + 64, m0, xz, &full[st]);
       };
       // the first ring's payloads go out before the dependency wait, their activations after it
       const int first = ksteps < GW_STAGES ? ksteps : GW_STAGES;
@@ -920,8 +855,8 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         unsigned char* sA = ring + ab * AB;
         unsigned char* sX = ring + GW_ABUF * AB + st * SB;
-        const uint64_t da = sw128_desc(smem_addr(sA)), db = sw128_desc(smem_addr(sX));
-        const uint64_t dal = sw128_desc(smem_addr(sA + GW_A_BYTES)), dbl = sw128_desc(smem_addr(sX + GW_X_BYTES));
+        const uint64_t da = pb_sw128_desc(pb_smem_addr(sA)), db = pb_sw128_desc(pb_smem_addr(sX));
+        const uint64_t dal = pb_sw128_desc(pb_smem_addr(sA + GW_A_BYTES)), dbl = pb_sw128_desc(pb_smem_addr(sX + GW_X_BYTES));
 #pragma unroll
         for (int kk = 0; kk < GW_K / 16; ++kk) {
           mma_f16(tmem_d, da + 2 * kk, db + 2 * kk, gm_idesc(GW_TOK), (g > 0 || kk > 0) ? 1u : 0u);
@@ -930,10 +865,10 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
             mma_f16(tmem_d, dal + 2 * kk, db + 2 * kk, gm_idesc(GW_TOK), 1u);
           }
         }
-        mma_commit(&empty[st]);
-        mma_commit(&afree[ab]);
+        pb_umma_commit(&empty[st]);
+        pb_umma_commit(&afree[ab]);
       }
-      if (ok && ksteps > 0) mma_commit(&accf);
+      if (ok && ksteps > 0) pb_umma_commit(&accf);
     }
   } else {
     // dequant: thread t = (block bb = t / 128 of the step, weight row n0 + t % 128); two
@@ -994,15 +929,15 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          *reinterpret_cast<uint4*>(sA + sw128(t, 4 * bb + c)) = make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+          *reinterpret_cast<uint4*>(sA + pb_sw128(t, 4 * bb + c)) = make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
           if (TERMS == 3)
-            *reinterpret_cast<uint4*>(sA + GW_A_BYTES + sw128(t, 4 * bb + c)) =
+            *reinterpret_cast<uint4*>(sA + GW_A_BYTES + pb_sw128(t, 4 * bb + c)) =
                 make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
         }
       }
       // generic-proxy reads of the payload and writes of the tile -> the async proxy
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&aready[ab])) : "memory");
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(pb_smem_addr(&aready[ab])) : "memory");
     }
     // epilogue: TMEM lanes of this warp's quadrant (warp % 4), two warps per quadrant, each
     // 32 of the 64 token columns
@@ -1012,7 +947,7 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
     if (ok) {
       const int q4 = warp & 3, erow = n0 + q4 * 32 + lane, c0 = bb * 32;
       uint32_t v[32];
-      tmem_ld32(tmem_d + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
+      pb_tmem_ld32(tmem_d + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, v);
       gemm_emit32(v, empty_split, erow, N, m0 + c0, M, C, ldc, epi);
     }
   }
@@ -1028,7 +963,7 @@ k_q4_gemm_ws(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ 
 // bytes (row layout: box 32 B x 128 rows) or 8-row tiles (tiled layout:
 // {128 B, nb, N_pad / 8}, box 128 B x 2 blocks x 16 tiles).
 static int make_map_q(pb_ctx* ctx, CUtensorMap* map, const pb_qmat* w) {
-  auto enc = tensor_map_encoder(ctx);
+  auto enc = pb_tensor_map_encoder(ctx);
   if (!enc) return PB_ERR_CUDA;
   CUresult r;
   cuuint32_t estr[3] = {1, 1, 1};

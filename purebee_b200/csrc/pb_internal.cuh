@@ -20,6 +20,7 @@ struct pb_ctx {
   int64_t launches = 0;
   bool pdl = true;              // launch matvecs with programmatic stream serialization
   int mvi_min_rows = 32768;     // fast mode: matrices of this many rows on take the int8 tensor-core matvec
+  bool mvt = false;             // fast mode: the tcgen05 int8 matvec for the matrices it takes (pb_set_mvt)
   std::string err;
   // scratch for one-shot host-buffer calls (grown on demand)
   void* scratch = nullptr;
@@ -57,9 +58,15 @@ struct pb_qmat {
   uint8_t* mq = nullptr;
   uint16_t* md = nullptr;
   int nbp = 0;  // blocks per row in the copy (a multiple of 8)
+  // The copy the tcgen05 matvec (k_mvt, pb_mvt.cu) streams: the payload in
+  // 128-row tiles, each tile's K steps (4 blocks) of 128 rows x 64 B
+  // contiguous, so one K step of a tile is one 8 KB run.  Built and
+  // invalidated with mq (mma_ok).
+  uint8_t* tq = nullptr;
   bool mma_ok = false;
 };
-int pb_qmat_build_mma(pb_ctx* ctx, pb_qmat* m);  // (re)build the tensor-core copy
+int pb_qmat_build_mma(pb_ctx* ctx, pb_qmat* m);  // (re)build the tensor-core copies (mq / md, and tq)
+int pb_qmat_build_mvt(pb_ctx* ctx, pb_qmat* m);  // (re)build tq (part of pb_qmat_build_mma)
 
 // ---- host helpers ---------------------------------------------------------
 
@@ -230,6 +237,38 @@ __device__ __forceinline__ void pb_bulk_g2s(void* dst, const void* src, uint32_t
                    pb_smem_addr(dst)),
                "l"(src), "r"(bytes), "r"(pb_smem_addr(bar))
                : "memory");
+}
+
+// One 32-value block of x (lane k holds element k) as three signed byte
+// digits for the int8 tensor-core matvecs (pb_mvi.cu, pb_mvt.cu):
+//   x[k] ~= f * (i0 + i1 / 254 + i2 / 254^2),  f = 2^e / 127,
+// e the binary exponent of the block's largest |x| (so 2^-e scales exactly),
+// each digit in [-127, 127]; the representation error is about 1e-7 of the
+// block's largest |x|.  Returns f, NaN (digits 0) when the block holds an
+// inf or NaN.  Every lane of the warp calls it.
+__device__ __forceinline__ float pb_x_digits(float xv, int& i0, int& i1, int& i2) {
+  // the block maximum of |x| as bits (order-preserving for non-negative floats)
+  const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(xv) & 0x7FFFFFFFu);
+  const uint32_t E = mb >> 23;  // biased exponent of the maximum
+  int e = 0;                    // m = g * 2^e, g in [0.5, 1): |x| * 2^-e < 1
+  float v = 0.0f, f = 0.0f;     // v = x * 127 * 2^-e, f = 2^e / 127
+  if (mb > 0x7F7FFFFFu) {       // inf or NaN in the block: its rows become NaN
+    f = __int_as_float(0x7fc00000);
+  } else if (E >= 1 && E <= 252) {
+    e = (int)E - 126;
+    // 127 * 2^-e is exact, so v is x * 2^-e * 127 rounded once; 2^e * f32(1/127) is f32(2^e / 127)
+    v = __fmul_rn(xv, __fmul_rn(__uint_as_float((uint32_t)(127 - e) << 23), 127.0f));
+    f = __fmul_rn(__uint_as_float((uint32_t)(127 + e) << 23), 1.0f / 127.0f);
+  } else if (mb != 0) {  // a subnormal maximum, or one near the top of the range
+    frexpf(__uint_as_float(mb), &e);
+    v = __fmul_rn(ldexpf(xv, -e), 127.0f);
+    f = __fdiv_rn(ldexpf(1.0f, e), 127.0f);
+  }
+  i0 = __float2int_rn(v);                                      // |v| <= 127
+  const float r1 = __fmul_rn(__fsub_rn(v, (float)i0), 254.0f);  // v - i0 in [-0.5, 0.5], exact
+  i1 = __float2int_rn(r1);
+  i2 = __float2int_rn(__fmul_rn(__fsub_rn(r1, (float)i1), 254.0f));
+  return f;
 }
 
 // Ordered-key argmax: larger key = larger value, ties -> lower index.
@@ -497,6 +536,9 @@ int pb_qmat_pack_from_device(pb_ctx* ctx, pb_qmat* m, const void* gguf_dev);
 int pb_setup_q4_kernels(void);
 int pb_setup_mvi_kernels(void);
 int pb_launch_mvi(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows, const pb_mv_epi& epi);
+int pb_setup_mvt_kernels(void);
+bool pb_mvt_ok(const pb_qmat* w);  // the tcgen05 int8 matvec takes the matrix
+int pb_launch_mvt(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows, const pb_mv_epi& epi);
 int pb_setup_ops_kernels(void);
 int pb_setup_gemm_kernels(void);
 int pb_setup_sample_kernels(void);

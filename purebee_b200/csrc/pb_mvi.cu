@@ -90,6 +90,7 @@ int pb_qmat_build_mma(pb_ctx* ctx, pb_qmat* m) {
   const int64_t tot = (int64_t)nt16 * (nbp / 2) * 32 + (int64_t)nt16 * (nbp / 8) * 32;
   k_pack_mma<<<pb_cdiv(tot, 256), 256, 0, ctx->stream>>>(m->qs, m->d, m->layout, m->N, m->nb, nbp, nt16, m->mq, m->md);
   PB_LAUNCHED(ctx, "k_pack_mma");
+  PB_TRY(pb_qmat_build_mvt(ctx, m));
   m->mma_ok = true;
   return PB_OK;
 }
@@ -158,27 +159,8 @@ __device__ __forceinline__ void mvi_stage(const float* __restrict__ x, const flo
     for (int u = 0; u < 4; ++u) {
       const int b = b0 + W * u;
       if (b >= nbp) break;
-      // the block maximum of |x| as bits (order-preserving for non-negative floats)
-      const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(xv[u]) & 0x7FFFFFFFu);
-      const uint32_t E = mb >> 23;  // biased exponent of the maximum
-      int e = 0;                    // m = f * 2^e, f in [0.5, 1): |x| * 2^-e < 1
-      float v = 0.0f, f = 0.0f;     // v = x * 127 * 2^-e, f = 2^e / 127
-      if (mb > 0x7F7FFFFFu) {       // inf or NaN in the block: its rows become NaN
-        f = __int_as_float(0x7fc00000);
-      } else if (E >= 1 && E <= 252) {
-        e = (int)E - 126;
-        // 127 * 2^-e is exact, so v is x * 2^-e * 127 rounded once; 2^e * f32(1/127) is f32(2^e / 127)
-        v = __fmul_rn(xv[u], __fmul_rn(__uint_as_float((uint32_t)(127 - e) << 23), 127.0f));
-        f = __fmul_rn(__uint_as_float((uint32_t)(127 + e) << 23), 1.0f / 127.0f);
-      } else if (mb != 0) {  // a subnormal maximum, or one near the top of the range
-        frexpf(__uint_as_float(mb), &e);
-        v = __fmul_rn(ldexpf(xv[u], -e), 127.0f);
-        f = __fdiv_rn(ldexpf(1.0f, e), 127.0f);
-      }
-      const int i0 = __float2int_rn(v);                            // |v| <= 127
-      const float r1 = __fmul_rn(__fsub_rn(v, (float)i0), 254.0f);  // v - i0 in [-0.5, 0.5], exact
-      const int i1 = __float2int_rn(r1);
-      const int i2 = __float2int_rn(__fmul_rn(__fsub_rn(r1, (float)i1), 254.0f));
+      int i0, i1, i2;
+      const float f = pb_x_digits(xv[u], i0, i1, i2);
       // byte `lane` of each digit: word lane / 4; lane t of the fragment keeps words t and 4 + t
       const int wd = lane >> 2, tt = wd & 3, hh = wd >> 2;
       unsigned char* base = reinterpret_cast<unsigned char*>(dig + (size_t)b * 12);

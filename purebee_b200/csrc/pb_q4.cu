@@ -995,6 +995,7 @@ int pb_launch_head_fast(pb_ctx* ctx, const pb_qmat* t, const float* h, const flo
   e.norm_w = norm_w;
   e.eps = eps;
   e.amax = amax;
+  if (ctx->mvt && pb_mvt_ok(t)) return pb_launch_mvt(ctx, t, h, logits, 0, t->N, e);
   if (t->mq && t->mma_ok && t->layout == PB_LAYOUT_ROWS && t->type == PB_TYPE_Q4_0 && t->N >= ctx->mvi_min_rows)
     return pb_launch_mvi(ctx, t, h, logits, 0, t->N, e);
   return launch_mvf(ctx, t, h, logits, 0, (t->N + 7) / 8, t->N, e);
@@ -1054,9 +1055,11 @@ int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, in
   if (!y && epi.kind != PB_EPI_SWIGLU4) return PB_ERR_ARG;
   const int tile_begin = row0 / 8, ntiles = pb_cdiv(rows, 8);
   if (fast) {
-    // the int8 tensor-core kernel on the matrix's current tensor-core copy (large
-    // matrices: on small ones its per-launch staging of x costs more than it saves),
-    // else the f32 one; chosen per matrix, so row slices of one matrix agree in bits
+    // the tcgen05 int8 kernel where it is on and takes the matrix; else the mma.sync int8
+    // kernel on the matrix's current tensor-core copy (large matrices: on small
+    // ones its per-launch staging of x costs more than it saves), else the f32
+    // one; chosen per matrix, so row slices of one matrix agree in bits
+    if (ctx->mvt && pb_mvt_ok(w)) return pb_launch_mvt(ctx, w, x, y, row0, rows, epi);
     if (w->mq && w->mma_ok && w->layout == PB_LAYOUT_ROWS && w->N >= ctx->mvi_min_rows)
       return pb_launch_mvi(ctx, w, x, y, row0, rows, epi);
     return launch_mvf(ctx, w, x, y, tile_begin, ntiles, row0 + rows, epi);

@@ -136,13 +136,18 @@ RTOL_MATVEC_FAST = 2e-6
 RTOL_ATTN_FAST = 5e-6
 
 
-@pytest.fixture(params=["f32", "int8"])
+@pytest.fixture(params=["f32", "int8", "tcgen05"])
 def fast_kernel(request, native, ctx):
-    """Each fast-mode Q4_0 kernel in turn: the f32 one, and the int8
-    tensor-core one (taken for every matrix size for the test)."""
-    ctx.set_mvi_min_rows(1 << 30 if request.param == "f32" else 0)
+    """Each fast-mode Q4_0 kernel in turn: the f32 one, the mma.sync int8
+    one (taken for every matrix size for the test), and the tcgen05 int8 one
+    (off by default; it takes K % 128 == 0, K <= 16384, other shapes fall
+    back to the f32 kernel).  The test's matrices are uploaded after the
+    switch, so they carry the tcgen05 kernel's copy."""
+    ctx.set_mvt(request.param == "tcgen05")
+    ctx.set_mvi_min_rows(1 << 30 if request.param != "int8" else 0)
     yield request.param
     ctx.set_mvi_min_rows(32768)
+    ctx.set_mvt(False)
 
 
 @pytest.mark.parametrize("N,K", [(64, 64), (136, 576), (512, 1536), (3072, 2048), (2048, 8192), (16384, 2048),
