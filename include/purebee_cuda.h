@@ -167,6 +167,14 @@ int pb_set_mvi_min_rows(pb_ctx* ctx, int rows);
  * turns it on), take the choice pb_set_mvi_min_rows makes.  A tuning knob
  * with no counterpart in the reference. */
 int pb_set_mvt(pb_ctx* ctx, int on);
+/* Fast mode, the one-sequence decode step: on = 1 runs each layer's RMSNorm
+ * -> q/k/v projection (RoPE, KV write) and its decode attention as one
+ * kernel, the 8 CTAs attending for a kv head computing that head group's
+ * projection rows first; the same bits as the two kernels.  Off by default
+ * (environment PB_FUSE_ATTN=1 at pb_init turns it on): measured slower, the
+ * projection then runs on 64 SMs.  Recorded decode graphs are re-recorded
+ * after a change.  A tuning knob with no counterpart in the reference. */
+int pb_set_fuse_attn(pb_ctx* ctx, int on);
 /* wasm-q4.js:716-747 q4_0_matvec(x, rawBuf, N, K): host buffers in and out. */
 int pb_q4_0_matvec(pb_ctx* ctx, const float* x_host, const uint8_t* raw_host, int N, int K, float* y_host);
 /* wasm-q4.js:758-785 q4_1_matvec(x, rawBuf, N, K) */

@@ -106,6 +106,7 @@ SIGNATURES = {
     "pb_matvec_mode": (I, [V]),
     "pb_set_mvi_min_rows": (I, [V, I]),
     "pb_set_mvt": (I, [V, I]),
+    "pb_set_fuse_attn": (I, [V, I]),
     "pb_swiglu": (I, [V, V, V, I, V]),
     "pb_quantize_q8a": (I, [V, V, I64, V, V]),
     "pb_quantize_q4a": (I, [V, V, I64, V, V]),
@@ -288,6 +289,10 @@ class Context:
     def set_mvi_min_rows(self, rows: int) -> None:
         """Fast mode: matrix rows from which Q4_0 matvecs take the int8 tensor-core kernel."""
         self._check(lib().pb_set_mvi_min_rows(self.h, int(rows)))
+
+    def set_fuse_attn(self, on: bool) -> None:
+        """Fast mode: one-sequence decode projection + attention in one kernel (default off; same bits)."""
+        self._check(lib().pb_set_fuse_attn(self.h, 1 if on else 0))
 
     def set_mvt(self, on: bool) -> None:
         """Fast mode: the tcgen05 int8 matvec for the Q4_0 matrices uploaded while it is on (default off)."""

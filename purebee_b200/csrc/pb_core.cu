@@ -118,6 +118,7 @@ extern "C" int pb_init(int device, pb_ctx** out) {
   // tuning override: matrix rows from which the fast mode takes the int8 tensor-core matvec
   if (const char* ev = getenv("PB_MVI_MIN_ROWS")) ctx->mvi_min_rows = atoi(ev);
   if (const char* ev = getenv("PB_MVT")) ctx->mvt = ev[0] == '1';  // tuning override: the tcgen05 matvec on
+  if (const char* ev = getenv("PB_FUSE_ATTN")) ctx->fuse_attn = ev[0] == '1';  // tuning override: fused decode
   const char* nopdl = getenv("PB_NO_PDL");  // programmatic dependent launch off (debugging aid)
   ctx->pdl = !(nopdl && nopdl[0] == '1');
 
@@ -178,6 +179,12 @@ extern "C" int pb_matvec_mode(const pb_ctx* ctx) { return ctx ? ctx->matvec_mode
 extern "C" int pb_set_mvi_min_rows(pb_ctx* ctx, int rows) {
   if (!ctx || rows < 0) return PB_ERR_ARG;
   ctx->mvi_min_rows = rows;
+  return PB_OK;
+}
+
+extern "C" int pb_set_fuse_attn(pb_ctx* ctx, int on) {
+  if (!ctx || (on != 0 && on != 1)) return PB_ERR_ARG;
+  ctx->fuse_attn = on == 1;
   return PB_OK;
 }
 

@@ -21,6 +21,7 @@ struct pb_ctx {
   bool pdl = true;              // launch matvecs with programmatic stream serialization
   int mvi_min_rows = 32768;     // fast mode: matrices of this many rows on take the int8 tensor-core matvec
   bool mvt = false;             // fast mode: the tcgen05 int8 matvec for the matrices it takes (pb_set_mvt)
+  bool fuse_attn = false;       // fast mode: decode projection + attention in one kernel (pb_set_fuse_attn)
   std::string err;
   // scratch for one-shot host-buffer calls (grown on demand)
   void* scratch = nullptr;
@@ -537,6 +538,9 @@ int pb_setup_q4_kernels(void);
 int pb_setup_mvi_kernels(void);
 int pb_launch_mvi(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows, const pb_mv_epi& epi);
 int pb_setup_mvt_kernels(void);
+// The fast-mode kernel choice of a row-layout Q4_0 matrix: true when its
+// matvecs run on k_mvf (not on k_mvi or k_mvt).
+bool pb_fast_uses_mvf(const pb_ctx* ctx, const pb_qmat* w);
 bool pb_mvt_ok(const pb_qmat* w);  // the tcgen05 int8 matvec takes the matrix
 int pb_launch_mvt(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows, const pb_mv_epi& epi);
 int pb_setup_ops_kernels(void);

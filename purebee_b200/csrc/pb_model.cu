@@ -31,6 +31,9 @@ int pb_launch_attn_decode(pb_ctx* ctx, const float* q, const float* kc, const fl
 
 int pb_attn_dec1_splits(int n_kv, int max_len, int sm_count);
 bool pb_attn_dec_fast_ok(int n_heads, int n_kv, int hd, int max_len);
+bool pb_qkv_attn_ok(const pb_qmat* w, int n_heads, int n_kv, int hd, int max_len);
+int pb_launch_qkv_attn(pb_ctx* ctx, const pb_qmat* w, const float* x, float* qkv_out, const pb_mv_epi& e, int n_heads,
+                       int n_kv, float* out);
 int pb_launch_attn_dec_fast(pb_ctx* ctx, const float* q, const float* kc, const float* vc, const int* pos_dev,
                             int n_heads, int n_kv, int hd, float* out, int max_len);
 size_t pb_attn_dec1_ws_doubles(int n_heads, int n_kv, int hd, int nsplit);
@@ -119,7 +122,7 @@ struct pb_model {
   std::vector<cudaGraph_t> lgraph;  // decode steps over the first L layers, index L
   std::vector<cudaGraphExec_t> lexec;
   int launches_per_step = 0;
-  int graph_mode = PB_MATVEC_FAST;  // matvec mode the recorded graphs were made with
+  int graph_mode = -1;  // graph_key of the context when the recorded graphs were made
   float* h_logits_pinned = nullptr;
   int* h_io_pinned = nullptr;
 };
@@ -641,8 +644,14 @@ static int run_layer_decode_q4(pb_model* m, int l) {
   e.vc = vcache(m, l);
   l2_hint(&e, 0, m->wo[l]);
   l2_hint(&e, 2, m->w2[l]);
-  PB_TRY(pb_launch_matvec(ctx, m->qkv[l], m->x, m->qkvo, 0, dim + 2 * kv, &e));
-  PB_TRY(launch_attn_decode1(m, l, m->qkvo, pos_dev));
+  if (ctx->matvec_mode == PB_MATVEC_FAST && ctx->fuse_attn && pb_fast_uses_mvf(ctx, m->qkv[l]) &&
+      pb_qkv_attn_ok(m->qkv[l], c.n_heads, c.n_kv_heads, c.head_dim, c.seq_len)) {
+    // one kernel: the 8 CTAs attending for a kv head compute its projection rows first
+    PB_TRY(pb_launch_qkv_attn(ctx, m->qkv[l], m->x, m->qkvo, e, c.n_heads, c.n_kv_heads, m->att));
+  } else {
+    PB_TRY(pb_launch_matvec(ctx, m->qkv[l], m->x, m->qkvo, 0, dim + 2 * kv, &e));
+    PB_TRY(launch_attn_decode1(m, l, m->qkvo, pos_dev));
+  }
   // wo with the residual add
   pb_mv_epi r;
   r.kind = PB_EPI_RESIDUAL;
@@ -800,12 +809,14 @@ static int ensure_sample_buffers(pb_model* m) {
   return PB_OK;
 }
 
-// Recorded graphs hold the matvec kernels of the context's matvec mode at
-// recording time; a mode change drops them so the next step records again.
+// Recorded graphs hold the kernels of the context's matvec mode and fusion
+// setting at recording time; a change drops them so the next step records
+// again.
+static int graph_key(const pb_ctx* ctx) { return ctx->matvec_mode | (ctx->fuse_attn ? 2 : 0); }
 static void check_graph_mode(pb_model* m) {
-  if (m->graph_mode != m->ctx->matvec_mode) {
+  if (m->graph_mode != graph_key(m->ctx)) {
     free_graph(m);
-    m->graph_mode = m->ctx->matvec_mode;
+    m->graph_mode = graph_key(m->ctx);
   }
 }
 

@@ -29,6 +29,9 @@
 #include <stdio.h>
 #include <stdlib.h>
 
+#include <cooperative_groups.h>
+
+#include "pb_attn_fast.cuh"
 #include "pb_internal.cuh"
 
 // ---------------------------------------------------------------------------
@@ -983,6 +986,223 @@ static int launch_mvf(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, i
                    pb_magics{PB_MAG0, PB_MAG4, PB_MAG8, PB_MAG12, PB_MAG16}, ctx->d_err);
 }
 
+// ---------------------------------------------------------------------------
+// Fused decode projection + attention (fast mode, one sequence,
+// llama-streaming.js:505-573): the RMSNorm -> [wq; wk; wv] matvec with RoPE
+// and the KV write at pos, and the decode attention, in one kernel.  Separate,
+// the attention waits for the whole projection grid to finish (a dependent
+// launch costs about 2 us per link); here the 8 CTAs that attend for kv head
+// g (one cluster, as k_attn_dec_fast) first compute g's own rows of the
+// projection -- PER q heads, k and v, (PER + 2) x 64 rows, PER + 2 8-row
+// tiles per CTA -- and meet at a cluster barrier.
+//   - before griddepcontrol.wait: the CTA's weight payloads and scales
+//     (final) and its split's K/V rows before pos into shared memory;
+//   - after it: x into shared memory, RMS-normalised as k_mvf does; each warp
+//     computes (8-row tile, 32-block chunk) units with k_mvf's block sums,
+//     scales and transposed reduction, the chunks added in order, and the
+//     tile goes through the matvec epilogue (RoPE on q and k, k and v into the
+//     cache at pos, q to y): the same bits as k_mvf;
+//   - cluster barrier (the group's q, k and v are written), then q and the
+//     row at pos (L2 reads: written by the other CTAs) and aq_attend, the
+//     attention of k_attn_dec_fast on the first 128 threads: the same bits.
+// Measured at the Llama-3.2-1B shape it is slower than the two kernels (15.6
+// against 6.3 + 5.8 us of marginal time per layer, 0.617 against 0.561 ms
+// per decode step): the projection's 768 units of 8 rows x 32 blocks run on
+// the 64 SMs of the clusters (12 per SM instead of about 5), and the
+// clusters (206 KB of shared memory per CTA with a 2048-position cache) start
+// only when 8 SMs of a GPC are free.  Off by default (pb_set_fuse_attn).
+// ---------------------------------------------------------------------------
+constexpr int QA_THREADS = 256;
+constexpr int QA_SMEM_MAX = 220 * 1024;  // dynamic shared memory (the static part is about 1 KB)
+
+static size_t qa_smem(const pb_qmat* w, int per, int pmax) {
+  const int KC = w->nb / 32, units = (per + 2) * KC;
+  return (size_t)w->K * 4 + (size_t)units * 256 * 16 + (size_t)units * 256 * 2 + (size_t)(per + 2) * KC * 8 * 4 +
+         aq_smem(per, pmax);
+}
+
+template <int PER>
+__global__ void __launch_bounds__(QA_THREADS)
+k_qkv_attn(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, int nb,
+           const float* __restrict__ x, float* __restrict__ y, pb_mv_epi epi, float scale, float* __restrict__ out,
+           int pmax, pb_magics M, int* err) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  constexpr int TPC = PER + 2;  // 8-row tiles per CTA: (PER + 2) x 64 rows over the 8 CTAs of the group
+  extern __shared__ __align__(16) unsigned char qa_raw[];
+  const int K = nb * 32, KC = nb / 32, units = TPC * KC;
+  float4* xs4 = reinterpret_cast<float4*>(qa_raw);                                  // [K / 4] swizzled
+  unsigned char* wst = qa_raw + (size_t)K * 4;                                      // [unit][8 rows][32 lanes] x 16 B
+  uint16_t* dst_s = reinterpret_cast<uint16_t*>(wst + (size_t)units * 4096);      // [unit][8 rows][32 lanes]
+  float* cpart = reinterpret_cast<float*>(dst_s + (size_t)units * 256);           // [tile][chunk][8]
+  float* ks = cpart + (size_t)TPC * KC * 8;                                         // attention: K, V, scores, q, PV
+  float* vs = ks + (size_t)pmax * AQ_KLD;
+  float* sc = vs + (size_t)pmax * AQ_HD;
+  float* qsm = sc + (size_t)PER * pmax;
+  float* gp = qsm + PER * AQ_HD;
+  __shared__ aq_parts<PER> pt;
+  __shared__ double red[4];
+  const int g = blockIdx.x, sp = (int)cl.block_rank(), nsplit = (int)cl.num_blocks(), tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int pos = *epi.pos_dev;
+  const int cache_len = pos + 1, max_len = epi.max_len;
+  const int P = (cache_len + nsplit - 1) / nsplit;
+  if (pos < 0 || cache_len > max_len || P > pmax) {  // the same for every CTA: all leave before any barrier
+    pb_pdl_trigger();
+    pb_pdl_wait();
+    if (tid == 0 && g == 0 && sp == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+    return;
+  }
+  const int qt = epi.q_rows / 8, kt = epi.kv_rows / 8;
+  auto gtile = [&](int lt) {  // local tile of the group -> 8-row tile of the matrix
+    return lt < PER * 8 ? g * PER * 8 + lt : lt < PER * 8 + 8 ? qt + g * 8 + (lt - PER * 8) : qt + kt + g * 8 + (lt - PER * 8 - 8);
+  };
+  // the CTA's weight payloads and scales: item (unit u, row r, lane), unit u =
+  // (tile u / KC, chunk u % KC), lane = block (u % KC) * 32 + lane
+  for (int i = tid; i < units * 256; i += QA_THREADS) {
+    const int u = i >> 8, r = (i >> 5) & 7, b = (u % KC) * 32 + (i & 31);
+    const int t = gtile(sp * TPC + u / KC);
+    cp_async16(wst + (size_t)i * 16, qs + ((size_t)(t * 8 + r) * nb + b) * 16);
+  }
+  for (int i = tid; i < units * 32; i += QA_THREADS) {  // 8 scales per 16-byte piece
+    const int u = i >> 5, r = (i >> 2) & 7, c = i & 3;
+    const int t = gtile(sp * TPC + u / KC);
+    cp_async16(dst_s + ((size_t)u * 8 + r) * 32 + c * 8, dsc + (size_t)(t * 8 + r) * nb + (u % KC) * 32 + c * 8);
+  }
+  // the split's K and V rows before pos (final: written by earlier steps)
+  const int kv_dim = epi.kv_rows;
+  const int j0 = sp * P;
+  const int n = cache_len - j0 < 0 ? 0 : (cache_len - j0 < P ? cache_len - j0 : P);
+  const bool has_pos = pos >= j0 && pos < j0 + n;
+  const int npre = has_pos ? n - 1 : n;
+  const float* kb = epi.kc + (size_t)g * AQ_HD;
+  const float* vb = epi.vc + (size_t)g * AQ_HD;
+  for (int i = tid; i < npre * 16; i += QA_THREADS) {
+    const int r = i >> 4, c = i & 15;
+    const size_t src = (size_t)(j0 + r) * kv_dim + 4 * c;
+    cp_async16(ks + r * AQ_KLD + 4 * c, kb + src);
+    cp_async16(vs + r * AQ_HD + 4 * c, vb + src);
+  }
+  cp_async_commit();
+  if (tid == 0) {
+    const int cta = (int)(blockIdx.y * gridDim.x + blockIdx.x), ncta = (int)(gridDim.x * gridDim.y);
+    for (int i = 0; i < PB_MAX_L2_NEXT; ++i) pb_l2_prefetch_share(epi.l2_next[i], epi.l2_next_bytes[i], cta, ncta);
+  }
+  pb_pdl_trigger();
+  pb_pdl_wait();  // x comes from the previous kernel
+  mvf_stage_x(x, epi.norm_w, epi.eps, K, xs4, red);
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  // the units, k_mvf's arithmetic: warp w takes units w, w + 8, ...
+  for (int u = warp; u < units; u += QA_THREADS / 32) {
+    const int lt = u / KC, ch = u % KC, b = ch * 32 + lane;
+    uint64_t xp[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = xs4[b * 8 + (i ^ (b & 7))];
+      xp[2 * i] = p2(v.x, v.y);
+      xp[2 * i + 1] = p2(v.z, v.w);
+    }
+    float v[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const uint4 pp = *reinterpret_cast<const uint4*>(wst + ((size_t)u * 256 + r * 32 + lane) * 16);
+      const float d = pb_f16_wasm(dst_s[((size_t)u * 8 + r) * 32 + lane]);
+      v[r] = __fmul_rn(q4_0_block_fast(pp, xp, M), d);
+    }
+    // transposed butterfly over the lanes: lane 4r ends with row r's sum
+    float w4[4], w2[2];
+    const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = b16 ? v[i] : v[i + 4], keep = b16 ? v[i + 4] : v[i];
+      w4[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = b8 ? w4[i] : w4[i + 2], keep = b8 ? w4[i + 2] : w4[i];
+      w2[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+    }
+    float z;
+    {
+      const float send = b4 ? w2[0] : w2[1], keep = b4 ? w2[1] : w2[0];
+      z = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+    }
+    z = __fadd_rn(z, __shfl_xor_sync(0xffffffffu, z, 2));
+    z = __fadd_rn(z, __shfl_xor_sync(0xffffffffu, z, 1));
+    const int row_of_lane = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    if ((lane & 3) == 0) cpart[((size_t)lt * KC + ch) * 8 + row_of_lane] = z;
+  }
+  __syncthreads();
+  // each tile: the chunks added in order, then the matvec epilogue
+  for (int lt = warp; lt < TPC; lt += QA_THREADS / 32) {
+    const int rr = lane >> 2;
+    float s_ = cpart[(size_t)lt * KC * 8 + rr];
+    for (int c = 1; c < KC; ++c) s_ = __fadd_rn(s_, cpart[((size_t)lt * KC + c) * 8 + rr]);
+    pb_mv_epilogue(s_, gtile(sp * TPC + lt), N, 0, N, y, epi, err);
+  }
+  cl.sync();  // the group's q, k and v rows are written
+  if (has_pos && tid < 32) {
+    const int r = pos - j0, c = tid & 15;
+    const float* src = (tid < 16 ? kb : vb) + (size_t)pos * kv_dim + 4 * c;
+    float* dst = tid < 16 ? ks + r * AQ_KLD + 4 * c : vs + r * AQ_HD + 4 * c;
+    *reinterpret_cast<float4*>(dst) = __ldcg(reinterpret_cast<const float4*>(src));
+  }
+  for (int i = tid; i < PER * AQ_HD / 4; i += QA_THREADS)
+    reinterpret_cast<float4*>(qsm)[i] = __ldcg(reinterpret_cast<const float4*>(y + (size_t)g * PER * AQ_HD) + i);
+  __syncthreads();
+  aq_attend<PER>(cl, ks, vs, sc, qsm, gp, pt, n, pmax, scale, out + (size_t)g * PER * AQ_HD);
+}
+
+// Whether the fused projection + attention takes the layer: the fast decode
+// attention's shape, a Q4_0 row-layout [q | k | v] matrix with K a multiple of
+// 1024, and its shared memory.
+bool pb_qkv_attn_ok(const pb_qmat* w, int n_heads, int n_kv, int hd, int max_len) {
+  if (!w || w->type != PB_TYPE_Q4_0 || w->layout != PB_LAYOUT_ROWS || w->nb % 32 || hd != AQ_HD || n_kv <= 0 ||
+      n_heads % n_kv || n_heads / n_kv > AQ_MAX_SPLIT || w->N != (n_heads + 2 * n_kv) * hd)
+    return false;
+  const int pmax = (max_len + AQ_MAX_SPLIT - 1) / AQ_MAX_SPLIT;
+  return pmax <= AQ_MAXP && qa_smem(w, n_heads / n_kv, pmax) <= (size_t)QA_SMEM_MAX;
+}
+
+// The projection of e (RoPE + KV epilogue, its norm and L2 hints) and the
+// decode attention into out, in one launch.
+int pb_launch_qkv_attn(pb_ctx* ctx, const pb_qmat* w, const float* x, float* qkv_out, const pb_mv_epi& e, int n_heads,
+                       int n_kv, float* out) {
+  if (e.kind != PB_EPI_ROPE_KV || !e.pos_dev || !pb_qkv_attn_ok(w, n_heads, n_kv, e.head_dim, e.max_len))
+    return pb_set_error(ctx, PB_ERR_ARG, "fused projection + attention: unsupported shape");
+  const int per = n_heads / n_kv, pmax = (e.max_len + AQ_MAX_SPLIT - 1) / AQ_MAX_SPLIT;
+  const float scale = (float)(1.0 / sqrt((double)e.head_dim));  // llama-streaming.js:546
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_kv, AQ_MAX_SPLIT);
+  cfg.blockDim = dim3(QA_THREADS);
+  cfg.dynamicSmemBytes = qa_smem(w, per, pmax);
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = AQ_MAX_SPLIT;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = ctx->pdl ? 2 : 1;
+  const pb_magics M{PB_MAG0, PB_MAG4, PB_MAG8, PB_MAG12, PB_MAG16};
+  cudaError_t err = cudaErrorInvalidValue;
+  switch (per) {
+#define PB_QA_CASE(P)                                                                                           \
+  case P:                                                                                                       \
+    err = cudaLaunchKernelEx(&cfg, k_qkv_attn<P>, (const uint8_t*)w->qs, (const uint16_t*)w->d, w->N, w->nb, x, \
+                             qkv_out, e, scale, out, pmax, M, ctx->d_err);                                      \
+    break;
+    PB_QA_CASE(1) PB_QA_CASE(2) PB_QA_CASE(3) PB_QA_CASE(4) PB_QA_CASE(5) PB_QA_CASE(6) PB_QA_CASE(7) PB_QA_CASE(8)
+#undef PB_QA_CASE
+    default: break;
+  }
+  if (err != cudaSuccess) return pb_cuda_error(ctx, err, "k_qkv_attn");
+  return pb_check_launch(ctx, "k_qkv_attn");
+}
+
 // The LM head in the fast mode: the fast kernel over the head table (Q4_0 /
 // Q8_0, either layout) with the final RMSNorm prologue and the logits +
 // greedy argmax epilogue.  The exact kernel (k_head) keeps batch_dot's order.
@@ -1034,6 +1254,10 @@ static int launch_mv(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, in
                      pb_magics{PB_MAG0, PB_MAG4, PB_MAG8, PB_MAG12, PB_MAG16}, ctx->d_err);
   }
   return launch_mv_nt<TYPE, MV_THREADS>(ctx, w, x, y, tile_begin, ntiles, row_end, epi);
+}
+
+bool pb_fast_uses_mvf(const pb_ctx* ctx, const pb_qmat* w) {
+  return !(ctx->mvt && pb_mvt_ok(w)) && !(w->mq && w->mma_ok && w->layout == PB_LAYOUT_ROWS && w->N >= ctx->mvi_min_rows);
 }
 
 int pb_launch_matvec(pb_ctx* ctx, const pb_qmat* w, const float* x, float* y, int row0, int rows,
@@ -1635,6 +1859,9 @@ int pb_setup_q4_kernels(void) {
   e = e ? e : cudaFuncSetAttribute(k_head_f32_double, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_head_f32_bd, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  for (auto k : {k_qkv_attn<1>, k_qkv_attn<2>, k_qkv_attn<3>, k_qkv_attn<4>, k_qkv_attn<5>, k_qkv_attn<6>,
+                 k_qkv_attn<7>, k_qkv_attn<8>})
+    e = e ? e : cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, QA_SMEM_MAX);
   e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_ROWS, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   e = e ? e : cudaFuncSetAttribute(k_mvf<PB_TYPE_Q4_0, PB_LAYOUT_TILED8>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);

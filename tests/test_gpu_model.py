@@ -206,6 +206,39 @@ def test_teacher_forced_random_tokens(native, ctx, oracle, name, n_prompt, n_ste
     rt.shutdown()
 
 
+def test_fused_projection_attention_same_bits(native, ctx, oracle):
+    """The fast mode's fused decode projection + attention (pb_set_fuse_attn)
+    gives the same logits, bit for bit, as the projection and attention
+    kernels run apart, at the Llama-3.2-1B shape and its 2048-position cache
+    (the benchmark's model), over steps that cross the attention's position
+    splits; and stays within LOGIT_RTOL of the oracle.  The launch count
+    shows which path ran: one kernel fewer per layer fused."""
+    kw = CONFIGS["llama1B"]
+    rt, om = make_pair(ctx, kw, 7, copy_weights_from_device=True)
+    toks = oracle.synth_tokens(16 + 96, 78, 1, kw["vocab"]).tolist()
+    runs, launches = [], []
+    for fuse in (True, False):
+        ctx.set_fuse_attn(fuse)
+        rt.resetCache()
+        rt.forward(toks[:16], 0)
+        steps = []
+        for pos in range(16, 16 + 96):
+            nxt, lg = rt.model.decode(toks[pos], pos, True)
+            steps.append((nxt, lg.copy()))
+        runs.append(steps)
+        launches.append(native.lib().pb_model_decode_launches(rt.model.h))
+    ctx.set_fuse_attn(False)
+    assert launches[0] == launches[1] - kw["n_layers"], launches
+    for (t1, l1), (t2, l2) in zip(*runs):
+        assert t1 == t2 and np.array_equal(l1.view(np.uint32), l2.view(np.uint32))
+    om_lg = om.forward(toks[:16], 0)
+    for i, pos in enumerate(range(16, 16 + 96)):
+        lg_orc = om.forward([toks[pos]], pos)
+        if i % 19 == 0:
+            assert np.max(np.abs(runs[0][i][1] - lg_orc)) <= LOGIT_RTOL * np.max(np.abs(lg_orc)), pos
+    rt.shutdown()
+
+
 def test_device_loop_equals_host_loop(native, ctx):
     """The replayed decode graph with the token kept on the device gives the
     same tokens as host-driven steps; KV rollback restores a position."""
