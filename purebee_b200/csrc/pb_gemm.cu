@@ -596,13 +596,100 @@ __global__ void k_splitk_reduce(const float* __restrict__ ws, int splits, int M,
   }
 }
 
+// k_splitk_reduce for a STORE / ADD GEMM followed by an RMSNorm (epi.norm_w):
+// one CTA of 1024 threads per row m.  Each value is k_splitk_reduce's (the
+// splits' partials summed in ascending order from 0, four loads in flight at
+// a time, then stored or added to C) and goes to shared memory; the row is then normalised with
+// k_rmsnorm_t's arithmetic: its first 256 threads take k_rmsnorm_t's values
+// (d = t, t + 256, ...) for the sum of squares, the other warps add exact
+// zeros to the same block sum.  So the output has the bits of the reduce and
+// the norm launched apart.
+constexpr int RN_THREADS = 1024, RN_NORM_THREADS = 256;
+__global__ void __launch_bounds__(RN_THREADS)
+k_splitk_reduce_norm(const float* __restrict__ ws, int splits, int M, int N, float* __restrict__ C, pb_gemm_epi epi) {
+  extern __shared__ float rn_row[];  // [N]
+  __shared__ double red[32];
+  const int m = blockIdx.x, tid = threadIdx.x;
+  pb_pdl_trigger();
+  pb_pdl_wait();  // the partials come from the GEMM before
+  for (int d = tid; d < N; d += RN_THREADS) {
+    // the splits in ascending order, four loads in flight at a time
+    const float* src = ws + (size_t)m * N + d;
+    const size_t zs = (size_t)M * N;
+    float acc = 0.0f;
+    int z = 0;
+    for (; z + 4 <= splits; z += 4) {
+      const float p0 = src[z * zs], p1 = src[(z + 1) * zs], p2 = src[(z + 2) * zs], p3 = src[(z + 3) * zs];
+      acc += p0;
+      acc += p1;
+      acc += p2;
+      acc += p3;
+    }
+    for (; z < splits; ++z) acc += src[z * zs];
+    float* c = C + (size_t)m * N + d;
+    const float v = epi.mode == PB_GEMM_ADD ? __fadd_rn(*c, acc) : acc;
+    *c = v;
+    rn_row[d] = v;
+  }
+  __syncthreads();
+  double ss = 0.0;
+  if (tid < RN_NORM_THREADS)
+    for (int d = tid; d < N; d += RN_NORM_THREADS) {
+      const double dv = (double)rn_row[d];
+      ss = __fma_rn(dv, dv, ss);
+    }
+  ss = pb_block_sum_d(ss, red);
+  const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)N), epi.norm_eps));
+  const float inv = (float)(1.0 / rms);
+  const float* w = epi.norm_w;
+  for (int d = tid; d < N; d += RN_THREADS) {
+    const float v = rn_row[d];
+    if (epi.norm_out16 && epi.norm_hl) pb_store_hl(epi.norm_out16, pb_hl_index((size_t)m * 2 * N, d), v * inv * w[d]);
+    else if (epi.norm_out16) epi.norm_out16[(size_t)m * N + d] = __float2half_rn(v * inv * w[d]);
+    else epi.norm_out[(size_t)m * N + d] = (float)__dmul_rn(__ddiv_rn((double)v, rms), (double)w[d]);
+  }
+}
+
+// The split-K partials of ws summed into C (and, when the GEMM is followed
+// by its RMSNorm and the shapes allow, normalised in the same kernel:
+// *norm_done).
+static int launch_reduce(pb_ctx* ctx, const float* ws, int splits, int M, int N, float* C, int ldc,
+                         const pb_gemm_epi& epi, bool* norm_done) {
+  if (epi.norm_w && epi.mode != PB_GEMM_SWIGLU && epi.xs.world == 0 && ldc == N && (size_t)N * 4 <= 48 * 1024) {
+    *norm_done = true;
+    return pb_launch(ctx, "k_splitk_reduce_norm", true, k_splitk_reduce_norm, dim3(M), dim3(RN_THREADS), (size_t)N * 4,
+                     ws, splits, M, N, C, epi);
+  }
+  const int cols = epi.mode == PB_GEMM_SWIGLU ? N / 2 : N;
+  return pb_launch(ctx, "k_splitk_reduce", true, k_splitk_reduce, dim3(pb_cdiv(cols, 256), M), dim3(256), 0, ws,
+                   splits, M, N, C, ldc, epi);
+}
+
 bool pb_gemm_uses_tma(const pb_qmat* w, int M) { return M >= PB_GEMM_TMA_MIN_M && w->K % TG_K == 0; }
 static int launch_gemm_ws(pb_ctx* ctx, const pb_qmat* w, const __half* Xh, int M, float* C, int ldc, float* ws,
-                          size_t ws_bytes, const pb_gemm_epi& epi);
+                          size_t ws_bytes, const pb_gemm_epi& epi, bool* norm_done);
+
+static int launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
+                          size_t ws_bytes, const pb_gemm_epi& epi, const __half* Xh, bool* norm_done);
 
 int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
                       size_t ws_bytes, const pb_gemm_epi* epi_in, const __half* Xh) {
   const pb_gemm_epi epi = epi_in ? *epi_in : pb_gemm_epi();
+  if (epi.norm_w && (epi.mode == PB_GEMM_SWIGLU || epi.xs.world > 0 || ldc != (w ? w->N : 0) ||
+                     !(epi.norm_out || epi.norm_out16)))
+    return pb_set_error(ctx, PB_ERR_ARG, "a GEMM's RMSNorm needs a STORE / ADD row-major C and an output");
+  bool norm_done = false;
+  PB_TRY(launch_q4_gemm(ctx, w, X, ldx, M, C, ldc, ws, ws_bytes, epi, Xh, &norm_done));
+  if (epi.norm_w && !norm_done) {
+    pb_launch_rmsnorm(ctx->stream, C, M, w->N, epi.norm_w, epi.norm_eps, epi.norm_out, epi.norm_out16, 0, epi.norm_hl,
+                      ctx->pdl);
+    PB_LAUNCHED(ctx, "k_rmsnorm");
+  }
+  return PB_OK;
+}
+
+static int launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, int M, float* C, int ldc, float* ws,
+                          size_t ws_bytes, const pb_gemm_epi& epi, const __half* Xh, bool* norm_done) {
   if (!ctx || !w || !(X || Xh) || M <= 0) return PB_ERR_ARG;
   if (epi.mode == PB_GEMM_SWIGLU ? (!(epi.h16 || epi.h32) || w->N % 8) : !C) return PB_ERR_ARG;
   if (w->type != PB_TYPE_Q4_0) return pb_set_error(ctx, PB_ERR_ARG, "the tensor-core GEMM needs a Q4_0 matrix");
@@ -612,7 +699,7 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
     return pb_set_error(ctx, PB_ERR_ARG, "column chunks of %d do not tile K=%d in steps of 64", epi.x_chunk, w->K);
   if (Xh && ((uintptr_t)Xh & 15)) return pb_set_error(ctx, PB_ERR_ARG, "f16 X must be 16-byte aligned");
   if (pb_gemm_uses_tma(w, M)) return launch_gemm_tma(ctx, w, X, Xh, ldx, M, C, ldc, epi);
-  if (Xh && pb_gemm_uses_ws(w, M)) return launch_gemm_ws(ctx, w, Xh, M, C, ldc, ws, ws_bytes, epi);
+  if (Xh && pb_gemm_uses_ws(w, M)) return launch_gemm_ws(ctx, w, Xh, M, C, ldc, ws, ws_bytes, epi, norm_done);
   if (!X)
     return pb_set_error(ctx, PB_ERR_ARG, "f16 activations need M >= %d or M <= 64", PB_GEMM_TMA_MIN_M);
   const int tok = M <= 64 ? 64 : GM_TOK;
@@ -657,11 +744,7 @@ int pb_launch_q4_gemm(pb_ctx* ctx, const pb_qmat* w, const float* X, int ldx, in
   PB_TRY(pb_launch(ctx, "k_q4_gemm_tc", true, kern, grid, dim3(GM_THREADS), gm_smem(epi.terms), (const uint8_t*)w->qs,
                    (const uint16_t*)w->d, w->layout, w->N, w->N_pad, w->nb, X, ldx, M, dst, ldd, kper, kepi,
                    ctx->d_err));
-  if (splits > 1) {
-    const int cols = epi.mode == PB_GEMM_SWIGLU ? w->N / 2 : w->N;
-    PB_TRY(pb_launch(ctx, "k_splitk_reduce", true, k_splitk_reduce, dim3(pb_cdiv(cols, 256), M), dim3(256), 0,
-                     (const float*)ws, splits, M, w->N, C, ldc, epi));
-  }
+  if (splits > 1) PB_TRY(launch_reduce(ctx, ws, splits, M, w->N, C, ldc, epi, norm_done));
   return PB_OK;
 }
 
@@ -989,7 +1072,7 @@ bool pb_gemm_uses_ws(const pb_qmat* w, int M) {
 }
 
 static int launch_gemm_ws(pb_ctx* ctx, const pb_qmat* w, const __half* Xh, int M, float* C, int ldc, float* ws,
-                          size_t ws_bytes, const pb_gemm_epi& epi) {
+                          size_t ws_bytes, const pb_gemm_epi& epi, bool* norm_done) {
   const int ktot = w->K / GW_K;
   dim3 grid(pb_cdiv(w->N, GW_ROWS), 1, 1);
   int splits = 1;
@@ -1028,11 +1111,7 @@ static int launch_gemm_ws(pb_ctx* ctx, const pb_qmat* w, const __half* Xh, int M
   PB_TRY(pb_launch(ctx, "k_q4_gemm_ws", true, kern, grid, dim3(GW_THREADS), gw_smem(epi.terms), mq, mx,
                    (const uint8_t*)w->qs, (const uint16_t*)w->d, w->layout, w->N, w->N_pad, w->nb, M, xkc, dst, ldd,
                    kper, kepi, ctx->d_err));
-  if (splits > 1) {
-    const int cols = epi.mode == PB_GEMM_SWIGLU ? w->N / 2 : w->N;
-    PB_TRY(pb_launch(ctx, "k_splitk_reduce", true, k_splitk_reduce, dim3(pb_cdiv(cols, 256), M), dim3(256), 0,
-                     (const float*)ws, splits, M, w->N, C, ldc, epi));
-  }
+  if (splits > 1) PB_TRY(launch_reduce(ctx, ws, splits, M, w->N, C, ldc, epi, norm_done));
   return PB_OK;
 }
 

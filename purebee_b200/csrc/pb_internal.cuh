@@ -458,6 +458,16 @@ struct pb_gemm_epi {
   // and h16 goes out, in the hi/lo layout below)
   int terms = 1;
   pb_xsend xs;  // PB_GEMM_ADD: the fused residual exchange (row split, decode steps)
+  // The RMSNorm after the GEMM (norm_w set; C row-major with ldc == N, no
+  // exchange): each finished row of C, normalised with weights norm_w as
+  // k_rmsnorm_t does, into norm_out (f32) or norm_out16 (f16, hi/lo pairs
+  // with norm_hl).  A split-K reduce does it in the same kernel; otherwise
+  // pb_launch_q4_gemm launches k_rmsnorm_t after the GEMM.  Same bits either way.
+  const float* norm_w = nullptr;
+  double norm_eps = 1e-5;
+  float* norm_out = nullptr;
+  __half* norm_out16 = nullptr;
+  int norm_hl = 0;
 };
 
 // The hi/lo f16 layout of the three-term GEMM operands: a value v is the

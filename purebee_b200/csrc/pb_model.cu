@@ -1768,7 +1768,7 @@ static bool dec16(const pb_batch* b, const pb_shard& s, int l, int rows) {
 // norm -> this rank's q | k | v -> RoPE + KV append -> attention of its heads
 // into its chunk of att.
 static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_per_seq, int start_pos,
-                           const int* pos_dev, bool recv_x = false) {
+                           const int* pos_dev, bool recv_x = false, bool normed = false) {
   pb_model* m = b->m;
   pb_ctx* ctx = m->ctx;
   const pb_model_config& c = m->c;
@@ -1789,11 +1789,11 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
                                    f16 ? xn16 : nullptr, dc, f16 && b->terms == 3, xrecv_of(b)));
     if (f16) PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], nullptr, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st, xn16));
     else PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], s.xn, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st));
-  } else if (pb_gemm_uses_tma(s.qkv[l], rows) || d16) {
-    PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, nullptr, xn16, dc, b->terms == 3));
+  } else if (pb_gemm_uses_tma(s.qkv[l], rows) || d16) {  // (normed: the previous down GEMM ran this norm)
+    if (!normed) PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, nullptr, xn16, dc, b->terms == 3));
     PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], nullptr, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st, xn16));
   } else {
-    PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, s.xn, nullptr, dc));
+    if (!normed) PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, s.xn, nullptr, dc));
     PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], s.xn, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st));
   }
   {
@@ -1825,7 +1825,21 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
 
 // this rank's rows of wo with the residual add into its chunk of x
 // (llama-streaming.js:579-580)
-static int shard_wo(pb_batch* b, pb_shard& s, int l, int rows, bool send_x = false) {
+// One process holding the whole model (no row split): a residual GEMM (wo,
+// down) also runs the RMSNorm that comes next (pb_gemm_epi::norm_w), into
+// the operand the next GEMM reads; its split-K reduce and the norm are then
+// one kernel.  The same bits as the norm launched by the next phase.
+static bool norm_in_gemm(const pb_batch* b) { return b->world == 1 && b->sh.size() == 1; }
+
+static void set_norm(pb_batch* b, pb_shard& s, pb_gemm_epi& e, const float* w, bool f16) {
+  e.norm_w = w;
+  e.norm_eps = b->m->c.eps;
+  e.norm_out = f16 ? nullptr : s.xn;
+  e.norm_out16 = f16 ? reinterpret_cast<__half*>(s.xn) : nullptr;
+  e.norm_hl = f16 && b->terms == 3;
+}
+
+static int shard_wo(pb_batch* b, pb_shard& s, int l, int rows, bool send_x = false, bool norm_next = false) {
   pb_model* m = b->m;
   const int dc = s.p.dim_chunk;
   pb_gemm_epi add;
@@ -1834,6 +1848,8 @@ static int shard_wo(pb_batch* b, pb_shard& s, int l, int rows, bool send_x = fal
   add.split_n = m->c.dim;
   add.terms = b->terms;
   if (send_x) add.xs = xsend_of(b, dc);
+  if (norm_next)  // the FFN norm, into the gate|up GEMM's operand
+    set_norm(b, s, add, m->rms_ffn + (size_t)l * m->c.dim, pb_gemm_uses_tma(s.gu[l], rows) || dec16(b, s, l, rows));
   if (dec16(b, s, l, rows))
     return pb_launch_q4_gemm(m->ctx, s.wo[l], nullptr, m->c.dim, rows, s.x + (size_t)s.rank * rows * dc, dc, b->ws,
                              b->ws_bytes, &add, reinterpret_cast<const __half*>(s.att));
@@ -1847,7 +1863,7 @@ static bool hidden_f16(const pb_batch* b, const pb_shard& s, int l, int rows) {
 
 // norm -> this rank's gate|up rows with SwiGLU in the epilogue, h into its
 // chunk of hb (f16 for the TMA path of w2, f32 otherwise)
-static int shard_gate_up(pb_batch* b, pb_shard& s, int l, int rows, bool recv_x = false) {
+static int shard_gate_up(pb_batch* b, pb_shard& s, int l, int rows, bool recv_x = false, bool normed = false) {
   pb_model* m = b->m;
   pb_ctx* ctx = m->ctx;
   const int dim = m->c.dim, fc = s.p.hidden_chunk;
@@ -1856,7 +1872,7 @@ static int shard_gate_up(pb_batch* b, pb_shard& s, int l, int rows, bool recv_x 
   if (recv_x)  // x's other chunks arrive with the norm (fused exchange)
     PB_TRY(pb_launch_rmsnorm_xrecv(ctx, s.x, rows, dim, m->rms_ffn + (size_t)l * dim, m->c.eps, gu16 ? nullptr : s.xn,
                                    gu16 ? xn16 : nullptr, s.p.dim_chunk, gu16 && b->terms == 3, xrecv_of(b)));
-  else
+  else if (!normed)  // (normed: the wo GEMM ran this norm)
     PB_TRY(launch_norm(m, s.x, rows, m->rms_ffn + (size_t)l * dim, gu16 ? nullptr : s.xn, gu16 ? xn16 : nullptr,
                        s.p.dim_chunk, b->terms == 3));
   pb_gemm_epi glu;
@@ -1871,7 +1887,7 @@ static int shard_gate_up(pb_batch* b, pb_shard& s, int l, int rows, bool recv_x 
 }
 
 // this rank's rows of w2 with the residual add into its chunk of x (:601)
-static int shard_down(pb_batch* b, pb_shard& s, int l, int rows, bool send_x = false) {
+static int shard_down(pb_batch* b, pb_shard& s, int l, int rows, bool send_x = false, bool norm_next = false) {
   pb_model* m = b->m;
   const int F = m->c.hidden_dim, dc = s.p.dim_chunk;
   pb_gemm_epi add;
@@ -1880,6 +1896,9 @@ static int shard_down(pb_batch* b, pb_shard& s, int l, int rows, bool send_x = f
   add.split_n = m->c.dim;
   add.terms = b->terms;
   if (send_x) add.xs = xsend_of(b, dc);
+  if (norm_next)  // the next layer's attention norm, into its qkv GEMM's operand
+    set_norm(b, s, add, m->rms_att + (size_t)(l + 1) * m->c.dim,
+             pb_gemm_uses_tma(s.qkv[l + 1], rows) || dec16(b, s, l + 1, rows));
   float* C = s.x + (size_t)s.rank * rows * dc;
   if (hidden_f16(b, s, l, rows))
     return pb_launch_q4_gemm(m->ctx, s.w2[l], nullptr, F, rows, C, dc, b->ws, b->ws_bytes, &add,
@@ -1898,15 +1917,18 @@ static int batch_layer(pb_batch* b, int l, int rows, int rows_per_seq, int start
   const size_t achunk = dec16(b, b->sh[0], l, rows) ? dchunk / 2 * op_halves(b) : dchunk;
   // fused residual exchanges: the wo / down GEMMs send, the next norm receives
   const bool fx = fused_x(b, rows);
-  for (auto& s : b->sh) PB_TRY(shard_attention(b, s, l, rows, rows_per_seq, start_pos, pos_dev, fx && l > 0));
+  // one process with the whole model: the residual GEMMs run the next norms
+  const bool ng = !fx && norm_in_gemm(b);
+  for (auto& s : b->sh)
+    PB_TRY(shard_attention(b, s, l, rows, rows_per_seq, start_pos, pos_dev, fx && l > 0, ng && l > 0));
   PB_TRY(batch_gather(b, XG_ATT, achunk));
-  for (auto& s : b->sh) PB_TRY(shard_wo(b, s, l, rows, fx));
+  for (auto& s : b->sh) PB_TRY(shard_wo(b, s, l, rows, fx, ng));
   if (!fx) PB_TRY(batch_gather(b, XG_X, dchunk));
-  for (auto& s : b->sh) PB_TRY(shard_gate_up(b, s, l, rows, fx));
+  for (auto& s : b->sh) PB_TRY(shard_gate_up(b, s, l, rows, fx, ng));
   const size_t hchunk =
       (size_t)rows * (c.hidden_dim / b->world) * (hidden_f16(b, b->sh[0], l, rows) ? 2 * op_halves(b) : 4);
   PB_TRY(batch_gather(b, XG_HB, hchunk));
-  for (auto& s : b->sh) PB_TRY(shard_down(b, s, l, rows, fx));
+  for (auto& s : b->sh) PB_TRY(shard_down(b, s, l, rows, fx, ng && l + 1 < c.n_layers));
   return fx ? PB_OK : batch_gather(b, XG_X, dchunk);
 }
 
