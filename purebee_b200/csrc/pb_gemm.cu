@@ -303,6 +303,20 @@ constexpr uint32_t TG_IDESC = (1u << 4) | ((uint32_t)(TG_TOK >> 3) << 17) | ((ui
 
 namespace {
 
+// Tile t of the persistent GEMM in panel order: panels of TG_PANEL weight-row
+// blocks, within a panel the token blocks in turn and the panel's row blocks
+// within each, so the tiles in flight at once (one per SM) share a panel of
+// W and a few token blocks of X that L2 holds.  (Row blocks fastest swept the
+// whole weight for every token block.)  Only the schedule changes.
+constexpr int TG_PANEL = 16;
+__device__ __forceinline__ void tg_tile(int t, int ntn, int ntm, int& n0, int& m0) {
+  const int panel = t / (TG_PANEL * ntm);
+  const int pn = ntn - panel * TG_PANEL < TG_PANEL ? ntn - panel * TG_PANEL : TG_PANEL;
+  const int within = t - panel * TG_PANEL * ntm;
+  n0 = (panel * TG_PANEL + within % pn) * TG_ROWS;
+  m0 = (within / pn) * TG_TOK;
+}
+
 __device__ __forceinline__ void mma_f16_n256(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -417,7 +431,8 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
     int g = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-      const int n0 = (t % ntn) * TG_ROWS, m0 = (t / ntn) * TG_TOK;
+      int n0, m0;
+      tg_tile(t, ntn, ntm, n0, m0);
       for (int ks = 0; ks < ksteps; ++ks, ++g) {
         const int s = g % NST;
         if (g >= NST && !(ok = pb_mbar_wait(&empty[s], ((g / NST) - 1) & 1, err))) break;
@@ -474,7 +489,8 @@ k_gemm_f16_tma(const __grid_constant__ CUtensorMap map_w, const __grid_constant_
       const int b = i & 1;
       if (!pb_mbar_wait(&acc_full[b], (i >> 1) & 1, err)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int n0 = (t % ntn) * TG_ROWS, m0 = (t / ntn) * TG_TOK;
+      int n0, m0;
+      tg_tile(t, ntn, ntm, n0, m0);
       const int row = n0 + q * 32 + lane;
 #pragma unroll 1
       for (int c0 = half * (TG_TOK / 2); c0 < (half + 1) * (TG_TOK / 2); c0 += 32) {

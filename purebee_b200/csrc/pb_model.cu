@@ -50,7 +50,7 @@ __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __re
                           const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
                           const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
                           float* __restrict__ kc, float* __restrict__ vc, int max_len, int rows_per_seq,
-                          int64_t cache_seq_stride, int* err);
+                          int64_t cache_seq_stride, int* err, int rows, int rows_per_cta);
 __global__ void k_glu(const float* __restrict__ g, int g_stride, const float* __restrict__ u, int u_stride, int F,
                       int mode, int interleave4, float* __restrict__ out);
 __global__ void k_embed(int type, const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc,
@@ -578,6 +578,10 @@ extern "C" int pb_model_get_tensor(pb_model* m, int layer, int which, void* host
 // forward
 // ---------------------------------------------------------------------------
 
+// Rows of k_rope_kv per CTA: one for decode batches (many CTAs for few rows),
+// 16 at prefill sizes (458K CTAs of 128 elements per layer otherwise).
+static int rope_rows_per_cta(int rows) { return rows >= 4096 ? 16 : 1; }
+
 static int launch_norm(pb_model* m, const float* x, int M, const float* w, float* out, __half* out16 = nullptr,
                        int xc = 0, int hl = 0) {
   pb_launch_rmsnorm(m->ctx->stream, x, M, m->c.dim, w, m->c.eps, out, out16, xc, hl, m->ctx->pdl);
@@ -703,10 +707,10 @@ static int run_layer(pb_model* m, int l, int M, int start_pos, bool dev_pos) {
   }
   {
     int tot = (c.n_heads + c.n_kv_heads) * (c.head_dim / 2) + kv;
-    k_rope_kv<<<dim3(pb_cdiv(tot, 128), M), 128, 0, ctx->stream>>>(q, qs_, k, ks_, v, vs_, c.n_heads, c.n_kv_heads,
-                                                                   c.head_dim, m->rope_tab, start_pos, pos_dev,
-                                                                   kcache(m, l), vcache(m, l), c.seq_len, M, 0,
-                                                                   ctx->d_err);
+    const int rpc = rope_rows_per_cta(M);
+    k_rope_kv<<<dim3(pb_cdiv(tot, 128), pb_cdiv(M, rpc)), 128, 0, ctx->stream>>>(
+        q, qs_, k, ks_, v, vs_, c.n_heads, c.n_kv_heads, c.head_dim, m->rope_tab, start_pos, pos_dev, kcache(m, l),
+        vcache(m, l), c.seq_len, M, 0, ctx->d_err, M, rpc);
     PB_LAUNCHED(ctx, "k_rope_kv");
   }
   if (M == 1 && pos_dev && (m->attn_ws || pb_attn_decode_ok(c.n_heads, c.n_kv_heads, c.head_dim, c.seq_len)))
@@ -1797,12 +1801,12 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
     PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], s.xn, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st));
   }
   {
-    const int tot = (p.n_heads + p.n_kv_heads) * (hd / 2) + kvl;
-    PB_TRY(pb_launch(ctx, "k_rope_kv", true, k_rope_kv, dim3(pb_cdiv(tot, 128), rows), dim3(128), 0, s.qkvo, qw,
-                     (const float*)(s.qkvo + p.n_heads * hd), qw,
+    const int tot = (p.n_heads + p.n_kv_heads) * (hd / 2) + kvl, rpc = rope_rows_per_cta(rows);
+    PB_TRY(pb_launch(ctx, "k_rope_kv", true, k_rope_kv, dim3(pb_cdiv(tot, 128), pb_cdiv(rows, rpc)), dim3(128), 0,
+                     s.qkvo, qw, (const float*)(s.qkvo + p.n_heads * hd), qw,
                      (const float*)(s.qkvo + (p.n_heads + p.n_kv_heads) * hd), qw, p.n_heads, p.n_kv_heads, hd,
                      (const double2*)m->rope_tab, start_pos, pos_dev, kc, vc, c.seq_len, rows_per_seq, cache_seq,
-                     ctx->d_err));
+                     ctx->d_err, rows, rpc));
   }
   float* att = s.att + (size_t)s.rank * rows * dc;
   pb_seq_geo geo;

@@ -40,25 +40,48 @@ __global__ void k_rmsnorm_t(const float* __restrict__ x, int dim, const float* _
   const float* xr = x + row * (CH ? xc : dim);
   const size_t cs = (size_t)gridDim.x * xc;
   auto X = [&](int d) { return CH ? xr[(size_t)(d / xc) * cs + d % xc] : xr[d]; };
+  // each thread's values d = t, t + blockDim, ... are loaded once, together,
+  // and kept (up to RMS_KEEP of them; longer rows read again below)
+  constexpr int RMS_KEEP = 8;  // a 2048-wide row at 256 threads
+  const int nt = blockDim.x;
+  float xv[RMS_KEEP];
   double ss = 0.0;
-  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+#pragma unroll
+  for (int k = 0; k < RMS_KEEP; ++k) {
+    const int d = threadIdx.x + k * nt;
+    if (d < dim) xv[k] = X(d);
+  }
+#pragma unroll
+  for (int k = 0; k < RMS_KEEP; ++k) {
+    const int d = threadIdx.x + k * nt;
+    if (d < dim) {
+      const double v = (double)xv[k];
+      ss = __fma_rn(v, v, ss);
+    }
+  }
+  for (int d = threadIdx.x + RMS_KEEP * nt; d < dim; d += nt) {
     const double v = (double)X(d);
     ss = __fma_rn(v, v, ss);
   }
   ss = pb_block_sum_d(ss, red);
   double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)dim), eps));
-  if (out16) {
-    const float inv = (float)(1.0 / rms);
-    if (hl) {  // the three-term GEMM operand: hi/lo pairs (pb_hl_index)
-      for (int d = threadIdx.x; d < dim; d += blockDim.x)
-        pb_store_hl(out16, pb_hl_index((size_t)row * 2 * dim, d), X(d) * inv * w[d]);
-      return;
+  auto XV = [&](int k, int d) { return k < RMS_KEEP ? xv[k] : X(d); };
+  const float inv = (float)(1.0 / rms);
+#pragma unroll
+  for (int k = 0; k < RMS_KEEP; ++k) {
+    const int d = threadIdx.x + k * nt;
+    if (d < dim) {
+      if (out16 && hl) pb_store_hl(out16, pb_hl_index((size_t)row * 2 * dim, d), xv[k] * inv * w[d]);
+      else if (out16) out16[row * dim + d] = __float2half_rn(xv[k] * inv * w[d]);
+      else out[row * dim + d] = (float)__dmul_rn(__ddiv_rn((double)xv[k], rms), (double)w[d]);
     }
-    for (int d = threadIdx.x; d < dim; d += blockDim.x) out16[row * dim + d] = __float2half_rn(X(d) * inv * w[d]);
-    return;
   }
-  for (int d = threadIdx.x; d < dim; d += blockDim.x)
-    out[row * dim + d] = (float)__dmul_rn(__ddiv_rn((double)X(d), rms), (double)w[d]);
+  for (int d = threadIdx.x + RMS_KEEP * nt, k = RMS_KEEP; d < dim; d += nt, ++k) {
+    const float xd = XV(k, d);
+    if (out16 && hl) pb_store_hl(out16, pb_hl_index((size_t)row * 2 * dim, d), xd * inv * w[d]);
+    else if (out16) out16[row * dim + d] = __float2half_rn(xd * inv * w[d]);
+    else out[row * dim + d] = (float)__dmul_rn(__ddiv_rn((double)xd, rms), (double)w[d]);
+  }
 }
 
 // The RMSNorm that ends the row split's fused residual exchange (decode
@@ -901,43 +924,42 @@ __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __re
                           const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
                           const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
                           float* __restrict__ kc, float* __restrict__ vc, int max_len, int rows_per_seq,
-                          int64_t cache_seq_stride, int* err) {
-  int t = blockIdx.y;  // row; rows of sequence s are s*rows_per_seq .. +rows_per_seq-1
+                          int64_t cache_seq_stride, int* err, int rows, int rows_per_cta) {
   pb_pdl_trigger();
   pb_pdl_wait();  // q, k, v come from the projection
-  const int sq = t / rows_per_seq;
-  kc += sq * cache_seq_stride;
-  vc += sq * cache_seq_stride;
-  int pos = (pos_dev ? *pos_dev : start_pos) + (t - sq * rows_per_seq);
-  if (pos < 0 || pos >= max_len) {
-    if (threadIdx.x == 0 && blockIdx.x == 0) pb_raise(err, PB_DEVERR_BOUNDS);
-    return;
-  }
-  int half = hd / 2, kv_dim = n_kv * hd;
-  int nq = n_heads * half, nk = n_kv * half;
-  int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx < nq + nk) {
-    bool isq = idx < nq;
-    int rel = isq ? idx : idx - nq;
-    int h = rel / half, pr = rel % half;
-    double2 cs = tab[(size_t)pos * half + pr];
-    size_t off = (size_t)h * hd + 2 * pr;
-    const float* src = isq ? q + (size_t)t * q_stride + off : k + (size_t)t * k_stride + off;
-    double x0 = src[0], x1 = src[1];
-    float r0 = (float)__dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y));
-    float r1 = (float)__dadd_rn(__dmul_rn(x0, cs.y), __dmul_rn(x1, cs.x));
-    if (isq) {
-      float* dst = q + (size_t)t * q_stride + off;
-      dst[0] = r0;
-      dst[1] = r1;
-    } else {
-      float* dst = kc + (size_t)pos * kv_dim + off;
-      dst[0] = r0;
-      dst[1] = r1;
+  const int half = hd / 2, kv_dim = n_kv * hd;
+  const int nq = n_heads * half, nk = n_kv * half;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const int p0 = pos_dev ? *pos_dev : start_pos;
+  // rows_per_cta rows of the same element columns per CTA (prefill sizes: fewer, longer CTAs)
+  for (int rr = 0; rr < rows_per_cta; ++rr) {
+    const int t = blockIdx.y * rows_per_cta + rr;  // row; rows of sequence s are s*rows_per_seq .. +rows_per_seq-1
+    if (t >= rows) break;
+    const int sq = t / rows_per_seq;
+    float* kcs = kc + sq * cache_seq_stride;
+    float* vcs = vc + sq * cache_seq_stride;
+    const int pos = p0 + (t - sq * rows_per_seq);
+    if (pos < 0 || pos >= max_len) {
+      if (threadIdx.x == 0 && blockIdx.x == 0) pb_raise(err, PB_DEVERR_BOUNDS);
+      return;
     }
-  } else if (idx < nq + nk + kv_dim) {
-    int dd = idx - nq - nk;
-    vc[(size_t)pos * kv_dim + dd] = v[(size_t)t * v_stride + dd];
+    if (idx < nq + nk) {
+      const bool isq = idx < nq;
+      const int rel = isq ? idx : idx - nq;
+      const int h = rel / half, pr = rel % half;
+      const double2 cs = tab[(size_t)pos * half + pr];
+      const size_t off = (size_t)h * hd + 2 * pr;
+      const float2 xv = *reinterpret_cast<const float2*>(isq ? q + (size_t)t * q_stride + off
+                                                              : k + (size_t)t * k_stride + off);
+      const double x0 = xv.x, x1 = xv.y;
+      float2 r;
+      r.x = (float)__dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y));
+      r.y = (float)__dadd_rn(__dmul_rn(x0, cs.y), __dmul_rn(x1, cs.x));
+      *reinterpret_cast<float2*>(isq ? q + (size_t)t * q_stride + off : kcs + (size_t)pos * kv_dim + off) = r;
+    } else if (idx < nq + nk + kv_dim) {
+      const int dd = idx - nq - nk;
+      vcs[(size_t)pos * kv_dim + dd] = v[(size_t)t * v_stride + dd];
+    }
   }
 }
 
