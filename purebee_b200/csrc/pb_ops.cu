@@ -166,6 +166,66 @@ int pb_launch_rmsnorm_xrecv(pb_ctx* ctx, float* x, int rows, int dim, const floa
                    eps, out, out16, xc, hl, r);
 }
 
+// The prefill-size form (rows >= PB_RMS_WARP_ROWS): a warp per row, 8 rows per
+// CTA, float4 loads (the row read again for the output: it is in L1), the
+// sum of squares over lane l's values 4(l + 32k) .. + 3 in order, then a warp
+// tree.  A different partition from k_rmsnorm_t (within the rounding of a
+// double sum); every path that normalises rows this many at a time takes it,
+// the row split included, so they agree in bits.
+constexpr int PB_RMS_WARP_ROWS = 4096;
+template <bool CH>
+__global__ void k_rmsnorm_w(const float* __restrict__ x, int dim, const float* __restrict__ w, double eps,
+                            float* __restrict__ out, __half* __restrict__ out16, int xc, int hl, int rows) {
+  pb_pdl_trigger();
+  pb_pdl_wait();  // x comes from the previous kernel
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* xr = x + (size_t)row * (CH ? xc : dim);
+  const size_t cs = (size_t)rows * xc;
+  auto X4 = [&](int d) {  // d % 4 == 0, xc % 4 == 0
+    return *reinterpret_cast<const float4*>(CH ? xr + (size_t)(d / xc) * cs + d % xc : xr + d);
+  };
+  double ss = 0.0;
+  for (int d = 4 * lane; d < dim; d += 128) {
+    const float4 v = X4(d);
+    ss = __fma_rn((double)v.x, (double)v.x, ss);
+    ss = __fma_rn((double)v.y, (double)v.y, ss);
+    ss = __fma_rn((double)v.z, (double)v.z, ss);
+    ss = __fma_rn((double)v.w, (double)v.w, ss);
+  }
+  ss = pb_warp_sum_d(ss);
+  const double rms = __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)dim), eps));
+  const float inv = (float)(1.0 / rms);
+  for (int d = 4 * lane; d < dim; d += 128) {
+    const float4 v = X4(d);
+    const float4 g = *reinterpret_cast<const float4*>(w + d);
+    if (out16) {
+      const float a0 = v.x * inv * g.x, a1 = v.y * inv * g.y, a2 = v.z * inv * g.z, a3 = v.w * inv * g.w;
+      const __half2 h01 = __floats2half2_rn(a0, a1), h23 = __floats2half2_rn(a2, a3);
+      if (hl) {  // hi halves of the 64-group at +0, lo at +64 (pb_hl_index); 4 values stay in one group
+        const size_t o = pb_hl_index((size_t)row * 2 * dim, d);
+        *reinterpret_cast<uint2*>(out16 + o) = make_uint2(*reinterpret_cast<const uint32_t*>(&h01),
+                                                          *reinterpret_cast<const uint32_t*>(&h23));
+        const __half2 l01 = __floats2half2_rn(a0 - __low2float(h01), a1 - __high2float(h01));
+        const __half2 l23 = __floats2half2_rn(a2 - __low2float(h23), a3 - __high2float(h23));
+        *reinterpret_cast<uint2*>(out16 + o + 64) = make_uint2(*reinterpret_cast<const uint32_t*>(&l01),
+                                                               *reinterpret_cast<const uint32_t*>(&l23));
+      } else {
+        *reinterpret_cast<uint2*>(out16 + (size_t)row * dim + d) =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+      }
+    } else {
+      float4 o;
+      o.x = (float)__dmul_rn(__ddiv_rn((double)v.x, rms), (double)g.x);
+      o.y = (float)__dmul_rn(__ddiv_rn((double)v.y, rms), (double)g.y);
+      o.z = (float)__dmul_rn(__ddiv_rn((double)v.z, rms), (double)g.z);
+      o.w = (float)__dmul_rn(__ddiv_rn((double)v.w, rms), (double)g.w);
+      *reinterpret_cast<float4*>(out + (size_t)row * dim + d) = o;
+    }
+  }
+}
+
 void pb_launch_rmsnorm(cudaStream_t st, const float* x, int rows, int dim, const float* w, double eps, float* out,
                        __half* out16, int xc, int hl, bool pdl) {
   cudaLaunchConfig_t cfg = {};
@@ -177,7 +237,14 @@ void pb_launch_rmsnorm(cudaStream_t st, const float* x, int rows, int dim, const
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (xc > 0 && xc < dim) cudaLaunchKernelEx(&cfg, k_rmsnorm_t<true>, x, dim, w, eps, out, out16, xc, hl);
+  const bool ch = xc > 0 && xc < dim;
+  if (rows >= PB_RMS_WARP_ROWS && dim % 128 == 0 && (!ch || xc % 4 == 0)) {
+    cfg.gridDim = dim3((rows + 7) / 8);
+    if (ch) cudaLaunchKernelEx(&cfg, k_rmsnorm_w<true>, x, dim, w, eps, out, out16, xc, hl, rows);
+    else cudaLaunchKernelEx(&cfg, k_rmsnorm_w<false>, x, dim, w, eps, out, out16, 0, hl, rows);
+    return;
+  }
+  if (ch) cudaLaunchKernelEx(&cfg, k_rmsnorm_t<true>, x, dim, w, eps, out, out16, xc, hl);
   else cudaLaunchKernelEx(&cfg, k_rmsnorm_t<false>, x, dim, w, eps, out, out16, 0, hl);
 }
 
