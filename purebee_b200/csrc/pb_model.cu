@@ -43,14 +43,16 @@ int pb_launch_attn_dec1(pb_ctx* ctx, const float* q, const float* kc, const floa
                         unsigned int* counters);
 
 int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
-                               int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo, int terms = 1);
+                               int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo, int terms = 1,
+                               const __half* khl = nullptr, const __half* vhl = nullptr, int64_t hl_seq_stride = 0);
 bool pb_attn_decode_ok(int n_heads, int n_kv, int hd, int max_len);
 bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len);
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
                           const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
                           const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
                           float* __restrict__ kc, float* __restrict__ vc, int max_len, int rows_per_seq,
-                          int64_t cache_seq_stride, int* err, int rows, int rows_per_cta);
+                          int64_t cache_seq_stride, int* err, int rows, int rows_per_cta, __half* __restrict__ khl,
+                          __half* __restrict__ vhl, int64_t hl_seq_stride);
 __global__ void k_glu(const float* __restrict__ g, int g_stride, const float* __restrict__ u, int u_stride, int F,
                       int mode, int interleave4, float* __restrict__ out);
 __global__ void k_embed(int type, const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc,
@@ -710,7 +712,7 @@ static int run_layer(pb_model* m, int l, int M, int start_pos, bool dev_pos) {
     const int rpc = rope_rows_per_cta(M);
     k_rope_kv<<<dim3(pb_cdiv(tot, 128), pb_cdiv(M, rpc)), 128, 0, ctx->stream>>>(
         q, qs_, k, ks_, v, vs_, c.n_heads, c.n_kv_heads, c.head_dim, m->rope_tab, start_pos, pos_dev, kcache(m, l),
-        vcache(m, l), c.seq_len, M, 0, ctx->d_err, M, rpc);
+        vcache(m, l), c.seq_len, M, 0, ctx->d_err, M, rpc, nullptr, nullptr, 0);
     PB_LAUNCHED(ctx, "k_rope_kv");
   }
   if (M == 1 && pos_dev && (m->attn_ws || pb_attn_decode_ok(c.n_heads, c.n_kv_heads, c.head_dim, c.seq_len)))
@@ -1278,6 +1280,10 @@ struct pb_shard {
   float* xl = nullptr;    // last row of every sequence, row-major [B][dim]
   float* logits = nullptr;               // [world][B][vocab_chunk]; the rank's chunk is computed
   unsigned long long* keys = nullptr;    // [world][B] argmax keys of each rank's vocab rows
+  // the prefill's K and V as hi/lo halves, [K, V][seq][prompt pos][kv head][hi 64 | lo 64]
+  // (three-term prefill attention operands, written by k_rope_kv)
+  __half* kvhl = nullptr;
+  size_t kvhl_bytes = 0;
 };
 
 struct pb_batch {
@@ -1435,7 +1441,7 @@ static void shard_free(pb_ctx* ctx, pb_shard& s) {
   s.qkv.clear(); s.wo.clear(); s.gu.clear(); s.w2.clear();
   s.head = nullptr;
   cudaFree(s.kc); cudaFree(s.vc); cudaFree(s.x); cudaFree(s.xn); cudaFree(s.qkvo); cudaFree(s.att); cudaFree(s.hb);
-  cudaFree(s.xl); cudaFree(s.logits); cudaFree(s.keys);
+  cudaFree(s.xl); cudaFree(s.logits); cudaFree(s.keys); cudaFree(s.kvhl);
   s.kc = s.vc = s.x = s.xn = s.qkvo = s.att = s.hb = s.xl = s.logits = nullptr;
   s.keys = nullptr;
 }
@@ -1800,13 +1806,30 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
     if (!normed) PB_TRY(launch_norm(m, s.x, rows, m->rms_att + (size_t)l * dim, s.xn, nullptr, dc));
     PB_TRY(pb_launch_q4_gemm(ctx, s.qkv[l], s.xn, dim, rows, s.qkvo, qw, b->ws, b->ws_bytes, &st));
   }
+  // the three-term prefill attention reads K and V as hi/lo halves converted once, here
+  const bool kv_hl = b->terms == 3 && hd == 64 && !pos_dev && start_pos == 0 && rows_per_seq > 1;
+  const int64_t hl_stride = (int64_t)rows_per_seq * 2 * kvl;  // halves per sequence
+  __half *khl = nullptr, *vhl = nullptr;
+  if (kv_hl) {
+    const size_t need = (size_t)2 * b->B * hl_stride * sizeof(__half);
+    if (s.kvhl_bytes < need) {
+      PB_TRY(pb_wait(ctx));
+      cudaFree(s.kvhl);
+      s.kvhl = nullptr;
+      s.kvhl_bytes = 0;
+      PB_TRY_CUDA(ctx, cudaMalloc(&s.kvhl, need));
+      s.kvhl_bytes = need;
+    }
+    khl = s.kvhl;
+    vhl = s.kvhl + (size_t)b->B * hl_stride;
+  }
   {
     const int tot = (p.n_heads + p.n_kv_heads) * (hd / 2) + kvl, rpc = rope_rows_per_cta(rows);
     PB_TRY(pb_launch(ctx, "k_rope_kv", true, k_rope_kv, dim3(pb_cdiv(tot, 128), pb_cdiv(rows, rpc)), dim3(128), 0,
                      s.qkvo, qw, (const float*)(s.qkvo + p.n_heads * hd), qw,
                      (const float*)(s.qkvo + (p.n_heads + p.n_kv_heads) * hd), qw, p.n_heads, p.n_kv_heads, hd,
                      (const double2*)m->rope_tab, start_pos, pos_dev, kc, vc, c.seq_len, rows_per_seq, cache_seq,
-                     ctx->d_err, rows, rpc));
+                     ctx->d_err, rows, rpc, khl, vhl, kv_hl ? hl_stride : (int64_t)0));
   }
   float* att = s.att + (size_t)s.rank * rows * dc;
   pb_seq_geo geo;
@@ -1822,7 +1845,7 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
   geo.out = (int64_t)rows_per_seq * dc;
   if (hd == 64 && !pos_dev)
     return pb_launch_attn_prefill(ctx, s.qkvo, qw, kc, vc, rows_per_seq, start_pos, p.n_heads, p.n_kv_heads, hd, att,
-                                  b->B, geo, b->terms);
+                                  b->B, geo, b->terms, khl, vhl, hl_stride);
   return pb_launch_attn_cached(ctx, s.qkvo, qw, kc, vc, rows_per_seq, start_pos, pos_dev, p.n_heads, p.n_kv_heads, hd,
                                att, c.seq_len, b->B, geo);
 }

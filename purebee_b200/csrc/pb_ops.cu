@@ -778,7 +778,8 @@ template <int TERMS>
 __global__ void __launch_bounds__(FT_THREADS)
 k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __restrict__ kc,
                   const float* __restrict__ vc, int seq, int start_pos, int n_heads, int n_kv, float scale,
-                  float* __restrict__ out, pb_seq_geo geo) {
+                  float* __restrict__ out, pb_seq_geo geo, const __half* __restrict__ khl,
+                  const __half* __restrict__ vhl, int64_t hl_seq_stride) {
   // [hi, lo] tiles of Q, K, V (the lo tiles only with three terms)
   constexpr int T = TERMS == 3 ? 2 : 1;
   extern __shared__ __align__(16) unsigned char ft_raw[];
@@ -792,6 +793,13 @@ k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __rest
   kc += z * geo.kv;
   vc += z * geo.kv;
   out += z * geo.out;
+  // khl / vhl (three terms): K and V already as hi/lo halves (k_rope_kv), copied
+  // into the tiles by cp.async instead of converted here by every CTA
+  const bool pre = TERMS == 3 && khl != nullptr;
+  if (pre) {
+    khl += z * hl_seq_stride + (size_t)kh * 2 * FT_HD;
+    vhl += z * hl_seq_stride + (size_t)kh * 2 * FT_HD;
+  }
   for (int i = tid; i < FT_Q * FT_HD / 4; i += FT_THREADS) {
     const int qr = i / (FT_HD / 4), d4 = i % (FT_HD / 4);
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -817,7 +825,23 @@ k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __rest
   const int qp0 = start_pos + q0 + warp * 16 + g, qp1 = qp0 + 8;
   for (int k0 = 0; k0 < kend; k0 += FT_KT) {
     __syncthreads();  // the previous tile is no longer read
-    for (int i = tid; i < FT_KT * FT_HD / 4; i += FT_THREADS) {
+    if (pre) {  // 16-byte pieces: (row, hi / lo, 8 halves); rows past kend are zero
+      for (int i = tid; i < FT_KT * 16; i += FT_THREADS) {
+        const int kr = i >> 4, part = (i >> 3) & 1, c8 = (i & 7) * 8;
+        __half* kd = &Ks[part * FT_KT + kr][c8];
+        __half* vd = &Vs[part * FT_KT + kr][c8];
+        if (k0 + kr < kend) {
+          const size_t so = (size_t)(k0 + kr) * 2 * kv_dim + part * FT_HD + c8;
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(pb_smem_addr(kd)), "l"(khl + so) : "memory");
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(pb_smem_addr(vd)), "l"(vhl + so) : "memory");
+        } else {
+          *reinterpret_cast<uint4*>(kd) = make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(vd) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+    }
+    for (int i = tid; !pre && i < FT_KT * FT_HD / 4; i += FT_THREADS) {
       const int kr = i / (FT_HD / 4), d4 = i % (FT_HD / 4);
       float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
       if (k0 + kr < kend) {
@@ -947,11 +971,12 @@ static size_t ft_smem(int terms) { return (size_t)(terms == 3 ? 2 : 1) * (FT_Q +
 
 int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
                            int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo,
-                           int terms) {
+                           int terms, const __half* khl, const __half* vhl, int64_t hl_seq_stride) {
   if (hd != FT_HD || (q_stride & 3) || (terms != 1 && terms != 3)) return PB_ERR_ARG;
   auto kern = terms == 3 ? k_attn_prefill_tc<3> : k_attn_prefill_tc<1>;
   kern<<<dim3(pb_cdiv(seq, FT_Q), n_heads, nseq), FT_THREADS, ft_smem(terms), ctx->stream>>>(
-      q, q_stride, kc, vc, seq, start_pos, n_heads, n_kv, (float)(1.0 / sqrt((double)hd)), out, geo);
+      q, q_stride, kc, vc, seq, start_pos, n_heads, n_kv, (float)(1.0 / sqrt((double)hd)), out, geo, khl, vhl,
+      hl_seq_stride);
   PB_LAUNCHED(ctx, "k_attn_prefill_tc");
   return PB_OK;
 }
@@ -987,11 +1012,23 @@ extern "C" int pb_attn_cached(pb_ctx* ctx, const float* q, const float* kc, cons
 // RoPE on q (in place, row stride q_stride) and k, then KV append
 // (llama-streaming.js:531-541): rows t = 0..seq-1 at position pos0 + t,
 // pos0 = *pos_dev when pos_dev is set.  tab has one entry per position.
+// The batched prefill attention's K / V operands, converted once: per position,
+// per kv head, its hd hi halves then its hd lo halves (hi = f16(v), lo =
+// f16(v - hi), as the attention converts them); off = head * hd + d, d even.
+__device__ __forceinline__ void ft_store_hl_pair(__half* row, size_t off, int hd, float a, float b) {
+  const size_t o = (off / hd) * 2 * hd + off % hd;
+  const __half2 hi = __floats2half2_rn(a, b);
+  *reinterpret_cast<__half2*>(row + o) = hi;
+  *reinterpret_cast<__half2*>(row + o + hd) =
+      __floats2half2_rn(__fsub_rn(a, __low2float(hi)), __fsub_rn(b, __high2float(hi)));
+}
+
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
                           const float* __restrict__ v, int v_stride, int n_heads, int n_kv, int hd,
                           const double2* __restrict__ tab, int start_pos, const int* __restrict__ pos_dev,
                           float* __restrict__ kc, float* __restrict__ vc, int max_len, int rows_per_seq,
-                          int64_t cache_seq_stride, int* err, int rows, int rows_per_cta) {
+                          int64_t cache_seq_stride, int* err, int rows, int rows_per_cta, __half* __restrict__ khl,
+                          __half* __restrict__ vhl, int64_t hl_seq_stride) {
   pb_pdl_trigger();
   pb_pdl_wait();  // q, k, v come from the projection
   const int half = hd / 2, kv_dim = n_kv * hd;
@@ -1023,9 +1060,17 @@ __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __re
       r.x = (float)__dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y));
       r.y = (float)__dadd_rn(__dmul_rn(x0, cs.y), __dmul_rn(x1, cs.x));
       *reinterpret_cast<float2*>(isq ? q + (size_t)t * q_stride + off : kcs + (size_t)pos * kv_dim + off) = r;
+      if (!isq && khl) ft_store_hl_pair(khl + sq * hl_seq_stride + (size_t)pos * 2 * kv_dim, off, hd, r.x, r.y);
     } else if (idx < nq + nk + kv_dim) {
       const int dd = idx - nq - nk;
-      vcs[(size_t)pos * kv_dim + dd] = v[(size_t)t * v_stride + dd];
+      const float vv = v[(size_t)t * v_stride + dd];
+      vcs[(size_t)pos * kv_dim + dd] = vv;
+      if (vhl) {
+        __half* row = vhl + sq * hl_seq_stride + (size_t)pos * 2 * kv_dim + (size_t)(dd / hd) * 2 * hd + dd % hd;
+        const __half hi = __float2half_rn(vv);
+        row[0] = hi;
+        row[hd] = __float2half_rn(__fsub_rn(vv, __half2float(hi)));
+      }
     }
   }
 }
