@@ -44,7 +44,8 @@ int pb_launch_attn_dec1(pb_ctx* ctx, const float* q, const float* kc, const floa
 
 int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
                                int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo, int terms = 1,
-                               const __half* khl = nullptr, const __half* vhl = nullptr, int64_t hl_seq_stride = 0);
+                               const __half* khl = nullptr, const __half* vhl = nullptr, int64_t hl_seq_stride = 0,
+                               __half* out16 = nullptr);
 bool pb_attn_decode_ok(int n_heads, int n_kv, int hd, int max_len);
 bool pb_attn_decode_group_ok(int n_heads, int n_kv, int hd, int max_len);
 __global__ void k_rope_kv(float* __restrict__ q, int q_stride, const float* __restrict__ k, int k_stride,
@@ -1775,6 +1776,14 @@ static bool dec16(const pb_batch* b, const pb_shard& s, int l, int rows) {
          pb_gemm_uses_ws(s.gu[l], rows) && pb_gemm_uses_ws(s.w2[l], rows);
 }
 
+// One process with the whole model, a three-term prefill whose wo GEMM takes
+// f16 operands (the TMA path): the prefill attention writes its output as the
+// GEMM's hi/lo pairs (the bits k_f32_to_f16 would make of the f32 rows).
+static bool att_hl_prefill(const pb_batch* b, const pb_shard& s, int l, int rows) {
+  return b->world == 1 && b->sh.size() == 1 && b->terms == 3 && !b->decoding && b->m->c.head_dim == 64 &&
+         pb_gemm_uses_tma(s.wo[l], rows);
+}
+
 // norm -> this rank's q | k | v -> RoPE + KV append -> attention of its heads
 // into its chunk of att.
 static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_per_seq, int start_pos,
@@ -1845,7 +1854,8 @@ static int shard_attention(pb_batch* b, pb_shard& s, int l, int rows, int rows_p
   geo.out = (int64_t)rows_per_seq * dc;
   if (hd == 64 && !pos_dev)
     return pb_launch_attn_prefill(ctx, s.qkvo, qw, kc, vc, rows_per_seq, start_pos, p.n_heads, p.n_kv_heads, hd, att,
-                                  b->B, geo, b->terms, khl, vhl, hl_stride);
+                                  b->B, geo, b->terms, khl, vhl, hl_stride,
+                                  att_hl_prefill(b, s, l, rows) ? reinterpret_cast<__half*>(att) : nullptr);
   return pb_launch_attn_cached(ctx, s.qkvo, qw, kc, vc, rows_per_seq, start_pos, pos_dev, p.n_heads, p.n_kv_heads, hd,
                                att, c.seq_len, b->B, geo);
 }
@@ -1877,7 +1887,7 @@ static int shard_wo(pb_batch* b, pb_shard& s, int l, int rows, bool send_x = fal
   if (send_x) add.xs = xsend_of(b, dc);
   if (norm_next)  // the FFN norm, into the gate|up GEMM's operand
     set_norm(b, s, add, m->rms_ffn + (size_t)l * m->c.dim, pb_gemm_uses_tma(s.gu[l], rows) || dec16(b, s, l, rows));
-  if (dec16(b, s, l, rows))
+  if (dec16(b, s, l, rows) || att_hl_prefill(b, s, l, rows))  // the attention wrote hi/lo pairs
     return pb_launch_q4_gemm(m->ctx, s.wo[l], nullptr, m->c.dim, rows, s.x + (size_t)s.rank * rows * dc, dc, b->ws,
                              b->ws_bytes, &add, reinterpret_cast<const __half*>(s.att));
   return pb_launch_q4_gemm(m->ctx, s.wo[l], s.att, m->c.dim, rows, s.x + (size_t)s.rank * rows * dc, dc, b->ws,

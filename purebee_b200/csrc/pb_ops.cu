@@ -779,7 +779,7 @@ __global__ void __launch_bounds__(FT_THREADS)
 k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __restrict__ kc,
                   const float* __restrict__ vc, int seq, int start_pos, int n_heads, int n_kv, float scale,
                   float* __restrict__ out, pb_seq_geo geo, const __half* __restrict__ khl,
-                  const __half* __restrict__ vhl, int64_t hl_seq_stride) {
+                  const __half* __restrict__ vhl, int64_t hl_seq_stride, __half* __restrict__ out16) {
   // [hi, lo] tiles of Q, K, V (the lo tiles only with three terms)
   constexpr int T = TERMS == 3 ? 2 : 1;
   extern __shared__ __align__(16) unsigned char ft_raw[];
@@ -793,6 +793,7 @@ k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __rest
   kc += z * geo.kv;
   vc += z * geo.kv;
   out += z * geo.out;
+  if (out16) out16 += z * geo.out * 2;  // hi/lo pairs take the bytes of the f32 rows
   // khl / vhl (three terms): K and V already as hi/lo halves (k_rope_kv), copied
   // into the tiles by cp.async instead of converted here by every CTA
   const bool pre = TERMS == 3 && khl != nullptr;
@@ -955,6 +956,22 @@ k_attn_prefill_tc(const float* __restrict__ q, int q_stride, const float* __rest
   }
   const float inv0 = 1.0f / l_r[0], inv1 = 1.0f / l_r[1];
   const int r0 = q0 + warp * 16 + g, r1 = r0 + 8;
+  if (out16) {  // the wo GEMM's operand directly: hi/lo pairs (pb_hl_index), as k_f32_to_f16 forms them
+    auto put = [&](int r, int d, float a, float b) {
+      const size_t o = pb_hl_index((size_t)r * 2 * dim, h * FT_HD + d);
+      const __half2 hi = __floats2half2_rn(a, b);
+      *reinterpret_cast<__half2*>(out16 + o) = hi;
+      *reinterpret_cast<__half2*>(out16 + o + 64) =
+          __floats2half2_rn(__fsub_rn(a, __low2float(hi)), __fsub_rn(b, __high2float(hi)));
+    };
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = 8 * j + 2 * t;
+      if (r0 < seq) put(r0, d, o[j][0] * inv0, o[j][1] * inv0);
+      if (r1 < seq) put(r1, d, o[j][2] * inv1, o[j][3] * inv1);
+    }
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int d = 8 * j + 2 * t;
@@ -971,12 +988,12 @@ static size_t ft_smem(int terms) { return (size_t)(terms == 3 ? 2 : 1) * (FT_Q +
 
 int pb_launch_attn_prefill(pb_ctx* ctx, const float* q, int q_stride, const float* kc, const float* vc, int seq,
                            int start_pos, int n_heads, int n_kv, int hd, float* out, int nseq, pb_seq_geo geo,
-                           int terms, const __half* khl, const __half* vhl, int64_t hl_seq_stride) {
+                           int terms, const __half* khl, const __half* vhl, int64_t hl_seq_stride, __half* out16) {
   if (hd != FT_HD || (q_stride & 3) || (terms != 1 && terms != 3)) return PB_ERR_ARG;
   auto kern = terms == 3 ? k_attn_prefill_tc<3> : k_attn_prefill_tc<1>;
   kern<<<dim3(pb_cdiv(seq, FT_Q), n_heads, nseq), FT_THREADS, ft_smem(terms), ctx->stream>>>(
       q, q_stride, kc, vc, seq, start_pos, n_heads, n_kv, (float)(1.0 / sqrt((double)hd)), out, geo, khl, vhl,
-      hl_seq_stride);
+      hl_seq_stride, terms == 3 ? out16 : nullptr);
   PB_LAUNCHED(ctx, "k_attn_prefill_tc");
   return PB_OK;
 }
