@@ -30,11 +30,13 @@ def close(a, b, rtol=RTOL_LOGITS):
 @pytest.mark.parametrize("n_seqs,n_prompt,hd,dim,terms", [(3, 5, 32, 128, 3), (4, 130, 32, 128, 3),
                                                           (3, 70, 64, 128, 3), (2, 300, 64, 128, 3),
                                                           (4, 9, 64, 512, 3), (3, 70, 64, 128, 1),
-                                                          (2, 300, 64, 128, 1)])
+                                                          (2, 300, 64, 128, 1), (16, 256, 64, 128, 3)])
 def test_batch_matches_single_sequence(native, ctx, n_seqs, n_prompt, hd, dim, terms):
     """15 / 210 rows run the fused-dequant GEMM, 520 / 600 the TMA one; head_dim 64
     takes the tiled prefill attention, 32 the per-query kernel; dim 512
-    makes the decode GEMMs split K over CTAs.  terms: the GEMM precision."""
+    makes the decode GEMMs split K over CTAs; 4096 rows take the prefill-size
+    RMSNorm (a warp per row) and, with three terms, the attention writing the
+    wo GEMM's hi/lo operand.  terms: the GEMM precision."""
     from purebee_b200.runtime import BatchedLlamaRuntime
     rt = make(native, ctx, dim=dim, hiddenDim=2 * dim, headDim=hd, nHeads=dim // hd, nKvHeads=max(1, dim // (2 * hd)),
               seqLen=400)

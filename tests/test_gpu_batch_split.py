@@ -40,12 +40,15 @@ def same_bits(a, b):
 
 @pytest.mark.parametrize("world,n_seqs,n_prompt,shape", [
     (2, 3, 9, "hd64"), (4, 3, 9, "hd64"), (2, 2, 300, "hd64"), (4, 2, 300, "hd64"), (8, 2, 17, "kv8"),
-    (2, 3, 9, "hd32"), (4, 2, 260, "hd32")])
+    (2, 3, 9, "hd32"), (4, 2, 260, "hd32"), (2, 16, 256, "hd64")])
 def test_group_split_same_bits(native, ctx, world, n_seqs, n_prompt, shape):
     """27 / 34 prompt rows take the fused-dequant GEMM, 520 / 600 the TMA
     one (chunked f16 operands through a 3-d tensor map); head_dim 64 takes the
     tensor-core prefill attention, 32 the per-query kernel; decode steps split
-    K over CTAs with the whole matrix's plan."""
+    K over CTAs with the whole matrix's plan.  4096 rows take the prefill-size
+    RMSNorm over chunked and row-major x, and the unsplit batch's attention
+    writes the wo operand as hi/lo pairs where the split converts its f32
+    rows: the same bits either way."""
     kw = {"hd64": {}, "kv8": dict(nKvHeads=8), "hd32": dict(dim=256, hiddenDim=512, headDim=32, nHeads=8,
                                                                nKvHeads=4)}[shape]
     rt = make(native, ctx, **kw)
