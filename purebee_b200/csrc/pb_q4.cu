@@ -933,6 +933,16 @@ k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, i
   if (xr) mvf_stage_x_regs(x, epi.eps, K, wr, xs4, red);
   else mvf_stage_x(x, epi.norm_w, epi.eps, K, xs4, red);
   __syncthreads();
+  // a residual epilogue's rows are loaded one tile ahead, during the sums
+  // (independent loads: nothing waits on them until the store)
+  auto res_row = [&](int it) -> float {
+    const int row = tile_of(it) * 8 + (lane >> 2);
+    return epi.kind == PB_EPI_RESIDUAL && active && ch == 0 && (lane & 3) == 0 && it < n_iter &&
+                   tile_of(it) < tile_end && row < row_end && row < N
+               ? epi.residual[row]
+               : 0.0f;
+  };
+  float res = res_row(0);
   uint64_t xp[16];
   if (has_b) {
 #pragma unroll
@@ -998,7 +1008,13 @@ k_mvf(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc, int N, i
       const int rr = lane >> 2;
       float s_ = pbuf[(size_t)tl * KC * 8 + rr];
       for (int c = 1; c < KC; ++c) s_ = __fadd_rn(s_, pbuf[((size_t)tl * KC + c) * 8 + rr]);
-      pb_mv_epilogue(s_, t, N, 0, row_end, y, epi, err);
+      if (epi.kind == PB_EPI_RESIDUAL) {  // pb_mv_epilogue's residual store, the row loaded above
+        const int row = t * 8 + rr;
+        if ((lane & 3) == 0 && row < row_end && row < N) y[row] = __fadd_rn(res, s_);
+        res = res_row(it + 1);
+      } else {
+        pb_mv_epilogue(s_, t, N, 0, row_end, y, epi, err);
+      }
     }
   }
   asm volatile("cp.async.wait_all;" ::: "memory");  // no copy outlives the CTA
