@@ -338,6 +338,22 @@ class _RuntimeBase:
                 "decodeTime": dt * 1000, "tokPerSec": max(generated - 1, 1) / max(dt, 1e-9),
                 "avgLayers": self.config.nLayers, "earlyExits": 0}
 
+    async def forwardAsync(self, tokenIds, startPos: int = 0, options: Optional[dict] = None):
+        """llama-streaming.js:821-823, kept there for API compatibility: forward()."""
+        return self.forward(tokenIds, startPos, options)
+
+    async def generateAsync(self, promptTokens, maxTokens: int = 50, opts: Optional[dict] = None):
+        """llama-streaming.js:976-978, kept there for API compatibility: generate()."""
+        return self.generate(promptTokens, maxTokens, opts)
+
+    async def initThreadPool(self, numWorkers: Optional[int] = None) -> bool:
+        """llama-streaming.js:230-244 starts host worker threads for the
+        row-split matvecs and resolves false when it cannot start them.  Every
+        matvec here runs on the device, so there is no host pool: false, the
+        reference's answer without one (the row split over several GPUs is
+        purebee_b200.thread_pool's)."""
+        return False
+
     def resetCache(self):
         self.model.reset_cache()
 
